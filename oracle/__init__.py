@@ -1,0 +1,218 @@
+"""TEST INFRASTRUCTURE ONLY -- the CPU checker for the CUDA MoE path.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg may import this
+package; the product path never does.
+
+Two CPU implementations are exposed:
+
+* ``liboracle.so`` -- the restated MoE block (oracle/moe_oracle.c), which follows the
+  reference's scalar FP32 forward (src/cpu_reference.cpp:422-520) operation by operation;
+* ``_ref/libgtref.so`` -- the reference's own src/cpu_reference.cpp helpers compiled from its
+  sources (built only where the reference tree is present; it travels as a prebuilt .so).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libgtref.so")
+
+HIDDEN, MOE_INTER, FFN, EXPERTS, TOP_K, EPS = 2816, 704, 2112, 128, 8, 1e-6
+
+
+def build(ref_dir: str | None = None) -> None:
+    """Builds liboracle.so, and _ref/libgtref.so when the reference sources are present."""
+    subprocess.check_call(["make", "-s", "-C", HERE, "oracle"])
+    ref = ref_dir or "/root/reference"
+    if os.path.isfile(os.path.join(ref, "src", "cpu_reference.cpp")):
+        subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF={ref}"])
+
+
+class QT(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p),
+                ("rows", C.c_uint32), ("in_dim", C.c_uint32), ("bits", C.c_int)]
+
+
+class Layer(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("moe_inter", C.c_uint32), ("ffn_inter", C.c_uint32),
+                ("num_experts", C.c_uint32), ("top_k", C.c_uint32), ("eps", C.c_float),
+                ("router", QT), ("router_scale", C.c_void_p), ("per_expert_scale", C.c_void_p),
+                ("sh_gate", QT), ("sh_up", QT), ("sh_down", QT),
+                ("w_pre", C.c_void_p), ("w_pre2", C.c_void_p), ("w_pf1", C.c_void_p),
+                ("w_pf2", C.c_void_p), ("w_pf", C.c_void_p), ("layer_scalar", C.c_uint16),
+                ("experts", C.c_void_p), ("expert_stride", C.c_uint64),
+                ("sub_off", C.c_uint64 * 9)]
+
+
+class BlockOut(C.Structure):
+    _fields_ = [("hidden_out", C.c_void_p), ("h1", C.c_void_p), ("h2", C.c_void_p),
+                ("logits", C.c_void_p), ("top_idx", C.c_void_p), ("top_w", C.c_void_p)]
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.orc_bf16.restype = C.c_float
+        L.orc_bf16.argtypes = [C.c_uint16]
+        L.orc_gelu_tanh.restype = C.c_float
+        L.orc_gelu_tanh.argtypes = [C.c_float]
+        L.orc_rms_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_void_p]
+        L.orc_matvec.argtypes = [C.POINTER(QT), C.c_void_p, C.c_void_p]
+        L.orc_topk.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_moe_block.argtypes = [C.POINTER(Layer), C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(BlockOut)]
+        L.orc_synth_resident.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]
+        L.orc_synth_expert.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]
+        L.orc_synth_x.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_void_p]
+        L.orc_synth_layer_create.restype = C.c_void_p
+        L.orc_synth_layer_create.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                             C.c_uint32, C.c_uint32, C.c_float]
+        L.orc_synth_layer_destroy.argtypes = [C.c_void_p]
+        L.orc_synth_layer_view.restype = C.POINTER(Layer)
+        L.orc_synth_layer_view.argtypes = [C.c_void_p]
+        L.orc_synth_layer_ensure.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32]
+        L.orc_synth_layer_block.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(BlockOut)]
+        L.orc_synth_stack.argtypes = [C.POINTER(C.c_void_p), C.c_uint32, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_void_p, C.c_void_p]
+        _lib = L
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH)
+
+
+def ref():
+    """The reference's own compiled helpers (oracle/_ref/libgtref.so)."""
+    global _ref
+    if _ref is None:
+        R = C.CDLL(REF_PATH)
+        R.gtref_bf16.restype = C.c_float
+        R.gtref_bf16.argtypes = [C.c_uint16]
+        R.gtref_gelu_tanh.restype = C.c_float
+        R.gtref_gelu_tanh.argtypes = [C.c_float]
+        R.gtref_rms_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_void_p]
+        R.gtref_matvec.argtypes = [C.POINTER(QT), C.c_void_p, C.c_void_p]
+        R.gtref_moe_block.argtypes = [C.POINTER(Layer), C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(BlockOut)]
+        _ref = R
+    return _ref
+
+
+# ---- numpy-facing helpers ------------------------------------------------------------------
+
+def matvec(w: np.ndarray, s: np.ndarray, b: np.ndarray, x: np.ndarray, rows: int, in_dim: int,
+           bits: int, impl: str = "oracle") -> np.ndarray:
+    """out[r] = sum_c (q[r][c] * s + b) * x[c] in the reference's accumulation order."""
+    w = np.ascontiguousarray(w); s = np.ascontiguousarray(s, dtype=np.uint16)
+    b = np.ascontiguousarray(b, dtype=np.uint16); x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(rows, np.float32)
+    qt = QT(w.ctypes.data, s.ctypes.data, b.ctypes.data, rows, in_dim, bits)
+    if impl == "ref":
+        ref().gtref_matvec(C.byref(qt), _ptr(x), _ptr(out))
+    else:
+        lib().orc_matvec(C.byref(qt), _ptr(x), _ptr(out))
+    return out
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray | None, eps: float = EPS, impl: str = "oracle") -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    wa = None if w is None else np.ascontiguousarray(w, dtype=np.uint16)
+    out = np.zeros_like(x)
+    f = ref().gtref_rms_norm if impl == "ref" else lib().orc_rms_norm
+    f(_ptr(x), _ptr(wa), x.size, eps, _ptr(out))
+    return out
+
+
+def gelu_tanh(x: np.ndarray, impl: str = "oracle") -> np.ndarray:
+    f = ref().gtref_gelu_tanh if impl == "ref" else lib().orc_gelu_tanh
+    return np.array([f(float(v)) for v in np.asarray(x, np.float32)], np.float32)
+
+
+def topk(logits: np.ndarray, k: int, per_expert_scale: np.ndarray):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    pes = np.ascontiguousarray(per_expert_scale, dtype=np.uint16)
+    idx = np.zeros(k, np.uint32)
+    w = np.zeros(k, np.float32)
+    lib().orc_topk(_ptr(logits), logits.size, k, _ptr(pes), _ptr(idx), _ptr(w))
+    return idx, w
+
+
+def synth_x(seed: int, token: int, hidden: int = HIDDEN) -> np.ndarray:
+    x = np.zeros(hidden, np.float32)
+    lib().orc_synth_x(seed, token, hidden, _ptr(x))
+    return x
+
+
+class SynthLayer:
+    """One synthetic MoE layer on the host, generated by the same counter RNG as the GPU side."""
+
+    def __init__(self, seed: int, layer: int, hidden=HIDDEN, moe_inter=MOE_INTER, ffn=FFN,
+                 experts=EXPERTS, top_k=TOP_K, eps=EPS):
+        self.hidden, self.top_k, self.experts, self.eps = hidden, top_k, experts, eps
+        self.h = lib().orc_synth_layer_create(seed, layer, hidden, moe_inter, ffn, experts, top_k, eps)
+        if not self.h:
+            raise MemoryError("orc_synth_layer_create failed")
+
+    def close(self):
+        if self.h:
+            lib().orc_synth_layer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def view(self):
+        return lib().orc_synth_layer_view(self.h)
+
+    def ensure(self, experts):
+        e = np.ascontiguousarray(np.asarray(experts, dtype=np.uint32))
+        lib().orc_synth_layer_ensure(self.h, _ptr(e), e.size)
+
+    def block(self, hidden_in, logit_bias=None, route_logits=None, impl: str = "oracle"):
+        """Runs the MoE block for one token. impl='ref' runs the reference's compiled helpers."""
+        D, K = self.hidden, self.top_k
+        x = np.ascontiguousarray(hidden_in, dtype=np.float32)
+        lb = None if logit_bias is None else np.ascontiguousarray(logit_bias, dtype=np.float32)
+        rl = None if route_logits is None else np.ascontiguousarray(route_logits, dtype=np.float32)
+        res = {"hidden": np.zeros(D, np.float32), "h1": np.zeros(D, np.float32), "h2": np.zeros(D, np.float32),
+               "logits": np.zeros(self.experts, np.float32), "idx": np.zeros(K, np.uint32),
+               "w": np.zeros(K, np.float32)}
+        out = BlockOut(res["hidden"].ctypes.data, res["h1"].ctypes.data, res["h2"].ctypes.data,
+                       res["logits"].ctypes.data, res["idx"].ctypes.data, res["w"].ctypes.data)
+        if impl == "ref":
+            # route with the oracle first only to learn which experts to materialise
+            probe = self.block(x, lb, rl, impl="oracle")
+            self.ensure(probe["idx"])
+            ref().gtref_moe_block(self.view(), _ptr(x), _ptr(lb), _ptr(rl), C.byref(out))
+        else:
+            lib().orc_synth_layer_block(self.h, _ptr(x), _ptr(lb), _ptr(rl), C.byref(out))
+        return res
+
+
+def synth_stack(layers: list[SynthLayer], hidden_in: np.ndarray):
+    """A stack of synthetic layers with a weightless RMSNorm between layers."""
+    n = len(layers)
+    D, K = layers[0].hidden, layers[0].top_k
+    arr = (C.c_void_p * n)(*[l.h for l in layers])
+    x = np.ascontiguousarray(hidden_in, dtype=np.float32)
+    out = np.zeros(D, np.float32)
+    per = np.zeros((n, D), np.float32)
+    idx = np.zeros((n, K), np.uint32)
+    w = np.zeros((n, K), np.float32)
+    lib().orc_synth_stack(arr, n, _ptr(x), _ptr(out), _ptr(per), _ptr(idx), _ptr(w))
+    return {"hidden": out, "hidden_per_layer": per, "idx": idx, "w": w}

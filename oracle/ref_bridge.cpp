@@ -1,0 +1,161 @@
+/*
+ * TEST INFRASTRUCTURE ONLY. Builds the reference's own scalar FP32 primitives into
+ * oracle/_ref/libgtref.so so tests can pin the restated oracle against them and bench.py can
+ * time the reference's CPU arithmetic as the CPU baseline.
+ *
+ * The reference source is compiled where it lies (the Makefile passes its path); nothing of
+ * it is copied here. Its numeric helpers are file-static (src/cpu_reference.cpp:21-106), so
+ * this translation unit includes that file and exposes the helpers through a C ABI. The MoE
+ * block below composes those helpers in the order of CpuReference::forward
+ * (src/cpu_reference.cpp:422-520); CpuReference::forward itself also runs attention and the
+ * LM head, so the block is reassembled from its parts.
+ */
+#include GTREF_CPU_REFERENCE_CPP
+
+#include <cstdint>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+using gturbo::QuantTensor;
+
+namespace {
+QuantTensor view(const uint8_t* data, const uint16_t* s, const uint16_t* b, uint32_t rows,
+                 uint32_t in_dim, int bits) {
+    QuantTensor t;
+    t.data = data;
+    t.scales = s;
+    t.biases = b;
+    t.rows = rows;
+    t.in_dim = in_dim;
+    t.groups = in_dim / 64;
+    t.bits = bits;
+    t.quantized = true;
+    return t;
+}
+}  // namespace
+
+extern "C" {
+
+struct gtref_qt {
+    const uint8_t* data;
+    const uint16_t* scales;
+    const uint16_t* biases;
+    uint32_t rows, in_dim;
+    int bits;
+};
+
+/* Mirrors orc_layer in oracle/moe_oracle.h field for field. */
+struct gtref_layer {
+    uint32_t hidden, moe_inter, ffn_inter, num_experts, top_k;
+    float eps;
+    gtref_qt router;
+    const uint16_t* router_scale;
+    const uint16_t* per_expert_scale;
+    gtref_qt sh_gate, sh_up, sh_down;
+    const uint16_t *w_pre, *w_pre2, *w_pf1, *w_pf2, *w_pf;
+    uint16_t layer_scalar;
+    const uint8_t* experts;
+    uint64_t expert_stride;
+    uint64_t sub_off[9];
+};
+
+struct gtref_block_out {
+    float* hidden_out;
+    float* h1;
+    float* h2;
+    float* logits;
+    uint32_t* top_idx;
+    float* top_w;
+};
+
+__attribute__((visibility("default"))) float gtref_bf16(uint16_t bits) { return gturbo::bf16(bits); }
+__attribute__((visibility("default"))) float gtref_gelu_tanh(float x) { return gturbo::gelu_tanh(x); }
+__attribute__((visibility("default"))) void gtref_rms_norm(const float* x, const uint16_t* w, size_t n,
+                                                           float eps, float* out) {
+    gturbo::rms_norm(x, w, n, eps, out);
+}
+__attribute__((visibility("default"))) void gtref_matvec(const gtref_qt* t, const float* x, float* out) {
+    gturbo::matvec(view(t->data, t->scales, t->biases, t->rows, t->in_dim, t->bits), x, out);
+}
+
+/* The MoE block of one token using only the reference's helpers, in its forward() order. */
+__attribute__((visibility("default"))) int gtref_moe_block(const gtref_layer* L, const float* hidden_in,
+                                                           const float* logit_bias, const float* route_logits,
+                                                           const gtref_block_out* out) {
+    const uint32_t D = L->hidden, E = L->num_experts, K = L->top_k;
+    const float eps = L->eps;
+    std::vector<float> tmp(D), dense_x(D), routed_x(D), router_in(D);
+    gturbo::rms_norm(hidden_in, nullptr, D, eps, tmp.data());
+    for (uint32_t i = 0; i < D; ++i) {
+        dense_x[i] = tmp[i] * gturbo::bf16(L->w_pre[i]);
+        routed_x[i] = tmp[i] * gturbo::bf16(L->w_pre2[i]);
+    }
+    const float inv_sqrt_d = 1.0f / std::sqrt(static_cast<float>(D));
+    for (uint32_t i = 0; i < D; ++i) router_in[i] = tmp[i] * gturbo::bf16(L->router_scale[i]) * inv_sqrt_d;
+
+    std::vector<float> logits(E);
+    if (route_logits) {
+        std::copy(route_logits, route_logits + E, logits.begin());
+    } else {
+        const gtref_qt& r = L->router;
+        gturbo::matvec(view(r.data, r.scales, r.biases, r.rows, r.in_dim, r.bits), router_in.data(), logits.data());
+    }
+    if (logit_bias) for (uint32_t e = 0; e < E; ++e) logits[e] = logits[e] + logit_bias[e];
+
+    std::vector<int> order(E);
+    std::iota(order.begin(), order.end(), 0);
+    std::partial_sort(order.begin(), order.begin() + K, order.end(), [&](int a, int b) {
+        if (logits[a] != logits[b]) return logits[a] > logits[b];
+        return a < b;
+    });
+    std::vector<float> w(K);
+    {
+        const float best = logits[order[0]];
+        float sum = 0.0f;
+        for (uint32_t i = 0; i < K; ++i) { w[i] = std::exp(logits[order[i]] - best); sum += w[i]; }
+        for (uint32_t i = 0; i < K; ++i) w[i] = w[i] / sum * gturbo::bf16(L->per_expert_scale[order[i]]);
+    }
+
+    const uint32_t F = std::max(L->ffn_inter, L->moe_inter);
+    std::vector<float> g(F), u(F), act(F), o(D);
+    auto qt = [](const gtref_qt& q) { return view(q.data, q.scales, q.biases, q.rows, q.in_dim, q.bits); };
+    gturbo::matvec(qt(L->sh_gate), dense_x.data(), g.data());
+    gturbo::matvec(qt(L->sh_up), dense_x.data(), u.data());
+    for (uint32_t i = 0; i < L->ffn_inter; ++i) act[i] = gturbo::gelu_tanh(g[i]) * u[i];
+    gturbo::matvec(qt(L->sh_down), act.data(), o.data());
+    gturbo::rms_norm(o.data(), L->w_pf1, D, eps, out->h1);
+
+    float* h2 = out->h2;
+    std::fill(h2, h2 + D, 0.0f);
+    for (uint32_t k = 0; k < K; ++k) {
+        const uint8_t* blk = L->experts + static_cast<uint64_t>(order[k]) * L->expert_stride;
+        auto ex = [&](int role) {
+            const bool down = role == 2;
+            return view(blk + L->sub_off[3 * role], reinterpret_cast<const uint16_t*>(blk + L->sub_off[3 * role + 1]),
+                        reinterpret_cast<const uint16_t*>(blk + L->sub_off[3 * role + 2]),
+                        down ? D : L->moe_inter, down ? L->moe_inter : D, 4);
+        };
+        gturbo::matvec(ex(0), routed_x.data(), g.data());
+        gturbo::matvec(ex(1), routed_x.data(), u.data());
+        for (uint32_t j = 0; j < L->moe_inter; ++j) act[j] = gturbo::gelu_tanh(g[j]) * u[j];
+        gturbo::matvec(ex(2), act.data(), o.data());
+        const float wk = w[k];
+        for (uint32_t j = 0; j < D; ++j) h2[j] += wk * o[j];
+    }
+
+    gturbo::rms_norm(h2, L->w_pf2, D, eps, tmp.data());
+    for (uint32_t i = 0; i < D; ++i) tmp[i] += out->h1[i];
+    gturbo::rms_norm(tmp.data(), L->w_pf, D, eps, o.data());
+    const float ls = gturbo::bf16(L->layer_scalar);
+    for (uint32_t i = 0; i < D; ++i) out->hidden_out[i] = (hidden_in[i] + o[i]) * ls;
+
+    if (out->logits) std::copy(logits.begin(), logits.end(), out->logits);
+    for (uint32_t k = 0; k < K; ++k) {
+        if (out->top_idx) out->top_idx[k] = static_cast<uint32_t>(order[k]);
+        if (out->top_w) out->top_w[k] = w[k];
+    }
+    return 0;
+}
+
+}  // extern "C"
