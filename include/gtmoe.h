@@ -1,0 +1,182 @@
+/*
+ * gtmoe.h -- C ABI of the B200 (sm_100a) MoE block of the Turbo-WinFare engine.
+ *
+ * Plain pointers and sizes only. Every pointer argument named *_dev is a CUDA device pointer;
+ * `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream). Calls are
+ * asynchronous on `stream` unless stated otherwise. All functions return GTM_OK (0) or a
+ * negative gtm_status; gtm_last_error() then holds a message for the calling thread (the
+ * reference's convention, include/gturbo/c_api.h:74-78 and src/c_api.cpp:29-34).
+ *
+ * Replaces, for the MoE path:
+ *   - ComputePipelineManager::dispatch (include/gturbo/pipeline.hpp:97-101, src/pipeline.cpp:409-518)
+ *     for the kernels GemvInt4, GemvInt8, RouterTopK, GeGLU, ScaleAccum, MulBF16, RMSNormK,
+ *     PostAttn and LayerTail: one entry each below, plus gtm_dispatch, which accepts the same
+ *     16 root constants and byte-offset buffer bindings as the HLSL kernels;
+ *   - the per-layer MoE sequence of ForwardRunner::produce_token (src/runner.cpp:549-716),
+ *     i.e. ~48 dispatches and a CPU read-back of the router's top-K per layer, by one fused
+ *     device-resident call (gtm_moe_decode) with all experts resident in HBM.
+ */
+#ifndef GTMOE_H
+#define GTMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GTM_API __attribute__((visibility("default")))
+
+typedef enum gtm_status {
+    GTM_OK = 0,
+    GTM_ERR_INVALID = -1,      /* bad argument: null pointer, zero or inconsistent size     */
+    GTM_ERR_UNSUPPORTED = -2,  /* shape the fused kernels are not built for                  */
+    GTM_ERR_CUDA = -3,         /* a CUDA runtime call failed                                 */
+    GTM_ERR_TIMEOUT = -4,      /* a bounded device-side wait gave up (see gtm_last_error)     */
+    GTM_ERR_WORKSPACE = -5,    /* workspace missing or smaller than *_workspace_bytes()       */
+    GTM_ERR_MISALIGNED = -6    /* pointer or byte offset without the alignment a kernel needs */
+} gtm_status;
+
+/* Message for the last failing call on this thread, "" after a successful one. The pointer
+ * stays valid until the next failing call on the same thread. */
+GTM_API const char* gtm_last_error(void);
+GTM_API const char* gtm_version(void);
+
+/* ---------------------------------------------------------------------------------------
+ * Kernel entry points (the reference's compute kernels, same arithmetic contract).
+ * Quantised matrices use MLX affine 4-/8-bit, group 64 along the input dimension, packed
+ * low nibble first, with bf16 scales and biases laid out [rows][in_dim/64].
+ * ------------------------------------------------------------------------------------- */
+
+/* GemvInt4 (shaders/GemvInt4.hlsl:18-38): out[r] = sum_c (q[r][c]*s + b) * x[c].
+ * Arithmetic is bit-identical to the reference CPU matvec (src/cpu_reference.cpp:55-83). */
+GTM_API int gtm_gemv_q4(uint32_t rows, uint32_t in_dim, const void* w_dev, const uint16_t* s_dev,
+                        const uint16_t* b_dev, const float* x_dev, float* out_dev, void* stream);
+/* GemvInt8 (shaders/GemvInt8.hlsl:13-33), unsigned bytes; bit-identical to
+ * src/cpu_reference.cpp:86-106. */
+GTM_API int gtm_gemv_q8(uint32_t rows, uint32_t in_dim, const void* w_dev, const uint16_t* s_dev,
+                        const uint16_t* b_dev, const float* x_dev, float* out_dev, void* stream);
+/* RouterTopK (shaders/RouterTopK.hlsl:23-68): top-k by (logit desc, index asc), softmax over
+ * the k selected, times bf16 per_expert_scale. k <= 32, num_experts <= 1024. */
+GTM_API int gtm_router_topk(uint32_t num_experts, uint32_t k, const float* logits_dev,
+                            const uint16_t* per_expert_scale_dev, uint32_t* idx_dev,
+                            float* weights_dev, void* stream);
+/* GeGLU (shaders/GeGLU.hlsl:15-28): act = gelu_tanh(gate) * up. */
+GTM_API int gtm_geglu(uint32_t n, const float* gate_dev, const float* up_dev, float* act_dev, void* stream);
+/* ScaleAccum (shaders/ScaleAccum.hlsl:20-35): out = (accumulate ? out : 0) + weights[w_index] * in. */
+GTM_API int gtm_scale_accum(uint32_t n, const float* in_dev, const float* weights_dev, uint32_t w_index,
+                            int accumulate, float* out_dev, void* stream);
+/* MulBF16 (shaders/MulBF16.hlsl:17-30): out = in * bf16(w) * scale. */
+GTM_API int gtm_mul_bf16(uint32_t n, const float* in_dev, const uint16_t* w_dev, float scale,
+                         float* out_dev, void* stream);
+/* RMSNormK (shaders/RMSNormK.hlsl:25-61): out = x / sqrt(mean(x^2) + eps) * [bf16 w].
+ * w_dev may be NULL. The mean of squares is formed exactly as src/cpu_reference.cpp:43-52
+ * (double accumulation), so results are bit-identical with the CPU reference. n <= 65536. */
+GTM_API int gtm_rmsnorm(uint32_t n, const float* x_dev, const uint16_t* w_dev, float eps,
+                        float* out_dev, void* stream);
+/* PostAttn (shaders/PostAttn.hlsl:43-84): hidden_out = hidden + rms(attn)*w_post, then the
+ * three views dense_x = h*w_pre, routed_x = h*w_pre2, router_x = h with h = rms(hidden_out). */
+GTM_API int gtm_post_attn(uint32_t d, const float* attn_dev, const float* hidden_dev,
+                          const uint16_t* w_post_dev, const uint16_t* w_pre_dev, const uint16_t* w_pre2_dev,
+                          float eps, float* hidden_out_dev, float* dense_x_dev, float* routed_x_dev,
+                          float* router_x_dev, void* stream);
+/* LayerTail (shaders/LayerTail.hlsl:39-78):
+ * hidden_out = (hidden + rms(rms(h2)*w_pf2 + h1) * w_pf) * layer_scalar. */
+GTM_API int gtm_layer_tail(uint32_t d, const float* h2_dev, const float* h1_dev, const float* hidden_dev,
+                           const uint16_t* w_pf2_dev, const uint16_t* w_pf_dev, float eps, float layer_scalar,
+                           float* hidden_out_dev, void* stream);
+
+/* Kernel ids for gtm_dispatch, in the order of gturbo::KernelType (include/gturbo/pipeline.hpp:17-33). */
+typedef enum gtm_kernel {
+    GTM_KERNEL_RMSNORMK = 1, GTM_KERNEL_GEMV_INT4 = 2, GTM_KERNEL_GEMV_INT8 = 3,
+    GTM_KERNEL_ROUTER_TOPK = 6, GTM_KERNEL_GEGLU = 7, GTM_KERNEL_POST_ATTN = 8,
+    GTM_KERNEL_LAYER_TAIL = 9, GTM_KERNEL_SCALE_ACCUM = 11, GTM_KERNEL_MUL_BF16 = 12
+} gtm_kernel;
+
+/* Drop-in for ComputePipelineManager::dispatch (src/pipeline.cpp:409-518): the same 16 root
+ * constants (gp0..gp3) each HLSL kernel reads, with srv/uav device buffers bound in the same
+ * slots (t0..t5 / u0..u3) and addressed by the constants' BYTE offsets. grid_x is accepted
+ * for signature parity; the CUDA launch shape is chosen internally. Kernels outside the MoE
+ * path return GTM_ERR_UNSUPPORTED. */
+GTM_API int gtm_dispatch(int kernel, const void* const* srv_dev, int n_srv, void* const* uav_dev, int n_uav,
+                         const uint32_t constants[16], uint32_t grid_x, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Fused MoE block, batch-1 decode (one token through 1..GTM_MAX_LAYERS layers).
+ * ------------------------------------------------------------------------------------- */
+
+#define GTM_MAX_LAYERS 64
+
+/* Byte offsets of one affine-quantised matrix (weight, bf16 scales, bf16 biases). */
+typedef struct GtmQuant {
+    uint64_t weight, scales, biases;
+} GtmQuant;
+
+/* One layer's MoE weights: a resident-tensor base with byte offsets (the resident index's
+ * file_offset / scale_offset / bias_offset, include/gturbo/resident_index.hpp:17-27) and the
+ * layer's packed expert image (packed_experts/layer_NN.bin) with the layout.json expertBlock
+ * offsets (include/gturbo/packed_experts.hpp:34-59). Nothing is re-packed. */
+typedef struct GtmLayer {
+    const void* resident_dev;
+    GtmQuant router;                 /* model.layers.L.router.proj.weight (8-bit)          */
+    uint64_t router_scale;           /* router.scale, bf16[hidden]                          */
+    uint64_t per_expert_scale;       /* router.per_expert_scale, bf16[experts]              */
+    GtmQuant shared_gate, shared_up, shared_down;       /* mlp.{gate,up,down}_proj          */
+    uint64_t pre_ffn_norm;           /* pre_feedforward_layernorm.weight    -> dense_x      */
+    uint64_t pre_ffn_norm_2;         /* pre_feedforward_layernorm_2.weight  -> routed_x     */
+    uint64_t post_ffn_norm_1;        /* post_feedforward_layernorm_1.weight -> h1           */
+    uint64_t post_ffn_norm_2;        /* post_feedforward_layernorm_2.weight (tail, h2)      */
+    uint64_t post_ffn_norm;          /* post_feedforward_layernorm.weight   (tail)          */
+    uint64_t layer_scalar;           /* layer_scalar, bf16[1]                               */
+    const void* experts_dev;         /* expert e at experts_dev + e * expert_stride         */
+    uint64_t expert_stride;
+    GtmQuant expert_gate, expert_up, expert_down;       /* layout.expertBlock offsets       */
+} GtmLayer;
+
+/* Model dimensions. The fused kernels are built for Gemma-4-26B-A4B's MoE shape:
+ * hidden 2816, moe_intermediate 704, ffn_intermediate 2112, 128 experts, top-8, group 64. */
+typedef struct GtmDims {
+    uint32_t hidden, moe_inter, ffn_inter, num_experts, top_k;
+    float eps;
+} GtmDims;
+
+enum {
+    GTM_DECODE_NORM_BETWEEN_LAYERS = 1   /* weightless RMSNorm on the residual after every layer but the last */
+};
+
+typedef struct GtmDecodeIO {
+    const float* hidden_in_dev;      /* [hidden] block input of layer 0                     */
+    float* hidden_out_dev;           /* [hidden] output of the last layer                   */
+    /* Optional per-layer outputs (NULL to skip): */
+    uint32_t* topk_idx_dev;          /* [layers][top_k]                                     */
+    float* topk_w_dev;               /* [layers][top_k]                                     */
+    float* logits_dev;               /* [layers][experts] router logits                      */
+    float* h1_dev;                   /* [layers][hidden] normed shared-expert output         */
+    float* h2_dev;                   /* [layers][hidden] weighted routed-expert sum          */
+    float* hidden_layers_dev;        /* [layers][hidden] residual after each layer (after the
+                                        between-layer norm when that flag is set)            */
+    const float* logit_bias_dev;     /* [layers][experts] added to the router logits before
+                                        selection (benchmark skew knob; NULL = none)         */
+    uint32_t flags;                  /* GTM_DECODE_* */
+} GtmDecodeIO;
+
+/* Workspace needed by gtm_moe_decode (device memory, 256-byte aligned, owned by the caller). */
+GTM_API size_t gtm_moe_decode_workspace_bytes(const GtmDims* dims);
+/* One token through `num_layers` MoE blocks in a single persistent launch: fused router
+ * (int8 GEMV + top-k + softmax, bit-identical logits and indices with the CPU reference),
+ * shared expert, the top-k experts' int4 gate/up + GeGLU and down + weighted combine, and the
+ * layer tail, with no host round trip. Device-side waits are bounded; on timeout the call
+ * returns GTM_ERR_TIMEOUT and the outputs are undefined. Synchronises `stream` only when a
+ * device-side error flag has to be read (it does not otherwise block the host). */
+GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_layers,
+                           const GtmDecodeIO* io, void* workspace_dev, size_t workspace_bytes,
+                           void* stream);
+/* Reads back and clears the device-side error flag of a workspace after gtm_moe_decode
+ * calls (synchronises `stream`). Returns GTM_OK or GTM_ERR_TIMEOUT. */
+GTM_API int gtm_moe_decode_check(void* workspace_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GTMOE_H */

@@ -87,6 +87,7 @@ def lib():
         L.orc_synth_layer_view.argtypes = [C.c_void_p]
         L.orc_synth_layer_ensure.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32]
         L.orc_synth_layer_block.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(BlockOut)]
+        L.orc_synth_layer_route.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_synth_stack.argtypes = [C.POINTER(C.c_void_p), C.c_uint32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.c_void_p]
         _lib = L
@@ -195,9 +196,8 @@ class SynthLayer:
         out = BlockOut(res["hidden"].ctypes.data, res["h1"].ctypes.data, res["h2"].ctypes.data,
                        res["logits"].ctypes.data, res["idx"].ctypes.data, res["w"].ctypes.data)
         if impl == "ref":
-            # route with the oracle first only to learn which experts to materialise
-            probe = self.block(x, lb, rl, impl="oracle")
-            self.ensure(probe["idx"])
+            # route first (views + router only) to learn which experts to materialise
+            lib().orc_synth_layer_route(self.h, _ptr(x), _ptr(lb), _ptr(rl), None)
             ref().gtref_moe_block(self.view(), _ptr(x), _ptr(lb), _ptr(rl), C.byref(out))
         else:
             lib().orc_synth_layer_block(self.h, _ptr(x), _ptr(lb), _ptr(rl), C.byref(out))

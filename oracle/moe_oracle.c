@@ -363,7 +363,13 @@ void orc_synth_layer_ensure(orc_synth_layer* s, const uint32_t* experts, uint32_
 
 int orc_synth_layer_block(orc_synth_layer* s, const float* hidden_in, const float* logit_bias,
                           const float* route_logits, const orc_block_out* out) {
-    /* Route first (cheap) to learn which experts to materialise, then run the block. */
+    orc_synth_layer_route(s, hidden_in, logit_bias, route_logits, NULL);
+    return orc_moe_block(&s->view, hidden_in, logit_bias, route_logits, out);
+}
+
+/* Views, router and top-k only (no expert work); materialises the selected experts. */
+void orc_synth_layer_route(orc_synth_layer* s, const float* hidden_in, const float* logit_bias,
+                           const float* route_logits, uint32_t* idx_out) {
     const uint32_t D = s->hidden, E = s->experts, K = s->top_k;
     float* tmp = (float*)malloc(sizeof(float) * D);
     float* rin = (float*)malloc(sizeof(float) * D);
@@ -378,8 +384,8 @@ int orc_synth_layer_block(orc_synth_layer* s, const float* hidden_in, const floa
     if (logit_bias) for (uint32_t e = 0; e < E; ++e) logits[e] = logits[e] + logit_bias[e];
     orc_topk(logits, E, K, s->view.per_expert_scale, idx, w);
     orc_synth_layer_ensure(s, idx, K);
+    if (idx_out) memcpy(idx_out, idx, sizeof(uint32_t) * K);
     free(tmp); free(rin); free(logits); free(idx); free(w);
-    return orc_moe_block(&s->view, hidden_in, logit_bias, route_logits, out);
 }
 
 int orc_synth_stack(orc_synth_layer** layers, uint32_t n, const float* hidden_in,

@@ -87,6 +87,9 @@ void orc_synth_layer_destroy(orc_synth_layer* s);
 /* The layer's weight view, and on-demand generation of the given experts. */
 const orc_layer* orc_synth_layer_view(const orc_synth_layer* s);
 void orc_synth_layer_ensure(orc_synth_layer* s, const uint32_t* experts, uint32_t n);
+/* Views, router and top-k only; generates the selected experts. idx_out may be NULL. */
+void orc_synth_layer_route(orc_synth_layer* s, const float* hidden_in, const float* logit_bias,
+                           const float* route_logits, uint32_t* idx_out);
 /* Runs the block; generates the selected experts first. */
 int orc_synth_layer_block(orc_synth_layer* s, const float* hidden_in, const float* logit_bias,
                           const float* route_logits, const orc_block_out* out);

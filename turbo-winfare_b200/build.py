@@ -1,0 +1,54 @@
+"""Builds libgtmoe.so (the C-ABI library with the sm_100a kernels) in-tree with nvcc.
+
+    python turbo-winfare_b200/build.py [--verbose]
+
+The library is written next to this file so it travels with the source tree; nothing is
+installed or JIT-compiled at import time.
+"""
+from __future__ import annotations
+
+import glob
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB = os.path.join(HERE, "libgtmoe.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared",
+         "-I", os.path.join(ROOT, "include")]
+
+
+def sources() -> list[str]:
+    return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")))
+
+
+def deps() -> list[str]:
+    return sources() + sorted(glob.glob(os.path.join(HERE, "csrc", "*.h*"))) + \
+        sorted(glob.glob(os.path.join(HERE, "csrc", "*.cuh"))) + [os.path.join(ROOT, "include", "gtmoe.h")]
+
+
+def up_to_date() -> bool:
+    if not os.path.exists(LIB):
+        return False
+    t = os.path.getmtime(LIB)
+    return all(os.path.getmtime(p) <= t for p in deps() if os.path.exists(p))
+
+
+def build(verbose: bool = False, force: bool = False) -> str:
+    if not force and up_to_date():
+        return LIB
+    cmd = [NVCC, *ARCH, *FLAGS, "-o", LIB + ".tmp", *sources()]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd))
+    subprocess.check_call(cmd)
+    os.replace(LIB + ".tmp", LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(verbose="--verbose" in sys.argv, force=True)
+    print(LIB)

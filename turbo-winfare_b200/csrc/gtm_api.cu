@@ -1,0 +1,251 @@
+// C ABI of libgtmoe (include/gtmoe.h): argument validation, error reporting and launches.
+// Errors never escape as exceptions; they become a gtm_status plus a thread-local message,
+// as src/c_api.cpp:29-34 does for the reference's C API.
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <cuda_runtime.h>
+
+#include "gtm_internal.h"
+
+namespace gtm {
+
+constexpr uint32_t kGroup = 64;
+
+static thread_local char g_err[512] = "";
+
+int set_error(int status, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return status;
+}
+int set_cuda_error(const char* what, cudaError_t e) {
+    return set_error(GTM_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+void clear_error() { g_err[0] = '\0'; }
+
+static int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error(what, e);
+    clear_error();
+    return GTM_OK;
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace gtm
+
+using namespace gtm;
+
+extern "C" {
+
+GTM_API const char* gtm_last_error(void) { return g_err; }
+GTM_API const char* gtm_version(void) { return "gtmoe 0.1 (sm_100a)"; }
+
+static int gemv_common(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
+                       const float* x, float* out, uint32_t row_begin, uint32_t row_end, void* stream,
+                       const char* name) {
+    if (!w || !s || !b || !x || !out) return set_error(GTM_ERR_INVALID, "%s: null pointer", name);
+    if (rows == 0 || in_dim == 0 || in_dim % kGroup != 0)
+        return set_error(GTM_ERR_INVALID, "%s: rows=%u in_dim=%u (in_dim must be a positive multiple of 64)", name,
+                         rows, in_dim);
+    if (in_dim / kGroup > 1024) return set_error(GTM_ERR_UNSUPPORTED, "%s: in_dim %u > 65536", name, in_dim);
+    if (!aligned(w, 16) || !aligned(s, 2) || !aligned(b, 2) || !aligned(x, 4) || !aligned(out, 4))
+        return set_error(GTM_ERR_MISALIGNED, "%s: weights need 16-byte alignment", name);
+    if (row_begin >= row_end) { clear_error(); return GTM_OK; }
+    k_gemv_exact(bits, rows, in_dim, w, s, b, x, out, row_begin, row_end, (cudaStream_t)stream);
+    return check_launch(name);
+}
+
+GTM_API int gtm_gemv_q4(uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
+                        const float* x, float* out, void* stream) {
+    return gemv_common(4, rows, in_dim, w, s, b, x, out, 0, rows, stream, "gtm_gemv_q4");
+}
+GTM_API int gtm_gemv_q8(uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
+                        const float* x, float* out, void* stream) {
+    return gemv_common(8, rows, in_dim, w, s, b, x, out, 0, rows, stream, "gtm_gemv_q8");
+}
+
+GTM_API int gtm_router_topk(uint32_t n, uint32_t k, const float* logits, const uint16_t* pes, uint32_t* idx,
+                            float* w, void* stream) {
+    if (!logits || !pes || !idx || !w) return set_error(GTM_ERR_INVALID, "gtm_router_topk: null pointer");
+    if (n == 0 || n > 1024 || k == 0 || k > 32 || k > n)
+        return set_error(GTM_ERR_INVALID, "gtm_router_topk: num_experts=%u k=%u (need 1 <= k <= min(32, n), n <= 1024)",
+                         n, k);
+    k_router_topk(n, k, logits, pes, idx, w, (cudaStream_t)stream);
+    return check_launch("gtm_router_topk");
+}
+
+GTM_API int gtm_geglu(uint32_t n, const float* g, const float* u, float* out, void* stream) {
+    if (!g || !u || !out) return set_error(GTM_ERR_INVALID, "gtm_geglu: null pointer");
+    if (n == 0) { clear_error(); return GTM_OK; }
+    k_geglu(n, g, u, out, (cudaStream_t)stream);
+    return check_launch("gtm_geglu");
+}
+
+GTM_API int gtm_scale_accum(uint32_t n, const float* in, const float* w, uint32_t wi, int acc, float* out,
+                            void* stream) {
+    if (!in || !w || !out) return set_error(GTM_ERR_INVALID, "gtm_scale_accum: null pointer");
+    if (n == 0) { clear_error(); return GTM_OK; }
+    k_scale_accum(n, in, w, wi, acc, out, (cudaStream_t)stream);
+    return check_launch("gtm_scale_accum");
+}
+
+GTM_API int gtm_mul_bf16(uint32_t n, const float* in, const uint16_t* w, float scale, float* out, void* stream) {
+    if (!in || !w || !out) return set_error(GTM_ERR_INVALID, "gtm_mul_bf16: null pointer");
+    if (n == 0) { clear_error(); return GTM_OK; }
+    k_mul_bf16(n, in, w, scale, out, (cudaStream_t)stream);
+    return check_launch("gtm_mul_bf16");
+}
+
+GTM_API int gtm_rmsnorm(uint32_t n, const float* x, const uint16_t* w, float eps, float* out, void* stream) {
+    if (!x || !out) return set_error(GTM_ERR_INVALID, "gtm_rmsnorm: null pointer");
+    if (n == 0 || n > kMaxNormDim) return set_error(GTM_ERR_INVALID, "gtm_rmsnorm: n=%u (1..%u)", n, kMaxNormDim);
+    k_rmsnorm(n, x, w, eps, out, (cudaStream_t)stream);
+    return check_launch("gtm_rmsnorm");
+}
+
+GTM_API int gtm_post_attn(uint32_t d, const float* attn, const float* hidden, const uint16_t* wpost,
+                          const uint16_t* wpre, const uint16_t* wpre2, float eps, float* hout, float* dense,
+                          float* routed, float* router, void* stream) {
+    if (!attn || !hidden || !wpost || !wpre || !wpre2 || !hout || !dense || !routed || !router)
+        return set_error(GTM_ERR_INVALID, "gtm_post_attn: null pointer");
+    if (d == 0 || d > kMaxNormDim / 2) return set_error(GTM_ERR_INVALID, "gtm_post_attn: d=%u (1..%u)", d, kMaxNormDim / 2);
+    k_post_attn(d, attn, hidden, wpost, wpre, wpre2, eps, hout, dense, routed, router, (cudaStream_t)stream);
+    return check_launch("gtm_post_attn");
+}
+
+GTM_API int gtm_layer_tail(uint32_t d, const float* h2, const float* h1, const float* hidden, const uint16_t* wpf2,
+                           const uint16_t* wpf, float eps, float ls, float* hout, void* stream) {
+    if (!h2 || !h1 || !hidden || !wpf2 || !wpf || !hout) return set_error(GTM_ERR_INVALID, "gtm_layer_tail: null pointer");
+    if (d == 0 || d > kMaxNormDim / 2) return set_error(GTM_ERR_INVALID, "gtm_layer_tail: d=%u (1..%u)", d, kMaxNormDim / 2);
+    k_layer_tail(d, h2, h1, hidden, wpf2, wpf, eps, ls, hout, (cudaStream_t)stream);
+    return check_launch("gtm_layer_tail");
+}
+
+// ---- gtm_dispatch: the reference's root-constant convention ------------------------------------
+static float f_of(uint32_t bits) { float f; memcpy(&f, &bits, 4); return f; }
+
+GTM_API int gtm_dispatch(int kernel, const void* const* srv, int n_srv, void* const* uav, int n_uav,
+                         const uint32_t c[16], uint32_t grid_x, void* stream) {
+    if (!c) return set_error(GTM_ERR_INVALID, "gtm_dispatch: constants are NULL");
+    auto in = [&](int i, uint32_t off) -> const unsigned char* {
+        return (i < n_srv && srv && srv[i]) ? static_cast<const unsigned char*>(srv[i]) + off : nullptr;
+    };
+    auto outp = [&](int i, uint32_t off) -> unsigned char* {
+        return (i < n_uav && uav && uav[i]) ? static_cast<unsigned char*>(uav[i]) + off : nullptr;
+    };
+    switch (kernel) {
+        case GTM_KERNEL_GEMV_INT4:
+        case GTM_KERNEL_GEMV_INT8: {
+            // gp0 = (rows, in_dim, w_off, s_off)  gp1 = (b_off, x_off, out_off, row_base)  (GemvInt4.hlsl:9-10)
+            const uint32_t rows = c[0], in_dim = c[1], row_base = c[7];
+            const uint32_t end = rows < row_base + grid_x ? rows : row_base + grid_x;
+            const unsigned char* o = outp(0, c[6]);
+            return gemv_common(kernel == GTM_KERNEL_GEMV_INT4 ? 4 : 8, rows, in_dim, in(0, c[2]),
+                               reinterpret_cast<const uint16_t*>(in(1, c[3])), reinterpret_cast<const uint16_t*>(in(2, c[4])),
+                               reinterpret_cast<const float*>(in(3, c[5])), (float*)o, row_base, end, stream,
+                               "gtm_dispatch(GemvInt)");
+        }
+        case GTM_KERNEL_RMSNORMK:   // gp0 = (n, x_off, w_off, out_off)  gp1 = (has_weight, eps_bits)
+            return gtm_rmsnorm(c[0], reinterpret_cast<const float*>(in(0, c[1])),
+                               c[4] ? reinterpret_cast<const uint16_t*>(in(1, c[2])) : nullptr, f_of(c[5]),
+                               reinterpret_cast<float*>(outp(0, c[3])), stream);
+        case GTM_KERNEL_ROUTER_TOPK: {  // gp0 = (num_experts, K, logits_off, scale_off)  gp1 = (idx_off, wgt_off)
+            const uint32_t k = c[1] < 8 ? c[1] : 8;   // the shader's MAX_TOPK
+            return gtm_router_topk(c[0], k, reinterpret_cast<const float*>(in(0, c[2])),
+                                   reinterpret_cast<const uint16_t*>(in(1, c[3])), reinterpret_cast<uint32_t*>(outp(0, c[4])),
+                                   reinterpret_cast<float*>(outp(1, c[5])), stream);
+        }
+        case GTM_KERNEL_GEGLU:      // gp0 = (n, gate_off, up_off, out_off)
+            return gtm_geglu(c[0], reinterpret_cast<const float*>(in(0, c[1])), reinterpret_cast<const float*>(in(1, c[2])),
+                             reinterpret_cast<float*>(outp(0, c[3])), stream);
+        case GTM_KERNEL_SCALE_ACCUM:  // gp0 = (n, in_off, out_off, w_off)  gp1 = (accumulate, weight_index)
+            return gtm_scale_accum(c[0], reinterpret_cast<const float*>(in(0, c[1])),
+                                   reinterpret_cast<const float*>(in(1, c[3])), c[5], c[4] != 0,
+                                   reinterpret_cast<float*>(outp(0, c[2])), stream);
+        case GTM_KERNEL_MUL_BF16:   // gp0 = (n, in_off, w_off, out_off)  gp1 = (scale_bits)
+            return gtm_mul_bf16(c[0], reinterpret_cast<const float*>(in(0, c[1])),
+                                reinterpret_cast<const uint16_t*>(in(1, c[2])), f_of(c[4]),
+                                reinterpret_cast<float*>(outp(0, c[3])), stream);
+        case GTM_KERNEL_POST_ATTN:  // gp0 = (D, attn, hidden, out_hidden) gp1 = (eps, w_post, w_pre, w_pre2) gp2 = (dense, routed, router)
+            return gtm_post_attn(c[0], reinterpret_cast<const float*>(in(0, c[1])), reinterpret_cast<const float*>(in(1, c[2])),
+                                 reinterpret_cast<const uint16_t*>(in(2, c[5])), reinterpret_cast<const uint16_t*>(in(3, c[6])),
+                                 reinterpret_cast<const uint16_t*>(in(4, c[7])), f_of(c[4]),
+                                 reinterpret_cast<float*>(outp(0, c[3])), reinterpret_cast<float*>(outp(1, c[8])),
+                                 reinterpret_cast<float*>(outp(2, c[9])), reinterpret_cast<float*>(outp(3, c[10])), stream);
+        case GTM_KERNEL_LAYER_TAIL:  // gp0 = (D, h2, h1, hidden) gp1 = (eps, w_pf2, w_pf, out) gp2 = (layer_scalar_bits, scratch)
+            return gtm_layer_tail(c[0], reinterpret_cast<const float*>(in(0, c[1])), reinterpret_cast<const float*>(in(1, c[2])),
+                                  reinterpret_cast<const float*>(in(2, c[3])), reinterpret_cast<const uint16_t*>(in(3, c[5])),
+                                  reinterpret_cast<const uint16_t*>(in(4, c[6])), f_of(c[4]), f_of(c[8]),
+                                  reinterpret_cast<float*>(outp(0, c[7])), stream);
+        default:
+            return set_error(GTM_ERR_UNSUPPORTED, "gtm_dispatch: kernel %d is not on the MoE path", kernel);
+    }
+}
+
+// ---- fused decode ---------------------------------------------------------------------------------
+static bool dims_supported(const GtmDims* d) {
+    return d->hidden == 2816 && d->moe_inter == 704 && d->ffn_inter == 2112 && d->num_experts == 128 && d->top_k == 8;
+}
+
+GTM_API size_t gtm_moe_decode_workspace_bytes(const GtmDims* dims) {
+    if (!dims || !dims_supported(dims)) return 0;
+    return decode_workspace_bytes();
+}
+
+GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_layers, const GtmDecodeIO* io,
+                           void* ws, size_t ws_bytes, void* stream) {
+    if (!dims || !layers || !io) return set_error(GTM_ERR_INVALID, "gtm_moe_decode: null argument");
+    if (!dims_supported(dims))
+        return set_error(GTM_ERR_UNSUPPORTED,
+                         "gtm_moe_decode: built for hidden 2816, moe 704, ffn 2112, 128 experts, top-8 (got %u/%u/%u/%u/%u)",
+                         dims->hidden, dims->moe_inter, dims->ffn_inter, dims->num_experts, dims->top_k);
+    if (num_layers < 1 || num_layers > GTM_MAX_LAYERS)
+        return set_error(GTM_ERR_INVALID, "gtm_moe_decode: num_layers=%d (1..%d)", num_layers, GTM_MAX_LAYERS);
+    if (!io->hidden_in_dev || !io->hidden_out_dev) return set_error(GTM_ERR_INVALID, "gtm_moe_decode: hidden in/out NULL");
+    if (!ws || ws_bytes < decode_workspace_bytes() || !aligned(ws, 256))
+        return set_error(GTM_ERR_WORKSPACE, "gtm_moe_decode: workspace needs %zu bytes, 256-byte aligned",
+                         decode_workspace_bytes());
+    for (int l = 0; l < num_layers; ++l) {
+        const GtmLayer& L = layers[l];
+        if (!L.resident_dev || !L.experts_dev || L.expert_stride == 0)
+            return set_error(GTM_ERR_INVALID, "gtm_moe_decode: layer %d has a null base or zero stride", l);
+        const uint64_t offs16[] = {L.router.weight, L.expert_stride, L.expert_gate.weight, L.expert_up.weight,
+                                   L.expert_down.weight, L.shared_gate.weight, L.shared_up.weight, L.shared_down.weight};
+        if (!aligned(L.resident_dev, 16) || !aligned(L.experts_dev, 16))
+            return set_error(GTM_ERR_MISALIGNED, "gtm_moe_decode: layer %d base pointers must be 16-byte aligned", l);
+        for (uint64_t o : offs16)
+            if (o % 16) return set_error(GTM_ERR_MISALIGNED, "gtm_moe_decode: layer %d weight offset %llu not 16-byte aligned",
+                                         l, (unsigned long long)o);
+    }
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: device query", e);
+    const int ctas = sms < 256 ? sms : 256;
+    int rc = launch_decode(*dims, layers, num_layers, *io, ws, ws_bytes, (cudaStream_t)stream, ctas);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_decode_check(void* ws, void* stream) {
+    if (!ws) return set_error(GTM_ERR_INVALID, "gtm_moe_decode_check: null workspace");
+    int flag = 0;
+    cudaError_t e = cudaMemcpyAsync(&flag, static_cast<char*>(ws) + 1024, sizeof(int), cudaMemcpyDeviceToHost,
+                                    (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode_check", e);
+    if (flag != 0) {
+        int zero = 0;
+        cudaMemcpy(static_cast<char*>(ws) + 1024, &zero, sizeof(int), cudaMemcpyHostToDevice);
+        return set_error(GTM_ERR_TIMEOUT, "gtm_moe_decode: a grid barrier wait timed out (device flag %d)", flag);
+    }
+    clear_error();
+    return GTM_OK;
+}
+
+}  // extern "C"

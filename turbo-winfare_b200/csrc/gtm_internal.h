@@ -1,0 +1,36 @@
+// Internal declarations shared by the .cu translation units of libgtmoe.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+
+#include "../../include/gtmoe.h"
+
+namespace gtm {
+
+int set_error(int status, const char* fmt, ...);
+int set_cuda_error(const char* what, cudaError_t e);
+void clear_error();
+
+size_t decode_workspace_bytes();
+int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, const GtmDecodeIO& io,
+                  void* ws, size_t ws_bytes, cudaStream_t stream, int num_ctas);
+
+// generic kernels (gtm_kernels.cu); arguments already validated
+void k_gemv_exact(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
+                  const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st);
+void k_router_topk(uint32_t n, uint32_t k, const float* logits, const uint16_t* pes, uint32_t* idx, float* w,
+                   cudaStream_t st);
+void k_geglu(uint32_t n, const float* g, const float* u, float* out, cudaStream_t st);
+void k_scale_accum(uint32_t n, const float* in, const float* w, uint32_t wi, int acc, float* out, cudaStream_t st);
+void k_mul_bf16(uint32_t n, const float* in, const uint16_t* w, float scale, float* out, cudaStream_t st);
+void k_rmsnorm(uint32_t n, const float* x, const uint16_t* w, float eps, float* out, cudaStream_t st);
+void k_post_attn(uint32_t d, const float* attn, const float* hidden, const uint16_t* wpost, const uint16_t* wpre,
+                 const uint16_t* wpre2, float eps, float* hout, float* dense, float* routed, float* router,
+                 cudaStream_t st);
+void k_layer_tail(uint32_t d, const float* h2, const float* h1, const float* hidden, const uint16_t* wpf2,
+                  const uint16_t* wpf, float eps, float ls, float* hout, cudaStream_t st);
+
+constexpr uint32_t kMaxNormDim = 16384;   // vectors normalised in one CTA's shared memory
+
+}  // namespace gtm

@@ -1,0 +1,252 @@
+"""Host side of the B200 MoE block: ctypes bindings to libgtmoe.so (include/gtmoe.h).
+
+PyTorch is used only for device memory and streams; every computation goes through the C ABI
+and the sm_100a kernels in libgtmoe.so. There is no fallback: if the library or a CUDA device
+is missing, calls raise.
+
+The classes mirror the reference's MoE section of ForwardRunner::produce_token
+(src/runner.cpp:549-716) for the batch-1 decode path, with all experts resident in HBM:
+
+* ``SynthModel`` -- random-init weights of the Gemma-4-26B-A4B MoE shape in the .gturbo byte
+  layouts (per-layer expert image + resident tensors), generated on the device;
+* ``Decoder`` -- one token through N MoE layers in one fused launch (gtm_moe_decode).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+LIB_PATH = os.path.join(PKG, "libgtmoe.so")
+
+HIDDEN, MOE_INTER, FFN, EXPERTS, TOP_K, EPS = 2816, 704, 2112, 128, 8, 1e-6
+MAX_LAYERS = 64
+NORM_BETWEEN_LAYERS = 1
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE, ERR_MISALIGNED = 0, -1, -2, -3, -4, -5, -6
+
+KERNEL_RMSNORMK, KERNEL_GEMV_INT4, KERNEL_GEMV_INT8 = 1, 2, 3
+KERNEL_ROUTER_TOPK, KERNEL_GEGLU, KERNEL_POST_ATTN, KERNEL_LAYER_TAIL = 6, 7, 8, 9
+KERNEL_SCALE_ACCUM, KERNEL_MUL_BF16 = 11, 12
+
+
+class GtmError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"[{status}] {msg}")
+        self.status = status
+
+
+class Quant(C.Structure):
+    _fields_ = [("weight", C.c_uint64), ("scales", C.c_uint64), ("biases", C.c_uint64)]
+
+
+class Layer(C.Structure):
+    _fields_ = [("resident_dev", C.c_void_p), ("router", Quant), ("router_scale", C.c_uint64),
+                ("per_expert_scale", C.c_uint64), ("shared_gate", Quant), ("shared_up", Quant),
+                ("shared_down", Quant), ("pre_ffn_norm", C.c_uint64), ("pre_ffn_norm_2", C.c_uint64),
+                ("post_ffn_norm_1", C.c_uint64), ("post_ffn_norm_2", C.c_uint64), ("post_ffn_norm", C.c_uint64),
+                ("layer_scalar", C.c_uint64), ("experts_dev", C.c_void_p), ("expert_stride", C.c_uint64),
+                ("expert_gate", Quant), ("expert_up", Quant), ("expert_down", Quant)]
+
+
+class Dims(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("moe_inter", C.c_uint32), ("ffn_inter", C.c_uint32),
+                ("num_experts", C.c_uint32), ("top_k", C.c_uint32), ("eps", C.c_float)]
+
+
+class DecodeIO(C.Structure):
+    _fields_ = [("hidden_in_dev", C.c_void_p), ("hidden_out_dev", C.c_void_p), ("topk_idx_dev", C.c_void_p),
+                ("topk_w_dev", C.c_void_p), ("logits_dev", C.c_void_p), ("h1_dev", C.c_void_p),
+                ("h2_dev", C.c_void_p), ("hidden_layers_dev", C.c_void_p), ("logit_bias_dev", C.c_void_p),
+                ("flags", C.c_uint32)]
+
+
+_lib = None
+
+# (name, restype, argtypes) for every entry point in include/gtmoe.h and include/gtmoe_synth.h
+_P, _U32, _U64, _I, _F, _SZ = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_size_t
+SIGNATURES = {
+    "gtm_last_error": (C.c_char_p, []),
+    "gtm_version": (C.c_char_p, []),
+    "gtm_gemv_q4": (_I, [_U32, _U32, _P, _P, _P, _P, _P, _P]),
+    "gtm_gemv_q8": (_I, [_U32, _U32, _P, _P, _P, _P, _P, _P]),
+    "gtm_router_topk": (_I, [_U32, _U32, _P, _P, _P, _P, _P]),
+    "gtm_geglu": (_I, [_U32, _P, _P, _P, _P]),
+    "gtm_scale_accum": (_I, [_U32, _P, _P, _U32, _I, _P, _P]),
+    "gtm_mul_bf16": (_I, [_U32, _P, _P, _F, _P, _P]),
+    "gtm_rmsnorm": (_I, [_U32, _P, _P, _F, _P, _P]),
+    "gtm_post_attn": (_I, [_U32, _P, _P, _P, _P, _P, _F, _P, _P, _P, _P, _P]),
+    "gtm_layer_tail": (_I, [_U32, _P, _P, _P, _P, _P, _F, _F, _P, _P]),
+    "gtm_dispatch": (_I, [_I, C.POINTER(_P), _I, C.POINTER(_P), _I, C.POINTER(_U32), _U32, _P]),
+    "gtm_moe_decode_workspace_bytes": (_SZ, [C.POINTER(Dims)]),
+    "gtm_moe_decode": (_I, [C.POINTER(Dims), C.POINTER(Layer), _I, C.POINTER(DecodeIO), _P, _SZ, _P]),
+    "gtm_moe_decode_check": (_I, [_P, _P]),
+    "gtm_synth_expert_layout": (_I, [_U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
+    "gtm_synth_resident_layout": (_I, [_U32, _U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
+    "gtm_synth_experts": (_I, [_U64, _U32, _U32, _U32, _U32, _U32, _P, _P]),
+    "gtm_synth_resident": (_I, [_U64, _U32, _U32, _U32, _U32, _P, _P]),
+    "gtm_synth_x": (_I, [_U64, _U32, _U32, _U32, _P, _P]),
+    "gtm_synth_layer_desc": (_I, [_U32, _U32, _U32, _U32, _P, _P, C.POINTER(Layer)]),
+}
+
+
+def lib():
+    """Loads libgtmoe.so. Raises if it has not been built -- there is no fallback path."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"libgtmoe.so not built at {LIB_PATH}; run python turbo-winfare_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().gtm_last_error().decode()
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        raise GtmError(rc, last_error())
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def ptr(t) -> C.c_void_p | None:
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def default_dims() -> Dims:
+    return Dims(HIDDEN, MOE_INTER, FFN, EXPERTS, TOP_K, EPS)
+
+
+# ---- single kernels (the reference's dispatch set) ----------------------------------------------
+
+def gemv_q4(w, s, b, x, out, rows: int, in_dim: int, stream=None):
+    check(lib().gtm_gemv_q4(rows, in_dim, ptr(w), ptr(s), ptr(b), ptr(x), ptr(out), _stream(stream)))
+
+
+def gemv_q8(w, s, b, x, out, rows: int, in_dim: int, stream=None):
+    check(lib().gtm_gemv_q8(rows, in_dim, ptr(w), ptr(s), ptr(b), ptr(x), ptr(out), _stream(stream)))
+
+
+def router_topk(logits, pes, idx, w, k: int, stream=None):
+    check(lib().gtm_router_topk(logits.numel(), k, ptr(logits), ptr(pes), ptr(idx), ptr(w), _stream(stream)))
+
+
+def geglu(g, u, out, stream=None):
+    check(lib().gtm_geglu(g.numel(), ptr(g), ptr(u), ptr(out), _stream(stream)))
+
+
+def scale_accum(inp, weights, w_index: int, accumulate: bool, out, stream=None):
+    check(lib().gtm_scale_accum(inp.numel(), ptr(inp), ptr(weights), w_index, int(accumulate), ptr(out), _stream(stream)))
+
+
+def mul_bf16(inp, w, scale: float, out, stream=None):
+    check(lib().gtm_mul_bf16(inp.numel(), ptr(inp), ptr(w), scale, ptr(out), _stream(stream)))
+
+
+def rmsnorm(x, w, eps: float, out, stream=None):
+    check(lib().gtm_rmsnorm(x.numel(), ptr(x), ptr(w), eps, ptr(out), _stream(stream)))
+
+
+def post_attn(attn, hidden, w_post, w_pre, w_pre2, eps, hidden_out, dense, routed, router, stream=None):
+    check(lib().gtm_post_attn(attn.numel(), ptr(attn), ptr(hidden), ptr(w_post), ptr(w_pre), ptr(w_pre2), eps,
+                              ptr(hidden_out), ptr(dense), ptr(routed), ptr(router), _stream(stream)))
+
+
+def layer_tail(h2, h1, hidden, w_pf2, w_pf, eps, layer_scalar, hidden_out, stream=None):
+    check(lib().gtm_layer_tail(h2.numel(), ptr(h2), ptr(h1), ptr(hidden), ptr(w_pf2), ptr(w_pf), eps, layer_scalar,
+                               ptr(hidden_out), _stream(stream)))
+
+
+def dispatch(kernel: int, srvs, uavs, constants, grid_x: int = 1, stream=None):
+    """gtm_dispatch: the reference's (srv, uav, 16 root constants) convention."""
+    srv = (C.c_void_p * max(1, len(srvs)))(*[t.data_ptr() for t in srvs])
+    uav = (C.c_void_p * max(1, len(uavs)))(*[t.data_ptr() for t in uavs])
+    c = (C.c_uint32 * 16)(*(list(constants) + [0] * (16 - len(constants))))
+    check(lib().gtm_dispatch(kernel, srv, len(srvs), uav, len(uavs), c, grid_x, _stream(stream)))
+
+
+# ---- synthetic model --------------------------------------------------------------------------
+
+def expert_layout(hidden=HIDDEN, inter=MOE_INTER):
+    off = (C.c_uint64 * 9)()
+    stride = C.c_uint64()
+    check(lib().gtm_synth_expert_layout(hidden, inter, off, C.byref(stride)))
+    return list(off), stride.value
+
+
+def resident_layout(hidden=HIDDEN, ffn=FFN, experts=EXPERTS):
+    off = (C.c_uint64 * 20)()
+    total = C.c_uint64()
+    check(lib().gtm_synth_resident_layout(hidden, ffn, experts, off, C.byref(total)))
+    return list(off), total.value
+
+
+class SynthModel:
+    """`num_layers` random-init MoE layers resident in HBM in the .gturbo byte layouts."""
+
+    def __init__(self, num_layers: int, seed: int = 0, device: str = "cuda", stream=None):
+        import torch
+        self.num_layers, self.seed = num_layers, seed
+        _, stride = expert_layout()
+        _, rtotal = resident_layout()
+        self.expert_stride = stride
+        self.resident = []
+        self.experts = []
+        self.layers = (Layer * num_layers)()
+        for l in range(num_layers):
+            r = torch.empty(rtotal, dtype=torch.uint8, device=device)
+            e = torch.empty(EXPERTS * stride, dtype=torch.uint8, device=device)
+            check(lib().gtm_synth_resident(seed, l, HIDDEN, FFN, EXPERTS, ptr(r), _stream(stream)))
+            check(lib().gtm_synth_experts(seed, l, HIDDEN, MOE_INTER, 0, EXPERTS, ptr(e), _stream(stream)))
+            check(lib().gtm_synth_layer_desc(HIDDEN, MOE_INTER, FFN, EXPERTS, ptr(r), ptr(e), C.byref(self.layers[l])))
+            self.resident.append(r)
+            self.experts.append(e)
+
+    def weight_bytes(self) -> int:
+        return sum(t.numel() for t in self.resident) + sum(t.numel() for t in self.experts)
+
+
+def synth_x(seed: int, token0: int, count: int, out, stream=None):
+    check(lib().gtm_synth_x(seed, token0, count, HIDDEN, ptr(out), _stream(stream)))
+
+
+class Decoder:
+    """Batch-1 decode through a stack of MoE layers: one fused launch per token."""
+
+    def __init__(self, layers, num_layers: int | None = None, device: str = "cuda"):
+        import torch
+        self.layers = layers
+        self.num_layers = num_layers if num_layers is not None else len(layers)
+        self.dims = default_dims()
+        n = lib().gtm_moe_decode_workspace_bytes(C.byref(self.dims))
+        if n == 0:
+            raise GtmError(ERR_UNSUPPORTED, "decode workspace size query failed")
+        self.workspace = torch.empty(n + 256, dtype=torch.uint8, device=device)
+        base = self.workspace.data_ptr()
+        self.ws_ptr = C.c_void_p((base + 255) // 256 * 256)
+        self.ws_bytes = n
+
+    def __call__(self, hidden_in, hidden_out, *, topk_idx=None, topk_w=None, logits=None, h1=None, h2=None,
+                 hidden_layers=None, logit_bias=None, norm_between_layers=True, stream=None, first_layer: int = 0,
+                 num_layers: int | None = None):
+        n = num_layers if num_layers is not None else self.num_layers
+        layer_arr = C.cast(C.addressof(self.layers) + first_layer * C.sizeof(Layer), C.POINTER(Layer))
+        io = DecodeIO(hidden_in.data_ptr(), hidden_out.data_ptr(), ptr(topk_idx), ptr(topk_w), ptr(logits), ptr(h1),
+                      ptr(h2), ptr(hidden_layers), ptr(logit_bias), NORM_BETWEEN_LAYERS if norm_between_layers else 0)
+        check(lib().gtm_moe_decode(C.byref(self.dims), layer_arr, n, C.byref(io), self.ws_ptr, self.ws_bytes,
+                                   _stream(stream)))
+
+    def check(self, stream=None):
+        check(lib().gtm_moe_decode_check(self.ws_ptr, _stream(stream)))
