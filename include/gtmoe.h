@@ -161,14 +161,16 @@ typedef struct GtmDecodeIO {
     uint32_t flags;                  /* GTM_DECODE_* */
 } GtmDecodeIO;
 
-/* Workspace needed by gtm_moe_decode (device memory, 256-byte aligned, owned by the caller). */
+/* Workspace needed by gtm_moe_decode (device memory, 256-byte aligned, owned by the caller).
+ * Zero it once before its first use (cudaMemset); calls keep it consistent afterwards. A
+ * workspace serves one stream at a time. Returns 0 for unsupported dims. */
 GTM_API size_t gtm_moe_decode_workspace_bytes(const GtmDims* dims);
 /* One token through `num_layers` MoE blocks in a single persistent launch: fused router
  * (int8 GEMV + top-k + softmax, bit-identical logits and indices with the CPU reference),
  * shared expert, the top-k experts' int4 gate/up + GeGLU and down + weighted combine, and the
- * layer tail, with no host round trip. Device-side waits are bounded; on timeout the call
- * returns GTM_ERR_TIMEOUT and the outputs are undefined. Synchronises `stream` only when a
- * device-side error flag has to be read (it does not otherwise block the host). */
+ * layer tail, with no host round trip. Asynchronous: the call validates, launches and returns.
+ * Device-side waits are bounded (2 s per grid barrier); a wait that gives up leaves the
+ * outputs undefined and is reported by the next gtm_moe_decode_check on the workspace. */
 GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_layers,
                            const GtmDecodeIO* io, void* workspace_dev, size_t workspace_bytes,
                            void* stream);

@@ -235,13 +235,13 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
 GTM_API int gtm_moe_decode_check(void* ws, void* stream) {
     if (!ws) return set_error(GTM_ERR_INVALID, "gtm_moe_decode_check: null workspace");
     int flag = 0;
-    cudaError_t e = cudaMemcpyAsync(&flag, static_cast<char*>(ws) + 1024, sizeof(int), cudaMemcpyDeviceToHost,
+    cudaError_t e = cudaMemcpyAsync(&flag, static_cast<char*>(ws) + 1032, sizeof(int), cudaMemcpyDeviceToHost,
                                     (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode_check", e);
     if (flag != 0) {
         int zero = 0;
-        cudaMemcpy(static_cast<char*>(ws) + 1024, &zero, sizeof(int), cudaMemcpyHostToDevice);
+        cudaMemcpy(static_cast<char*>(ws) + 1032, &zero, sizeof(int), cudaMemcpyHostToDevice);
         return set_error(GTM_ERR_TIMEOUT, "gtm_moe_decode: a grid barrier wait timed out (device flag %d)", flag);
     }
     clear_error();

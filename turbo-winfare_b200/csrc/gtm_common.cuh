@@ -91,12 +91,20 @@ __device__ inline float exact_rms_inv(const float* x, int n, float eps, double* 
 // word is set and false is returned so the caller unwinds instead of hanging.
 struct GridSync {
     unsigned* flags;   // [gridDim.x]
-    int* err;          // shared error word (0 = ok)
+    int* err;          // this launch's error word (0 = ok), cleared before every launch
+    int* sticky;       // error word kept until the host reads and clears it
 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Polling load: relaxed (independent loads stay in flight together); the caller fences once
+// after the condition holds.
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
@@ -117,11 +125,11 @@ __device__ inline bool grid_barrier(const GridSync& gs, unsigned epoch, uint64_t
         bool ok = true;
         for (;;) {
             bool mine = true;
-            for (unsigned b = lane; b < gridDim.x; b += 32) mine &= (ld_acquire(gs.flags + b) >= epoch);
+            for (unsigned b = lane; b < gridDim.x; b += 32) mine &= (ld_relaxed(gs.flags + b) >= epoch);
             if (__all_sync(0xffffffffu, mine)) break;
             if (ld_volatile_int(gs.err) != 0) { ok = false; break; }
             if (globaltimer_ns() - t0 > timeout_ns) {
-                if (lane == 0) atomicExch(gs.err, 1);
+                if (lane == 0) { atomicExch(gs.err, 1); atomicExch(gs.sticky, 1); }
                 ok = false;
                 break;
             }

@@ -48,7 +48,8 @@ struct Params {
     float inv_sqrt_d;
     // workspace
     unsigned* flags;
-    int* err;
+    int* err;          // this launch's error word
+    int* sticky;       // error word read and cleared by gtm_moe_decode_check
     float* logits;     // [NE]
     float* act;        // [UNITS]: routed (slot-major) then shared
     float* h2;         // [D]
@@ -391,7 +392,7 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x;
     const int G = gridDim.x, cta = blockIdx.x;
-    const GridSync gs{P.flags, P.err};
+    const GridSync gs{P.flags, P.err, P.sticky};
     unsigned epoch = 0;
     const GtmDecodeIO& io = P.io;
     const bool writer = cta == 0;
@@ -467,7 +468,10 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
 
 }  // namespace dec
 
-// Workspace: [0, 1024) barrier flags, [1024] error word, then logits, act, h2, shared out.
+// Workspace: [0, 1024) barrier flags and [1024] this launch's error word (both cleared before
+// every launch), [1032] the sticky error word (zero-initialised once by the owner of the
+// workspace, read and cleared by gtm_moe_decode_check), then logits, act, h2, shared out.
+constexpr size_t kStickyOffset = 1032;
 size_t decode_workspace_bytes() {
     return 2048 + sizeof(float) * (dec::NE + dec::UNITS + 2 * dec::D) + 256;
 }
@@ -485,13 +489,14 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
     unsigned char* w = static_cast<unsigned char*>(ws);
     P.flags = reinterpret_cast<unsigned*>(w);
     P.err = reinterpret_cast<int*>(w + 1024);
+    P.sticky = reinterpret_cast<int*>(w + kStickyOffset);
     float* f = reinterpret_cast<float*>(w + 2048);
     P.logits = f;
     P.act = f + NE;
     P.h2 = P.act + UNITS;
     P.sh_out = P.h2 + D;
     (void)ws_bytes;
-    cudaError_t e = cudaMemsetAsync(w, 0, 1024, stream);   // barrier flags restart at epoch 0
+    cudaError_t e = cudaMemsetAsync(w, 0, 1028, stream);   // barrier flags restart at epoch 0
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: memset", e);
     const size_t smem = sizeof(Smem);
     static bool attr_done = false;

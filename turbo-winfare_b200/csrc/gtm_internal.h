@@ -4,7 +4,7 @@
 
 #include <cstddef>
 
-#include "../../include/gtmoe.h"
+#include "gtmoe.h"
 
 namespace gtm {
 

@@ -4,7 +4,7 @@
 #include <cstring>
 #include <cuda_runtime.h>
 
-#include "../../include/gtmoe_synth.h"
+#include "gtmoe_synth.h"
 #include "gtm_internal.h"
 #include "gtm_synth.h"
 

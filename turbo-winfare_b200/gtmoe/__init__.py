@@ -233,7 +233,7 @@ class Decoder:
         n = lib().gtm_moe_decode_workspace_bytes(C.byref(self.dims))
         if n == 0:
             raise GtmError(ERR_UNSUPPORTED, "decode workspace size query failed")
-        self.workspace = torch.empty(n + 256, dtype=torch.uint8, device=device)
+        self.workspace = torch.zeros(n + 256, dtype=torch.uint8, device=device)  # zeroed once, as required
         base = self.workspace.data_ptr()
         self.ws_ptr = C.c_void_p((base + 255) // 256 * 256)
         self.ws_bytes = n
