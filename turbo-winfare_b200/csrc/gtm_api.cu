@@ -215,7 +215,9 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
         if (!L.resident_dev || !L.experts_dev || L.expert_stride == 0)
             return set_error(GTM_ERR_INVALID, "gtm_moe_decode: layer %d has a null base or zero stride", l);
         const uint64_t offs16[] = {L.router.weight, L.expert_stride, L.expert_gate.weight, L.expert_up.weight,
-                                   L.expert_down.weight, L.shared_gate.weight, L.shared_up.weight, L.shared_down.weight};
+                                   L.expert_down.weight, L.shared_gate.weight, L.shared_up.weight, L.shared_down.weight,
+                                   L.pre_ffn_norm, L.pre_ffn_norm_2, L.router_scale, L.post_ffn_norm_1,
+                                   L.post_ffn_norm_2, L.post_ffn_norm};
         if (!aligned(L.resident_dev, 16) || !aligned(L.experts_dev, 16))
             return set_error(GTM_ERR_MISALIGNED, "gtm_moe_decode: layer %d base pointers must be 16-byte aligned", l);
         for (uint64_t o : offs16)
@@ -227,6 +229,8 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: device query", e);
     const int ctas = sms < 256 ? sms : 256;
+    if (ctas < kDecodeMinCtas)
+        return set_error(GTM_ERR_UNSUPPORTED, "gtm_moe_decode: needs >= %d SMs (device has %d)", kDecodeMinCtas, sms);
     int rc = launch_decode(*dims, layers, num_layers, *io, ws, ws_bytes, (cudaStream_t)stream, ctas);
     if (rc == GTM_OK) clear_error();
     return rc;
@@ -235,13 +239,14 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
 GTM_API int gtm_moe_decode_check(void* ws, void* stream) {
     if (!ws) return set_error(GTM_ERR_INVALID, "gtm_moe_decode_check: null workspace");
     int flag = 0;
-    cudaError_t e = cudaMemcpyAsync(&flag, static_cast<char*>(ws) + 1032, sizeof(int), cudaMemcpyDeviceToHost,
+    char* sticky = static_cast<char*>(ws) + decode_sticky_offset();
+    cudaError_t e = cudaMemcpyAsync(&flag, sticky, sizeof(int), cudaMemcpyDeviceToHost,
                                     (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode_check", e);
     if (flag != 0) {
         int zero = 0;
-        cudaMemcpy(static_cast<char*>(ws) + 1032, &zero, sizeof(int), cudaMemcpyHostToDevice);
+        cudaMemcpy(sticky, &zero, sizeof(int), cudaMemcpyHostToDevice);
         return set_error(GTM_ERR_TIMEOUT, "gtm_moe_decode: a grid barrier wait timed out (device flag %d)", flag);
     }
     clear_error();

@@ -5,18 +5,29 @@
 // MulBF16 -> GemvInt8 -> RouterTopK -> CPU read-back -> shared expert (GemvInt4 x3, GeGLU,
 // RMSNormK) -> per expert GemvInt4 gate/up, GeGLU, GemvInt4 down, ScaleAccum -> LayerTail.
 //
-// Per layer, three phases separated by bounded grid barriers:
-//   P1  every CTA rebuilds the block input from the previous layer's h2 / shared output (layer
-//       tail, optional between-layer RMSNorm) and the three views (dense_x, routed_x and the
-//       router input) in shared memory; CTAs 0..127 each compute one router logit with the
-//       reference's exact accumulation order (bit-identical logits).
-//   P2  every CTA selects the top-8 itself from the 128 logits, then computes its share of the
-//       7744 gate/up row pairs (8 x 704 routed + 2112 shared) with GeGLU fused.
-//   P3  every CTA computes ~19 rows of the 2816-wide down projection: the shared expert's row
-//       and the 8 routed experts' rows, combined with the routing weights (h2) in one pass.
-// Within a CTA the 352 threads split the input dimension of each row (one 32-bit word = 8
-// int4 weights per thread and row) and rows are reduced with a warp transpose-reduce.
+// Int4 products (gemv_groups): weights are dequantised to fp16 in registers (exact integers
+// 0..15, two LOP3 masks per nibble pair) and fed as the A operand of mma.sync.m16n8k16; the
+// activation goes in as B split into an fp16 high part (column 0) and low part (column 1), so
+// sum_k q_k * x_k comes out in fp32 to ~2^-22 of x. The group's bf16 scale and bias are applied
+// in fp32 after each 64-element group: y += s * (d_hi + d_lo) + b * sum(x). A 16-row tile is
+// either 8 gate rows on top of the same 8 up rows (so GeGLU happens in registers) or 16 rows of a
+// down projection. tcgen05 would need the dequantised tile staged through shared memory for a
+// one-column product; mma.sync consumes the register fragments the dequant produces directly.
+//
+// Per layer (one token), with split arrive/wait grid barriers (bounded waits):
+//   P1  every CTA: layer tail of the previous layer from the down partials, optional
+//       between-layer RMSNorm, views (dense_x, routed_x, router input); CTAs 0..127: one router
+//       logit each in the reference's exact order (bit-identical logits)      -> arrive A1
+//       every CTA: its share of the 264 shared gate/up tiles (+GeGLU)        -> arrive A2
+//   P2  wait A1; top-8 (each CTA); L2-prefetch its routed down rows; its share of the 704 routed
+//       gate/up tiles (+GeGLU)                                                -> arrive B
+//       wait A2; its share of the shared down (176 row tiles x 3 thirds of K)
+//   P3  wait B; its share of the routed down (176 row tiles x 8 experts), partials x w_k;
+//       L2-prefetch the next layer's router row, shared gate/up and down     -> arrive C
+// The down partials [3 shared + 8 routed][2816] are summed in fixed order by the next tail.
 #include <cstdint>
+#include <cstring>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "gtm_common.cuh"
@@ -26,19 +37,23 @@ namespace gtm {
 namespace dec {
 
 constexpr int D = 2816, FE = 704, FS = 2112, NE = 128, TOPK = 8;
-constexpr int NT = D / 8;                     // 352 threads, one word of a K=2816 row each
-constexpr int NWARP = NT / 32;                // 11
-constexpr int GD = D / kGroup;                // 44
-constexpr int UNITS_R = TOPK * FE;            // 5632 routed gate/up row pairs
-constexpr int UNITS = UNITS_R + FS;           // + 2112 shared
-constexpr int DW_SH = FS / 8;                 // 264 words in a shared-down row
-constexpr int DW_EX = FE / 8;                 // 88 words in a routed-down row
-constexpr int DWORDS = DW_SH + TOPK * DW_EX;  // 968 words in a combined down row
-constexpr int ROW_GU = D / 2;                 // 1408 bytes per gate/up row
-constexpr int CH2 = 16;                       // gate/up row pairs per chunk (32 rows)
-constexpr int CH3 = 8;                        // down rows per chunk (16 accumulators)
-constexpr int RIN_PITCH = 65;                 // padded router-input row (bank spread)
+constexpr int NT = 512, NW = NT / 32;
+constexpr int GD = D / kGroup;            // 44 groups in a hidden-sized input
+constexpr int GFE = FE / kGroup;          // 11
+constexpr int GFS = FS / kGroup;          // 33
+constexpr int TILES_R = TOPK * FE / 8;    // 704 routed gate/up tiles (8 row pairs each)
+constexpr int TILES_S = FS / 8;           // 264 shared gate/up tiles
+constexpr int OT = D / 16;                // 176 output row tiles of the down projection
+constexpr int NSEG = 3 + TOPK;            // down partials: 3 shared thirds + 8 routed experts
+constexpr int ITEMS_SD = OT * 3;          // 528 shared-down items
+constexpr int ITEMS_RD = OT * TOPK;       // 1408 routed-down items
+constexpr int MAX_ITEMS = 12;             // per CTA and phase (148 CTAs: <= 10)
+constexpr int ROW_GU = D / 2;             // 1408 bytes per gate/up row
+constexpr int RIN_PITCH = 65;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr int ACT_R = TOPK * FE;          // 5632 routed activations, then 2112 shared
+
+enum { BAR_A1 = 0, BAR_A2 = 1, BAR_B = 2, BAR_C = 3 };
 
 struct Params {
     GtmLayer layers[GTM_MAX_LAYERS];
@@ -46,90 +61,493 @@ struct Params {
     int num_layers;
     float eps;
     float inv_sqrt_d;
-    // workspace
-    unsigned* flags;
-    int* err;          // this launch's error word
-    int* sticky;       // error word read and cleared by gtm_moe_decode_check
+    unsigned* flags;   // [4][256]
+    int* err;
+    int* sticky;
     float* logits;     // [NE]
-    float* act;        // [UNITS]: routed (slot-major) then shared
-    float* h2;         // [D]
-    float* sh_out;     // [D]
+    float* act;        // [ACT_R + FS]
+    float* part;       // [NSEG][D]
 };
 
+// B-operand fragment tables: per 64-element group, 8 slots (4 thread columns x hi/lo) of 8
+// packed fp16 pairs, stored half-major so the 8 reading lanes hit consecutive 16-byte chunks.
+constexpr int TBL_WORDS = 64;   // 32-bit words per group (256 bytes)
+
+// Arrays read or written with 16-byte vector accesses or cp.async carry alignas(16).
 struct Smem {
-    float hid[D];
-    float a[D];
-    float b[D];
-    float xr[D];
-    float xd[D];
-    float rin[GD * RIN_PITCH];
-    float part[NWARP][32];
+    alignas(16) float hid[D];
+    alignas(16) float ab[2 * D];   // scratch: [0, D) and [D, 2D), or one 2D-float vector
+    alignas(16) float rin[GD * RIN_PITCH];
+    alignas(16) uint32_t tbl_r[GD * TBL_WORDS];        // routed_x
+    alignas(16) uint32_t tbl_d[GD * TBL_WORDS];        // dense_x
+    alignas(16) uint32_t tbl_sh[GFS * TBL_WORDS];      // shared act
+    alignas(16) uint32_t tbl_rk[TOPK * GFE * TBL_WORDS];  // routed act, expert-slot major
+    float xs_r[GD], xs_d[GD], xs_sh[GFS], xs_rk[TOPK * GFE];
+    float cs_r[GD], cs_d[GD], cs_sh[GFS], cs_rk[TOPK * GFE];
+    // bf16 norm vectors, copied ahead of use: this layer's pre_ffn_norm, pre_ffn_norm_2,
+    // router.scale and the previous layer's post_ffn_norm_1, post_ffn_norm_2, post_ffn_norm
+    alignas(16) uint16_t nw[6][D];
+    float slot[MAX_ITEMS][NW][16];
     float terms[GD];
     double red[40];
-    uint64_t rows[32][3];
+    double red2[2][NW][2];   // two-value block reductions, double-buffered
     float topw[TOPK];
     int topi[TOPK];
     int flag;
 };
 
+static_assert(offsetof(Smem, nw) % 16 == 0 && offsetof(Smem, ab) % 16 == 0 && offsetof(Smem, tbl_r) % 16 == 0 &&
+                  offsetof(Smem, tbl_d) % 16 == 0 && offsetof(Smem, tbl_sh) % 16 == 0 &&
+                  offsetof(Smem, tbl_rk) % 16 == 0 && offsetof(Smem, hid) % 16 == 0,
+              "vector-accessed shared arrays must be 16-byte aligned");
+
 __device__ __forceinline__ const uint8_t* rp(const void* base, uint64_t off) {
     return static_cast<const uint8_t*>(base) + off;
 }
+__device__ __forceinline__ const uint16_t* rp16(const void* base, uint64_t off) {
+    return reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(base) + off);
+}
 
-// ---- P1 helpers --------------------------------------------------------------------------
-// Layer tail of layer `L` (src/cpu_reference.cpp:512-520) on the block's copies of h2 (a) and
-// the shared expert's output (b), updating s.hid in place; h1 is produced on the way.
-__device__ void layer_tail(Smem& s, const GtmLayer& L, float eps, float* h1_out, float* h2_out) {
+__device__ __forceinline__ uint2 ldg_nc_u2(const void* p) {
+    uint2 v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ldg_nc_u16(const void* p) {
+    uint16_t v;
+    asm("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    // 16-byte aligned start, size a multiple of 16 (callers round inside the tensor's region)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_range(const void* p, uint64_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes + 15) & ~uintptr_t(15);
+    for (uintptr_t q = a; q < e; q += 32768) {
+        const uint32_t n = (uint32_t)min((uintptr_t)32768, e - q);
+        prefetch_l2(reinterpret_cast<const void*>(q), n);
+    }
+}
+
+// ---- fp16 fragments ------------------------------------------------------------------------
+// Dequantise one 32-bit word (8 int4, low nibble first) into four fp16x2 registers with one LOP3
+// each: (1024+n0, 1024+n4), (1024+16n1, 1024+16n5), (1024+n2, 1024+n6), (1024+16n3, 1024+16n7),
+// all exact in fp16. The activation table carries x for the even elements and x/16 for the odd
+// ones, so each product is 1024*x + n*x or 64*x + n*x; the per-group constant
+// C = 1024 * sum(x_even) + 64 * sum(x_odd) is subtracted once per group in fp32.
+__device__ __forceinline__ void dq_word(uint32_t w, uint32_t (&r)[4]) {
+    const uint32_t m = 0x64006400u;                         // fp16 1024.0 in both halves
+    const uint32_t w8 = w >> 8;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[0]) : "r"(w), "r"(0x000F000Fu), "r"(m));
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[1]) : "r"(w), "r"(0x00F000F0u), "r"(m));
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[2]) : "r"(w8), "r"(0x000F000Fu), "r"(m));
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[3]) : "r"(w8), "r"(0x00F000F0u), "r"(m));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
+// Builds the fragment table of `groups` 64-element groups of the fp32 vector v (in shared
+// memory): for thread column t and part hl (0 = fp16 high part, 1 = low part) the 16 elements
+// 16t..16t+15 as (x0,x4)(x1,x5)(x2,x6)(x3,x7)(x8,x12)(x9,x13)(x10,x14)(x11,x15), odd elements
+// divided by 16 (exact). Also per-group sums xs (for the bias) and the offset constants cs.
+__device__ void build_table(const float* v, int groups, uint32_t* tbl, float* xs, float* cs) {
+    for (int i = threadIdx.x; i < groups * 8; i += blockDim.x) {
+        const int j = i >> 3, t = (i >> 1) & 3, hl = i & 1, slotn = t * 2 + hl;
+        const float4* src = reinterpret_cast<const float4*>(v + j * 64 + t * 16);
+        float x[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 f = src[q];
+            x[4 * q] = f.x; x[4 * q + 1] = f.y; x[4 * q + 2] = f.z; x[4 * q + 3] = f.w;
+        }
+        __half h[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            const float b = (q & 1) ? x[q] * 0.0625f : x[q];
+            const __half hi = __float2half_rn(b);
+            h[q] = hl == 0 ? hi : __float2half_rn(b - __half2float(hi));
+        }
+        // pairs (x0,x4)(x1,x5)(x2,x6)(x3,x7) | (x8,x12)(x9,x13)(x10,x14)(x11,x15)
+        uint4 p0 = make_uint4(pack_h2(h[0], h[4]), pack_h2(h[1], h[5]), pack_h2(h[2], h[6]), pack_h2(h[3], h[7]));
+        uint4 p1 = make_uint4(pack_h2(h[8], h[12]), pack_h2(h[9], h[13]), pack_h2(h[10], h[14]), pack_h2(h[11], h[15]));
+        *reinterpret_cast<uint4*>(tbl + ((j * 2 + 0) * 8 + slotn) * 4) = p0;
+        *reinterpret_cast<uint4*>(tbl + ((j * 2 + 1) * 8 + slotn) * 4) = p1;
+    }
+    const int lane = threadIdx.x & 31;
+    for (int j = threadIdx.x >> 5; j < groups; j += blockDim.x >> 5) {
+        float s = 0.0f, c = 0.0f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float x = v[j * 64 + 32 * h + lane];
+            const float b = (lane & 1) ? x * 0.0625f : x;
+            const __half hi = __float2half_rn(b);
+            const __half lo = __float2half_rn(b - __half2float(hi));
+            s += x;
+            c += 1024.0f * (__half2float(hi) + __half2float(lo));   // what the MMA adds besides n*x
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s += __shfl_xor_sync(0xffffffffu, s, o);
+            c += __shfl_xor_sync(0xffffffffu, c, o);
+        }
+        if (lane == 0) { xs[j] = s; cs[j] = c; }
+    }
+}
+
+// Copies n floats (n % 4 == 0) written by other CTAs in this launch into shared memory.
+__device__ __forceinline__ void stage_from_global(float* dst, const float* src, int n) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
+    __syncthreads();
+}
+
+// One warp: groups [j0, j1) of a 16-row tile. Rows g (pointer set a) and g + 8 (set b); lane
+// (g, t = 0) accumulates y_a (row g) and y_b (row g + 8).
+struct TileRows {
+    const uint8_t* wa;     // row g, byte 0 of group 0
+    const uint8_t* wb;     // row g + 8
+    const uint16_t* sa;    // scales of row g
+    const uint16_t* ba;
+    const uint16_t* sb;
+    const uint16_t* bb;
+};
+
+// Groups are taken four at a time: group q0 + m puts its activation in B columns 2m (fp16 high
+// part) and 2m + 1 (low part), so after the quad lane (g, t) holds group q0 + t's products for
+// rows g and g + 8 and applies that group's scale, bias and offset constant. The per-lane sums
+// cover the groups congruent to t mod 4; the caller adds the four lanes of a row.
+// Global loads of one quad: the 4 groups' weight words for rows g and g + 8 (always from a valid
+// group of the run) and this lane's group's scales and biases.
+struct QuadLoads {
+    uint2 wa[4], wb[4];
+    uint16_t sa, ba, sb, bb;
+};
+
+__device__ __forceinline__ QuadLoads load_quad(const TileRows& R, int q0, int j0, int j1, int t) {
+    QuadLoads Q;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int j = q0 + m;
+        const int jc = (j >= j0 && j < j1) ? j : j0;
+        Q.wa[m] = ldg_nc_u2(R.wa + 32 * jc + 8 * t);
+        Q.wb[m] = ldg_nc_u2(R.wb + 32 * jc + 8 * t);
+    }
+    const int j = q0 + t;
+    const int jc = (j >= j0 && j < j1) ? j : j0;
+    Q.sa = ldg_nc_u16(R.sa + jc);
+    Q.ba = ldg_nc_u16(R.ba + jc);
+    Q.sb = ldg_nc_u16(R.sb + jc);
+    Q.bb = ldg_nc_u16(R.bb + jc);
+    return Q;
+}
+
+__device__ __forceinline__ void compute_quad(const QuadLoads& Q, int q0, int j0, int j1, const uint32_t* tbl,
+                                             const float* xs, const float* cs, float& ya, float& yb) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int slotn = t * 2 + (g & 1);
+    float dE[4] = {0.0f, 0.0f, 0.0f, 0.0f}, dO[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int j = q0 + m;
+        const bool on = j >= j0 && j < j1;           // warp-uniform
+        uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = make_uint4(0u, 0u, 0u, 0u);
+        if (on && (g >> 1) == m) {
+            b0 = *reinterpret_cast<const uint4*>(tbl + ((j * 2 + 0) * 8 + slotn) * 4);
+            b1 = *reinterpret_cast<const uint4*>(tbl + ((j * 2 + 1) * 8 + slotn) * 4);
+        }
+        uint32_t qa0[4], qa1[4], qb0[4], qb1[4];
+        dq_word(Q.wa[m].x, qa0);
+        dq_word(Q.wa[m].y, qa1);
+        dq_word(Q.wb[m].x, qb0);
+        dq_word(Q.wb[m].y, qb1);
+        float (&d)[4] = (m & 1) ? dO : dE;
+        mma16816(d, qa0[0], qb0[0], qa0[1], qb0[1], b0.x, b0.y);
+        mma16816(d, qa0[2], qb0[2], qa0[3], qb0[3], b0.z, b0.w);
+        mma16816(d, qa1[0], qb1[0], qa1[1], qb1[1], b1.x, b1.y);
+        mma16816(d, qa1[2], qb1[2], qa1[3], qb1[3], b1.z, b1.w);
+    }
+    const int j = q0 + t;
+    if (j >= j0 && j < j1) {
+        const float x = xs[j], c = cs[j];
+        ya = fmaf(bf16f(Q.ba), x, fmaf(bf16f(Q.sa), ((dE[0] + dO[0]) + (dE[1] + dO[1])) - c, ya));
+        yb = fmaf(bf16f(Q.bb), x, fmaf(bf16f(Q.sb), ((dE[2] + dO[2]) + (dE[3] + dO[3])) - c, yb));
+    }
+}
+
+// Loads of the next quad are issued before the current one is computed, so each warp keeps two
+// quads (4 KB of weights) in flight.
+__device__ __forceinline__ void gemv_groups(const TileRows& R, int j0, int j1, const uint32_t* tbl, const float* xs,
+                                            const float* cs, float& ya, float& yb) {
+    const int t = threadIdx.x & 3;
+    int q0 = j0 & ~3;
+    QuadLoads cur = load_quad(R, q0, j0, j1, t);
+    for (; q0 < j1; q0 += 4) {
+        QuadLoads nxt = cur;
+        if (q0 + 4 < j1) nxt = load_quad(R, q0 + 4, j0, j1, t);
+        compute_quad(cur, q0, j0, j1, tbl, xs, cs, ya, yb);
+        cur = nxt;
+    }
+}
+
+// Splits n_items x L groups evenly over the CTA's warps; each warp walks its contiguous run of
+// (item, group) pairs and leaves one partial per item it touched in s.slot[item][warp].
+template <class RowsFn>
+__device__ __forceinline__ void warp_items(Smem& s, int slot_base, int n_items, int L, int jbase, const uint32_t* tbl,
+                                           const float* xs, const float* cs, RowsFn rows_of) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int total = n_items * L;
+    int p = warp * total / NW;
+    const int p1 = (warp + 1) * total / NW;
+    while (p < p1) {
+        const int item = p / L, j0 = p - item * L;
+        const int j1 = min(L, j0 + (p1 - p));
+        const TileRows R = rows_of(item);
+        float ya = 0.0f, yb = 0.0f;
+        gemv_groups(R, jbase + j0, jbase + j1, tbl, xs, cs, ya, yb);
+        ya += __shfl_xor_sync(0xffffffffu, ya, 1);
+        ya += __shfl_xor_sync(0xffffffffu, ya, 2);
+        yb += __shfl_xor_sync(0xffffffffu, yb, 1);
+        yb += __shfl_xor_sync(0xffffffffu, yb, 2);
+        if (t == 0) {
+            s.slot[slot_base + item][warp][g] = ya;
+            s.slot[slot_base + item][warp][8 + g] = yb;
+        }
+        p += j1 - j0;
+    }
+}
+
+__device__ __forceinline__ void zero_slots(Smem& s, int n_items) {
+    float* f = &s.slot[0][0][0];
+    for (int i = threadIdx.x; i < n_items * NW * 16; i += blockDim.x) f[i] = 0.0f;
+}
+
+__device__ __forceinline__ float slot_sum(const Smem& s, int item, int r) {
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) v += s.slot[item][w][r];
+    return v;
+}
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
+// ---- barriers ------------------------------------------------------------------------------
+__device__ __forceinline__ void arrive(const Params& P, int kind, unsigned value) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        st_release(P.flags + kind * 256 + blockIdx.x, value);
+    }
+}
+
+__device__ bool wait_all(const Params& P, Smem& s, int kind, unsigned value) {
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const unsigned* f = P.flags + kind * 256;
+        const uint64_t t0 = globaltimer_ns();
+        bool ok = true;
+        for (;;) {
+            bool mine = true;
+            for (unsigned b = lane; b < gridDim.x; b += 32) mine &= (ld_relaxed(f + b) >= value);
+            const int e = lane == 0 ? ld_volatile_int(P.err) : 0;
+            if (__all_sync(0xffffffffu, mine)) break;
+            if (__shfl_sync(0xffffffffu, e, 0) != 0) { ok = false; break; }
+            if (globaltimer_ns() - t0 > kTimeoutNs) {
+                if (lane == 0) { atomicExch(P.err, 1); atomicExch(P.sticky, 1); }
+                ok = false;
+                break;
+            }
+        }
+        __threadfence();
+        if (lane == 0) s.flag = ok ? 0 : 1;
+    }
+    __syncthreads();
+    return s.flag == 0;
+}
+
+// ---- P1 pieces ----------------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(sa), "l"(gmem) : "memory");
+}
+
+// Starts copying norm vectors into s.nw: the pre-FFN set (pre_ffn_norm, pre_ffn_norm_2,
+// router.scale) of layer Lpre into slots 0..2 and the post-FFN set (post_ffn_norm_1, _2, and
+// post_ffn_norm) of layer Lpost into slots 3..5; either may be null. Completed by
+// tail_and_views.
+__device__ void load_norms_async(Smem& s, const GtmLayer* Lpre, const GtmLayer* Lpost) {
+    constexpr int per = D * 2 / 16;   // 16-byte chunks per vector
+    for (int i = threadIdx.x; i < 6 * per; i += NT) {
+        const int v = i / per, c = i - v * per;
+        const GtmLayer* L = v < 3 ? Lpre : Lpost;
+        if (!L) continue;
+        const uint64_t off = v == 0 ? L->pre_ffn_norm : v == 1 ? L->pre_ffn_norm_2 : v == 2 ? L->router_scale
+                           : v == 3 ? L->post_ffn_norm_1 : v == 4 ? L->post_ffn_norm_2 : L->post_ffn_norm;
+        cp_async16(&s.nw[v][c * 8], rp(L->resident_dev, off) + c * 16);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Sums a and b over the block with one barrier: each thread adds the warp partials itself in
+// warp order, so every thread (and every CTA, given the same data) gets the same bits.
+// Consecutive calls must alternate `buf`.
+__device__ __forceinline__ double2 block_sum2(Smem& s, double a, double b, int buf) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (lane == 0) { s.red2[buf][warp][0] = a; s.red2[buf][warp][1] = b; }
+    __syncthreads();
+    double ra = 0.0, rb = 0.0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) { ra += s.red2[buf][w][0]; rb += s.red2[buf][w][1]; }
+    return make_double2(ra, rb);
+}
+
+// 1 / sqrt(float(sum / D) + eps), the reference's formula (src/cpu_reference.cpp:46); the mean
+// is formed with a multiply by 1/D (one extra rounding, far below the float conversion).
+constexpr double kInvD = 1.0 / (double)D;
+__device__ __forceinline__ float rms_inv_from_sum(double sum, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(__dmul_rn(sum, kInvD)), eps)));
+}
+
+// The same with the reference's exact bits when `sum` is a parallel double sum of x*x: see
+// exact_rms_inv for the argument; the bound (D + 48) ulps also covers the tree depth (< 30) and
+// the multiply by the rounded 1/D. The check is identical on every thread, so the rare fallback
+// (a sequential sum by thread 0, then the reference's division) is a uniform branch.
+__device__ float certified_rms_inv(Smem& s, const float* x, double sum, float eps) {
+    const double q = __dmul_rn(sum, kInvD);
+    float f = __double2float_rn(q);
+    const double fd = (double)f;
+    const double lo = (fd + (double)nextafterf(f, -INFINITY)) * 0.5;
+    const double hi = (fd + (double)nextafterf(f, INFINITY)) * 0.5;
+    const double bound = q * ((double)D + 48.0) * 1.1102230246251565e-16;
+    if (!(q - lo > bound && hi - q > bound)) {
+        if (threadIdx.x == 0) {
+            double seq = 0.0;
+            for (int i = 0; i < D; ++i) seq = __dadd_rn(seq, __dmul_rn((double)x[i], (double)x[i]));
+            s.red[32] = seq;
+        }
+        __syncthreads();
+        f = __double2float_rn(__ddiv_rn(s.red[32], (double)D));
+    }
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, eps)));
+}
+
+// Layer tail of the previous layer Lp (src/cpu_reference.cpp:512-520), when there is one, from
+// the down partials (shared output = the 3 shared thirds, h2 = the 8 routed experts in router
+// order), the optional weightless RMSNorm between layers, then the views of layer L
+// (src/cpu_reference.cpp:425-443): dense_x = h*w_pre, routed_x = h*w_pre2 and
+// router_in = h*bf16(router.scale)*(1/sqrt(D)) with h = rmsnorm_no_scale(hidden), exactly as the
+// reference rounds them; finally the fragment tables of dense_x and routed_x.
+__device__ void tail_and_views(Smem& s, const Params& P, const GtmLayer* Lp, bool norm_between, bool do_views,
+                               float* h1_out, float* h2_out, float* hid_out) {
     const int tid = threadIdx.x;
-    const uint16_t* w_pf1 = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.post_ffn_norm_1));
-    const uint16_t* w_pf2 = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.post_ffn_norm_2));
-    const uint16_t* w_pf = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.post_ffn_norm));
-    const float ls = bf16f(*reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.layer_scalar)));
-    const float inv1 = exact_rms_inv(s.b, D, eps, s.red);   // h1 = rms(shared_out) * w_pf1
-    const float inv2 = exact_rms_inv(s.a, D, eps, s.red);   // rms(h2) * w_pf2
-    for (int i = tid; i < D; i += blockDim.x) {
-        const float h1 = __fmul_rn(__fmul_rn(s.b[i], inv1), bf16f(w_pf1[i]));
-        if (h1_out) h1_out[i] = h1;
-        if (h2_out) h2_out[i] = s.a[i];
-        s.a[i] = __fadd_rn(__fmul_rn(__fmul_rn(s.a[i], inv2), bf16f(w_pf2[i])), h1);
-    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    const float inv3 = exact_rms_inv(s.a, D, eps, s.red);
-    for (int i = tid; i < D; i += blockDim.x) {
-        const float t2 = __fmul_rn(__fmul_rn(s.a[i], inv3), bf16f(w_pf[i]));
-        s.hid[i] = __fmul_rn(__fadd_rn(s.hid[i], t2), ls);
+    float* h2 = s.ab;
+    float* sh = s.ab + D;
+    double a = 0.0;
+    int buf = 0;
+    if (Lp) {
+        const float ls = bf16f(*rp16(Lp->resident_dev, Lp->layer_scalar));
+        double b = 0.0;
+        for (int i = tid; i < D / 4; i += NT) {
+            const float4* pp = reinterpret_cast<const float4*>(P.part) + i;
+            float4 vs = __ldcg(pp), vh = __ldcg(pp + 3 * (D / 4));
+            const float4 s1 = __ldcg(pp + (D / 4)), s2 = __ldcg(pp + 2 * (D / 4));
+            vs.x += s1.x; vs.y += s1.y; vs.z += s1.z; vs.w += s1.w;
+            vs.x += s2.x; vs.y += s2.y; vs.z += s2.z; vs.w += s2.w;
+#pragma unroll
+            for (int k = 1; k < TOPK; ++k) {
+                const float4 r = __ldcg(pp + (3 + k) * (D / 4));
+                vh.x += r.x; vh.y += r.y; vh.z += r.z; vh.w += r.w;
+            }
+            reinterpret_cast<float4*>(sh)[i] = vs;
+            reinterpret_cast<float4*>(h2)[i] = vh;
+            a += (double)vs.x * vs.x + (double)vs.y * vs.y + (double)vs.z * vs.z + (double)vs.w * vs.w;
+            b += (double)vh.x * vh.x + (double)vh.y * vh.y + (double)vh.z * vh.z + (double)vh.w * vh.w;
+        }
+        double2 r = block_sum2(s, a, b, buf); buf ^= 1;
+        const float inv1 = rms_inv_from_sum(r.x, P.eps), inv2 = rms_inv_from_sum(r.y, P.eps);
+        a = 0.0;
+        for (int i = tid; i < D; i += NT) {
+            const float h1 = __fmul_rn(__fmul_rn(sh[i], inv1), bf16f(s.nw[3][i]));
+            if (h1_out) h1_out[i] = h1;
+            if (h2_out) h2_out[i] = h2[i];
+            const float t = __fadd_rn(__fmul_rn(__fmul_rn(h2[i], inv2), bf16f(s.nw[4][i])), h1);
+            h2[i] = t;
+            a += (double)t * t;
+        }
+        r = block_sum2(s, a, 0.0, buf); buf ^= 1;
+        const float inv3 = rms_inv_from_sum(r.x, P.eps);
+        a = 0.0;
+        for (int i = tid; i < D; i += NT) {
+            const float hv = __fmul_rn(__fadd_rn(s.hid[i], __fmul_rn(__fmul_rn(h2[i], inv3), bf16f(s.nw[5][i]))), ls);
+            s.hid[i] = hv;
+            a += (double)hv * hv;
+        }
+        if (norm_between) {
+            r = block_sum2(s, a, 0.0, buf); buf ^= 1;
+            const float inv4 = rms_inv_from_sum(r.x, P.eps);
+            a = 0.0;
+            for (int i = tid; i < D; i += NT) {
+                const float hv = __fmul_rn(s.hid[i], inv4);
+                s.hid[i] = hv;
+                a += (double)hv * hv;
+            }
+        }
+        if (hid_out)
+            for (int i = tid; i < D; i += NT) hid_out[i] = s.hid[i];
+    } else {
+        for (int i = tid; i < D; i += NT) a += (double)s.hid[i] * s.hid[i];
     }
-    __syncthreads();
-}
-
-// dense_x = h*w_pre, routed_x = h*w_pre2, router_in = h*bf16(router.scale)*(1/sqrt(D)) with
-// h = rmsnorm_no_scale(hidden) (src/cpu_reference.cpp:425-443).
-__device__ void views(Smem& s, const GtmLayer& L, float eps, float inv_sqrt_d) {
-    const uint16_t* w_pre = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.pre_ffn_norm));
-    const uint16_t* w_pre2 = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.pre_ffn_norm_2));
-    const uint16_t* rs = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.router_scale));
-    const float inv = exact_rms_inv(s.hid, D, eps, s.red);
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    if (!do_views) {
+        __syncthreads();
+        return;
+    }
+    const double2 r = block_sum2(s, a, 0.0, buf);
+    const float inv = certified_rms_inv(s, s.hid, r.x, P.eps);
+    for (int i = tid; i < D; i += NT) {
         const float h = __fmul_rn(s.hid[i], inv);
-        s.xd[i] = __fmul_rn(h, bf16f(w_pre[i]));
-        s.xr[i] = __fmul_rn(h, bf16f(w_pre2[i]));
-        s.rin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(h, bf16f(rs[i])), inv_sqrt_d);
+        sh[i] = __fmul_rn(h, bf16f(s.nw[0][i]));    // dense_x
+        h2[i] = __fmul_rn(h, bf16f(s.nw[1][i]));    // routed_x
+        s.rin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(h, bf16f(s.nw[2][i])), P.inv_sqrt_d);
     }
+    __syncthreads();
+    build_table(h2, GD, s.tbl_r, s.xs_r, s.cs_r);
+    build_table(sh, GD, s.tbl_d, s.xs_d, s.cs_d);
     __syncthreads();
 }
 
-// One router logit with src/cpu_reference.cpp:86-106's order: per group a sequential dot and
-// x-sum over 64 bytes, then the group terms summed in group order.
+// One router logit in src/cpu_reference.cpp:86-106's order (bit-identical).
 __device__ float router_row(Smem& s, const GtmLayer& L, int row) {
     const int tid = threadIdx.x;
     const uint8_t* W = rp(L.resident_dev, L.router.weight) + (size_t)row * D;
-    const uint16_t* S = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.router.scales)) + row * GD;
-    const uint16_t* B = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.router.biases)) + row * GD;
+    const uint16_t* S = rp16(L.resident_dev, L.router.scales) + row * GD;
+    const uint16_t* B = rp16(L.resident_dev, L.router.biases) + row * GD;
     if (tid < GD) {
         const uint4* wg = reinterpret_cast<const uint4*>(W + tid * kGroup);
         uint4 q[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) q[i] = ldg_stream_u4(wg + i);
+        const float sc = bf16f(ldg_u16(S + tid)), bi = bf16f(ldg_u16(B + tid));
         const float* x = s.rin + tid * RIN_PITCH;
         float dot = 0.0f, sum = 0.0f;
 #pragma unroll
@@ -145,21 +563,19 @@ __device__ float router_row(Smem& s, const GtmLayer& L, int row) {
                 }
             }
         }
-        s.terms[tid] = __fadd_rn(__fmul_rn(bf16f(ldg_u16(S + tid)), dot), __fmul_rn(bf16f(ldg_u16(B + tid)), sum));
+        s.terms[tid] = __fadd_rn(__fmul_rn(sc, dot), __fmul_rn(bi, sum));
     }
     __syncthreads();
     float acc = 0.0f;
-    if (tid == 0) {
+    if (tid == 0)
         for (int g = 0; g < GD; ++g) acc = __fadd_rn(acc, s.terms[g]);
-    }
-    __syncthreads();
     return acc;
 }
 
 // Top-8 of the 128 logits by (value desc, index asc), softmax over the 8, times
-// per_expert_scale (src/cpu_reference.cpp:447-480). Warp 0.
-__device__ void select_topk(Smem& s, const GtmLayer& L, const float* logits, bool write_out,
-                            uint32_t* idx_out, float* w_out, float* logits_out) {
+// per_expert_scale (src/cpu_reference.cpp:447-480). Warp 0; results in s.topi / s.topw.
+__device__ void select_topk(Smem& s, const GtmLayer& L, const float* logits, bool writer, uint32_t* idx_out,
+                            float* w_out, float* logits_out) {
     if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
     float v[4];
@@ -167,223 +583,232 @@ __device__ void select_topk(Smem& s, const GtmLayer& L, const float* logits, boo
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         v[j] = __ldcg(logits + lane + 32 * j);
-        if (write_out && logits_out) logits_out[lane + 32 * j] = v[j];
+        if (writer && logits_out) logits_out[lane + 32 * j] = v[j];
     }
-    float sel[TOPK];
-    int seli[TOPK];
+    // Order-preserving unsigned keys (-0 folded onto +0, which compare equal as floats); each
+    // round takes the largest key, then the lowest index holding it: (value desc, index asc).
+    uint32_t key[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t u = __float_as_uint(v[j] == 0.0f ? 0.0f : v[j]);
+        key[j] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    }
+    float my_sel = 0.0f;
+    int my_idx = 0;
+    float top0 = 0.0f;
 #pragma unroll
     for (int k = 0; k < TOPK; ++k) {
-        float bv = -INFINITY;
-        int bi = 1 << 30;
+        uint32_t ck = 0u, ci = 0xFFFFFFFFu;          // this lane's best untaken (key desc, index asc)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int e = lane + 32 * j;
-            if (!taken[j] && (bi == (1 << 30) || v[j] > bv || (v[j] == bv && e < bi))) { bv = v[j]; bi = e; }
-        }
+        for (int j = 0; j < 4; ++j)
+            if (!taken[j] && (ci == 0xFFFFFFFFu || key[j] > ck)) { ck = key[j]; ci = (uint32_t)(lane + 32 * j); }
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, ck);
+        const uint32_t bi = __reduce_min_sync(0xffffffffu, ck == mk ? ci : 0xFFFFFFFFu);
+        const float bv = __uint_as_float((mk & 0x80000000u) ? (mk & 0x7FFFFFFFu) : ~mk);
+        if (k == 0) top0 = bv;
+        if (lane == k) { my_sel = bv; my_idx = (int)bi; }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi != (1 << 30) && (bi == (1 << 30) || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
-        }
-        sel[k] = bv;
-        seli[k] = bi;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) if (lane + 32 * j == bi) taken[j] = true;
+        for (int j = 0; j < 4; ++j) if ((uint32_t)(lane + 32 * j) == bi) taken[j] = true;
     }
-    if (lane == 0) {
-        const uint16_t* pes = reinterpret_cast<const uint16_t*>(rp(L.resident_dev, L.per_expert_scale));
-        float e[TOPK], sum = 0.0f;
-        for (int k = 0; k < TOPK; ++k) { e[k] = expf(__fsub_rn(sel[k], sel[0])); sum = __fadd_rn(sum, e[k]); }
-        for (int k = 0; k < TOPK; ++k) {
-            const float w = __fmul_rn(__fdiv_rn(e[k], sum), bf16f(pes[seli[k]]));
-            s.topi[k] = seli[k];
-            s.topw[k] = w;
-            if (write_out && idx_out) idx_out[k] = (uint32_t)seli[k];
-            if (write_out && w_out) w_out[k] = w;
-        }
+    // lanes 0..7: exp and per-expert scale in parallel, the sum in order on every lane
+    const float e = lane < TOPK ? expf(__fsub_rn(my_sel, top0)) : 0.0f;
+    const uint16_t pes_bits = lane < TOPK ? *rp16(L.resident_dev, L.per_expert_scale + 2ull * (uint32_t)my_idx) : 0;
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < TOPK; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, k));
+    if (lane < TOPK) {
+        const float w = __fmul_rn(__fdiv_rn(e, sum), bf16f(pes_bits));
+        s.topi[lane] = my_idx;
+        s.topw[lane] = w;
+        if (writer && idx_out) idx_out[lane] = (uint32_t)my_idx;
+        if (writer && w_out) w_out[lane] = w;
     }
 }
 
-__device__ __forceinline__ float sum8(const float* x) {
-    float a = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a += x[i];
-    return a;
+// ---- work lists ----------------------------------------------------------------------------------
+__device__ __forceinline__ int share(int n, int c, int G) { return (int)((long long)c * n / G); }
+
+// gate/up tile rows: row g = gate row r0 + g, row g + 8 = up row r0 + g (same x)
+__device__ __forceinline__ TileRows gu_rows(const uint8_t* base_g, const uint8_t* base_u, const GtmQuant& qg,
+                                            const GtmQuant& qu, int r) {
+    TileRows R;
+    R.wa = base_g + qg.weight + (uint64_t)r * ROW_GU;
+    R.wb = base_u + qu.weight + (uint64_t)r * ROW_GU;
+    R.sa = reinterpret_cast<const uint16_t*>(base_g + qg.scales) + (uint64_t)r * GD;
+    R.ba = reinterpret_cast<const uint16_t*>(base_g + qg.biases) + (uint64_t)r * GD;
+    R.sb = reinterpret_cast<const uint16_t*>(base_u + qu.scales) + (uint64_t)r * GD;
+    R.bb = reinterpret_cast<const uint16_t*>(base_u + qu.biases) + (uint64_t)r * GD;
+    return R;
 }
 
-// ---- P2: gate/up row pairs [u0, u1) of one kind with GeGLU ------------------------------
-// routed == true: units index (slot k, row r) = (u / FE, u % FE); else shared row u - UNITS_R.
-__device__ void gate_up_range(Smem& s, const GtmLayer& L, const Params& P, int u0, int u1, bool routed,
-                              const XSlice& xs, float xsum) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int c = u0; c < u1; c += CH2) {
-        const int n = min(CH2, u1 - c);
-        if (tid < 2 * CH2) {
-            const int p = tid >> 1, up = tid & 1;
-            uint64_t w = 0, sc = 0, bi = 0;
-            if (p < n) {
-                const int u = c + p;
-                if (routed) {
-                    const int k = u / FE, r = u - k * FE;
-                    const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
-                    const GtmQuant& q = up ? L.expert_up : L.expert_gate;
-                    w = (uint64_t)(blk + q.weight + (uint64_t)r * ROW_GU);
-                    sc = (uint64_t)(blk + q.scales + (uint64_t)r * GD * 2);
-                    bi = (uint64_t)(blk + q.biases + (uint64_t)r * GD * 2);
-                } else {
-                    const int r = u - UNITS_R;
-                    const GtmQuant& q = up ? L.shared_up : L.shared_gate;
-                    const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
-                    w = (uint64_t)(base + q.weight + (uint64_t)r * ROW_GU);
-                    sc = (uint64_t)(base + q.scales + (uint64_t)r * GD * 2);
-                    bi = (uint64_t)(base + q.biases + (uint64_t)r * GD * 2);
-                }
-            }
-            s.rows[tid][0] = w; s.rows[tid][1] = sc; s.rows[tid][2] = bi;
-        }
-        __syncthreads();
-        uint32_t wv[2 * CH2];
-        uint16_t sv[2 * CH2], bv[2 * CH2];
-        const int g = tid >> 3;
-#pragma unroll
-        for (int r = 0; r < 2 * CH2; ++r) {
-            if ((r >> 1) < n) {
-                wv[r] = ldg_stream_u32(reinterpret_cast<const uint8_t*>(s.rows[r][0]) + 4 * tid);
-                sv[r] = ldg_u16(reinterpret_cast<const uint16_t*>(s.rows[r][1]) + g);
-                bv[r] = ldg_u16(reinterpret_cast<const uint16_t*>(s.rows[r][2]) + g);
-            } else {
-                wv[r] = 0; sv[r] = 0; bv[r] = 0;
-            }
-        }
-        float v[2 * CH2];
-#pragma unroll
-        for (int r = 0; r < 2 * CH2; ++r) v[r] = fmaf(bf16f(sv[r]), dot_word(wv[r], xs), bf16f(bv[r]) * xsum);
-        const float red = warp_transpose_reduce(v);
-        s.part[warp][lane] = red;
-        __syncthreads();
-        if (tid < 2 * CH2) {
-            float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < NWARP; ++w) tot += s.part[w][tid];
-            const float other = __shfl_xor_sync(0xffffffffu, tot, 1);
-            if ((tid & 1) == 0 && (tid >> 1) < n) {
-                // tot = gate row, other = up row: gelu_pytorch_tanh(gate) * up
-                const float x = tot;
-                const float t = tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x));
-                P.act[c + (tid >> 1)] = 0.5f * x * (1.0f + t) * other;
-            }
-        }
-        __syncthreads();
+__device__ __forceinline__ TileRows down_rows(const uint8_t* base, const GtmQuant& q, int row, uint32_t row_bytes,
+                                              uint32_t groups) {
+    TileRows R;
+    R.wa = base + q.weight + (uint64_t)row * row_bytes;
+    R.wb = base + q.weight + (uint64_t)(row + 8) * row_bytes;
+    R.sa = reinterpret_cast<const uint16_t*>(base + q.scales) + (uint64_t)row * groups;
+    R.ba = reinterpret_cast<const uint16_t*>(base + q.biases) + (uint64_t)row * groups;
+    R.sb = reinterpret_cast<const uint16_t*>(base + q.scales) + (uint64_t)(row + 8) * groups;
+    R.bb = reinterpret_cast<const uint16_t*>(base + q.biases) + (uint64_t)(row + 8) * groups;
+    return R;
+}
+
+// Shared gate/up tiles [t0, t1) -> act[ACT_R + 8*T + r]
+__device__ void shared_gate_up(Smem& s, const Params& P, const GtmLayer& L, int t0, int t1) {
+    const int n = t1 - t0;
+    if (n <= 0) return;
+    zero_slots(s, n);
+    __syncthreads();
+    const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
+    const int lane_g = (threadIdx.x & 31) >> 2;
+    warp_items(s, 0, n, GD, 0, s.tbl_d, s.xs_d, s.cs_d, [&](int item) {
+        return gu_rows(base, base, L.shared_gate, L.shared_up, (t0 + item) * 8 + lane_g);
+    });
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * 8; i += NT) {
+        const int item = i >> 3, r = i & 7;
+        const float gt = slot_sum(s, item, r), up = slot_sum(s, item, 8 + r);
+        P.act[ACT_R + (t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
     }
 }
 
-// Reduce R = 16 per-lane values across the warp: lane l (< 16) ends with value l's total.
-__device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16]) {
+// Routed gate/up tiles [t0, t1) (tile T: expert slot T / 88, rows 8 * (T % 88) ..) -> act[8*T + r]
+__device__ void routed_gate_up(Smem& s, const Params& P, const GtmLayer& L, int t0, int t1) {
+    const int n = t1 - t0;
+    if (n <= 0) return;
+    zero_slots(s, n);
+    __syncthreads();
+    const int lane_g = (threadIdx.x & 31) >> 2;
+    warp_items(s, 0, n, GD, 0, s.tbl_r, s.xs_r, s.cs_r, [&](int item) {
+        const int T = t0 + item, k = T / (FE / 8), r = (T - k * (FE / 8)) * 8 + lane_g;
+        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
+        return gu_rows(blk, blk, L.expert_gate, L.expert_up, r);
+    });
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * 8; i += NT) {
+        const int item = i >> 3, r = i & 7;
+        const float gt = slot_sum(s, item, r), up = slot_sum(s, item, 8 + r);
+        P.act[(t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
+    }
+}
+
+// Shared down items [i0, i1): item i -> third q = i / OT, row tile ot = i % OT; K groups
+// [11q, 11q + 11) of 33 -> part[q][16*ot + r]
+__device__ void shared_down(Smem& s, const Params& P, const GtmLayer& L, int i0, int i1) {
+    const int n = i1 - i0;
+    if (n <= 0) return;
+    zero_slots(s, n);
+    __syncthreads();
+    const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
+    const int lane_g = (threadIdx.x & 31) >> 2;
+    // items of different thirds use different group ranges: walk third by third
+    int a = i0;
+    while (a < i1) {
+        const int q = a / OT;
+        const int b = min(i1, (q + 1) * OT);
+        const int off = a - i0;
+        const int nn = b - a;
+        warp_items(s, off, nn, GFE, q * GFE, s.tbl_sh, s.xs_sh, s.cs_sh, [&](int item) {
+            const int ot = (a + item) - q * OT;
+            return down_rows(base, L.shared_down, ot * 16 + lane_g, FS / 2, GFS);
+        });
+        a = b;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * 16; i += NT) {
+        const int item = i >> 4, r = i & 15;
+        const int it = i0 + item, q = it / OT, ot = it - q * OT;
+        P.part[(size_t)q * D + ot * 16 + r] = slot_sum(s, item, r);
+    }
+}
+
+// Routed down items [i0, i1): item i -> expert slot k = i / OT, row tile ot = i % OT
+// -> part[3 + k][16*ot + r] = w_k * (expert k's down row)
+__device__ void routed_down(Smem& s, const Params& P, const GtmLayer& L, int i0, int i1) {
+    const int n = i1 - i0;
+    if (n <= 0) return;
+    zero_slots(s, n);
+    __syncthreads();
+    const int lane_g = (threadIdx.x & 31) >> 2;
+    int a = i0;
+    while (a < i1) {
+        const int k = a / OT;
+        const int b = min(i1, (k + 1) * OT);
+        const int off = a - i0, nn = b - a;
+        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
+        warp_items(s, off, nn, GFE, 0, s.tbl_rk + k * GFE * TBL_WORDS, s.xs_rk + k * GFE, s.cs_rk + k * GFE, [&](int item) {
+            const int ot = (a + item) - k * OT;
+            return down_rows(blk, L.expert_down, ot * 16 + lane_g, FE / 2, GFE);
+        });
+        a = b;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * 16; i += NT) {
+        const int item = i >> 4, r = i & 15;
+        const int it = i0 + item, k = it / OT, ot = it - k * OT;
+        P.part[(size_t)(3 + k) * D + ot * 16 + r] = s.topw[k] * slot_sum(s, item, r);
+    }
+}
+
+// L2 prefetch of the weights this CTA reads in the next layer's P1 (router row, shared gate/up
+// tiles, norm vectors) and of its shared-down rows.
+// Every range below is at most 32 KB and lies inside one tensor whose region starts and ends on
+// 16-byte bounds (router scale rows are 88 bytes and get rounded outwards within the region);
+// the last warp issues them, one range per lane at a time.
+__device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
+    if ((threadIdx.x >> 5) != NW - 1) return;
     const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int half = 8; half >= 1; half >>= 1) {
-        const bool upper = (lane & half) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-            const float send = upper ? v[i] : v[i + half];
-            const float keep = upper ? v[i + half] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+    const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
+    const int nrow = cta < NE ? (NE - 1 - cta) / G + 1 : 0;          // router rows of this CTA
+    const int t0 = share(TILES_S, cta, G), t1 = share(TILES_S, cta + 1, G);
+    const int i0 = share(ITEMS_SD, cta, G), i1 = share(ITEMS_SD, cta + 1, G);
+    const int n_router = 3 * nrow, n_sgu = t1 > t0 ? 6 : 0, n_sd = 18 * (i1 - i0), n_vec = 6;
+    const int total = n_router + n_sgu + n_sd + n_vec;
+    for (int i = lane; i < total; i += 32) {
+        const uint8_t* p;
+        uint32_t n;
+        if (i < n_router) {
+            const uint64_t row = (uint64_t)(cta + (i / 3) * G);
+            const int part = i % 3;
+            if (part == 0) { p = base + L.router.weight + row * D; n = D; }
+            else { p = base + (part == 1 ? L.router.scales : L.router.biases) + row * GD * 2; n = GD * 2; }
+        } else if (i < n_router + n_sgu) {
+            const int k = i - n_router, m = k / 3, part = k % 3;
+            const GtmQuant& q = m ? L.shared_up : L.shared_gate;
+            if (part == 0) { p = base + q.weight + (uint64_t)t0 * 8 * ROW_GU; n = (t1 - t0) * 8 * ROW_GU; }
+            else { p = base + (part == 1 ? q.scales : q.biases) + (uint64_t)t0 * 8 * GD * 2; n = (t1 - t0) * 8 * GD * 2; }
+        } else if (i < n_router + n_sgu + n_sd) {
+            const int k = i - n_router - n_sgu, it = i0 + k / 18, part = k % 18;
+            const int q = it / OT, ot = it - q * OT;
+            if (part < 16) {
+                p = base + L.shared_down.weight + ((uint64_t)ot * 16 + part) * (FS / 2) + q * GFE * 32;
+                n = GFE * 32;
+            } else {
+                p = base + (part == 16 ? L.shared_down.scales : L.shared_down.biases) + (uint64_t)ot * 16 * GFS * 2;
+                n = 16 * GFS * 2;
+            }
+        } else {
+            const int v = i - n_router - n_sgu - n_sd;
+            const uint64_t off = v == 0 ? L.pre_ffn_norm : v == 1 ? L.pre_ffn_norm_2 : v == 2 ? L.router_scale
+                               : v == 3 ? L.post_ffn_norm_1 : v == 4 ? L.post_ffn_norm_2 : L.post_ffn_norm;
+            p = base + off;
+            n = D * 2;
         }
+        prefetch_range(p, n);   // rounds to 16-byte bounds inside the tensor's region
     }
-    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
 }
 
-// ---- P3: down rows [j0, j1): shared row and the 8 routed rows, combined ------------------
-__device__ void down_range(Smem& s, const GtmLayer& L, const Params& P, int j0, int j1) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // this thread's (up to) three words of the combined 968-word row
-    const uint8_t* wb[3];
-    const uint8_t* sb[3];
-    const uint8_t* bb[3];
-    uint32_t wstride[3], sstride[3];
-    float fac[3];
-    bool shared_seg[3], valid[3];
-    XSlice xs[3];
-    float xsum[3];
-#pragma unroll
-    for (int m = 0; m < 3; ++m) {
-        const int i = tid + NT * m;
-        valid[m] = i < DWORDS;
-        const int ii = valid[m] ? i : 0;
-        float x8[8];
-        if (ii < DW_SH) {
-            const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
-            wb[m] = base + L.shared_down.weight + 4 * ii;
-            sb[m] = base + L.shared_down.scales + 2 * (ii >> 3);
-            bb[m] = base + L.shared_down.biases + 2 * (ii >> 3);
-            wstride[m] = FS / 2;
-            sstride[m] = (FS / kGroup) * 2;
-            fac[m] = 1.0f;
-            shared_seg[m] = true;
-            const float4* a = reinterpret_cast<const float4*>(P.act + UNITS_R + 8 * ii);
-            const float4 a0 = __ldcg(a), a1 = __ldcg(a + 1);
-            x8[0] = a0.x; x8[1] = a0.y; x8[2] = a0.z; x8[3] = a0.w; x8[4] = a1.x; x8[5] = a1.y; x8[6] = a1.z; x8[7] = a1.w;
-        } else {
-            const int k = (ii - DW_SH) / DW_EX, wis = (ii - DW_SH) - k * DW_EX;
-            const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
-            wb[m] = blk + L.expert_down.weight + 4 * wis;
-            sb[m] = blk + L.expert_down.scales + 2 * (wis >> 3);
-            bb[m] = blk + L.expert_down.biases + 2 * (wis >> 3);
-            wstride[m] = FE / 2;
-            sstride[m] = (FE / kGroup) * 2;
-            fac[m] = s.topw[k];
-            shared_seg[m] = false;
-            const float4* a = reinterpret_cast<const float4*>(P.act + k * FE + 8 * wis);
-            const float4 a0 = __ldcg(a), a1 = __ldcg(a + 1);
-            x8[0] = a0.x; x8[1] = a0.y; x8[2] = a0.z; x8[3] = a0.w; x8[4] = a1.x; x8[5] = a1.y; x8[6] = a1.z; x8[7] = a1.w;
-        }
-        xs[m] = make_xslice(x8);
-        xsum[m] = sum8(x8);
-    }
-    for (int c = j0; c < j1; c += CH3) {
-        const int n = min(CH3, j1 - c);
-        uint32_t wv[CH3][3];
-        uint16_t sv[CH3][3], bv[CH3][3];
-#pragma unroll
-        for (int r = 0; r < CH3; ++r) {
-#pragma unroll
-            for (int m = 0; m < 3; ++m) {
-                if (r < n && valid[m]) {
-                    const uint32_t j = (uint32_t)(c + r);
-                    wv[r][m] = ldg_stream_u32(wb[m] + (uint64_t)j * wstride[m]);
-                    sv[r][m] = ldg_u16(sb[m] + (uint64_t)j * sstride[m]);
-                    bv[r][m] = ldg_u16(bb[m] + (uint64_t)j * sstride[m]);
-                } else {
-                    wv[r][m] = 0; sv[r][m] = 0; bv[r][m] = 0;
-                }
-            }
-        }
-        float v[16];
-#pragma unroll
-        for (int r = 0; r < CH3; ++r) {
-            float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-            for (int m = 0; m < 3; ++m) {
-                const float t = fmaf(bf16f(sv[r][m]), dot_word(wv[r][m], xs[m]), bf16f(bv[r][m]) * xsum[m]);
-                if (shared_seg[m]) a0 += t; else a1 = fmaf(fac[m], t, a1);
-            }
-            v[2 * r] = a0;
-            v[2 * r + 1] = a1;
-        }
-        const float red = warp_transpose_reduce16(v);
-        if (lane < 16) s.part[warp][lane] = red;
-        __syncthreads();
-        if (tid < 2 * CH3) {
-            float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < NWARP; ++w) tot += s.part[w][tid];
-            const int r = tid >> 1;
-            if (r < n) {
-                if (tid & 1) P.h2[c + r] = tot; else P.sh_out[c + r] = tot;
-            }
-        }
-        __syncthreads();
+// L2 prefetch of this CTA's routed-down rows (known once the top-8 is).
+__device__ void prefetch_routed_down(const Smem& s, const GtmLayer& L, int cta, int G) {
+    if ((threadIdx.x >> 5) != NW - 1) return;
+    const int lane = threadIdx.x & 31;
+    const int i0 = share(ITEMS_RD, cta, G), i1 = share(ITEMS_RD, cta + 1, G);
+    for (int i = lane; i < 3 * (i1 - i0); i += 32) {
+        const int it = i0 + i / 3, part = i % 3, k = it / OT, ot = it - k * OT;
+        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
+        if (part == 0) prefetch_l2(blk + L.expert_down.weight + (uint64_t)ot * 16 * (FE / 2), 16 * (FE / 2));
+        else prefetch_l2(blk + (part == 1 ? L.expert_down.scales : L.expert_down.biases) + (uint64_t)ot * 16 * GFE * 2,
+                         16 * GFE * 2);
     }
 }
 
@@ -392,94 +817,92 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x;
     const int G = gridDim.x, cta = blockIdx.x;
-    const GridSync gs{P.flags, P.err, P.sticky};
-    unsigned epoch = 0;
     const GtmDecodeIO& io = P.io;
     const bool writer = cta == 0;
 
+    prefetch_layer_static(P.layers[0], cta, G);
+    load_norms_async(s, &P.layers[0], nullptr);
     for (int i = tid; i < D; i += NT) s.hid[i] = io.hidden_in_dev[i];
     __syncthreads();
 
     for (int l = 0; l < P.num_layers; ++l) {
         const GtmLayer& L = P.layers[l];
-        // ---- P1: tail of the previous layer, views, router -------------------------------
+        const unsigned ep = (unsigned)(l + 1);
+        // ---- P1 ----
         if (l > 0) {
-            for (int i = tid; i < D; i += NT) { s.a[i] = __ldcg(P.h2 + i); s.b[i] = __ldcg(P.sh_out + i); }
-            __syncthreads();
-            const GtmLayer& Lp = P.layers[l - 1];
-            layer_tail(s, Lp, P.eps, writer && io.h1_dev ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
-                       writer && io.h2_dev ? io.h2_dev + (size_t)(l - 1) * D : nullptr);
-            if (io.flags & GTM_DECODE_NORM_BETWEEN_LAYERS) {
-                const float inv = exact_rms_inv(s.hid, D, P.eps, s.red);
-                for (int i = tid; i < D; i += NT) s.hid[i] = __fmul_rn(s.hid[i], inv);
-                __syncthreads();
-            }
-            if (writer && io.hidden_layers_dev)
-                for (int i = tid; i < D; i += NT) io.hidden_layers_dev[(size_t)(l - 1) * D + i] = s.hid[i];
+            if (!wait_all(P, s, BAR_C, ep - 1)) return;
+            tail_and_views(s, P, &P.layers[l - 1], (io.flags & GTM_DECODE_NORM_BETWEEN_LAYERS) != 0, true,
+                           writer && io.h1_dev ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
+                           writer && io.h2_dev ? io.h2_dev + (size_t)(l - 1) * D : nullptr,
+                           writer && io.hidden_layers_dev ? io.hidden_layers_dev + (size_t)(l - 1) * D : nullptr);
+        } else {
+            tail_and_views(s, P, nullptr, false, true, nullptr, nullptr, nullptr);
         }
-        views(s, L, P.eps, P.inv_sqrt_d);
         for (int row = cta; row < NE; row += G) {
             float lg = router_row(s, L, row);
             if (tid == 0) {
                 if (io.logit_bias_dev) lg = __fadd_rn(lg, io.logit_bias_dev[(size_t)l * NE + row]);
                 P.logits[row] = lg;
             }
+            __syncthreads();
         }
-        if (!grid_barrier(gs, ++epoch, kTimeoutNs, &s.flag)) return;
+        arrive(P, BAR_A1, ep);
+        shared_gate_up(s, P, L, share(TILES_S, cta, G), share(TILES_S, cta + 1, G));
+        arrive(P, BAR_A2, ep);
 
-        // ---- P2: top-8, gate/up + GeGLU -------------------------------------------------
+        // ---- P2 ----
+        if (!wait_all(P, s, BAR_A1, ep)) return;
         select_topk(s, L, P.logits, writer, io.topk_idx_dev ? io.topk_idx_dev + (size_t)l * TOPK : nullptr,
                     io.topk_w_dev ? io.topk_w_dev + (size_t)l * TOPK : nullptr,
                     io.logits_dev ? io.logits_dev + (size_t)l * NE : nullptr);
         __syncthreads();
-        {
-            const int u0 = (int)((long long)cta * UNITS / G), u1 = (int)((long long)(cta + 1) * UNITS / G);
-            if (u0 < UNITS_R) {
-                const XSlice xs = make_xslice(s.xr + 8 * tid);
-                gate_up_range(s, L, P, u0, min(u1, UNITS_R), true, xs, sum8(s.xr + 8 * tid));
-            }
-            if (u1 > UNITS_R) {
-                const XSlice xs = make_xslice(s.xd + 8 * tid);
-                gate_up_range(s, L, P, max(u0, UNITS_R), u1, false, xs, sum8(s.xd + 8 * tid));
-            }
-        }
-        if (!grid_barrier(gs, ++epoch, kTimeoutNs, &s.flag)) return;
+        prefetch_routed_down(s, L, cta, G);
+        routed_gate_up(s, P, L, share(TILES_R, cta, G), share(TILES_R, cta + 1, G));
+        arrive(P, BAR_B, ep);
+        if (!wait_all(P, s, BAR_A2, ep)) return;
+        stage_from_global(s.ab, P.act + ACT_R, FS);
+        build_table(s.ab, GFS, s.tbl_sh, s.xs_sh, s.cs_sh);
+        __syncthreads();
+        shared_down(s, P, L, share(ITEMS_SD, cta, G), share(ITEMS_SD, cta + 1, G));
 
-        // ---- P3: down + combine ------------------------------------------------------------
-        {
-            const int j0 = (int)((long long)cta * D / G), j1 = (int)((long long)(cta + 1) * D / G);
-            down_range(s, L, P, j0, j1);
-        }
-        if (!grid_barrier(gs, ++epoch, kTimeoutNs, &s.flag)) return;
+        // ---- P3 ----
+        if (!wait_all(P, s, BAR_B, ep)) return;
+        stage_from_global(s.ab, P.act, ACT_R);
+        build_table(s.ab, TOPK * GFE, s.tbl_rk, s.xs_rk, s.cs_rk);
+        __syncthreads();
+        if (l + 1 < P.num_layers) prefetch_layer_static(P.layers[l + 1], cta, G);
+        load_norms_async(s, l + 1 < P.num_layers ? &P.layers[l + 1] : nullptr, &L);
+        routed_down(s, P, L, share(ITEMS_RD, cta, G), share(ITEMS_RD, cta + 1, G));
+        arrive(P, BAR_C, ep);
     }
 
     // final tail by CTA 0
     if (!writer) return;
     const int l = P.num_layers;
-    for (int i = tid; i < D; i += NT) { s.a[i] = __ldcg(P.h2 + i); s.b[i] = __ldcg(P.sh_out + i); }
-    __syncthreads();
-    layer_tail(s, P.layers[l - 1], P.eps, io.h1_dev ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
-               io.h2_dev ? io.h2_dev + (size_t)(l - 1) * D : nullptr);
-    for (int i = tid; i < D; i += NT) {
-        io.hidden_out_dev[i] = s.hid[i];
-        if (io.hidden_layers_dev) io.hidden_layers_dev[(size_t)(l - 1) * D + i] = s.hid[i];
-    }
+    if (!wait_all(P, s, BAR_C, (unsigned)l)) return;
+    tail_and_views(s, P, &P.layers[l - 1], false, false, io.h1_dev ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
+                   io.h2_dev ? io.h2_dev + (size_t)(l - 1) * D : nullptr,
+                   io.hidden_layers_dev ? io.hidden_layers_dev + (size_t)(l - 1) * D : nullptr);
+    for (int i = tid; i < D; i += NT) io.hidden_out_dev[i] = s.hid[i];
 }
 
 }  // namespace dec
 
-// Workspace: [0, 1024) barrier flags and [1024] this launch's error word (both cleared before
-// every launch), [1032] the sticky error word (zero-initialised once by the owner of the
-// workspace, read and cleared by gtm_moe_decode_check), then logits, act, h2, shared out.
-constexpr size_t kStickyOffset = 1032;
+// Workspace: [0, 4096) barrier flags (4 kinds x 256 CTAs) and [4096] this launch's error word,
+// both cleared before every launch; [4100] the sticky error word (zero-initialised once by the
+// workspace's owner, read and cleared by gtm_moe_decode_check); from 4352: logits, act, partials.
+constexpr size_t kErrOffset = 4096, kStickyOffset = 4100, kDataOffset = 4352;
+
 size_t decode_workspace_bytes() {
-    return 2048 + sizeof(float) * (dec::NE + dec::UNITS + 2 * dec::D) + 256;
+    return kDataOffset + sizeof(float) * (dec::NE + dec::ACT_R + dec::FS + (size_t)dec::NSEG * dec::D) + 256;
 }
+size_t decode_sticky_offset() { return kStickyOffset; }
 
 int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, const GtmDecodeIO& io,
                   void* ws, size_t ws_bytes, cudaStream_t stream, int num_ctas) {
     using namespace dec;
-    Params P;  // ~17 KB, copied into the launch's parameter space by the launch call
+    (void)ws_bytes;
+    Params P;
     memset(&P, 0, sizeof(P));
     for (int l = 0; l < num_layers; ++l) P.layers[l] = layers[l];
     P.io = io;
@@ -488,15 +911,13 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
     P.inv_sqrt_d = 1.0f / sqrtf((float)D);
     unsigned char* w = static_cast<unsigned char*>(ws);
     P.flags = reinterpret_cast<unsigned*>(w);
-    P.err = reinterpret_cast<int*>(w + 1024);
+    P.err = reinterpret_cast<int*>(w + kErrOffset);
     P.sticky = reinterpret_cast<int*>(w + kStickyOffset);
-    float* f = reinterpret_cast<float*>(w + 2048);
+    float* f = reinterpret_cast<float*>(w + kDataOffset);
     P.logits = f;
     P.act = f + NE;
-    P.h2 = P.act + UNITS;
-    P.sh_out = P.h2 + D;
-    (void)ws_bytes;
-    cudaError_t e = cudaMemsetAsync(w, 0, 1028, stream);   // barrier flags restart at epoch 0
+    P.part = P.act + ACT_R + FS;
+    cudaError_t e = cudaMemsetAsync(w, 0, kErrOffset + sizeof(int), stream);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: memset", e);
     const size_t smem = sizeof(Smem);
     static bool attr_done = false;
