@@ -178,6 +178,42 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
  * calls (synchronises `stream`). Returns GTM_OK or GTM_ERR_TIMEOUT. */
 GTM_API int gtm_moe_decode_check(void* workspace_dev, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * MoE block for T > 1 tokens (batched decode, prefill): one layer, tokens grouped by expert.
+ * The reference has no batched path (prefill runs the per-token chain, src/runner.cpp:845-854);
+ * this replaces that loop for one layer with routing, a tcgen05 grouped GEMM over the routed
+ * and shared experts, and the combine + layer tail.
+ * ------------------------------------------------------------------------------------- */
+
+typedef struct GtmTokensIO {
+    uint32_t num_tokens;             /* T >= 1                                              */
+    const float* x_dev;              /* [T][hidden] fp32 block input, or NULL ...           */
+    const uint16_t* x_bf16_dev;      /* ... [T][hidden] bf16 block input                    */
+    float* hidden_out_dev;           /* [T][hidden]                                         */
+    /* Optional outputs (NULL to skip): */
+    uint32_t* topk_idx_dev;          /* [T][top_k]                                          */
+    float* topk_w_dev;               /* [T][top_k]                                          */
+    float* logits_dev;               /* [T][experts] router logits after the bias           */
+    float* h1_dev;                   /* [T][hidden] normed shared-expert output             */
+    float* h2_dev;                   /* [T][hidden] weighted routed-expert sum              */
+    /* Optional inputs: */
+    const float* logit_bias_dev;     /* [experts] added to every token's logits (NULL = none) */
+    const float* route_logits_dev;   /* [T][experts] routing logits given by the caller; the
+                                        router GEMV is skipped (NULL = compute them)        */
+} GtmTokensIO;
+
+/* Workspace for gtm_moe_tokens with up to `max_tokens` tokens (0 for unsupported dims).
+ * Zero it once before its first use; a workspace serves one stream at a time. */
+GTM_API size_t gtm_moe_tokens_workspace_bytes(const GtmDims* dims, uint32_t max_tokens);
+/* One layer for io->num_tokens tokens. Routing (router logits in the reference's exact order,
+ * bit-identical top-k indices), grouped expert products on the tensor cores with int4 dequant in
+ * the kernel, combine in router order and the layer tail. Asynchronous; pipeline waits on the
+ * device are bounded (1 s) and reported by gtm_moe_tokens_check. */
+GTM_API int gtm_moe_tokens(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                           void* workspace_dev, size_t workspace_bytes, void* stream);
+/* Reads back and clears the device-side error flag (synchronises `stream`). */
+GTM_API int gtm_moe_tokens_check(void* workspace_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -253,4 +253,71 @@ GTM_API int gtm_moe_decode_check(void* ws, void* stream) {
     return GTM_OK;
 }
 
+// ---- T > 1 tokens -------------------------------------------------------------------------------
+static constexpr uint32_t kMaxTokens = 65536;
+
+static int check_layer(const char* fn, const GtmLayer& L) {
+    if (!L.resident_dev || !L.experts_dev || L.expert_stride == 0)
+        return set_error(GTM_ERR_INVALID, "%s: null base or zero expert stride", fn);
+    if (!aligned(L.resident_dev, 16) || !aligned(L.experts_dev, 16))
+        return set_error(GTM_ERR_MISALIGNED, "%s: base pointers must be 16-byte aligned", fn);
+    const uint64_t offs16[] = {L.router.weight, L.expert_stride, L.expert_gate.weight, L.expert_up.weight,
+                               L.expert_down.weight, L.shared_gate.weight, L.shared_up.weight, L.shared_down.weight};
+    for (uint64_t o : offs16)
+        if (o % 16) return set_error(GTM_ERR_MISALIGNED, "%s: weight offset %llu not 16-byte aligned", fn, (unsigned long long)o);
+    const uint64_t offs2[] = {L.router.scales, L.router.biases, L.router_scale, L.per_expert_scale,
+                              L.shared_gate.scales, L.shared_gate.biases, L.shared_up.scales, L.shared_up.biases,
+                              L.shared_down.scales, L.shared_down.biases, L.expert_gate.scales, L.expert_gate.biases,
+                              L.expert_up.scales, L.expert_up.biases, L.expert_down.scales, L.expert_down.biases,
+                              L.pre_ffn_norm, L.pre_ffn_norm_2, L.post_ffn_norm_1, L.post_ffn_norm_2,
+                              L.post_ffn_norm, L.layer_scalar};
+    for (uint64_t o : offs2)
+        if (o % 2) return set_error(GTM_ERR_MISALIGNED, "%s: bf16 offset %llu is odd", fn, (unsigned long long)o);
+    return GTM_OK;
+}
+
+GTM_API size_t gtm_moe_tokens_workspace_bytes(const GtmDims* dims, uint32_t max_tokens) {
+    if (!dims || !dims_supported(dims) || max_tokens == 0 || max_tokens > kMaxTokens) return 0;
+    return tokens_workspace_bytes(max_tokens);
+}
+
+GTM_API int gtm_moe_tokens(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io, void* ws,
+                           size_t ws_bytes, void* stream) {
+    if (!dims || !layer || !io) return set_error(GTM_ERR_INVALID, "gtm_moe_tokens: null argument");
+    if (!dims_supported(dims))
+        return set_error(GTM_ERR_UNSUPPORTED,
+                         "gtm_moe_tokens: built for hidden 2816, moe 704, ffn 2112, 128 experts, top-8 (got %u/%u/%u/%u/%u)",
+                         dims->hidden, dims->moe_inter, dims->ffn_inter, dims->num_experts, dims->top_k);
+    const uint32_t T = io->num_tokens;
+    if (T == 0 || T > kMaxTokens)
+        return set_error(GTM_ERR_INVALID, "gtm_moe_tokens: num_tokens=%u (1..%u)", T, kMaxTokens);
+    if ((io->x_dev == nullptr) == (io->x_bf16_dev == nullptr))
+        return set_error(GTM_ERR_INVALID, "gtm_moe_tokens: give exactly one of x_dev and x_bf16_dev");
+    if (!io->hidden_out_dev) return set_error(GTM_ERR_INVALID, "gtm_moe_tokens: hidden_out_dev is NULL");
+    if (!aligned(io->x_dev, 4) || !aligned(io->x_bf16_dev, 2) || !aligned(io->hidden_out_dev, 4) ||
+        !aligned(io->h1_dev, 4) || !aligned(io->h2_dev, 4) || !aligned(io->logits_dev, 4) ||
+        !aligned(io->topk_idx_dev, 4) || !aligned(io->topk_w_dev, 4) || !aligned(io->logit_bias_dev, 4) ||
+        !aligned(io->route_logits_dev, 4))
+        return set_error(GTM_ERR_MISALIGNED, "gtm_moe_tokens: an io pointer is not aligned to its element size");
+    const size_t need = tokens_workspace_bytes(T);
+    if (!ws || ws_bytes < need || !aligned(ws, 256))
+        return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes, 256-byte aligned", need);
+    int rc = check_layer("gtm_moe_tokens", *layer);
+    if (rc) return rc;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return set_cuda_error("gtm_moe_tokens: device query", e);
+    rc = launch_tokens(*dims, *layer, *io, ws, ws_bytes, (cudaStream_t)stream, sms);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_tokens_check(void* ws, void* stream) {
+    if (!ws) return set_error(GTM_ERR_INVALID, "gtm_moe_tokens_check: null workspace");
+    const int rc = tokens_check(ws, (cudaStream_t)stream);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
 }  // extern "C"

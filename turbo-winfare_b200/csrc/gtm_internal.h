@@ -18,6 +18,11 @@ constexpr int kDecodeMinCtas = 118;   // per-CTA work lists of the fused decode 
 int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, const GtmDecodeIO& io,
                   void* ws, size_t ws_bytes, cudaStream_t stream, int num_ctas);
 
+size_t tokens_workspace_bytes(uint32_t max_tokens);
+int launch_tokens(const GtmDims& dims, const GtmLayer& layer, const GtmTokensIO& io, void* ws, size_t ws_bytes,
+                  cudaStream_t stream, int num_sms);
+int tokens_check(void* ws, cudaStream_t stream);
+
 // generic kernels (gtm_kernels.cu); arguments already validated
 void k_gemv_exact(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
                   const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st);

@@ -9,7 +9,10 @@ The classes mirror the reference's MoE section of ForwardRunner::produce_token
 
 * ``SynthModel`` -- random-init weights of the Gemma-4-26B-A4B MoE shape in the .gturbo byte
   layouts (per-layer expert image + resident tensors), generated on the device;
-* ``Decoder`` -- one token through N MoE layers in one fused launch (gtm_moe_decode).
+* ``Decoder`` -- one token through N MoE layers in one fused launch (gtm_moe_decode);
+* ``TokenBlock`` -- T > 1 tokens through one MoE layer: routing, tcgen05 grouped expert
+  products and combine (gtm_moe_tokens), replacing the reference's token-at-a-time prefill
+  loop (src/runner.cpp:845-854).
 """
 from __future__ import annotations
 
@@ -62,6 +65,13 @@ class DecodeIO(C.Structure):
                 ("flags", C.c_uint32)]
 
 
+class TokensIO(C.Structure):
+    _fields_ = [("num_tokens", C.c_uint32), ("x_dev", C.c_void_p), ("x_bf16_dev", C.c_void_p),
+                ("hidden_out_dev", C.c_void_p), ("topk_idx_dev", C.c_void_p), ("topk_w_dev", C.c_void_p),
+                ("logits_dev", C.c_void_p), ("h1_dev", C.c_void_p), ("h2_dev", C.c_void_p),
+                ("logit_bias_dev", C.c_void_p), ("route_logits_dev", C.c_void_p)]
+
+
 _lib = None
 
 # (name, restype, argtypes) for every entry point in include/gtmoe.h and include/gtmoe_synth.h
@@ -82,6 +92,9 @@ SIGNATURES = {
     "gtm_moe_decode_workspace_bytes": (_SZ, [C.POINTER(Dims)]),
     "gtm_moe_decode": (_I, [C.POINTER(Dims), C.POINTER(Layer), _I, C.POINTER(DecodeIO), _P, _SZ, _P]),
     "gtm_moe_decode_check": (_I, [_P, _P]),
+    "gtm_moe_tokens_workspace_bytes": (_SZ, [C.POINTER(Dims), _U32]),
+    "gtm_moe_tokens": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), _P, _SZ, _P]),
+    "gtm_moe_tokens_check": (_I, [_P, _P]),
     "gtm_synth_expert_layout": (_I, [_U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_resident_layout": (_I, [_U32, _U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_experts": (_I, [_U64, _U32, _U32, _U32, _U32, _U32, _P, _P]),
@@ -250,3 +263,36 @@ class Decoder:
 
     def check(self, stream=None):
         check(lib().gtm_moe_decode_check(self.ws_ptr, _stream(stream)))
+
+
+class TokenBlock:
+    """T > 1 tokens through one MoE layer (gtm_moe_tokens), workspace sized for `max_tokens`."""
+
+    def __init__(self, max_tokens: int, device: str = "cuda"):
+        import torch
+        self.dims = default_dims()
+        self.max_tokens = max_tokens
+        n = lib().gtm_moe_tokens_workspace_bytes(C.byref(self.dims), max_tokens)
+        if n == 0:
+            raise GtmError(ERR_UNSUPPORTED, f"tokens workspace size query failed for {max_tokens} tokens")
+        self.workspace = torch.zeros(n + 256, dtype=torch.uint8, device=device)  # zeroed once, as required
+        base = self.workspace.data_ptr()
+        self.ws_ptr = C.c_void_p((base + 255) // 256 * 256)
+        self.ws_bytes = n
+
+    def __call__(self, layer: Layer, x, hidden_out, *, topk_idx=None, topk_w=None, logits=None, h1=None, h2=None,
+                 logit_bias=None, route_logits=None, stream=None):
+        """x: [T, hidden] float32 or bfloat16 on the device; hidden_out: [T, hidden] float32."""
+        import torch
+        T = x.shape[0]
+        xf = x if x.dtype == torch.float32 else None
+        xb = x if x.dtype == torch.bfloat16 else None
+        if xf is None and xb is None:
+            raise TypeError("x must be float32 or bfloat16")
+        io = TokensIO(T, ptr(xf), ptr(xb), hidden_out.data_ptr(), ptr(topk_idx), ptr(topk_w), ptr(logits), ptr(h1),
+                      ptr(h2), ptr(logit_bias), ptr(route_logits))
+        check(lib().gtm_moe_tokens(C.byref(self.dims), C.byref(layer), C.byref(io), self.ws_ptr, self.ws_bytes,
+                                   _stream(stream)))
+
+    def check(self, stream=None):
+        check(lib().gtm_moe_tokens_check(self.ws_ptr, _stream(stream)))
