@@ -25,13 +25,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false (and raises *abort) when `limit_ns` passes or *abort is set.
+// try_wait that lets the hardware suspend the thread until the phase completes or `hint_ns` passes.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+// Bounded wait: returns false (and raises *abort) when `limit_ns` passes or *abort is set. The
+// waiting thread sleeps in the hardware wait (up to 0.5 ms per try) instead of spinning, so
+// waiting warps take no issue slots; the abort flag and the clock are read once per try.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     for (;;) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;
         if (*abort) return false;
         uint64_t t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -44,7 +53,25 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
                  :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int32_t x, int32_t y, int32_t z, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
+}
+// L2 prefetch of the 16-byte-aligned part of [p, p + bytes) (rounded inwards, so it never touches
+// bytes outside the range), issued in 32 KB pieces.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint64_t bytes) {
+    const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15);
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t(15);
+    for (uintptr_t o = a; o < e; o += 32768) {
+        const uint32_t n = (uint32_t)(e - o < 32768 ? e - o : 32768);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(o), "r"(n) : "memory");
+    }
+}
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Barrier among `nthreads` threads (whole warps) on hardware barrier `id` (1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
 
 // ---- tcgen05 ------------------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {

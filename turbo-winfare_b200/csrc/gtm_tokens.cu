@@ -8,22 +8,33 @@
 //                         order (or caller-given routing logits), optional logit bias, top-8
 //   2. tok_route          counts per expert, token-slot rows grouped by expert, GEMM tile lists
 //   3. tok_gather         routed_x rows in expert order, split into fp16 high and low parts
-//   4. grouped_gemm<0>    gate/up of the 8 routed experts and the shared expert, GeGLU fused,
+//   4. grouped_gemm<0>    gate/up of the routed experts and the shared expert, GeGLU fused,
 //                         activations written as fp16 high/low parts
 //   5. grouped_gemm<1>    down projections, routing weight fused (routed rows)
 //   6. tok_combine        h2 = sum over the 8 slots in router order, shared output, layer tail
 //
-// Grouped GEMM (one CTA per SM, persistent over a device-built tile list). A tile is 128 token
-// rows x 512 output features (four 128-column fp32 accumulators in TMEM) over K in blocks of 64
-// (one quantisation group). Operand A (tokens) is the fp16 high part and the fp16 low part of the
-// activations, each loaded by TMA in the 128-byte swizzle layout; both are multiplied against the
-// same B tile, so the products carry ~22 bits of the activation. Operand B (features) is the int4
-// weight matrix dequantised in the kernel by six producer warps to fp16 w = q * scale + bias
-// (exact when the bias is a multiple of the scale that fits fp16, as for the benchmark's
-// zero-point 8) and written straight into the swizzled layout. One thread issues the tcgen05.mma
-// (M=128, N=128, K=16); mbarriers hand stages between TMA, dequant and MMA; the epilogue warps read
-// TMEM with tcgen05.ld. Every wait is bounded; on expiry the CTA unwinds, frees its TMEM and
-// reports through the error word.
+// Grouped GEMM: one CTA per SM, persistent over a tile list built on the device. A tile is 256
+// weight rows (two MMA M=128 halves, two TMEM accumulators) by up to 128 tokens of one expert
+// (MMA N), over K in blocks of 64 (one quantisation group): D[row][token] += W[row][k] X[token][k].
+// Gate/up tiles put 128 gate rows in one half and the same 128 up rows in the other, so one
+// epilogue thread holds both halves of its GeGLU pair. Per K block:
+//   * warps 8-15 (one thread per weight row) fetch the row's 32 packed bytes through a private
+//     cp.async pipeline 6 blocks deep, dequantise them to fp16 w = q * scale + bias (the bf16
+//     scale/bias prefetched into registers two blocks ahead; w is exact in fp16 when the bias is
+//     a small multiple of the scale, as for zero-point-8 weights) and store the row in the
+//     128-byte swizzle layout the MMA reads;
+//   * warp 0 loads the activation tile by TMA, the fp16 high part and the fp16 low part
+//     (x - hi), so the MMAs against the same weights carry ~22 bits of the activation; it also
+//     prefetches the CTA's next tile of weights into L2;
+//   * one thread of warp 1 issues tcgen05.mma (kind::f16, M=128, N=16..128, K=16) for both halves
+//     and both activation parts into one of two TMEM accumulator sets, committing stage and tile
+//     completion to mbarriers;
+//   * warps 4-7 drain the other accumulator set with tcgen05.ld while the next tile runs.
+// Within every 8-element chunk of K the dequantised weights come out in the order
+// (0,4,1,5,2,6,3,7), the order the nibble extraction yields; activations are stored in the same
+// order, so the products are unchanged and no permute instructions are spent.
+// Every wait is bounded; on expiry the CTA unwinds, frees its TMEM and reports through the error
+// word of the workspace.
 #include <cstdint>
 #include <cstring>
 #include <cuda.h>
@@ -38,20 +49,39 @@ namespace gtm {
 namespace tok {
 
 constexpr int D = 2816, FE = 704, FS = 2112, NE = 128, TOPK = 8, GD = D / kGroup;
-constexpr int BM = 128, BK = 64, NSUB = 4, BNF = NSUB * 128, STAGES = 2;
-constexpr int GEMM_THREADS = 256;
-constexpr int DQ_THREADS = 192;          // warps 2..7
-constexpr uint32_t A_TILE = BM * BK * 2; // 16 KB per fp16 operand tile
-constexpr uint32_t B_TILE = BNF * BK * 2;  // 64 KB
+constexpr int BK = 64;                  // K block = one quantisation group
+constexpr int NT = 128;                 // tokens per tile (MMA N, at most)
+constexpr int SX = 3;                   // activation stages
+constexpr int SW = 2;                   // dequantised-weight stages
+constexpr int DR = 6;                   // packed-weight cp.async depth per dequant thread
+constexpr int THREADS = 512;
+constexpr int DQ0 = 256, DQ_THREADS = 256;   // dequant threads: warps 8..15, one weight row each
+constexpr uint32_t W_TILE = 256 * BK * 2;    // 32 KB fp16 weights (two 128-row halves)
+constexpr uint32_t X_TILE = NT * BK * 2;     // 16 KB per activation part
+constexpr uint32_t XBOX = 32 * BK * 2;       // 4 KB: one TMA box of 32 token rows
+constexpr uint32_t RAW_TILE = 256 * 32;      // 8 KB packed int4 per K block
+constexpr size_t SMEM_BYTES = 1024 + SW * W_TILE + 2 * SX * X_TILE + DR * RAW_TILE + (2 * SX + 2 * SW + 4) * 8 + 16;
+constexpr int FB0_R = (FE + 127) / 128, FB0_S = (FS + 127) / 128;   // gate/up tiles: 128 intermediate rows
+constexpr int FB1 = D / 256;                                        // down tiles: 256 output rows
 constexpr uint64_t kWaitNs = 1000000000ull;
 constexpr int RIN_PITCH = 65;
 
+static_assert(SMEM_BYTES <= 232448, "grouped GEMM shared memory");
+static_assert(FE % 64 == 0 && FS % 64 == 0 && D % 256 == 0, "tile shapes");
+
 struct Tile {
     int32_t expert;   // routed expert id, or -1 for the shared expert
-    int32_t row0;     // first activation row
-    int32_t rows;     // valid rows (<= 128)
-    int32_t ftile;    // feature tile (512 features)
+    int32_t row0;     // first activation row of the token range
+    int32_t rows;     // tokens (1..NT)
+    int32_t fb;       // weight-row block
 };
+
+// K position of element k inside its 8-element chunk, in the order the dequant produces.
+__host__ __device__ __forceinline__ int kperm(int k) { return (k & ~7) | ((k & 3) << 1) | ((k >> 2) & 1); }
+
+__device__ __forceinline__ const uint16_t* rp16(const void* base, uint64_t off) {
+    return reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(base) + off);
+}
 
 // ================================================================================================
 // 1. views + router + top-8, one CTA per token
@@ -60,12 +90,11 @@ struct ViewsArgs {
     int T;
     const float* x_f32;          // [T][D] or null
     const uint16_t* x_bf16;      // [T][D] or null
-    const uint8_t* resident;
     GtmLayer L;
     float eps, inv_sqrt_d;
     const float* logit_bias;     // [E] or null
     const float* route_logits;   // [T][E] or null
-    __half* dense_hi;            // [T][D]
+    __half* dense_hi;            // [T][D] (K-permuted)
     __half* dense_lo;
     float* routed;               // [T][D] fp32
     uint32_t* idx;               // [T][8]
@@ -73,15 +102,12 @@ struct ViewsArgs {
     float* logits_out;           // [T][E] or null
 };
 
-__device__ __forceinline__ const uint16_t* rp16(const void* base, uint64_t off) {
-    return reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(base) + off);
-}
-
 __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ ViewsArgs A) {
     __shared__ __align__(16) float sx[D];
     __shared__ float srin[GD * RIN_PITCH];
     __shared__ float slog[NE];
     __shared__ double red[40];
+    __shared__ float terms[11][GD];
     const int t = blockIdx.x, tid = threadIdx.x;
     const GtmLayer& L = A.L;
     for (int i = tid; i < D; i += blockDim.x)
@@ -95,8 +121,8 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
         const float h = __fmul_rn(sx[i], inv);
         const float dx = __fmul_rn(h, bf16f(w_pre[i]));
         const __half hi = __float2half_rn(dx);
-        A.dense_hi[(size_t)t * D + i] = hi;
-        A.dense_lo[(size_t)t * D + i] = __float2half_rn(dx - __half2float(hi));
+        A.dense_hi[(size_t)t * D + kperm(i)] = hi;
+        A.dense_lo[(size_t)t * D + kperm(i)] = __float2half_rn(dx - __half2float(hi));
         A.routed[(size_t)t * D + i] = __fmul_rn(h, bf16f(w_pre2[i]));
         srin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(h, bf16f(rs[i])), A.inv_sqrt_d);
     }
@@ -106,9 +132,8 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
     } else {
         // logits in src/cpu_reference.cpp:86-106's order: 11 rows at a time, 44 threads a row
         const uint8_t* W = static_cast<const uint8_t*>(L.resident_dev) + L.router.weight;
-        const uint16_t* S = rp16(L.resident_dev, L.router.scales);
-        const uint16_t* B = rp16(L.resident_dev, L.router.biases);
-        __shared__ float terms[11][GD];
+        const uint16_t* Sc = rp16(L.resident_dev, L.router.scales);
+        const uint16_t* Bi = rp16(L.resident_dev, L.router.biases);
         for (int r0 = 0; r0 < NE; r0 += 11) {
             const int rr = tid / GD, g = tid - rr * GD, row = r0 + rr;
             if (rr < 11 && row < NE) {
@@ -128,7 +153,7 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
                             sum = __fadd_rn(sum, xv);
                         }
                 }
-                terms[rr][g] = __fadd_rn(__fmul_rn(bf16f(S[row * GD + g]), dot), __fmul_rn(bf16f(B[row * GD + g]), sum));
+                terms[rr][g] = __fadd_rn(__fmul_rn(bf16f(Sc[row * GD + g]), dot), __fmul_rn(bf16f(Bi[row * GD + g]), sum));
             }
             __syncthreads();
             if (tid < 11 && r0 + tid < NE) {
@@ -141,16 +166,16 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
     }
     __syncthreads();
     if (tid < 32) {
+        // top-8 by (value desc, index asc), src/cpu_reference.cpp:447-480
         const int lane = tid;
-        float v[4];
         uint32_t key[4];
         bool taken[4] = {false, false, false, false};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int e = lane + 32 * j;
-            v[j] = A.logit_bias ? __fadd_rn(slog[e], A.logit_bias[e]) : slog[e];
-            if (A.logits_out) A.logits_out[(size_t)t * NE + e] = v[j];
-            const uint32_t u = __float_as_uint(v[j] == 0.0f ? 0.0f : v[j]);
+            const float v = A.logit_bias ? __fadd_rn(slog[e], A.logit_bias[e]) : slog[e];
+            if (A.logits_out) A.logits_out[(size_t)t * NE + e] = v;
+            const uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
             key[j] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
         }
         float my_sel = 0.0f, top0 = 0.0f;
@@ -188,94 +213,86 @@ struct RouteArgs {
     int T;
     const uint32_t* idx;     // [T][8]
     const float* w;          // [T][8]
-    int* counts;             // [E]
-    int* offsets;            // [E + 1]
-    int* perm_token;         // [8T]
-    float* perm_w;           // [8T]
-    int* pos;                // [T][8]
+    int* perm_token;         // [8T] token of each expert-ordered row
+    float* perm_w;           // [8T] routing weight of each row
+    int* pos;                // [T][8] row of each (token, slot)
     Tile* tiles0;            // gate/up tiles
     Tile* tiles1;            // down tiles
     int* n_tiles;            // [2]
 };
 
-constexpr int FT0_R = (2 * FE + BNF - 1) / BNF;   // 3 feature tiles of routed gate/up (1408 features)
-constexpr int FT0_S = (2 * FS + BNF - 1) / BNF;   // 9 of shared gate/up (4224)
-constexpr int FT1 = (D + BNF - 1) / BNF;          // 6 of the down projections (2816)
+__device__ __forceinline__ int ntok_tiles(int c) { return (c + NT - 1) / NT; }
 
 __global__ void __launch_bounds__(1024) tok_route(const __grid_constant__ RouteArgs A) {
     __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
     const int tid = threadIdx.x, n = A.T * TOPK;
     for (int e = tid; e < NE; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-        const int e = (int)A.idx[i];
-        A.pos[i] = atomicAdd(&cnt[e], 1);          // slot within the expert, completed below
-    }
+    for (int i = tid; i < n; i += blockDim.x) A.pos[i] = atomicAdd(&cnt[(int)A.idx[i]], 1);
     __syncthreads();
     if (tid == 0) {
         int o = 0, a = 0, b = 0;
         for (int e = 0; e < NE; ++e) {
             off[e] = o; t0[e] = a; t1[e] = b;
-            const int mt = (cnt[e] + BM - 1) / BM;
-            o += cnt[e]; a += mt * FT0_R; b += mt * FT1;
+            const int nt = ntok_tiles(cnt[e]);
+            o += cnt[e]; a += nt * FB0_R; b += nt * FB1;
         }
         off[NE] = o; t0[NE] = a; t1[NE] = b;
     }
     __syncthreads();
     for (int i = tid; i < n; i += blockDim.x) {
-        const int e = (int)A.idx[i];
-        const int row = off[e] + A.pos[i];
+        const int row = off[(int)A.idx[i]] + A.pos[i];
         A.pos[i] = row;
         A.perm_token[row] = i / TOPK;
         A.perm_w[row] = A.w[i];
     }
+    // tiles of one (expert, row block) are adjacent over the token ranges, for L2 reuse of the weights
     for (int e = tid; e < NE; e += blockDim.x) {
-        A.counts[e] = cnt[e];
-        A.offsets[e] = off[e];
-        const int mt = (cnt[e] + BM - 1) / BM;
-        for (int m = 0; m < mt; ++m) {
-            const int r0 = off[e] + m * BM, rows = min(BM, cnt[e] - m * BM);
-            for (int f = 0; f < FT0_R; ++f) A.tiles0[t0[e] + m * FT0_R + f] = Tile{e, r0, rows, f};
-            for (int f = 0; f < FT1; ++f) A.tiles1[t1[e] + m * FT1 + f] = Tile{e, r0, rows, f};
+        const int c = cnt[e], nt = ntok_tiles(c);
+        for (int m = 0; m < nt; ++m) {
+            const int r0 = c * m / nt, r1 = c * (m + 1) / nt;
+            for (int f = 0; f < FB0_R; ++f) A.tiles0[t0[e] + f * nt + m] = Tile{e, off[e] + r0, r1 - r0, f};
+            for (int f = 0; f < FB1; ++f) A.tiles1[t1[e] + f * nt + m] = Tile{e, off[e] + r0, r1 - r0, f};
         }
     }
-    if (tid == 0) A.offsets[NE] = off[NE];
-    // shared expert over all T tokens, after the routed tiles
-    const int mts = (A.T + BM - 1) / BM;
-    for (int i = tid; i < mts * FT0_S; i += blockDim.x) {
-        const int m = i / FT0_S, f = i - m * FT0_S;
-        A.tiles0[t0[NE] + i] = Tile{-1, m * BM, min(BM, A.T - m * BM), f};
+    const int nts = ntok_tiles(A.T);
+    for (int i = tid; i < nts * FB0_S; i += blockDim.x) {
+        const int f = i / nts, m = i - f * nts, r0 = A.T * m / nts, r1 = A.T * (m + 1) / nts;
+        A.tiles0[t0[NE] + i] = Tile{-1, r0, r1 - r0, f};
     }
-    for (int i = tid; i < mts * FT1; i += blockDim.x) {
-        const int m = i / FT1, f = i - m * FT1;
-        A.tiles1[t1[NE] + i] = Tile{-1, m * BM, min(BM, A.T - m * BM), f};
+    for (int i = tid; i < nts * FB1; i += blockDim.x) {
+        const int f = i / nts, m = i - f * nts, r0 = A.T * m / nts, r1 = A.T * (m + 1) / nts;
+        A.tiles1[t1[NE] + i] = Tile{-1, r0, r1 - r0, f};
     }
     if (tid == 0) {
-        A.n_tiles[0] = t0[NE] + mts * FT0_S;
-        A.n_tiles[1] = t1[NE] + mts * FT1;
+        A.n_tiles[0] = t0[NE] + nts * FB0_S;
+        A.n_tiles[1] = t1[NE] + nts * FB1;
     }
 }
 
 // ================================================================================================
-// 3. gather routed_x rows in expert order as fp16 high / low parts
+// 3. gather routed_x rows in expert order as fp16 high / low parts (K-permuted)
 // ================================================================================================
-__global__ void __launch_bounds__(256) tok_gather(const float* routed, const int* perm_token, __half* xhi, __half* xlo) {
+__global__ void __launch_bounds__(128) tok_gather(const float* routed, const int* perm_token, __half* xhi, __half* xlo) {
     const int row = blockIdx.x;
-    const int t = perm_token[row];
-    const float4* src = reinterpret_cast<const float4*>(routed + (size_t)t * D);
-    for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
-        const float4 v = src[i];
-        const float f[4] = {v.x, v.y, v.z, v.w};
-        __half h[4], l[4];
+    const float4* src = reinterpret_cast<const float4*>(routed + (size_t)perm_token[row] * D);
+    for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
+        const float4 a = src[2 * c], b = src[2 * c + 1];
+        const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        uint16_t h[8], l[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            h[q] = __float2half_rn(f[q]);
-            l[q] = __float2half_rn(f[q] - __half2float(h[q]));
+        for (int e = 0; e < 8; ++e) {
+            const __half hv = __float2half_rn(f[e]);
+            h[kperm(e)] = __half_as_ushort(hv);
+            l[kperm(e)] = __half_as_ushort(__float2half_rn(f[e] - __half2float(hv)));
         }
-        __half2* dh = reinterpret_cast<__half2*>(xhi + (size_t)row * D) + 2 * i;
-        __half2* dl = reinterpret_cast<__half2*>(xlo + (size_t)row * D) + 2 * i;
-        dh[0] = __halves2half2(h[0], h[1]); dh[1] = __halves2half2(h[2], h[3]);
-        dl[0] = __halves2half2(l[0], l[1]); dl[1] = __halves2half2(l[2], l[3]);
+        uint4 ph, pl;
+        ph.x = h[0] | ((uint32_t)h[1] << 16); ph.y = h[2] | ((uint32_t)h[3] << 16);
+        ph.z = h[4] | ((uint32_t)h[5] << 16); ph.w = h[6] | ((uint32_t)h[7] << 16);
+        pl.x = l[0] | ((uint32_t)l[1] << 16); pl.y = l[2] | ((uint32_t)l[3] << 16);
+        pl.z = l[4] | ((uint32_t)l[5] << 16); pl.w = l[6] | ((uint32_t)l[7] << 16);
+        reinterpret_cast<uint4*>(xhi + (size_t)row * D)[c] = ph;
+        reinterpret_cast<uint4*>(xlo + (size_t)row * D)[c] = pl;
     }
 }
 
@@ -283,54 +300,45 @@ __global__ void __launch_bounds__(256) tok_gather(const float* routed, const int
 // 4/5. grouped GEMM
 // ================================================================================================
 struct GemmArgs {
-    CUtensorMap map_r_hi, map_r_lo, map_s_hi, map_s_lo;   // A operands (routed rows / shared rows)
+    CUtensorMap x_rhi, x_rlo, x_shi, x_slo;   // activations, 2D fp16, 32-row boxes
     const Tile* tiles;
     const int* n_tiles;
     const uint8_t* experts;
     uint64_t expert_stride;
-    GtmQuant ex_a, ex_b;        // routed: gate, up (mode 0) or down (mode 1)
+    uint64_t r_wa, r_wb, r_sa, r_ba, r_sb, r_bb;   // routed weight / scale / bias byte offsets (matrix a, b)
     const uint8_t* resident;
-    GtmQuant sh_a, sh_b;        // shared: gate, up (mode 0) or down (mode 1)
-    int k_r, k_s;               // input width of the routed / shared operand
-    int nf_r, nf_s;             // output features (mode 0: 2 x intermediate, gate/up interleaved)
-    __half* act_r_hi; __half* act_r_lo;   // mode 0 outputs [rows][k of mode 1]
+    uint64_t s_wa, s_wb, s_sa, s_ba, s_sb, s_bb;   // shared
+    int k_r, k_s;                         // K of the routed / shared matrices
+    int rows_r, rows_s;                   // rows of each routed / shared matrix
+    __half* act_r_hi; __half* act_r_lo;   // mode 0 outputs, rows of FE (routed) / FS (shared)
     __half* act_s_hi; __half* act_s_lo;
     float* out_r; float* out_s;           // mode 1 outputs [rows][D]
     const float* perm_w;                  // mode 1: routing weight per routed row
     int* err;
 };
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t d;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-    return d;
-}
-
-// 8 int4 (low nibble first) -> 8 fp16 w = q * s + b in element order, packed in a uint4.
-__device__ __forceinline__ uint4 dequant8(uint32_t w, uint32_t s2, uint32_t b2) {
+// 8 int4 (low nibble first) -> 8 fp16 w = q * s + b in the order (0,4,1,5,2,6,3,7).
+__device__ __forceinline__ uint4 dq8(uint32_t w, uint32_t s2, uint32_t b2) {
     const uint32_t m = 0x64006400u, w8 = w >> 8;
     uint32_t l0, h0, l1, h1;
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(l0) : "r"(w), "r"(0x000F000Fu), "r"(m));
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(h0) : "r"(w), "r"(0x00F000F0u), "r"(m));
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(l1) : "r"(w8), "r"(0x000F000Fu), "r"(m));
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(h1) : "r"(w8), "r"(0x00F000F0u), "r"(m));
-    uint32_t q0, q1, q2, q3;   // (n0,n4) (n1,n5) (n2,n6) (n3,n7) as exact fp16
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q0) : "r"(l0), "r"(m));
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(q1) : "r"(h0), "r"(0x2C002C00u), "r"(0xD400D400u));
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q2) : "r"(l1), "r"(m));
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(q3) : "r"(h1), "r"(0x2C002C00u), "r"(0xD400D400u));
-    // element order (n0,n1) (n2,n3) (n4,n5) (n6,n7)
-    uint32_t p0 = prmt(q0, q1, 0x5410), p1 = prmt(q2, q3, 0x5410), p2 = prmt(q0, q1, 0x7632), p3 = prmt(q2, q3, 0x7632);
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p0) : "r"(p0), "r"(s2), "r"(b2));
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p1) : "r"(p1), "r"(s2), "r"(b2));
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p2) : "r"(p2), "r"(s2), "r"(b2));
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p3) : "r"(p3), "r"(s2), "r"(b2));
-    return make_uint4(p0, p1, p2, p3);
+    uint4 r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(l0) : "r"(l0), "r"(m));                                   // (n0, n4)
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h0) : "r"(h0), "r"(0x2C002C00u), "r"(0xD400D400u));  // (n1, n5)
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(l1) : "r"(l1), "r"(m));                                   // (n2, n6)
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h1) : "r"(h1), "r"(0x2C002C00u), "r"(0xD400D400u));  // (n3, n7)
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r.x) : "r"(l0), "r"(s2), "r"(b2));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r.y) : "r"(h0), "r"(s2), "r"(b2));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r.z) : "r"(l1), "r"(s2), "r"(b2));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r.w) : "r"(h1), "r"(s2), "r"(b2));
+    return r;
 }
 
 __device__ __forceinline__ uint32_t bf16_to_h2(uint16_t b) {
-    const __half h = __float2half_rn(bf16f(b));
-    const uint32_t u = __half_as_ushort(h);
+    const uint32_t u = __half_as_ushort(__float2half_rn(bf16f(b)));
     return u | (u << 16);
 }
 
@@ -338,48 +346,50 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
     return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
 struct TileInfo {
     Tile t;
     bool routed;
-    int K, nkb, nf, nsub;
+    int nkb;
 };
 
 __device__ __forceinline__ TileInfo tile_info(const GemmArgs& A, int i) {
     TileInfo ti;
     ti.t = A.tiles[i];
     ti.routed = ti.t.expert >= 0;
-    ti.K = ti.routed ? A.k_r : A.k_s;
-    ti.nkb = ti.K / BK;
-    ti.nf = ti.routed ? A.nf_r : A.nf_s;
-    ti.nsub = min(NSUB, (ti.nf - ti.t.ftile * BNF + 127) / 128);
+    ti.nkb = (ti.routed ? A.k_r : A.k_s) / BK;
     return ti;
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(GEMM_THREADS, 1) grouped_gemm(const __grid_constant__ GemmArgs A) {
+__global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant__ GemmArgs A) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sAhi = base;                        // [STAGES][16 KB]
-    uint8_t* sAlo = base + STAGES * A_TILE;      // [STAGES][16 KB]
-    uint8_t* sB = base + 2 * STAGES * A_TILE;    // [STAGES][64 KB]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_TILE);
-    uint64_t* a_full = bars;                     // [STAGES]
-    uint64_t* b_full = bars + STAGES;
-    uint64_t* empty = bars + 2 * STAGES;
-    uint64_t* acc_full = bars + 3 * STAGES;
-    uint64_t* acc_empty = acc_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+    uint8_t* sW = base;                          // [SW][2][16 KB] fp16 weights, SW128, two 128-row halves
+    uint8_t* sXh = sW + SW * W_TILE;             // [SX][16 KB]    activation high parts, SW128
+    uint8_t* sXl = sXh + SX * X_TILE;            // [SX][16 KB]    activation low parts
+    uint8_t* sRaw = sXl + SX * X_TILE;           // [DR][256][32]  packed int4, one row per dequant thread
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + DR * RAW_TILE);
+    uint64_t* act_full = bars;
+    uint64_t* act_empty = act_full + SX;
+    uint64_t* w_full = act_empty + SX;
+    uint64_t* w_empty = w_full + SW;
+    uint64_t* acc_full = w_empty + SW;       // [2]
+    uint64_t* acc_empty = acc_full + 2;      // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            tc::mbar_init(&a_full[s], 1);
-            tc::mbar_init(&b_full[s], DQ_THREADS);
-            tc::mbar_init(&empty[s], 1);
-        }
-        tc::mbar_init(acc_full, 1);
-        tc::mbar_init(acc_empty, 128);
+        for (int s = 0; s < SX; ++s) { tc::mbar_init(&act_full[s], 1); tc::mbar_init(&act_empty[s], 1); }
+        for (int s = 0; s < SW; ++s) { tc::mbar_init(&w_full[s], DQ_THREADS); tc::mbar_init(&w_empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], 128); }
         *abort_flag = 0;
         tc::mbar_fence_init();
     }
@@ -389,159 +399,225 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) grouped_gemm(const __grid_con
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int ntiles = *A.n_tiles;
-    const uint32_t idesc = tc::idesc_f16(BM, 128);
 
     if (warp == 0) {
-        // ---- TMA producer: activation high/low tiles ----
+        // ---- activation producer; L2 prefetch of the next tile's weights ----
         if (lane == 0) {
+            auto prefetch_tile = [&](int i2) {
+                const TileInfo tn = tile_info(A, i2);
+                const uint8_t* wb = tn.routed ? A.experts + (uint64_t)tn.t.expert * A.expert_stride : A.resident;
+                const uint64_t K = (uint64_t)tn.nkb * BK, G = tn.nkb;
+                const uint64_t nr = tn.routed ? A.rows_r : A.rows_s;
+                const uint64_t span = MODE == 0 ? 128 : 256, j0 = (uint64_t)tn.t.fb * span;
+                const uint64_t rows = j0 + span <= nr ? span : nr - j0;
+                for (int mtx = 0; mtx < (MODE == 0 ? 2 : 1); ++mtx) {
+                    const uint64_t wo = tn.routed ? (mtx ? A.r_wb : A.r_wa) : (mtx ? A.s_wb : A.s_wa);
+                    const uint64_t so = tn.routed ? (mtx ? A.r_sb : A.r_sa) : (mtx ? A.s_sb : A.s_sa);
+                    const uint64_t bo = tn.routed ? (mtx ? A.r_bb : A.r_ba) : (mtx ? A.s_bb : A.s_ba);
+                    tc::prefetch_l2_bulk(wb + wo + j0 * (K / 2), rows * (K / 2));
+                    tc::prefetch_l2_bulk(wb + so + j0 * G * 2, rows * G * 2);
+                    tc::prefetch_l2_bulk(wb + bo + j0 * G * 2, rows * G * 2);
+                }
+            };
+            if ((int)blockIdx.x < ntiles) prefetch_tile(blockIdx.x);
             uint32_t it = 0;
             bool ok = true;
             for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+                if (i + (int)gridDim.x < ntiles) prefetch_tile(i + gridDim.x);
                 const TileInfo ti = tile_info(A, i);
-                const CUtensorMap* mh = ti.routed ? &A.map_r_hi : &A.map_s_hi;
-                const CUtensorMap* ml = ti.routed ? &A.map_r_lo : &A.map_s_lo;
+                const CUtensorMap* mh = ti.routed ? &A.x_rhi : &A.x_shi;
+                const CUtensorMap* ml = ti.routed ? &A.x_rlo : &A.x_slo;
+                const int nbox = (ti.t.rows + 31) >> 5;
                 for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-                    const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-                    if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitNs)) { ok = false; break; }
-                    tc::mbar_arrive_expect_tx(&a_full[s], 2 * A_TILE);
-                    tc::tma_load_2d(sAhi + s * A_TILE, mh, kb * BK, ti.t.row0, &a_full[s]);
-                    tc::tma_load_2d(sAlo + s * A_TILE, ml, kb * BK, ti.t.row0, &a_full[s]);
+                    const uint32_t s = it % SX, ph = (it / SX) & 1;
+                    if (!tc::mbar_wait(&act_empty[s], ph ^ 1, abort_flag, kWaitNs)) { ok = false; break; }
+                    tc::mbar_arrive_expect_tx(&act_full[s], 2u * XBOX * (uint32_t)nbox);
+                    for (int j = 0; j < nbox; ++j) {
+                        tc::tma_load_2d(sXh + s * X_TILE + j * XBOX, mh, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
+                        tc::tma_load_2d(sXl + s * X_TILE + j * XBOX, ml, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
+                    }
                 }
             }
-            // do not leave the CTA while TMA writes into its shared memory are in flight
-            for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j) {
-                volatile int dummy = 0;
-                tc::mbar_wait(&a_full[j % STAGES], (j / STAGES) & 1, &dummy, kWaitNs);
-            }
+            // no exit while TMA writes into this CTA's shared memory are in flight
+            volatile int never = 0;
+            for (uint32_t j = it > SX ? it - SX : 0; j < it; ++j)
+                tc::mbar_wait(&act_full[j % SX], (j / SX) & 1, &never, kWaitNs);
         }
     } else if (warp == 1) {
-        // ---- MMA issuer ----
+        // ---- MMA issuer: per K step, both 128-row halves x (activation high, low) ----
         if (lane == 0) {
             uint32_t it = 0, acc_it = 0;
             bool ok = true;
             for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
                 const TileInfo ti = tile_info(A, i);
-                if (!tc::mbar_wait(acc_empty, (acc_it & 1) ^ 1, abort_flag, kWaitNs)) break;
+                const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+                if (!tc::mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag, kWaitNs)) break;
                 tc::tc_fence_after();
+                const uint32_t d = tmem + ab * 256;
+                const uint32_t idesc = tc::idesc_f16(128, (uint32_t)((ti.t.rows + 15) & ~15));
                 for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-                    const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-                    if (!tc::mbar_wait(&a_full[s], ph, abort_flag, kWaitNs) ||
-                        !tc::mbar_wait(&b_full[s], ph, abort_flag, kWaitNs)) { ok = false; break; }
+                    const uint32_t sx = it % SX, phx = (it / SX) & 1, sw = it % SW, phw = (it / SW) & 1;
+                    if (!tc::mbar_wait(&w_full[sw], phw, abort_flag, kWaitNs) ||
+                        !tc::mbar_wait(&act_full[sx], phx, abort_flag, kWaitNs)) { ok = false; break; }
                     tc::tc_fence_after();
-                    const uint64_t dhi = tc::sdesc_sw128(tc::smem_u32(sAhi + s * A_TILE));
-                    const uint64_t dlo = tc::sdesc_sw128(tc::smem_u32(sAlo + s * A_TILE));
-                    const uint64_t db = tc::sdesc_sw128(tc::smem_u32(sB + s * B_TILE));
-                    for (int sub = 0; sub < ti.nsub; ++sub) {
+                    const uint64_t da0 = tc::sdesc_sw128(tc::smem_u32(sW + sw * W_TILE));
+                    const uint64_t da1 = tc::sdesc_sw128(tc::smem_u32(sW + sw * W_TILE + W_TILE / 2));
+                    const uint64_t dh = tc::sdesc_sw128(tc::smem_u32(sXh + sx * X_TILE));
+                    const uint64_t dl = tc::sdesc_sw128(tc::smem_u32(sXl + sx * X_TILE));
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k) {
-                            const uint64_t bk = db + (uint64_t)(sub * (128 * 128 / 16)) + (uint64_t)(2 * k);
-                            tc::mma_f16(tmem + sub * 128, dhi + 2 * k, bk, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                            tc::mma_f16(tmem + sub * 128, dlo + 2 * k, bk, idesc, 1u);
-                        }
+                    for (int k = 0; k < BK / 16; ++k) {
+                        const uint32_t first = (kb > 0 || k > 0) ? 1u : 0u;
+                        tc::mma_f16(d, da0 + 2 * k, dh + 2 * k, idesc, first);
+                        tc::mma_f16(d + 128, da1 + 2 * k, dh + 2 * k, idesc, first);
+                        tc::mma_f16(d, da0 + 2 * k, dl + 2 * k, idesc, 1u);
+                        tc::mma_f16(d + 128, da1 + 2 * k, dl + 2 * k, idesc, 1u);
                     }
-                    tc::mma_commit(&empty[s]);
+                    tc::mma_commit(&w_empty[sw]);
+                    tc::mma_commit(&act_empty[sx]);
                 }
                 if (!ok) break;
-                tc::mma_commit(acc_full);
+                tc::mma_commit(&acc_full[ab]);
                 ++acc_it;
             }
-            // let issued MMAs finish before TMEM is released
-            if (it > 0) {
-                volatile int dummy = 0;
-                const uint32_t j = it - 1;
-                tc::mbar_wait(&empty[j % STAGES], (j / STAGES) & 1, &dummy, kWaitNs);
+            if (it > 0) {   // issued MMAs finish before TMEM is released
+                volatile int never = 0;
+                tc::mbar_wait(&w_empty[(it - 1) % SW], ((it - 1) / SW) & 1, &never, kWaitNs);
             }
         }
-    } else {
-        // ---- warps 2..7: B producers (dequant); warps 4..7 also the epilogue ----
-        const int dq = tid - 64;
-        const bool epi = warp >= 4;
-        const int q = warp & 3;                   // TMEM lane quadrant of this warp
-        uint32_t it = 0, acc_it = 0;
+    } else if (warp >= 8) {
+        // ---- dequant: one weight row per thread; its packed bytes come through a private
+        //      cp.async pipeline DR blocks deep (no barrier: each thread reads only what it copied) ----
+        const int r = tid - DQ0;                    // tile row 0..255
+        const int hr = r >> 7, rr = r & 127;        // 128-row half, row within the half
+        const uint32_t wrow = (uint32_t)hr * (W_TILE / 2) + (uint32_t)(rr >> 3) * 1024u + (uint32_t)(rr & 7) * 128u;
+        const uint32_t swz = (uint32_t)(rr & 7);
+        const uint32_t raw_row = tc::smem_u32(sRaw) + (uint32_t)r * 32u;
+        const uint32_t rsw = (uint32_t)((r >> 2) & 1);   // 16-byte half swap: conflict-free 16-byte reads
+        uint32_t it = 0;
+        bool ok = true;
+        for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+            const TileInfo ti = tile_info(A, i);
+            const uint8_t* wb = ti.routed ? A.experts + (uint64_t)ti.t.expert * A.expert_stride : A.resident;
+            const int G = ti.nkb;
+            const int nrows = ti.routed ? A.rows_r : A.rows_s;
+            int row;
+            uint64_t wo, so, bo;
+            if (MODE == 0) {
+                row = ti.t.fb * 128 + rr;
+                wo = ti.routed ? (hr ? A.r_wb : A.r_wa) : (hr ? A.s_wb : A.s_wa);
+                so = ti.routed ? (hr ? A.r_sb : A.r_sa) : (hr ? A.s_sb : A.s_sa);
+                bo = ti.routed ? (hr ? A.r_bb : A.r_ba) : (hr ? A.s_bb : A.s_ba);
+            } else {
+                row = ti.t.fb * 256 + r;
+                wo = ti.routed ? A.r_wa : A.s_wa;
+                so = ti.routed ? A.r_sa : A.s_sa;
+                bo = ti.routed ? A.r_ba : A.s_ba;
+            }
+            const bool valid = row < nrows;   // rows past the matrix (last gate/up block) dequantise to 0
+            const uint8_t* wsrc = wb + wo + (uint64_t)(valid ? row : 0) * (uint64_t)(G * 32);
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(wb + so) + (size_t)(valid ? row : 0) * G;
+            const uint16_t* bp = reinterpret_cast<const uint16_t*>(wb + bo) + (size_t)(valid ? row : 0) * G;
+            auto issue = [&](int kb) {
+                if (valid && kb < G) {
+                    const uint32_t dst = raw_row + (uint32_t)(kb % DR) * RAW_TILE;
+                    cp_async16(dst + (rsw << 4), wsrc + kb * 32);
+                    cp_async16(dst + ((rsw ^ 1u) << 4), wsrc + kb * 32 + 16);
+                }
+                cp_async_commit();
+            };
+#pragma unroll
+            for (int k = 0; k < DR - 1; ++k) issue(k);
+            auto step = [&](int kb, uint16_t sbits, uint16_t bbits) -> bool {
+                issue(kb + DR - 1);
+                cp_async_wait<DR - 1>();
+                const uint8_t* src = sRaw + (uint32_t)(kb % DR) * RAW_TILE + r * 32;
+                const uint4 q0 = *reinterpret_cast<const uint4*>(src + (rsw << 4));
+                const uint4 q1 = *reinterpret_cast<const uint4*>(src + ((rsw ^ 1u) << 4));
+                const uint32_t sc = valid ? bf16_to_h2(sbits) : 0u, bi = valid ? bf16_to_h2(bbits) : 0u;
+                uint4 o[8];
+                o[0] = dq8(q0.x, sc, bi); o[1] = dq8(q0.y, sc, bi); o[2] = dq8(q0.z, sc, bi); o[3] = dq8(q0.w, sc, bi);
+                o[4] = dq8(q1.x, sc, bi); o[5] = dq8(q1.y, sc, bi); o[6] = dq8(q1.z, sc, bi); o[7] = dq8(q1.w, sc, bi);
+                const uint32_t sw = it % SW, phw = (it / SW) & 1;
+                if (!tc::mbar_wait(&w_empty[sw], phw ^ 1, abort_flag, kWaitNs)) return false;
+                uint8_t* wt = sW + sw * W_TILE + wrow;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wt + (((uint32_t)c ^ swz) << 4)) = o[c];
+                tc::fence_proxy_async_smem();
+                tc::mbar_arrive(&w_full[sw]);
+                ++it;
+                return true;
+            };
+            // scale/bias of blocks kb, kb+1 in registers; those of kb+2, kb+3 load during two blocks' work
+            uint16_t s0 = sp[0], b0 = bp[0], s1 = G > 1 ? sp[1] : 0, b1 = G > 1 ? bp[1] : 0;
+            for (int kb = 0; kb < G; kb += 2) {
+                const uint16_t s2 = kb + 2 < G ? sp[kb + 2] : 0, b2 = kb + 2 < G ? bp[kb + 2] : 0;
+                const uint16_t s3 = kb + 3 < G ? sp[kb + 3] : 0, b3 = kb + 3 < G ? bp[kb + 3] : 0;
+                if (!step(kb, s0, b0) || (kb + 1 < G && !step(kb + 1, s1, b1))) { ok = false; break; }
+                s0 = s2; b0 = b2; s1 = s3; b1 = b3;
+            }
+            cp_async_wait<0>();
+        }
+    } else if (warp >= 4) {
+        // ---- epilogue: warp (4 + q) reads TMEM lanes 32q..32q+31 of both accumulators ----
+        const int q = warp & 3;
+        uint32_t acc_it = 0;
         for (int i = blockIdx.x; i < ntiles; i += gridDim.x) {
             const TileInfo ti = tile_info(A, i);
-            const uint8_t* wbase = ti.routed ? A.experts + (uint64_t)ti.t.expert * A.expert_stride : A.resident;
-            const GtmQuant& qa = ti.routed ? A.ex_a : A.sh_a;
-            const GtmQuant& qb = ti.routed ? A.ex_b : A.sh_b;
-            const int K = ti.K, G = K / kGroup;
-            bool ok = true;
-            for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-                const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-                if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitNs)) { ok = false; break; }
-                uint8_t* dst = sB + s * B_TILE;
-                for (int r = dq; r < ti.nsub * 128; r += DQ_THREADS) {
-                    const int g = ti.t.ftile * BNF + r;
-                    const GtmQuant* qm;
-                    int row;
-                    if (MODE == 0) { qm = (g & 1) ? &qb : &qa; row = g >> 1; }
-                    else { qm = &qa; row = g; }
-                    const uint8_t* wrow = wbase + qm->weight + (uint64_t)row * (K / 2) + kb * 32;
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(wrow);
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(wrow + 16);
-                    const uint32_t s2 = bf16_to_h2(*reinterpret_cast<const uint16_t*>(wbase + qm->scales + ((uint64_t)row * G + kb) * 2));
-                    const uint32_t b2 = bf16_to_h2(*reinterpret_cast<const uint16_t*>(wbase + qm->biases + ((uint64_t)row * G + kb) * 2));
-                    const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                    uint8_t* rowp = dst + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = dequant8(words[c], s2, b2);
-                }
-                tc::fence_proxy_async_smem();
-                tc::mbar_arrive(&b_full[s]);
-            }
-            if (!ok) break;
-            if (!epi) continue;
-            // ---- epilogue: thread (quadrant q, lane) owns token row row0 + 32q + lane ----
-            if (!tc::mbar_wait(acc_full, acc_it & 1, abort_flag, kWaitNs)) break;
-            ++acc_it;
+            const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+            // warp-uniform outcome: tcgen05.ld is warp-collective
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[ab], aph, abort_flag, kWaitNs))) break;
             tc::tc_fence_after();
-            const int r = 32 * q + lane;
-            const bool valid = r < ti.t.rows;
-            const int row = ti.t.row0 + r;
-            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
-            const float wgt = (MODE == 1 && ti.routed && valid) ? A.perm_w[row] : 1.0f;
-            for (int sub = 0; sub < ti.nsub; ++sub) {
-#pragma unroll 1
-                for (int c16 = 0; c16 < 8; ++c16) {
-                    uint32_t v[16];
-                    tc::tmem_ld16_sync(taddr + sub * 128 + c16 * 16, v);
-                    const int f0 = ti.t.ftile * BNF + sub * 128 + c16 * 16;
-                    if (!valid || f0 >= ti.nf) continue;
-                    if (MODE == 0) {
-                        // columns alternate gate / up of intermediate rows f0/2 .. f0/2 + 7
-                        __half hi[8], lo[8];
+            const uint32_t taddr = tmem + ab * 256 + ((uint32_t)(32 * q) << 16);
+            const int rows = ti.t.rows, row0 = ti.t.row0;
+            if (MODE == 1) {
+                // accumulator a holds output rows fb*256 + 128a + (32q + lane)
+                const int f0 = ti.t.fb * 256 + 32 * q + lane;
+                float* out = ti.routed ? A.out_r : A.out_s;
+                for (int c0 = 0; c0 < rows; c0 += 16) {
+                    const int tl = c0 + (lane & 15);
+                    const float wl = ti.routed && tl < rows ? A.perm_w[row0 + tl] : 1.0f;
+                    uint32_t v0[16], v1[16];
+                    tc::tmem_ld16_sync(taddr + c0, v0);
+                    tc::tmem_ld16_sync(taddr + 128 + c0, v1);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float a = gelu_tanh_f(__uint_as_float(v[2 * j])) * __uint_as_float(v[2 * j + 1]);
-                            hi[j] = __float2half_rn(a);
-                            lo[j] = __float2half_rn(a - __half2float(hi[j]));
+                    for (int j = 0; j < 16; ++j) {
+                        const int t = c0 + j;
+                        const float wgt = __shfl_sync(0xffffffffu, wl, j);
+                        if (t < rows) {
+                            float* o = out + (size_t)(row0 + t) * D + f0;
+                            o[0] = __uint_as_float(v0[j]) * wgt;
+                            o[128] = __uint_as_float(v1[j]) * wgt;
                         }
-                        const int kout = ti.nf / 2;
-                        __half* dh = (ti.routed ? A.act_r_hi : A.act_s_hi) + (size_t)row * kout + f0 / 2;
-                        __half* dl = (ti.routed ? A.act_r_lo : A.act_s_lo) + (size_t)row * kout + f0 / 2;
-                        uint4 ph4, pl4;
-                        ph4.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
-                        ph4.y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
-                        ph4.z = (uint32_t)__half_as_ushort(hi[4]) | ((uint32_t)__half_as_ushort(hi[5]) << 16);
-                        ph4.w = (uint32_t)__half_as_ushort(hi[6]) | ((uint32_t)__half_as_ushort(hi[7]) << 16);
-                        pl4.x = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
-                        pl4.y = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
-                        pl4.z = (uint32_t)__half_as_ushort(lo[4]) | ((uint32_t)__half_as_ushort(lo[5]) << 16);
-                        pl4.w = (uint32_t)__half_as_ushort(lo[6]) | ((uint32_t)__half_as_ushort(lo[7]) << 16);
-                        *reinterpret_cast<uint4*>(dh) = ph4;
-                        *reinterpret_cast<uint4*>(dl) = pl4;
-                    } else {
-                        float* dst = (ti.routed ? A.out_r : A.out_s) + (size_t)row * D + f0;
+                    }
+                }
+            } else {
+                // accumulator 0: gate rows, accumulator 1: the same up rows -> GeGLU in-thread
+                const int kout = ti.routed ? FE : FS;
+                const int f = ti.t.fb * 128 + 32 * q + lane;
+                const bool fvalid = f < kout;
+                const int fcol = kperm(fvalid ? f : 0);
+                __half* oh = (ti.routed ? A.act_r_hi : A.act_s_hi) + fcol;
+                __half* ol = (ti.routed ? A.act_r_lo : A.act_s_lo) + fcol;
+                for (int c0 = 0; c0 < rows; c0 += 16) {
+                    uint32_t g[16], u[16];
+                    tc::tmem_ld16_sync(taddr + c0, g);
+                    tc::tmem_ld16_sync(taddr + 128 + c0, u);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            reinterpret_cast<float4*>(dst)[j] =
-                                make_float4(__uint_as_float(v[4 * j]) * wgt, __uint_as_float(v[4 * j + 1]) * wgt,
-                                            __uint_as_float(v[4 * j + 2]) * wgt, __uint_as_float(v[4 * j + 3]) * wgt);
+                    for (int j = 0; j < 16; ++j) {
+                        const int t = c0 + j;
+                        if (t < rows && fvalid) {
+                            const float a = gelu_tanh_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                            const __half hi = __float2half_rn(a);
+                            const size_t o = (size_t)(row0 + t) * kout;
+                            oh[o] = hi;
+                            ol[o] = __float2half_rn(a - __half2float(hi));
+                        }
                     }
                 }
             }
             tc::tc_fence_before();
-            tc::mbar_arrive(acc_empty);
+            tc::mbar_arrive(&acc_empty[ab]);
+            ++acc_it;
         }
     }
     tc::tc_fence_before();
@@ -584,6 +660,8 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
     return s;
 }
 
+// h1 = rms(shared)*w_pf1 (cpu_reference.cpp:492-493); h2 = sum_k w_k out_k in router order
+// (:508-509); hidden = (x + rms(rms(h2)*w_pf2 + h1)*w_pf) * layer_scalar (:512-520).
 __global__ void __launch_bounds__(512) tok_combine(const __grid_constant__ CombineArgs A) {
     __shared__ __align__(16) float sh[D];
     __shared__ __align__(16) float h2[D];
@@ -630,8 +708,8 @@ __global__ void __launch_bounds__(512) tok_combine(const __grid_constant__ Combi
 // host side
 // ================================================================================================
 struct WsLayout {
-    size_t dense_hi, dense_lo, routed, idx, w, counts, offsets, perm_token, perm_w, pos, tiles0, tiles1, n_tiles,
-        xhi, xlo, act_r_hi, act_r_lo, act_s_hi, act_s_lo, out_r, out_s, total;
+    size_t dense_hi, dense_lo, routed, idx, w, perm_token, perm_w, pos, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
+        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, total;
 };
 
 static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
@@ -639,7 +717,7 @@ static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 static WsLayout ws_layout(uint32_t T) {
     WsLayout W;
     const size_t R = (size_t)T * TOPK;
-    const size_t mt_max = R / BM + NE + 1, mts = (T + BM - 1) / BM;
+    const size_t ntr = R / NT + NE, nts = (T + NT - 1) / NT;   // bounds on routed / shared token tiles
     size_t o = 256;   // [0, 256): error word
     auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + bytes); return at; };
     W.dense_hi = take((size_t)T * D * 2);
@@ -647,13 +725,11 @@ static WsLayout ws_layout(uint32_t T) {
     W.routed = take((size_t)T * D * 4);
     W.idx = take(R * 4);
     W.w = take(R * 4);
-    W.counts = take(NE * 4);
-    W.offsets = take((NE + 1) * 4);
     W.perm_token = take(R * 4);
     W.perm_w = take(R * 4);
     W.pos = take(R * 4);
-    W.tiles0 = take((mt_max * FT0_R + mts * FT0_S) * sizeof(Tile));
-    W.tiles1 = take((mt_max * FT1 + mts * FT1) * sizeof(Tile));
+    W.tiles0 = take((ntr * FB0_R + nts * FB0_S) * sizeof(Tile));
+    W.tiles1 = take((ntr * FB1 + nts * FB1) * sizeof(Tile));
     W.n_tiles = take(2 * 4);
     W.xhi = take(R * D * 2);
     W.xlo = take(R * D * 2);
@@ -675,23 +751,30 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static int encode_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k) {
+static EncodeTiledFn encode_fn() {
     static EncodeTiledFn fn = nullptr;
     if (!fn) {
         void* f = nullptr;
         cudaDriverEntryPointQueryResult q;
-        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
-        if (e != cudaSuccess || !f) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled not available");
-        fn = reinterpret_cast<EncodeTiledFn>(f);
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
     }
+    return fn;
+}
+
+// Activation map: fp16 [rows][k], boxes of 64 (k) x 32 rows in the 128-byte swizzle layout.
+static int map_act(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled not available");
     const cuuint64_t dims[2] = {k, rows};
     const cuuint64_t strides[1] = {k * 2};
-    const cuuint32_t box[2] = {tok::BK, tok::BM};
+    const cuuint32_t box[2] = {tok::BK, 32};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed (%d)", (int)r);
     return GTM_OK;
 }
 
@@ -703,7 +786,20 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     if (ws_bytes < W.total) return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes", W.total);
     uint8_t* w = static_cast<uint8_t*>(ws);
     auto P = [&](size_t off) { return static_cast<void*>(w + off); };
-    int* err = reinterpret_cast<int*>(w);
+    const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
+    const uint8_t* exb = static_cast<const uint8_t*>(L.experts_dev);
+    const uint64_t R = (uint64_t)T * TOPK;
+
+    // all tensor maps first, so a failure launches nothing
+    GemmArgs g0, g1;
+    memset(&g0, 0, sizeof(g0));
+    memset(&g1, 0, sizeof(g1));
+    int rc;
+    if ((rc = map_act(&g0.x_rhi, P(W.xhi), R, D)) || (rc = map_act(&g0.x_rlo, P(W.xlo), R, D)) ||
+        (rc = map_act(&g0.x_shi, P(W.dense_hi), T, D)) || (rc = map_act(&g0.x_slo, P(W.dense_lo), T, D)) ||
+        (rc = map_act(&g1.x_rhi, P(W.act_r_hi), R, FE)) || (rc = map_act(&g1.x_rlo, P(W.act_r_lo), R, FE)) ||
+        (rc = map_act(&g1.x_shi, P(W.act_s_hi), T, FS)) || (rc = map_act(&g1.x_slo, P(W.act_s_lo), T, FS)))
+        return rc;
 
     ViewsArgs va;
     memset(&va, 0, sizeof(va));
@@ -718,50 +814,40 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
 
     RouteArgs ra;
     ra.T = (int)T; ra.idx = va.idx; ra.w = va.w;
-    ra.counts = static_cast<int*>(P(W.counts)); ra.offsets = static_cast<int*>(P(W.offsets));
     ra.perm_token = static_cast<int*>(P(W.perm_token)); ra.perm_w = static_cast<float*>(P(W.perm_w));
     ra.pos = static_cast<int*>(P(W.pos));
     ra.tiles0 = static_cast<Tile*>(P(W.tiles0)); ra.tiles1 = static_cast<Tile*>(P(W.tiles1));
     ra.n_tiles = static_cast<int*>(P(W.n_tiles));
     tok_route<<<1, 1024, 0, st>>>(ra);
 
-    tok_gather<<<T * TOPK, 256, 0, st>>>(va.routed, ra.perm_token, static_cast<__half*>(P(W.xhi)),
-                                         static_cast<__half*>(P(W.xlo)));
+    tok_gather<<<(unsigned)R, 128, 0, st>>>(va.routed, ra.perm_token, static_cast<__half*>(P(W.xhi)),
+                                            static_cast<__half*>(P(W.xlo)));
 
-    const size_t smem = 1024 + 2 * STAGES * A_TILE + STAGES * B_TILE + 256;
-    cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const uint64_t R = (uint64_t)T * TOPK;
-    GemmArgs g0;
-    memset(&g0, 0, sizeof(g0));
-    int rc;
-    if ((rc = encode_map(&g0.map_r_hi, P(W.xhi), R, D)) || (rc = encode_map(&g0.map_r_lo, P(W.xlo), R, D)) ||
-        (rc = encode_map(&g0.map_s_hi, P(W.dense_hi), T, D)) || (rc = encode_map(&g0.map_s_lo, P(W.dense_lo), T, D)))
-        return rc;
+    cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+
     g0.tiles = ra.tiles0; g0.n_tiles = ra.n_tiles;
-    g0.experts = static_cast<const uint8_t*>(L.experts_dev); g0.expert_stride = L.expert_stride;
-    g0.ex_a = L.expert_gate; g0.ex_b = L.expert_up;
-    g0.resident = static_cast<const uint8_t*>(L.resident_dev); g0.sh_a = L.shared_gate; g0.sh_b = L.shared_up;
-    g0.k_r = D; g0.k_s = D; g0.nf_r = 2 * FE; g0.nf_s = 2 * FS;
+    g0.experts = exb; g0.expert_stride = L.expert_stride; g0.resident = res;
+    g0.r_wa = L.expert_gate.weight; g0.r_wb = L.expert_up.weight;
+    g0.s_wa = L.shared_gate.weight; g0.s_wb = L.shared_up.weight;
+    g0.r_sa = L.expert_gate.scales; g0.r_ba = L.expert_gate.biases; g0.r_sb = L.expert_up.scales; g0.r_bb = L.expert_up.biases;
+    g0.s_sa = L.shared_gate.scales; g0.s_ba = L.shared_gate.biases; g0.s_sb = L.shared_up.scales; g0.s_bb = L.shared_up.biases;
+    g0.k_r = D; g0.k_s = D; g0.rows_r = FE; g0.rows_s = FS;
     g0.act_r_hi = static_cast<__half*>(P(W.act_r_hi)); g0.act_r_lo = static_cast<__half*>(P(W.act_r_lo));
     g0.act_s_hi = static_cast<__half*>(P(W.act_s_hi)); g0.act_s_lo = static_cast<__half*>(P(W.act_s_lo));
-    g0.err = err;
-    grouped_gemm<0><<<num_sms, GEMM_THREADS, smem, st>>>(g0);
+    g0.err = static_cast<int*>(ws);
+    grouped_gemm<0><<<num_sms, THREADS, SMEM_BYTES, st>>>(g0);
 
-    GemmArgs g1;
-    memset(&g1, 0, sizeof(g1));
-    if ((rc = encode_map(&g1.map_r_hi, g0.act_r_hi, R, FE)) || (rc = encode_map(&g1.map_r_lo, g0.act_r_lo, R, FE)) ||
-        (rc = encode_map(&g1.map_s_hi, g0.act_s_hi, T, FS)) || (rc = encode_map(&g1.map_s_lo, g0.act_s_lo, T, FS)))
-        return rc;
     g1.tiles = ra.tiles1; g1.n_tiles = ra.n_tiles + 1;
-    g1.experts = g0.experts; g1.expert_stride = L.expert_stride;
-    g1.ex_a = L.expert_down; g1.ex_b = L.expert_down;
-    g1.resident = g0.resident; g1.sh_a = L.shared_down; g1.sh_b = L.shared_down;
-    g1.k_r = FE; g1.k_s = FS; g1.nf_r = D; g1.nf_s = D;
+    g1.experts = exb; g1.expert_stride = L.expert_stride; g1.resident = res;
+    g1.r_wa = L.expert_down.weight; g1.r_wb = g1.r_wa; g1.s_wa = L.shared_down.weight; g1.s_wb = g1.s_wa;
+    g1.r_sa = L.expert_down.scales; g1.r_ba = L.expert_down.biases; g1.r_sb = g1.r_sa; g1.r_bb = g1.r_ba;
+    g1.s_sa = L.shared_down.scales; g1.s_ba = L.shared_down.biases; g1.s_sb = g1.s_sa; g1.s_bb = g1.s_ba;
+    g1.k_r = FE; g1.k_s = FS; g1.rows_r = D; g1.rows_s = D;
     g1.out_r = static_cast<float*>(P(W.out_r)); g1.out_s = static_cast<float*>(P(W.out_s));
     g1.perm_w = ra.perm_w;
-    g1.err = err;
-    grouped_gemm<1><<<num_sms, GEMM_THREADS, smem, st>>>(g1);
+    g1.err = static_cast<int*>(ws);
+    grouped_gemm<1><<<num_sms, THREADS, SMEM_BYTES, st>>>(g1);
 
     CombineArgs ca;
     ca.T = (int)T; ca.x_f32 = io.x_dev; ca.x_bf16 = io.x_bf16_dev; ca.pos = ra.pos;
@@ -771,7 +857,7 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
 
     if (io.topk_idx_dev) cudaMemcpyAsync(io.topk_idx_dev, va.idx, R * 4, cudaMemcpyDeviceToDevice, st);
     if (io.topk_w_dev) cudaMemcpyAsync(io.topk_w_dev, va.w, R * 4, cudaMemcpyDeviceToDevice, st);
-    cudaError_t e = cudaGetLastError();
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_tokens", e);
     return GTM_OK;
 }
