@@ -214,6 +214,60 @@ GTM_API int gtm_moe_tokens(const GtmDims* dims, const GtmLayer* layer, const Gtm
 /* Reads back and clears the device-side error flag (synchronises `stream`). */
 GTM_API int gtm_moe_tokens_check(void* workspace_dev, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Expert-parallel MoE layer: rank r of `world` owns experts [r*E/world, (r+1)*E/world) and
+ * its own tokens. No reference counterpart (the reference is single-GPU). The caller moves
+ * rows between ranks (NCCL all-to-all over NVLink) between the phases:
+ *   1. gtm_moe_ep_dispatch  own tokens: views, router, top-k; one fp32 routed_x row per
+ *                           (token, slot), grouped by destination rank in (token, slot) order
+ *   2. gtm_moe_ep_shared    own tokens: shared expert (independent of the exchange)
+ *      -- all-to-all of send_counts, then of rows and metadata --
+ *   3. gtm_moe_ep_experts   received rows through this rank's experts; result rows (routing
+ *                           weight applied) in the order the rows were received
+ *      -- all-to-all back, with the split sizes reversed --
+ *   4. gtm_moe_ep_combine   own tokens: h2 = sum over the slots in router order, layer tail
+ * With world = 1 the four phases compute what gtm_moe_tokens computes.
+ * ------------------------------------------------------------------------------------- */
+
+typedef struct GtmEpMeta {
+    uint32_t expert;                 /* global expert id                                    */
+    float weight;                    /* routing weight of the (token, slot)                 */
+} GtmEpMeta;
+
+#define GTM_EP_MAX_WORLD 64
+
+/* One rank's view of the expert-parallel group. world divides the expert count; the rank
+ * owns experts [rank*E/world, (rank+1)*E/world). Every phase of the rank gets the same
+ * config and the same workspace. */
+typedef struct GtmEpConfig {
+    uint32_t world, rank;
+    uint32_t max_tokens;             /* own tokens per call, at most                        */
+    uint32_t max_recv_rows;          /* rows received for this rank's experts, at most      */
+} GtmEpConfig;
+
+/* Workspace for the EP phases of one rank (0 for unsupported dims or sizes). Zero it once
+ * before its first use. */
+GTM_API size_t gtm_moe_ep_workspace_bytes(const GtmDims* dims, const GtmEpConfig* ep);
+/* send_rows_dev: [num_tokens * top_k][hidden] fp32; send_meta_dev: [num_tokens * top_k];
+ * send_counts_dev: [world] device int32, rows for each destination rank. */
+GTM_API int gtm_moe_ep_dispatch(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                const GtmEpConfig* ep, float* send_rows_dev, GtmEpMeta* send_meta_dev,
+                                int32_t* send_counts_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
+GTM_API int gtm_moe_ep_shared(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                              const GtmEpConfig* ep, void* workspace_dev, size_t workspace_bytes, void* stream);
+/* layer->experts_dev points at this rank's first expert (its slice of the expert image); every
+ * received row names one of the rank's experts. ret_rows_dev: [n_recv][hidden] fp32, in the
+ * order of recv_rows_dev. n_recv = 0 is a no-op. */
+GTM_API int gtm_moe_ep_experts(const GtmDims* dims, const GtmLayer* layer, const GtmEpConfig* ep,
+                               const float* recv_rows_dev, const GtmEpMeta* recv_meta_dev, uint32_t n_recv,
+                               float* ret_rows_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
+/* ret_rows_dev: the returned rows in this rank's send order ([num_tokens * top_k][hidden]). */
+GTM_API int gtm_moe_ep_combine(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                               const GtmEpConfig* ep, const float* ret_rows_dev, void* workspace_dev,
+                               size_t workspace_bytes, void* stream);
+/* Reads back and clears the device-side error flag of an EP workspace (synchronises `stream`). */
+GTM_API int gtm_moe_ep_check(void* workspace_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -320,4 +320,113 @@ GTM_API int gtm_moe_tokens_check(void* ws, void* stream) {
     return rc;
 }
 
+// ---- expert parallelism -------------------------------------------------------------------------
+static bool ep_config_ok(const GtmEpConfig* ep) {
+    return ep && ep->world >= 1 && ep->world <= GTM_EP_MAX_WORLD && 128 % ep->world == 0 && ep->rank < ep->world &&
+           ep->max_tokens >= 1 && ep->max_tokens <= kMaxTokens && ep->max_recv_rows >= 1 &&
+           ep->max_recv_rows <= kMaxTokens * 8u;
+}
+
+static int ep_common(const char* fn, const GtmDims* dims, const GtmLayer* layer, const GtmEpConfig* ep, void* ws,
+                     size_t ws_bytes) {
+    if (!dims || !layer || !ep) return set_error(GTM_ERR_INVALID, "%s: null argument", fn);
+    if (!dims_supported(dims))
+        return set_error(GTM_ERR_UNSUPPORTED, "%s: built for hidden 2816, moe 704, ffn 2112, 128 experts, top-8", fn);
+    if (!ep_config_ok(ep))
+        return set_error(GTM_ERR_INVALID, "%s: bad EP config (world %u must divide 128, rank %u < world, sizes %u/%u)",
+                         fn, ep->world, ep->rank, ep->max_tokens, ep->max_recv_rows);
+    const size_t need = ep_workspace_bytes(ep->max_tokens, ep->max_recv_rows);
+    if (!ws || ws_bytes < need || !aligned(ws, 256))
+        return set_error(GTM_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-byte aligned", fn, need);
+    return check_layer(fn, *layer);
+}
+
+static int ep_io(const char* fn, const GtmTokensIO* io, const GtmEpConfig* ep, bool need_out) {
+    if (!io) return set_error(GTM_ERR_INVALID, "%s: null io", fn);
+    if (io->num_tokens == 0 || io->num_tokens > ep->max_tokens)
+        return set_error(GTM_ERR_INVALID, "%s: num_tokens=%u (1..max_tokens %u)", fn, io->num_tokens, ep->max_tokens);
+    if ((io->x_dev == nullptr) == (io->x_bf16_dev == nullptr))
+        return set_error(GTM_ERR_INVALID, "%s: give exactly one of x_dev and x_bf16_dev", fn);
+    if (need_out && !io->hidden_out_dev) return set_error(GTM_ERR_INVALID, "%s: hidden_out_dev is NULL", fn);
+    return GTM_OK;
+}
+
+static int sm_count(const char* fn, int* sms) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return set_cuda_error(fn, e);
+    return GTM_OK;
+}
+
+GTM_API size_t gtm_moe_ep_workspace_bytes(const GtmDims* dims, const GtmEpConfig* ep) {
+    if (!dims || !dims_supported(dims) || !ep_config_ok(ep)) return 0;
+    return ep_workspace_bytes(ep->max_tokens, ep->max_recv_rows);
+}
+
+GTM_API int gtm_moe_ep_dispatch(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                const GtmEpConfig* ep, float* send_rows, GtmEpMeta* send_meta, int32_t* send_counts,
+                                void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_dispatch";
+    int rc = ep_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (!rc) rc = ep_io(fn, io, ep, false);
+    if (rc) return rc;
+    if (!send_rows || !send_meta || !send_counts) return set_error(GTM_ERR_INVALID, "%s: null send buffer", fn);
+    if (!aligned(send_rows, 16) || !aligned(send_meta, 8) || !aligned(send_counts, 4))
+        return set_error(GTM_ERR_MISALIGNED, "%s: send_rows must be 16-byte aligned", fn);
+    rc = launch_ep_dispatch(*dims, *layer, *io, *ep, send_rows, send_meta, send_counts, ws, (cudaStream_t)stream);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_ep_shared(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                              const GtmEpConfig* ep, void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_shared";
+    int rc = ep_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (!rc) rc = ep_io(fn, io, ep, false);
+    int sms = 0;
+    if (!rc) rc = sm_count(fn, &sms);
+    if (rc) return rc;
+    rc = launch_ep_shared(*layer, *io, *ep, ws, (cudaStream_t)stream, sms);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_ep_experts(const GtmDims* dims, const GtmLayer* layer, const GtmEpConfig* ep,
+                               const float* recv_rows, const GtmEpMeta* recv_meta, uint32_t n_recv, float* ret_rows,
+                               void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_experts";
+    int rc = ep_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (rc) return rc;
+    if (n_recv > ep->max_recv_rows)
+        return set_error(GTM_ERR_WORKSPACE, "%s: %u rows > max_recv_rows %u", fn, n_recv, ep->max_recv_rows);
+    if (n_recv > 0 && (!recv_rows || !recv_meta || !ret_rows)) return set_error(GTM_ERR_INVALID, "%s: null row buffer", fn);
+    if (!aligned(recv_rows, 16) || !aligned(recv_meta, 8) || !aligned(ret_rows, 16))
+        return set_error(GTM_ERR_MISALIGNED, "%s: row buffers must be 16-byte aligned", fn);
+    int sms = 0;
+    if ((rc = sm_count(fn, &sms))) return rc;
+    rc = launch_ep_experts(*layer, *ep, recv_rows, recv_meta, n_recv, ret_rows, ws, (cudaStream_t)stream, sms);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_ep_combine(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                               const GtmEpConfig* ep, const float* ret_rows, void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_combine";
+    int rc = ep_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (!rc) rc = ep_io(fn, io, ep, true);
+    if (rc) return rc;
+    if (!ret_rows) return set_error(GTM_ERR_INVALID, "%s: null ret_rows", fn);
+    rc = launch_ep_combine(*dims, *layer, *io, *ep, ret_rows, ws, (cudaStream_t)stream);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_ep_check(void* ws, void* stream) {
+    if (!ws) return set_error(GTM_ERR_INVALID, "gtm_moe_ep_check: null workspace");
+    const int rc = tokens_check(ws, (cudaStream_t)stream);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
 }  // extern "C"

@@ -210,12 +210,16 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
 // 2. routing tables and tile lists (one CTA)
 // ================================================================================================
 struct RouteArgs {
-    int T;
-    const uint32_t* idx;     // [T][8]
-    const float* w;          // [T][8]
-    int* perm_token;         // [8T] token of each expert-ordered row
-    float* perm_w;           // [8T] routing weight of each row
-    int* pos;                // [T][8] row of each (token, slot)
+    int n;                   // routed entries (0: shared tiles only)
+    int src_div;             // activation source row of entry i = i / src_div
+    const uint32_t* idx;     // expert id of entry i at idx[i * stride]
+    const float* w;          // routing weight of entry i at w[i * stride]
+    int stride;
+    int e0, ne;              // experts of this launch: [e0, e0 + ne); tiles carry e - e0
+    int t_shared;            // tokens of the shared-expert tiles (0: none)
+    int* perm_src;           // [n] source row of each expert-ordered row
+    float* perm_w;           // [n] routing weight of each row
+    int* pos;                // [n] expert-ordered row of each entry
     Tile* tiles0;            // gate/up tiles
     Tile* tiles1;            // down tiles
     int* n_tiles;            // [2]
@@ -225,29 +229,33 @@ __device__ __forceinline__ int ntok_tiles(int c) { return (c + NT - 1) / NT; }
 
 __global__ void __launch_bounds__(1024) tok_route(const __grid_constant__ RouteArgs A) {
     __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
-    const int tid = threadIdx.x, n = A.T * TOPK;
+    const int tid = threadIdx.x, n = A.n;
     for (int e = tid; e < NE; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) A.pos[i] = atomicAdd(&cnt[(int)A.idx[i]], 1);
+    for (int i = tid; i < n; i += blockDim.x) {
+        const int e = (int)A.idx[(size_t)i * A.stride] - A.e0;
+        A.pos[i] = (e >= 0 && e < A.ne) ? atomicAdd(&cnt[e], 1) : -1;
+    }
     __syncthreads();
     if (tid == 0) {
         int o = 0, a = 0, b = 0;
-        for (int e = 0; e < NE; ++e) {
+        for (int e = 0; e < A.ne; ++e) {
             off[e] = o; t0[e] = a; t1[e] = b;
             const int nt = ntok_tiles(cnt[e]);
             o += cnt[e]; a += nt * FB0_R; b += nt * FB1;
         }
-        off[NE] = o; t0[NE] = a; t1[NE] = b;
+        off[A.ne] = o; t0[A.ne] = a; t1[A.ne] = b;
     }
     __syncthreads();
     for (int i = tid; i < n; i += blockDim.x) {
-        const int row = off[(int)A.idx[i]] + A.pos[i];
+        if (A.pos[i] < 0) continue;   // entry of another rank's expert (not produced by the dispatch)
+        const int row = off[(int)A.idx[(size_t)i * A.stride] - A.e0] + A.pos[i];
         A.pos[i] = row;
-        A.perm_token[row] = i / TOPK;
-        A.perm_w[row] = A.w[i];
+        A.perm_src[row] = i / A.src_div;
+        A.perm_w[row] = A.w[(size_t)i * A.stride];
     }
     // tiles of one (expert, row block) are adjacent over the token ranges, for L2 reuse of the weights
-    for (int e = tid; e < NE; e += blockDim.x) {
+    for (int e = tid; e < A.ne; e += blockDim.x) {
         const int c = cnt[e], nt = ntok_tiles(c);
         for (int m = 0; m < nt; ++m) {
             const int r0 = c * m / nt, r1 = c * (m + 1) / nt;
@@ -255,27 +263,92 @@ __global__ void __launch_bounds__(1024) tok_route(const __grid_constant__ RouteA
             for (int f = 0; f < FB1; ++f) A.tiles1[t1[e] + f * nt + m] = Tile{e, off[e] + r0, r1 - r0, f};
         }
     }
-    const int nts = ntok_tiles(A.T);
+    const int T = A.t_shared, nts = ntok_tiles(T), b0 = t0[A.ne], b1 = t1[A.ne];
     for (int i = tid; i < nts * FB0_S; i += blockDim.x) {
-        const int f = i / nts, m = i - f * nts, r0 = A.T * m / nts, r1 = A.T * (m + 1) / nts;
-        A.tiles0[t0[NE] + i] = Tile{-1, r0, r1 - r0, f};
+        const int f = i / nts, m = i - f * nts, r0 = T * m / nts, r1 = T * (m + 1) / nts;
+        A.tiles0[b0 + i] = Tile{-1, r0, r1 - r0, f};
     }
     for (int i = tid; i < nts * FB1; i += blockDim.x) {
-        const int f = i / nts, m = i - f * nts, r0 = A.T * m / nts, r1 = A.T * (m + 1) / nts;
-        A.tiles1[t1[NE] + i] = Tile{-1, r0, r1 - r0, f};
+        const int f = i / nts, m = i - f * nts, r0 = T * m / nts, r1 = T * (m + 1) / nts;
+        A.tiles1[b1 + i] = Tile{-1, r0, r1 - r0, f};
     }
     if (tid == 0) {
-        A.n_tiles[0] = t0[NE] + nts * FB0_S;
-        A.n_tiles[1] = t1[NE] + nts * FB1;
+        A.n_tiles[0] = b0 + nts * FB0_S;
+        A.n_tiles[1] = b1 + nts * FB1;
     }
+}
+
+// ================================================================================================
+// 2b. expert-parallel dispatch: (token, slot) entries grouped by destination rank, in (token,
+//     slot) order inside each group, so the layout is the same on every run
+// ================================================================================================
+struct DispatchArgs {
+    int n;                   // entries (tokens x top_k)
+    int world, epr;          // ranks, experts per rank
+    const uint32_t* idx;     // [n]
+    const float* w;          // [n]
+    int* send_counts;        // [world]
+    int* send_pos;           // [n] send row of each entry
+    int* send_src;           // [n] token of each send row
+    GtmEpMeta* send_meta;    // [n] (expert, weight) of each send row
+};
+
+constexpr int kMaxWorld = 64;
+
+__global__ void __launch_bounds__(1024) tok_dispatch(const __grid_constant__ DispatchArgs A) {
+    __shared__ int run[kMaxWorld], wtot[32][kMaxWorld], off[kMaxWorld];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int d = tid; d < A.world; d += blockDim.x) run[d] = 0;
+    __syncthreads();
+    for (int base = 0; base < A.n; base += blockDim.x) {
+        const int i = base + tid;
+        const int d = i < A.n ? (int)A.idx[i] / A.epr : -1;
+        int mine = 0;
+        for (int q = 0; q < A.world; ++q) {
+            const unsigned m = __ballot_sync(0xffffffffu, d == q);
+            if (d == q) mine = __popc(m & ((1u << lane) - 1u));
+            if (lane == 0) wtot[warp][q] = __popc(m);
+        }
+        __syncthreads();
+        if (d >= 0) {
+            int before = run[d];
+            for (int w2 = 0; w2 < warp; ++w2) before += wtot[w2][d];
+            A.send_pos[i] = before + mine;   // position inside destination d's group
+        }
+        __syncthreads();
+        for (int q = tid; q < A.world; q += blockDim.x) {
+            int s = 0;
+            for (int w2 = 0; w2 < 32; ++w2) s += wtot[w2][q];
+            run[q] += s;
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {
+        int o = 0;
+        for (int q = 0; q < A.world; ++q) { off[q] = o; o += run[q]; A.send_counts[q] = run[q]; }
+    }
+    __syncthreads();
+    for (int i = tid; i < A.n; i += blockDim.x) {
+        const int row = off[(int)A.idx[i] / A.epr] + A.send_pos[i];
+        A.send_pos[i] = row;
+        A.send_src[row] = i / TOPK;
+        A.send_meta[row] = GtmEpMeta{A.idx[i], A.w[i]};
+    }
+}
+
+__global__ void __launch_bounds__(256) tok_copy_rows(const float* src, const int* src_row, float* dst) {
+    const int row = blockIdx.x;
+    const float4* s4 = reinterpret_cast<const float4*>(src + (size_t)src_row[row] * D);
+    float4* d4 = reinterpret_cast<float4*>(dst + (size_t)row * D);
+    for (int c = threadIdx.x; c < D / 4; c += blockDim.x) d4[c] = s4[c];
 }
 
 // ================================================================================================
 // 3. gather routed_x rows in expert order as fp16 high / low parts (K-permuted)
 // ================================================================================================
-__global__ void __launch_bounds__(128) tok_gather(const float* routed, const int* perm_token, __half* xhi, __half* xlo) {
+__global__ void __launch_bounds__(128) tok_gather(const float* routed, const int* perm_src, __half* xhi, __half* xlo) {
     const int row = blockIdx.x;
-    const float4* src = reinterpret_cast<const float4*>(routed + (size_t)perm_token[row] * D);
+    const float4* src = reinterpret_cast<const float4*>(routed + (size_t)perm_src[row] * D);
     for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
         const float4 a = src[2 * c], b = src[2 * c + 1];
         const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -314,6 +387,7 @@ struct GemmArgs {
     __half* act_s_hi; __half* act_s_lo;
     float* out_r; float* out_s;           // mode 1 outputs [rows][D]
     const float* perm_w;                  // mode 1: routing weight per routed row
+    const int* out_index;                 // mode 1: output row of each routed row (null: same row)
     int* err;
 };
 
@@ -584,7 +658,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                         const int t = c0 + j;
                         const float wgt = __shfl_sync(0xffffffffu, wl, j);
                         if (t < rows) {
-                            float* o = out + (size_t)(row0 + t) * D + f0;
+                            const int orow = ti.routed && A.out_index ? A.out_index[row0 + t] : row0 + t;
+                            float* o = out + (size_t)orow * D + f0;
                             o[0] = __uint_as_float(v0[j]) * wgt;
                             o[128] = __uint_as_float(v1[j]) * wgt;
                         }
@@ -708,24 +783,26 @@ __global__ void __launch_bounds__(512) tok_combine(const __grid_constant__ Combi
 // host side
 // ================================================================================================
 struct WsLayout {
-    size_t dense_hi, dense_lo, routed, idx, w, perm_token, perm_w, pos, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
-        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, total;
+    size_t dense_hi, dense_lo, routed, idx, w, perm_src, perm_w, pos, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
+        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, total;
 };
 
 static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
-static WsLayout ws_layout(uint32_t T) {
+// T: own tokens; R: routed rows through the experts (T * top_k on one GPU, the received rows
+// with expert parallelism); ep: room for the dispatch tables.
+static WsLayout ws_layout(uint32_t T, uint32_t Rrows, bool ep) {
     WsLayout W;
-    const size_t R = (size_t)T * TOPK;
+    const size_t E8 = (size_t)T * TOPK, R = Rrows;
     const size_t ntr = R / NT + NE, nts = (T + NT - 1) / NT;   // bounds on routed / shared token tiles
     size_t o = 256;   // [0, 256): error word
     auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + bytes); return at; };
     W.dense_hi = take((size_t)T * D * 2);
     W.dense_lo = take((size_t)T * D * 2);
     W.routed = take((size_t)T * D * 4);
-    W.idx = take(R * 4);
-    W.w = take(R * 4);
-    W.perm_token = take(R * 4);
+    W.idx = take(E8 * 4);
+    W.w = take(E8 * 4);
+    W.perm_src = take(R * 4);
     W.perm_w = take(R * 4);
     W.pos = take(R * 4);
     W.tiles0 = take((ntr * FB0_R + nts * FB0_S) * sizeof(Tile));
@@ -737,15 +814,18 @@ static WsLayout ws_layout(uint32_t T) {
     W.act_r_lo = take(R * FE * 2);
     W.act_s_hi = take((size_t)T * FS * 2);
     W.act_s_lo = take((size_t)T * FS * 2);
-    W.out_r = take(R * D * 4);
+    W.out_r = ep ? 0 : take(R * D * 4);
     W.out_s = take((size_t)T * D * 4);
+    W.send_pos = ep ? take(E8 * 4) : 0;
+    W.send_src = ep ? take(E8 * 4) : 0;
     W.total = o;
     return W;
 }
 
 }  // namespace tok
 
-size_t tokens_workspace_bytes(uint32_t max_tokens) { return tok::ws_layout(max_tokens).total; }
+size_t tokens_workspace_bytes(uint32_t max_tokens) { return tok::ws_layout(max_tokens, max_tokens * tok::TOPK, false).total; }
+size_t ep_workspace_bytes(uint32_t max_tokens, uint32_t max_recv) { return tok::ws_layout(max_tokens, max_recv, true).total; }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -778,50 +858,68 @@ static int map_act(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k) {
     return GTM_OK;
 }
 
-int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, void* ws, size_t ws_bytes,
-                  cudaStream_t st, int num_sms) {
-    using namespace tok;
-    const uint32_t T = io.num_tokens;
-    const WsLayout W = ws_layout(T);
-    if (ws_bytes < W.total) return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes", W.total);
-    uint8_t* w = static_cast<uint8_t*>(ws);
-    auto P = [&](size_t off) { return static_cast<void*>(w + off); };
+namespace {
+
+using namespace tok;
+
+struct Ws {
+    WsLayout W;
+    uint8_t* base;
+    void* at(size_t off) const { return base + off; }
+    template <class T> T* p(size_t off) const { return reinterpret_cast<T*>(base + off); }
+};
+
+void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const Ws& w, cudaStream_t st) {
+    ViewsArgs va;
+    memset(&va, 0, sizeof(va));
+    va.T = (int)io.num_tokens; va.x_f32 = io.x_dev; va.x_bf16 = io.x_bf16_dev; va.L = L; va.eps = dims.eps;
+    va.inv_sqrt_d = 1.0f / sqrtf((float)D);
+    va.logit_bias = io.logit_bias_dev; va.route_logits = io.route_logits_dev;
+    va.dense_hi = w.p<__half>(w.W.dense_hi); va.dense_lo = w.p<__half>(w.W.dense_lo);
+    va.routed = w.p<float>(w.W.routed);
+    va.idx = w.p<uint32_t>(w.W.idx); va.w = w.p<float>(w.W.w);
+    va.logits_out = io.logits_dev;
+    tok_views_router<<<io.num_tokens, 512, 0, st>>>(va);
+}
+
+// What one pass of the two grouped GEMMs runs over.
+struct Plan {
+    int n;                        // routed entries (rows through the experts)
+    int src_div;                  // activation source row of entry i = i / src_div
+    const uint32_t* idx;          // expert ids, stride `stride`
+    const float* w;               // routing weights, stride `stride`
+    int stride;
+    int e0, ne;                   // experts [e0, e0 + ne), layer.experts_dev pointing at e0
+    int t_shared;                 // tokens through the shared expert (0: none)
+    const float* src_rows;        // fp32 routed_x rows the entries read
+    const int* out_index;         // mode 1 output row of each expert-ordered row (null: same)
+    float* out_r;                 // mode 1 routed output rows
+};
+
+int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaStream_t st) {
+    const WsLayout& W = w.W;
     const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
     const uint8_t* exb = static_cast<const uint8_t*>(L.experts_dev);
-    const uint64_t R = (uint64_t)T * TOPK;
+    const uint64_t R = pl.n > 0 ? (uint64_t)pl.n : 1, T = pl.t_shared > 0 ? (uint64_t)pl.t_shared : 1;
 
-    // all tensor maps first, so a failure launches nothing
     GemmArgs g0, g1;
     memset(&g0, 0, sizeof(g0));
     memset(&g1, 0, sizeof(g1));
     int rc;
-    if ((rc = map_act(&g0.x_rhi, P(W.xhi), R, D)) || (rc = map_act(&g0.x_rlo, P(W.xlo), R, D)) ||
-        (rc = map_act(&g0.x_shi, P(W.dense_hi), T, D)) || (rc = map_act(&g0.x_slo, P(W.dense_lo), T, D)) ||
-        (rc = map_act(&g1.x_rhi, P(W.act_r_hi), R, FE)) || (rc = map_act(&g1.x_rlo, P(W.act_r_lo), R, FE)) ||
-        (rc = map_act(&g1.x_shi, P(W.act_s_hi), T, FS)) || (rc = map_act(&g1.x_slo, P(W.act_s_lo), T, FS)))
+    if ((rc = map_act(&g0.x_rhi, w.at(W.xhi), R, D)) || (rc = map_act(&g0.x_rlo, w.at(W.xlo), R, D)) ||
+        (rc = map_act(&g0.x_shi, w.at(W.dense_hi), T, D)) || (rc = map_act(&g0.x_slo, w.at(W.dense_lo), T, D)) ||
+        (rc = map_act(&g1.x_rhi, w.at(W.act_r_hi), R, FE)) || (rc = map_act(&g1.x_rlo, w.at(W.act_r_lo), R, FE)) ||
+        (rc = map_act(&g1.x_shi, w.at(W.act_s_hi), T, FS)) || (rc = map_act(&g1.x_slo, w.at(W.act_s_lo), T, FS)))
         return rc;
 
-    ViewsArgs va;
-    memset(&va, 0, sizeof(va));
-    va.T = (int)T; va.x_f32 = io.x_dev; va.x_bf16 = io.x_bf16_dev; va.L = L; va.eps = dims.eps;
-    va.inv_sqrt_d = 1.0f / sqrtf((float)D);
-    va.logit_bias = io.logit_bias_dev; va.route_logits = io.route_logits_dev;
-    va.dense_hi = static_cast<__half*>(P(W.dense_hi)); va.dense_lo = static_cast<__half*>(P(W.dense_lo));
-    va.routed = static_cast<float*>(P(W.routed));
-    va.idx = static_cast<uint32_t*>(P(W.idx)); va.w = static_cast<float*>(P(W.w));
-    va.logits_out = io.logits_dev;
-    tok_views_router<<<T, 512, 0, st>>>(va);
-
     RouteArgs ra;
-    ra.T = (int)T; ra.idx = va.idx; ra.w = va.w;
-    ra.perm_token = static_cast<int*>(P(W.perm_token)); ra.perm_w = static_cast<float*>(P(W.perm_w));
-    ra.pos = static_cast<int*>(P(W.pos));
-    ra.tiles0 = static_cast<Tile*>(P(W.tiles0)); ra.tiles1 = static_cast<Tile*>(P(W.tiles1));
-    ra.n_tiles = static_cast<int*>(P(W.n_tiles));
+    ra.n = pl.n; ra.src_div = pl.src_div; ra.idx = pl.idx; ra.w = pl.w; ra.stride = pl.stride;
+    ra.e0 = pl.e0; ra.ne = pl.ne; ra.t_shared = pl.t_shared;
+    ra.perm_src = w.p<int>(W.perm_src); ra.perm_w = w.p<float>(W.perm_w); ra.pos = w.p<int>(W.pos);
+    ra.tiles0 = w.p<Tile>(W.tiles0); ra.tiles1 = w.p<Tile>(W.tiles1); ra.n_tiles = w.p<int>(W.n_tiles);
     tok_route<<<1, 1024, 0, st>>>(ra);
-
-    tok_gather<<<(unsigned)R, 128, 0, st>>>(va.routed, ra.perm_token, static_cast<__half*>(P(W.xhi)),
-                                            static_cast<__half*>(P(W.xlo)));
+    if (pl.n > 0)
+        tok_gather<<<(unsigned)pl.n, 128, 0, st>>>(pl.src_rows, ra.perm_src, w.p<__half>(W.xhi), w.p<__half>(W.xlo));
 
     cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
@@ -833,9 +931,9 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     g0.r_sa = L.expert_gate.scales; g0.r_ba = L.expert_gate.biases; g0.r_sb = L.expert_up.scales; g0.r_bb = L.expert_up.biases;
     g0.s_sa = L.shared_gate.scales; g0.s_ba = L.shared_gate.biases; g0.s_sb = L.shared_up.scales; g0.s_bb = L.shared_up.biases;
     g0.k_r = D; g0.k_s = D; g0.rows_r = FE; g0.rows_s = FS;
-    g0.act_r_hi = static_cast<__half*>(P(W.act_r_hi)); g0.act_r_lo = static_cast<__half*>(P(W.act_r_lo));
-    g0.act_s_hi = static_cast<__half*>(P(W.act_s_hi)); g0.act_s_lo = static_cast<__half*>(P(W.act_s_lo));
-    g0.err = static_cast<int*>(ws);
+    g0.act_r_hi = w.p<__half>(W.act_r_hi); g0.act_r_lo = w.p<__half>(W.act_r_lo);
+    g0.act_s_hi = w.p<__half>(W.act_s_hi); g0.act_s_lo = w.p<__half>(W.act_s_lo);
+    g0.err = w.p<int>(0);
     grouped_gemm<0><<<num_sms, THREADS, SMEM_BYTES, st>>>(g0);
 
     g1.tiles = ra.tiles1; g1.n_tiles = ra.n_tiles + 1;
@@ -844,22 +942,106 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     g1.r_sa = L.expert_down.scales; g1.r_ba = L.expert_down.biases; g1.r_sb = g1.r_sa; g1.r_bb = g1.r_ba;
     g1.s_sa = L.shared_down.scales; g1.s_ba = L.shared_down.biases; g1.s_sb = g1.s_sa; g1.s_bb = g1.s_ba;
     g1.k_r = FE; g1.k_s = FS; g1.rows_r = D; g1.rows_s = D;
-    g1.out_r = static_cast<float*>(P(W.out_r)); g1.out_s = static_cast<float*>(P(W.out_s));
-    g1.perm_w = ra.perm_w;
-    g1.err = static_cast<int*>(ws);
+    g1.out_r = pl.out_r; g1.out_s = w.p<float>(W.out_s);
+    g1.perm_w = ra.perm_w; g1.out_index = pl.out_index;
+    g1.err = w.p<int>(0);
     grouped_gemm<1><<<num_sms, THREADS, SMEM_BYTES, st>>>(g1);
-
-    CombineArgs ca;
-    ca.T = (int)T; ca.x_f32 = io.x_dev; ca.x_bf16 = io.x_bf16_dev; ca.pos = ra.pos;
-    ca.out_r = g1.out_r; ca.out_s = g1.out_s; ca.L = L; ca.eps = dims.eps;
-    ca.hidden_out = io.hidden_out_dev; ca.h1_out = io.h1_dev; ca.h2_out = io.h2_dev;
-    tok_combine<<<T, 512, 0, st>>>(ca);
-
-    if (io.topk_idx_dev) cudaMemcpyAsync(io.topk_idx_dev, va.idx, R * 4, cudaMemcpyDeviceToDevice, st);
-    if (io.topk_w_dev) cudaMemcpyAsync(io.topk_w_dev, va.w, R * 4, cudaMemcpyDeviceToDevice, st);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return set_cuda_error("gtm_moe_tokens", e);
     return GTM_OK;
+}
+
+void launch_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const Ws& w, const int* pos,
+                    const float* out_r, cudaStream_t st) {
+    CombineArgs ca;
+    ca.T = (int)io.num_tokens; ca.x_f32 = io.x_dev; ca.x_bf16 = io.x_bf16_dev; ca.pos = pos;
+    ca.out_r = out_r; ca.out_s = w.p<float>(w.W.out_s); ca.L = L; ca.eps = dims.eps;
+    ca.hidden_out = io.hidden_out_dev; ca.h1_out = io.h1_dev; ca.h2_out = io.h2_dev;
+    tok_combine<<<io.num_tokens, 512, 0, st>>>(ca);
+}
+
+int finish(const char* what, const GtmTokensIO* io, const Ws* w, cudaStream_t st) {
+    if (io && w) {
+        const size_t n = (size_t)io->num_tokens * TOPK * 4;
+        if (io->topk_idx_dev) cudaMemcpyAsync(io->topk_idx_dev, w->at(w->W.idx), n, cudaMemcpyDeviceToDevice, st);
+        if (io->topk_w_dev) cudaMemcpyAsync(io->topk_w_dev, w->at(w->W.w), n, cudaMemcpyDeviceToDevice, st);
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error(what, e);
+    return GTM_OK;
+}
+
+}  // namespace
+
+int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, void* ws, size_t ws_bytes,
+                  cudaStream_t st, int num_sms) {
+    const uint32_t T = io.num_tokens;
+    const Ws w{ws_layout(T, T * TOPK, false), static_cast<uint8_t*>(ws)};
+    if (ws_bytes < w.W.total) return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes", w.W.total);
+    launch_views(dims, L, io, w, st);
+    Plan pl;
+    pl.n = (int)(T * TOPK); pl.src_div = TOPK; pl.idx = w.p<uint32_t>(w.W.idx); pl.w = w.p<float>(w.W.w); pl.stride = 1;
+    pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.src_rows = w.p<float>(w.W.routed); pl.out_index = nullptr;
+    pl.out_r = w.p<float>(w.W.out_r);
+    const int rc = run_gemms(L, w, pl, num_sms, st);
+    if (rc) return rc;
+    launch_combine(dims, L, io, w, w.p<int>(w.W.pos), pl.out_r, st);
+    return finish("gtm_moe_tokens", &io, &w, st);
+}
+
+// ---- expert parallelism ----------------------------------------------------------------------
+// Every phase of a rank lays the workspace out from (max_tokens, max_recv_rows) of its config, so
+// the regions that carry data from one phase to the next (views, dispatch tables, shared-expert
+// output) are the same in all of them.
+static Ws ep_ws(const GtmEpConfig& ep, void* ws) {
+    return Ws{ws_layout(ep.max_tokens, ep.max_recv_rows, true), static_cast<uint8_t*>(ws)};
+}
+
+int launch_ep_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
+                       float* send_rows, GtmEpMeta* send_meta, int32_t* send_counts, void* ws, cudaStream_t st) {
+    const uint32_t T = io.num_tokens;
+    const Ws w = ep_ws(ep, ws);
+    launch_views(dims, L, io, w, st);
+    DispatchArgs da;
+    da.n = (int)(T * TOPK); da.world = (int)ep.world; da.epr = NE / (int)ep.world;
+    da.idx = w.p<uint32_t>(w.W.idx); da.w = w.p<float>(w.W.w);
+    da.send_counts = send_counts; da.send_pos = w.p<int>(w.W.send_pos); da.send_src = w.p<int>(w.W.send_src);
+    da.send_meta = send_meta;
+    tok_dispatch<<<1, 1024, 0, st>>>(da);
+    tok_copy_rows<<<T * TOPK, 256, 0, st>>>(w.p<float>(w.W.routed), da.send_src, send_rows);
+    return finish("gtm_moe_ep_dispatch", &io, &w, st);
+}
+
+int launch_ep_shared(const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep, void* ws, cudaStream_t st,
+                     int num_sms) {
+    const Ws w = ep_ws(ep, ws);
+    Plan pl;
+    memset(&pl, 0, sizeof(pl));
+    pl.n = 0; pl.src_div = 1; pl.idx = w.p<uint32_t>(w.W.idx); pl.w = w.p<float>(w.W.w); pl.stride = 1;
+    pl.e0 = 0; pl.ne = 0; pl.t_shared = (int)io.num_tokens;
+    const int rc = run_gemms(L, w, pl, num_sms, st);
+    if (rc) return rc;
+    return finish("gtm_moe_ep_shared", nullptr, nullptr, st);
+}
+
+int launch_ep_experts(const GtmLayer& L, const GtmEpConfig& ep, const float* recv_rows, const GtmEpMeta* recv_meta,
+                      uint32_t n_recv, float* ret_rows, void* ws, cudaStream_t st, int num_sms) {
+    if (n_recv == 0) return GTM_OK;
+    const Ws w = ep_ws(ep, ws);
+    const int epr = NE / (int)ep.world;
+    Plan pl;
+    pl.n = (int)n_recv; pl.src_div = 1;
+    pl.idx = &recv_meta->expert; pl.w = &recv_meta->weight; pl.stride = 2;
+    pl.e0 = (int)ep.rank * epr; pl.ne = epr; pl.t_shared = 0;
+    pl.src_rows = recv_rows; pl.out_index = w.p<int>(w.W.perm_src); pl.out_r = ret_rows;
+    const int rc = run_gemms(L, w, pl, num_sms, st);
+    if (rc) return rc;
+    return finish("gtm_moe_ep_experts", nullptr, nullptr, st);
+}
+
+int launch_ep_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
+                      const float* ret_rows, void* ws, cudaStream_t st) {
+    const Ws w = ep_ws(ep, ws);
+    launch_combine(dims, L, io, w, w.p<int>(w.W.send_pos), ret_rows, st);
+    return finish("gtm_moe_ep_combine", nullptr, nullptr, st);
 }
 
 int tokens_check(void* ws, cudaStream_t st) {

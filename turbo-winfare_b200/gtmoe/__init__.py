@@ -72,6 +72,11 @@ class TokensIO(C.Structure):
                 ("logit_bias_dev", C.c_void_p), ("route_logits_dev", C.c_void_p)]
 
 
+class EpConfig(C.Structure):
+    _fields_ = [("world", C.c_uint32), ("rank", C.c_uint32), ("max_tokens", C.c_uint32),
+                ("max_recv_rows", C.c_uint32)]
+
+
 _lib = None
 
 # (name, restype, argtypes) for every entry point in include/gtmoe.h and include/gtmoe_synth.h
@@ -95,6 +100,16 @@ SIGNATURES = {
     "gtm_moe_tokens_workspace_bytes": (_SZ, [C.POINTER(Dims), _U32]),
     "gtm_moe_tokens": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), _P, _SZ, _P]),
     "gtm_moe_tokens_check": (_I, [_P, _P]),
+    "gtm_moe_ep_workspace_bytes": (_SZ, [C.POINTER(Dims), C.POINTER(EpConfig)]),
+    "gtm_moe_ep_dispatch": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
+                                 _P, _P, _P, _P, _SZ, _P]),
+    "gtm_moe_ep_shared": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
+                               _P, _SZ, _P]),
+    "gtm_moe_ep_experts": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(EpConfig), _P, _P, _U32, _P,
+                                _P, _SZ, _P]),
+    "gtm_moe_ep_combine": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
+                                _P, _P, _SZ, _P]),
+    "gtm_moe_ep_check": (_I, [_P, _P]),
     "gtm_synth_expert_layout": (_I, [_U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_resident_layout": (_I, [_U32, _U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_experts": (_I, [_U64, _U32, _U32, _U32, _U32, _U32, _P, _P]),
