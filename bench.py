@@ -14,6 +14,13 @@ the 30 layers = 30 MoE-layer tokens = one gtm_moe_decode launch.
 Multi-GPU (--gpus N under torchrun): batch-1 decode does not shard (one token's all-to-all
 would cost more than the layer), so each rank runs an independent replica ("weak" scaling).
 
+Other workloads (--workload), parity configs measured on request, not the default line:
+  batch64      BASELINE config 2: 64 tokens per step through one layer, router logits biased to
+               Zipf(1.1) expert popularity (gtm_moe_tokens); N>1 runs replicas
+  prefill4096  BASELINE config 3: 4096 bf16 tokens per step through one layer, uniform routing
+               logits; with N GPUs the layer is expert-parallel (128/N experts and 4096/N tokens
+               per rank, NCCL all-to-all dispatch and combine, gtmoe.ep)
+
 --impl reference runs the reference's own CPU arithmetic (src/cpu_reference.cpp compiled from
 its sources into oracle/_ref/libgtref.so, single-threaded as shipped) on every host core in
 parallel processes, for the same metric.
@@ -45,13 +52,14 @@ NORM_BYTES = 6 * 2816 * 2 + 128 * 2 + 2                           # norm weights
 LAYER_FLOPS = 2 * (8 * 3 * 704 * 2816 + 3 * 2112 * 2816 + 128 * 2816)  # 131,563,520
 
 
-def peaks():
+def peaks(kind: str = "hbm"):
+    """(peak, source): HBM GB/s or dense bf16 TFLOP/s (burst) of this pool's B200s."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return (float(d["hbm_gbs"]) if kind == "hbm" else float(d["bf16_tflops"])), "measured"
+    return (6650.0 if kind == "hbm" else 1590.0), "fallback"
 
 
 class ClockSampler:
@@ -163,12 +171,15 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS_DEFAULT, help="stack depth (profiling only)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode30", choices=["decode30", "batch64", "prefill4096"])
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
 
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload != "decode30":
+        return bench_tokens(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -275,6 +286,199 @@ def main():
                          "tflops": L * LAYER_FLOPS / (per_launch_ms / 1000.0) / 1e12},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": D * 4, "d2h_bytes_per_step": D * 4},
             "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ---- T > 1 workloads (configs 2 and 3) ------------------------------------------------------------
+WEIGHT_BYTES_EXPERT = EXPERT_BYTES
+
+
+def token_cpu_baseline(seconds: float, cfg: str):
+    """The reference's CPU arithmetic on a bounded sample of the workload's tokens (rank 0)."""
+    import multiprocessing as mp
+    import oracle
+    kind, impl = ("reference", "ref") if oracle.ref_available() else ("port", "oracle")
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(1) as pool:
+        done, wall = pool.map(token_cpu_worker, [(seconds, cfg, impl)])[0]
+    return {"value": done / wall, "unit": "tokens/s", "cores": 1, "kind": kind,
+            "sample": f"{done} tokens of the {cfg} workload through layer 0 (1 process, ~{seconds:.0f} s)"}
+
+
+def token_cpu_worker(a):
+    seconds, cfg, impl = a
+    import numpy as np
+    import oracle
+    from gtmoe import workloads
+    L = oracle.SynthLayer(0, 0)
+    bias = workloads.zipf_logit_bias() if cfg == "batch64" else None
+    rl = workloads.uniform_route_logits(64) if cfg == "prefill4096" else None
+    xs = [oracle.synth_x(0, t) for t in range(64)]
+    if cfg == "prefill4096":
+        xs = [workloads.bf16_round(x) for x in xs]
+    for t in range(4):   # materialise experts outside the timed loop
+        L.block(xs[t], logit_bias=bias, route_logits=None if rl is None else rl[t], impl=impl)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        t = done % 64
+        L.block(xs[t], logit_bias=bias, route_logits=None if rl is None else rl[t], impl=impl)
+        done += 1
+    return done, time.perf_counter() - t0
+
+
+def bench_tokens(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = args.workload
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = token_cpu_baseline(args.cpu_seconds, cfg)
+
+    import numpy as np
+    import torch
+    import gtmoe
+    from gtmoe import ep, workloads
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    D, K = gtmoe.HIDDEN, gtmoe.TOP_K
+    T_total = 64 if cfg == "batch64" else 4096
+    expert_parallel = cfg == "prefill4096" and world > 1
+    T = T_total // world if expert_parallel else T_total
+    n_sets = 4   # distinct token batches cycled over the steps
+    x32 = torch.empty(n_sets * T * D, device="cuda")
+    gtmoe.synth_x(0, rank * n_sets * T, n_sets * T, x32)
+    xs = x32.view(n_sets, T, D)
+    kw = {}
+    if cfg == "batch64":
+        kw["logit_bias"] = torch.from_numpy(workloads.zipf_logit_bias()).cuda()
+    else:
+        xs = xs.to(torch.bfloat16)
+        rl_all = torch.from_numpy(workloads.uniform_route_logits(n_sets * T_total)).cuda().view(n_sets, T_total, -1)
+        rl = rl_all[:, rank * T:(rank + 1) * T] if expert_parallel else rl_all
+    out = torch.empty(T, D, device="cuda")
+    idx_hist = torch.empty(n_sets, T, K, dtype=torch.int32, device="cuda")
+
+    if expert_parallel:
+        shard = ep.EpShardModel(0, rank, world)
+        ops = ep.CudaEpOps(shard.layer, rank, world, max_tokens=T, max_recv_rows=T_total * K)
+        xch = ep.NcclExchange()
+        weights_gb = shard.weight_bytes() / 1e9
+
+        def step(i, x=None, o=None):
+            j = i % n_sets
+            a = dict(kw, route_logits=rl[j].contiguous())
+            ep.ep_layer(ops, xch, xs[j] if x is None else x, out if o is None else o, topk_idx=idx_hist[j], **a)
+        check = ops.check
+    else:
+        model = gtmoe.SynthModel(1, seed=0)
+        blk = gtmoe.TokenBlock(T)
+        weights_gb = model.weight_bytes() / 1e9
+
+        def step(i, x=None, o=None):
+            j = i % n_sets
+            a = dict(kw)
+            if cfg == "prefill4096":
+                a["route_logits"] = rl[j]
+            blk(model.layers[0], xs[j] if x is None else x, out if o is None else o, topk_idx=idx_hist[j], **a)
+        check = blk.check
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        step(i)
+    check()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    check()
+    ms = ev0.elapsed_time(ev1)
+    barrier()
+    # end to end: host -> device copy of the step's tokens, device -> host of the result
+    xh = torch.empty((n_sets, T, D), dtype=xs.dtype, pin_memory=True)
+    xh.copy_(xs.cpu())
+    oh = torch.empty((T, D), dtype=torch.float32, pin_memory=True)
+    xin = torch.empty(T, D, dtype=xs.dtype, device="cuda")
+    for i in range(args.warmup):
+        xin.copy_(xh[i % n_sets], non_blocking=True)
+        step(i, xin)
+        oh.copy_(out, non_blocking=True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        xin.copy_(xh[i % n_sets], non_blocking=True)
+        step(i, xin)
+        oh.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    check()
+    ms_e2e = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms, ms_e2e], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = float(t[0]), float(t[1])
+    per_step_ms = ms / args.steps
+    tokens_per_step = T_total if expert_parallel else T * world
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+    e2e = tokens_per_step * args.steps / (ms_e2e / 1000.0)
+    ids = idx_hist.cpu().numpy()
+    distinct = float(np.mean([len(np.unique(ids[j])) for j in range(n_sets)]))
+    act_bytes = T * D * (2 if cfg == "prefill4096" else 4) + T * D * 4
+    if cfg == "batch64":
+        alg = distinct * EXPERT_BYTES + SHARED_BYTES + ROUTER_BYTES + act_bytes
+        achieved = alg / (per_step_ms / 1000.0) / 1e9
+        peak, pk = peaks("hbm")
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": pk, "traffic": None, "algorithmic_bytes_per_step": alg,
+                "scope": "whole layer call (views, routing, two grouped GEMMs, combine)",
+                "distinct_experts_per_step": distinct}
+        metric = "MoE-layer tokens/s (batch 64 decode, Zipf routing)"
+    else:
+        flops = T_total * (LAYER_FLOPS - 2 * 128 * 2816)   # experts + shared (routing logits given)
+        achieved = flops / (per_step_ms / 1000.0) / 1e12 / (world if expert_parallel else 1)
+        peak, pk = peaks("tensor")
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": pk, "traffic": None, "flops_per_step": flops,
+                "scope": "whole layer call, useful FLOPs per GPU (the fp16 high/low activation split doubles "
+                         "the tensor-core work)"}
+        metric = "MoE-layer tokens/s (prefill 4096 bf16 tokens)"
+    if rank == 0:
+        line = {
+            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_step_ms, "higher_is_better": True,
+            "scaling": "strong" if expert_parallel else "weak", "vs_baseline": None,
+            "dtype": "f32 (fp16 hi/lo tensor-core operands)", "data": "synthetic",
+            "config": {"workload": ("config2: 64 tokens through one MoE layer, Zipf(1.1) router bias" if cfg == "batch64"
+                                    else "config3: 4096 bf16 tokens through one MoE layer, uniform routing logits"),
+                       "tokens_per_step": tokens_per_step, "weights_gb_per_gpu": weights_gb,
+                       "parallelism": (f"ep{world}" if expert_parallel else ("replicas" if world > 1 else "single")),
+                       "l2": "4 token sets cycled; weights of touched experts 0.3-0.45 GB > L2"},
+            "roofline": roof,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * D * xs.element_size(),
+                    "d2h_bytes_per_step": T * D * 4},
+            "gpu_launches": args.steps * (11 if expert_parallel else 6),
             "clocks": clk.summary(),
             "cpu_baseline": cb,
         }
