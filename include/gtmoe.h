@@ -44,6 +44,31 @@ GTM_API const char* gtm_last_error(void);
 GTM_API const char* gtm_version(void);
 
 /* ---------------------------------------------------------------------------------------
+ * Device context, buffers and fences (replaces the D3D12Context calls the MoE path makes,
+ * include/gturbo/d3d12_context.hpp:22-54). One CUDA stream per context; not thread-safe per
+ * context, as the reference runs one generation at a time.
+ * ------------------------------------------------------------------------------------- */
+
+/* D3D12Context construction: a context on CUDA device `device` with its own stream. */
+GTM_API int gtm_ctx_create(int device, void** ctx_out);
+GTM_API int gtm_ctx_destroy(void* ctx);
+/* The context's cudaStream_t (pass it as `stream` to the calls below). */
+GTM_API void* gtm_ctx_stream(void* ctx);
+/* create_uma_buffer (d3d12_context.cpp:135-160): device memory, 64-bit addresses (no 4 GB
+ * root-descriptor limit, runner.cpp:330-333). */
+GTM_API int gtm_buffer_alloc(void* ctx, uint64_t bytes, void** dev_out);
+GTM_API int gtm_buffer_free(void* ctx, void* dev);
+/* Host <-> device copies on the context's stream, ordered with the kernels submitted there. */
+GTM_API int gtm_buffer_upload(void* ctx, void* dev, uint64_t offset, const void* host, uint64_t bytes);
+GTM_API int gtm_buffer_download(void* ctx, void* host, const void* dev, uint64_t offset, uint64_t bytes);
+/* submit_command_list -> fence value (d3d12_context.cpp:100-114): a ticket for all work issued
+ * on the context's stream so far. */
+GTM_API int gtm_submit(void* ctx, uint64_t* ticket_out);
+/* wait_for_fence (d3d12_context.cpp:122-127) with a bound instead of INFINITE: GTM_OK when the
+ * work up to `ticket` is done, GTM_ERR_TIMEOUT after timeout_ms. */
+GTM_API int gtm_wait(void* ctx, uint64_t ticket, uint32_t timeout_ms);
+
+/* ---------------------------------------------------------------------------------------
  * Kernel entry points (the reference's compute kernels, same arithmetic contract).
  * Quantised matrices use MLX affine 4-/8-bit, group 64 along the input dimension, packed
  * low nibble first, with bf16 scales and biases laid out [rows][in_dim/64].

@@ -84,6 +84,15 @@ _P, _U32, _U64, _I, _F, _SZ = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_f
 SIGNATURES = {
     "gtm_last_error": (C.c_char_p, []),
     "gtm_version": (C.c_char_p, []),
+    "gtm_ctx_create": (_I, [_I, C.POINTER(_P)]),
+    "gtm_ctx_destroy": (_I, [_P]),
+    "gtm_ctx_stream": (_P, [_P]),
+    "gtm_buffer_alloc": (_I, [_P, _U64, C.POINTER(_P)]),
+    "gtm_buffer_free": (_I, [_P, _P]),
+    "gtm_buffer_upload": (_I, [_P, _P, _U64, _P, _U64]),
+    "gtm_buffer_download": (_I, [_P, _P, _P, _U64, _U64]),
+    "gtm_submit": (_I, [_P, C.POINTER(_U64)]),
+    "gtm_wait": (_I, [_P, _U64, _U32]),
     "gtm_gemv_q4": (_I, [_U32, _U32, _P, _P, _P, _P, _P, _P]),
     "gtm_gemv_q8": (_I, [_U32, _U32, _P, _P, _P, _P, _P, _P]),
     "gtm_router_topk": (_I, [_U32, _U32, _P, _P, _P, _P, _P]),
@@ -311,3 +320,4 @@ class TokenBlock:
 
     def check(self, stream=None):
         check(lib().gtm_moe_tokens_check(self.ws_ptr, _stream(stream)))
+
