@@ -202,6 +202,16 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
 /* Reads back and clears the device-side error flag of a workspace after gtm_moe_decode
  * calls (synchronises `stream`). Returns GTM_OK or GTM_ERR_TIMEOUT. */
 GTM_API int gtm_moe_decode_check(void* workspace_dev, void* stream);
+/* gtm_moe_decode without a caller workspace. No counterpart in the reference. For callers that
+ * cannot allocate device memory (a bare C/FFI host with no device allocator, or a process that
+ * reserves all device memory at start-up and forbids later allocation): the scratch is a
+ * statically sized array of the library, 256 KB per device, so the call allocates nothing. The
+ * first call on each device looks that array up and should come before any stream capture.
+ * Every call on a device shares the one array: calls that overlap on the GPU race. layers ==
+ * NULL with num_layers == 0 reads and clears the array's device-side error word instead
+ * (synchronises `stream`; returns GTM_OK or GTM_ERR_TIMEOUT). */
+GTM_API int gtm_moe_decode_noalloc(const GtmDims* dims, const GtmLayer* layers, int num_layers,
+                                   const GtmDecodeIO* io, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * MoE block for T > 1 tokens (batched decode, prefill): one layer, tokens grouped by expert.

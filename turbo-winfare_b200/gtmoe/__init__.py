@@ -106,6 +106,7 @@ SIGNATURES = {
     "gtm_moe_decode_workspace_bytes": (_SZ, [C.POINTER(Dims)]),
     "gtm_moe_decode": (_I, [C.POINTER(Dims), C.POINTER(Layer), _I, C.POINTER(DecodeIO), _P, _SZ, _P]),
     "gtm_moe_decode_check": (_I, [_P, _P]),
+    "gtm_moe_decode_noalloc": (_I, [C.POINTER(Dims), C.POINTER(Layer), _I, C.POINTER(DecodeIO), _P]),
     "gtm_moe_tokens_workspace_bytes": (_SZ, [C.POINTER(Dims), _U32]),
     "gtm_moe_tokens": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), _P, _SZ, _P]),
     "gtm_moe_tokens_check": (_I, [_P, _P]),
@@ -321,3 +322,21 @@ class TokenBlock:
     def check(self, stream=None):
         check(lib().gtm_moe_tokens_check(self.ws_ptr, _stream(stream)))
 
+
+
+def decode_noalloc(layers, hidden_in, hidden_out, *, num_layers: int | None = None, first_layer: int = 0,
+                   topk_idx=None, topk_w=None, logits=None, h1=None, h2=None, hidden_layers=None, logit_bias=None,
+                   norm_between_layers=True, stream=None):
+    """gtm_moe_decode_noalloc: the batch-1 decode using the library's static per-device scratch,
+    for callers that cannot allocate a workspace (see include/gtmoe.h)."""
+    n = num_layers if num_layers is not None else len(layers) - first_layer
+    layer_arr = C.cast(C.addressof(layers) + first_layer * C.sizeof(Layer), C.POINTER(Layer))
+    io = DecodeIO(hidden_in.data_ptr(), hidden_out.data_ptr(), ptr(topk_idx), ptr(topk_w), ptr(logits), ptr(h1),
+                  ptr(h2), ptr(hidden_layers), ptr(logit_bias), NORM_BETWEEN_LAYERS if norm_between_layers else 0)
+    dims = default_dims()
+    check(lib().gtm_moe_decode_noalloc(C.byref(dims), layer_arr, n, C.byref(io), _stream(stream)))
+
+
+def decode_noalloc_check(stream=None):
+    """Reads and clears the static scratch's device-side error word (synchronises the stream)."""
+    check(lib().gtm_moe_decode_noalloc(None, None, 0, None, _stream(stream)))
