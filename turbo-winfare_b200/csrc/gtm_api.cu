@@ -214,10 +214,14 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
         const GtmLayer& L = layers[l];
         if (!L.resident_dev || !L.experts_dev || L.expert_stride == 0)
             return set_error(GTM_ERR_INVALID, "gtm_moe_decode: layer %d has a null base or zero stride", l);
+        // weight rows, scales and biases move by 16-byte bulk copies; norm vectors by 16-byte cp.async
         const uint64_t offs16[] = {L.router.weight, L.expert_stride, L.expert_gate.weight, L.expert_up.weight,
                                    L.expert_down.weight, L.shared_gate.weight, L.shared_up.weight, L.shared_down.weight,
-                                   L.pre_ffn_norm, L.pre_ffn_norm_2, L.router_scale, L.post_ffn_norm_1,
-                                   L.post_ffn_norm_2, L.post_ffn_norm};
+                                   L.expert_gate.scales, L.expert_gate.biases, L.expert_up.scales, L.expert_up.biases,
+                                   L.expert_down.scales, L.expert_down.biases, L.shared_gate.scales,
+                                   L.shared_gate.biases, L.shared_up.scales, L.shared_up.biases, L.shared_down.scales,
+                                   L.shared_down.biases, L.per_expert_scale, L.pre_ffn_norm, L.pre_ffn_norm_2,
+                                   L.router_scale, L.post_ffn_norm_1, L.post_ffn_norm_2, L.post_ffn_norm};
         if (!aligned(L.resident_dev, 16) || !aligned(L.experts_dev, 16))
             return set_error(GTM_ERR_MISALIGNED, "gtm_moe_decode: layer %d base pointers must be 16-byte aligned", l);
         for (uint64_t o : offs16)

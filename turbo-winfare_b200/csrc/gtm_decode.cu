@@ -87,6 +87,7 @@ struct Smem {
     // bf16 norm vectors, copied ahead of use: this layer's pre_ffn_norm, pre_ffn_norm_2,
     // router.scale and the previous layer's post_ffn_norm_1, post_ffn_norm_2, post_ffn_norm
     alignas(16) uint16_t nw[6][D];
+    alignas(16) uint16_t pes[NE];   // per_expert_scale of the layer (copied with the pre-FFN norms)
     float slot[MAX_ITEMS][NW][16];
     float terms[GD];
     double red[40];
@@ -399,6 +400,8 @@ __device__ void load_norms_async(Smem& s, const GtmLayer* Lpre, const GtmLayer* 
                            : v == 3 ? L->post_ffn_norm_1 : v == 4 ? L->post_ffn_norm_2 : L->post_ffn_norm;
         cp_async16(&s.nw[v][c * 8], rp(L->resident_dev, off) + c * 16);
     }
+    if (Lpre && threadIdx.x < NE * 2 / 16)
+        cp_async16(&s.pes[threadIdx.x * 8], rp(Lpre->resident_dev, Lpre->per_expert_scale) + threadIdx.x * 16);
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
@@ -612,7 +615,7 @@ __device__ void select_topk(Smem& s, const GtmLayer& L, const float* logits, boo
     }
     // lanes 0..7: exp and per-expert scale in parallel, the sum in order on every lane
     const float e = lane < TOPK ? expf(__fsub_rn(my_sel, top0)) : 0.0f;
-    const uint16_t pes_bits = lane < TOPK ? *rp16(L.resident_dev, L.per_expert_scale + 2ull * (uint32_t)my_idx) : 0;
+    const uint16_t pes_bits = lane < TOPK ? s.pes[my_idx] : 0;
     float sum = 0.0f;
 #pragma unroll
     for (int k = 0; k < TOPK; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, k));
@@ -798,6 +801,22 @@ __device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
     }
 }
 
+// L2 prefetch of this CTA's routed gate/up rows (known once the top-8 is): per tile 8 gate rows,
+// 8 up rows and their scales and biases, each a contiguous range.
+__device__ void prefetch_routed_gate_up(const Smem& s, const GtmLayer& L, int cta, int G) {
+    if ((threadIdx.x >> 5) != NW - 2) return;
+    const int lane = threadIdx.x & 31;
+    const int t0 = share(TILES_R, cta, G), t1 = share(TILES_R, cta + 1, G);
+    for (int i = lane; i < 6 * (t1 - t0); i += 32) {
+        const int T = t0 + i / 6, part = i % 6, k = T / (FE / 8), r8 = T - k * (FE / 8);
+        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
+        const GtmQuant& q = part < 3 ? L.expert_gate : L.expert_up;
+        const int pp = part % 3;
+        if (pp == 0) prefetch_l2(blk + q.weight + (uint64_t)r8 * 8 * ROW_GU, 8 * ROW_GU);
+        else prefetch_l2(blk + (pp == 1 ? q.scales : q.biases) + (uint64_t)r8 * 8 * GD * 2, 8 * GD * 2);
+    }
+}
+
 // L2 prefetch of this CTA's routed-down rows (known once the top-8 is).
 __device__ void prefetch_routed_down(const Smem& s, const GtmLayer& L, int cta, int G) {
     if ((threadIdx.x >> 5) != NW - 1) return;
@@ -856,6 +875,7 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
                     io.topk_w_dev ? io.topk_w_dev + (size_t)l * TOPK : nullptr,
                     io.logits_dev ? io.logits_dev + (size_t)l * NE : nullptr);
         __syncthreads();
+        prefetch_routed_gate_up(s, L, cta, G);
         prefetch_routed_down(s, L, cta, G);
         routed_gate_up(s, P, L, share(TILES_R, cta, G), share(TILES_R, cta + 1, G));
         arrive(P, BAR_B, ep);
@@ -867,9 +887,16 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
 
         // ---- P3 ----
         if (!wait_all(P, s, BAR_B, ep)) return;
-        stage_from_global(s.ab, P.act, ACT_R);
-        build_table(s.ab, TOPK * GFE, s.tbl_rk, s.xs_rk, s.cs_rk);
-        __syncthreads();
+        {
+            const int i0 = share(ITEMS_RD, cta, G), i1 = share(ITEMS_RD, cta + 1, G);
+            if (i1 > i0) {
+                const int kmin = i0 / OT, kmax = (i1 - 1) / OT;
+                stage_from_global(s.ab + kmin * FE, P.act + kmin * FE, (kmax - kmin + 1) * FE);
+                build_table(s.ab + kmin * FE, (kmax - kmin + 1) * GFE, s.tbl_rk + kmin * GFE * TBL_WORDS,
+                            s.xs_rk + kmin * GFE, s.cs_rk + kmin * GFE);
+            }
+            __syncthreads();
+        }
         if (l + 1 < P.num_layers) prefetch_layer_static(P.layers[l + 1], cta, G);
         load_norms_async(s, l + 1 < P.num_layers ? &P.layers[l + 1] : nullptr, &L);
         routed_down(s, P, L, share(ITEMS_RD, cta, G), share(ITEMS_RD, cta + 1, G));
