@@ -63,12 +63,66 @@ def peaks(kind: str = "hbm"):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region.
+
+    A thread polls NVML every 5 ms between __enter__ and __exit__; `sample()` called right
+    before the closing synchronize adds one reading taken while the queued steps still run, so a
+    timed region of a few milliseconds has at least one sample under load. Falls back to
+    `nvidia-smi -lms 200` when NVML cannot be opened. Only reads; changes no GPU setting."""
+
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu: int):
-        self.gpu, self.samples, self.proc = gpu, [], None
+        self.gpu, self.samples, self.proc, self.nv, self.h = gpu, [], None, None, None
+        self.stop = threading.Event()
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            try:
+                import torch
+                p = torch.cuda.get_device_properties(gpu)
+                bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+                self.h = nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+            except Exception:
+                self.h = nv.nvmlDeviceGetHandleByIndex(gpu)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            g = lambda n, d: getattr(nv, n, d)
+            self.bits = [g("nvmlClocksEventReasonHwSlowdown", g("nvmlClocksThrottleReasonHwSlowdown", 0x8)),
+                         g("nvmlClocksEventReasonHwThermalSlowdown", g("nvmlClocksThrottleReasonHwThermalSlowdown", 0x40)),
+                         g("nvmlClocksEventReasonSwThermalSlowdown", g("nvmlClocksThrottleReasonSwThermalSlowdown", 0x20)),
+                         g("nvmlClocksEventReasonSwPowerCap", g("nvmlClocksThrottleReasonSwPowerCap", 0x4))]
+            self._reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:
+            self.nv = None
+
+    def sample(self):
+        if self.nv is None:
+            return
+        try:
+            mhz = float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            r = int(self._reasons(self.h))
+            self.samples.append((mhz, self.max_mhz, [n for n, b in zip(self.NAMES, self.bits) if r & b]))
+        except Exception:
+            pass
+
+    def _poll(self):
+        while not self.stop.wait(0.005):
+            self.sample()
+
+    def _read_smi(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                self.samples.append((float(parts[1]), float(parts[2]) if parts[2].replace(".", "").isdigit() else None,
+                                     [n for i, n in enumerate(self.NAMES) if parts[5 + i] == "Active"]))
 
     def __enter__(self):
+        if self.nv is not None:
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -76,19 +130,16 @@ class ClockSampler:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t = threading.Thread(target=self._read_smi, daemon=True)
             self.t.start()
         except OSError:
             self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.samples.append(parts)
-
     def __exit__(self, *a):
+        self.stop.set()
+        if self.nv is not None:
+            self.t.join(timeout=1)
         if self.proc:
             self.proc.terminate()
             try:
@@ -99,12 +150,11 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
-        mx = max((float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()), default=None)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i] == "Active"})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(self.samples)}
+        sm = sorted(s[0] for s in self.samples)
+        mx = max((s[1] for s in self.samples if s[1] is not None), default=None)
+        reasons = sorted({n for s in self.samples for n in s[2]})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml" if self.nv is not None else "nvidia-smi"}
 
 
 def cpu_reference_worker(args):
@@ -227,6 +277,7 @@ def main():
             j = args.warmup + i
             dec(xs[j * D:(j + 1) * D], out)
         ev1.record(stream)
+        clk.sample()
         torch.cuda.synchronize()
     dec.check()
     ms = ev0.elapsed_time(ev1)
@@ -411,6 +462,7 @@ def bench_tokens(args):
         for i in range(args.steps):
             step(i)
         ev1.record(stream)
+        clk.sample()
         torch.cuda.synchronize()
     check()
     ms = ev0.elapsed_time(ev1)

@@ -14,21 +14,22 @@
 //   6. tok_combine        h2 = sum over the 8 slots in router order, shared output, layer tail
 //
 // Grouped GEMM: one CTA per SM, persistent over a tile list built on the device. A tile is 256
-// weight rows (two MMA M=128 halves, two TMEM accumulators) by up to 128 tokens of one expert
-// (MMA N), over K in blocks of 64 (one quantisation group): D[row][token] += W[row][k] X[token][k].
-// Gate/up tiles put 128 gate rows in one half and the same 128 up rows in the other, so one
-// epilogue thread holds both halves of its GeGLU pair. Per K block:
+// weight rows (two MMA M=128 halves) by up to 96 tokens of one expert (MMA N), over K in blocks of
+// 64 (one quantisation group): D[row][token] += W[row][k] X[token][k]. Gate/up tiles put 128 gate
+// rows in one half and the same 128 up rows in the other, so one epilogue thread holds both
+// halves of its GeGLU pair. Tensor memory (512 columns) holds two accumulator sets of 2 x 96
+// columns and two weight stages of 64 columns. Per K block:
 //   * warps 8-15 (one thread per weight row) fetch the row's 32 packed bytes through a private
 //     cp.async pipeline 6 blocks deep, dequantise them to fp16 w = q * scale + bias (the bf16
 //     scale/bias prefetched into registers two blocks ahead; w is exact in fp16 when the bias is
-//     a small multiple of the scale, as for zero-point-8 weights) and store the row in the
-//     128-byte swizzle layout the MMA reads;
+//     a small multiple of the scale, as for zero-point-8 weights) and store the row straight into
+//     its tensor-memory lane with tcgen05.st, so the weights never pass through shared memory;
 //   * warp 0 loads the activation tile by TMA, the fp16 high part and the fp16 low part
 //     (x - hi), so the MMAs against the same weights carry ~22 bits of the activation; it also
 //     prefetches the CTA's next tile of weights into L2;
-//   * one thread of warp 1 issues tcgen05.mma (kind::f16, M=128, N=16..128, K=16) for both halves
-//     and both activation parts into one of two TMEM accumulator sets, committing stage and tile
-//     completion to mbarriers;
+//   * one thread of warp 1 issues tcgen05.mma (kind::f16, M=128, N=16..96, K=16, A from tensor
+//     memory, B from shared memory) for both halves and both activation parts into one of the two
+//     accumulator sets, committing stage and tile completion to mbarriers;
 //   * warps 4-7 drain the other accumulator set with tcgen05.ld while the next tile runs.
 // Within every 8-element chunk of K the dequantised weights come out in the order
 // (0,4,1,5,2,6,3,7), the order the nibble extraction yields; activations are stored in the same
@@ -50,17 +51,20 @@ namespace tok {
 
 constexpr int D = 2816, FE = 704, FS = 2112, NE = 128, TOPK = 8, GD = D / kGroup;
 constexpr int BK = 64;                  // K block = one quantisation group
-constexpr int NT = 128;                 // tokens per tile (MMA N, at most)
-constexpr int SX = 3;                   // activation stages
-constexpr int SW = 2;                   // dequantised-weight stages
+constexpr int NT = 96;                  // tokens per tile (MMA N, at most)
+constexpr int SX = 4;                   // activation stages (shared memory)
+constexpr int SW = 2;                   // dequantised-weight stages (tensor memory)
+constexpr int NACC = 2;                 // accumulator sets (tensor memory, 2 x NT columns each)
+constexpr uint32_t ACC_SET = 2 * NT;    // one set: the two 128-row halves, NT token columns each
+constexpr uint32_t A_COL0 = NACC * ACC_SET;  // first TMEM column of the weight stages (64 columns each)
 constexpr int DR = 6;                   // packed-weight cp.async depth per dequant thread
 constexpr int THREADS = 512;
 constexpr int DQ0 = 256, DQ_THREADS = 256;   // dequant threads: warps 8..15, one weight row each
-constexpr uint32_t W_TILE = 256 * BK * 2;    // 32 KB fp16 weights (two 128-row halves)
-constexpr uint32_t X_TILE = NT * BK * 2;     // 16 KB per activation part
+constexpr uint32_t X_TILE = NT * BK * 2;     // 12 KB per activation part
 constexpr uint32_t XBOX = 32 * BK * 2;       // 4 KB: one TMA box of 32 token rows
 constexpr uint32_t RAW_TILE = 256 * 32;      // 8 KB packed int4 per K block
-constexpr size_t SMEM_BYTES = 1024 + SW * W_TILE + 2 * SX * X_TILE + DR * RAW_TILE + (2 * SX + 2 * SW + 4) * 8 + 16;
+constexpr size_t SMEM_BYTES = 1024 + 2 * SX * X_TILE + DR * RAW_TILE + (2 * SX + 2 * SW + 2 * NACC) * 8 + 16;
+static_assert(A_COL0 + SW * 64 <= 512, "tensor memory columns");
 constexpr int FB0_R = (FE + 127) / 128, FB0_S = (FS + 127) / 128;   // gate/up tiles: 128 intermediate rows
 constexpr int FB1 = D / 256;                                        // down tiles: 256 output rows
 constexpr uint64_t kWaitNs = 1000000000ull;
@@ -445,25 +449,24 @@ template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant__ GemmArgs A) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sW = base;                          // [SW][2][16 KB] fp16 weights, SW128, two 128-row halves
-    uint8_t* sXh = sW + SW * W_TILE;             // [SX][16 KB]    activation high parts, SW128
-    uint8_t* sXl = sXh + SX * X_TILE;            // [SX][16 KB]    activation low parts
+    uint8_t* sXh = base;                         // [SX][12 KB]    activation high parts, SW128
+    uint8_t* sXl = sXh + SX * X_TILE;            // [SX][12 KB]    activation low parts
     uint8_t* sRaw = sXl + SX * X_TILE;           // [DR][256][32]  packed int4, one row per dequant thread
     uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + DR * RAW_TILE);
     uint64_t* act_full = bars;
     uint64_t* act_empty = act_full + SX;
     uint64_t* w_full = act_empty + SX;
     uint64_t* w_empty = w_full + SW;
-    uint64_t* acc_full = w_empty + SW;       // [2]
-    uint64_t* acc_empty = acc_full + 2;      // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* acc_full = w_empty + SW;       // [NACC]
+    uint64_t* acc_empty = acc_full + NACC;   // [NACC]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NACC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < SX; ++s) { tc::mbar_init(&act_full[s], 1); tc::mbar_init(&act_empty[s], 1); }
         for (int s = 0; s < SW; ++s) { tc::mbar_init(&w_full[s], DQ_THREADS); tc::mbar_init(&w_empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], 128); }
+        for (int b = 0; b < NACC; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], 128); }
         *abort_flag = 0;
         tc::mbar_fence_init();
     }
@@ -518,53 +521,52 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                 tc::mbar_wait(&act_full[j % SX], (j / SX) & 1, &never, kWaitNs);
         }
     } else if (warp == 1) {
-        // ---- MMA issuer: per K step, both 128-row halves x (activation high, low) ----
-        if (lane == 0) {
-            uint32_t it = 0, acc_it = 0;
-            bool ok = true;
-            for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
-                const TileInfo ti = tile_info(A, i);
-                const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
-                if (!tc::mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag, kWaitNs)) break;
+        // ---- MMA issuer (the whole warp; one elected lane issues): per K step, both 128-row
+        //      halves x (activation high, low). Waits are warp-uniform so the warp stays converged.
+        uint32_t it = 0, acc_it = 0;
+        bool ok = true;
+        for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+            const TileInfo ti = tile_info(A, i);
+            const uint32_t ab = acc_it % NACC, aph = (acc_it / NACC) & 1;
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag, kWaitNs))) break;
+            tc::tc_fence_after();
+            const uint32_t d = tmem + ab * ACC_SET;
+            const uint32_t idesc = tc::idesc_f16(128, (uint32_t)((ti.t.rows + 15) & ~15));
+            for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+                const uint32_t sx = it % SX, phx = (it / SX) & 1, sw = it % SW, phw = (it / SW) & 1;
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_full[sw], phw, abort_flag, kWaitNs) &&
+                                                 tc::mbar_wait(&act_full[sx], phx, abort_flag, kWaitNs))) { ok = false; break; }
                 tc::tc_fence_after();
-                const uint32_t d = tmem + ab * 256;
-                const uint32_t idesc = tc::idesc_f16(128, (uint32_t)((ti.t.rows + 15) & ~15));
-                for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-                    const uint32_t sx = it % SX, phx = (it / SX) & 1, sw = it % SW, phw = (it / SW) & 1;
-                    if (!tc::mbar_wait(&w_full[sw], phw, abort_flag, kWaitNs) ||
-                        !tc::mbar_wait(&act_full[sx], phx, abort_flag, kWaitNs)) { ok = false; break; }
-                    tc::tc_fence_after();
-                    const uint64_t da0 = tc::sdesc_sw128(tc::smem_u32(sW + sw * W_TILE));
-                    const uint64_t da1 = tc::sdesc_sw128(tc::smem_u32(sW + sw * W_TILE + W_TILE / 2));
-                    const uint64_t dh = tc::sdesc_sw128(tc::smem_u32(sXh + sx * X_TILE));
-                    const uint64_t dl = tc::sdesc_sw128(tc::smem_u32(sXl + sx * X_TILE));
+                // weights in TMEM: half h of stage sw at columns A_COL0 + 64 sw + 32 h, 8 per K step
+                const uint32_t ta0 = tmem + A_COL0 + sw * 64, ta1 = ta0 + 32;
+                const uint64_t dh = tc::sdesc_sw128(tc::smem_u32(sXh + sx * X_TILE));
+                const uint64_t dl = tc::sdesc_sw128(tc::smem_u32(sXl + sx * X_TILE));
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        const uint32_t first = (kb > 0 || k > 0) ? 1u : 0u;
-                        tc::mma_f16(d, da0 + 2 * k, dh + 2 * k, idesc, first);
-                        tc::mma_f16(d + 128, da1 + 2 * k, dh + 2 * k, idesc, first);
-                        tc::mma_f16(d, da0 + 2 * k, dl + 2 * k, idesc, 1u);
-                        tc::mma_f16(d + 128, da1 + 2 * k, dl + 2 * k, idesc, 1u);
-                    }
-                    tc::mma_commit(&w_empty[sw]);
-                    tc::mma_commit(&act_empty[sx]);
+                for (int k = 0; k < BK / 16; ++k) {
+                    const uint32_t first = (kb > 0 || k > 0) ? 1u : 0u;
+                    tc::mma_f16_ts(d, ta0 + 8 * k, dh + 2 * k, idesc, first);
+                    tc::mma_f16_ts(d + NT, ta1 + 8 * k, dh + 2 * k, idesc, first);
+                    tc::mma_f16_ts(d, ta0 + 8 * k, dl + 2 * k, idesc, 1u);
+                    tc::mma_f16_ts(d + NT, ta1 + 8 * k, dl + 2 * k, idesc, 1u);
                 }
-                if (!ok) break;
-                tc::mma_commit(&acc_full[ab]);
-                ++acc_it;
+                tc::mma_commit(&w_empty[sw]);
+                tc::mma_commit(&act_empty[sx]);
             }
-            if (it > 0) {   // issued MMAs finish before TMEM is released
-                volatile int never = 0;
-                tc::mbar_wait(&w_empty[(it - 1) % SW], ((it - 1) / SW) & 1, &never, kWaitNs);
-            }
+            if (!ok) break;
+            tc::mma_commit(&acc_full[ab]);
+            ++acc_it;
+        }
+        if (it > 0) {   // issued MMAs finish before TMEM is released
+            volatile int never = 0;
+            tc::mbar_wait(&w_empty[(it - 1) % SW], ((it - 1) / SW) & 1, &never, kWaitNs);
         }
     } else if (warp >= 8) {
         // ---- dequant: one weight row per thread; its packed bytes come through a private
         //      cp.async pipeline DR blocks deep (no barrier: each thread reads only what it copied) ----
         const int r = tid - DQ0;                    // tile row 0..255
         const int hr = r >> 7, rr = r & 127;        // 128-row half, row within the half
-        const uint32_t wrow = (uint32_t)hr * (W_TILE / 2) + (uint32_t)(rr >> 3) * 1024u + (uint32_t)(rr & 7) * 128u;
-        const uint32_t swz = (uint32_t)(rr & 7);
+        // this thread's TMEM lane is rr (warp 8 + r/32 reaches lanes 32 (warp % 4) ..)
+        const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + A_COL0 + (uint32_t)hr * 32u;
         const uint32_t raw_row = tc::smem_u32(sRaw) + (uint32_t)r * 32u;
         const uint32_t rsw = (uint32_t)((r >> 2) & 1);   // 16-byte half swap: conflict-free 16-byte reads
         uint32_t it = 0;
@@ -608,15 +610,22 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                 const uint4 q0 = *reinterpret_cast<const uint4*>(src + (rsw << 4));
                 const uint4 q1 = *reinterpret_cast<const uint4*>(src + ((rsw ^ 1u) << 4));
                 const uint32_t sc = valid ? bf16_to_h2(sbits) : 0u, bi = valid ? bf16_to_h2(bbits) : 0u;
-                uint4 o[8];
-                o[0] = dq8(q0.x, sc, bi); o[1] = dq8(q0.y, sc, bi); o[2] = dq8(q0.z, sc, bi); o[3] = dq8(q0.w, sc, bi);
-                o[4] = dq8(q1.x, sc, bi); o[5] = dq8(q1.y, sc, bi); o[6] = dq8(q1.z, sc, bi); o[7] = dq8(q1.w, sc, bi);
+                uint32_t o[32];
+                *reinterpret_cast<uint4*>(&o[0]) = dq8(q0.x, sc, bi);
+                *reinterpret_cast<uint4*>(&o[4]) = dq8(q0.y, sc, bi);
+                *reinterpret_cast<uint4*>(&o[8]) = dq8(q0.z, sc, bi);
+                *reinterpret_cast<uint4*>(&o[12]) = dq8(q0.w, sc, bi);
+                *reinterpret_cast<uint4*>(&o[16]) = dq8(q1.x, sc, bi);
+                *reinterpret_cast<uint4*>(&o[20]) = dq8(q1.y, sc, bi);
+                *reinterpret_cast<uint4*>(&o[24]) = dq8(q1.z, sc, bi);
+                *reinterpret_cast<uint4*>(&o[28]) = dq8(q1.w, sc, bi);
                 const uint32_t sw = it % SW, phw = (it / SW) & 1;
-                if (!tc::mbar_wait(&w_empty[sw], phw ^ 1, abort_flag, kWaitNs)) return false;
-                uint8_t* wt = sW + sw * W_TILE + wrow;
-#pragma unroll
-                for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wt + (((uint32_t)c ^ swz) << 4)) = o[c];
-                tc::fence_proxy_async_smem();
+                // warp-uniform outcome: tcgen05.st is warp-collective
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_empty[sw], phw ^ 1, abort_flag, kWaitNs))) return false;
+                tc::tc_fence_after();
+                tc::tmem_st32(tlane + sw * 64, o);
+                tc::tmem_st_wait();
+                tc::tc_fence_before();
                 tc::mbar_arrive(&w_full[sw]);
                 ++it;
                 return true;
@@ -637,11 +646,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
         uint32_t acc_it = 0;
         for (int i = blockIdx.x; i < ntiles; i += gridDim.x) {
             const TileInfo ti = tile_info(A, i);
-            const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+            const uint32_t ab = acc_it % NACC, aph = (acc_it / NACC) & 1;
             // warp-uniform outcome: tcgen05.ld is warp-collective
             if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[ab], aph, abort_flag, kWaitNs))) break;
             tc::tc_fence_after();
-            const uint32_t taddr = tmem + ab * 256 + ((uint32_t)(32 * q) << 16);
+            const uint32_t taddr = tmem + ab * ACC_SET + ((uint32_t)(32 * q) << 16);
             const int rows = ti.t.rows, row0 = ti.t.row0;
             if (MODE == 1) {
                 // accumulator a holds output rows fb*256 + 128a + (32q + lane)
@@ -652,7 +661,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                     const float wl = ti.routed && tl < rows ? A.perm_w[row0 + tl] : 1.0f;
                     uint32_t v0[16], v1[16];
                     tc::tmem_ld16_sync(taddr + c0, v0);
-                    tc::tmem_ld16_sync(taddr + 128 + c0, v1);
+                    tc::tmem_ld16_sync(taddr + NT + c0, v1);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int t = c0 + j;
@@ -676,7 +685,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                 for (int c0 = 0; c0 < rows; c0 += 16) {
                     uint32_t g[16], u[16];
                     tc::tmem_ld16_sync(taddr + c0, g);
-                    tc::tmem_ld16_sync(taddr + 128 + c0, u);
+                    tc::tmem_ld16_sync(taddr + NT + c0, u);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int t = c0 + j;
