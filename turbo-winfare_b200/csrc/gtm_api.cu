@@ -265,14 +265,17 @@ static int check_layer(const char* fn, const GtmLayer& L) {
         return set_error(GTM_ERR_INVALID, "%s: null base or zero expert stride", fn);
     if (!aligned(L.resident_dev, 16) || !aligned(L.experts_dev, 16))
         return set_error(GTM_ERR_MISALIGNED, "%s: base pointers must be 16-byte aligned", fn);
+    // packed weights load by TMA and the expert/shared scale and bias rows by bulk copy: both want
+    // 16-byte aligned sources
     const uint64_t offs16[] = {L.router.weight, L.expert_stride, L.expert_gate.weight, L.expert_up.weight,
-                               L.expert_down.weight, L.shared_gate.weight, L.shared_up.weight, L.shared_down.weight};
+                               L.expert_down.weight, L.shared_gate.weight, L.shared_up.weight, L.shared_down.weight,
+                               L.shared_gate.scales, L.shared_gate.biases, L.shared_up.scales, L.shared_up.biases,
+                               L.shared_down.scales, L.shared_down.biases, L.expert_gate.scales, L.expert_gate.biases,
+                               L.expert_up.scales, L.expert_up.biases, L.expert_down.scales, L.expert_down.biases};
     for (uint64_t o : offs16)
-        if (o % 16) return set_error(GTM_ERR_MISALIGNED, "%s: weight offset %llu not 16-byte aligned", fn, (unsigned long long)o);
+        if (o % 16) return set_error(GTM_ERR_MISALIGNED, "%s: weight/scale/bias offset %llu not 16-byte aligned", fn,
+                                     (unsigned long long)o);
     const uint64_t offs2[] = {L.router.scales, L.router.biases, L.router_scale, L.per_expert_scale,
-                              L.shared_gate.scales, L.shared_gate.biases, L.shared_up.scales, L.shared_up.biases,
-                              L.shared_down.scales, L.shared_down.biases, L.expert_gate.scales, L.expert_gate.biases,
-                              L.expert_up.scales, L.expert_up.biases, L.expert_down.scales, L.expert_down.biases,
                               L.pre_ffn_norm, L.pre_ffn_norm_2, L.post_ffn_norm_1, L.post_ffn_norm_2,
                               L.post_ffn_norm, L.layer_scalar};
     for (uint64_t o : offs2)

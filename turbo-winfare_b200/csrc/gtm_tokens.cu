@@ -14,23 +14,27 @@
 //   6. tok_combine        h2 = sum over the 8 slots in router order, shared output, layer tail
 //
 // Grouped GEMM: one CTA per SM, persistent over a tile list built on the device. A tile is 256
-// weight rows (two MMA M=128 halves) by up to 96 tokens of one expert (MMA N), over K in blocks of
-// 64 (one quantisation group): D[row][token] += W[row][k] X[token][k]. Gate/up tiles put 128 gate
-// rows in one half and the same 128 up rows in the other, so one epilogue thread holds both
-// halves of its GeGLU pair. Tensor memory (512 columns) holds two accumulator sets of 2 x 96
-// columns and two weight stages of 64 columns. Per K block:
-//   * warps 8-15 (one thread per weight row) fetch the row's 32 packed bytes through a private
-//     cp.async pipeline 6 blocks deep, dequantise them to fp16 w = q * scale + bias (the bf16
-//     scale/bias prefetched into registers two blocks ahead; w is exact in fp16 when the bias is
-//     a small multiple of the scale, as for zero-point-8 weights) and store the row straight into
-//     its tensor-memory lane with tcgen05.st, so the weights never pass through shared memory;
-//   * warp 0 loads the activation tile by TMA, the fp16 high part and the fp16 low part
-//     (x - hi), so the MMAs against the same weights carry ~22 bits of the activation; it also
-//     prefetches the CTA's next tile of weights into L2;
-//   * one thread of warp 1 issues tcgen05.mma (kind::f16, M=128, N=16..96, K=16, A from tensor
-//     memory, B from shared memory) for both halves and both activation parts into one of the two
-//     accumulator sets, committing stage and tile completion to mbarriers;
-//   * warps 4-7 drain the other accumulator set with tcgen05.ld while the next tile runs.
+// weight rows (two M=128 row blocks, one tensor-memory lane per row) by up to 128 tokens of one
+// expert (MMA N), over K in blocks of 64 (one quantisation group): D[row][token] += W[row][k]
+// X[token][k]. Both row blocks share each activation stage, which halves the activation bytes per
+// MMA against 128-row tiles: at 128 tokens the activation (high + low part) is 32 KB per K block,
+// and streaming it per 128 weight rows would need about the whole L2-to-SM bandwidth of an SM. A
+// gate/up tile holds 128 features (row block b: features 64b..64b+63; in each 32-lane quarter,
+// lanes 0-15 the gate rows and lanes 16-31 the up rows of the same 16 features, so GeGLU needs
+// one shuffle). Tensor memory (512 columns): the two accumulators (128 columns each) and four
+// weight stages of 2 x 32 columns. On B200 a 128 x N x 16 MMA costs ~62 cycles for any N up to
+// ~128 (measured), so N = 128 is the narrowest tile that keeps the tensor pipe busy. Warp roles:
+//   * warp 0 loads the activation tile by TMA per K block, the fp16 high part and the fp16 low
+//     part (x - hi), so the MMAs against the same weights carry ~22 bits of the activation;
+//   * warp 2 loads the tile's 256 packed int4 rows per K block by TMA (rows of 32 bytes, 32-byte
+//     swizzle);
+//   * warps 12-19, one thread per weight row, dequantise to fp16 w = q * scale + bias (exact in
+//     fp16 when the bias is a small multiple of the scale, as for zero-point-8 weights) and store
+//     the block straight into the row's tensor-memory lane;
+//   * warp 1 issues tcgen05.mma (kind::f16, M=128, N=16..128, K=16, A from tensor memory, B from
+//     shared memory) with the whole warp converged and one elected lane issuing;
+//   * warps 4-11 (two per lane quarter, alternate 16-token chunks) drain row block 0 and release
+//     it, then row block 1, so the next tile's first MMAs overlap the second half of the drain.
 // Within every 8-element chunk of K the dequantised weights come out in the order
 // (0,4,1,5,2,6,3,7), the order the nibble extraction yields; activations are stored in the same
 // order, so the products are unchanged and no permute instructions are spent.
@@ -51,27 +55,30 @@ namespace tok {
 
 constexpr int D = 2816, FE = 704, FS = 2112, NE = 128, TOPK = 8, GD = D / kGroup;
 constexpr int BK = 64;                  // K block = one quantisation group
-constexpr int NT = 96;                  // tokens per tile (MMA N, at most)
-constexpr int SX = 4;                   // activation stages (shared memory)
-constexpr int SW = 2;                   // dequantised-weight stages (tensor memory)
-constexpr int NACC = 2;                 // accumulator sets (tensor memory, 2 x NT columns each)
-constexpr uint32_t ACC_SET = 2 * NT;    // one set: the two 128-row halves, NT token columns each
-constexpr uint32_t A_COL0 = NACC * ACC_SET;  // first TMEM column of the weight stages (64 columns each)
-constexpr int DR = 6;                   // packed-weight cp.async depth per dequant thread
-constexpr int THREADS = 512;
-constexpr int DQ0 = 256, DQ_THREADS = 256;   // dequant threads: warps 8..15, one weight row each
-constexpr uint32_t X_TILE = NT * BK * 2;     // 12 KB per activation part
-constexpr uint32_t XBOX = 32 * BK * 2;       // 4 KB: one TMA box of 32 token rows
-constexpr uint32_t RAW_TILE = 256 * 32;      // 8 KB packed int4 per K block
-constexpr size_t SMEM_BYTES = 1024 + 2 * SX * X_TILE + DR * RAW_TILE + (2 * SX + 2 * SW + 2 * NACC) * 8 + 16;
+constexpr int MW = 256;                 // weight rows per tile: two M=128 row blocks
+constexpr int NT = 128;                 // tokens per tile (MMA N, at most)
+constexpr int SX = 6;                   // activation stages (shared memory, high + low part each)
+constexpr int RS = 4;                   // packed-weight stages (shared memory)
+constexpr int SW = 4;                   // dequantised-weight stages (tensor memory, 2 x 32 columns each)
+constexpr uint32_t A_COL0 = 2 * NT;     // accumulators: row block b at columns b * NT; weights after
+constexpr int THREADS = 640;            // 20 warps; roles in grouped_gemm
+constexpr int EPI0 = 128, EPI_THREADS = 256;  // epilogue: warps 4..11, two per tensor-memory lane quarter
+constexpr int DQ0 = 384, DQ_THREADS = 256;    // dequant: warps 12..19, one thread per weight row
+constexpr uint32_t X_TILE = NT * BK * 2;      // 16 KB per activation part
+constexpr uint32_t XBOX = 32 * BK * 2;        // 4 KB: one TMA box of 32 token rows
+// TMA moves a few large boxes faster than many small ones (~64 cycles a box on top of the bytes,
+// measured): tiles of more than 64 tokens load each activation part as one 128-row box.
+constexpr int XWIDE_MIN = 65;
+constexpr uint32_t RAW_TILE = MW * BK / 2;    // 8 KB packed int4 per K block, rows of 32 bytes
+constexpr size_t SMEM_BYTES = 1024 + 2 * SX * X_TILE + RS * RAW_TILE + (2 * SX + 2 * RS + 2 * SW + 3) * 8 + 16;
 static_assert(A_COL0 + SW * 64 <= 512, "tensor memory columns");
-constexpr int FB0_R = (FE + 127) / 128, FB0_S = (FS + 127) / 128;   // gate/up tiles: 128 intermediate rows
-constexpr int FB1 = D / 256;                                        // down tiles: 256 output rows
+constexpr int FB0_R = (FE + 127) / 128, FB0_S = (FS + 127) / 128;   // gate/up tiles: 128 features (gate + up)
+constexpr int FB1 = D / MW;                                         // down tiles: 256 output rows
 constexpr uint64_t kWaitNs = 1000000000ull;
 constexpr int RIN_PITCH = 65;
 
 static_assert(SMEM_BYTES <= 232448, "grouped GEMM shared memory");
-static_assert(FE % 64 == 0 && FS % 64 == 0 && D % 256 == 0, "tile shapes");
+static_assert(FE % 64 == 0 && FS % 64 == 0 && D % MW == 0, "tile shapes");
 
 struct Tile {
     int32_t expert;   // routed expert id, or -1 for the shared expert
@@ -217,12 +224,10 @@ struct RouteArgs {
     int n;                   // routed entries (0: shared tiles only)
     int src_div;             // activation source row of entry i = i / src_div
     const uint32_t* idx;     // expert id of entry i at idx[i * stride]
-    const float* w;          // routing weight of entry i at w[i * stride]
     int stride;
     int e0, ne;              // experts of this launch: [e0, e0 + ne); tiles carry e - e0
     int t_shared;            // tokens of the shared-expert tiles (0: none)
     int* perm_src;           // [n] source row of each expert-ordered row
-    float* perm_w;           // [n] routing weight of each row
     int* pos;                // [n] expert-ordered row of each entry
     Tile* tiles0;            // gate/up tiles
     Tile* tiles1;            // down tiles
@@ -256,7 +261,6 @@ __global__ void __launch_bounds__(1024) tok_route(const __grid_constant__ RouteA
         const int row = off[(int)A.idx[(size_t)i * A.stride] - A.e0] + A.pos[i];
         A.pos[i] = row;
         A.perm_src[row] = i / A.src_div;
-        A.perm_w[row] = A.w[(size_t)i * A.stride];
     }
     // tiles of one (expert, row block) are adjacent over the token ranges, for L2 reuse of the weights
     for (int e = tid; e < A.ne; e += blockDim.x) {
@@ -377,20 +381,23 @@ __global__ void __launch_bounds__(128) tok_gather(const float* routed, const int
 // 4/5. grouped GEMM
 // ================================================================================================
 struct GemmArgs {
-    CUtensorMap x_rhi, x_rlo, x_shi, x_slo;   // activations, 2D fp16, 32-row boxes
+    CUtensorMap x_rhi, x_rlo, x_shi, x_slo;   // activations: 2D fp16, 32-row boxes, 128-byte swizzle
+    CUtensorMap y_rhi, y_rlo, y_shi, y_slo;   // the same tensors in 128-row boxes (tiles of > 64 tokens)
+    CUtensorMap w_ra, w_rb, w_sa, w_sb;       // packed int4 weights (matrix a, b): routed 3D (byte, row,
+                                              // expert), shared 2D; rows of 32 bytes, 32-byte swizzle
     const Tile* tiles;
     const int* n_tiles;
     const uint8_t* experts;
     uint64_t expert_stride;
-    uint64_t r_wa, r_wb, r_sa, r_ba, r_sb, r_bb;   // routed weight / scale / bias byte offsets (matrix a, b)
+    uint64_t r_sa, r_ba, r_sb, r_bb;      // routed scale / bias byte offsets (matrix a, b)
     const uint8_t* resident;
-    uint64_t s_wa, s_wb, s_sa, s_ba, s_sb, s_bb;   // shared
+    uint64_t s_sa, s_ba, s_sb, s_bb;      // shared
     int k_r, k_s;                         // K of the routed / shared matrices
-    int rows_r, rows_s;                   // rows of each routed / shared matrix
+    int rows_r, rows_s;                   // rows of each routed / shared matrix (mode 0: features)
+    int wide_r, wide_s;                   // the 128-row box maps exist (the tensor has >= 128 rows)
     __half* act_r_hi; __half* act_r_lo;   // mode 0 outputs, rows of FE (routed) / FS (shared)
     __half* act_s_hi; __half* act_s_lo;
     float* out_r; float* out_s;           // mode 1 outputs [rows][D]
-    const float* perm_w;                  // mode 1: routing weight per routed row
     const int* out_index;                 // mode 1: output row of each routed row (null: same row)
     int* err;
 };
@@ -420,17 +427,6 @@ __device__ __forceinline__ uint32_t bf16_to_h2(uint16_t b) {
     return u | (u << 16);
 }
 
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
-
 struct TileInfo {
     Tile t;
     bool routed;
@@ -445,28 +441,60 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& A, int i) {
     return ti;
 }
 
+// x * 0.5 * (1 + tanh(u)) written as x / (1 + exp(-2u)), u = sqrt(2/pi) (x + 0.044715 x^3): the
+// same function as gelu_pytorch_tanh (cpu_reference.cpp:34-38), evaluated with one exponential.
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+    const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+    return __fdividef(x, 1.0f + __expf(-2.0f * u));
+}
+
+// a = hi + lo with hi, lo fp16 (~22 significant bits together), returned as one fp16x2 word (lo in
+// the low half), for |a| inside the fp16 range. hi is a rounded to 11 significant bits by
+// Veltkamp splitting in fp32 (exact in fp16 for |a| >= 2^-14; below that the fp16 conversion
+// rounds it again, an absolute error under 2^-25), lo = a - hi is exact in fp32; one packed
+// conversion then produces both halves.
+__device__ __forceinline__ uint32_t split_hi_lo(float a) {
+    const float c = __fmul_rn(a, 8193.0f);   // 2^13 + 1: keeps 24 - 13 = 11 bits
+    const float hi = __fsub_rn(c, __fsub_rn(c, a));
+    const float lo = __fsub_rn(a, hi);
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Gate/up tile of 128 features f0 .. f0+127: row block b holds features f0 + 64b + (0..63); in
+// each 32-lane quarter q, lanes 0-15 are the gate rows and lanes 16-31 the up rows of features
+// f0 + 64b + 16q + (0..15), so GeGLU needs one shuffle. Packed rows sit in shared memory as the
+// 128 gate rows, then the 128 up rows.
+__device__ __forceinline__ int gu_feature(int b, int q, int lane) { return 64 * b + 16 * q + (lane & 15); }
+
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant__ GemmArgs A) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sXh = base;                         // [SX][12 KB]    activation high parts, SW128
-    uint8_t* sXl = sXh + SX * X_TILE;            // [SX][12 KB]    activation low parts
-    uint8_t* sRaw = sXl + SX * X_TILE;           // [DR][256][32]  packed int4, one row per dequant thread
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + DR * RAW_TILE);
-    uint64_t* act_full = bars;
-    uint64_t* act_empty = act_full + SX;
-    uint64_t* w_full = act_empty + SX;
-    uint64_t* w_empty = w_full + SW;
-    uint64_t* acc_full = w_empty + SW;       // [NACC]
-    uint64_t* acc_empty = acc_full + NACC;   // [NACC]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NACC);
+    uint8_t* sXh = base;                         // [SX][16 KB]   activation high parts, 128-byte swizzle
+    uint8_t* sXl = sXh + SX * X_TILE;            // [SX][16 KB]   activation low parts
+    uint8_t* sRaw = sXl + SX * X_TILE;           // [RS][256][32] packed int4 rows, 32-byte swizzle
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + RS * RAW_TILE);
+    uint64_t* act_full = bars;                   // [SX]
+    uint64_t* act_empty = act_full + SX;         // [SX]
+    uint64_t* raw_full = act_empty + SX;         // [RS]
+    uint64_t* raw_empty = raw_full + RS;         // [RS]
+    uint64_t* w_full = raw_empty + RS;           // [SW]
+    uint64_t* w_empty = w_full + SW;             // [SW]
+    uint64_t* acc_full = w_empty + SW;           // [1]
+    uint64_t* acc_empty = acc_full + 1;          // [2] one per row block
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < SX; ++s) { tc::mbar_init(&act_full[s], 1); tc::mbar_init(&act_empty[s], 1); }
+        for (int s = 0; s < RS; ++s) { tc::mbar_init(&raw_full[s], 1); tc::mbar_init(&raw_empty[s], DQ_THREADS); }
         for (int s = 0; s < SW; ++s) { tc::mbar_init(&w_full[s], DQ_THREADS); tc::mbar_init(&w_empty[s], 1); }
-        for (int b = 0; b < NACC; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], 128); }
+        tc::mbar_init(&acc_full[0], 1);
+        tc::mbar_init(&acc_empty[0], EPI_THREADS);
+        tc::mbar_init(&acc_empty[1], EPI_THREADS);
         *abort_flag = 0;
         tc::mbar_fence_init();
     }
@@ -478,37 +506,21 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
     const int ntiles = *A.n_tiles;
 
     if (warp == 0) {
-        // ---- activation producer; L2 prefetch of the next tile's weights ----
+        // ---- activation producer: per K block the tile's token rows, high and low part ----
         if (lane == 0) {
-            auto prefetch_tile = [&](int i2) {
-                const TileInfo tn = tile_info(A, i2);
-                const uint8_t* wb = tn.routed ? A.experts + (uint64_t)tn.t.expert * A.expert_stride : A.resident;
-                const uint64_t K = (uint64_t)tn.nkb * BK, G = tn.nkb;
-                const uint64_t nr = tn.routed ? A.rows_r : A.rows_s;
-                const uint64_t span = MODE == 0 ? 128 : 256, j0 = (uint64_t)tn.t.fb * span;
-                const uint64_t rows = j0 + span <= nr ? span : nr - j0;
-                for (int mtx = 0; mtx < (MODE == 0 ? 2 : 1); ++mtx) {
-                    const uint64_t wo = tn.routed ? (mtx ? A.r_wb : A.r_wa) : (mtx ? A.s_wb : A.s_wa);
-                    const uint64_t so = tn.routed ? (mtx ? A.r_sb : A.r_sa) : (mtx ? A.s_sb : A.s_sa);
-                    const uint64_t bo = tn.routed ? (mtx ? A.r_bb : A.r_ba) : (mtx ? A.s_bb : A.s_ba);
-                    tc::prefetch_l2_bulk(wb + wo + j0 * (K / 2), rows * (K / 2));
-                    tc::prefetch_l2_bulk(wb + so + j0 * G * 2, rows * G * 2);
-                    tc::prefetch_l2_bulk(wb + bo + j0 * G * 2, rows * G * 2);
-                }
-            };
-            if ((int)blockIdx.x < ntiles) prefetch_tile(blockIdx.x);
             uint32_t it = 0;
             bool ok = true;
             for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
-                if (i + (int)gridDim.x < ntiles) prefetch_tile(i + gridDim.x);
                 const TileInfo ti = tile_info(A, i);
-                const CUtensorMap* mh = ti.routed ? &A.x_rhi : &A.x_shi;
-                const CUtensorMap* ml = ti.routed ? &A.x_rlo : &A.x_slo;
-                const int nbox = (ti.t.rows + 31) >> 5;
+                const bool wide = ti.t.rows >= XWIDE_MIN && (ti.routed ? A.wide_r : A.wide_s);
+                const CUtensorMap* mh = wide ? (ti.routed ? &A.y_rhi : &A.y_shi) : (ti.routed ? &A.x_rhi : &A.x_shi);
+                const CUtensorMap* ml = wide ? (ti.routed ? &A.y_rlo : &A.y_slo) : (ti.routed ? &A.x_rlo : &A.x_slo);
+                const int nbox = wide ? 1 : (ti.t.rows + 31) >> 5;
+                const uint32_t box_bytes = wide ? X_TILE : XBOX;
                 for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
                     const uint32_t s = it % SX, ph = (it / SX) & 1;
                     if (!tc::mbar_wait(&act_empty[s], ph ^ 1, abort_flag, kWaitNs)) { ok = false; break; }
-                    tc::mbar_arrive_expect_tx(&act_full[s], 2u * XBOX * (uint32_t)nbox);
+                    tc::mbar_arrive_expect_tx(&act_full[s], 2u * box_bytes * (uint32_t)nbox);
                     for (int j = 0; j < nbox; ++j) {
                         tc::tma_load_2d(sXh + s * X_TILE + j * XBOX, mh, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
                         tc::tma_load_2d(sXl + s * X_TILE + j * XBOX, ml, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
@@ -520,95 +532,118 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
             for (uint32_t j = it > SX ? it - SX : 0; j < it; ++j)
                 tc::mbar_wait(&act_full[j % SX], (j / SX) & 1, &never, kWaitNs);
         }
+    } else if (warp == 2) {
+        // ---- weight producer: per K block the tile's 256 packed rows (TMA, 32 bytes a row) ----
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+                const TileInfo ti = tile_info(A, i);
+                for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+                    const uint32_t s = it % RS, ph = (it / RS) & 1;
+                    if (!tc::mbar_wait(&raw_empty[s], ph ^ 1, abort_flag, kWaitNs)) { ok = false; break; }
+                    tc::mbar_arrive_expect_tx(&raw_full[s], RAW_TILE);
+                    uint8_t* dst = sRaw + s * RAW_TILE;
+                    if (MODE == 0) {   // 128 gate rows then 128 up rows (rows past the matrix read as 0)
+                        if (ti.routed) {
+                            tc::tma_load_3d(dst, &A.w_ra, kb * 32, ti.t.fb * 128, ti.t.expert, &raw_full[s]);
+                            tc::tma_load_3d(dst + RAW_TILE / 2, &A.w_rb, kb * 32, ti.t.fb * 128, ti.t.expert, &raw_full[s]);
+                        } else {
+                            tc::tma_load_2d(dst, &A.w_sa, kb * 32, ti.t.fb * 128, &raw_full[s]);
+                            tc::tma_load_2d(dst + RAW_TILE / 2, &A.w_sb, kb * 32, ti.t.fb * 128, &raw_full[s]);
+                        }
+                    } else {
+                        if (ti.routed) tc::tma_load_3d(dst, &A.w_ra, kb * 32, ti.t.fb * MW, ti.t.expert, &raw_full[s]);
+                        else tc::tma_load_2d(dst, &A.w_sa, kb * 32, ti.t.fb * MW, &raw_full[s]);
+                    }
+                }
+            }
+            volatile int never = 0;
+            for (uint32_t j = it > RS ? it - RS : 0; j < it; ++j)
+                tc::mbar_wait(&raw_full[j % RS], (j / RS) & 1, &never, kWaitNs);
+        }
     } else if (warp == 1) {
-        // ---- MMA issuer (the whole warp; one elected lane issues): per K step, both 128-row
-        //      halves x (activation high, low). Waits are warp-uniform so the warp stays converged.
+        // ---- MMA issuer (the whole warp; one elected lane issues). Per K step and row block:
+        //      weights (A, tensor memory) x activation high part, then x low part (B, shared
+        //      memory). Row block 1 of the last gate/up tile lies past the matrix: skipped. ----
         uint32_t it = 0, acc_it = 0;
         bool ok = true;
-        for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+        for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x, ++acc_it) {
             const TileInfo ti = tile_info(A, i);
-            const uint32_t ab = acc_it % NACC, aph = (acc_it / NACC) & 1;
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag, kWaitNs))) break;
-            tc::tc_fence_after();
-            const uint32_t d = tmem + ab * ACC_SET;
+            const int kout = ti.routed ? A.rows_r : A.rows_s;
+            const bool rb1 = MODE == 1 || ti.t.fb * 128 + 64 < kout;
             const uint32_t idesc = tc::idesc_f16(128, (uint32_t)((ti.t.rows + 15) & ~15));
+            const uint32_t eph = (acc_it & 1) ^ 1;
             for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
                 const uint32_t sx = it % SX, phx = (it / SX) & 1, sw = it % SW, phw = (it / SW) & 1;
                 if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_full[sw], phw, abort_flag, kWaitNs) &&
                                                  tc::mbar_wait(&act_full[sx], phx, abort_flag, kWaitNs))) { ok = false; break; }
                 tc::tc_fence_after();
-                // weights in TMEM: half h of stage sw at columns A_COL0 + 64 sw + 32 h, 8 per K step
-                const uint32_t ta0 = tmem + A_COL0 + sw * 64, ta1 = ta0 + 32;
                 const uint64_t dh = tc::sdesc_sw128(tc::smem_u32(sXh + sx * X_TILE));
                 const uint64_t dl = tc::sdesc_sw128(tc::smem_u32(sXl + sx * X_TILE));
+                for (int b = 0; b < 2; ++b) {
+                    if (kb == 0) {   // the epilogue has drained this row block's accumulator
+                        if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_empty[b], eph, abort_flag, kWaitNs))) { ok = false; break; }
+                        tc::tc_fence_after();
+                    }
+                    if (b == 1 && !rb1) break;
+                    const uint32_t d = tmem + (uint32_t)b * NT;
+                    const uint32_t wa = tmem + A_COL0 + sw * 64 + (uint32_t)b * 32;   // 8 columns per K step
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k) {
-                    const uint32_t first = (kb > 0 || k > 0) ? 1u : 0u;
-                    tc::mma_f16_ts(d, ta0 + 8 * k, dh + 2 * k, idesc, first);
-                    tc::mma_f16_ts(d + NT, ta1 + 8 * k, dh + 2 * k, idesc, first);
-                    tc::mma_f16_ts(d, ta0 + 8 * k, dl + 2 * k, idesc, 1u);
-                    tc::mma_f16_ts(d + NT, ta1 + 8 * k, dl + 2 * k, idesc, 1u);
+                    for (int k = 0; k < BK / 16; ++k) {
+                        tc::mma_f16_ts(d, wa + 8 * k, dh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        tc::mma_f16_ts(d, wa + 8 * k, dl + 2 * k, idesc, 1u);
+                    }
                 }
+                if (!ok) break;
                 tc::mma_commit(&w_empty[sw]);
                 tc::mma_commit(&act_empty[sx]);
             }
             if (!ok) break;
-            tc::mma_commit(&acc_full[ab]);
-            ++acc_it;
+            tc::mma_commit(&acc_full[0]);
         }
-        if (it > 0) {   // issued MMAs finish before TMEM is released
+        if (it > 0) {   // issued MMAs finish before tensor memory is released
             volatile int never = 0;
             tc::mbar_wait(&w_empty[(it - 1) % SW], ((it - 1) / SW) & 1, &never, kWaitNs);
         }
-    } else if (warp >= 8) {
-        // ---- dequant: one weight row per thread; its packed bytes come through a private
-        //      cp.async pipeline DR blocks deep (no barrier: each thread reads only what it copied) ----
-        const int r = tid - DQ0;                    // tile row 0..255
-        const int hr = r >> 7, rr = r & 127;        // 128-row half, row within the half
-        // this thread's TMEM lane is rr (warp 8 + r/32 reaches lanes 32 (warp % 4) ..)
-        const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + A_COL0 + (uint32_t)hr * 32u;
-        const uint32_t raw_row = tc::smem_u32(sRaw) + (uint32_t)r * 32u;
-        const uint32_t rsw = (uint32_t)((r >> 2) & 1);   // 16-byte half swap: conflict-free 16-byte reads
+    } else if (warp >= DQ0 / 32) {
+        // ---- dequant: one thread per weight row (row block b = warps 12-15 / 16-19, lane quarter
+        //      warp % 4); packed bytes from the TMA stage, bf16 scale/bias loaded two blocks ahead,
+        //      the block's 64 fp16 weights stored into the row's tensor-memory lane ----
+        const int q = warp & 3, b = (warp - DQ0 / 32) >> 2;
+        const int L = 32 * q + lane;                                   // tensor-memory lane
+        const int srow = MODE == 0 ? (lane >> 4) * 128 + gu_feature(b, q, lane) : 128 * b + L;
+        const uint32_t sw_bit = (uint32_t)((srow >> 2) & 1);           // 32-byte swizzle: 16-byte halves swap
+        const uint32_t raw_c0 = (uint32_t)srow * 32u + (sw_bit << 4), raw_c1 = (uint32_t)srow * 32u + ((sw_bit ^ 1u) << 4);
+        const uint32_t tl_addr = tmem + ((uint32_t)(32 * q) << 16) + A_COL0 + 32u * (uint32_t)b;
         uint32_t it = 0;
         bool ok = true;
         for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
             const TileInfo ti = tile_info(A, i);
-            const uint8_t* wb = ti.routed ? A.experts + (uint64_t)ti.t.expert * A.expert_stride : A.resident;
             const int G = ti.nkb;
-            const int nrows = ti.routed ? A.rows_r : A.rows_s;
-            int row;
-            uint64_t wo, so, bo;
+            const uint8_t* wb = ti.routed ? A.experts + (uint64_t)ti.t.expert * A.expert_stride : A.resident;
+            int grow, nrows;
+            uint64_t so, bo;
             if (MODE == 0) {
-                row = ti.t.fb * 128 + rr;
-                wo = ti.routed ? (hr ? A.r_wb : A.r_wa) : (hr ? A.s_wb : A.s_wa);
-                so = ti.routed ? (hr ? A.r_sb : A.r_sa) : (hr ? A.s_sb : A.s_sa);
-                bo = ti.routed ? (hr ? A.r_bb : A.r_ba) : (hr ? A.s_bb : A.s_ba);
+                const bool up = lane >= 16;
+                grow = ti.t.fb * 128 + gu_feature(b, q, lane);
+                nrows = ti.routed ? A.rows_r : A.rows_s;
+                so = ti.routed ? (up ? A.r_sb : A.r_sa) : (up ? A.s_sb : A.s_sa);
+                bo = ti.routed ? (up ? A.r_bb : A.r_ba) : (up ? A.s_bb : A.s_ba);
             } else {
-                row = ti.t.fb * 256 + r;
-                wo = ti.routed ? A.r_wa : A.s_wa;
+                grow = ti.t.fb * MW + 128 * b + L;
+                nrows = D;
                 so = ti.routed ? A.r_sa : A.s_sa;
                 bo = ti.routed ? A.r_ba : A.s_ba;
             }
-            const bool valid = row < nrows;   // rows past the matrix (last gate/up block) dequantise to 0
-            const uint8_t* wsrc = wb + wo + (uint64_t)(valid ? row : 0) * (uint64_t)(G * 32);
-            const uint16_t* sp = reinterpret_cast<const uint16_t*>(wb + so) + (size_t)(valid ? row : 0) * G;
-            const uint16_t* bp = reinterpret_cast<const uint16_t*>(wb + bo) + (size_t)(valid ? row : 0) * G;
-            auto issue = [&](int kb) {
-                if (valid && kb < G) {
-                    const uint32_t dst = raw_row + (uint32_t)(kb % DR) * RAW_TILE;
-                    cp_async16(dst + (rsw << 4), wsrc + kb * 32);
-                    cp_async16(dst + ((rsw ^ 1u) << 4), wsrc + kb * 32 + 16);
-                }
-                cp_async_commit();
-            };
-#pragma unroll
-            for (int k = 0; k < DR - 1; ++k) issue(k);
+            const bool valid = grow < nrows;   // rows past the matrix dequantise to 0
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(wb + so) + (size_t)(valid ? grow : 0) * G;
+            const uint16_t* bp = reinterpret_cast<const uint16_t*>(wb + bo) + (size_t)(valid ? grow : 0) * G;
             auto step = [&](int kb, uint16_t sbits, uint16_t bbits) -> bool {
-                issue(kb + DR - 1);
-                cp_async_wait<DR - 1>();
-                const uint8_t* src = sRaw + (uint32_t)(kb % DR) * RAW_TILE + r * 32;
-                const uint4 q0 = *reinterpret_cast<const uint4*>(src + (rsw << 4));
-                const uint4 q1 = *reinterpret_cast<const uint4*>(src + ((rsw ^ 1u) << 4));
+                const uint32_t rs = it % RS, rph = (it / RS) & 1, sw = it % SW, wph = (it / SW) & 1;
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&raw_full[rs], rph, abort_flag, kWaitNs))) return false;
+                const uint4 q0 = *reinterpret_cast<const uint4*>(sRaw + rs * RAW_TILE + raw_c0);
+                const uint4 q1 = *reinterpret_cast<const uint4*>(sRaw + rs * RAW_TILE + raw_c1);
                 const uint32_t sc = valid ? bf16_to_h2(sbits) : 0u, bi = valid ? bf16_to_h2(bbits) : 0u;
                 uint32_t o[32];
                 *reinterpret_cast<uint4*>(&o[0]) = dq8(q0.x, sc, bi);
@@ -619,89 +654,111 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                 *reinterpret_cast<uint4*>(&o[20]) = dq8(q1.y, sc, bi);
                 *reinterpret_cast<uint4*>(&o[24]) = dq8(q1.z, sc, bi);
                 *reinterpret_cast<uint4*>(&o[28]) = dq8(q1.w, sc, bi);
-                const uint32_t sw = it % SW, phw = (it / SW) & 1;
                 // warp-uniform outcome: tcgen05.st is warp-collective
-                if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_empty[sw], phw ^ 1, abort_flag, kWaitNs))) return false;
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_empty[sw], wph ^ 1, abort_flag, kWaitNs))) return false;
                 tc::tc_fence_after();
-                tc::tmem_st32(tlane + sw * 64, o);
+                tc::tmem_st32(tl_addr + sw * 64, o);
                 tc::tmem_st_wait();
                 tc::tc_fence_before();
                 tc::mbar_arrive(&w_full[sw]);
+                // The packed stage goes back to the TMA only now, after its words have been used:
+                // releasing it straight after the shared-memory loads let the next TMA write land
+                // before the loads had read it (measured: a few weight rows per run corrupted).
+                tc::mbar_arrive(&raw_empty[rs]);
                 ++it;
                 return true;
             };
             // scale/bias of blocks kb, kb+1 in registers; those of kb+2, kb+3 load during two blocks' work
-            uint16_t s0 = sp[0], b0 = bp[0], s1 = G > 1 ? sp[1] : 0, b1 = G > 1 ? bp[1] : 0;
+            uint16_t s0 = valid ? sp[0] : 0, b0 = valid ? bp[0] : 0;
+            uint16_t s1 = valid && G > 1 ? sp[1] : 0, b1 = valid && G > 1 ? bp[1] : 0;
             for (int kb = 0; kb < G; kb += 2) {
-                const uint16_t s2 = kb + 2 < G ? sp[kb + 2] : 0, b2 = kb + 2 < G ? bp[kb + 2] : 0;
-                const uint16_t s3 = kb + 3 < G ? sp[kb + 3] : 0, b3 = kb + 3 < G ? bp[kb + 3] : 0;
+                const uint16_t s2 = valid && kb + 2 < G ? sp[kb + 2] : 0, b2 = valid && kb + 2 < G ? bp[kb + 2] : 0;
+                const uint16_t s3 = valid && kb + 3 < G ? sp[kb + 3] : 0, b3 = valid && kb + 3 < G ? bp[kb + 3] : 0;
                 if (!step(kb, s0, b0) || (kb + 1 < G && !step(kb + 1, s1, b1))) { ok = false; break; }
                 s0 = s2; b0 = b2; s1 = s3; b1 = b3;
             }
-            cp_async_wait<0>();
         }
-    } else if (warp >= 4) {
-        // ---- epilogue: warp (4 + q) reads TMEM lanes 32q..32q+31 of both accumulators ----
-        const int q = warp & 3;
+    } else if (warp >= EPI0 / 32) {
+        // ---- epilogue: warps 4..7 and 8..11 each cover tensor-memory lane quarter (warp % 4),
+        //      taking alternate 32-token column chunks; row block 0 is drained and released
+        //      first, so the next tile's MMAs on it overlap the drain of row block 1 ----
+        const int q = warp & 3, c = (warp - EPI0 / 32) >> 2;
         uint32_t acc_it = 0;
-        for (int i = blockIdx.x; i < ntiles; i += gridDim.x) {
+        for (int i = blockIdx.x; i < ntiles; i += gridDim.x, ++acc_it) {
             const TileInfo ti = tile_info(A, i);
-            const uint32_t ab = acc_it % NACC, aph = (acc_it / NACC) & 1;
-            // warp-uniform outcome: tcgen05.ld is warp-collective
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[ab], aph, abort_flag, kWaitNs))) break;
-            tc::tc_fence_after();
-            const uint32_t taddr = tmem + ab * ACC_SET + ((uint32_t)(32 * q) << 16);
             const int rows = ti.t.rows, row0 = ti.t.row0;
-            if (MODE == 1) {
-                // accumulator a holds output rows fb*256 + 128a + (32q + lane)
-                const int f0 = ti.t.fb * 256 + 32 * q + lane;
-                float* out = ti.routed ? A.out_r : A.out_s;
-                for (int c0 = 0; c0 < rows; c0 += 16) {
-                    const int tl = c0 + (lane & 15);
-                    const float wl = ti.routed && tl < rows ? A.perm_w[row0 + tl] : 1.0f;
-                    uint32_t v0[16], v1[16];
-                    tc::tmem_ld16_sync(taddr + c0, v0);
-                    tc::tmem_ld16_sync(taddr + NT + c0, v1);
+            // mode 1, expert parallelism: output row of token (chunk j, lane), loaded before the wait
+            const bool remap = MODE == 1 && ti.routed && A.out_index != nullptr;
+            int ol[NT / 64];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int t = c0 + j;
-                        const float wgt = __shfl_sync(0xffffffffu, wl, j);
-                        if (t < rows) {
-                            const int orow = ti.routed && A.out_index ? A.out_index[row0 + t] : row0 + t;
-                            float* o = out + (size_t)orow * D + f0;
-                            o[0] = __uint_as_float(v0[j]) * wgt;
-                            o[128] = __uint_as_float(v1[j]) * wgt;
-                        }
-                    }
-                }
-            } else {
-                // accumulator 0: gate rows, accumulator 1: the same up rows -> GeGLU in-thread
-                const int kout = ti.routed ? FE : FS;
-                const int f = ti.t.fb * 128 + 32 * q + lane;
-                const bool fvalid = f < kout;
-                const int fcol = kperm(fvalid ? f : 0);
-                __half* oh = (ti.routed ? A.act_r_hi : A.act_s_hi) + fcol;
-                __half* ol = (ti.routed ? A.act_r_lo : A.act_s_lo) + fcol;
-                for (int c0 = 0; c0 < rows; c0 += 16) {
-                    uint32_t g[16], u[16];
-                    tc::tmem_ld16_sync(taddr + c0, g);
-                    tc::tmem_ld16_sync(taddr + NT + c0, u);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int t = c0 + j;
-                        if (t < rows && fvalid) {
-                            const float a = gelu_tanh_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-                            const __half hi = __float2half_rn(a);
-                            const size_t o = (size_t)(row0 + t) * kout;
-                            oh[o] = hi;
-                            ol[o] = __float2half_rn(a - __half2float(hi));
-                        }
-                    }
-                }
+            for (int j = 0; j < NT / 64; ++j) {
+                const int tl = 32 * c + 64 * j + lane;
+                ol[j] = remap && tl < rows ? A.out_index[row0 + tl] : row0 + tl;
             }
-            tc::tc_fence_before();
-            tc::mbar_arrive(&acc_empty[ab]);
-            ++acc_it;
+            // warp-uniform outcome: tcgen05.ld is warp-collective
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[0], acc_it & 1, abort_flag, kWaitNs))) break;
+            tc::tc_fence_after();
+            const int kout = ti.routed ? A.rows_r : A.rows_s;
+            for (int b = 0; b < 2; ++b) {
+                const uint32_t taddr = tmem + (uint32_t)b * NT + ((uint32_t)(32 * q) << 16);
+                if (MODE == 1) {
+                    // lane = output row f; per token one coalesced 128-byte store per warp
+                    const int f = ti.t.fb * MW + 128 * b + 32 * q + lane;
+                    float* out = (ti.routed ? A.out_r : A.out_s) + f;
+#pragma unroll
+                    for (int j = 0; j < NT / 64; ++j) {
+                        const int c0 = 32 * c + 64 * j;
+                        if (c0 >= rows) break;
+                        uint32_t v[32];
+                        tc::tmem_ld32_sync(taddr + c0, v);
+                        if (remap) {
+#pragma unroll
+                            for (int u = 0; u < 32; ++u) {
+                                const int orow = __shfl_sync(0xffffffffu, ol[j], u);
+                                if (c0 + u < rows) out[(size_t)orow * D] = __uint_as_float(v[u]);
+                            }
+                        } else {
+                            float* o = out + (size_t)(row0 + c0) * D;
+#pragma unroll
+                            for (int u = 0; u < 32; ++u)
+                                if (c0 + u < rows) o[(size_t)u * D] = __uint_as_float(v[u]);
+                        }
+                    }
+                } else if (ti.t.fb * 128 + 64 * b < kout) {
+                    // lanes 0-15 hold gate, lanes 16-31 up of the same 16 features; one exchange
+                    // gives lanes 0-15 tokens 0..15 and lanes 16-31 tokens 16..31 of each chunk
+                    const int f = ti.t.fb * 128 + gu_feature(b, q, lane);
+                    const bool up = lane >= 16;
+                    const int fcol = kperm(f);
+                    __half* oh = (ti.routed ? A.act_r_hi : A.act_s_hi) + fcol;
+                    __half* olo = (ti.routed ? A.act_r_lo : A.act_s_lo) + fcol;
+                    for (int c0 = 32 * c; c0 < rows; c0 += 64) {
+                        uint32_t v[32];
+                        tc::tmem_ld32_sync(taddr + c0, v);
+                        // all 16 activations first, branch-free, so their exp/reciprocal chains
+                        // overlap; the stores for tokens past the tile follow under a predicate
+                        uint32_t hl[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float own = __uint_as_float(up ? v[16 + j] : v[j]);
+                            const float other = __shfl_xor_sync(0xffffffffu, __uint_as_float(up ? v[j] : v[16 + j]), 16);
+                            const float g = up ? other : own, u = up ? own : other;
+                            hl[j] = split_hi_lo(gelu_tanh_fast(g) * u);
+                        }
+                        const int t0 = c0 + (up ? 16 : 0);
+                        uint16_t* ph = reinterpret_cast<uint16_t*>(oh) + (size_t)(row0 + t0) * kout;
+                        uint16_t* pl = reinterpret_cast<uint16_t*>(olo) + (size_t)(row0 + t0) * kout;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (t0 + j < rows) {
+                                ph[(size_t)j * kout] = (uint16_t)(hl[j] >> 16);
+                                pl[(size_t)j * kout] = (uint16_t)(hl[j] & 0xFFFFu);
+                            }
+                    }
+                }
+                tc::tc_fence_before();
+                tc::mbar_arrive(&acc_empty[b]);
+            }
         }
     }
     tc::tc_fence_before();
@@ -723,7 +780,8 @@ struct CombineArgs {
     const float* x_f32;
     const uint16_t* x_bf16;
     const int* pos;           // [T][8]
-    const float* out_r;       // [8T][D], routing weight applied
+    const float* w;           // [T][8] routing weights
+    const float* out_r;       // [8T][D], expert outputs (routing weight not applied)
     const float* out_s;       // [T][D]
     GtmLayer L;
     float eps;
@@ -753,13 +811,14 @@ __global__ void __launch_bounds__(512) tok_combine(const __grid_constant__ Combi
     const int t = blockIdx.x, tid = threadIdx.x;
     const GtmLayer& L = A.L;
     int p[TOPK];
+    float wk[TOPK];
 #pragma unroll
-    for (int k = 0; k < TOPK; ++k) p[k] = A.pos[(size_t)t * TOPK + k];
+    for (int k = 0; k < TOPK; ++k) { p[k] = A.pos[(size_t)t * TOPK + k]; wk[k] = A.w[(size_t)t * TOPK + k]; }
     double a = 0.0, b = 0.0;
     for (int i = tid; i < D; i += blockDim.x) {
         float acc = 0.0f;
 #pragma unroll
-        for (int k = 0; k < TOPK; ++k) acc += A.out_r[(size_t)p[k] * D + i];
+        for (int k = 0; k < TOPK; ++k) acc = __fadd_rn(acc, __fmul_rn(wk[k], A.out_r[(size_t)p[k] * D + i]));
         const float so = A.out_s[(size_t)t * D + i];
         h2[i] = acc;
         sh[i] = so;
@@ -792,7 +851,7 @@ __global__ void __launch_bounds__(512) tok_combine(const __grid_constant__ Combi
 // host side
 // ================================================================================================
 struct WsLayout {
-    size_t dense_hi, dense_lo, routed, idx, w, perm_src, perm_w, pos, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
+    size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
         act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, total;
 };
 
@@ -812,7 +871,6 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, bool ep) {
     W.idx = take(E8 * 4);
     W.w = take(E8 * 4);
     W.perm_src = take(R * 4);
-    W.perm_w = take(R * 4);
     W.pos = take(R * 4);
     W.tiles0 = take((ntr * FB0_R + nts * FB0_S) * sizeof(Tile));
     W.tiles1 = take((ntr * FB1 + nts * FB1) * sizeof(Tile));
@@ -852,18 +910,36 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Activation map: fp16 [rows][k], boxes of 64 (k) x 32 rows in the 128-byte swizzle layout.
-static int map_act(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k) {
+// Activation map: fp16 [rows][k], boxes of 64 (k) x `box_rows` rows in the 128-byte swizzle layout.
+static int map_act(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t k, uint32_t box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled not available");
     const cuuint64_t dims[2] = {k, rows};
     const cuuint64_t strides[1] = {k * 2};
-    const cuuint32_t box[2] = {tok::BK, 32};
+    const cuuint32_t box[2] = {tok::BK, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed (%d)", (int)r);
+    return GTM_OK;
+}
+
+// Packed int4 weights of one matrix kind: rows of k/2 bytes, boxes of 32 bytes (one K block) x
+// `box_rows` rows in the 32-byte swizzle layout. Routed: 3D over (byte, row, expert) with the
+// expert block stride; shared: 2D.
+static int map_w(CUtensorMap* m, const void* ptr, uint64_t k, uint64_t rows, uint64_t experts, uint64_t stride,
+                 uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled not available");
+    const cuuint64_t dims[3] = {k / 2, rows, experts ? experts : 1};
+    const cuuint64_t strides[2] = {k / 2, experts ? stride : k / 2 * rows};
+    const cuuint32_t box[3] = {32, box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, experts ? 3 : 2, const_cast<void*>(ptr), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GTM_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed (%d)", (int)r);
     return GTM_OK;
 }
 
@@ -896,7 +972,6 @@ struct Plan {
     int n;                        // routed entries (rows through the experts)
     int src_div;                  // activation source row of entry i = i / src_div
     const uint32_t* idx;          // expert ids, stride `stride`
-    const float* w;               // routing weights, stride `stride`
     int stride;
     int e0, ne;                   // experts [e0, e0 + ne), layer.experts_dev pointing at e0
     int t_shared;                 // tokens through the shared expert (0: none)
@@ -915,16 +990,24 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     memset(&g0, 0, sizeof(g0));
     memset(&g1, 0, sizeof(g1));
     int rc;
-    if ((rc = map_act(&g0.x_rhi, w.at(W.xhi), R, D)) || (rc = map_act(&g0.x_rlo, w.at(W.xlo), R, D)) ||
-        (rc = map_act(&g0.x_shi, w.at(W.dense_hi), T, D)) || (rc = map_act(&g0.x_slo, w.at(W.dense_lo), T, D)) ||
-        (rc = map_act(&g1.x_rhi, w.at(W.act_r_hi), R, FE)) || (rc = map_act(&g1.x_rlo, w.at(W.act_r_lo), R, FE)) ||
-        (rc = map_act(&g1.x_shi, w.at(W.act_s_hi), T, FS)) || (rc = map_act(&g1.x_slo, w.at(W.act_s_lo), T, FS)))
-        return rc;
+    g0.wide_r = g1.wide_r = R >= (uint64_t)NT;
+    g0.wide_s = g1.wide_s = T >= (uint64_t)NT;
+    // 32-row boxes over every activation tensor; 128-row boxes where the tensor has >= 128 rows
+    struct ActMap { CUtensorMap* narrow; CUtensorMap* wide; const void* ptr; uint64_t rows, k; };
+    const ActMap maps[] = {
+        {&g0.x_rhi, &g0.y_rhi, w.at(W.xhi), R, D},          {&g0.x_rlo, &g0.y_rlo, w.at(W.xlo), R, D},
+        {&g0.x_shi, &g0.y_shi, w.at(W.dense_hi), T, D},     {&g0.x_slo, &g0.y_slo, w.at(W.dense_lo), T, D},
+        {&g1.x_rhi, &g1.y_rhi, w.at(W.act_r_hi), R, FE},    {&g1.x_rlo, &g1.y_rlo, w.at(W.act_r_lo), R, FE},
+        {&g1.x_shi, &g1.y_shi, w.at(W.act_s_hi), T, FS},    {&g1.x_slo, &g1.y_slo, w.at(W.act_s_lo), T, FS}};
+    for (const ActMap& m : maps) {
+        if ((rc = map_act(m.narrow, m.ptr, m.rows, m.k, 32))) return rc;
+        if (m.rows >= (uint64_t)NT && (rc = map_act(m.wide, m.ptr, m.rows, m.k, NT))) return rc;
+    }
 
     RouteArgs ra;
-    ra.n = pl.n; ra.src_div = pl.src_div; ra.idx = pl.idx; ra.w = pl.w; ra.stride = pl.stride;
+    ra.n = pl.n; ra.src_div = pl.src_div; ra.idx = pl.idx; ra.stride = pl.stride;
     ra.e0 = pl.e0; ra.ne = pl.ne; ra.t_shared = pl.t_shared;
-    ra.perm_src = w.p<int>(W.perm_src); ra.perm_w = w.p<float>(W.perm_w); ra.pos = w.p<int>(W.pos);
+    ra.perm_src = w.p<int>(W.perm_src); ra.pos = w.p<int>(W.pos);
     ra.tiles0 = w.p<Tile>(W.tiles0); ra.tiles1 = w.p<Tile>(W.tiles1); ra.n_tiles = w.p<int>(W.n_tiles);
     tok_route<<<1, 1024, 0, st>>>(ra);
     if (pl.n > 0)
@@ -933,10 +1016,19 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
 
+    const uint64_t ne = pl.ne > 0 ? (uint64_t)pl.ne : 1, es = L.expert_stride;
+    if ((rc = map_w(&g0.w_ra, exb + L.expert_gate.weight, D, FE, ne, es, 128)) ||
+        (rc = map_w(&g0.w_rb, exb + L.expert_up.weight, D, FE, ne, es, 128)) ||
+        (rc = map_w(&g0.w_sa, res + L.shared_gate.weight, D, FS, 0, 0, 128)) ||
+        (rc = map_w(&g0.w_sb, res + L.shared_up.weight, D, FS, 0, 0, 128)) ||
+        (rc = map_w(&g1.w_ra, exb + L.expert_down.weight, FE, D, ne, es, MW)) ||
+        (rc = map_w(&g1.w_sa, res + L.shared_down.weight, FS, D, 0, 0, MW)))
+        return rc;
+    g1.w_rb = g1.w_ra;
+    g1.w_sb = g1.w_sa;
+
     g0.tiles = ra.tiles0; g0.n_tiles = ra.n_tiles;
     g0.experts = exb; g0.expert_stride = L.expert_stride; g0.resident = res;
-    g0.r_wa = L.expert_gate.weight; g0.r_wb = L.expert_up.weight;
-    g0.s_wa = L.shared_gate.weight; g0.s_wb = L.shared_up.weight;
     g0.r_sa = L.expert_gate.scales; g0.r_ba = L.expert_gate.biases; g0.r_sb = L.expert_up.scales; g0.r_bb = L.expert_up.biases;
     g0.s_sa = L.shared_gate.scales; g0.s_ba = L.shared_gate.biases; g0.s_sb = L.shared_up.scales; g0.s_bb = L.shared_up.biases;
     g0.k_r = D; g0.k_s = D; g0.rows_r = FE; g0.rows_s = FS;
@@ -947,12 +1039,11 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
 
     g1.tiles = ra.tiles1; g1.n_tiles = ra.n_tiles + 1;
     g1.experts = exb; g1.expert_stride = L.expert_stride; g1.resident = res;
-    g1.r_wa = L.expert_down.weight; g1.r_wb = g1.r_wa; g1.s_wa = L.shared_down.weight; g1.s_wb = g1.s_wa;
     g1.r_sa = L.expert_down.scales; g1.r_ba = L.expert_down.biases; g1.r_sb = g1.r_sa; g1.r_bb = g1.r_ba;
     g1.s_sa = L.shared_down.scales; g1.s_ba = L.shared_down.biases; g1.s_sb = g1.s_sa; g1.s_bb = g1.s_ba;
     g1.k_r = FE; g1.k_s = FS; g1.rows_r = D; g1.rows_s = D;
     g1.out_r = pl.out_r; g1.out_s = w.p<float>(W.out_s);
-    g1.perm_w = ra.perm_w; g1.out_index = pl.out_index;
+    g1.out_index = pl.out_index;
     g1.err = w.p<int>(0);
     grouped_gemm<1><<<num_sms, THREADS, SMEM_BYTES, st>>>(g1);
     return GTM_OK;
@@ -961,7 +1052,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
 void launch_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const Ws& w, const int* pos,
                     const float* out_r, cudaStream_t st) {
     CombineArgs ca;
-    ca.T = (int)io.num_tokens; ca.x_f32 = io.x_dev; ca.x_bf16 = io.x_bf16_dev; ca.pos = pos;
+    ca.T = (int)io.num_tokens; ca.x_f32 = io.x_dev; ca.x_bf16 = io.x_bf16_dev; ca.pos = pos; ca.w = w.p<float>(w.W.w);
     ca.out_r = out_r; ca.out_s = w.p<float>(w.W.out_s); ca.L = L; ca.eps = dims.eps;
     ca.hidden_out = io.hidden_out_dev; ca.h1_out = io.h1_dev; ca.h2_out = io.h2_dev;
     tok_combine<<<io.num_tokens, 512, 0, st>>>(ca);
@@ -987,7 +1078,7 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     if (ws_bytes < w.W.total) return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes", w.W.total);
     launch_views(dims, L, io, w, st);
     Plan pl;
-    pl.n = (int)(T * TOPK); pl.src_div = TOPK; pl.idx = w.p<uint32_t>(w.W.idx); pl.w = w.p<float>(w.W.w); pl.stride = 1;
+    pl.n = (int)(T * TOPK); pl.src_div = TOPK; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
     pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.src_rows = w.p<float>(w.W.routed); pl.out_index = nullptr;
     pl.out_r = w.p<float>(w.W.out_r);
     const int rc = run_gemms(L, w, pl, num_sms, st);
@@ -1024,7 +1115,7 @@ int launch_ep_shared(const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig
     const Ws w = ep_ws(ep, ws);
     Plan pl;
     memset(&pl, 0, sizeof(pl));
-    pl.n = 0; pl.src_div = 1; pl.idx = w.p<uint32_t>(w.W.idx); pl.w = w.p<float>(w.W.w); pl.stride = 1;
+    pl.n = 0; pl.src_div = 1; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
     pl.e0 = 0; pl.ne = 0; pl.t_shared = (int)io.num_tokens;
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
@@ -1038,7 +1129,7 @@ int launch_ep_experts(const GtmLayer& L, const GtmEpConfig& ep, const float* rec
     const int epr = NE / (int)ep.world;
     Plan pl;
     pl.n = (int)n_recv; pl.src_div = 1;
-    pl.idx = &recv_meta->expert; pl.w = &recv_meta->weight; pl.stride = 2;
+    pl.idx = &recv_meta->expert; pl.stride = 2;
     pl.e0 = (int)ep.rank * epr; pl.ne = epr; pl.t_shared = 0;
     pl.src_rows = recv_rows; pl.out_index = w.p<int>(w.W.perm_src); pl.out_r = ret_rows;
     const int rc = run_gemms(L, w, pl, num_sms, st);
