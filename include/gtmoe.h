@@ -253,14 +253,19 @@ GTM_API int gtm_moe_tokens_check(void* workspace_dev, void* stream);
  * Expert-parallel MoE layer: rank r of `world` owns experts [r*E/world, (r+1)*E/world) and
  * its own tokens. No reference counterpart (the reference is single-GPU). The caller moves
  * rows between ranks (NCCL all-to-all over NVLink) between the phases:
- *   1. gtm_moe_ep_dispatch  own tokens: views, router, top-k; one fp32 routed_x row per
- *                           (token, slot), grouped by destination rank in (token, slot) order
+ *   1. gtm_moe_ep_dispatch  own tokens: views, router, top-k; one routed_x row per (token,
+ *                           slot), grouped by destination rank in (token, slot) order. A row
+ *                           is `hidden` 32-bit words (4*hidden bytes) holding the fp16 high
+ *                           part then the fp16 low part of routed_x; the caller moves it as
+ *                           opaque bytes
  *   2. gtm_moe_ep_shared    own tokens: shared expert (independent of the exchange)
  *      -- all-to-all of send_counts, then of rows and metadata --
- *   3. gtm_moe_ep_experts   received rows through this rank's experts; result rows (routing
- *                           weight applied) in the order the rows were received
+ *   3. gtm_moe_ep_experts   received rows through this rank's experts; result rows (fp32
+ *                           expert outputs, routing weight not applied) in the order the rows
+ *                           were received
  *      -- all-to-all back, with the split sizes reversed --
- *   4. gtm_moe_ep_combine   own tokens: h2 = sum over the slots in router order, layer tail
+ *   4. gtm_moe_ep_combine   own tokens: h2 = sum over the slots in router order of routing
+ *                           weight x returned row, layer tail
  * With world = 1 the four phases compute what gtm_moe_tokens computes.
  * ------------------------------------------------------------------------------------- */
 
@@ -283,7 +288,7 @@ typedef struct GtmEpConfig {
 /* Workspace for the EP phases of one rank (0 for unsupported dims or sizes). Zero it once
  * before its first use. */
 GTM_API size_t gtm_moe_ep_workspace_bytes(const GtmDims* dims, const GtmEpConfig* ep);
-/* send_rows_dev: [num_tokens * top_k][hidden] fp32; send_meta_dev: [num_tokens * top_k];
+/* send_rows_dev: [num_tokens * top_k][hidden] 32-bit words (see phase 1); send_meta_dev: [num_tokens * top_k];
  * send_counts_dev: [world] device int32, rows for each destination rank. */
 GTM_API int gtm_moe_ep_dispatch(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
                                 const GtmEpConfig* ep, float* send_rows_dev, GtmEpMeta* send_meta_dev,

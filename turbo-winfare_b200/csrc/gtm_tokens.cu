@@ -7,11 +7,12 @@
 //   1. tok_views_router   per token: views (exact RMS), router logits in the reference's exact
 //                         order (or caller-given routing logits), optional logit bias, top-8
 //   2. tok_route          counts per expert, token-slot rows grouped by expert, GEMM tile lists
-//   3. tok_gather         routed_x rows in expert order, split into fp16 high and low parts
+//   3. tok_gather         routed_x rows (fp16 high and low parts) copied into expert order
 //   4. grouped_gemm<0>    gate/up of the routed experts and the shared expert, GeGLU fused,
 //                         activations written as fp16 high/low parts
-//   5. grouped_gemm<1>    down projections, routing weight fused (routed rows)
-//   6. tok_combine        h2 = sum over the 8 slots in router order, shared output, layer tail
+//   5. grouped_gemm<1>    down projections
+//   6. tok_combine        h2 = routing-weighted sum over the 8 slots in router order, shared
+//                         output, layer tail
 //
 // Grouped GEMM: one CTA per SM, persistent over a tile list built on the device. A tile is 256
 // weight rows (two M=128 row blocks, one tensor-memory lane per row) by up to 128 tokens of one
@@ -107,7 +108,7 @@ struct ViewsArgs {
     const float* route_logits;   // [T][E] or null
     __half* dense_hi;            // [T][D] (K-permuted)
     __half* dense_lo;
-    float* routed;               // [T][D] fp32
+    __half* routed_hl;           // [T][2][D] routed view: fp16 high part, then low part (K-permuted)
     uint32_t* idx;               // [T][8]
     float* w;                    // [T][8]
     float* logits_out;           // [T][E] or null
@@ -134,7 +135,10 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
         const __half hi = __float2half_rn(dx);
         A.dense_hi[(size_t)t * D + kperm(i)] = hi;
         A.dense_lo[(size_t)t * D + kperm(i)] = __float2half_rn(dx - __half2float(hi));
-        A.routed[(size_t)t * D + i] = __fmul_rn(h, bf16f(w_pre2[i]));
+        const float rx = __fmul_rn(h, bf16f(w_pre2[i]));
+        const __half rh = __float2half_rn(rx);
+        A.routed_hl[(size_t)t * 2 * D + kperm(i)] = rh;
+        A.routed_hl[(size_t)t * 2 * D + D + kperm(i)] = __float2half_rn(rx - __half2float(rh));
         srin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(h, bf16f(rs[i])), A.inv_sqrt_d);
     }
     __syncthreads();
@@ -352,28 +356,17 @@ __global__ void __launch_bounds__(256) tok_copy_rows(const float* src, const int
 }
 
 // ================================================================================================
-// 3. gather routed_x rows in expert order as fp16 high / low parts (K-permuted)
+// 3. gather the routed views in expert order: each is already an fp16 high row and low row
+//    (K-permuted, written once per token by the views kernel), so this is a row copy
 // ================================================================================================
-__global__ void __launch_bounds__(128) tok_gather(const float* routed, const int* perm_src, __half* xhi, __half* xlo) {
+__global__ void __launch_bounds__(128) tok_gather(const __half* routed_hl, const int* perm_src, __half* xhi, __half* xlo) {
     const int row = blockIdx.x;
-    const float4* src = reinterpret_cast<const float4*>(routed + (size_t)perm_src[row] * D);
+    const uint4* src = reinterpret_cast<const uint4*>(routed_hl + (size_t)perm_src[row] * 2 * D);
+    uint4* dh = reinterpret_cast<uint4*>(xhi + (size_t)row * D);
+    uint4* dl = reinterpret_cast<uint4*>(xlo + (size_t)row * D);
     for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
-        const float4 a = src[2 * c], b = src[2 * c + 1];
-        const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        uint16_t h[8], l[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const __half hv = __float2half_rn(f[e]);
-            h[kperm(e)] = __half_as_ushort(hv);
-            l[kperm(e)] = __half_as_ushort(__float2half_rn(f[e] - __half2float(hv)));
-        }
-        uint4 ph, pl;
-        ph.x = h[0] | ((uint32_t)h[1] << 16); ph.y = h[2] | ((uint32_t)h[3] << 16);
-        ph.z = h[4] | ((uint32_t)h[5] << 16); ph.w = h[6] | ((uint32_t)h[7] << 16);
-        pl.x = l[0] | ((uint32_t)l[1] << 16); pl.y = l[2] | ((uint32_t)l[3] << 16);
-        pl.z = l[4] | ((uint32_t)l[5] << 16); pl.w = l[6] | ((uint32_t)l[7] << 16);
-        reinterpret_cast<uint4*>(xhi + (size_t)row * D)[c] = ph;
-        reinterpret_cast<uint4*>(xlo + (size_t)row * D)[c] = pl;
+        dh[c] = src[c];
+        dl[c] = src[D / 8 + c];
     }
 }
 
@@ -790,60 +783,102 @@ struct CombineArgs {
     float* h2_out;            // [T][D] or null
 };
 
-__device__ __forceinline__ double block_sum(double v, double* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+constexpr int CT = 256;                       // combine: threads per token
+constexpr int CV = (D / 4 + CT - 1) / CT;     // float4 chunks of a row per thread
+
+// Block-wide sums of (a, b), every thread gets the same bits (warp partials added in warp
+// order). Consecutive calls alternate `buf`.
+__device__ __forceinline__ double2 combine_sum2(double a, double b, double (*red)[CT / 32][2], int buf) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (lane == 0) { red[buf][warp][0] = a; red[buf][warp][1] = b; }
     __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    double s = 0.0;
-    for (int w = 0; w < nw; ++w) s += red[w];
-    return s;
+    double ra = 0.0, rb = 0.0;
+#pragma unroll
+    for (int w = 0; w < CT / 32; ++w) { ra += red[buf][w][0]; rb += red[buf][w][1]; }
+    return make_double2(ra, rb);
 }
 
 // h1 = rms(shared)*w_pf1 (cpu_reference.cpp:492-493); h2 = sum_k w_k out_k in router order
 // (:508-509); hidden = (x + rms(rms(h2)*w_pf2 + h1)*w_pf) * layer_scalar (:512-520).
-__global__ void __launch_bounds__(512) tok_combine(const __grid_constant__ CombineArgs A) {
-    __shared__ __align__(16) float sh[D];
-    __shared__ __align__(16) float h2[D];
-    __shared__ double red[32];
+// One CTA per token; each thread keeps its float4 chunks of every vector in registers and
+// issues all of its row loads before the first reduction.
+__global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ CombineArgs A) {
+    __shared__ double red[2][CT / 32][2];
     const int t = blockIdx.x, tid = threadIdx.x;
     const GtmLayer& L = A.L;
     int p[TOPK];
     float wk[TOPK];
 #pragma unroll
     for (int k = 0; k < TOPK; ++k) { p[k] = A.pos[(size_t)t * TOPK + k]; wk[k] = A.w[(size_t)t * TOPK + k]; }
+    const float4* outs = reinterpret_cast<const float4*>(A.out_s) + (size_t)t * (D / 4);
+    float sv[CV][4], hv[CV][4], xv[CV][4];
     double a = 0.0, b = 0.0;
-    for (int i = tid; i < D; i += blockDim.x) {
-        float acc = 0.0f;
 #pragma unroll
-        for (int k = 0; k < TOPK; ++k) acc = __fadd_rn(acc, __fmul_rn(wk[k], A.out_r[(size_t)p[k] * D + i]));
-        const float so = A.out_s[(size_t)t * D + i];
-        h2[i] = acc;
-        sh[i] = so;
-        a += (double)so * so;
-        b += (double)acc * acc;
+    for (int v = 0; v < CV; ++v) {
+        const int c = tid + v * CT;
+        if (c < D / 4) {
+            const float4 so = outs[c];
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int k = 0; k < TOPK; ++k) {
+                const float4 r = reinterpret_cast<const float4*>(A.out_r + (size_t)p[k] * D)[c];
+                acc[0] = __fadd_rn(acc[0], __fmul_rn(wk[k], r.x));
+                acc[1] = __fadd_rn(acc[1], __fmul_rn(wk[k], r.y));
+                acc[2] = __fadd_rn(acc[2], __fmul_rn(wk[k], r.z));
+                acc[3] = __fadd_rn(acc[3], __fmul_rn(wk[k], r.w));
+            }
+            sv[v][0] = so.x; sv[v][1] = so.y; sv[v][2] = so.z; sv[v][3] = so.w;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                hv[v][e] = acc[e];
+                const size_t xi = (size_t)t * D + 4 * c + e;
+                xv[v][e] = A.x_f32 ? A.x_f32[xi] : bf16f(A.x_bf16[xi]);
+                a += (double)sv[v][e] * sv[v][e];
+                b += (double)acc[e] * acc[e];
+            }
+        }
     }
-    const float inv1 = 1.0f / sqrtf((float)(block_sum(a, red) / D) + A.eps);
-    const float inv2 = 1.0f / sqrtf((float)(block_sum(b, red) / D) + A.eps);
+    double2 r = combine_sum2(a, b, red, 0);
+    const float inv1 = 1.0f / sqrtf((float)(r.x / D) + A.eps);
+    const float inv2 = 1.0f / sqrtf((float)(r.y / D) + A.eps);
     const uint16_t* w_pf1 = rp16(L.resident_dev, L.post_ffn_norm_1);
     const uint16_t* w_pf2 = rp16(L.resident_dev, L.post_ffn_norm_2);
     const uint16_t* w_pf = rp16(L.resident_dev, L.post_ffn_norm);
     const float ls = bf16f(*rp16(L.resident_dev, L.layer_scalar));
     a = 0.0;
-    for (int i = tid; i < D; i += blockDim.x) {
-        const float h1 = (sh[i] * inv1) * bf16f(w_pf1[i]);
-        if (A.h1_out) A.h1_out[(size_t)t * D + i] = h1;
-        if (A.h2_out) A.h2_out[(size_t)t * D + i] = h2[i];
-        const float tv = (h2[i] * inv2) * bf16f(w_pf2[i]) + h1;
-        h2[i] = tv;
-        a += (double)tv * tv;
+#pragma unroll
+    for (int v = 0; v < CV; ++v) {
+        const int c = tid + v * CT;
+        if (c < D / 4) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = 4 * c + e;
+                const float h1 = (sv[v][e] * inv1) * bf16f(w_pf1[i]);
+                if (A.h1_out) A.h1_out[(size_t)t * D + i] = h1;
+                if (A.h2_out) A.h2_out[(size_t)t * D + i] = hv[v][e];
+                const float tv = (hv[v][e] * inv2) * bf16f(w_pf2[i]) + h1;
+                hv[v][e] = tv;
+                a += (double)tv * tv;
+            }
+        }
     }
-    const float inv3 = 1.0f / sqrtf((float)(block_sum(a, red) / D) + A.eps);
-    for (int i = tid; i < D; i += blockDim.x) {
-        const float x = A.x_f32 ? A.x_f32[(size_t)t * D + i] : bf16f(A.x_bf16[(size_t)t * D + i]);
-        A.hidden_out[(size_t)t * D + i] = (x + (h2[i] * inv3) * bf16f(w_pf[i])) * ls;
+    r = combine_sum2(a, 0.0, red, 1);
+    const float inv3 = 1.0f / sqrtf((float)(r.x / D) + A.eps);
+#pragma unroll
+    for (int v = 0; v < CV; ++v) {
+        const int c = tid + v * CT;
+        if (c < D / 4) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = 4 * c + e;
+                A.hidden_out[(size_t)t * D + i] = (xv[v][e] + (hv[v][e] * inv3) * bf16f(w_pf[i])) * ls;
+            }
+        }
     }
 }
 
@@ -961,7 +996,7 @@ void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     va.inv_sqrt_d = 1.0f / sqrtf((float)D);
     va.logit_bias = io.logit_bias_dev; va.route_logits = io.route_logits_dev;
     va.dense_hi = w.p<__half>(w.W.dense_hi); va.dense_lo = w.p<__half>(w.W.dense_lo);
-    va.routed = w.p<float>(w.W.routed);
+    va.routed_hl = w.p<__half>(w.W.routed);
     va.idx = w.p<uint32_t>(w.W.idx); va.w = w.p<float>(w.W.w);
     va.logits_out = io.logits_dev;
     tok_views_router<<<io.num_tokens, 512, 0, st>>>(va);
@@ -975,7 +1010,7 @@ struct Plan {
     int stride;
     int e0, ne;                   // experts [e0, e0 + ne), layer.experts_dev pointing at e0
     int t_shared;                 // tokens through the shared expert (0: none)
-    const float* src_rows;        // fp32 routed_x rows the entries read
+    const __half* src_hl;         // routed views (high row, low row) the entries read
     const int* out_index;         // mode 1 output row of each expert-ordered row (null: same)
     float* out_r;                 // mode 1 routed output rows
 };
@@ -1011,7 +1046,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     ra.tiles0 = w.p<Tile>(W.tiles0); ra.tiles1 = w.p<Tile>(W.tiles1); ra.n_tiles = w.p<int>(W.n_tiles);
     tok_route<<<1, 1024, 0, st>>>(ra);
     if (pl.n > 0)
-        tok_gather<<<(unsigned)pl.n, 128, 0, st>>>(pl.src_rows, ra.perm_src, w.p<__half>(W.xhi), w.p<__half>(W.xlo));
+        tok_gather<<<(unsigned)pl.n, 128, 0, st>>>(pl.src_hl, ra.perm_src, w.p<__half>(W.xhi), w.p<__half>(W.xlo));
 
     cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
@@ -1055,7 +1090,7 @@ void launch_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& i
     ca.T = (int)io.num_tokens; ca.x_f32 = io.x_dev; ca.x_bf16 = io.x_bf16_dev; ca.pos = pos; ca.w = w.p<float>(w.W.w);
     ca.out_r = out_r; ca.out_s = w.p<float>(w.W.out_s); ca.L = L; ca.eps = dims.eps;
     ca.hidden_out = io.hidden_out_dev; ca.h1_out = io.h1_dev; ca.h2_out = io.h2_dev;
-    tok_combine<<<io.num_tokens, 512, 0, st>>>(ca);
+    tok_combine<<<io.num_tokens, CT, 0, st>>>(ca);
 }
 
 int finish(const char* what, const GtmTokensIO* io, const Ws* w, cudaStream_t st) {
@@ -1079,7 +1114,7 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     launch_views(dims, L, io, w, st);
     Plan pl;
     pl.n = (int)(T * TOPK); pl.src_div = TOPK; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
-    pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.src_rows = w.p<float>(w.W.routed); pl.out_index = nullptr;
+    pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.src_hl = w.p<__half>(w.W.routed); pl.out_index = nullptr;
     pl.out_r = w.p<float>(w.W.out_r);
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
@@ -1131,7 +1166,7 @@ int launch_ep_experts(const GtmLayer& L, const GtmEpConfig& ep, const float* rec
     pl.n = (int)n_recv; pl.src_div = 1;
     pl.idx = &recv_meta->expert; pl.stride = 2;
     pl.e0 = (int)ep.rank * epr; pl.ne = epr; pl.t_shared = 0;
-    pl.src_rows = recv_rows; pl.out_index = w.p<int>(w.W.perm_src); pl.out_r = ret_rows;
+    pl.src_hl = reinterpret_cast<const __half*>(recv_rows); pl.out_index = w.p<int>(w.W.perm_src); pl.out_r = ret_rows;
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
     return finish("gtm_moe_ep_experts", nullptr, nullptr, st);
