@@ -119,17 +119,14 @@ __device__ __forceinline__ uint16_t ldg_nc_u16(const void* p) {
     asm("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
     return v;
 }
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-    // 16-byte aligned start, size a multiple of 16 (callers round inside the tensor's region)
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void prefetch_range(const void* p, uint64_t bytes) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
-    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes + 15) & ~uintptr_t(15);
-    for (uintptr_t q = a; q < e; q += 32768) {
-        const uint32_t n = (uint32_t)min((uintptr_t)32768, e - q);
-        prefetch_l2(reinterpret_cast<const void*>(q), n);
-    }
+// L2 prefetch hint for [p, p + bytes): one prefetch.global.L2 per 128-byte line, the warp's lanes
+// striding over the lines. Per-thread hints cost the issuing warp next to nothing, whereas a bulk
+// prefetch is a TMA operation (~64 cycles each, measured) and a warp issuing dozens of small ones
+// blocked for microseconds while the other warps waited for it at the phase's first barrier.
+__device__ __forceinline__ void prefetch_lines(const void* p, uint32_t bytes, int lane) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    for (uint32_t o = (uint32_t)lane * 128u; o < bytes; o += 32u * 128u)
+        asm volatile("prefetch.global.L2 [%0];" :: "l"(b + o));
 }
 
 // ---- fp16 fragments ------------------------------------------------------------------------
@@ -755,19 +752,16 @@ __device__ void routed_down(Smem& s, const Params& P, const GtmLayer& L, int i0,
 
 // L2 prefetch of the weights this CTA reads in the next layer's P1 (router row, shared gate/up
 // tiles, norm vectors) and of its shared-down rows.
-// Every range below is at most 32 KB and lies inside one tensor whose region starts and ends on
-// 16-byte bounds (router scale rows are 88 bytes and get rounded outwards within the region);
-// the last warp issues them, one range per lane at a time.
+// Every range below lies inside one tensor; the CTA's warps take the ranges round-robin.
 __device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
-    if ((threadIdx.x >> 5) != NW - 1) return;
-    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
     const int nrow = cta < NE ? (NE - 1 - cta) / G + 1 : 0;          // router rows of this CTA
     const int t0 = share(TILES_S, cta, G), t1 = share(TILES_S, cta + 1, G);
     const int i0 = share(ITEMS_SD, cta, G), i1 = share(ITEMS_SD, cta + 1, G);
     const int n_router = 3 * nrow, n_sgu = t1 > t0 ? 6 : 0, n_sd = 18 * (i1 - i0), n_vec = 6;
     const int total = n_router + n_sgu + n_sd + n_vec;
-    for (int i = lane; i < total; i += 32) {
+    for (int i = warp; i < total; i += NW) {
         const uint8_t* p;
         uint32_t n;
         if (i < n_router) {
@@ -797,37 +791,35 @@ __device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
             p = base + off;
             n = D * 2;
         }
-        prefetch_range(p, n);   // rounds to 16-byte bounds inside the tensor's region
+        prefetch_lines(p, n, lane);
     }
 }
 
 // L2 prefetch of this CTA's routed gate/up rows (known once the top-8 is): per tile 8 gate rows,
 // 8 up rows and their scales and biases, each a contiguous range.
 __device__ void prefetch_routed_gate_up(const Smem& s, const GtmLayer& L, int cta, int G) {
-    if ((threadIdx.x >> 5) != NW - 2) return;
-    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = share(TILES_R, cta, G), t1 = share(TILES_R, cta + 1, G);
-    for (int i = lane; i < 6 * (t1 - t0); i += 32) {
+    for (int i = warp; i < 6 * (t1 - t0); i += NW) {
         const int T = t0 + i / 6, part = i % 6, k = T / (FE / 8), r8 = T - k * (FE / 8);
         const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
         const GtmQuant& q = part < 3 ? L.expert_gate : L.expert_up;
         const int pp = part % 3;
-        if (pp == 0) prefetch_l2(blk + q.weight + (uint64_t)r8 * 8 * ROW_GU, 8 * ROW_GU);
-        else prefetch_l2(blk + (pp == 1 ? q.scales : q.biases) + (uint64_t)r8 * 8 * GD * 2, 8 * GD * 2);
+        if (pp == 0) prefetch_lines(blk + q.weight + (uint64_t)r8 * 8 * ROW_GU, 8 * ROW_GU, lane);
+        else prefetch_lines(blk + (pp == 1 ? q.scales : q.biases) + (uint64_t)r8 * 8 * GD * 2, 8 * GD * 2, lane);
     }
 }
 
 // L2 prefetch of this CTA's routed-down rows (known once the top-8 is).
 __device__ void prefetch_routed_down(const Smem& s, const GtmLayer& L, int cta, int G) {
-    if ((threadIdx.x >> 5) != NW - 1) return;
-    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i0 = share(ITEMS_RD, cta, G), i1 = share(ITEMS_RD, cta + 1, G);
-    for (int i = lane; i < 3 * (i1 - i0); i += 32) {
+    for (int i = warp; i < 3 * (i1 - i0); i += NW) {
         const int it = i0 + i / 3, part = i % 3, k = it / OT, ot = it - k * OT;
         const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
-        if (part == 0) prefetch_l2(blk + L.expert_down.weight + (uint64_t)ot * 16 * (FE / 2), 16 * (FE / 2));
-        else prefetch_l2(blk + (part == 1 ? L.expert_down.scales : L.expert_down.biases) + (uint64_t)ot * 16 * GFE * 2,
-                         16 * GFE * 2);
+        if (part == 0) prefetch_lines(blk + L.expert_down.weight + (uint64_t)ot * 16 * (FE / 2), 16 * (FE / 2), lane);
+        else prefetch_lines(blk + (part == 1 ? L.expert_down.scales : L.expert_down.biases) + (uint64_t)ot * 16 * GFE * 2,
+                            16 * GFE * 2, lane);
     }
 }
 
