@@ -6,7 +6,8 @@
 // cores:
 //   1. tok_views_router   per token: views (exact RMS), router logits in the reference's exact
 //                         order (or caller-given routing logits), optional logit bias, top-8
-//   2. tok_route          counts per expert, token-slot rows grouped by expert, GEMM tile lists
+//   2. tok_route_*        counts per expert, token-slot rows grouped by expert (in entry order),
+//                         GEMM tile lists
 //   3. tok_gather         routed_x rows (fp16 high and low parts) copied into expert order
 //   4. grouped_gemm<0>    gate/up of the routed experts and the shared expert, GeGLU fused,
 //                         activations written as fp16 high/low parts
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
 }
 
 // ================================================================================================
-// 2. routing tables and tile lists (one CTA)
+// 2. routing tables and tile lists
 // ================================================================================================
 struct RouteArgs {
     int n;                   // routed entries (0: shared tiles only)
@@ -231,8 +232,10 @@ struct RouteArgs {
     int stride;
     int e0, ne;              // experts of this launch: [e0, e0 + ne); tiles carry e - e0
     int t_shared;            // tokens of the shared-expert tiles (0: none)
+    int nchunks;             // ceil(n / RC)
+    int* chunk;              // [nchunks][NE]: per-chunk counts, then each chunk's first row per expert
     int* perm_src;           // [n] source row of each expert-ordered row
-    int* pos;                // [n] expert-ordered row of each entry
+    int* pos;                // [n] expert-ordered row of each entry (-1: another rank's expert)
     Tile* tiles0;            // gate/up tiles
     Tile* tiles1;            // down tiles
     int* n_tiles;            // [2]
@@ -240,14 +243,48 @@ struct RouteArgs {
 
 __device__ __forceinline__ int ntok_tiles(int c) { return (c + NT - 1) / NT; }
 
-__global__ void __launch_bounds__(1024) tok_route(const __grid_constant__ RouteArgs A) {
-    __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
-    const int tid = threadIdx.x, n = A.n;
-    for (int e = tid; e < NE; e += blockDim.x) cnt[e] = 0;
+// Routing tables in three steps. Rows of one expert keep the entries' order, so the layout is the
+// same on every run: an entry's row = its expert's first row + the entries of that expert in
+// earlier chunks + those before it in its own chunk.
+constexpr int RC = 1024;   // entries per counting CTA
+
+// 2a. per-chunk counts and in-chunk ranks (warp match_any, then a prefix over the warps)
+__global__ void __launch_bounds__(RC) tok_route_count(const __grid_constant__ RouteArgs A) {
+    __shared__ int wc[RC / 32][NE];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int j = tid; j < (RC / 32) * NE; j += RC) (&wc[0][0])[j] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-        const int e = (int)A.idx[(size_t)i * A.stride] - A.e0;
-        A.pos[i] = (e >= 0 && e < A.ne) ? atomicAdd(&cnt[e], 1) : -1;
+    const int i = blockIdx.x * RC + tid;
+    int e = -1;
+    if (i < A.n) {
+        e = (int)A.idx[(size_t)i * A.stride] - A.e0;
+        if (e < 0 || e >= A.ne) e = -1;   // another rank's expert (not produced by the dispatch)
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_w = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank_w == 0) wc[warp][e] = __popc(peers);
+    __syncthreads();
+    for (int ex = tid; ex < A.ne; ex += RC) {
+        int run = 0;
+        for (int w = 0; w < RC / 32; ++w) { const int c = wc[w][ex]; wc[w][ex] = run; run += c; }
+        A.chunk[(size_t)blockIdx.x * NE + ex] = run;
+    }
+    __syncthreads();
+    if (i < A.n) A.pos[i] = e >= 0 ? wc[warp][e] + rank_w : -1;
+}
+
+// 2b. expert offsets, each chunk's first row per expert, and the tile lists (one CTA)
+__global__ void __launch_bounds__(1024) tok_route_scan(const __grid_constant__ RouteArgs A) {
+    __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
+    const int tid = threadIdx.x;
+    for (int ex = tid; ex < A.ne; ex += blockDim.x) {
+        int run = 0;
+        for (int c = 0; c < A.nchunks; ++c) {
+            const int v = A.chunk[(size_t)c * NE + ex];
+            A.chunk[(size_t)c * NE + ex] = run;
+            run += v;
+        }
+        cnt[ex] = run;
     }
     __syncthreads();
     if (tid == 0) {
@@ -260,11 +297,9 @@ __global__ void __launch_bounds__(1024) tok_route(const __grid_constant__ RouteA
         off[A.ne] = o; t0[A.ne] = a; t1[A.ne] = b;
     }
     __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-        if (A.pos[i] < 0) continue;   // entry of another rank's expert (not produced by the dispatch)
-        const int row = off[(int)A.idx[(size_t)i * A.stride] - A.e0] + A.pos[i];
-        A.pos[i] = row;
-        A.perm_src[row] = i / A.src_div;
+    for (int j = tid; j < A.nchunks * A.ne; j += blockDim.x) {
+        const int c = j / A.ne, ex = j - c * A.ne;
+        A.chunk[(size_t)c * NE + ex] += off[ex];
     }
     // tiles of one (expert, row block) are adjacent over the token ranges, for L2 reuse of the weights
     for (int e = tid; e < A.ne; e += blockDim.x) {
@@ -288,6 +323,18 @@ __global__ void __launch_bounds__(1024) tok_route(const __grid_constant__ RouteA
         A.n_tiles[0] = b0 + nts * FB0_S;
         A.n_tiles[1] = b1 + nts * FB1;
     }
+}
+
+// 2c. final rows: pos = expert-ordered row of each entry, perm_src = its source row
+__global__ void __launch_bounds__(RC) tok_route_scatter(const __grid_constant__ RouteArgs A) {
+    const int i = blockIdx.x * RC + threadIdx.x;
+    if (i >= A.n) return;
+    const int r = A.pos[i];
+    if (r < 0) return;
+    const int e = (int)A.idx[(size_t)i * A.stride] - A.e0;
+    const int row = A.chunk[(size_t)blockIdx.x * NE + e] + r;
+    A.pos[i] = row;
+    A.perm_src[row] = i / A.src_div;
 }
 
 // ================================================================================================
@@ -886,7 +933,7 @@ __global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ Combin
 // host side
 // ================================================================================================
 struct WsLayout {
-    size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
+    size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
         act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, total;
 };
 
@@ -907,6 +954,7 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, bool ep) {
     W.w = take(E8 * 4);
     W.perm_src = take(R * 4);
     W.pos = take(R * 4);
+    W.chunk = take((R + RC - 1) / RC * NE * 4);
     W.tiles0 = take((ntr * FB0_R + nts * FB0_S) * sizeof(Tile));
     W.tiles1 = take((ntr * FB1 + nts * FB1) * sizeof(Tile));
     W.n_tiles = take(2 * 4);
@@ -1042,9 +1090,12 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     RouteArgs ra;
     ra.n = pl.n; ra.src_div = pl.src_div; ra.idx = pl.idx; ra.stride = pl.stride;
     ra.e0 = pl.e0; ra.ne = pl.ne; ra.t_shared = pl.t_shared;
+    ra.nchunks = (pl.n + RC - 1) / RC; ra.chunk = w.p<int>(W.chunk);
     ra.perm_src = w.p<int>(W.perm_src); ra.pos = w.p<int>(W.pos);
     ra.tiles0 = w.p<Tile>(W.tiles0); ra.tiles1 = w.p<Tile>(W.tiles1); ra.n_tiles = w.p<int>(W.n_tiles);
-    tok_route<<<1, 1024, 0, st>>>(ra);
+    if (ra.nchunks > 0) tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
+    tok_route_scan<<<1, 1024, 0, st>>>(ra);
+    if (ra.nchunks > 0) tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
     if (pl.n > 0)
         tok_gather<<<(unsigned)pl.n, 128, 0, st>>>(pl.src_hl, ra.perm_src, w.p<__half>(W.xhi), w.p<__half>(W.xlo));
 
