@@ -23,8 +23,9 @@
 // and streaming it per 128 weight rows would need about the whole L2-to-SM bandwidth of an SM. A
 // gate/up tile holds 128 features (row block b: features 64b..64b+63; in each 32-lane quarter,
 // lanes 0-15 the gate rows and lanes 16-31 the up rows of the same 16 features, so GeGLU needs
-// one shuffle). Tensor memory (512 columns): the two accumulators (128 columns each) and four
-// weight stages of 2 x 32 columns. On B200 a 128 x N x 16 MMA costs ~62 cycles for any N up to
+// one shuffle). Tensor memory (512 columns): three accumulator slots of 128 columns that the row
+// blocks rotate through (row block b of tile n in slot (2n + b) % 3) and two weight stages of
+// 2 x 32 columns. On B200 a 128 x N x 16 MMA costs ~62 cycles for any N up to
 // ~128 (measured), so N = 128 is the narrowest tile that keeps the tensor pipe busy. Warp roles:
 //   * warp 0 loads the activation tile by TMA per K block, the fp16 high part and the fp16 low
 //     part (x - hi), so the MMAs against the same weights carry ~22 bits of the activation;
@@ -35,8 +36,9 @@
 //     the block straight into the row's tensor-memory lane;
 //   * warp 1 issues tcgen05.mma (kind::f16, M=128, N=16..128, K=16, A from tensor memory, B from
 //     shared memory) with the whole warp converged and one elected lane issuing;
-//   * warps 4-11 (two per lane quarter, alternate 16-token chunks) drain row block 0 and release
-//     it, then row block 1, so the next tile's first MMAs overlap the second half of the drain.
+//   * warps 4-11 (two per lane quarter, alternate 32-token chunks) drain row block 0's slot and
+//     release it, then row block 1's: the next tile's row block 0 already has the third slot,
+//     and its row block 1 waits only for the first half of the drain.
 // Within every 8-element chunk of K the dequantised weights come out in the order
 // (0,4,1,5,2,6,3,7), the order the nibble extraction yields; activations are stored in the same
 // order, so the products are unchanged and no permute instructions are spent.
@@ -61,8 +63,9 @@ constexpr int MW = 256;                 // weight rows per tile: two M=128 row b
 constexpr int NT = 128;                 // tokens per tile (MMA N, at most)
 constexpr int SX = 6;                   // activation stages (shared memory, high + low part each)
 constexpr int RS = 4;                   // packed-weight stages (shared memory)
-constexpr int SW = 4;                   // dequantised-weight stages (tensor memory, 2 x 32 columns each)
-constexpr uint32_t A_COL0 = 2 * NT;     // accumulators: row block b at columns b * NT; weights after
+constexpr int SW = 2;                   // dequantised-weight stages (tensor memory, 2 x 32 columns each)
+constexpr int NSLOT = 3;                // accumulator slots of NT columns; row blocks rotate through them
+constexpr uint32_t A_COL0 = NSLOT * NT; // first tensor-memory column of the weight stages
 constexpr int THREADS = 640;            // 20 warps; roles in grouped_gemm
 constexpr int EPI0 = 128, EPI_THREADS = 256;  // epilogue: warps 4..11, two per tensor-memory lane quarter
 constexpr int DQ0 = 384, DQ_THREADS = 256;    // dequant: warps 12..19, one thread per weight row
@@ -72,7 +75,7 @@ constexpr uint32_t XBOX = 32 * BK * 2;        // 4 KB: one TMA box of 32 token r
 // measured): tiles of more than 64 tokens load each activation part as one 128-row box.
 constexpr int XWIDE_MIN = 65;
 constexpr uint32_t RAW_TILE = MW * BK / 2;    // 8 KB packed int4 per K block, rows of 32 bytes
-constexpr size_t SMEM_BYTES = 1024 + 2 * SX * X_TILE + RS * RAW_TILE + (2 * SX + 2 * RS + 2 * SW + 3) * 8 + 16;
+constexpr size_t SMEM_BYTES = 1024 + 2 * SX * X_TILE + RS * RAW_TILE + (2 * SX + 2 * RS + 2 * SW + 1 + NSLOT) * 8 + 16;
 static_assert(A_COL0 + SW * 64 <= 512, "tensor memory columns");
 constexpr int FB0_R = (FE + 127) / 128, FB0_S = (FS + 127) / 128;   // gate/up tiles: 128 features (gate + up)
 constexpr int FB1 = D / MW;                                         // down tiles: 256 output rows
@@ -523,8 +526,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
     uint64_t* w_full = raw_empty + RS;           // [SW]
     uint64_t* w_empty = w_full + SW;             // [SW]
     uint64_t* acc_full = w_empty + SW;           // [1]
-    uint64_t* acc_empty = acc_full + 1;          // [2] one per row block
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* acc_empty = acc_full + 1;          // [NSLOT] one per accumulator slot
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NSLOT);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -533,8 +536,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
         for (int s = 0; s < RS; ++s) { tc::mbar_init(&raw_full[s], 1); tc::mbar_init(&raw_empty[s], DQ_THREADS); }
         for (int s = 0; s < SW; ++s) { tc::mbar_init(&w_full[s], DQ_THREADS); tc::mbar_init(&w_empty[s], 1); }
         tc::mbar_init(&acc_full[0], 1);
-        tc::mbar_init(&acc_empty[0], EPI_THREADS);
-        tc::mbar_init(&acc_empty[1], EPI_THREADS);
+        for (int b = 0; b < NSLOT; ++b) tc::mbar_init(&acc_empty[b], EPI_THREADS);
         *abort_flag = 0;
         tc::mbar_fence_init();
     }
@@ -605,7 +607,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
     } else if (warp == 1) {
         // ---- MMA issuer (the whole warp; one elected lane issues). Per K step and row block:
         //      weights (A, tensor memory) x activation high part, then x low part (B, shared
-        //      memory). Row block 1 of the last gate/up tile lies past the matrix: skipped. ----
+        //      memory). Row block b of tile n accumulates in slot (2n + b) % 3, so the next
+        //      tile's row block 0 finds a free slot while the epilogue drains this tile. Row
+        //      block 1 of the last gate/up tile lies past the matrix: skipped. ----
         uint32_t it = 0, acc_it = 0;
         bool ok = true;
         for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x, ++acc_it) {
@@ -613,7 +617,6 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
             const int kout = ti.routed ? A.rows_r : A.rows_s;
             const bool rb1 = MODE == 1 || ti.t.fb * 128 + 64 < kout;
             const uint32_t idesc = tc::idesc_f16(128, (uint32_t)((ti.t.rows + 15) & ~15));
-            const uint32_t eph = (acc_it & 1) ^ 1;
             for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
                 const uint32_t sx = it % SX, phx = (it / SX) & 1, sw = it % SW, phw = (it / SW) & 1;
                 if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_full[sw], phw, abort_flag, kWaitNs) &&
@@ -622,12 +625,14 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                 const uint64_t dh = tc::sdesc_sw128(tc::smem_u32(sXh + sx * X_TILE));
                 const uint64_t dl = tc::sdesc_sw128(tc::smem_u32(sXl + sx * X_TILE));
                 for (int b = 0; b < 2; ++b) {
-                    if (kb == 0) {   // the epilogue has drained this row block's accumulator
-                        if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_empty[b], eph, abort_flag, kWaitNs))) { ok = false; break; }
+                    const uint32_t rbg = 2 * acc_it + (uint32_t)b, slot = rbg % NSLOT;
+                    if (kb == 0) {   // the epilogue has drained the slot's previous row block
+                        if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_empty[slot], ((rbg / NSLOT) & 1) ^ 1, abort_flag,
+                                                                   kWaitNs))) { ok = false; break; }
                         tc::tc_fence_after();
                     }
                     if (b == 1 && !rb1) break;
-                    const uint32_t d = tmem + (uint32_t)b * NT;
+                    const uint32_t d = tmem + slot * NT;
                     const uint32_t wa = tmem + A_COL0 + sw * 64 + (uint32_t)b * 32;   // 8 columns per K step
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
@@ -720,8 +725,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
         }
     } else if (warp >= EPI0 / 32) {
         // ---- epilogue: warps 4..7 and 8..11 each cover tensor-memory lane quarter (warp % 4),
-        //      taking alternate 32-token column chunks; row block 0 is drained and released
-        //      first, so the next tile's MMAs on it overlap the drain of row block 1 ----
+        //      taking alternate 32-token column chunks; row block 0's slot is drained and
+        //      released first ----
         const int q = warp & 3, c = (warp - EPI0 / 32) >> 2;
         uint32_t acc_it = 0;
         for (int i = blockIdx.x; i < ntiles; i += gridDim.x, ++acc_it) {
@@ -740,7 +745,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
             tc::tc_fence_after();
             const int kout = ti.routed ? A.rows_r : A.rows_s;
             for (int b = 0; b < 2; ++b) {
-                const uint32_t taddr = tmem + (uint32_t)b * NT + ((uint32_t)(32 * q) << 16);
+                const uint32_t slot = (2 * acc_it + (uint32_t)b) % NSLOT;
+                const uint32_t taddr = tmem + slot * NT + ((uint32_t)(32 * q) << 16);
                 if (MODE == 1) {
                     // lane = output row f; per token one coalesced 128-byte store per warp
                     const int f = ti.t.fb * MW + 128 * b + 32 * q + lane;
@@ -797,7 +803,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                     }
                 }
                 tc::tc_fence_before();
-                tc::mbar_arrive(&acc_empty[b]);
+                tc::mbar_arrive(&acc_empty[slot]);
             }
         }
     }
