@@ -152,55 +152,68 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
-    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-}
 
 // Builds the fragment table of `groups` 64-element groups of the fp32 vector v (in shared
 // memory): for thread column t and part hl (0 = fp16 high part, 1 = low part) the 16 elements
 // 16t..16t+15 as (x0,x4)(x1,x5)(x2,x6)(x3,x7)(x8,x12)(x9,x13)(x10,x14)(x11,x15), odd elements
 // divided by 16 (exact). Also per-group sums xs (for the bias) and the offset constants cs.
+// hi + lo = b with hi = b rounded to 11 significant bits (Veltkamp split, exact in fp32) and lo =
+// b - hi; converted in pairs with one packed instruction each. hi is exact in fp16 for
+// |b| >= 2^-14; below that the fp16 conversion rounds it again (an absolute error under 2^-25).
+__device__ __forceinline__ void split11(float b, float& hi, float& lo) {
+    const float c = __fmul_rn(b, 8193.0f);
+    hi = __fsub_rn(c, __fsub_rn(c, b));
+    lo = __fsub_rn(b, hi);
+}
+__device__ __forceinline__ uint32_t cvt2(float lo_half, float hi_half) {   // (low 16 bits, high 16 bits)
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi_half), "f"(lo_half));
+    return r;
+}
+
 __device__ void build_table(const float* v, int groups, uint32_t* tbl, float* xs, float* cs) {
-    for (int i = threadIdx.x; i < groups * 8; i += blockDim.x) {
-        const int j = i >> 3, t = (i >> 1) & 3, hl = i & 1, slotn = t * 2 + hl;
+    // one thread per (group j, thread column t): both parts of its 16 elements, then the group's
+    // sums over the 4 columns (adjacent lanes)
+    for (int i = threadIdx.x; i < ((groups * 4 + 31) & ~31); i += blockDim.x) {
+        const bool on = i < groups * 4;
+        const int j = on ? i >> 2 : 0, t = i & 3;
         const float4* src = reinterpret_cast<const float4*>(v + j * 64 + t * 16);
-        float x[16];
+        float x[16], hi[16], lo[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const float4 f = src[q];
             x[4 * q] = f.x; x[4 * q + 1] = f.y; x[4 * q + 2] = f.z; x[4 * q + 3] = f.w;
         }
-        __half h[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-            const float b = (q & 1) ? x[q] * 0.0625f : x[q];
-            const __half hi = __float2half_rn(b);
-            h[q] = hl == 0 ? hi : __float2half_rn(b - __half2float(hi));
-        }
+        for (int q = 0; q < 16; ++q) split11((q & 1) ? x[q] * 0.0625f : x[q], hi[q], lo[q]);
         // pairs (x0,x4)(x1,x5)(x2,x6)(x3,x7) | (x8,x12)(x9,x13)(x10,x14)(x11,x15)
-        uint4 p0 = make_uint4(pack_h2(h[0], h[4]), pack_h2(h[1], h[5]), pack_h2(h[2], h[6]), pack_h2(h[3], h[7]));
-        uint4 p1 = make_uint4(pack_h2(h[8], h[12]), pack_h2(h[9], h[13]), pack_h2(h[10], h[14]), pack_h2(h[11], h[15]));
-        *reinterpret_cast<uint4*>(tbl + ((j * 2 + 0) * 8 + slotn) * 4) = p0;
-        *reinterpret_cast<uint4*>(tbl + ((j * 2 + 1) * 8 + slotn) * 4) = p1;
-    }
-    const int lane = threadIdx.x & 31;
-    for (int j = threadIdx.x >> 5; j < groups; j += blockDim.x >> 5) {
-        float s = 0.0f, c = 0.0f;
+        const uint4 h0 = make_uint4(cvt2(hi[0], hi[4]), cvt2(hi[1], hi[5]), cvt2(hi[2], hi[6]), cvt2(hi[3], hi[7]));
+        const uint4 h1 = make_uint4(cvt2(hi[8], hi[12]), cvt2(hi[9], hi[13]), cvt2(hi[10], hi[14]), cvt2(hi[11], hi[15]));
+        const uint4 l0 = make_uint4(cvt2(lo[0], lo[4]), cvt2(lo[1], lo[5]), cvt2(lo[2], lo[6]), cvt2(lo[3], lo[7]));
+        const uint4 l1 = make_uint4(cvt2(lo[8], lo[12]), cvt2(lo[9], lo[13]), cvt2(lo[10], lo[14]), cvt2(lo[11], lo[15]));
+        float sx = 0.0f, c = 0.0f;
+        if (on) {
+            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 0) * 8 + t * 2 + 0) * 4) = h0;
+            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 1) * 8 + t * 2 + 0) * 4) = h1;
+            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 0) * 8 + t * 2 + 1) * 4) = l0;
+            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 1) * 8 + t * 2 + 1) * 4) = l1;
+            // what the MMA adds besides n*x: 1024 * (hi + lo) as the fp16 operands hold them
+            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const float x = v[j * 64 + 32 * h + lane];
-            const float b = (lane & 1) ? x * 0.0625f : x;
-            const __half hi = __float2half_rn(b);
-            const __half lo = __float2half_rn(b - __half2float(hi));
-            s += x;
-            c += 1024.0f * (__half2float(hi) + __half2float(lo));   // what the MMA adds besides n*x
-        }
+            for (int q = 0; q < 8; ++q) {
+                const float2 fh = __half22float2(*reinterpret_cast<const __half2*>(&hw[q]));
+                const float2 fl = __half22float2(*reinterpret_cast<const __half2*>(&lw[q]));
+                c += 1024.0f * ((fh.x + fl.x) + (fh.y + fl.y));
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            s += __shfl_xor_sync(0xffffffffu, s, o);
-            c += __shfl_xor_sync(0xffffffffu, c, o);
+            for (int q = 0; q < 16; ++q) sx += x[q];
         }
-        if (lane == 0) { xs[j] = s; cs[j] = c; }
+        sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+        sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+        c += __shfl_xor_sync(0xffffffffu, c, 1);
+        c += __shfl_xor_sync(0xffffffffu, c, 2);
+        if (on && t == 0) { xs[j] = sx; cs[j] = c; }
     }
 }
 
