@@ -74,6 +74,12 @@ constexpr uint32_t XBOX = 32 * BK * 2;        // 4 KB: one TMA box of 32 token r
 // TMA moves a few large boxes faster than many small ones (~64 cycles a box on top of the bytes,
 // measured): tiles of more than 64 tokens load each activation part as one 128-row box.
 constexpr int XWIDE_MIN = 65;
+// Tiles of at most 64 tokens stack the high and low activation parts as rows of one B operand
+// (high rows, then low rows, each rounded up to 32), so one MMA per K step and row block covers
+// both; the epilogue adds the two column ranges. A 128 x N x 16 MMA costs ~62 cycles for any
+// N <= 128, so this halves the tensor time of small tiles.
+constexpr int STACK_MAX = 64;
+__device__ __forceinline__ int stacked_hi_rows(int rows) { return rows <= STACK_MAX ? ((rows + 31) >> 5) * 32 : 0; }
 constexpr uint32_t RAW_TILE = MW * BK / 2;    // 8 KB packed int4 per K block, rows of 32 bytes
 constexpr size_t SMEM_BYTES = 1024 + 2 * SX * X_TILE + RS * RAW_TILE + (2 * SX + 2 * RS + 2 * SW + 1 + NSLOT) * 8 + 16;
 static_assert(A_COL0 + SW * 64 <= 512, "tensor memory columns");
@@ -505,6 +511,17 @@ __device__ __forceinline__ uint32_t split_hi_lo(float a) {
     return r;
 }
 
+// v[u] += the accumulator column taddr + u (u < 32), loaded 16 columns at a time.
+__device__ __forceinline__ void add_low_part(uint32_t taddr, uint32_t (&v)[32]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint32_t w[16];
+        tc::tmem_ld16_sync(taddr + 16 * h, w);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[16 * h + u] = __float_as_uint(__uint_as_float(v[16 * h + u]) + __uint_as_float(w[u]));
+    }
+}
+
 // Gate/up tile of 128 features f0 .. f0+127: row block b holds features f0 + 64b + (0..63); in
 // each 32-lane quarter q, lanes 0-15 are the gate rows and lanes 16-31 the up rows of features
 // f0 + 64b + 16q + (0..15), so GeGLU needs one shuffle. Packed rows sit in shared memory as the
@@ -563,9 +580,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                     const uint32_t s = it % SX, ph = (it / SX) & 1;
                     if (!tc::mbar_wait(&act_empty[s], ph ^ 1, abort_flag, kWaitNs)) { ok = false; break; }
                     tc::mbar_arrive_expect_tx(&act_full[s], 2u * box_bytes * (uint32_t)nbox);
+                    // stacked tiles: low part right after the high part in the same stage
+                    uint8_t* lo_dst = stacked_hi_rows(ti.t.rows) ? sXh + s * X_TILE + nbox * XBOX : sXl + s * X_TILE;
                     for (int j = 0; j < nbox; ++j) {
                         tc::tma_load_2d(sXh + s * X_TILE + j * XBOX, mh, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
-                        tc::tma_load_2d(sXl + s * X_TILE + j * XBOX, ml, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
+                        tc::tma_load_2d(lo_dst + j * XBOX, ml, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
                     }
                 }
             }
@@ -616,7 +635,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
             const TileInfo ti = tile_info(A, i);
             const int kout = ti.routed ? A.rows_r : A.rows_s;
             const bool rb1 = MODE == 1 || ti.t.fb * 128 + 64 < kout;
-            const uint32_t idesc = tc::idesc_f16(128, (uint32_t)((ti.t.rows + 15) & ~15));
+            const int hrows = stacked_hi_rows(ti.t.rows);
+            const uint32_t idesc = tc::idesc_f16(128, hrows ? 2u * (uint32_t)hrows : (uint32_t)((ti.t.rows + 15) & ~15));
             for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
                 const uint32_t sx = it % SX, phx = (it / SX) & 1, sw = it % SW, phw = (it / SW) & 1;
                 if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_full[sw], phw, abort_flag, kWaitNs) &&
@@ -634,10 +654,16 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                     if (b == 1 && !rb1) break;
                     const uint32_t d = tmem + slot * NT;
                     const uint32_t wa = tmem + A_COL0 + sw * 64 + (uint32_t)b * 32;   // 8 columns per K step
+                    if (hrows) {
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        tc::mma_f16_ts(d, wa + 8 * k, dh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                        tc::mma_f16_ts(d, wa + 8 * k, dl + 2 * k, idesc, 1u);
+                        for (int k = 0; k < BK / 16; ++k)
+                            tc::mma_f16_ts(d, wa + 8 * k, dh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k) {
+                            tc::mma_f16_ts(d, wa + 8 * k, dh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                            tc::mma_f16_ts(d, wa + 8 * k, dl + 2 * k, idesc, 1u);
+                        }
                     }
                 }
                 if (!ok) break;
@@ -744,6 +770,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
             if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[0], acc_it & 1, abort_flag, kWaitNs))) break;
             tc::tc_fence_after();
             const int kout = ti.routed ? A.rows_r : A.rows_s;
+            const int hrows = stacked_hi_rows(rows);   // stacked tile: low-part sums at column + hrows
             for (int b = 0; b < 2; ++b) {
                 const uint32_t slot = (2 * acc_it + (uint32_t)b) % NSLOT;
                 const uint32_t taddr = tmem + slot * NT + ((uint32_t)(32 * q) << 16);
@@ -757,6 +784,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                         if (c0 >= rows) break;
                         uint32_t v[32];
                         tc::tmem_ld32_sync(taddr + c0, v);
+                        if (hrows) add_low_part(taddr + hrows + c0, v);
                         if (remap) {
 #pragma unroll
                             for (int u = 0; u < 32; ++u) {
@@ -781,6 +809,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                     for (int c0 = 32 * c; c0 < rows; c0 += 64) {
                         uint32_t v[32];
                         tc::tmem_ld32_sync(taddr + c0, v);
+                        if (hrows) add_low_part(taddr + hrows + c0, v);
                         // all 16 activations first, branch-free, so their exp/reciprocal chains
                         // overlap; the stores for tokens past the tile follow under a predicate
                         uint32_t hl[16];
