@@ -136,3 +136,19 @@ def test_repeat_is_deterministic(model, block):
     b = run(block, model, x)
     for k in a:
         assert np.array_equal(a[k], b[k]), k
+
+
+@pytest.mark.parametrize("T", [1, 31, 32, 33, 63, 64, 65, 127, 128, 129, 200])
+def test_forced_routing_tile_edges(model, ref_layer, block, T):
+    """Every token routed to the same 8 experts, so each expert's token count is T: covers the
+    stacked high/low operand (<= 64 tokens, 32-row boxes), 128-row activation boxes (65..128)
+    and two token tiles per expert (> 128) at their exact edges."""
+    x = synth_tokens(T, token0=5000 + T)
+    rl = np.tile(np.arange(E, dtype=np.float32) * 1e-3, (T, 1))
+    hot = [3, 17, 40, 41, 77, 90, 101, 127]
+    rl[:, hot] += 5.0
+    got = run(block, model, x, route_logits=torch.from_numpy(rl).cuda())
+    assert all(sorted(got["idx"][t].tolist()) == hot for t in range(T))
+    xs = x.cpu().numpy()
+    for t in sorted({0, 31 % T, 32 % T, 63 % T, 64 % T, T // 2, T - 1}):
+        check_token(ref_layer, got, t, xs[t], route_logits=rl[t], exact_logits=False)
