@@ -258,7 +258,10 @@ GTM_API int gtm_moe_tokens_check(void* workspace_dev, void* stream);
  *                           is `hidden` 32-bit words (4*hidden bytes) holding the fp16 high
  *                           part then the fp16 low part of routed_x; the caller moves it as
  *                           opaque bytes
- *   2. gtm_moe_ep_shared    own tokens: shared expert (independent of the exchange)
+ *   2. gtm_moe_ep_shared    own tokens: shared expert (independent of the exchange; it uses
+ *                           its own part of the workspace, so it may run on a second stream
+ *                           concurrently with phase 3 once phase 1 has completed; phase 4
+ *                           must follow both)
  *      -- all-to-all of send_counts, then of rows and metadata --
  *   3. gtm_moe_ep_experts   received rows through this rank's experts; result rows (fp32
  *                           expert outputs, routing weight not applied) in the order the rows

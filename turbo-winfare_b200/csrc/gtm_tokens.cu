@@ -234,6 +234,8 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
 // ================================================================================================
 // 2. routing tables and tile lists
 // ================================================================================================
+constexpr int kMaxPeers = 8;   // ranks of a peer-memory expert-parallel group (NVLink domain of one box)
+
 struct RouteArgs {
     int n;                   // routed entries (0: shared tiles only)
     int src_div;             // activation source row of entry i = i / src_div
@@ -242,6 +244,12 @@ struct RouteArgs {
     int e0, ne;              // experts of this launch: [e0, e0 + ne); tiles carry e - e0
     int t_shared;            // tokens of the shared-expert tiles (0: none)
     int nchunks;             // ceil(n / RC)
+    // peer-memory expert parallelism: entry i is entry i % per_src of source rank i / per_src,
+    // read from that rank's workspace (src_idx), valid below 8 x its token count (src_ntok)
+    int nsrc, per_src;
+    const uint32_t* src_idx[kMaxPeers];
+    const int* src_ntok[kMaxPeers];
+    int* nrows;              // peer mode: rows through this launch's experts (for the gather)
     int* chunk;              // [nchunks][NE]: per-chunk counts, then each chunk's first row per expert
     int* perm_src;           // [n] source row of each expert-ordered row
     int* pos;                // [n] expert-ordered row of each entry (-1: another rank's expert)
@@ -251,6 +259,20 @@ struct RouteArgs {
 };
 
 __device__ __forceinline__ int ntok_tiles(int c) { return (c + NT - 1) / NT; }
+
+// Expert id of entry i (-1: not one of this launch's experts, or past its source's tokens).
+__device__ __forceinline__ int route_expert(const RouteArgs& A, int i) {
+    if (i >= A.n) return -1;
+    int e;
+    if (A.nsrc > 0) {
+        const int s = i / A.per_src, j = i - s * A.per_src;
+        if (j >= *A.src_ntok[s] * TOPK) return -1;
+        e = (int)A.src_idx[s][j] - A.e0;
+    } else {
+        e = (int)A.idx[(size_t)i * A.stride] - A.e0;
+    }
+    return (e >= 0 && e < A.ne) ? e : -1;
+}
 
 // Routing tables in three steps. Rows of one expert keep the entries' order, so the layout is the
 // same on every run: an entry's row = its expert's first row + the entries of that expert in
@@ -264,11 +286,7 @@ __global__ void __launch_bounds__(RC) tok_route_count(const __grid_constant__ Ro
     for (int j = tid; j < (RC / 32) * NE; j += RC) (&wc[0][0])[j] = 0;
     __syncthreads();
     const int i = blockIdx.x * RC + tid;
-    int e = -1;
-    if (i < A.n) {
-        e = (int)A.idx[(size_t)i * A.stride] - A.e0;
-        if (e < 0 || e >= A.ne) e = -1;   // another rank's expert (not produced by the dispatch)
-    }
+    const int e = route_expert(A, i);   // -1: another rank's expert (or no entry)
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_w = __popc(peers & ((1u << lane) - 1u));
     if (e >= 0 && rank_w == 0) wc[warp][e] = __popc(peers);
@@ -304,6 +322,7 @@ __global__ void __launch_bounds__(1024) tok_route_scan(const __grid_constant__ R
             o += cnt[e]; a += nt * FB0_R; b += nt * FB1;
         }
         off[A.ne] = o; t0[A.ne] = a; t1[A.ne] = b;
+        if (A.nrows) *A.nrows = o;
     }
     __syncthreads();
     for (int j = tid; j < A.nchunks * A.ne; j += blockDim.x) {
@@ -340,7 +359,7 @@ __global__ void __launch_bounds__(RC) tok_route_scatter(const __grid_constant__ 
     if (i >= A.n) return;
     const int r = A.pos[i];
     if (r < 0) return;
-    const int e = (int)A.idx[(size_t)i * A.stride] - A.e0;
+    const int e = route_expert(A, i);
     const int row = A.chunk[(size_t)blockIdx.x * NE + e] + r;
     A.pos[i] = row;
     A.perm_src[row] = i / A.src_div;
@@ -968,7 +987,7 @@ __global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ Combin
 // host side
 // ================================================================================================
 struct WsLayout {
-    size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, xhi, xlo, act_r_hi,
+    size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, stiles0, stiles1, sn_tiles, xhi, xlo, act_r_hi,
         act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, total;
 };
 
@@ -993,6 +1012,11 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, bool ep) {
     W.tiles0 = take((ntr * FB0_R + nts * FB0_S) * sizeof(Tile));
     W.tiles1 = take((ntr * FB1 + nts * FB1) * sizeof(Tile));
     W.n_tiles = take(2 * 4);
+    // expert parallelism: the shared-expert phase keeps its own tile lists, so it can run on
+    // another stream while the experts phase (same workspace) runs
+    W.stiles0 = ep ? take(nts * FB0_S * sizeof(Tile)) : 0;
+    W.stiles1 = ep ? take(nts * FB1 * sizeof(Tile)) : 0;
+    W.sn_tiles = ep ? take(2 * 4) : 0;
     W.xhi = take(R * D * 2);
     W.xlo = take(R * D * 2);
     W.act_r_hi = take(R * FE * 2);
@@ -1096,6 +1120,7 @@ struct Plan {
     const __half* src_hl;         // routed views (high row, low row) the entries read
     const int* out_index;         // mode 1 output row of each expert-ordered row (null: same)
     float* out_r;                 // mode 1 routed output rows
+    bool own_tiles;               // shared-expert-only plan: tile lists in the stiles* regions
 };
 
 int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaStream_t st) {
@@ -1123,11 +1148,14 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     }
 
     RouteArgs ra;
+    memset(&ra, 0, sizeof(ra));
     ra.n = pl.n; ra.src_div = pl.src_div; ra.idx = pl.idx; ra.stride = pl.stride;
     ra.e0 = pl.e0; ra.ne = pl.ne; ra.t_shared = pl.t_shared;
     ra.nchunks = (pl.n + RC - 1) / RC; ra.chunk = w.p<int>(W.chunk);
     ra.perm_src = w.p<int>(W.perm_src); ra.pos = w.p<int>(W.pos);
-    ra.tiles0 = w.p<Tile>(W.tiles0); ra.tiles1 = w.p<Tile>(W.tiles1); ra.n_tiles = w.p<int>(W.n_tiles);
+    ra.tiles0 = w.p<Tile>(pl.own_tiles ? W.stiles0 : W.tiles0);
+    ra.tiles1 = w.p<Tile>(pl.own_tiles ? W.stiles1 : W.tiles1);
+    ra.n_tiles = w.p<int>(pl.own_tiles ? W.sn_tiles : W.n_tiles);
     if (ra.nchunks > 0) tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
     tok_route_scan<<<1, 1024, 0, st>>>(ra);
     if (ra.nchunks > 0) tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
@@ -1199,6 +1227,7 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     if (ws_bytes < w.W.total) return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes", w.W.total);
     launch_views(dims, L, io, w, st);
     Plan pl;
+    memset(&pl, 0, sizeof(pl));
     pl.n = (int)(T * TOPK); pl.src_div = TOPK; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
     pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.src_hl = w.p<__half>(w.W.routed); pl.out_index = nullptr;
     pl.out_r = w.p<float>(w.W.out_r);
@@ -1238,6 +1267,7 @@ int launch_ep_shared(const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig
     memset(&pl, 0, sizeof(pl));
     pl.n = 0; pl.src_div = 1; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
     pl.e0 = 0; pl.ne = 0; pl.t_shared = (int)io.num_tokens;
+    pl.own_tiles = true;
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
     return finish("gtm_moe_ep_shared", nullptr, nullptr, st);
@@ -1249,6 +1279,7 @@ int launch_ep_experts(const GtmLayer& L, const GtmEpConfig& ep, const float* rec
     const Ws w = ep_ws(ep, ws);
     const int epr = NE / (int)ep.world;
     Plan pl;
+    memset(&pl, 0, sizeof(pl));
     pl.n = (int)n_recv; pl.src_div = 1;
     pl.idx = &recv_meta->expert; pl.stride = 2;
     pl.e0 = (int)ep.rank * epr; pl.ne = epr; pl.t_shared = 0;

@@ -88,14 +88,18 @@ class LocalExchange:
 # ---- the protocol --------------------------------------------------------------------------------
 
 def ep_layer(ops, exchange, x, hidden_out, **io_kw):
-    """One expert-parallel layer for this rank's tokens x -> hidden_out (see module docstring)."""
+    """One expert-parallel layer for this rank's tokens x -> hidden_out (see module docstring).
+    The shared expert is issued right after the dispatch: ops that own a second stream run it
+    there, overlapping the exchanges; the combine waits for it."""
+    import torch
     send_rows, send_meta, send_counts = ops.dispatch(x, **io_kw)
+    ops.shared(x, **io_kw)
     recv_counts = exchange.counts(send_counts)
-    s_split = [int(v) for v in send_counts.cpu().tolist()]
-    r_split = [int(v) for v in recv_counts.cpu().tolist()]
+    P = send_counts.numel()
+    both = [int(v) for v in torch.cat([send_counts.reshape(-1), recv_counts.reshape(-1)]).cpu().tolist()]  # one host trip
+    s_split, r_split = both[:P], both[P:]
     recv_rows = exchange.rows(send_rows, s_split, r_split)
     recv_meta = exchange.rows(send_meta, s_split, r_split)
-    ops.shared(x, **io_kw)
     ret_rows = ops.experts(recv_rows, recv_meta, sum(r_split))
     back = exchange.rows(ret_rows, r_split, s_split)
     ops.combine(x, hidden_out, back, **io_kw)
@@ -144,6 +148,10 @@ class CudaEpOps:
         self.send_meta = torch.empty(max_tokens * TOP_K, META_WORDS, dtype=torch.int32, device=device)
         self.send_counts = torch.empty(world, dtype=torch.int32, device=device)
         self.ret_rows = torch.empty(max_recv_rows, HIDDEN, device=device)
+        # the shared-expert phase runs on its own stream (it has its own workspace tiles)
+        self.side = torch.cuda.Stream(device=device)
+        self.ev_dispatch = torch.cuda.Event()
+        self.ev_shared = torch.cuda.Event()
 
     def _io(self, x, hidden_out=None, topk_idx=None, topk_w=None, logits=None, h1=None, h2=None, logit_bias=None,
             route_logits=None):
@@ -159,12 +167,16 @@ class CudaEpOps:
         check(lib().gtm_moe_ep_dispatch(C.byref(self.dims), C.byref(self.layer), C.byref(io), C.byref(self.cfg),
                                         ptr(self.send_rows), ptr(self.send_meta), ptr(self.send_counts),
                                         self.ws_ptr, self.ws_bytes, _stream()))
+        self.ev_dispatch.record()
         return self.send_rows[:n], self.send_meta[:n], self.send_counts
 
     def shared(self, x, **kw):
+        """On the side stream, after the dispatch (which wrote the dense views it reads)."""
         io = self._io(x, **kw)
+        self.side.wait_event(self.ev_dispatch)
         check(lib().gtm_moe_ep_shared(C.byref(self.dims), C.byref(self.layer), C.byref(io), C.byref(self.cfg),
-                                      self.ws_ptr, self.ws_bytes, _stream()))
+                                      self.ws_ptr, self.ws_bytes, _stream(self.side)))
+        self.ev_shared.record(self.side)
 
     def experts(self, recv_rows, recv_meta, n_recv: int):
         if n_recv > self.cfg.max_recv_rows:
@@ -179,6 +191,7 @@ class CudaEpOps:
     def combine(self, x, hidden_out, back_rows, **kw):
         io = self._io(x, hidden_out=hidden_out, **kw)
         back_rows = back_rows.contiguous()
+        self.torch.cuda.current_stream().wait_event(self.ev_shared)
         check(lib().gtm_moe_ep_combine(C.byref(self.dims), C.byref(self.layer), C.byref(io), C.byref(self.cfg),
                                        ptr(back_rows), self.ws_ptr, self.ws_bytes, _stream()))
 
