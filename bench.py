@@ -222,6 +222,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode30", choices=["decode30", "batch64", "prefill4096"])
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
+                    help="prefill4096 on N>1 GPUs: expert exchange over peer memory or NCCL all-to-all")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
@@ -421,16 +423,33 @@ def bench_tokens(args):
     out = torch.empty(T, D, device="cuda")
     idx_hist = torch.empty(n_sets, T, K, dtype=torch.int32, device="cuda")
 
+    # kernels of ours per step (the NCCL collectives not counted): views 1, routing 3 (count, scan,
+    # scatter), gather 1, grouped GEMMs 2, combine 1; expert parallelism adds the dispatch (NCCL:
+    # 2 kernels; peer memory: the token-count word) and the shared-expert pass (scan + 2 GEMMs)
+    launches = 8
     if expert_parallel:
         shard = ep.EpShardModel(0, rank, world)
-        ops = ep.CudaEpOps(shard.layer, rank, world, max_tokens=T, max_recv_rows=T_total * K)
-        xch = ep.NcclExchange()
         weights_gb = shard.weight_bytes() / 1e9
+        rl_c = [rl[j].contiguous() for j in range(n_sets)]
+        if args.ep == "peer":
+            ops = ep.PeerEpOps(shard.layer, rank, world, max_tokens=T)
+            ops.connect()
+            bar = ep.NcclBarrier()
+            launches = 12
 
-        def step(i, x=None, o=None):
-            j = i % n_sets
-            a = dict(kw, route_logits=rl[j].contiguous())
-            ep.ep_layer(ops, xch, xs[j] if x is None else x, out if o is None else o, topk_idx=idx_hist[j], **a)
+            def step(i, x=None, o=None):
+                j = i % n_sets
+                ep.ep_layer_peer(ops, bar, xs[j] if x is None else x, out if o is None else o,
+                                 topk_idx=idx_hist[j], route_logits=rl_c[j], **kw)
+        else:
+            ops = ep.CudaEpOps(shard.layer, rank, world, max_tokens=T, max_recv_rows=T_total * K)
+            xch = ep.NcclExchange()
+            launches = 13
+
+            def step(i, x=None, o=None):
+                j = i % n_sets
+                ep.ep_layer(ops, xch, xs[j] if x is None else x, out if o is None else o, topk_idx=idx_hist[j],
+                            route_logits=rl_c[j], **kw)
         check = ops.check
     else:
         model = gtmoe.SynthModel(1, seed=0)
@@ -526,17 +545,23 @@ def bench_tokens(args):
                                     else "config3: 4096 bf16 tokens through one MoE layer, uniform routing logits"),
                        "tokens_per_step": tokens_per_step, "weights_gb_per_gpu": weights_gb,
                        "parallelism": (f"ep{world}" if expert_parallel else ("replicas" if world > 1 else "single")),
+                       **({"ep_exchange": ("peer memory (CUDA IPC, NVLink loads/stores)" if args.ep == "peer"
+                                           else "NCCL all-to-all")} if expert_parallel else {}),
                        "l2": "4 token sets cycled; weights of touched experts 0.3-0.45 GB > L2"},
             "roofline": roof,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * D * xs.element_size(),
                     "d2h_bytes_per_step": T * D * 4},
-            "gpu_launches": args.steps * (11 if expert_parallel else 6),
+            "gpu_launches": args.steps * launches,
             "clocks": clk.summary(),
             "cpu_baseline": cb,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
+        if expert_parallel and args.ep == "peer":
+            torch.cuda.synchronize()
+            ops.close()
+            dist.barrier()
         dist.destroy_process_group()
     return 0
 

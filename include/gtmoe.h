@@ -311,6 +311,66 @@ GTM_API int gtm_moe_ep_combine(const GtmDims* dims, const GtmLayer* layer, const
 /* Reads back and clears the device-side error flag of an EP workspace (synchronises `stream`). */
 GTM_API int gtm_moe_ep_check(void* workspace_dev, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Expert-parallel MoE layer over peer memory. No reference counterpart. The ranks of one
+ * NVLink domain map each other's workspaces (gtm_ipc_* below, or any other peer mapping) and
+ * the kernels move the data themselves with plain peer loads and stores; there is no
+ * all-to-all and no host round trip. Every rank uses the same config (world, max_tokens;
+ * max_recv_rows is ignored: room for world * max_tokens * top_k rows is always reserved),
+ * so the workspaces have the same layout. One layer:
+ *   1. gtm_moe_ep_peer_dispatch  own tokens: views, router, top-k into the own workspace,
+ *                                and the own token count for the peers
+ *   2. gtm_moe_ep_peer_shared    own tokens: shared expert; may run on a second stream
+ *                                concurrently with phase 3 once phase 1 has completed
+ *      -- barrier: every rank has completed phase 1 --
+ *   3. gtm_moe_ep_peer_experts   this rank's experts over every rank's (token, slot) entries:
+ *                                the routing tables read the peers' top-k, the rows are read
+ *                                from the peers' workspaces, and each expert output row is
+ *                                stored into its token's rank's workspace (routing weight not
+ *                                applied); rows of one expert keep the source-rank-major entry
+ *                                order, so the results match gtm_moe_tokens on the whole batch
+ *      -- barrier: every rank has completed phase 3 --
+ *   4. gtm_moe_ep_peer_combine   own tokens: h2 = sum over the slots in router order of
+ *                                routing weight x expert output, layer tail (after phase 2)
+ * The barriers are the caller's (a stream-ordered one-element all-reduce over NCCL is
+ * enough: a kernel's peer stores are complete at system scope when it ends). The second
+ * barrier also keeps the next layer's phase 1 from overwriting rows a peer still reads.
+ * ------------------------------------------------------------------------------------- */
+#define GTM_EP_PEER_MAX_WORLD 8
+
+/* Every rank's workspace, indexed by rank, as mapped in this process (own one included). */
+typedef struct GtmEpPeers {
+    void* workspace_dev[GTM_EP_PEER_MAX_WORLD];
+} GtmEpPeers;
+
+/* Workspace of one rank (0 for unsupported dims or config: world must divide 128 and be at
+ * most GTM_EP_PEER_MAX_WORLD, world * max_tokens at most 65536). Zero it once before its first
+ * use (gtm_ipc_alloc returns it zeroed). */
+GTM_API size_t gtm_moe_ep_peer_workspace_bytes(const GtmDims* dims, const GtmEpConfig* ep);
+GTM_API int gtm_moe_ep_peer_dispatch(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                     const GtmEpConfig* ep, void* workspace_dev, size_t workspace_bytes,
+                                     void* stream);
+GTM_API int gtm_moe_ep_peer_shared(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                   const GtmEpConfig* ep, void* workspace_dev, size_t workspace_bytes,
+                                   void* stream);
+/* layer->experts_dev points at this rank's first expert; peers->workspace_dev[ep->rank] is the
+ * own workspace. */
+GTM_API int gtm_moe_ep_peer_experts(const GtmDims* dims, const GtmLayer* layer, const GtmEpConfig* ep,
+                                    const GtmEpPeers* peers, size_t workspace_bytes, void* stream);
+GTM_API int gtm_moe_ep_peer_combine(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                    const GtmEpConfig* ep, void* workspace_dev, size_t workspace_bytes,
+                                    void* stream);
+
+/* Device memory shared between the processes of one box (CUDA IPC; peer access is enabled
+ * when a handle is opened). gtm_ipc_alloc returns zeroed memory and its 64-byte handle;
+ * another process opens the handle to map the same memory. Close what was opened before the
+ * owner frees it. */
+#define GTM_IPC_HANDLE_BYTES 64
+GTM_API int gtm_ipc_alloc(size_t bytes, void** dev_ptr, uint8_t handle_out[GTM_IPC_HANDLE_BYTES]);
+GTM_API int gtm_ipc_open(const uint8_t handle[GTM_IPC_HANDLE_BYTES], void** dev_ptr);
+GTM_API int gtm_ipc_close(void* dev_ptr);
+GTM_API int gtm_ipc_free(void* dev_ptr);
+
 #ifdef __cplusplus
 }
 #endif

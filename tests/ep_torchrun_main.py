@@ -1,7 +1,9 @@
 """Launched by tests/test_ep_multigpu.py under torch.distributed.run: one process per GPU runs
-the expert-parallel layer over NCCL (gtmoe.ep.ep_layer + NcclExchange) on its share of 4096
-bf16 tokens with uniform routing logits; rank 0 gathers the outputs and compares them with the
-single-GPU path over all tokens (bit-identical) and the top-8 indices."""
+the expert-parallel layer on its share of 4096 bf16 tokens with uniform routing logits, over
+NCCL all-to-all (EP_MODE=nccl: gtmoe.ep.ep_layer + NcclExchange) or over peer memory
+(EP_MODE=peer: gtmoe.ep.ep_layer_peer + PeerEpOps, workspaces mapped through CUDA IPC); rank 0
+gathers the outputs and compares them with the single-GPU path over all tokens (bit-identical)
+and the top-8 indices. The layer runs twice, so the second call meets the first one's data."""
 import datetime
 import os
 import sys
@@ -28,11 +30,20 @@ def main():
     x = x32.view(T, D).to(torch.bfloat16)
     rl = torch.from_numpy(workloads.uniform_route_logits(T)).cuda()
     shard = ep.EpShardModel(0, rank, world)
-    ops = ep.CudaEpOps(shard.layer, rank, world, max_tokens=Tp, max_recv_rows=T * K)
+    mode = os.environ.get("EP_MODE", "nccl")
     out = torch.empty(Tp, D, device="cuda")
     idx = torch.empty(Tp, K, dtype=torch.int32, device="cuda")
     sl = slice(rank * Tp, (rank + 1) * Tp)
-    ep.ep_layer(ops, ep.NcclExchange(), x[sl], out, topk_idx=idx, route_logits=rl[sl])
+    if mode == "peer":
+        ops = ep.PeerEpOps(shard.layer, rank, world, max_tokens=Tp)
+        ops.connect()
+        bar = ep.NcclBarrier()
+        for _ in range(2):
+            ep.ep_layer_peer(ops, bar, x[sl], out, topk_idx=idx, route_logits=rl[sl])
+    else:
+        ops = ep.CudaEpOps(shard.layer, rank, world, max_tokens=Tp, max_recv_rows=T * K)
+        for _ in range(2):
+            ep.ep_layer(ops, ep.NcclExchange(), x[sl], out, topk_idx=idx, route_logits=rl[sl])
     ops.check()
     outs = [torch.empty_like(out) for _ in range(world)]
     idxs = [torch.empty_like(idx) for _ in range(world)]
@@ -48,10 +59,15 @@ def main():
         blk.check()
         got = torch.cat(outs)
         ok = torch.equal(torch.cat(idxs), ridx) and torch.equal(got, ref)
-        print(f"EP world={world}: top-8 equal and outputs bit-identical to one GPU: {ok}; "
+        print(f"EP {mode} world={world}: top-8 equal and outputs bit-identical to one GPU: {ok}; "
               f"max diff {float((got - ref).abs().max()):.3e}", flush=True)
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.broadcast(flag, 0)
+    if mode == "peer":
+        torch.cuda.synchronize()
+        dist.barrier()        # no rank still reads or writes a peer's workspace
+        ops.close()
+        dist.barrier()
     dist.destroy_process_group()
     sys.exit(0 if int(flag.item()) == 1 else 1)
 

@@ -89,3 +89,37 @@ def test_resident_layout_is_16k_aligned():
 @pytest.mark.parametrize("field,size", [("Layer", 8 + 24 + 16 + 72 + 48 + 8 + 8 + 72), ("DecodeIO", 9 * 8 + 8)])
 def test_struct_sizes(field, size):
     assert C.sizeof(getattr(gtmoe, field)) == size
+
+
+def test_ep_peer_config_bounds_and_argument_checks():
+    # peer-memory expert parallelism: world divides 128 and is at most 8; world x max_tokens <= 65536
+    L = gtmoe.lib()
+    d = gtmoe.default_dims()
+    sizes = {}
+    for world, max_tokens in [(1, 64), (2, 64), (8, 64), (8, 8192)]:
+        sizes[world, max_tokens] = L.gtm_moe_ep_peer_workspace_bytes(C.byref(d), C.byref(gtmoe.EpConfig(world, 0, max_tokens, 0)))
+        assert sizes[world, max_tokens] > 0, (world, max_tokens)
+    assert sizes[2, 64] > sizes[1, 64] and sizes[8, 64] > sizes[2, 64]
+    for world, rank, max_tokens in [(3, 0, 64), (16, 0, 64), (2, 2, 64), (8, 0, 8193), (2, 0, 0)]:
+        cfg = gtmoe.EpConfig(world, rank, max_tokens, 0)
+        assert L.gtm_moe_ep_peer_workspace_bytes(C.byref(d), C.byref(cfg)) == 0, (world, rank, max_tokens)
+    cfg = gtmoe.EpConfig(2, 0, 64, 0)
+    layer, io = gtmoe.Layer(), gtmoe.TokensIO()
+    assert L.gtm_moe_ep_peer_experts(C.byref(d), C.byref(layer), C.byref(cfg), None, 0, None) == gtmoe.ERR_INVALID
+    peers = gtmoe.EpPeers()
+    rc = L.gtm_moe_ep_peer_experts(C.byref(d), C.byref(layer), C.byref(cfg), C.byref(peers), 1 << 40, None)
+    assert rc == gtmoe.ERR_WORKSPACE and "gtm_moe_ep_peer_experts" in gtmoe.last_error()
+    rc = L.gtm_moe_ep_peer_dispatch(C.byref(d), C.byref(layer), C.byref(io), C.byref(cfg), C.c_void_p(4096), 16, None)
+    assert rc == gtmoe.ERR_WORKSPACE
+
+
+def test_ipc_argument_checks():
+    L = gtmoe.lib()
+    p = C.c_void_p()
+    h = (C.c_uint8 * gtmoe.IPC_HANDLE_BYTES)()
+    assert L.gtm_ipc_alloc(0, C.byref(p), h) == gtmoe.ERR_INVALID
+    assert L.gtm_ipc_alloc(256, None, h) == gtmoe.ERR_INVALID
+    assert L.gtm_ipc_open(None, C.byref(p)) == gtmoe.ERR_INVALID
+    assert L.gtm_ipc_close(None) == gtmoe.ERR_INVALID
+    assert L.gtm_ipc_free(None) == gtmoe.ERR_INVALID
+    assert C.sizeof(gtmoe.EpPeers) == 8 * gtmoe.EP_PEER_MAX_WORLD

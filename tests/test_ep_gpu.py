@@ -1,4 +1,4 @@
-"""GPU parity of the expert-parallel MoE layer (gtm_moe_ep_* phases).
+"""GPU parity of the expert-parallel MoE layer (gtm_moe_ep_* and gtm_moe_ep_peer_* phases).
 
 P ranks are emulated in one process on one GPU (gtmoe.ep.ep_layer_local: the same phases and
 the same split bookkeeping as the NCCL path, the all-to-all replaced by tensor slicing). Each
@@ -107,5 +107,106 @@ def test_ep_router_zipf_two_ranks(full_model, ref_layer):
     xs = x.cpu().numpy()
     for t in (0, 31, 63):
         ref = ref_layer.block(xs[t], logit_bias=bias)
+        assert np.array_equal(gidx[t], ref["idx"])
+        assert rel_max(got[t], ref["hidden"]) <= TOL
+
+
+# ---- expert parallelism over peer memory (gtm_moe_ep_peer_*) ---------------------------------------
+# The ranks are emulated in one process: every rank's workspace is device memory of this process,
+# so the kernels' "peer" loads and stores are local ones, but they follow the same pointers,
+# entry order and barriers (stream order here) as the multi-GPU run.
+
+def make_peer_ops(P, max_tokens):
+    shards = [ep.EpShardModel(0, r, P) for r in range(P)]
+    ops = [ep.PeerEpOps(shards[r].layer, r, P, max_tokens=max_tokens) for r in range(P)]
+    for o in ops:
+        o.connect_local(ops)
+    return shards, ops
+
+
+def run_peer(ops, xs, route_logits=None, logit_bias=None, h2=None):
+    """h2: list that receives the routed sums (combine input) of all ranks' tokens."""
+    P = len(ops)
+    outs = [torch.empty(x.shape[0], D, device="cuda") for x in xs]
+    idx = [torch.empty(x.shape[0], K, dtype=torch.int32, device="cuda") for x in xs]
+    h2s = [torch.empty(x.shape[0], D, device="cuda") for x in xs]
+    kw, off = [], 0
+    for r in range(P):
+        n = xs[r].shape[0]
+        d = {"topk_idx": idx[r], "h2": h2s[r] if h2 is not None else None}
+        if route_logits is not None:
+            d["route_logits"] = route_logits[off:off + n]
+        if logit_bias is not None:
+            d["logit_bias"] = logit_bias
+        kw.append(d)
+        off += n
+    ep.ep_layer_peer_local(ops, xs, outs, kw)
+    for o in ops:
+        o.check()
+    torch.cuda.synchronize()
+    if h2 is not None:
+        h2.append(torch.cat(h2s).cpu().numpy())
+    return torch.cat(outs).cpu().numpy(), torch.cat(idx).cpu().numpy().view(np.uint32)
+
+
+@pytest.mark.parametrize("P", [1, 2, 4, 8])
+def test_ep_peer_matches_single_gpu_and_oracle(full_model, ref_layer, P):
+    T = 1024
+    x32 = torch.empty(T * D, device="cuda")
+    gtmoe.synth_x(0, 0, T, x32)
+    x = x32.view(T, D).to(torch.bfloat16)
+    rl = torch.from_numpy(workloads.uniform_route_logits(T)).cuda()
+    _, ops = make_peer_ops(P, T // P)
+    try:
+        got, gidx = run_peer(ops, list(x.split(T // P)), route_logits=rl)
+    finally:
+        for o in ops:
+            o.close()
+    single, sidx = run_single(full_model, x, route_logits=rl)
+    assert np.array_equal(gidx, sidx)
+    assert np.array_equal(got, single), f"max diff {np.abs(got - single).max()}"
+    xs = x.float().cpu().numpy()
+    rls = rl.cpu().numpy()
+    for t in (0, (T // P) % T, T - 1):
+        ref = ref_layer.block(xs[t], route_logits=rls[t])
+        assert np.array_equal(gidx[t], ref["idx"])
+        assert rel_max(got[t], ref["hidden"]) <= TOL
+
+
+def test_ep_peer_ragged_ranks_and_stale_entries(full_model, ref_layer):
+    """Ranks with different token counts (one with none) after a call with full ranks: entries
+    past a rank's current count are stale and must be ignored. Each expert sees the same rows in
+    the same order as on one GPU, so the routed sum h2 is bit-identical; the shared expert runs
+    per rank, and a rank's token tiles of <= 64 rows take the stacked high/low operand (the
+    high and low products summed after the MMAs, not in one accumulator), so the layer output
+    agrees to rounding there."""
+    P, MT = 4, 128
+    counts = [100, 1, 37, 0]
+    n_all = P * MT
+    x32 = torch.empty(n_all * D, device="cuda")
+    gtmoe.synth_x(0, 0, n_all, x32)
+    x = x32.view(n_all, D)
+    bias = torch.from_numpy(workloads.zipf_logit_bias()).cuda()
+    _, ops = make_peer_ops(P, MT)
+    try:
+        full_got, _ = run_peer(ops, list(x.split(MT)), logit_bias=bias)
+        xr = x[:sum(counts)]
+        h2 = []
+        got, gidx = run_peer(ops, list(xr.split(counts)), logit_bias=bias, h2=h2)
+    finally:
+        for o in ops:
+            o.close()
+    single_full, _ = run_single(full_model, x, logit_bias=bias)
+    assert np.array_equal(full_got, single_full)
+    sh2 = torch.empty(sum(counts), D, device="cuda")
+    single, sidx = run_single(full_model, xr, logit_bias=bias, h2=sh2)
+    assert np.array_equal(gidx, sidx)
+    assert np.array_equal(h2[0], sh2.cpu().numpy())
+    assert np.array_equal(got[:counts[0]], single[:counts[0]])   # rank 0: > 64 rows in both
+    assert rel_max(got, single) <= 1e-5
+    xs = xr.cpu().numpy()
+    b = bias.cpu().numpy()
+    for t in (0, counts[0], counts[0] + counts[1] + counts[2] - 1):
+        ref = ref_layer.block(xs[t], logit_bias=b)
         assert np.array_equal(gidx[t], ref["idx"])
         assert rel_max(got[t], ref["hidden"]) <= TOL

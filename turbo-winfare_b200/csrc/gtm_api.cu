@@ -348,8 +348,10 @@ static int ep_common(const char* fn, const GtmDims* dims, const GtmLayer* layer,
     return check_layer(fn, *layer);
 }
 
-static int ep_io(const char* fn, const GtmTokensIO* io, const GtmEpConfig* ep, bool need_out) {
+// allow_empty: a rank with no tokens in this call still takes part (peer-memory phases)
+static int ep_io(const char* fn, const GtmTokensIO* io, const GtmEpConfig* ep, bool need_out, bool allow_empty = false) {
     if (!io) return set_error(GTM_ERR_INVALID, "%s: null io", fn);
+    if (allow_empty && io->num_tokens == 0) return GTM_OK;
     if (io->num_tokens == 0 || io->num_tokens > ep->max_tokens)
         return set_error(GTM_ERR_INVALID, "%s: num_tokens=%u (1..max_tokens %u)", fn, io->num_tokens, ep->max_tokens);
     if ((io->x_dev == nullptr) == (io->x_bf16_dev == nullptr))
@@ -394,7 +396,7 @@ GTM_API int gtm_moe_ep_shared(const GtmDims* dims, const GtmLayer* layer, const 
     int sms = 0;
     if (!rc) rc = sm_count(fn, &sms);
     if (rc) return rc;
-    rc = launch_ep_shared(*layer, *io, *ep, ws, (cudaStream_t)stream, sms);
+    rc = launch_ep_shared(*layer, *io, *ep, ws, (cudaStream_t)stream, sms, false);
     if (rc == GTM_OK) clear_error();
     return rc;
 }
@@ -434,6 +436,135 @@ GTM_API int gtm_moe_ep_check(void* ws, void* stream) {
     const int rc = tokens_check(ws, (cudaStream_t)stream);
     if (rc == GTM_OK) clear_error();
     return rc;
+}
+
+// ---- expert parallelism over peer memory --------------------------------------------------------
+static bool peer_config_ok(const GtmEpConfig* ep) {
+    return ep && ep->world >= 1 && ep->world <= GTM_EP_PEER_MAX_WORLD && 128 % ep->world == 0 &&
+           ep->rank < ep->world && ep->max_tokens >= 1 && (uint64_t)ep->world * ep->max_tokens <= kMaxTokens;
+}
+
+static int peer_common(const char* fn, const GtmDims* dims, const GtmLayer* layer, const GtmEpConfig* ep,
+                       const void* ws, size_t ws_bytes) {
+    if (!dims || !layer || !ep) return set_error(GTM_ERR_INVALID, "%s: null argument", fn);
+    if (!dims_supported(dims))
+        return set_error(GTM_ERR_UNSUPPORTED, "%s: built for hidden 2816, moe 704, ffn 2112, 128 experts, top-8", fn);
+    if (!peer_config_ok(ep))
+        return set_error(GTM_ERR_INVALID,
+                         "%s: bad EP config (world %u divides 128 and is at most %d, rank %u < world, "
+                         "world x max_tokens %u at most %u)", fn, ep->world, GTM_EP_PEER_MAX_WORLD, ep->rank,
+                         ep->max_tokens, kMaxTokens);
+    const size_t need = ep_peer_workspace_bytes(ep->world, ep->max_tokens);
+    if (!ws || ws_bytes < need || !aligned(ws, 256))
+        return set_error(GTM_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-byte aligned", fn, need);
+    return check_layer(fn, *layer);
+}
+
+GTM_API size_t gtm_moe_ep_peer_workspace_bytes(const GtmDims* dims, const GtmEpConfig* ep) {
+    if (!dims || !dims_supported(dims) || !peer_config_ok(ep)) return 0;
+    return ep_peer_workspace_bytes(ep->world, ep->max_tokens);
+}
+
+GTM_API int gtm_moe_ep_peer_dispatch(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                     const GtmEpConfig* ep, void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_peer_dispatch";
+    int rc = peer_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (!rc) rc = ep_io(fn, io, ep, false, true);
+    if (rc) return rc;
+    rc = launch_ep_peer_dispatch(*dims, *layer, *io, *ep, ws, (cudaStream_t)stream);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_ep_peer_shared(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                   const GtmEpConfig* ep, void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_peer_shared";
+    int rc = peer_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (!rc) rc = ep_io(fn, io, ep, false, true);
+    int sms = 0;
+    if (!rc) rc = sm_count(fn, &sms);
+    if (rc) return rc;
+    if (io->num_tokens == 0) { clear_error(); return GTM_OK; }
+    rc = launch_ep_shared(*layer, *io, *ep, ws, (cudaStream_t)stream, sms, true);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_ep_peer_experts(const GtmDims* dims, const GtmLayer* layer, const GtmEpConfig* ep,
+                                    const GtmEpPeers* peers, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_peer_experts";
+    if (!peers || !ep) return set_error(GTM_ERR_INVALID, "%s: null argument", fn);
+    int rc = peer_common(fn, dims, layer, ep, ep->rank < GTM_EP_PEER_MAX_WORLD ? peers->workspace_dev[ep->rank] : nullptr,
+                         ws_bytes);
+    if (rc) return rc;
+    for (uint32_t s = 0; s < ep->world; ++s)
+        if (!peers->workspace_dev[s] || !aligned(peers->workspace_dev[s], 256))
+            return set_error(GTM_ERR_INVALID, "%s: workspace of rank %u is null or not 256-byte aligned", fn, s);
+    int sms = 0;
+    if ((rc = sm_count(fn, &sms))) return rc;
+    rc = launch_ep_peer_experts(*layer, *ep, peers->workspace_dev, (cudaStream_t)stream, sms);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_moe_ep_peer_combine(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
+                                    const GtmEpConfig* ep, void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_moe_ep_peer_combine";
+    int rc = peer_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (!rc) rc = ep_io(fn, io, ep, true, true);
+    if (rc) return rc;
+    if (io->num_tokens == 0) { clear_error(); return GTM_OK; }
+    rc = launch_ep_peer_combine(*dims, *layer, *io, *ep, ws, (cudaStream_t)stream);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+// ---- device memory shared between processes (CUDA IPC) ------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == GTM_IPC_HANDLE_BYTES, "IPC handle size");
+
+GTM_API int gtm_ipc_alloc(size_t bytes, void** dev_ptr, uint8_t handle_out[GTM_IPC_HANDLE_BYTES]) {
+    if (!dev_ptr || !handle_out || bytes == 0) return set_error(GTM_ERR_INVALID, "gtm_ipc_alloc: bad argument");
+    *dev_ptr = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return set_cuda_error("gtm_ipc_alloc", e);
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    *dev_ptr = p;
+    clear_error();
+    return GTM_OK;
+}
+
+GTM_API int gtm_ipc_open(const uint8_t handle[GTM_IPC_HANDLE_BYTES], void** dev_ptr) {
+    if (!handle || !dev_ptr) return set_error(GTM_ERR_INVALID, "gtm_ipc_open: null argument");
+    *dev_ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return set_cuda_error("gtm_ipc_open", e);
+    clear_error();
+    return GTM_OK;
+}
+
+GTM_API int gtm_ipc_close(void* dev_ptr) {
+    if (!dev_ptr) return set_error(GTM_ERR_INVALID, "gtm_ipc_close: null pointer");
+    const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    if (e != cudaSuccess) return set_cuda_error("gtm_ipc_close", e);
+    clear_error();
+    return GTM_OK;
+}
+
+GTM_API int gtm_ipc_free(void* dev_ptr) {
+    if (!dev_ptr) return set_error(GTM_ERR_INVALID, "gtm_ipc_free: null pointer");
+    const cudaError_t e = cudaFree(dev_ptr);
+    if (e != cudaSuccess) return set_cuda_error("gtm_ipc_free", e);
+    clear_error();
+    return GTM_OK;
 }
 
 }  // extern "C"

@@ -26,11 +26,18 @@ size_t ep_workspace_bytes(uint32_t max_tokens, uint32_t max_recv);
 int launch_ep_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
                        float* send_rows, GtmEpMeta* send_meta, int32_t* send_counts, void* ws, cudaStream_t st);
 int launch_ep_shared(const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep, void* ws, cudaStream_t st,
-                     int num_sms);
+                     int num_sms, bool peer);
 int launch_ep_experts(const GtmLayer& L, const GtmEpConfig& ep, const float* recv_rows, const GtmEpMeta* recv_meta,
                       uint32_t n_recv, float* ret_rows, void* ws, cudaStream_t st, int num_sms);
 int launch_ep_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
                       const float* ret_rows, void* ws, cudaStream_t st);
+size_t ep_peer_workspace_bytes(uint32_t world, uint32_t max_tokens);
+int launch_ep_peer_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
+                            void* ws, cudaStream_t st);
+int launch_ep_peer_experts(const GtmLayer& L, const GtmEpConfig& ep, void* const* peer_ws, cudaStream_t st,
+                           int num_sms);
+int launch_ep_peer_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
+                           void* ws, cudaStream_t st);
 
 // generic kernels (gtm_kernels.cu); arguments already validated
 void k_gemv_exact(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,

@@ -235,6 +235,7 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
 // 2. routing tables and tile lists
 // ================================================================================================
 constexpr int kMaxPeers = 8;   // ranks of a peer-memory expert-parallel group (NVLink domain of one box)
+static_assert(kMaxPeers == GTM_EP_PEER_MAX_WORLD, "peer group size");
 
 struct RouteArgs {
     int n;                   // routed entries (0: shared tiles only)
@@ -445,6 +446,42 @@ __global__ void __launch_bounds__(128) tok_gather(const __half* routed_hl, const
     }
 }
 
+// Peer-memory expert parallelism: row r of this rank's experts is global entry perm_src[r] =
+// source rank s x per_src + (token x 8 + slot), gathered from rank s's routed views over NVLink
+// (plain peer loads). Each thread issues all of its 16-byte loads of a row before its stores.
+struct PeerGatherArgs {
+    const __half* routed[kMaxPeers];   // every rank's routed views (high row, low row per token)
+    int per_src;
+    const int* perm_src;
+    const int* nrows;                  // rows routed to this rank (written by the routing scan)
+    __half* xhi;
+    __half* xlo;
+};
+
+__global__ void __launch_bounds__(128) tok_gather_peer(const __grid_constant__ PeerGatherArgs A) {
+    constexpr int NC = (D / 8 + 127) / 128;
+    const int n = *A.nrows;
+    for (int row = blockIdx.x; row < n; row += gridDim.x) {
+        const int i = A.perm_src[row], s = i / A.per_src, t = (i - s * A.per_src) / TOPK;
+        const uint4* src = reinterpret_cast<const uint4*>(A.routed[s] + (size_t)t * 2 * D);
+        uint4 h[NC], l[NC];
+#pragma unroll
+        for (int v = 0; v < NC; ++v) {
+            const int c = threadIdx.x + 128 * v;
+            if (c < D / 8) { h[v] = src[c]; l[v] = src[D / 8 + c]; }
+        }
+        uint4* dh = reinterpret_cast<uint4*>(A.xhi + (size_t)row * D);
+        uint4* dl = reinterpret_cast<uint4*>(A.xlo + (size_t)row * D);
+#pragma unroll
+        for (int v = 0; v < NC; ++v) {
+            const int c = threadIdx.x + 128 * v;
+            if (c < D / 8) { dh[c] = h[v]; dl[c] = l[v]; }
+        }
+    }
+}
+
+__global__ void tok_set_word(int* p, int v) { *p = v; }
+
 // ================================================================================================
 // 4/5. grouped GEMM
 // ================================================================================================
@@ -467,8 +504,20 @@ struct GemmArgs {
     __half* act_s_hi; __half* act_s_lo;
     float* out_r; float* out_s;           // mode 1 outputs [rows][D]
     const int* out_index;                 // mode 1: output row of each routed row (null: same row)
+    // mode 1, peer-memory expert parallelism (per_src > 0): output row o of a routed row goes to
+    // rank o / per_src's return region, row o % per_src (a peer store over NVLink)
+    int per_src;
+    float* out_peer[kMaxPeers];
     int* err;
 };
+
+__device__ __forceinline__ float* remap_row(const GemmArgs& A, int orow) {
+    if (A.per_src > 0) {
+        const int s = orow / A.per_src;
+        return A.out_peer[s] + (size_t)(orow - s * A.per_src) * D;
+    }
+    return A.out_r + (size_t)orow * D;
+}
 
 // 8 int4 (low nibble first) -> 8 fp16 w = q * s + b in the order (0,4,1,5,2,6,3,7).
 __device__ __forceinline__ uint4 dq8(uint32_t w, uint32_t s2, uint32_t b2) {
@@ -779,11 +828,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
             const int rows = ti.t.rows, row0 = ti.t.row0;
             // mode 1, expert parallelism: output row of token (chunk j, lane), loaded before the wait
             const bool remap = MODE == 1 && ti.routed && A.out_index != nullptr;
-            int ol[NT / 64];
+            float* ol[NT / 64];
 #pragma unroll
             for (int j = 0; j < NT / 64; ++j) {
                 const int tl = 32 * c + 64 * j + lane;
-                ol[j] = remap && tl < rows ? A.out_index[row0 + tl] : row0 + tl;
+                ol[j] = remap && tl < rows ? remap_row(A, A.out_index[row0 + tl]) : nullptr;
             }
             // warp-uniform outcome: tcgen05.ld is warp-collective
             if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[0], acc_it & 1, abort_flag, kWaitNs))) break;
@@ -807,8 +856,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
                         if (remap) {
 #pragma unroll
                             for (int u = 0; u < 32; ++u) {
-                                const int orow = __shfl_sync(0xffffffffu, ol[j], u);
-                                if (c0 + u < rows) out[(size_t)orow * D] = __uint_as_float(v[u]);
+                                float* orow = reinterpret_cast<float*>(
+                                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ol[j]), u));
+                                if (c0 + u < rows) orow[f] = __uint_as_float(v[u]);
                             }
                         } else {
                             float* o = out + (size_t)(row0 + c0) * D;
@@ -855,6 +905,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
             }
         }
     }
+    // peer stores complete at system scope before this kernel ends (the ranks' barrier follows)
+    if (MODE == 1 && A.per_src > 0) __threadfence_system();
     tc::tc_fence_before();
     __syncthreads();
     if (tid == 0 && *abort_flag) atomicExch(A.err, 2);
@@ -873,7 +925,7 @@ struct CombineArgs {
     int T;
     const float* x_f32;
     const uint16_t* x_bf16;
-    const int* pos;           // [T][8]
+    const int* pos;           // [T][8] row of each (token, slot) in out_r (null: token x 8 + slot)
     const float* w;           // [T][8] routing weights
     const float* out_r;       // [8T][D], expert outputs (routing weight not applied)
     const float* out_s;       // [T][D]
@@ -915,7 +967,10 @@ __global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ Combin
     int p[TOPK];
     float wk[TOPK];
 #pragma unroll
-    for (int k = 0; k < TOPK; ++k) { p[k] = A.pos[(size_t)t * TOPK + k]; wk[k] = A.w[(size_t)t * TOPK + k]; }
+    for (int k = 0; k < TOPK; ++k) {
+        p[k] = A.pos ? A.pos[(size_t)t * TOPK + k] : t * TOPK + k;
+        wk[k] = A.w[(size_t)t * TOPK + k];
+    }
     const float4* outs = reinterpret_cast<const float4*>(A.out_s) + (size_t)t * (D / 4);
     float sv[CV][4], hv[CV][4], xv[CV][4];
     double a = 0.0, b = 0.0;
@@ -988,14 +1043,19 @@ __global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ Combin
 // ================================================================================================
 struct WsLayout {
     size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, stiles0, stiles1, sn_tiles, xhi, xlo, act_r_hi,
-        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, total;
+        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, hdr, ret, total;
 };
+
+// single GPU; expert parallelism with the caller's all-to-all; expert parallelism over peer memory
+enum WsMode { WS_SINGLE, WS_EP, WS_PEER };
 
 static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
 // T: own tokens; R: routed rows through the experts (T * top_k on one GPU, the received rows
-// with expert parallelism); ep: room for the dispatch tables.
-static WsLayout ws_layout(uint32_t T, uint32_t Rrows, bool ep) {
+// with expert parallelism, every rank's entries (world * T * top_k) over peer memory).
+// Over peer memory every rank has the same layout, so a peer's regions sit at the same offsets.
+static WsLayout ws_layout(uint32_t T, uint32_t Rrows, WsMode mode) {
+    const bool ep = mode != WS_SINGLE;
     WsLayout W;
     const size_t E8 = (size_t)T * TOPK, R = Rrows;
     const size_t ntr = R / NT + NE, nts = (T + NT - 1) / NT;   // bounds on routed / shared token tiles
@@ -1025,16 +1085,27 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, bool ep) {
     W.act_s_lo = take((size_t)T * FS * 2);
     W.out_r = ep ? 0 : take(R * D * 4);
     W.out_s = take((size_t)T * D * 4);
-    W.send_pos = ep ? take(E8 * 4) : 0;
-    W.send_src = ep ? take(E8 * 4) : 0;
+    W.send_pos = mode == WS_EP ? take(E8 * 4) : 0;
+    W.send_src = mode == WS_EP ? take(E8 * 4) : 0;
+    // peer memory: [0] own token count (read by the peers' routing), [1] rows routed here;
+    // ret: [T * top_k][D] expert outputs of the own entries, stored by the experts' owners
+    W.hdr = mode == WS_PEER ? take(2 * 4) : 0;
+    W.ret = mode == WS_PEER ? take(E8 * D * 4) : 0;
     W.total = o;
     return W;
 }
 
 }  // namespace tok
 
-size_t tokens_workspace_bytes(uint32_t max_tokens) { return tok::ws_layout(max_tokens, max_tokens * tok::TOPK, false).total; }
-size_t ep_workspace_bytes(uint32_t max_tokens, uint32_t max_recv) { return tok::ws_layout(max_tokens, max_recv, true).total; }
+size_t tokens_workspace_bytes(uint32_t max_tokens) {
+    return tok::ws_layout(max_tokens, max_tokens * tok::TOPK, tok::WS_SINGLE).total;
+}
+size_t ep_workspace_bytes(uint32_t max_tokens, uint32_t max_recv) {
+    return tok::ws_layout(max_tokens, max_recv, tok::WS_EP).total;
+}
+size_t ep_peer_workspace_bytes(uint32_t world, uint32_t max_tokens) {
+    return tok::ws_layout(max_tokens, world * max_tokens * tok::TOPK, tok::WS_PEER).total;
+}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1121,6 +1192,13 @@ struct Plan {
     const int* out_index;         // mode 1 output row of each expert-ordered row (null: same)
     float* out_r;                 // mode 1 routed output rows
     bool own_tiles;               // shared-expert-only plan: tile lists in the stiles* regions
+    // peer-memory expert parallelism (nsrc > 0): entry i is entry i % per_src of rank i / per_src,
+    // read from that rank's workspace; its result goes to that rank's return region
+    int nsrc, per_src;
+    const uint32_t* src_idx[kMaxPeers];
+    const int* src_ntok[kMaxPeers];
+    const __half* src_routed[kMaxPeers];
+    float* src_ret[kMaxPeers];
 };
 
 int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaStream_t st) {
@@ -1156,11 +1234,22 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     ra.tiles0 = w.p<Tile>(pl.own_tiles ? W.stiles0 : W.tiles0);
     ra.tiles1 = w.p<Tile>(pl.own_tiles ? W.stiles1 : W.tiles1);
     ra.n_tiles = w.p<int>(pl.own_tiles ? W.sn_tiles : W.n_tiles);
+    ra.nsrc = pl.nsrc; ra.per_src = pl.per_src;
+    for (int s = 0; s < pl.nsrc; ++s) { ra.src_idx[s] = pl.src_idx[s]; ra.src_ntok[s] = pl.src_ntok[s]; }
+    ra.nrows = pl.nsrc > 0 ? w.p<int>(W.hdr) + 1 : nullptr;
     if (ra.nchunks > 0) tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
     tok_route_scan<<<1, 1024, 0, st>>>(ra);
     if (ra.nchunks > 0) tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
-    if (pl.n > 0)
+    if (pl.nsrc > 0) {
+        PeerGatherArgs ga;
+        memset(&ga, 0, sizeof(ga));
+        for (int s = 0; s < pl.nsrc; ++s) ga.routed[s] = pl.src_routed[s];
+        ga.per_src = pl.per_src; ga.perm_src = ra.perm_src; ga.nrows = ra.nrows;
+        ga.xhi = w.p<__half>(W.xhi); ga.xlo = w.p<__half>(W.xlo);
+        tok_gather_peer<<<(unsigned)num_sms * 8, 128, 0, st>>>(ga);
+    } else if (pl.n > 0) {
         tok_gather<<<(unsigned)pl.n, 128, 0, st>>>(pl.src_hl, ra.perm_src, w.p<__half>(W.xhi), w.p<__half>(W.xlo));
+    }
 
     cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
@@ -1193,6 +1282,8 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     g1.k_r = FE; g1.k_s = FS; g1.rows_r = D; g1.rows_s = D;
     g1.out_r = pl.out_r; g1.out_s = w.p<float>(W.out_s);
     g1.out_index = pl.out_index;
+    g1.per_src = pl.nsrc > 0 ? pl.per_src : 0;
+    for (int s = 0; s < pl.nsrc; ++s) g1.out_peer[s] = pl.src_ret[s];
     g1.err = w.p<int>(0);
     grouped_gemm<1><<<num_sms, THREADS, SMEM_BYTES, st>>>(g1);
     return GTM_OK;
@@ -1223,7 +1314,7 @@ int finish(const char* what, const GtmTokensIO* io, const Ws* w, cudaStream_t st
 int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, void* ws, size_t ws_bytes,
                   cudaStream_t st, int num_sms) {
     const uint32_t T = io.num_tokens;
-    const Ws w{ws_layout(T, T * TOPK, false), static_cast<uint8_t*>(ws)};
+    const Ws w{ws_layout(T, T * TOPK, WS_SINGLE), static_cast<uint8_t*>(ws)};
     if (ws_bytes < w.W.total) return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes", w.W.total);
     launch_views(dims, L, io, w, st);
     Plan pl;
@@ -1242,7 +1333,10 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
 // the regions that carry data from one phase to the next (views, dispatch tables, shared-expert
 // output) are the same in all of them.
 static Ws ep_ws(const GtmEpConfig& ep, void* ws) {
-    return Ws{ws_layout(ep.max_tokens, ep.max_recv_rows, true), static_cast<uint8_t*>(ws)};
+    return Ws{ws_layout(ep.max_tokens, ep.max_recv_rows, WS_EP), static_cast<uint8_t*>(ws)};
+}
+static Ws peer_ws(const GtmEpConfig& ep, void* ws) {
+    return Ws{ws_layout(ep.max_tokens, ep.world * ep.max_tokens * TOPK, WS_PEER), static_cast<uint8_t*>(ws)};
 }
 
 int launch_ep_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
@@ -1261,8 +1355,8 @@ int launch_ep_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO
 }
 
 int launch_ep_shared(const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep, void* ws, cudaStream_t st,
-                     int num_sms) {
-    const Ws w = ep_ws(ep, ws);
+                     int num_sms, bool peer) {
+    const Ws w = peer ? peer_ws(ep, ws) : ep_ws(ep, ws);
     Plan pl;
     memset(&pl, 0, sizeof(pl));
     pl.n = 0; pl.src_div = 1; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
@@ -1294,6 +1388,44 @@ int launch_ep_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO&
     const Ws w = ep_ws(ep, ws);
     launch_combine(dims, L, io, w, w.p<int>(w.W.send_pos), ret_rows, st);
     return finish("gtm_moe_ep_combine", nullptr, nullptr, st);
+}
+
+// ---- expert parallelism over peer memory -------------------------------------------------------
+int launch_ep_peer_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
+                            void* ws, cudaStream_t st) {
+    const Ws w = peer_ws(ep, ws);
+    if (io.num_tokens > 0) launch_views(dims, L, io, w, st);   // a rank may have no tokens in a call
+    tok_set_word<<<1, 1, 0, st>>>(w.p<int>(w.W.hdr), (int)io.num_tokens);
+    return finish("gtm_moe_ep_peer_dispatch", &io, &w, st);
+}
+
+int launch_ep_peer_experts(const GtmLayer& L, const GtmEpConfig& ep, void* const* peer_ws_dev, cudaStream_t st,
+                           int num_sms) {
+    const Ws w = peer_ws(ep, peer_ws_dev[ep.rank]);
+    const int P = (int)ep.world, epr = NE / P;
+    Plan pl;
+    memset(&pl, 0, sizeof(pl));
+    pl.nsrc = P; pl.per_src = (int)ep.max_tokens * TOPK;
+    pl.n = P * pl.per_src; pl.src_div = 1; pl.stride = 1;
+    pl.e0 = (int)ep.rank * epr; pl.ne = epr; pl.t_shared = 0;
+    pl.out_index = w.p<int>(w.W.perm_src);
+    for (int s = 0; s < P; ++s) {
+        const Ws ps{w.W, static_cast<uint8_t*>(peer_ws_dev[s])};
+        pl.src_idx[s] = ps.p<uint32_t>(w.W.idx);
+        pl.src_ntok[s] = ps.p<int>(w.W.hdr);
+        pl.src_routed[s] = ps.p<__half>(w.W.routed);
+        pl.src_ret[s] = ps.p<float>(w.W.ret);
+    }
+    const int rc = run_gemms(L, w, pl, num_sms, st);
+    if (rc) return rc;
+    return finish("gtm_moe_ep_peer_experts", nullptr, nullptr, st);
+}
+
+int launch_ep_peer_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
+                           void* ws, cudaStream_t st) {
+    const Ws w = peer_ws(ep, ws);
+    launch_combine(dims, L, io, w, nullptr, w.p<float>(w.W.ret), st);
+    return finish("gtm_moe_ep_peer_combine", nullptr, nullptr, st);
 }
 
 int tokens_check(void* ws, cudaStream_t st) {

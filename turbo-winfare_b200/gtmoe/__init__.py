@@ -77,6 +77,14 @@ class EpConfig(C.Structure):
                 ("max_recv_rows", C.c_uint32)]
 
 
+EP_PEER_MAX_WORLD = 8
+IPC_HANDLE_BYTES = 64
+
+
+class EpPeers(C.Structure):
+    _fields_ = [("workspace_dev", C.c_void_p * EP_PEER_MAX_WORLD)]
+
+
 _lib = None
 
 # (name, restype, argtypes) for every entry point in include/gtmoe.h and include/gtmoe_synth.h
@@ -120,6 +128,19 @@ SIGNATURES = {
     "gtm_moe_ep_combine": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
                                 _P, _P, _SZ, _P]),
     "gtm_moe_ep_check": (_I, [_P, _P]),
+    "gtm_moe_ep_peer_workspace_bytes": (_SZ, [C.POINTER(Dims), C.POINTER(EpConfig)]),
+    "gtm_moe_ep_peer_dispatch": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
+                                      _P, _SZ, _P]),
+    "gtm_moe_ep_peer_shared": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
+                                    _P, _SZ, _P]),
+    "gtm_moe_ep_peer_experts": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(EpConfig), C.POINTER(EpPeers),
+                                     _SZ, _P]),
+    "gtm_moe_ep_peer_combine": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
+                                     _P, _SZ, _P]),
+    "gtm_ipc_alloc": (_I, [_SZ, C.POINTER(_P), _P]),
+    "gtm_ipc_open": (_I, [_P, C.POINTER(_P)]),
+    "gtm_ipc_close": (_I, [_P]),
+    "gtm_ipc_free": (_I, [_P]),
     "gtm_synth_expert_layout": (_I, [_U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_resident_layout": (_I, [_U32, _U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_experts": (_I, [_U64, _U32, _U32, _U32, _U32, _U32, _P, _P]),

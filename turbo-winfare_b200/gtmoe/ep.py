@@ -17,13 +17,25 @@ Rank r of P owns experts [r*E/P, (r+1)*E/P) and its own tokens. One layer:
 `NcclExchange` (torch.distributed) and `CudaEpOps` (the C ABI); the CPU tests drive the same
 function with gloo and stand-in ops. The reference has no multi-GPU path; this replaces its
 token-at-a-time prefill (src/runner.cpp:845-854) for a layer sharded over GPUs.
+
+Over peer memory (`PeerEpOps`, `ep_layer_peer`) the ranks map each other's workspaces (CUDA
+IPC) and the kernels move the rows themselves: the experts phase reads every rank's top-8 and
+routed rows with plain NVLink loads and stores each expert output row into its token's rank.
+The only collectives are two one-element all-reduces used as stream-ordered barriers:
+
+  1. dispatch   own tokens: views, router, top-k, own token count (gtm_moe_ep_peer_dispatch)
+  2. shared     on a second stream (gtm_moe_ep_peer_shared)
+     -- barrier --
+  3. experts    this rank's experts over all ranks' entries (gtm_moe_ep_peer_experts)
+     -- barrier --
+  4. combine    after the shared expert (gtm_moe_ep_peer_combine)
 """
 from __future__ import annotations
 
 import ctypes as C
 
-from . import (ERR_UNSUPPORTED, EXPERTS, HIDDEN, MOE_INTER, TOP_K, EpConfig, GtmError, Layer, TokensIO, _stream,
-               check, default_dims, expert_layout, lib, ptr, resident_layout)
+from . import (ERR_UNSUPPORTED, EXPERTS, HIDDEN, IPC_HANDLE_BYTES, MOE_INTER, TOP_K, EpConfig, EpPeers, GtmError,
+               Layer, TokensIO, _stream, check, default_dims, expert_layout, lib, ptr, resident_layout)
 
 
 META_WORDS = 2   # GtmEpMeta = (uint32 expert, float weight)
@@ -194,6 +206,134 @@ class CudaEpOps:
         self.torch.cuda.current_stream().wait_event(self.ev_shared)
         check(lib().gtm_moe_ep_combine(C.byref(self.dims), C.byref(self.layer), C.byref(io), C.byref(self.cfg),
                                        ptr(back_rows), self.ws_ptr, self.ws_bytes, _stream()))
+
+    def check(self):
+        check(lib().gtm_moe_ep_check(self.ws_ptr, _stream()))
+
+
+# ---- peer memory --------------------------------------------------------------------------------
+
+class NcclBarrier:
+    """Stream-ordered barrier of the peer protocol: a one-element all-reduce on the current
+    stream (NCCL; gloo on CPU). Work queued after it on this stream runs once every rank has
+    queued and finished the work before its own call."""
+
+    def __init__(self, group=None, device="cuda"):
+        import torch
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.flag = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def __call__(self):
+        self.dist.all_reduce(self.flag, group=self.group)
+
+
+def ep_layer_peer(ops, barrier, x, hidden_out, **io_kw):
+    """One expert-parallel layer over peer memory (module docstring, second protocol)."""
+    ops.dispatch(x, **io_kw)
+    ops.shared(x, **io_kw)
+    barrier()
+    ops.experts()
+    barrier()
+    ops.combine(x, hidden_out, **io_kw)
+
+
+def ep_layer_peer_local(ops_per_rank, xs, outs, io_kw_per_rank=None):
+    """The peer protocol with P ranks emulated in one process on one GPU: the workspaces are
+    plain device memory of this process and the phases run rank after rank on one stream, so
+    stream order stands in for the barriers."""
+    P = len(ops_per_rank)
+    kw = io_kw_per_rank or [{} for _ in range(P)]
+    for r in range(P):
+        ops_per_rank[r].dispatch(xs[r], **kw[r])
+        ops_per_rank[r].shared(xs[r], **kw[r])
+    for r in range(P):
+        ops_per_rank[r].experts()
+    for r in range(P):
+        ops_per_rank[r].combine(xs[r], outs[r], **kw[r])
+
+
+class PeerEpOps:
+    """This rank's peer-memory EP phases through libgtmoe's C ABI. The workspace is allocated
+    for CUDA IPC (zeroed); `connect` exchanges the handles over a process group and maps the
+    peers' workspaces, `connect_local` takes the workspaces of ranks emulated in this process."""
+
+    def __init__(self, layer: Layer, rank: int, world: int, max_tokens: int, device: str = "cuda"):
+        import torch
+        self.torch = torch
+        self.layer = layer
+        self.rank, self.world = rank, world
+        self.dims = default_dims()
+        self.cfg = EpConfig(world, rank, max_tokens, 0)
+        n = lib().gtm_moe_ep_peer_workspace_bytes(C.byref(self.dims), C.byref(self.cfg))
+        if n == 0:
+            raise GtmError(ERR_UNSUPPORTED, f"peer EP workspace size query failed ({world=}, {max_tokens=})")
+        self.ws_bytes = n
+        self.ws_ptr = C.c_void_p()
+        self.handle = (C.c_uint8 * IPC_HANDLE_BYTES)()
+        check(lib().gtm_ipc_alloc(n, C.byref(self.ws_ptr), self.handle))
+        self.peers = EpPeers()
+        self.peers.workspace_dev[rank] = self.ws_ptr.value
+        self.opened = []
+        self.device = device
+        self.side = torch.cuda.Stream(device=device)
+        self.ev_dispatch = torch.cuda.Event()
+        self.ev_shared = torch.cuda.Event()
+
+    def connect_local(self, ops_per_rank):
+        for o in ops_per_rank:
+            self.peers.workspace_dev[o.rank] = o.ws_ptr.value
+
+    def connect(self, group=None):
+        import torch.distributed as dist
+        torch = self.torch
+        dev = self.device if dist.get_backend(group) == "nccl" else "cpu"
+        mine = torch.tensor(list(bytes(self.handle)), dtype=torch.uint8, device=dev)
+        allh = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(allh, mine, group=group)
+        for s in range(self.world):
+            if s == self.rank:
+                continue
+            h = (C.c_uint8 * IPC_HANDLE_BYTES)(*allh[s].cpu().tolist())
+            p = C.c_void_p()
+            check(lib().gtm_ipc_open(h, C.byref(p)))
+            self.opened.append(p)
+            self.peers.workspace_dev[s] = p.value
+
+    def close(self):
+        """Unmaps the peers' workspaces and frees the own one (after a barrier: no peer may
+        still read or write it)."""
+        for p in self.opened:
+            check(lib().gtm_ipc_close(p))
+        self.opened = []
+        if self.ws_ptr.value:
+            check(lib().gtm_ipc_free(self.ws_ptr))
+            self.ws_ptr = C.c_void_p()
+
+    _io = CudaEpOps._io
+
+    def dispatch(self, x, **kw):
+        io = self._io(x, **kw)
+        check(lib().gtm_moe_ep_peer_dispatch(C.byref(self.dims), C.byref(self.layer), C.byref(io),
+                                             C.byref(self.cfg), self.ws_ptr, self.ws_bytes, _stream()))
+        self.ev_dispatch.record()
+
+    def shared(self, x, **kw):
+        io = self._io(x, **kw)
+        self.side.wait_event(self.ev_dispatch)
+        check(lib().gtm_moe_ep_peer_shared(C.byref(self.dims), C.byref(self.layer), C.byref(io),
+                                           C.byref(self.cfg), self.ws_ptr, self.ws_bytes, _stream(self.side)))
+        self.ev_shared.record(self.side)
+
+    def experts(self):
+        check(lib().gtm_moe_ep_peer_experts(C.byref(self.dims), C.byref(self.layer), C.byref(self.cfg),
+                                            C.byref(self.peers), self.ws_bytes, _stream()))
+
+    def combine(self, x, hidden_out, **kw):
+        io = self._io(x, hidden_out=hidden_out, **kw)
+        self.torch.cuda.current_stream().wait_event(self.ev_shared)
+        check(lib().gtm_moe_ep_peer_combine(C.byref(self.dims), C.byref(self.layer), C.byref(io),
+                                            C.byref(self.cfg), self.ws_ptr, self.ws_bytes, _stream()))
 
     def check(self):
         check(lib().gtm_moe_ep_check(self.ws_ptr, _stream()))
