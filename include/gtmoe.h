@@ -318,15 +318,16 @@ GTM_API int gtm_moe_ep_check(void* workspace_dev, void* stream);
  * all-to-all and no host round trip. Every rank uses the same config (world, max_tokens;
  * max_recv_rows is ignored: room for world * max_tokens * top_k rows is always reserved),
  * so the workspaces have the same layout. One layer:
- *   1. gtm_moe_ep_peer_dispatch  own tokens: views, router, top-k into the own workspace,
- *                                and the own token count for the peers
+ *   1. gtm_moe_ep_peer_dispatch  own tokens: views, router, top-k; stores the top-8 ids and
+ *                                the token count into every rank's workspace and each token's
+ *                                routed view into the workspaces of the ranks that own one of
+ *                                its experts (NVLink stores)
  *   2. gtm_moe_ep_peer_shared    own tokens: shared expert; may run on a second stream
  *                                concurrently with phase 3 once phase 1 has completed
  *      -- barrier: every rank has completed phase 1 --
- *   3. gtm_moe_ep_peer_experts   this rank's experts over every rank's (token, slot) entries:
- *                                the routing tables read the peers' top-k, the rows are read
- *                                from the peers' workspaces, and each expert output row is
- *                                stored into its token's rank's workspace (routing weight not
+ *   3. gtm_moe_ep_peer_experts   this rank's experts over every rank's (token, slot) entries,
+ *                                read from the own workspace; each expert output row is stored
+ *                                into its token's rank's workspace (routing weight not
  *                                applied); rows of one expert keep the source-rank-major entry
  *                                order, so the results match gtm_moe_tokens on the whole batch
  *      -- barrier: every rank has completed phase 3 --
@@ -335,6 +336,7 @@ GTM_API int gtm_moe_ep_check(void* workspace_dev, void* stream);
  * The barriers are the caller's (a stream-ordered one-element all-reduce over NCCL is
  * enough: a kernel's peer stores are complete at system scope when it ends). The second
  * barrier also keeps the next layer's phase 1 from overwriting rows a peer still reads.
+ * Phases 1 and 3 take every rank's workspace (GtmEpPeers); 2 and 4 only the own one.
  * ------------------------------------------------------------------------------------- */
 #define GTM_EP_PEER_MAX_WORLD 8
 
@@ -347,8 +349,9 @@ typedef struct GtmEpPeers {
  * most GTM_EP_PEER_MAX_WORLD, world * max_tokens at most 65536). Zero it once before its first
  * use (gtm_ipc_alloc returns it zeroed). */
 GTM_API size_t gtm_moe_ep_peer_workspace_bytes(const GtmDims* dims, const GtmEpConfig* ep);
+/* peers->workspace_dev[ep->rank] is the own workspace. */
 GTM_API int gtm_moe_ep_peer_dispatch(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
-                                     const GtmEpConfig* ep, void* workspace_dev, size_t workspace_bytes,
+                                     const GtmEpConfig* ep, const GtmEpPeers* peers, size_t workspace_bytes,
                                      void* stream);
 GTM_API int gtm_moe_ep_peer_shared(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
                                    const GtmEpConfig* ep, void* workspace_dev, size_t workspace_bytes,

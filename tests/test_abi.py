@@ -109,8 +109,10 @@ def test_ep_peer_config_bounds_and_argument_checks():
     peers = gtmoe.EpPeers()
     rc = L.gtm_moe_ep_peer_experts(C.byref(d), C.byref(layer), C.byref(cfg), C.byref(peers), 1 << 40, None)
     assert rc == gtmoe.ERR_WORKSPACE and "gtm_moe_ep_peer_experts" in gtmoe.last_error()
-    rc = L.gtm_moe_ep_peer_dispatch(C.byref(d), C.byref(layer), C.byref(io), C.byref(cfg), C.c_void_p(4096), 16, None)
+    peers.workspace_dev[0] = 4096
+    rc = L.gtm_moe_ep_peer_dispatch(C.byref(d), C.byref(layer), C.byref(io), C.byref(cfg), C.byref(peers), 16, None)
     assert rc == gtmoe.ERR_WORKSPACE
+    assert L.gtm_moe_ep_peer_dispatch(C.byref(d), C.byref(layer), C.byref(io), C.byref(cfg), None, 16, None) == gtmoe.ERR_INVALID
 
 
 def test_ipc_argument_checks():

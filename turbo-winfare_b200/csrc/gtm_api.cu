@@ -465,13 +465,23 @@ GTM_API size_t gtm_moe_ep_peer_workspace_bytes(const GtmDims* dims, const GtmEpC
     return ep_peer_workspace_bytes(ep->world, ep->max_tokens);
 }
 
+static int peers_ok(const char* fn, const GtmEpConfig* ep, const GtmEpPeers* peers) {
+    for (uint32_t s = 0; s < ep->world; ++s)
+        if (!peers->workspace_dev[s] || !aligned(peers->workspace_dev[s], 256))
+            return set_error(GTM_ERR_INVALID, "%s: workspace of rank %u is null or not 256-byte aligned", fn, s);
+    return GTM_OK;
+}
+
 GTM_API int gtm_moe_ep_peer_dispatch(const GtmDims* dims, const GtmLayer* layer, const GtmTokensIO* io,
-                                     const GtmEpConfig* ep, void* ws, size_t ws_bytes, void* stream) {
+                                     const GtmEpConfig* ep, const GtmEpPeers* peers, size_t ws_bytes, void* stream) {
     const char* fn = "gtm_moe_ep_peer_dispatch";
-    int rc = peer_common(fn, dims, layer, ep, ws, ws_bytes);
+    if (!peers || !ep) return set_error(GTM_ERR_INVALID, "%s: null argument", fn);
+    int rc = peer_common(fn, dims, layer, ep, ep->rank < GTM_EP_PEER_MAX_WORLD ? peers->workspace_dev[ep->rank] : nullptr,
+                         ws_bytes);
+    if (!rc) rc = peers_ok(fn, ep, peers);
     if (!rc) rc = ep_io(fn, io, ep, false, true);
     if (rc) return rc;
-    rc = launch_ep_peer_dispatch(*dims, *layer, *io, *ep, ws, (cudaStream_t)stream);
+    rc = launch_ep_peer_dispatch(*dims, *layer, *io, *ep, peers->workspace_dev, (cudaStream_t)stream);
     if (rc == GTM_OK) clear_error();
     return rc;
 }
@@ -496,10 +506,8 @@ GTM_API int gtm_moe_ep_peer_experts(const GtmDims* dims, const GtmLayer* layer, 
     if (!peers || !ep) return set_error(GTM_ERR_INVALID, "%s: null argument", fn);
     int rc = peer_common(fn, dims, layer, ep, ep->rank < GTM_EP_PEER_MAX_WORLD ? peers->workspace_dev[ep->rank] : nullptr,
                          ws_bytes);
+    if (!rc) rc = peers_ok(fn, ep, peers);
     if (rc) return rc;
-    for (uint32_t s = 0; s < ep->world; ++s)
-        if (!peers->workspace_dev[s] || !aligned(peers->workspace_dev[s], 256))
-            return set_error(GTM_ERR_INVALID, "%s: workspace of rank %u is null or not 256-byte aligned", fn, s);
     int sms = 0;
     if ((rc = sm_count(fn, &sms))) return rc;
     rc = launch_ep_peer_experts(*layer, *ep, peers->workspace_dev, (cudaStream_t)stream, sms);

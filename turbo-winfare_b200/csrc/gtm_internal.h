@@ -33,7 +33,7 @@ int launch_ep_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO&
                       const float* ret_rows, void* ws, cudaStream_t st);
 size_t ep_peer_workspace_bytes(uint32_t world, uint32_t max_tokens);
 int launch_ep_peer_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
-                            void* ws, cudaStream_t st);
+                            void* const* peer_ws, cudaStream_t st);
 int launch_ep_peer_experts(const GtmLayer& L, const GtmEpConfig& ep, void* const* peer_ws, cudaStream_t st,
                            int num_sms);
 int launch_ep_peer_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,

@@ -87,6 +87,8 @@ constexpr int FB0_R = (FE + 127) / 128, FB0_S = (FS + 127) / 128;   // gate/up t
 constexpr int FB1 = D / MW;                                         // down tiles: 256 output rows
 constexpr uint64_t kWaitNs = 1000000000ull;
 constexpr int RIN_PITCH = 65;
+constexpr int kMaxPeers = 8;   // ranks of a peer-memory expert-parallel group (NVLink domain of one box)
+static_assert(kMaxPeers == GTM_EP_PEER_MAX_WORLD, "peer group size");
 
 static_assert(SMEM_BYTES <= 232448, "grouped GEMM shared memory");
 static_assert(FE % 64 == 0 && FS % 64 == 0 && D % MW == 0, "tile shapes");
@@ -122,10 +124,18 @@ struct ViewsArgs {
     uint32_t* idx;               // [T][8]
     float* w;                    // [T][8]
     float* logits_out;           // [T][E] or null
+    // peer-memory expert parallelism: this rank's slots in every rank's workspace (null: own
+    // rank, or not expert parallel). Every rank gets each token's top-8 ids; the routed view
+    // goes only to the ranks that own one of the token's experts (epr experts per rank).
+    uint32_t* push_idx[kMaxPeers];
+    __half* push_views[kMaxPeers];
+    int npeers, epr;
 };
 
 __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ ViewsArgs A) {
     __shared__ __align__(16) float sx[D];
+    __shared__ __align__(16) __half srh[2 * D];   // routed view (high row, low row), K-permuted
+    __shared__ uint32_t sdest;                    // peer mode: ranks owning one of the token's experts
     __shared__ float srin[GD * RIN_PITCH];
     __shared__ float slog[NE];
     __shared__ double red[40];
@@ -147,11 +157,16 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
         A.dense_lo[(size_t)t * D + kperm(i)] = __float2half_rn(dx - __half2float(hi));
         const float rx = __fmul_rn(h, bf16f(w_pre2[i]));
         const __half rh = __float2half_rn(rx);
-        A.routed_hl[(size_t)t * 2 * D + kperm(i)] = rh;
-        A.routed_hl[(size_t)t * 2 * D + D + kperm(i)] = __float2half_rn(rx - __half2float(rh));
+        srh[kperm(i)] = rh;
+        srh[D + kperm(i)] = __float2half_rn(rx - __half2float(rh));
         srin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(h, bf16f(rs[i])), A.inv_sqrt_d);
     }
     __syncthreads();
+    {
+        const uint4* s4 = reinterpret_cast<const uint4*>(srh);
+        uint4* d4 = reinterpret_cast<uint4*>(A.routed_hl + (size_t)t * 2 * D);
+        for (int c = tid; c < 2 * D / 8; c += blockDim.x) d4[c] = s4[c];
+    }
     if (A.route_logits) {
         for (int e = tid; e < NE; e += blockDim.x) slog[e] = A.route_logits[(size_t)t * NE + e];
     } else {
@@ -228,14 +243,29 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
             A.idx[(size_t)t * TOPK + lane] = (uint32_t)my_idx;
             A.w[(size_t)t * TOPK + lane] = __fmul_rn(__fdiv_rn(e, sum), bf16f(pes));
         }
+        if (A.npeers > 0) {
+            const uint32_t dest = __reduce_or_sync(0xffffffffu, lane < TOPK ? 1u << (my_idx / A.epr) : 0u);
+            if (lane == 0) sdest = dest;
+            for (int s = 0; s < A.npeers; ++s)
+                if (A.push_idx[s] && lane < TOPK) A.push_idx[s][(size_t)t * TOPK + lane] = (uint32_t)my_idx;
+        }
+    }
+    if (A.npeers > 0) {
+        // the routed view to each peer that owns one of the token's experts: 16-byte NVLink stores
+        __syncthreads();
+        const uint32_t dest = sdest;
+        const uint4* s4 = reinterpret_cast<const uint4*>(srh);
+        for (int s = 0; s < A.npeers; ++s) {
+            if (!A.push_views[s] || !((dest >> s) & 1u)) continue;
+            uint4* d4 = reinterpret_cast<uint4*>(A.push_views[s] + (size_t)t * 2 * D);
+            for (int c = tid; c < 2 * D / 8; c += blockDim.x) d4[c] = s4[c];
+        }
     }
 }
 
 // ================================================================================================
 // 2. routing tables and tile lists
 // ================================================================================================
-constexpr int kMaxPeers = 8;   // ranks of a peer-memory expert-parallel group (NVLink domain of one box)
-static_assert(kMaxPeers == GTM_EP_PEER_MAX_WORLD, "peer group size");
 
 struct RouteArgs {
     int n;                   // routed entries (0: shared tiles only)
@@ -447,8 +477,9 @@ __global__ void __launch_bounds__(128) tok_gather(const __half* routed_hl, const
 }
 
 // Peer-memory expert parallelism: row r of this rank's experts is global entry perm_src[r] =
-// source rank s x per_src + (token x 8 + slot), gathered from rank s's routed views over NVLink
-// (plain peer loads). Each thread issues all of its 16-byte loads of a row before its stores.
+// source rank s x per_src + (token x 8 + slot), gathered from the copy of rank s's routed views
+// that rank s's dispatch stored into this workspace. Each thread issues all of its 16-byte loads
+// of a row before its stores.
 struct PeerGatherArgs {
     const __half* routed[kMaxPeers];   // every rank's routed views (high row, low row per token)
     int per_src;
@@ -480,7 +511,11 @@ __global__ void __launch_bounds__(128) tok_gather_peer(const __grid_constant__ P
     }
 }
 
-__global__ void tok_set_word(int* p, int v) { *p = v; }
+// Peer mode: this rank's token count into its slot of every rank's header.
+struct CountArgs { int* dst[kMaxPeers]; int n, v; };
+__global__ void tok_set_count(const __grid_constant__ CountArgs A) {
+    for (int s = 0; s < A.n; ++s) *A.dst[s] = A.v;
+}
 
 // ================================================================================================
 // 4/5. grouped GEMM
@@ -1043,7 +1078,7 @@ __global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ Combin
 // ================================================================================================
 struct WsLayout {
     size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, stiles0, stiles1, sn_tiles, xhi, xlo, act_r_hi,
-        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, hdr, ret, total;
+        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, views_all, idx_all, hdr, ret, total;
 };
 
 // single GPU; expert parallelism with the caller's all-to-all; expert parallelism over peer memory
@@ -1053,8 +1088,10 @@ static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
 // T: own tokens; R: routed rows through the experts (T * top_k on one GPU, the received rows
 // with expert parallelism, every rank's entries (world * T * top_k) over peer memory).
-// Over peer memory every rank has the same layout, so a peer's regions sit at the same offsets.
-static WsLayout ws_layout(uint32_t T, uint32_t Rrows, WsMode mode) {
+// Over peer memory (P ranks) every rank has the same layout, so a peer's regions sit at the same
+// offsets; the routed views and top-8 ids of rank s live in slot s of views_all / idx_all on
+// every rank (written there by rank s's dispatch), and `routed` / `idx` name this rank's slot.
+static WsLayout ws_layout(uint32_t T, uint32_t Rrows, WsMode mode, uint32_t P = 1, uint32_t rank = 0) {
     const bool ep = mode != WS_SINGLE;
     WsLayout W;
     const size_t E8 = (size_t)T * TOPK, R = Rrows;
@@ -1063,8 +1100,16 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, WsMode mode) {
     auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + bytes); return at; };
     W.dense_hi = take((size_t)T * D * 2);
     W.dense_lo = take((size_t)T * D * 2);
-    W.routed = take((size_t)T * D * 4);
-    W.idx = take(E8 * 4);
+    if (mode == WS_PEER) {
+        W.views_all = take((size_t)P * T * D * 4);
+        W.idx_all = take((size_t)P * E8 * 4);
+        W.routed = W.views_all + (size_t)rank * T * D * 4;
+        W.idx = W.idx_all + (size_t)rank * E8 * 4;
+    } else {
+        W.views_all = W.idx_all = 0;
+        W.routed = take((size_t)T * D * 4);
+        W.idx = take(E8 * 4);
+    }
     W.w = take(E8 * 4);
     W.perm_src = take(R * 4);
     W.pos = take(R * 4);
@@ -1087,9 +1132,9 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, WsMode mode) {
     W.out_s = take((size_t)T * D * 4);
     W.send_pos = mode == WS_EP ? take(E8 * 4) : 0;
     W.send_src = mode == WS_EP ? take(E8 * 4) : 0;
-    // peer memory: [0] own token count (read by the peers' routing), [1] rows routed here;
+    // peer memory: [s] token count of rank s (written by its dispatch), [P] rows routed here;
     // ret: [T * top_k][D] expert outputs of the own entries, stored by the experts' owners
-    W.hdr = mode == WS_PEER ? take(2 * 4) : 0;
+    W.hdr = mode == WS_PEER ? take((P + 1) * 4) : 0;
     W.ret = mode == WS_PEER ? take(E8 * D * 4) : 0;
     W.total = o;
     return W;
@@ -1104,7 +1149,7 @@ size_t ep_workspace_bytes(uint32_t max_tokens, uint32_t max_recv) {
     return tok::ws_layout(max_tokens, max_recv, tok::WS_EP).total;
 }
 size_t ep_peer_workspace_bytes(uint32_t world, uint32_t max_tokens) {
-    return tok::ws_layout(max_tokens, world * max_tokens * tok::TOPK, tok::WS_PEER).total;
+    return tok::ws_layout(max_tokens, world * max_tokens * tok::TOPK, tok::WS_PEER, world, 0).total;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1167,7 +1212,9 @@ struct Ws {
     template <class T> T* p(size_t off) const { return reinterpret_cast<T*>(base + off); }
 };
 
-void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const Ws& w, cudaStream_t st) {
+// peer_ws: every rank's workspace (peer-memory expert parallelism; null otherwise)
+void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const Ws& w, cudaStream_t st,
+                  const GtmEpConfig* ep = nullptr, void* const* peer_ws = nullptr) {
     ViewsArgs va;
     memset(&va, 0, sizeof(va));
     va.T = (int)io.num_tokens; va.x_f32 = io.x_dev; va.x_bf16 = io.x_bf16_dev; va.L = L; va.eps = dims.eps;
@@ -1177,6 +1224,15 @@ void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     va.routed_hl = w.p<__half>(w.W.routed);
     va.idx = w.p<uint32_t>(w.W.idx); va.w = w.p<float>(w.W.w);
     va.logits_out = io.logits_dev;
+    if (peer_ws) {
+        va.npeers = (int)ep->world; va.epr = NE / (int)ep->world;
+        for (uint32_t s = 0; s < ep->world; ++s) {
+            if (s == ep->rank) continue;
+            const Ws ps{w.W, static_cast<uint8_t*>(peer_ws[s])};
+            va.push_idx[s] = ps.p<uint32_t>(w.W.idx);
+            va.push_views[s] = ps.p<__half>(w.W.routed);
+        }
+    }
     tok_views_router<<<io.num_tokens, 512, 0, st>>>(va);
 }
 
@@ -1199,6 +1255,7 @@ struct Plan {
     const int* src_ntok[kMaxPeers];
     const __half* src_routed[kMaxPeers];
     float* src_ret[kMaxPeers];
+    int* nrows;                   // rows routed to this rank (written by the routing scan)
 };
 
 int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaStream_t st) {
@@ -1236,7 +1293,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     ra.n_tiles = w.p<int>(pl.own_tiles ? W.sn_tiles : W.n_tiles);
     ra.nsrc = pl.nsrc; ra.per_src = pl.per_src;
     for (int s = 0; s < pl.nsrc; ++s) { ra.src_idx[s] = pl.src_idx[s]; ra.src_ntok[s] = pl.src_ntok[s]; }
-    ra.nrows = pl.nsrc > 0 ? w.p<int>(W.hdr) + 1 : nullptr;
+    ra.nrows = pl.nrows;
     if (ra.nchunks > 0) tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
     tok_route_scan<<<1, 1024, 0, st>>>(ra);
     if (ra.nchunks > 0) tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
@@ -1336,7 +1393,8 @@ static Ws ep_ws(const GtmEpConfig& ep, void* ws) {
     return Ws{ws_layout(ep.max_tokens, ep.max_recv_rows, WS_EP), static_cast<uint8_t*>(ws)};
 }
 static Ws peer_ws(const GtmEpConfig& ep, void* ws) {
-    return Ws{ws_layout(ep.max_tokens, ep.world * ep.max_tokens * TOPK, WS_PEER), static_cast<uint8_t*>(ws)};
+    return Ws{ws_layout(ep.max_tokens, ep.world * ep.max_tokens * TOPK, WS_PEER, ep.world, ep.rank),
+              static_cast<uint8_t*>(ws)};
 }
 
 int launch_ep_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
@@ -1392,10 +1450,14 @@ int launch_ep_combine(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO&
 
 // ---- expert parallelism over peer memory -------------------------------------------------------
 int launch_ep_peer_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
-                            void* ws, cudaStream_t st) {
-    const Ws w = peer_ws(ep, ws);
-    if (io.num_tokens > 0) launch_views(dims, L, io, w, st);   // a rank may have no tokens in a call
-    tok_set_word<<<1, 1, 0, st>>>(w.p<int>(w.W.hdr), (int)io.num_tokens);
+                            void* const* peer_ws_dev, cudaStream_t st) {
+    const Ws w = peer_ws(ep, peer_ws_dev[ep.rank]);
+    if (io.num_tokens > 0) launch_views(dims, L, io, w, st, &ep, peer_ws_dev);   // a rank may have no tokens
+    CountArgs ca;
+    memset(&ca, 0, sizeof(ca));
+    ca.n = (int)ep.world; ca.v = (int)io.num_tokens;
+    for (uint32_t s = 0; s < ep.world; ++s) ca.dst[s] = reinterpret_cast<int*>(static_cast<uint8_t*>(peer_ws_dev[s]) + w.W.hdr) + ep.rank;
+    tok_set_count<<<1, 1, 0, st>>>(ca);
     return finish("gtm_moe_ep_peer_dispatch", &io, &w, st);
 }
 
@@ -1409,12 +1471,14 @@ int launch_ep_peer_experts(const GtmLayer& L, const GtmEpConfig& ep, void* const
     pl.n = P * pl.per_src; pl.src_div = 1; pl.stride = 1;
     pl.e0 = (int)ep.rank * epr; pl.ne = epr; pl.t_shared = 0;
     pl.out_index = w.p<int>(w.W.perm_src);
+    pl.nrows = w.p<int>(w.W.hdr) + P;
+    // every rank's top-8 ids, token counts and routed views were stored into this workspace by
+    // their dispatch; only the results cross NVLink here
     for (int s = 0; s < P; ++s) {
-        const Ws ps{w.W, static_cast<uint8_t*>(peer_ws_dev[s])};
-        pl.src_idx[s] = ps.p<uint32_t>(w.W.idx);
-        pl.src_ntok[s] = ps.p<int>(w.W.hdr);
-        pl.src_routed[s] = ps.p<__half>(w.W.routed);
-        pl.src_ret[s] = ps.p<float>(w.W.ret);
+        pl.src_idx[s] = w.p<uint32_t>(w.W.idx_all) + (size_t)s * pl.per_src;
+        pl.src_ntok[s] = w.p<int>(w.W.hdr) + s;
+        pl.src_routed[s] = w.p<__half>(w.W.views_all) + (size_t)s * ep.max_tokens * 2 * D;
+        pl.src_ret[s] = reinterpret_cast<float*>(static_cast<uint8_t*>(peer_ws_dev[s]) + w.W.ret);
     }
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;

@@ -130,7 +130,7 @@ SIGNATURES = {
     "gtm_moe_ep_check": (_I, [_P, _P]),
     "gtm_moe_ep_peer_workspace_bytes": (_SZ, [C.POINTER(Dims), C.POINTER(EpConfig)]),
     "gtm_moe_ep_peer_dispatch": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
-                                      _P, _SZ, _P]),
+                                      C.POINTER(EpPeers), _SZ, _P]),
     "gtm_moe_ep_peer_shared": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
                                     _P, _SZ, _P]),
     "gtm_moe_ep_peer_experts": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(EpConfig), C.POINTER(EpPeers),

@@ -19,11 +19,13 @@ function with gloo and stand-in ops. The reference has no multi-GPU path; this r
 token-at-a-time prefill (src/runner.cpp:845-854) for a layer sharded over GPUs.
 
 Over peer memory (`PeerEpOps`, `ep_layer_peer`) the ranks map each other's workspaces (CUDA
-IPC) and the kernels move the rows themselves: the experts phase reads every rank's top-8 and
-routed rows with plain NVLink loads and stores each expert output row into its token's rank.
-The only collectives are two one-element all-reduces used as stream-ordered barriers:
+IPC) and the kernels move the rows themselves with plain NVLink stores: the dispatch stores each
+token's top-8 ids into every rank and its routed view into the ranks that own one of its
+experts, the experts phase reads only its own workspace and stores each expert output row into
+its token's rank. The only collectives are two one-element all-reduces used as stream-ordered
+barriers:
 
-  1. dispatch   own tokens: views, router, top-k, own token count (gtm_moe_ep_peer_dispatch)
+  1. dispatch   own tokens: views, router, top-k, pushes to the peers (gtm_moe_ep_peer_dispatch)
   2. shared     on a second stream (gtm_moe_ep_peer_shared)
      -- barrier --
   3. experts    this rank's experts over all ranks' entries (gtm_moe_ep_peer_experts)
@@ -315,7 +317,7 @@ class PeerEpOps:
     def dispatch(self, x, **kw):
         io = self._io(x, **kw)
         check(lib().gtm_moe_ep_peer_dispatch(C.byref(self.dims), C.byref(self.layer), C.byref(io),
-                                             C.byref(self.cfg), self.ws_ptr, self.ws_bytes, _stream()))
+                                             C.byref(self.cfg), C.byref(self.peers), self.ws_bytes, _stream()))
         self.ev_dispatch.record()
 
     def shared(self, x, **kw):
