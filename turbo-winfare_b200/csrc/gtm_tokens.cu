@@ -8,11 +8,11 @@
 //                         order (or caller-given routing logits), optional logit bias, top-8
 //   2. tok_route_*        counts per expert, token-slot rows grouped by expert (in entry order),
 //                         GEMM tile lists
-//   3. tok_gather         routed_x rows (fp16 high and low parts) copied into expert order
-//   4. grouped_gemm<0>    gate/up of the routed experts and the shared expert, GeGLU fused,
-//                         activations written as fp16 high/low parts
-//   5. grouped_gemm<1>    down projections
-//   6. tok_combine        h2 = routing-weighted sum over the 8 slots in router order, shared
+//   3. grouped_gemm<0>    gate/up of the routed experts and the shared expert, GeGLU fused,
+//                         activations written as fp16 high/low parts; the routed tiles gather
+//                         their token rows from the per-token routed views themselves
+//   4. grouped_gemm<1>    down projections
+//   5. tok_combine        h2 = routing-weighted sum over the 8 slots in router order, shared
 //                         output, layer tail
 //
 // Grouped GEMM: one CTA per SM, persistent over a tile list built on the device. A tile is 256
@@ -27,8 +27,10 @@
 // blocks rotate through (row block b of tile n in slot (2n + b) % 3) and two weight stages of
 // 2 x 32 columns. On B200 a 128 x N x 16 MMA costs ~62 cycles for any N up to
 // ~128 (measured), so N = 128 is the narrowest tile that keeps the tensor pipe busy. Warp roles:
-//   * warp 0 loads the activation tile by TMA per K block, the fp16 high part and the fp16 low
-//     part (x - hi), so the MMAs against the same weights carry ~22 bits of the activation;
+//   * warp 0 loads the activation tile per K block, the fp16 high part and the fp16 low part
+//     (x - hi), so the MMAs against the same weights carry ~22 bits of the activation: by TMA
+//     from the dense tensors, or, for the gate/up of routed experts, gathered row by row from the
+//     per-token routed views with cp.async (no expert-ordered copy of the rows is materialised);
 //   * warp 2 loads the tile's 256 packed int4 rows per K block by TMA (rows of 32 bytes, 32-byte
 //     swizzle);
 //   * warps 12-19, one thread per weight row, dequantise to fp16 w = q * scale + bias (exact in
@@ -461,56 +463,6 @@ __global__ void __launch_bounds__(256) tok_copy_rows(const float* src, const int
     for (int c = threadIdx.x; c < D / 4; c += blockDim.x) d4[c] = s4[c];
 }
 
-// ================================================================================================
-// 3. gather the routed views in expert order: each is already an fp16 high row and low row
-//    (K-permuted, written once per token by the views kernel), so this is a row copy
-// ================================================================================================
-__global__ void __launch_bounds__(128) tok_gather(const __half* routed_hl, const int* perm_src, __half* xhi, __half* xlo) {
-    const int row = blockIdx.x;
-    const uint4* src = reinterpret_cast<const uint4*>(routed_hl + (size_t)perm_src[row] * 2 * D);
-    uint4* dh = reinterpret_cast<uint4*>(xhi + (size_t)row * D);
-    uint4* dl = reinterpret_cast<uint4*>(xlo + (size_t)row * D);
-    for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
-        dh[c] = src[c];
-        dl[c] = src[D / 8 + c];
-    }
-}
-
-// Peer-memory expert parallelism: row r of this rank's experts is global entry perm_src[r] =
-// source rank s x per_src + (token x 8 + slot), gathered from the copy of rank s's routed views
-// that rank s's dispatch stored into this workspace. Each thread issues all of its 16-byte loads
-// of a row before its stores.
-struct PeerGatherArgs {
-    const __half* routed[kMaxPeers];   // every rank's routed views (high row, low row per token)
-    int per_src;
-    const int* perm_src;
-    const int* nrows;                  // rows routed to this rank (written by the routing scan)
-    __half* xhi;
-    __half* xlo;
-};
-
-__global__ void __launch_bounds__(128) tok_gather_peer(const __grid_constant__ PeerGatherArgs A) {
-    constexpr int NC = (D / 8 + 127) / 128;
-    const int n = *A.nrows;
-    for (int row = blockIdx.x; row < n; row += gridDim.x) {
-        const int i = A.perm_src[row], s = i / A.per_src, t = (i - s * A.per_src) / TOPK;
-        const uint4* src = reinterpret_cast<const uint4*>(A.routed[s] + (size_t)t * 2 * D);
-        uint4 h[NC], l[NC];
-#pragma unroll
-        for (int v = 0; v < NC; ++v) {
-            const int c = threadIdx.x + 128 * v;
-            if (c < D / 8) { h[v] = src[c]; l[v] = src[D / 8 + c]; }
-        }
-        uint4* dh = reinterpret_cast<uint4*>(A.xhi + (size_t)row * D);
-        uint4* dl = reinterpret_cast<uint4*>(A.xlo + (size_t)row * D);
-#pragma unroll
-        for (int v = 0; v < NC; ++v) {
-            const int c = threadIdx.x + 128 * v;
-            if (c < D / 8) { dh[c] = h[v]; dl[c] = l[v]; }
-        }
-    }
-}
-
 // Peer mode: this rank's token count into its slot of every rank's header.
 struct CountArgs { int* dst[kMaxPeers]; int n, v; };
 __global__ void tok_set_count(const __grid_constant__ CountArgs A) {
@@ -523,6 +475,7 @@ __global__ void tok_set_count(const __grid_constant__ CountArgs A) {
 struct GemmArgs {
     CUtensorMap x_rhi, x_rlo, x_shi, x_slo;   // activations: 2D fp16, 32-row boxes, 128-byte swizzle
     CUtensorMap y_rhi, y_rlo, y_shi, y_slo;   // the same tensors in 128-row boxes (tiles of > 64 tokens)
+                                              // (mode 0 routed tiles gather instead, see act_src)
     CUtensorMap w_ra, w_rb, w_sa, w_sb;       // packed int4 weights (matrix a, b): routed 3D (byte, row,
                                               // expert), shared 2D; rows of 32 bytes, 32-byte swizzle
     const Tile* tiles;
@@ -543,6 +496,11 @@ struct GemmArgs {
     // rank o / per_src's return region, row o % per_src (a peer store over NVLink)
     int per_src;
     float* out_peer[kMaxPeers];
+    // mode 0 routed tiles: activation row r is routed view act_row[r] / act_div of act_src
+    // ([rows][2][D] fp16, high row then low row), copied into the stage by the producer warp
+    const __half* act_src;
+    const int* act_row;
+    int act_div;
     int* err;
 };
 
@@ -652,7 +610,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < SX; ++s) { tc::mbar_init(&act_full[s], 1); tc::mbar_init(&act_empty[s], 1); }
+        for (int s = 0; s < SX; ++s) { tc::mbar_init(&act_full[s], 2); tc::mbar_init(&act_empty[s], 1); }
         for (int s = 0; s < RS; ++s) { tc::mbar_init(&raw_full[s], 1); tc::mbar_init(&raw_empty[s], DQ_THREADS); }
         for (int s = 0; s < SW; ++s) { tc::mbar_init(&w_full[s], DQ_THREADS); tc::mbar_init(&w_empty[s], 1); }
         tc::mbar_init(&acc_full[0], 1);
@@ -667,31 +625,89 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
     const uint32_t tmem = *tmem_slot;
     const int ntiles = *A.n_tiles;
 
-    if (warp == 0) {
-        // ---- activation producer: per K block the tile's token rows, high and low part ----
-        if (lane == 0) {
-            uint32_t it = 0;
-            bool ok = true;
-            for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
-                const TileInfo ti = tile_info(A, i);
-                const bool wide = ti.t.rows >= XWIDE_MIN && (ti.routed ? A.wide_r : A.wide_s);
-                const CUtensorMap* mh = wide ? (ti.routed ? &A.y_rhi : &A.y_shi) : (ti.routed ? &A.x_rhi : &A.x_shi);
-                const CUtensorMap* ml = wide ? (ti.routed ? &A.y_rlo : &A.y_slo) : (ti.routed ? &A.x_rlo : &A.x_slo);
-                const int nbox = wide ? 1 : (ti.t.rows + 31) >> 5;
-                const uint32_t box_bytes = wide ? X_TILE : XBOX;
-                for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-                    const uint32_t s = it % SX, ph = (it / SX) & 1;
-                    if (!tc::mbar_wait(&act_empty[s], ph ^ 1, abort_flag, kWaitNs)) { ok = false; break; }
+    if (warp == 0 || warp == 3) {
+        // ---- activation producers (two arrivals per stage): per K block the tile's token rows,
+        //      high and low part. Shared-expert and mode 1 tiles: warp 0 loads TMA boxes of the
+        //      dense activation tensors, warp 3 only arrives. Mode 0 routed tiles: warp 0 (high
+        //      part) and warp 3 (low part) gather the rows from the routed views with 16-byte
+        //      cp.async copies into the 128-byte-swizzled layout TMA would produce (row r at
+        //      r * 128, chunk c at c ^ (r & 7)); a warp hands its part of a stage to the MMA warp
+        //      GLAG stages later, after its copies have landed and been fenced for the tensor
+        //      core. The two warps sit on different schedulers ----
+        constexpr int GLAG = 2;
+        const int part = warp == 3 ? 1 : 0;
+        uint32_t it = 0, gath = 0;   // gath bit j: stage it - 1 - j was gathered (arrive pending)
+        bool ok = true;
+        for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+            const TileInfo ti = tile_info(A, i);
+            const int rows = ti.t.rows, row0 = ti.t.row0, hrows = stacked_hi_rows(rows);
+            const bool gather = MODE == 0 && ti.routed;
+            // gathered tiles: source row (in views) of tile rows lane + 32 m
+            int srow[NT / 32];
+#pragma unroll
+            for (int m = 0; m < NT / 32; ++m) {
+                const int r = lane + 32 * m;
+                srow[m] = gather && r < rows ? A.act_row[row0 + r] / A.act_div : 0;
+            }
+            const bool wide = rows >= XWIDE_MIN && (ti.routed ? A.wide_r : A.wide_s);
+            const CUtensorMap* mh = wide ? (ti.routed ? &A.y_rhi : &A.y_shi) : (ti.routed ? &A.x_rhi : &A.x_shi);
+            const CUtensorMap* ml = wide ? (ti.routed ? &A.y_rlo : &A.y_slo) : (ti.routed ? &A.x_rlo : &A.x_slo);
+            const int nbox = wide ? 1 : (rows + 31) >> 5;
+            const uint32_t box_bytes = wide ? X_TILE : XBOX;
+            for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+                const uint32_t s = it % SX, ph = (it / SX) & 1;
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&act_empty[s], ph ^ 1, abort_flag, kWaitNs))) { ok = false; break; }
+                uint8_t* hi_dst = sXh + s * X_TILE;
+                // stacked tiles: low part right after the high part in the same stage
+                uint8_t* lo_dst = hrows ? hi_dst + hrows * 128 : sXl + s * X_TILE;
+                if (gather) {
+                    const int c = lane & 7, rq = lane >> 3;
+                    const uint32_t dst = tc::smem_u32(part ? lo_dst : hi_dst) + (uint32_t)rq * 128;
+                    // row r & 7 = rq + 4 (jj & 1): the swizzled chunk of the two row parities
+                    const uint32_t cx0 = (uint32_t)((c ^ rq) << 4), cx1 = (uint32_t)((c ^ (rq + 4)) << 4);
+                    const __half* col = A.act_src + part * D + kb * BK + c * 8;
+                    // rows 32 m + 4 jj + rq; lane % 8 = the row's 16-byte chunk
+#pragma unroll
+                    for (int m = 0; m < NT / 32; ++m) {
+                        if (32 * m >= rows) break;
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const int rl = 4 * jj + rq;
+                            const int sr = __shfl_sync(0xffffffffu, srow[m], rl);
+                            if (32 * m + rl < rows)
+                                tc::cp_async16(dst + (uint32_t)(32 * m + 4 * jj) * 128 + ((jj & 1) ? cx1 : cx0),
+                                               col + (size_t)sr * 2 * D);
+                        }
+                    }
+                } else if (part == 0 && lane == 0) {
                     tc::mbar_arrive_expect_tx(&act_full[s], 2u * box_bytes * (uint32_t)nbox);
-                    // stacked tiles: low part right after the high part in the same stage
-                    uint8_t* lo_dst = stacked_hi_rows(ti.t.rows) ? sXh + s * X_TILE + nbox * XBOX : sXl + s * X_TILE;
                     for (int j = 0; j < nbox; ++j) {
-                        tc::tma_load_2d(sXh + s * X_TILE + j * XBOX, mh, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
-                        tc::tma_load_2d(lo_dst + j * XBOX, ml, kb * BK, ti.t.row0 + 32 * j, &act_full[s]);
+                        tc::tma_load_2d(hi_dst + j * XBOX, mh, kb * BK, row0 + 32 * j, &act_full[s]);
+                        tc::tma_load_2d(lo_dst + j * XBOX, ml, kb * BK, row0 + 32 * j, &act_full[s]);
+                    }
+                } else if (lane == 0) {
+                    tc::mbar_arrive(&act_full[s]);
+                }
+                tc::cp_async_commit();
+                gath = (gath << 1) | (gather ? 1u : 0u);
+                if (it >= (uint32_t)GLAG) {
+                    tc::cp_async_wait<GLAG>();
+                    if ((gath >> GLAG) & 1u) {   // stage it - GLAG: its copies have landed
+                        tc::fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&act_full[(it - GLAG) % SX]);
                     }
                 }
             }
-            // no exit while TMA writes into this CTA's shared memory are in flight
+        }
+        // hand over the stages still pending, then no exit while TMA writes into this CTA's
+        // shared memory are in flight
+        tc::cp_async_wait<0>();
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        for (uint32_t j = it > (uint32_t)GLAG ? it - GLAG : 0; j < it; ++j)
+            if (((gath >> (it - 1 - j)) & 1u) && lane == 0) tc::mbar_arrive(&act_full[j % SX]);
+        if (part == 0 && lane == 0) {
             volatile int never = 0;
             for (uint32_t j = it > SX ? it - SX : 0; j < it; ++j)
                 tc::mbar_wait(&act_full[j % SX], (j / SX) & 1, &never, kWaitNs);
@@ -1077,7 +1093,7 @@ __global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ Combin
 // host side
 // ================================================================================================
 struct WsLayout {
-    size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, stiles0, stiles1, sn_tiles, xhi, xlo, act_r_hi,
+    size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, stiles0, stiles1, sn_tiles, act_r_hi,
         act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, views_all, idx_all, hdr, ret, total;
 };
 
@@ -1122,8 +1138,6 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, WsMode mode, uint32_t P = 
     W.stiles0 = ep ? take(nts * FB0_S * sizeof(Tile)) : 0;
     W.stiles1 = ep ? take(nts * FB1 * sizeof(Tile)) : 0;
     W.sn_tiles = ep ? take(2 * 4) : 0;
-    W.xhi = take(R * D * 2);
-    W.xlo = take(R * D * 2);
     W.act_r_hi = take(R * FE * 2);
     W.act_r_lo = take(R * FE * 2);
     W.act_s_hi = take((size_t)T * FS * 2);
@@ -1244,7 +1258,7 @@ struct Plan {
     int stride;
     int e0, ne;                   // experts [e0, e0 + ne), layer.experts_dev pointing at e0
     int t_shared;                 // tokens through the shared expert (0: none)
-    const __half* src_hl;         // routed views (high row, low row) the entries read
+    const __half* act_src;        // routed views (high row, low row): row perm_src[r] / act_div
     const int* out_index;         // mode 1 output row of each expert-ordered row (null: same)
     float* out_r;                 // mode 1 routed output rows
     bool own_tiles;               // shared-expert-only plan: tile lists in the stiles* regions
@@ -1253,8 +1267,8 @@ struct Plan {
     int nsrc, per_src;
     const uint32_t* src_idx[kMaxPeers];
     const int* src_ntok[kMaxPeers];
-    const __half* src_routed[kMaxPeers];
     float* src_ret[kMaxPeers];
+    int act_div;                  // routed view of row r = perm_src[r] / act_div (1 when not set)
     int* nrows;                   // rows routed to this rank (written by the routing scan)
 };
 
@@ -1272,8 +1286,8 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     g0.wide_s = g1.wide_s = T >= (uint64_t)NT;
     // 32-row boxes over every activation tensor; 128-row boxes where the tensor has >= 128 rows
     struct ActMap { CUtensorMap* narrow; CUtensorMap* wide; const void* ptr; uint64_t rows, k; };
+    // (mode 0 routed tiles gather their rows from the routed views instead of a map)
     const ActMap maps[] = {
-        {&g0.x_rhi, &g0.y_rhi, w.at(W.xhi), R, D},          {&g0.x_rlo, &g0.y_rlo, w.at(W.xlo), R, D},
         {&g0.x_shi, &g0.y_shi, w.at(W.dense_hi), T, D},     {&g0.x_slo, &g0.y_slo, w.at(W.dense_lo), T, D},
         {&g1.x_rhi, &g1.y_rhi, w.at(W.act_r_hi), R, FE},    {&g1.x_rlo, &g1.y_rlo, w.at(W.act_r_lo), R, FE},
         {&g1.x_shi, &g1.y_shi, w.at(W.act_s_hi), T, FS},    {&g1.x_slo, &g1.y_slo, w.at(W.act_s_lo), T, FS}};
@@ -1297,17 +1311,6 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     if (ra.nchunks > 0) tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
     tok_route_scan<<<1, 1024, 0, st>>>(ra);
     if (ra.nchunks > 0) tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
-    if (pl.nsrc > 0) {
-        PeerGatherArgs ga;
-        memset(&ga, 0, sizeof(ga));
-        for (int s = 0; s < pl.nsrc; ++s) ga.routed[s] = pl.src_routed[s];
-        ga.per_src = pl.per_src; ga.perm_src = ra.perm_src; ga.nrows = ra.nrows;
-        ga.xhi = w.p<__half>(W.xhi); ga.xlo = w.p<__half>(W.xlo);
-        tok_gather_peer<<<(unsigned)num_sms * 8, 128, 0, st>>>(ga);
-    } else if (pl.n > 0) {
-        tok_gather<<<(unsigned)pl.n, 128, 0, st>>>(pl.src_hl, ra.perm_src, w.p<__half>(W.xhi), w.p<__half>(W.xlo));
-    }
-
     cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
 
@@ -1329,6 +1332,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     g0.k_r = D; g0.k_s = D; g0.rows_r = FE; g0.rows_s = FS;
     g0.act_r_hi = w.p<__half>(W.act_r_hi); g0.act_r_lo = w.p<__half>(W.act_r_lo);
     g0.act_s_hi = w.p<__half>(W.act_s_hi); g0.act_s_lo = w.p<__half>(W.act_s_lo);
+    g0.act_src = pl.act_src; g0.act_row = ra.perm_src; g0.act_div = pl.act_div > 0 ? pl.act_div : 1;
     g0.err = w.p<int>(0);
     grouped_gemm<0><<<num_sms, THREADS, SMEM_BYTES, st>>>(g0);
 
@@ -1377,7 +1381,7 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     Plan pl;
     memset(&pl, 0, sizeof(pl));
     pl.n = (int)(T * TOPK); pl.src_div = TOPK; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
-    pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.src_hl = w.p<__half>(w.W.routed); pl.out_index = nullptr;
+    pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.act_src = w.p<__half>(w.W.routed); pl.out_index = nullptr;
     pl.out_r = w.p<float>(w.W.out_r);
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
@@ -1435,7 +1439,7 @@ int launch_ep_experts(const GtmLayer& L, const GtmEpConfig& ep, const float* rec
     pl.n = (int)n_recv; pl.src_div = 1;
     pl.idx = &recv_meta->expert; pl.stride = 2;
     pl.e0 = (int)ep.rank * epr; pl.ne = epr; pl.t_shared = 0;
-    pl.src_hl = reinterpret_cast<const __half*>(recv_rows); pl.out_index = w.p<int>(w.W.perm_src); pl.out_r = ret_rows;
+    pl.act_src = reinterpret_cast<const __half*>(recv_rows); pl.out_index = w.p<int>(w.W.perm_src); pl.out_r = ret_rows;
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
     return finish("gtm_moe_ep_experts", nullptr, nullptr, st);
@@ -1473,11 +1477,13 @@ int launch_ep_peer_experts(const GtmLayer& L, const GtmEpConfig& ep, void* const
     pl.out_index = w.p<int>(w.W.perm_src);
     pl.nrows = w.p<int>(w.W.hdr) + P;
     // every rank's top-8 ids, token counts and routed views were stored into this workspace by
-    // their dispatch; only the results cross NVLink here
+    // their dispatch; only the results cross NVLink here. Entry i = s * per_src + token * 8 + slot
+    // reads row i / 8 = s * max_tokens + token of views_all.
+    pl.act_src = w.p<__half>(w.W.views_all);
+    pl.act_div = TOPK;
     for (int s = 0; s < P; ++s) {
         pl.src_idx[s] = w.p<uint32_t>(w.W.idx_all) + (size_t)s * pl.per_src;
         pl.src_ntok[s] = w.p<int>(w.W.hdr) + s;
-        pl.src_routed[s] = w.p<__half>(w.W.views_all) + (size_t)s * ep.max_tokens * 2 * D;
         pl.src_ret[s] = reinterpret_cast<float*>(static_cast<uint8_t*>(peer_ws_dev[s]) + w.W.ret);
     }
     const int rc = run_gemms(L, w, pl, num_sms, st);
