@@ -338,11 +338,17 @@ __global__ void __launch_bounds__(1024) tok_route_scan(const __grid_constant__ R
     __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
     const int tid = threadIdx.x;
     for (int ex = tid; ex < A.ne; ex += blockDim.x) {
+        // exclusive prefix over the chunks, 16 loads in flight at a time
         int run = 0;
-        for (int c = 0; c < A.nchunks; ++c) {
-            const int v = A.chunk[(size_t)c * NE + ex];
-            A.chunk[(size_t)c * NE + ex] = run;
-            run += v;
+        for (int c0 = 0; c0 < A.nchunks; c0 += 16) {
+            int v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = c0 + j < A.nchunks ? A.chunk[(size_t)(c0 + j) * NE + ex] : 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                if (c0 + j < A.nchunks) A.chunk[(size_t)(c0 + j) * NE + ex] = run;
+                run += v[j];
+            }
         }
         cnt[ex] = run;
     }
@@ -987,7 +993,7 @@ struct CombineArgs {
     float* h2_out;            // [T][D] or null
 };
 
-constexpr int CT = 256;                       // combine: threads per token
+constexpr int CT = D / 4;                     // combine: threads per token, one float4 of each row
 constexpr int CV = (D / 4 + CT - 1) / CT;     // float4 chunks of a row per thread
 
 // Block-wide sums of (a, b), every thread gets the same bits (warp partials added in warp
@@ -1011,7 +1017,7 @@ __device__ __forceinline__ double2 combine_sum2(double a, double b, double (*red
 // (:508-509); hidden = (x + rms(rms(h2)*w_pf2 + h1)*w_pf) * layer_scalar (:512-520).
 // One CTA per token; each thread keeps its float4 chunks of every vector in registers and
 // issues all of its row loads before the first reduction.
-__global__ void __launch_bounds__(CT) tok_combine(const __grid_constant__ CombineArgs A) {
+__global__ void __launch_bounds__(CT, 2) tok_combine(const __grid_constant__ CombineArgs A) {
     __shared__ double red[2][CT / 32][2];
     const int t = blockIdx.x, tid = threadIdx.x;
     const GtmLayer& L = A.L;
