@@ -18,12 +18,13 @@
 //   P1  every CTA: layer tail of the previous layer from the down partials, optional
 //       between-layer RMSNorm, views (dense_x, routed_x, router input); CTAs 0..127: one router
 //       logit each in the reference's exact order (bit-identical logits)      -> arrive A1
-//       every CTA: its share of the 264 shared gate/up tiles (+GeGLU)        -> arrive A2
+//       every CTA: its share of the 264 shared gate/up tiles (+GeGLU)
 //   P2  wait A1; top-8 (each CTA); L2-prefetch its routed down rows; its share of the 704 routed
 //       gate/up tiles (+GeGLU)                                                -> arrive B
-//       wait A2; its share of the shared down (176 row tiles x 3 thirds of K)
-//   P3  wait B; its share of the routed down (176 row tiles x 8 experts), partials x w_k;
-//       L2-prefetch the next layer's router row, shared gate/up and down     -> arrive C
+//   P3  wait B (every CTA's shared and routed activations); its share of the 1936 down items,
+//       the shared down (3 thirds of K x 176 row tiles) and the routed down (8 experts x 176 row
+//       tiles, partials x w_k) in one pass; L2-prefetch the next layer's router row, shared
+//       gate/up and down                                                      -> arrive C
 // The down partials [3 shared + 8 routed][2816] are summed in fixed order by the next tail.
 #include <cstdint>
 #include <cstring>
@@ -45,15 +46,16 @@ constexpr int TILES_R = TOPK * FE / 8;    // 704 routed gate/up tiles (8 row pai
 constexpr int TILES_S = FS / 8;           // 264 shared gate/up tiles
 constexpr int OT = D / 16;                // 176 output row tiles of the down projection
 constexpr int NSEG = 3 + TOPK;            // down partials: 3 shared thirds + 8 routed experts
-constexpr int ITEMS_SD = OT * 3;          // 528 shared-down items
-constexpr int ITEMS_RD = OT * TOPK;       // 1408 routed-down items
-constexpr int MAX_ITEMS = 12;             // per CTA and phase (148 CTAs: <= 10)
+constexpr int ITEMS_SD = OT * 3;          // 528 shared-down items (3 thirds of K x 176 row tiles)
+constexpr int ITEMS_DN = OT * NSEG;       // 1936 down items: segment s = item / OT, shared thirds first
+constexpr int MAX_ITEMS = 17;             // per CTA and phase (down items over >= 118 CTAs)
 constexpr int ROW_GU = D / 2;             // 1408 bytes per gate/up row
 constexpr int RIN_PITCH = 65;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
-constexpr int ACT_R = TOPK * FE;          // 5632 routed activations, then 2112 shared
+constexpr int ACT_R = TOPK * FE;          // 5632 routed activations, after the 2112 shared ones
+constexpr int SEGK = FE;                  // 704 activations per down segment (a shared third or a slot)
 
-enum { BAR_A1 = 0, BAR_A2 = 1, BAR_B = 2, BAR_C = 3 };
+enum { BAR_A1 = 0, BAR_B = 2, BAR_C = 3 };
 
 struct Params {
     GtmLayer layers[GTM_MAX_LAYERS];
@@ -65,7 +67,7 @@ struct Params {
     int* err;
     int* sticky;
     float* logits;     // [NE]
-    float* act;        // [ACT_R + FS]
+    float* act;        // [FS + ACT_R]: shared activations, then the 8 routed slots (segment s at s * 704)
     float* part;       // [NSEG][D]
 };
 
@@ -80,10 +82,9 @@ struct Smem {
     alignas(16) float rin[GD * RIN_PITCH];
     alignas(16) uint32_t tbl_r[GD * TBL_WORDS];        // routed_x
     alignas(16) uint32_t tbl_d[GD * TBL_WORDS];        // dense_x
-    alignas(16) uint32_t tbl_sh[GFS * TBL_WORDS];      // shared act
-    alignas(16) uint32_t tbl_rk[TOPK * GFE * TBL_WORDS];  // routed act, expert-slot major
-    float xs_r[GD], xs_d[GD], xs_sh[GFS], xs_rk[TOPK * GFE];
-    float cs_r[GD], cs_d[GD], cs_sh[GFS], cs_rk[TOPK * GFE];
+    alignas(16) uint32_t tbl_dn[NSEG * GFE * TBL_WORDS];  // down inputs: shared act, then routed slots
+    float xs_r[GD], xs_d[GD], xs_dn[NSEG * GFE];
+    float cs_r[GD], cs_d[GD], cs_dn[NSEG * GFE];
     // bf16 norm vectors, copied ahead of use: this layer's pre_ffn_norm, pre_ffn_norm_2,
     // router.scale and the previous layer's post_ffn_norm_1, post_ffn_norm_2, post_ffn_norm
     alignas(16) uint16_t nw[6][D];
@@ -98,8 +99,8 @@ struct Smem {
 };
 
 static_assert(offsetof(Smem, nw) % 16 == 0 && offsetof(Smem, ab) % 16 == 0 && offsetof(Smem, tbl_r) % 16 == 0 &&
-                  offsetof(Smem, tbl_d) % 16 == 0 && offsetof(Smem, tbl_sh) % 16 == 0 &&
-                  offsetof(Smem, tbl_rk) % 16 == 0 && offsetof(Smem, hid) % 16 == 0,
+                  offsetof(Smem, tbl_d) % 16 == 0 && offsetof(Smem, tbl_dn) % 16 == 0 &&
+                  offsetof(Smem, hid) % 16 == 0,
               "vector-accessed shared arrays must be 16-byte aligned");
 
 __device__ __forceinline__ const uint8_t* rp(const void* base, uint64_t off) {
@@ -666,7 +667,7 @@ __device__ __forceinline__ TileRows down_rows(const uint8_t* base, const GtmQuan
     return R;
 }
 
-// Shared gate/up tiles [t0, t1) -> act[ACT_R + 8*T + r]
+// Shared gate/up tiles [t0, t1) -> act[8*T + r]
 __device__ void shared_gate_up(Smem& s, const Params& P, const GtmLayer& L, int t0, int t1) {
     const int n = t1 - t0;
     if (n <= 0) return;
@@ -681,11 +682,11 @@ __device__ void shared_gate_up(Smem& s, const Params& P, const GtmLayer& L, int 
     for (int i = threadIdx.x; i < n * 8; i += NT) {
         const int item = i >> 3, r = i & 7;
         const float gt = slot_sum(s, item, r), up = slot_sum(s, item, 8 + r);
-        P.act[ACT_R + (t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
+        P.act[(t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
     }
 }
 
-// Routed gate/up tiles [t0, t1) (tile T: expert slot T / 88, rows 8 * (T % 88) ..) -> act[8*T + r]
+// Routed gate/up tiles [t0, t1) (tile T: expert slot T / 88, rows 8 * (T % 88) ..) -> act[FS + 8*T + r]
 __device__ void routed_gate_up(Smem& s, const Params& P, const GtmLayer& L, int t0, int t1) {
     const int n = t1 - t0;
     if (n <= 0) return;
@@ -701,65 +702,48 @@ __device__ void routed_gate_up(Smem& s, const Params& P, const GtmLayer& L, int 
     for (int i = threadIdx.x; i < n * 8; i += NT) {
         const int item = i >> 3, r = i & 7;
         const float gt = slot_sum(s, item, r), up = slot_sum(s, item, 8 + r);
-        P.act[(t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
+        P.act[FS + (t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
     }
 }
 
-// Shared down items [i0, i1): item i -> third q = i / OT, row tile ot = i % OT; K groups
-// [11q, 11q + 11) of 33 -> part[q][16*ot + r]
-__device__ void shared_down(Smem& s, const Params& P, const GtmLayer& L, int i0, int i1) {
+// Down items [i0, i1) of the shared expert and the 8 routed experts, one pass: item i ->
+// segment q = i / OT, row tile ot = i % OT. Segments 0..2: K groups [11q, 11q + 11) of the shared
+// down rows (33 groups) -> part[q][16*ot + r]; segments 3..10: expert slot k = q - 3, all 11 groups
+// of its down rows -> part[q][16*ot + r] = w_k * row. The table of segment q is tbl_dn + 11 q.
+__device__ void down_items(Smem& s, const Params& P, const GtmLayer& L, int i0, int i1) {
     const int n = i1 - i0;
     if (n <= 0) return;
     zero_slots(s, n);
     __syncthreads();
-    const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
+    const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
     const int lane_g = (threadIdx.x & 31) >> 2;
-    // items of different thirds use different group ranges: walk third by third
+    // items of different segments use different rows and tables: walk segment by segment
     int a = i0;
     while (a < i1) {
         const int q = a / OT;
         const int b = min(i1, (q + 1) * OT);
-        const int off = a - i0;
-        const int nn = b - a;
-        warp_items(s, off, nn, GFE, q * GFE, s.tbl_sh, s.xs_sh, s.cs_sh, [&](int item) {
-            const int ot = (a + item) - q * OT;
-            return down_rows(base, L.shared_down, ot * 16 + lane_g, FS / 2, GFS);
-        });
+        const int off = a - i0, nn = b - a;
+        if (q < 3) {
+            warp_items(s, off, nn, GFE, q * GFE, s.tbl_dn, s.xs_dn, s.cs_dn, [&](int item) {
+                const int ot = (a + item) - q * OT;
+                return down_rows(res, L.shared_down, ot * 16 + lane_g, FS / 2, GFS);
+            });
+        } else {
+            const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[q - 3] * L.expert_stride);
+            warp_items(s, off, nn, GFE, 0, s.tbl_dn + q * GFE * TBL_WORDS, s.xs_dn + q * GFE, s.cs_dn + q * GFE,
+                       [&](int item) {
+                           const int ot = (a + item) - q * OT;
+                           return down_rows(blk, L.expert_down, ot * 16 + lane_g, FE / 2, GFE);
+                       });
+        }
         a = b;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < n * 16; i += NT) {
         const int item = i >> 4, r = i & 15;
         const int it = i0 + item, q = it / OT, ot = it - q * OT;
-        P.part[(size_t)q * D + ot * 16 + r] = slot_sum(s, item, r);
-    }
-}
-
-// Routed down items [i0, i1): item i -> expert slot k = i / OT, row tile ot = i % OT
-// -> part[3 + k][16*ot + r] = w_k * (expert k's down row)
-__device__ void routed_down(Smem& s, const Params& P, const GtmLayer& L, int i0, int i1) {
-    const int n = i1 - i0;
-    if (n <= 0) return;
-    zero_slots(s, n);
-    __syncthreads();
-    const int lane_g = (threadIdx.x & 31) >> 2;
-    int a = i0;
-    while (a < i1) {
-        const int k = a / OT;
-        const int b = min(i1, (k + 1) * OT);
-        const int off = a - i0, nn = b - a;
-        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
-        warp_items(s, off, nn, GFE, 0, s.tbl_rk + k * GFE * TBL_WORDS, s.xs_rk + k * GFE, s.cs_rk + k * GFE, [&](int item) {
-            const int ot = (a + item) - k * OT;
-            return down_rows(blk, L.expert_down, ot * 16 + lane_g, FE / 2, GFE);
-        });
-        a = b;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < n * 16; i += NT) {
-        const int item = i >> 4, r = i & 15;
-        const int it = i0 + item, k = it / OT, ot = it - k * OT;
-        P.part[(size_t)(3 + k) * D + ot * 16 + r] = s.topw[k] * slot_sum(s, item, r);
+        const float v = slot_sum(s, item, r);
+        P.part[(size_t)q * D + ot * 16 + r] = q < 3 ? v : s.topw[q - 3] * v;
     }
 }
 
@@ -771,7 +755,7 @@ __device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
     const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
     const int nrow = cta < NE ? (NE - 1 - cta) / G + 1 : 0;          // router rows of this CTA
     const int t0 = share(TILES_S, cta, G), t1 = share(TILES_S, cta + 1, G);
-    const int i0 = share(ITEMS_SD, cta, G), i1 = share(ITEMS_SD, cta + 1, G);
+    const int i0 = min(share(ITEMS_DN, cta, G), ITEMS_SD), i1 = min(share(ITEMS_DN, cta + 1, G), ITEMS_SD);
     const int n_router = 3 * nrow, n_sgu = t1 > t0 ? 6 : 0, n_sd = 18 * (i1 - i0), n_vec = 6;
     const int total = n_router + n_sgu + n_sd + n_vec;
     for (int i = warp; i < total; i += NW) {
@@ -826,7 +810,7 @@ __device__ void prefetch_routed_gate_up(const Smem& s, const GtmLayer& L, int ct
 // L2 prefetch of this CTA's routed-down rows (known once the top-8 is).
 __device__ void prefetch_routed_down(const Smem& s, const GtmLayer& L, int cta, int G) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i0 = share(ITEMS_RD, cta, G), i1 = share(ITEMS_RD, cta + 1, G);
+    const int i0 = max(share(ITEMS_DN, cta, G), ITEMS_SD) - ITEMS_SD, i1 = max(share(ITEMS_DN, cta + 1, G), ITEMS_SD) - ITEMS_SD;
     for (int i = warp; i < 3 * (i1 - i0); i += NW) {
         const int it = i0 + i / 3, part = i % 3, k = it / OT, ot = it - k * OT;
         const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
@@ -871,8 +855,8 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
             __syncthreads();
         }
         arrive(P, BAR_A1, ep);
+        // (its shared activations are published by the B arrival below, which follows in order)
         shared_gate_up(s, P, L, share(TILES_S, cta, G), share(TILES_S, cta + 1, G));
-        arrive(P, BAR_A2, ep);
 
         // ---- P2 ----
         if (!wait_all(P, s, BAR_A1, ep)) return;
@@ -884,27 +868,22 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
         prefetch_routed_down(s, L, cta, G);
         routed_gate_up(s, P, L, share(TILES_R, cta, G), share(TILES_R, cta + 1, G));
         arrive(P, BAR_B, ep);
-        if (!wait_all(P, s, BAR_A2, ep)) return;
-        stage_from_global(s.ab, P.act + ACT_R, FS);
-        build_table(s.ab, GFS, s.tbl_sh, s.xs_sh, s.cs_sh);
-        __syncthreads();
-        shared_down(s, P, L, share(ITEMS_SD, cta, G), share(ITEMS_SD, cta + 1, G));
 
-        // ---- P3 ----
+        // ---- P3: shared and routed down in one pass (every CTA's B arrival follows its shared
+        //      gate/up, so B covers both activation sets) ----
         if (!wait_all(P, s, BAR_B, ep)) return;
-        {
-            const int i0 = share(ITEMS_RD, cta, G), i1 = share(ITEMS_RD, cta + 1, G);
-            if (i1 > i0) {
-                const int kmin = i0 / OT, kmax = (i1 - 1) / OT;
-                stage_from_global(s.ab + kmin * FE, P.act + kmin * FE, (kmax - kmin + 1) * FE);
-                build_table(s.ab + kmin * FE, (kmax - kmin + 1) * GFE, s.tbl_rk + kmin * GFE * TBL_WORDS,
-                            s.xs_rk + kmin * GFE, s.cs_rk + kmin * GFE);
-            }
-            __syncthreads();
+        const int d0 = share(ITEMS_DN, cta, G), d1 = share(ITEMS_DN, cta + 1, G);
+        if (d1 > d0) {
+            // the segments this CTA's items read (at most 2 for >= 118 CTAs), staged from 0
+            const int qmin = d0 / OT, qmax = (d1 - 1) / OT;
+            stage_from_global(s.ab, P.act + qmin * SEGK, (qmax - qmin + 1) * SEGK);
+            build_table(s.ab, (qmax - qmin + 1) * GFE, s.tbl_dn + qmin * GFE * TBL_WORDS, s.xs_dn + qmin * GFE,
+                        s.cs_dn + qmin * GFE);
         }
+        __syncthreads();
         if (l + 1 < P.num_layers) prefetch_layer_static(P.layers[l + 1], cta, G);
         load_norms_async(s, l + 1 < P.num_layers ? &P.layers[l + 1] : nullptr, &L);
-        routed_down(s, P, L, share(ITEMS_RD, cta, G), share(ITEMS_RD, cta + 1, G));
+        down_items(s, P, L, d0, d1);
         arrive(P, BAR_C, ep);
     }
 
@@ -948,7 +927,7 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
     float* f = reinterpret_cast<float*>(w + kDataOffset);
     P.logits = f;
     P.act = f + NE;
-    P.part = P.act + ACT_R + FS;
+    P.part = P.act + FS + ACT_R;
     cudaError_t e = cudaMemsetAsync(w, 0, kErrOffset + sizeof(int), stream);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: memset", e);
     const size_t smem = sizeof(Smem);
