@@ -22,12 +22,12 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hid
 
 
 def sources() -> list[str]:
-    return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")))
+    return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")) + glob.glob(os.path.join(HERE, "csrc", "*.cpp")))
 
 
 def deps() -> list[str]:
     return sources() + sorted(glob.glob(os.path.join(HERE, "csrc", "*.h*"))) + \
-        sorted(glob.glob(os.path.join(HERE, "csrc", "*.cuh"))) + [os.path.join(ROOT, "include", "gtmoe.h")]
+        sorted(glob.glob(os.path.join(HERE, "csrc", "*.cuh"))) + sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
 def up_to_date() -> bool:

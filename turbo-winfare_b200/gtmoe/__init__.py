@@ -85,9 +85,18 @@ class EpPeers(C.Structure):
     _fields_ = [("workspace_dev", C.c_void_p * EP_PEER_MAX_WORLD)]
 
 
+class BundleInfo(C.Structure):
+    _fields_ = [("num_layers", C.c_uint32), ("experts_per_layer", C.c_uint32), ("hidden", C.c_uint32),
+                ("moe_inter", C.c_uint32), ("ffn_inter", C.c_uint32), ("top_k", C.c_uint32),
+                ("rms_norm_eps", C.c_float), ("resident_entries", C.c_uint32), ("expert_stride", C.c_uint64),
+                ("resident_bytes", C.c_uint64), ("resident_index_bytes", C.c_uint64),
+                ("layer_file_bytes", C.c_uint64)]
+
+
 _lib = None
 
-# (name, restype, argtypes) for every entry point in include/gtmoe.h and include/gtmoe_synth.h
+# (name, restype, argtypes) for every entry point in include/gtmoe.h, include/gtmoe_synth.h and
+# include/gtmoe_bundle.h
 _P, _U32, _U64, _I, _F, _SZ = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_size_t
 SIGNATURES = {
     "gtm_last_error": (C.c_char_p, []),
@@ -141,6 +150,12 @@ SIGNATURES = {
     "gtm_ipc_open": (_I, [_P, C.POINTER(_P)]),
     "gtm_ipc_close": (_I, [_P]),
     "gtm_ipc_free": (_I, [_P]),
+    "gtm_bundle_open": (_I, [C.c_char_p, C.POINTER(_P)]),
+    "gtm_bundle_close": (_I, [_P]),
+    "gtm_bundle_info": (_I, [_P, C.POINTER(BundleInfo)]),
+    "gtm_bundle_load_resident": (_I, [_P, _P, _U64]),
+    "gtm_bundle_load_experts": (_I, [_P, _U32, _U32, _U32, _P, _U64]),
+    "gtm_bundle_layer_desc": (_I, [_P, _U32, _P, _P, C.POINTER(Layer)]),
     "gtm_synth_expert_layout": (_I, [_U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_resident_layout": (_I, [_U32, _U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_experts": (_I, [_U64, _U32, _U32, _U32, _U32, _U32, _P, _P]),
