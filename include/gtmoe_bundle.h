@@ -17,7 +17,8 @@
  * cache. The bytes are copied unchanged; GtmLayer then addresses them by the index's offsets.
  *
  * Loads are blocking: they return once the bytes are in device memory. Reader threads read the
- * files into pinned staging buffers and copy each chunk to the device with cudaMemcpyAsync.
+ * files into pinned staging buffers (allocated on the first load, kept until gtm_bundle_close)
+ * and copy each chunk to the device with cudaMemcpyAsync. One thread at a time per bundle.
  */
 #ifndef GTMOE_BUNDLE_H
 #define GTMOE_BUNDLE_H

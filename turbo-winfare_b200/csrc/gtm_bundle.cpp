@@ -295,6 +295,48 @@ struct Sub {
     uint8_t dtype;
 };
 
+// Staging kept for the bundle's lifetime (pinned allocations are slow): per reader thread two
+// pinned chunk buffers, a stream and two events, created on the first load.
+constexpr int kReaders = 4;
+constexpr uint64_t kChunk = 16ull << 20;
+struct Reader {
+    cudaStream_t st = nullptr;
+    void* stage[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+};
+struct Stager {
+    int device = -1;
+    Reader r[kReaders];
+    cudaError_t init(int dev) {
+        if (device == dev) return cudaSuccess;
+        release();
+        cudaError_t e = cudaSuccess;
+        for (int k = 0; k < kReaders && e == cudaSuccess; ++k) {
+            e = cudaStreamCreateWithFlags(&r[k].st, cudaStreamNonBlocking);
+            for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+                e = cudaHostAlloc(&r[k].stage[b], kChunk, cudaHostAllocDefault);
+                if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r[k].done[b], cudaEventDisableTiming);
+            }
+        }
+        if (e != cudaSuccess) release();
+        else device = dev;
+        return e;
+    }
+    void release() {
+        for (Reader& x : r) {
+            for (int b = 0; b < 2; ++b) {
+                if (x.done[b]) cudaEventDestroy(x.done[b]);
+                if (x.stage[b]) cudaFreeHost(x.stage[b]);
+                x.done[b] = nullptr;
+                x.stage[b] = nullptr;
+            }
+            if (x.st) cudaStreamDestroy(x.st);
+            x.st = nullptr;
+        }
+        device = -1;
+    }
+};
+
 }  // namespace bundle
 }  // namespace gtm
 
@@ -304,6 +346,8 @@ struct GtmBundle {
     std::map<std::string, gtm::bundle::Entry> entries;
     std::map<std::string, gtm::bundle::Sub> block;
     std::vector<std::string> layer_files;   // by layer id
+    gtm::bundle::Stager stager;
+    ~GtmBundle() { stager.release(); }
 };
 
 namespace gtm {
@@ -461,38 +505,33 @@ void parse_resident(GtmBundle& B) {
 }
 
 // ---- file -> device ---------------------------------------------------------------------------
-// Chunks of the byte range go round-robin to reader threads; each thread owns two pinned
-// staging buffers and a stream, reads a chunk with pread while its previous chunk's copy runs.
-int load_range(const std::string& path, uint64_t offset, uint64_t bytes, void* dst, const char* what) {
+// Chunks of the byte range go round-robin to the reader threads; each reads a chunk with pread
+// into one of its two pinned buffers while the copy of its previous chunk runs on its stream.
+int load_range(Stager& S, const std::string& path, uint64_t offset, uint64_t bytes, void* dst, const char* what) {
     if (bytes == 0) return GTM_OK;
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 == cudaSuccess) e0 = S.init(dev);
+    if (e0 != cudaSuccess) return set_cuda_error(what, e0);
     const int fd = open(path.c_str(), O_RDONLY);
     if (fd < 0) return set_error(GTM_ERR_INVALID, "%s: cannot open %s", what, path.c_str());
-    constexpr uint64_t kChunk = 16ull << 20;
     const uint64_t nchunks = (bytes + kChunk - 1) / kChunk;
-    const int nthreads = (int)std::min<uint64_t>(nchunks, 4);
-    int dev = 0;
-    cudaGetDevice(&dev);
+    const int nthreads = (int)std::min<uint64_t>(nchunks, kReaders);
     std::vector<int> status(nthreads, GTM_OK);
     std::vector<std::string> msg(nthreads);
     auto worker = [&](int k) {
         cudaSetDevice(dev);
-        cudaStream_t st = nullptr;
-        void* stage[2] = {nullptr, nullptr};
-        cudaEvent_t done[2] = {nullptr, nullptr};
-        cudaError_t e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
-        for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
-            e = cudaHostAlloc(&stage[b], kChunk, cudaHostAllocDefault);
-            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming);
-        }
+        Reader& R = S.r[k];
+        cudaError_t e = cudaSuccess;
         int used = 0;
-        for (uint64_t c = (uint64_t)k; e == cudaSuccess && c < nchunks; c += (uint64_t)nthreads, ++used) {
+        for (uint64_t c = (uint64_t)k; c < nchunks; c += (uint64_t)nthreads, ++used) {
             const int b = used & 1;
-            if (used >= 2) e = cudaEventSynchronize(done[b]);   // the copy that last used this buffer
+            if (used >= 2) e = cudaEventSynchronize(R.done[b]);   // the copy that last used this buffer
             if (e != cudaSuccess) break;
             const uint64_t off = c * kChunk, n = std::min(kChunk, bytes - off);
             uint64_t got = 0;
             while (got < n) {
-                const ssize_t r = pread(fd, static_cast<uint8_t*>(stage[b]) + got, n - got, (off_t)(offset + off + got));
+                const ssize_t r = pread(fd, static_cast<uint8_t*>(R.stage[b]) + got, n - got, (off_t)(offset + off + got));
                 if (r <= 0) {
                     if (r < 0 && errno == EINTR) continue;
                     status[k] = GTM_ERR_INVALID;
@@ -502,22 +541,16 @@ int load_range(const std::string& path, uint64_t offset, uint64_t bytes, void* d
                 got += (uint64_t)r;
             }
             if (status[k] != GTM_OK) break;
-            e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, stage[b], n, cudaMemcpyHostToDevice, st);
-            if (e == cudaSuccess) e = cudaEventRecord(done[b], st);
+            e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, R.stage[b], n, cudaMemcpyHostToDevice, R.st);
+            if (e == cudaSuccess) e = cudaEventRecord(R.done[b], R.st);
+            if (e != cudaSuccess) break;
         }
-        if (st) {
-            const cudaError_t e2 = cudaStreamSynchronize(st);
-            if (e == cudaSuccess) e = e2;
-        }
+        const cudaError_t e2 = cudaStreamSynchronize(R.st);
+        if (e == cudaSuccess) e = e2;
         if (e != cudaSuccess && status[k] == GTM_OK) {
             status[k] = GTM_ERR_CUDA;
             msg[k] = cudaGetErrorString(e);
         }
-        for (int b = 0; b < 2; ++b) {
-            if (done[b]) cudaEventDestroy(done[b]);
-            if (stage[b]) cudaFreeHost(stage[b]);
-        }
-        if (st) cudaStreamDestroy(st);
     };
     std::vector<std::thread> th;
     for (int k = 0; k < nthreads; ++k) th.emplace_back(worker, k);
@@ -607,7 +640,7 @@ GTM_API int gtm_bundle_load_resident(GtmBundle* B, void* dst, uint64_t dst_bytes
     if (dst_bytes < B->info.resident_bytes)
         return gtm::set_error(GTM_ERR_WORKSPACE, "gtm_bundle_load_resident: needs %llu bytes",
                               (unsigned long long)B->info.resident_bytes);
-    const int rc = gtm::bundle::load_range(B->dir + "/resident.bin", 0, B->info.resident_bytes, dst,
+    const int rc = gtm::bundle::load_range(B->stager, B->dir + "/resident.bin", 0, B->info.resident_bytes, dst,
                                            "gtm_bundle_load_resident");
     if (rc == GTM_OK) gtm::clear_error();
     return rc;
@@ -622,7 +655,7 @@ GTM_API int gtm_bundle_load_experts(GtmBundle* B, uint32_t layer, uint32_t first
     const uint64_t bytes = (uint64_t)count * B->info.expert_stride;
     if (dst_bytes < bytes)
         return gtm::set_error(GTM_ERR_WORKSPACE, "gtm_bundle_load_experts: needs %llu bytes", (unsigned long long)bytes);
-    const int rc = gtm::bundle::load_range(B->dir + "/packed_experts/" + B->layer_files[layer],
+    const int rc = gtm::bundle::load_range(B->stager, B->dir + "/packed_experts/" + B->layer_files[layer],
                                            (uint64_t)first * B->info.expert_stride, bytes, dst, "gtm_bundle_load_experts");
     if (rc == GTM_OK) gtm::clear_error();
     return rc;
