@@ -250,6 +250,25 @@ GTM_API int gtm_moe_tokens(const GtmDims* dims, const GtmLayer* layer, const Gtm
 GTM_API int gtm_moe_tokens_check(void* workspace_dev, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Tied LM head with greedy argmax: LMHeadGreedy + ArgmaxReduce (shaders/LMHeadGreedy.hlsl:1-73,
+ * shaders/ArgmaxReduce.hlsl:1-62; runner.cpp:720-770). token = argmax_r logits[r], ties to the
+ * lower row, over the int4 matvec of x (the final-normed hidden state) with the embedding
+ * matrix (rows = vocab, in_dim = hidden; group-64 bf16 scales and biases). The winning logit
+ * is bit-identical to the CPU reference's (cpu_reference.cpp:55-83 order), so the token is the
+ * reference's: every row is first evaluated on the tensor cores with a rigorous error bound,
+ * and every row whose bound interval reaches the best lower bound is recomputed in the exact
+ * CPU order. Softcap is monotonic and, as in the reference's greedy path, not applied.
+ * ------------------------------------------------------------------------------------- */
+GTM_API size_t gtm_lm_head_workspace_bytes(uint32_t rows);
+/* in_dim must be 2816; rows >= 1. token_dev: uint32 on the device; logit_dev (nullable): the
+ * exact logit of the token. Asynchronous on `stream`; the workspace needs no initialisation. */
+GTM_API int gtm_lm_head_greedy(uint32_t rows, uint32_t in_dim, const void* w_dev, const uint16_t* s_dev,
+                               const uint16_t* b_dev, const float* x_dev, uint32_t* token_dev, float* logit_dev,
+                               void* workspace_dev, size_t workspace_bytes, void* stream);
+/* Rows the last call on this workspace recomputed exactly (synchronises `stream`). */
+GTM_API int gtm_lm_head_candidates(void* workspace_dev, void* stream, int32_t* count_out);
+
+/* ---------------------------------------------------------------------------------------
  * Expert-parallel MoE layer: rank r of `world` owns experts [r*E/world, (r+1)*E/world) and
  * its own tokens. No reference counterpart (the reference is single-GPU). The caller moves
  * rows between ranks (NCCL all-to-all over NVLink) between the phases:

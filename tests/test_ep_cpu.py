@@ -165,3 +165,111 @@ def test_local_exchange_matches_protocol():
     assert got[2].view(-1).tolist() == [3, 4, 5, 24, 25]
     counts = xch.counts([torch.tensor(s, dtype=torch.int32) for s in splits])
     assert [c.tolist() for c in counts] == recv_splits
+
+
+# ---- the peer-memory protocol (ep_layer_peer) ------------------------------------------------------
+# Stand-in ops keep each rank's "workspace" as files in a directory shared by the processes: the
+# dispatch stores every token's top-K into each rank's directory and its row into the directories
+# of the ranks that own one of its experts; the experts phase reads only its own directory and
+# stores each unweighted result into the token's rank; the combine reads its own results. Without
+# the two barriers a rank would read files a peer has not written yet.
+
+class StandInPeerOps:
+    def __init__(self, rank, world, root, skew):
+        self.rank, self.world, self.root, self.skew = rank, world, root, skew
+        self.e0, self.e1 = ep.experts_of(rank, world, E)
+        self.layer = 0
+
+    def _ws(self, r):
+        return os.path.join(self.root, f"ws{r}")
+
+    def dispatch(self, x):
+        xs = x.numpy()
+        idx, w = route(xs, self.skew) if len(xs) else (np.zeros((0, K), np.int64), np.zeros((0, K), np.float32))
+        self.w = w
+        epr = E // self.world
+        for r in range(self.world):
+            owns = [t for t in range(len(xs)) if any(idx[t, k] // epr == r for k in range(K))]
+            np.savez(os.path.join(self._ws(r), f"L{self.layer}_from{self.rank}.npz"), idx=idx,
+                     rows=xs[owns] if owns else np.zeros((0, D), np.float32), owns=np.asarray(owns, np.int64))
+
+    def shared(self, x):
+        self.shared_out = 2.0 * x.numpy()
+
+    def experts(self):
+        for s in range(self.world):
+            z = np.load(os.path.join(self._ws(self.rank), f"L{self.layer}_from{s}.npz"))
+            idx, rows, owns = z["idx"], z["rows"], list(z["owns"])
+            ret = {}
+            for t in range(len(idx)):
+                for k in range(K):
+                    e = int(idx[t, k])
+                    if self.e0 <= e < self.e1:
+                        ret[t * K + k] = expert_fn(e, np.float32(1.0), rows[owns.index(t)])
+            np.savez(os.path.join(self._ws(s), f"L{self.layer}_ret{self.rank}.npz"),
+                     pos=np.asarray(list(ret.keys()), np.int64),
+                     val=np.asarray(list(ret.values()), np.float32).reshape(-1, D))
+
+    def combine(self, x, hidden_out):
+        T = x.shape[0]
+        got = np.full((T * K, D), np.nan, np.float32)
+        for r in range(self.world):
+            z = np.load(os.path.join(self._ws(self.rank), f"L{self.layer}_ret{r}.npz"))
+            for p, v in zip(z["pos"], z["val"]):
+                got[p] = v
+        res = self.shared_out.copy()
+        for t in range(T):
+            for k in range(K):
+                res[t] += self.w[t, k] * got[t * K + k]
+        hidden_out.copy_(torch.from_numpy(res))
+        self.layer += 1
+
+
+def peer_worker(rank, world, port, root, counts, skews, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        bar = ep.NcclBarrier(device="cpu")
+        errs = []
+        ops = StandInPeerOps(rank, world, root, None)
+        for case, (n, skew) in enumerate(zip(counts, skews)):
+            ops.skew = np.asarray(skew, np.float32)
+            rng = np.random.default_rng(200 + 10 * case + rank)
+            x = rng.standard_normal((n[rank], D)).astype(np.float32)
+            out = torch.zeros(n[rank], D)
+            ep.ep_layer_peer(ops, bar, torch.from_numpy(x), out)
+            exp = expected(x, ops.skew) if len(x) else np.zeros((0, D), np.float32)
+            errs.append(float(np.abs(out.numpy() - exp).max()) if len(x) else 0.0)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, errs, None))
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, repr(e)))
+
+
+def test_ep_peer_protocol_two_gloo_ranks(tmp_path):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world = 2
+    for r in range(world):
+        os.makedirs(tmp_path / f"ws{r}")
+    counts = [(6, 6), (5, 0), (0, 3), (7, 2)]   # ragged ranks, empty ranks
+    skews = [[0.0] * E, [0.0] * E, [60.0] * 4 + [0.0] * 4, [0.0] * 6 + [60.0] * 2]
+    port = free_port()
+    procs = [ctx.Process(target=peer_worker, args=(r, world, port, str(tmp_path), counts, skews, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        rank, errs, err = q.get(timeout=120)
+        assert err is None, f"rank {rank}: {err}"
+        out[rank] = errs
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert max(out[r]) < 1e-5, out[r]

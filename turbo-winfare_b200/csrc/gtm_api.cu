@@ -327,6 +327,41 @@ GTM_API int gtm_moe_tokens_check(void* ws, void* stream) {
     return rc;
 }
 
+// ---- tied LM head, greedy --------------------------------------------------------------------------
+static int sm_count(const char* fn, int* sms);
+
+GTM_API size_t gtm_lm_head_workspace_bytes(uint32_t rows) {
+    return rows == 0 ? 0 : lm_head_workspace_bytes(rows);
+}
+
+GTM_API int gtm_lm_head_greedy(uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
+                               const float* x, uint32_t* token, float* logit, void* ws, size_t ws_bytes, void* stream) {
+    const char* fn = "gtm_lm_head_greedy";
+    if (rows == 0 || !w || !s || !b || !x || !token) return set_error(GTM_ERR_INVALID, "%s: null pointer or zero rows", fn);
+    if (in_dim != 2816) return set_error(GTM_ERR_UNSUPPORTED, "%s: built for in_dim 2816 (got %u)", fn, in_dim);
+    if (!aligned(w, 16) || !aligned(s, 2) || !aligned(b, 2) || !aligned(x, 16) || !aligned(token, 4) || !aligned(logit, 4))
+        return set_error(GTM_ERR_MISALIGNED, "%s: weights and x must be 16-byte aligned", fn);
+    const size_t need = lm_head_workspace_bytes(rows);
+    if (!ws || ws_bytes < need || !aligned(ws, 256))
+        return set_error(GTM_ERR_WORKSPACE, "%s: workspace needs %zu bytes, 256-byte aligned", fn, need);
+    int sms = 0;
+    int rc = sm_count(fn, &sms);
+    if (rc) return rc;
+    rc = launch_lm_head(rows, w, s, b, x, token, logit, ws, (cudaStream_t)stream, sms);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
+GTM_API int gtm_lm_head_candidates(void* ws, void* stream, int32_t* count) {
+    if (!ws || !count) return set_error(GTM_ERR_INVALID, "gtm_lm_head_candidates: null argument");
+    int n = 0;
+    const int rc = lm_head_candidates(ws, (cudaStream_t)stream, &n);
+    if (rc) return rc;
+    *count = n;
+    clear_error();
+    return GTM_OK;
+}
+
 // ---- expert parallelism -------------------------------------------------------------------------
 static bool ep_config_ok(const GtmEpConfig* ep) {
     return ep && ep->world >= 1 && ep->world <= GTM_EP_MAX_WORLD && 128 % ep->world == 0 && ep->rank < ep->world &&

@@ -26,6 +26,7 @@
 //       tiles, partials x w_k) in one pass; L2-prefetch the next layer's router row, shared
 //       gate/up and down                                                      -> arrive C
 // The down partials [3 shared + 8 routed][2816] are summed in fixed order by the next tail.
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <cuda_fp16.h>
@@ -897,6 +898,198 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
     for (int i = tid; i < D; i += NT) io.hidden_out_dev[i] = s.hid[i];
 }
 
+// ================================================================================================
+// Tied LM head + greedy argmax (LMHeadGreedy.hlsl:1-73 + ArgmaxReduce.hlsl:1-62, runner.cpp:720-770)
+//
+// token = argmax_r logits[r], ties to the lower row, where logits = the int4 matvec of the normed
+// hidden state in the CPU reference's exact operation order (cpu_reference.cpp:55-83; softcap is
+// monotonic and skipped, as in the reference's greedy path). Computing every row in that order
+// is issue-bound, so:
+//   1. lm_approx: every row by the decode's mma.sync tiles (fp16 integer weights, fp16 high/low
+//      activations, fp32 accumulation), HBM-bound, together with a rigorous bound E_r on the
+//      distance between that value and the exact CPU-order value:
+//        E_r = 2^-14 * sum_g (1100 |s_g| + 2 |b_g|) * sum_{k in g} |x_k|
+//      (the MMA path's fp32 accumulation around its 1024 offset errs by < 64 * 2^-23 * 1039 |s| A_g
+//      per group, the CPU order's own roundings by < (64 * 15 + 44 * 16) * 2^-24 (|s| + |b|) A_g,
+//      and the x-sum orders differ by < 64 * 2^-24 A_g: E_r is 8x or more above each);
+//   2. lm_exact: L = max_r (approx_r - E_r); only rows with approx_r + E_r >= L can hold the
+//      maximum. Each of them is recomputed in the exact CPU order (one warp per row, a lane per
+//      group, the groups summed in order by one lane) and folded into a 64-bit key (orderable
+//      value, then the complement of the row) by atomicMax, which keeps (value desc, row asc)
+//      independently of the order the rows arrive in;
+//   3. lm_finish: the key -> token id and exact logit.
+// Degenerate inputs (x = 0: every row ties) only make step 2 longer: every candidate is exact.
+// ================================================================================================
+constexpr int LM_THREADS = 256;   // 75 registers: three CTAs (24 warps) per SM
+
+struct LmArgs {
+    const uint8_t* w;        // [rows][D/2] packed int4, low nibble first
+    const uint16_t* s;       // [rows][GD] bf16 scales
+    const uint16_t* b;       // [rows][GD] bf16 biases
+    const float* x;          // [D] normed hidden state
+    int rows;
+    float2* ae;              // [rows] (approximate logit, bound)
+    float* cta_lb;           // [gridDim of lm_approx] max of approx - bound per CTA
+    int n_lb;
+    unsigned long long* key; // best (value, row)
+    int* n_cand;             // rows recomputed exactly
+    uint32_t* token;
+    float* logit;            // exact logit of the token (nullable)
+};
+
+__device__ __forceinline__ uint32_t orderable(float v) {
+    const uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float from_orderable(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+__global__ void __launch_bounds__(LM_THREADS) lm_approx(const __grid_constant__ LmArgs A) {
+    __shared__ __align__(16) float sx[D];
+    __shared__ __align__(16) uint32_t tbl[GD * TBL_WORDS];
+    __shared__ float xs[GD], cs[GD], xa[GD];
+    __shared__ float wlb[LM_THREADS / 32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    if (blockIdx.x == 0 && tid == 0) { *A.key = 0ull; *A.n_cand = 0; }
+    for (int i = tid; i < D; i += blockDim.x) sx[i] = A.x[i];
+    __syncthreads();
+    build_table(sx, GD, tbl, xs, cs);
+    for (int j = tid; j < GD; j += blockDim.x) {
+        float a = 0.0f;
+        for (int k = 0; k < kGroup; ++k) a += fabsf(sx[j * kGroup + k]);
+        xa[j] = a;
+    }
+    __syncthreads();
+    float lb = -INFINITY;
+    const int ntiles = (A.rows + 15) / 16;
+    for (int tile = blockIdx.x * (LM_THREADS / 32) + warp; tile < ntiles; tile += gridDim.x * (LM_THREADS / 32)) {
+        const int ra = min(tile * 16 + g, A.rows - 1), rb = min(tile * 16 + 8 + g, A.rows - 1);
+        TileRows R;
+        R.wa = A.w + (size_t)ra * (D / 2);
+        R.wb = A.w + (size_t)rb * (D / 2);
+        R.sa = A.s + (size_t)ra * GD;
+        R.ba = A.b + (size_t)ra * GD;
+        R.sb = A.s + (size_t)rb * GD;
+        R.bb = A.b + (size_t)rb * GD;
+        float ya = 0.0f, yb = 0.0f, ea = 0.0f, eb = 0.0f;
+        QuadLoads cur = load_quad(R, 0, 0, GD, t);
+        for (int q0 = 0; q0 < GD; q0 += 4) {
+            QuadLoads nxt = cur;
+            if (q0 + 4 < GD) nxt = load_quad(R, q0 + 4, 0, GD, t);
+            compute_quad(cur, q0, 0, GD, tbl, xs, cs, ya, yb);
+            const int j = q0 + t;
+            if (j < GD) {
+                ea = fmaf(fmaf(1100.0f, fabsf(bf16f(cur.sa)), 2.0f * fabsf(bf16f(cur.ba))), xa[j], ea);
+                eb = fmaf(fmaf(1100.0f, fabsf(bf16f(cur.sb)), 2.0f * fabsf(bf16f(cur.bb))), xa[j], eb);
+            }
+            cur = nxt;
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            ya += __shfl_xor_sync(0xffffffffu, ya, o);
+            yb += __shfl_xor_sync(0xffffffffu, yb, o);
+            ea += __shfl_xor_sync(0xffffffffu, ea, o);
+            eb += __shfl_xor_sync(0xffffffffu, eb, o);
+        }
+        // the bound's own fp32 sums are below 2^-20 of it: round it up by 2^-10
+        ea *= 6.103515625e-05f * 1.0009765625f;
+        eb *= 6.103515625e-05f * 1.0009765625f;
+        if (t == 0) {
+            const int r0 = tile * 16 + g, r1 = r0 + 8;
+            if (r0 < A.rows) { A.ae[r0] = make_float2(ya, ea); lb = fmaxf(lb, ya - ea); }
+            if (r1 < A.rows) { A.ae[r1] = make_float2(yb, eb); lb = fmaxf(lb, yb - eb); }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lb = fmaxf(lb, __shfl_xor_sync(0xffffffffu, lb, o));
+    if (lane == 0) wlb[warp] = lb;
+    __syncthreads();
+    if (tid == 0) {
+        float m = wlb[0];
+        for (int w = 1; w < LM_THREADS / 32; ++w) m = fmaxf(m, wlb[w]);
+        A.cta_lb[blockIdx.x] = m;
+    }
+}
+
+// Exact CPU-order logit of one row (cpu_reference.cpp:55-83): lane l takes groups l and l + 32;
+// per group dot += q_lo * x0, dot += q_hi * x1, sum += x0 + x1 element pair by pair, then
+// term = s * dot + b * sum; lane 0 adds the 44 terms in group order.
+__device__ float exact_row(const LmArgs& A, const float* sx, float* terms, int row) {
+    const int lane = threadIdx.x & 31;
+    const uint8_t* wr = A.w + (size_t)row * (D / 2);
+    for (int gi = lane; gi < GD; gi += 32) {
+        const float s = bf16f(A.s[(size_t)row * GD + gi]), b = bf16f(A.b[(size_t)row * GD + gi]);
+        const uint4* wq = reinterpret_cast<const uint4*>(wr + gi * (kGroup / 2));
+        const uint4 q0 = wq[0], q1 = wq[1];
+        const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const float* xg = sx + gi * kGroup;
+        float dot = 0.0f, sum = 0.0f;
+#pragma unroll
+        for (int wi = 0; wi < 8; ++wi) {
+#pragma unroll
+            for (int by = 0; by < 4; ++by) {
+                const uint32_t byte = (words[wi] >> (8 * by)) & 0xFFu;
+                const int e = wi * 8 + by * 2;
+                const float x0 = xg[e], x1 = xg[e + 1];
+                dot = __fadd_rn(dot, __fmul_rn((float)(byte & 0x0Fu), x0));
+                dot = __fadd_rn(dot, __fmul_rn((float)(byte >> 4), x1));
+                sum = __fadd_rn(sum, __fadd_rn(x0, x1));
+            }
+        }
+        terms[gi] = __fadd_rn(__fmul_rn(s, dot), __fmul_rn(b, sum));
+    }
+    __syncwarp();
+    float acc = 0.0f;
+    if (lane == 0)
+        for (int gi = 0; gi < GD; ++gi) acc = __fadd_rn(acc, terms[gi]);
+    __syncwarp();
+    return acc;
+}
+
+__global__ void __launch_bounds__(256) lm_exact(const __grid_constant__ LmArgs A) {
+    __shared__ __align__(16) float sx[D];
+    __shared__ float terms[256 / 32][GD];
+    __shared__ float s_l;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < D; i += blockDim.x) sx[i] = A.x[i];
+    if (tid < 32) {
+        float m = -INFINITY;
+        for (int i = tid; i < A.n_lb; i += 32) m = fmaxf(m, A.cta_lb[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (tid == 0) s_l = m;
+    }
+    __syncthreads();
+    const float L = s_l;
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    for (int base = (blockIdx.x * (blockDim.x >> 5) + warp) * 32; base < A.rows; base += nw * 32) {
+        const int r = base + lane;
+        bool cand = false;
+        if (r < A.rows) {
+            const float2 v = A.ae[r];
+            cand = v.x + v.y >= L;
+        }
+        unsigned m = __ballot_sync(0xffffffffu, cand);
+        while (m) {
+            const int k = __ffs(m) - 1;
+            m &= m - 1;
+            const int row = base + k;
+            const float v = exact_row(A, sx, terms[warp], row);
+            if (lane == 0) {
+                atomicMax(A.key, ((unsigned long long)orderable(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row));
+                atomicAdd(A.n_cand, 1);
+            }
+        }
+    }
+}
+
+__global__ void lm_finish(const __grid_constant__ LmArgs A) {
+    const unsigned long long k = *A.key;
+    *A.token = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+    if (A.logit) *A.logit = from_orderable((uint32_t)(k >> 32));
+}
+
 }  // namespace dec
 
 // Workspace: [0, 4096) barrier flags (4 kinds x 256 CTAs) and [4096] this launch's error word,
@@ -940,6 +1133,43 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
     void* args[] = {(void*)&P};
     e = cudaLaunchCooperativeKernel((const void*)moe_decode_kernel, dim3(num_ctas), dim3(NT), args, smem, stream);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: cooperative launch", e);
+    return GTM_OK;
+}
+
+}  // namespace gtm
+
+namespace gtm {
+
+size_t lm_head_workspace_bytes(uint32_t rows) {
+    return 256 + (size_t)rows * 8 + 4096 * 4;
+}
+
+int launch_lm_head(uint32_t rows, const void* w, const uint16_t* s, const uint16_t* b, const float* x, uint32_t* token,
+                   float* logit, void* ws, cudaStream_t st, int num_sms) {
+    using namespace dec;
+    uint8_t* p = static_cast<uint8_t*>(ws);
+    LmArgs A;
+    memset(&A, 0, sizeof(A));
+    A.w = static_cast<const uint8_t*>(w); A.s = s; A.b = b; A.x = x; A.rows = (int)rows;
+    A.key = reinterpret_cast<unsigned long long*>(p);
+    A.n_cand = reinterpret_cast<int*>(p + 8);
+    A.ae = reinterpret_cast<float2*>(p + 256);
+    A.cta_lb = reinterpret_cast<float*>(p + 256 + (size_t)rows * 8);
+    A.token = token; A.logit = logit;
+    const int g1 = std::min(num_sms * 3, 4096);   // persistent: three CTAs per SM
+    A.n_lb = g1;
+    lm_approx<<<g1, LM_THREADS, 0, st>>>(A);
+    lm_exact<<<num_sms * 4, 256, 0, st>>>(A);
+    lm_finish<<<1, 1, 0, st>>>(A);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("gtm_lm_head_greedy", e);
+    return GTM_OK;
+}
+
+int lm_head_candidates(void* ws, cudaStream_t st, int* n) {
+    const cudaError_t e = cudaMemcpyAsync(n, static_cast<uint8_t*>(ws) + 8, sizeof(int), cudaMemcpyDeviceToHost, st);
+    const cudaError_t e2 = e == cudaSuccess ? cudaStreamSynchronize(st) : e;
+    if (e2 != cudaSuccess) return set_cuda_error("gtm_lm_head_candidates", e2);
     return GTM_OK;
 }
 

@@ -18,6 +18,11 @@ constexpr int kDecodeMinCtas = 118;   // per-CTA work lists of the fused decode 
 int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, const GtmDecodeIO& io,
                   void* ws, size_t ws_bytes, cudaStream_t stream, int num_ctas);
 
+size_t lm_head_workspace_bytes(uint32_t rows);
+int launch_lm_head(uint32_t rows, const void* w, const uint16_t* s, const uint16_t* b, const float* x, uint32_t* token,
+                   float* logit, void* ws, cudaStream_t st, int num_sms);
+int lm_head_candidates(void* ws, cudaStream_t st, int* n);
+
 size_t tokens_workspace_bytes(uint32_t max_tokens);
 int launch_tokens(const GtmDims& dims, const GtmLayer& layer, const GtmTokensIO& io, void* ws, size_t ws_bytes,
                   cudaStream_t stream, int num_sms);

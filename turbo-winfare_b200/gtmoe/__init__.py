@@ -127,6 +127,9 @@ SIGNATURES = {
     "gtm_moe_tokens_workspace_bytes": (_SZ, [C.POINTER(Dims), _U32]),
     "gtm_moe_tokens": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), _P, _SZ, _P]),
     "gtm_moe_tokens_check": (_I, [_P, _P]),
+    "gtm_lm_head_workspace_bytes": (_SZ, [_U32]),
+    "gtm_lm_head_greedy": (_I, [_U32, _U32, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "gtm_lm_head_candidates": (_I, [_P, _P, C.POINTER(C.c_int32)]),
     "gtm_moe_ep_workspace_bytes": (_SZ, [C.POINTER(Dims), C.POINTER(EpConfig)]),
     "gtm_moe_ep_dispatch": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), C.POINTER(EpConfig),
                                  _P, _P, _P, _P, _SZ, _P]),
@@ -290,6 +293,31 @@ class SynthModel:
 
     def weight_bytes(self) -> int:
         return sum(t.numel() for t in self.resident) + sum(t.numel() for t in self.experts)
+
+
+class LmHead:
+    """Tied LM head with greedy argmax (gtm_lm_head_greedy) over `rows` vocabulary rows."""
+
+    def __init__(self, rows: int, device: str = "cuda"):
+        import torch
+        self.rows = rows
+        n = lib().gtm_lm_head_workspace_bytes(rows)
+        if n == 0:
+            raise GtmError(ERR_INVALID, "LM head workspace size query failed")
+        self.workspace = torch.empty(n + 256, dtype=torch.uint8, device=device)
+        self.ws_ptr = C.c_void_p((self.workspace.data_ptr() + 255) // 256 * 256)
+        self.ws_bytes = n
+
+    def __call__(self, w, s, b, x, token, logit=None, stream=None):
+        """w: uint8 [rows, hidden/2]; s, b: bf16 bits (int16/uint16) [rows, hidden/64]; x: fp32 [hidden];
+        token: int32/uint32 [1] on the device; logit: fp32 [1] or None."""
+        check(lib().gtm_lm_head_greedy(self.rows, x.numel(), ptr(w), ptr(s), ptr(b), ptr(x), ptr(token), ptr(logit),
+                                       self.ws_ptr, self.ws_bytes, _stream(stream)))
+
+    def candidates(self, stream=None) -> int:
+        n = C.c_int32()
+        check(lib().gtm_lm_head_candidates(self.ws_ptr, _stream(stream), C.byref(n)))
+        return n.value
 
 
 def synth_x(seed: int, token0: int, count: int, out, stream=None):
