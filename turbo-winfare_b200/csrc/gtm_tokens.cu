@@ -134,14 +134,17 @@ struct ViewsArgs {
     int npeers, epr;
 };
 
-__global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ ViewsArgs A) {
+// 512 threads a token when the routing logits are given; 1024 when the router GEMV runs, so that
+// one round covers 23 router rows (44 threads a row) instead of 11.
+constexpr int VIEWS_RR_MAX = 1024 / GD;
+__global__ void __launch_bounds__(1024) tok_views_router(const __grid_constant__ ViewsArgs A) {
     __shared__ __align__(16) float sx[D];
     __shared__ __align__(16) __half srh[2 * D];   // routed view (high row, low row), K-permuted
     __shared__ uint32_t sdest;                    // peer mode: ranks owning one of the token's experts
     __shared__ float srin[GD * RIN_PITCH];
     __shared__ float slog[NE];
     __shared__ double red[40];
-    __shared__ float terms[11][GD];
+    __shared__ float terms[VIEWS_RR_MAX][GD];
     const int t = blockIdx.x, tid = threadIdx.x;
     const GtmLayer& L = A.L;
     for (int i = tid; i < D; i += blockDim.x)
@@ -172,13 +175,14 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
     if (A.route_logits) {
         for (int e = tid; e < NE; e += blockDim.x) slog[e] = A.route_logits[(size_t)t * NE + e];
     } else {
-        // logits in src/cpu_reference.cpp:86-106's order: 11 rows at a time, 44 threads a row
+        // logits in src/cpu_reference.cpp:86-106's order: RR rows at a time, 44 threads a row
+        const int RR = (int)blockDim.x / GD;
         const uint8_t* W = static_cast<const uint8_t*>(L.resident_dev) + L.router.weight;
         const uint16_t* Sc = rp16(L.resident_dev, L.router.scales);
         const uint16_t* Bi = rp16(L.resident_dev, L.router.biases);
-        for (int r0 = 0; r0 < NE; r0 += 11) {
+        for (int r0 = 0; r0 < NE; r0 += RR) {
             const int rr = tid / GD, g = tid - rr * GD, row = r0 + rr;
-            if (rr < 11 && row < NE) {
+            if (rr < RR && row < NE) {
                 const uint4* wg = reinterpret_cast<const uint4*>(W + (size_t)row * D + g * kGroup);
                 const float* x = srin + g * RIN_PITCH;
                 float dot = 0.0f, sum = 0.0f;
@@ -198,7 +202,7 @@ __global__ void __launch_bounds__(512) tok_views_router(const __grid_constant__ 
                 terms[rr][g] = __fadd_rn(__fmul_rn(bf16f(Sc[row * GD + g]), dot), __fmul_rn(bf16f(Bi[row * GD + g]), sum));
             }
             __syncthreads();
-            if (tid < 11 && r0 + tid < NE) {
+            if (tid < RR && r0 + tid < NE) {
                 float acc = 0.0f;
                 for (int g2 = 0; g2 < GD; ++g2) acc = __fadd_rn(acc, terms[tid][g2]);
                 slog[r0 + tid] = acc;
@@ -1253,7 +1257,7 @@ void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
             va.push_views[s] = ps.p<__half>(w.W.routed);
         }
     }
-    tok_views_router<<<io.num_tokens, 512, 0, st>>>(va);
+    tok_views_router<<<io.num_tokens, io.route_logits_dev ? 512 : 1024, 0, st>>>(va);
 }
 
 // What one pass of the two grouped GEMMs runs over.
