@@ -339,47 +339,83 @@ __global__ void __launch_bounds__(RC) tok_route_count(const __grid_constant__ Ro
 
 // 2b. expert offsets, each chunk's first row per expert, and the tile lists (one CTA)
 __global__ void __launch_bounds__(1024) tok_route_scan(const __grid_constant__ RouteArgs A) {
+    constexpr int SP = 8;   // threads per expert in the chunk scan (1024 / NE)
     __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
-    const int tid = threadIdx.x;
-    for (int ex = tid; ex < A.ne; ex += blockDim.x) {
-        // exclusive prefix over the chunks, 16 loads in flight at a time
-        int run = 0;
-        for (int c0 = 0; c0 < A.nchunks; c0 += 16) {
-            int v[16];
+    __shared__ int wsum[NE / 32][3];
+    const int tid = threadIdx.x, lane = tid & 31;
+    // (1) per expert, exclusive prefix of its per-chunk counts: SP adjacent lanes per expert, each a
+    //     contiguous run of chunks, combined by shuffles inside the warp
+    {
+        const int e = tid / SP, p = tid % SP;
+        const int per = (A.nchunks + SP - 1) / SP, c0 = p * per, c1 = min(A.nchunks, c0 + per);
+        int local = 0;
+        if (e < A.ne)
+            for (int c = c0; c < c1; ++c) local += A.chunk[(size_t)c * NE + e];
+        int incl = local;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = c0 + j < A.nchunks ? A.chunk[(size_t)(c0 + j) * NE + ex] : 0;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                if (c0 + j < A.nchunks) A.chunk[(size_t)(c0 + j) * NE + ex] = run;
-                run += v[j];
+        for (int o = 1; o < SP; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o, SP);
+            if (p >= o) incl += v;
+        }
+        int run = incl - local;
+        const int total = __shfl_sync(0xffffffffu, incl, SP - 1, SP);
+        if (e < A.ne) {
+            for (int c = c0; c < c1; ++c) {
+                const int v = A.chunk[(size_t)c * NE + e];
+                A.chunk[(size_t)c * NE + e] = run;
+                run += v;
             }
+            if (p == 0) cnt[e] = total;
         }
-        cnt[ex] = run;
     }
     __syncthreads();
-    if (tid == 0) {
-        int o = 0, a = 0, b = 0;
-        for (int e = 0; e < A.ne; ++e) {
-            off[e] = o; t0[e] = a; t1[e] = b;
-            const int nt = ntok_tiles(cnt[e]);
-            o += cnt[e]; a += nt * FB0_R; b += nt * FB1;
+    // (2) expert offsets and tile-list bases: a block scan over the experts
+    if (tid < NE) {
+        const int c = tid < A.ne ? cnt[tid] : 0, nt = ntok_tiles(c);
+        int v0 = c, v1 = nt * FB0_R, v2 = nt * FB1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a0 = __shfl_up_sync(0xffffffffu, v0, o), a1 = __shfl_up_sync(0xffffffffu, v1, o),
+                      a2 = __shfl_up_sync(0xffffffffu, v2, o);
+            if (lane >= o) { v0 += a0; v1 += a1; v2 += a2; }
         }
-        off[A.ne] = o; t0[A.ne] = a; t1[A.ne] = b;
-        if (A.nrows) *A.nrows = o;
+        if (lane == 31) { wsum[tid >> 5][0] = v0; wsum[tid >> 5][1] = v1; wsum[tid >> 5][2] = v2; }
+        cnt[tid] = c;
+        off[tid + 1] = v0; t0[tid + 1] = v1; t1[tid + 1] = v2;   // inclusive within the warp
     }
     __syncthreads();
+    if (tid < NE) {
+        int b0 = 0, b1 = 0, b2 = 0;
+        for (int w = 0; w < (tid >> 5); ++w) { b0 += wsum[w][0]; b1 += wsum[w][1]; b2 += wsum[w][2]; }
+        off[tid + 1] += b0; t0[tid + 1] += b1; t1[tid + 1] += b2;
+    }
+    if (tid == 0) { off[0] = 0; t0[0] = 0; t1[0] = 0; }
+    __syncthreads();
+    if (tid == 0 && A.nrows) *A.nrows = off[A.ne];
     for (int j = tid; j < A.nchunks * A.ne; j += blockDim.x) {
         const int c = j / A.ne, ex = j - c * A.ne;
         A.chunk[(size_t)c * NE + ex] += off[ex];
     }
-    // tiles of one (expert, row block) are adjacent over the token ranges, for L2 reuse of the weights
-    for (int e = tid; e < A.ne; e += blockDim.x) {
-        const int c = cnt[e], nt = ntok_tiles(c);
-        for (int m = 0; m < nt; ++m) {
-            const int r0 = c * m / nt, r1 = c * (m + 1) / nt;
-            for (int f = 0; f < FB0_R; ++f) A.tiles0[t0[e] + f * nt + m] = Tile{e, off[e] + r0, r1 - r0, f};
-            for (int f = 0; f < FB1; ++f) A.tiles1[t1[e] + f * nt + m] = Tile{e, off[e] + r0, r1 - r0, f};
+    // (3) routed tiles, one thread per entry: entry t0[e] + f * nt + m of expert e covers token range
+    //     m of nt and row block f, so the tiles of one (expert, row block) stay adjacent over the token
+    //     ranges (L2 reuse of the weights); the expert of an entry is found by binary search
+    auto expert_of = [&](const int* base, int i) {
+        int lo = 0, hi = A.ne - 1;   // largest e with base[e] <= i
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (base[mid] <= i) lo = mid; else hi = mid - 1;
         }
+        return lo;
+    };
+    for (int i = tid; i < t0[A.ne]; i += blockDim.x) {
+        const int e = expert_of(t0, i), c = cnt[e], nt = ntok_tiles(c), k = i - t0[e], f = k / nt, m = k - f * nt;
+        const int r0 = c * m / nt, r1 = c * (m + 1) / nt;
+        A.tiles0[i] = Tile{e, off[e] + r0, r1 - r0, f};
+    }
+    for (int i = tid; i < t1[A.ne]; i += blockDim.x) {
+        const int e = expert_of(t1, i), c = cnt[e], nt = ntok_tiles(c), k = i - t1[e], f = k / nt, m = k - f * nt;
+        const int r0 = c * m / nt, r1 = c * (m + 1) / nt;
+        A.tiles1[i] = Tile{e, off[e] + r0, r1 - r0, f};
     }
     const int T = A.t_shared, nts = ntok_tiles(T), b0 = t0[A.ne], b1 = t1[A.ne];
     for (int i = tid; i < nts * FB0_S; i += blockDim.x) {
