@@ -201,6 +201,19 @@ def run_reference_arm(args):
         return 0
     cores = len(os.sched_getaffinity(0))
     per_step = max(2.0, 20.0 / max(1, args.steps + args.warmup))
+    if args.workload != "decode30":
+        # the token workloads: the reference runs its block one token at a time on the CPU
+        cfg = args.workload
+        cb = token_cpu_baseline(per_step * args.steps, cfg, cores)
+        line = {"impl": "reference", "metric": TOKEN_METRIC[cfg], "value": cb["value"], "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1000.0 * TOKENS_PER_STEP[cfg] / cb["value"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": TOKEN_WORKLOAD[cfg] + " (CPU sample)", "tokens_per_step": TOKENS_PER_STEP[cfg]},
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
     cb = cpu_baseline(per_step * args.steps, cores)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * LAYERS_DEFAULT / cb["value"],
@@ -353,16 +366,26 @@ def main():
 WEIGHT_BYTES_EXPERT = EXPERT_BYTES
 
 
-def token_cpu_baseline(seconds: float, cfg: str):
-    """The reference's CPU arithmetic on a bounded sample of the workload's tokens (rank 0)."""
+TOKEN_METRIC = {"batch64": "MoE-layer tokens/s (batch 64 decode, Zipf routing)",
+                "prefill4096": "MoE-layer tokens/s (prefill 4096 bf16 tokens)"}
+TOKEN_WORKLOAD = {"batch64": "config2: 64 tokens through one MoE layer, Zipf(1.1) router bias",
+                  "prefill4096": "config3: 4096 bf16 tokens through one MoE layer, uniform routing logits"}
+TOKENS_PER_STEP = {"batch64": 64, "prefill4096": 4096}
+
+
+def token_cpu_baseline(seconds: float, cfg: str, processes: int = 1):
+    """The reference's CPU arithmetic on a bounded sample of the workload's tokens (rank 0),
+    in `processes` spawned processes (one token at a time each, as the reference runs them)."""
     import multiprocessing as mp
     import oracle
     kind, impl = ("reference", "ref") if oracle.ref_available() else ("port", "oracle")
     ctx = mp.get_context("spawn")
-    with ctx.Pool(1) as pool:
-        done, wall = pool.map(token_cpu_worker, [(seconds, cfg, impl)])[0]
-    return {"value": done / wall, "unit": "tokens/s", "cores": 1, "kind": kind,
-            "sample": f"{done} tokens of the {cfg} workload through layer 0 (1 process, ~{seconds:.0f} s)"}
+    with ctx.Pool(processes) as pool:
+        res = pool.map(token_cpu_worker, [(seconds, cfg, impl)] * processes)
+    done = sum(r[0] for r in res)
+    wall = max(r[1] for r in res)
+    return {"value": done / wall, "unit": "tokens/s", "cores": processes, "kind": kind,
+            "sample": f"{done} tokens of the {cfg} workload through layer 0 ({processes} process(es), ~{seconds:.0f} s)"}
 
 
 def token_cpu_worker(a):
@@ -525,7 +548,7 @@ def bench_tokens(args):
                 "peak_source": pk, "traffic": None, "algorithmic_bytes_per_step": alg,
                 "scope": "whole layer call (views, routing, two grouped GEMMs, combine)",
                 "distinct_experts_per_step": distinct}
-        metric = "MoE-layer tokens/s (batch 64 decode, Zipf routing)"
+        metric = TOKEN_METRIC[cfg]
     else:
         flops = T_total * (LAYER_FLOPS - 2 * 128 * 2816)   # experts + shared (routing logits given)
         achieved = flops / (per_step_ms / 1000.0) / 1e12 / (world if expert_parallel else 1)
@@ -534,15 +557,14 @@ def bench_tokens(args):
                 "peak_source": pk, "traffic": None, "flops_per_step": flops,
                 "scope": "whole layer call, useful FLOPs per GPU (the fp16 high/low activation split doubles "
                          "the tensor-core work)"}
-        metric = "MoE-layer tokens/s (prefill 4096 bf16 tokens)"
+        metric = TOKEN_METRIC[cfg]
     if rank == 0:
         line = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": per_step_ms, "higher_is_better": True,
             "scaling": "strong" if expert_parallel else "weak", "vs_baseline": None,
             "dtype": "f32 (fp16 hi/lo tensor-core operands)", "data": "synthetic",
-            "config": {"workload": ("config2: 64 tokens through one MoE layer, Zipf(1.1) router bias" if cfg == "batch64"
-                                    else "config3: 4096 bf16 tokens through one MoE layer, uniform routing logits"),
+            "config": {"workload": TOKEN_WORKLOAD[cfg],
                        "tokens_per_step": tokens_per_step, "weights_gb_per_gpu": weights_gb,
                        "parallelism": (f"ep{world}" if expert_parallel else ("replicas" if world > 1 else "single")),
                        **({"ep_exchange": ("peer memory (CUDA IPC, NVLink loads/stores)" if args.ep == "peer"
