@@ -88,7 +88,7 @@ static_assert(A_COL0 + SW * 64 <= 512, "tensor memory columns");
 constexpr int FB0_R = (FE + 127) / 128, FB0_S = (FS + 127) / 128;   // gate/up tiles: 128 features (gate + up)
 constexpr int FB1 = D / MW;                                         // down tiles: 256 output rows
 constexpr uint64_t kWaitNs = 1000000000ull;
-constexpr int RIN_PITCH = 65;
+constexpr int RIN_PITCH = 68;   // router input per group of 64, padded: 16-byte rows, float4 reads
 constexpr int kMaxPeers = 8;   // ranks of a peer-memory expert-parallel group (NVLink domain of one box)
 static_assert(kMaxPeers == GTM_EP_PEER_MAX_WORLD, "peer group size");
 
@@ -141,7 +141,8 @@ __global__ void __launch_bounds__(1024) tok_views_router(const __grid_constant__
     __shared__ __align__(16) float sx[D];
     __shared__ __align__(16) __half srh[2 * D];   // routed view (high row, low row), K-permuted
     __shared__ uint32_t sdest;                    // peer mode: ranks owning one of the token's experts
-    __shared__ float srin[GD * RIN_PITCH];
+    __shared__ __align__(16) float srin[GD * RIN_PITCH];
+    __shared__ float xsum[GD];
     __shared__ float slog[NE];
     __shared__ double red[40];
     __shared__ float terms[VIEWS_RR_MAX][GD];
@@ -175,8 +176,16 @@ __global__ void __launch_bounds__(1024) tok_views_router(const __grid_constant__
     if (A.route_logits) {
         for (int e = tid; e < NE; e += blockDim.x) slog[e] = A.route_logits[(size_t)t * NE + e];
     } else {
-        // logits in src/cpu_reference.cpp:86-106's order: RR rows at a time, 44 threads a row
+        // logits in src/cpu_reference.cpp:86-106's order: RR rows at a time, 44 threads a row. A
+        // group's x-sum is the same for every row: summed once, in the same element order. Bytes
+        // become floats exactly as 0x4B0000bb - 2^23 (no conversion unit).
         const int RR = (int)blockDim.x / GD;
+        if (tid < GD) {
+            float sm = 0.0f;
+            for (int k = 0; k < kGroup; ++k) sm = __fadd_rn(sm, srin[tid * RIN_PITCH + k]);
+            xsum[tid] = sm;
+        }
+        __syncthreads();
         const uint8_t* W = static_cast<const uint8_t*>(L.resident_dev) + L.router.weight;
         const uint16_t* Sc = rp16(L.resident_dev, L.router.scales);
         const uint16_t* Bi = rp16(L.resident_dev, L.router.biases);
@@ -184,22 +193,24 @@ __global__ void __launch_bounds__(1024) tok_views_router(const __grid_constant__
             const int rr = tid / GD, g = tid - rr * GD, row = r0 + rr;
             if (rr < RR && row < NE) {
                 const uint4* wg = reinterpret_cast<const uint4*>(W + (size_t)row * D + g * kGroup);
-                const float* x = srin + g * RIN_PITCH;
-                float dot = 0.0f, sum = 0.0f;
+                const float4* x4 = reinterpret_cast<const float4*>(srin + g * RIN_PITCH);
+                float dot = 0.0f;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const uint4 q = ldg_stream_u4(wg + i);
                     const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                    for (int c = 0; c < 4; ++c)
+                    for (int c = 0; c < 4; ++c) {
+                        const float4 xv = x4[i * 4 + c];
+                        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
                         for (int b = 0; b < 4; ++b) {
-                            const float xv = x[i * 16 + c * 4 + b];
-                            dot = __fadd_rn(dot, __fmul_rn((float)((wv[c] >> (8 * b)) & 0xFFu), xv));
-                            sum = __fadd_rn(sum, xv);
+                            const float wf = __uint_as_float(__byte_perm(wv[c], 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388608.0f;
+                            dot = __fadd_rn(dot, __fmul_rn(wf, xs[b]));
                         }
+                    }
                 }
-                terms[rr][g] = __fadd_rn(__fmul_rn(bf16f(Sc[row * GD + g]), dot), __fmul_rn(bf16f(Bi[row * GD + g]), sum));
+                terms[rr][g] = __fadd_rn(__fmul_rn(bf16f(Sc[row * GD + g]), dot), __fmul_rn(bf16f(Bi[row * GD + g]), xsum[g]));
             }
             __syncthreads();
             if (tid < RR && r0 + tid < NE) {
