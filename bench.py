@@ -509,22 +509,43 @@ def bench_tokens(args):
     check()
     ms = ev0.elapsed_time(ev1)
     barrier()
-    # end to end: host -> device copy of the step's tokens, device -> host of the result
+    # end to end, as a serving host runs it: every step's tokens go host -> device and its result
+    # device -> host inside the timed region, on two copy streams with double buffers, so the copies
+    # of steps i + 1 and i - 1 overlap the compute of step i
     xh = torch.empty((n_sets, T, D), dtype=xs.dtype, pin_memory=True)
     xh.copy_(xs.cpu())
-    oh = torch.empty((T, D), dtype=torch.float32, pin_memory=True)
-    xin = torch.empty(T, D, dtype=xs.dtype, device="cuda")
-    for i in range(args.warmup):
-        xin.copy_(xh[i % n_sets], non_blocking=True)
-        step(i, xin)
-        oh.copy_(out, non_blocking=True)
+    oh = [torch.empty((T, D), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+    xin = [torch.empty(T, D, dtype=xs.dtype, device="cuda") for _ in range(2)]
+    outs = [torch.empty(T, D, device="cuda") for _ in range(2)]
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]   # the buffer's last step has computed
+    ev_out = [torch.cuda.Event() for _ in range(2)]    # the buffer's last result is on the host
+
+    def run_e2e(n):
+        for i in range(n):
+            b = i % 2
+            with torch.cuda.stream(h2d):
+                if i >= 2:
+                    h2d.wait_event(ev_used[b])
+                xin[b].copy_(xh[i % n_sets], non_blocking=True)
+                ev_in[b].record(h2d)
+            stream.wait_event(ev_in[b])
+            if i >= 2:
+                stream.wait_event(ev_out[b])
+            step(i, xin[b], outs[b])
+            ev_used[b].record(stream)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev_used[b])
+                oh[b].copy_(outs[b], non_blocking=True)
+                ev_out[b].record(d2h)
+        stream.wait_stream(d2h)
+
+    run_e2e(args.warmup)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        xin.copy_(xh[i % n_sets], non_blocking=True)
-        step(i, xin)
-        oh.copy_(out, non_blocking=True)
+    run_e2e(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
     check()
@@ -571,7 +592,8 @@ def bench_tokens(args):
                                            else "NCCL all-to-all")} if expert_parallel else {}),
                        "l2": "4 token sets cycled; weights of touched experts 0.3-0.45 GB > L2"},
             "roofline": roof,
-            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * D * xs.element_size(),
+            "e2e": {"value": e2e, "unit": "tokens/s", "copies": "two copy streams, double buffers: the copies of "
+                    "steps i+1 and i-1 overlap step i", "h2d_bytes_per_step": T * D * xs.element_size(),
                     "d2h_bytes_per_step": T * D * 4},
             "gpu_launches": args.steps * launches,
             "clocks": clk.summary(),
