@@ -173,11 +173,20 @@ __device__ __forceinline__ uint32_t cvt2(float lo_half, float hi_half) {   // (l
     return r;
 }
 
-__device__ void build_table(const float* v, int groups, uint32_t* tbl, float* xs, float* cs) {
+// nv (1 or 2) tables in one pass: items [0, 4 groups) build table 0, [4 groups, 8 groups) table 1
+// (4 groups is a multiple of 4, so no 4-lane shuffle group straddles the two)
+__device__ void build_tables(int nv, int groups, const float* v0, uint32_t* tbl0, float* xs0, float* cs0,
+                             const float* v1, uint32_t* tbl1, float* xs1, float* cs1) {
     // one thread per (group j, thread column t): both parts of its 16 elements, then the group's
-    // sums over the 4 columns (adjacent lanes)
-    for (int i = threadIdx.x; i < ((groups * 4 + 31) & ~31); i += blockDim.x) {
-        const bool on = i < groups * 4;
+    // sums over the 4 columns (adjacent lanes). Items past the last table read row 0 of table 0.
+    for (int i2 = threadIdx.x; i2 < ((nv * groups * 4 + 31) & ~31); i2 += blockDim.x) {
+        const bool on = i2 < nv * groups * 4;
+        const bool second = on && i2 >= groups * 4;
+        const int i = second ? i2 - groups * 4 : i2;
+        const float* v = second ? v1 : v0;
+        uint32_t* tbl = second ? tbl1 : tbl0;
+        float* xs = second ? xs1 : xs0;
+        float* cs = second ? cs1 : cs0;
         const int j = on ? i >> 2 : 0, t = i & 3;
         const float4* src = reinterpret_cast<const float4*>(v + j * 64 + t * 16);
         float x[16], hi[16], lo[16];
@@ -217,6 +226,10 @@ __device__ void build_table(const float* v, int groups, uint32_t* tbl, float* xs
         c += __shfl_xor_sync(0xffffffffu, c, 2);
         if (on && t == 0) { xs[j] = sx; cs[j] = c; }
     }
+}
+
+__device__ void build_table(const float* v, int groups, uint32_t* tbl, float* xs, float* cs) {
+    build_tables(1, groups, v, tbl, xs, cs, v, tbl, xs, cs);
 }
 
 // Copies n floats (n % 4 == 0) written by other CTAs in this launch into shared memory.
@@ -546,8 +559,7 @@ __device__ void tail_and_views(Smem& s, const Params& P, const GtmLayer* Lp, boo
         s.rin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(h, bf16f(s.nw[2][i])), P.inv_sqrt_d);
     }
     __syncthreads();
-    build_table(h2, GD, s.tbl_r, s.xs_r, s.cs_r);
-    build_table(sh, GD, s.tbl_d, s.xs_d, s.cs_d);
+    build_tables(2, GD, h2, s.tbl_r, s.xs_r, s.cs_r, sh, s.tbl_d, s.xs_d, s.cs_d);
     __syncthreads();
 }
 
