@@ -6,9 +6,11 @@ package; the product path never does.
 Two CPU implementations are exposed:
 
 * ``liboracle.so`` -- the restated MoE block (oracle/moe_oracle.c), which follows the
-  reference's scalar FP32 forward (src/cpu_reference.cpp:422-520) operation by operation;
-* ``_ref/libgtref.so`` -- the reference's own src/cpu_reference.cpp helpers compiled from its
-  sources (built only where the reference tree is present; it travels as a prebuilt .so).
+  reference's scalar FP32 forward (src/cpu_reference.cpp:422-520) operation by operation, and
+  the restated token sampling (oracle/sampling_oracle.c, src/sampling.cpp:1-171);
+* ``_ref/libgtref.so`` -- the reference's own src/cpu_reference.cpp helpers and src/sampling.cpp
+  compiled from its sources (built only where the reference tree is present; it travels as a
+  prebuilt .so).
 """
 from __future__ import annotations
 
@@ -47,6 +49,18 @@ class Layer(C.Structure):
                 ("w_pf2", C.c_void_p), ("w_pf", C.c_void_p), ("layer_scalar", C.c_uint16),
                 ("experts", C.c_void_p), ("expert_stride", C.c_uint64),
                 ("sub_off", C.c_uint64 * 9)]
+
+
+class Sampling(C.Structure):
+    """orc_sampling / gtref_sampling (include/gturbo/sampling.hpp:21-30 SamplingParams)."""
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int32),
+                ("repetition_penalty", C.c_float), ("has_seed", C.c_int32), ("pad_", C.c_uint32),
+                ("seed", C.c_uint64)]
+
+
+def sampling_params(temperature=0.0, top_p=1.0, top_k=0, repetition_penalty=1.0, seed=None) -> Sampling:
+    return Sampling(temperature, top_p, top_k, repetition_penalty, 0 if seed is None else 1, 0,
+                    0 if seed is None else seed)
 
 
 class BlockOut(C.Structure):
@@ -90,6 +104,20 @@ def lib():
         L.orc_synth_layer_route.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_synth_stack.argtypes = [C.POINTER(C.c_void_p), C.c_uint32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_validate_sampling.restype = C.c_int
+        L.orc_validate_sampling.argtypes = [C.POINTER(Sampling)]
+        L.orc_splitmix64.restype = C.c_uint64
+        L.orc_splitmix64.argtypes = [C.c_uint64]
+        L.orc_seed_for.restype = C.c_uint64
+        L.orc_seed_for.argtypes = [C.POINTER(Sampling), C.c_int]
+        L.orc_apply_repetition_penalty.argtypes = [C.c_void_p, C.c_uint32, C.c_void_p, C.c_size_t, C.c_float,
+                                                   C.c_float]
+        L.orc_sample_token.restype = C.c_int
+        L.orc_sample_token.argtypes = [C.c_void_p, C.c_uint32, C.POINTER(Sampling), C.c_uint64,
+                                       C.POINTER(C.c_uint32)]
+        L.orc_sample_shortlist.restype = C.c_int
+        L.orc_sample_shortlist.argtypes = [C.c_void_p, C.c_uint32, C.POINTER(Sampling), C.c_void_p,
+                                           C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]
         _lib = L
     return _lib
 
@@ -110,6 +138,17 @@ def ref():
         R.gtref_rms_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_void_p]
         R.gtref_matvec.argtypes = [C.POINTER(QT), C.c_void_p, C.c_void_p]
         R.gtref_moe_block.argtypes = [C.POINTER(Layer), C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(BlockOut)]
+        R.gtref_validate_sampling.restype = C.c_int
+        R.gtref_validate_sampling.argtypes = [C.POINTER(Sampling)]
+        R.gtref_splitmix64.restype = C.c_uint64
+        R.gtref_splitmix64.argtypes = [C.c_uint64]
+        R.gtref_seed_for.restype = C.c_uint64
+        R.gtref_seed_for.argtypes = [C.POINTER(Sampling), C.c_int]
+        R.gtref_apply_repetition_penalty.argtypes = [C.c_void_p, C.c_uint32, C.c_void_p, C.c_size_t, C.c_float,
+                                                     C.c_float]
+        R.gtref_sample_token.restype = C.c_int
+        R.gtref_sample_token.argtypes = [C.c_void_p, C.c_uint32, C.POINTER(Sampling), C.c_uint64,
+                                         C.POINTER(C.c_uint32)]
         _ref = R
     return _ref
 
@@ -216,3 +255,76 @@ def synth_stack(layers: list[SynthLayer], hidden_in: np.ndarray):
     w = np.zeros((n, K), np.float32)
     lib().orc_synth_stack(arr, n, _ptr(x), _ptr(out), _ptr(per), _ptr(idx), _ptr(w))
     return {"hidden": out, "hidden_per_layer": per, "idx": idx, "w": w}
+
+
+# ---- token sampling (src/sampling.cpp) ------------------------------------------------------
+
+def _slib(impl: str):
+    return (lib(), "orc_") if impl == "oracle" else (ref(), "gtref_")
+
+
+def validate_sampling(p: Sampling, impl: str = "oracle") -> int:
+    """0 when accepted; otherwise the oracle's rule code, or 1 from the reference."""
+    L, pre = _slib(impl)
+    return getattr(L, pre + "validate_sampling")(C.byref(p))
+
+
+def splitmix64(x: int, impl: str = "oracle") -> int:
+    L, pre = _slib(impl)
+    return getattr(L, pre + "splitmix64")(x)
+
+
+def seed_for(p: Sampling, position: int, impl: str = "oracle") -> int:
+    L, pre = _slib(impl)
+    return getattr(L, pre + "seed_for")(C.byref(p), position)
+
+
+def apply_repetition_penalty(logits: np.ndarray, history, penalty: float, softcap: float,
+                             impl: str = "oracle") -> np.ndarray:
+    """Returns a penalised copy of fp32 logits."""
+    L, pre = _slib(impl)
+    out = np.ascontiguousarray(logits, dtype=np.float32).copy()
+    h = np.ascontiguousarray(history, dtype=np.uint32)
+    getattr(L, pre + "apply_repetition_penalty")(_ptr(out), out.size, _ptr(h) if h.size else None, h.size,
+                                                 penalty, softcap)
+    return out
+
+
+def sample_token(logits: np.ndarray, p: Sampling, seed: int, impl: str = "oracle") -> tuple[int, int]:
+    """(status, token): status 0 with a token, else the failure code (token -1)."""
+    L, pre = _slib(impl)
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    tok = C.c_uint32(0)
+    rc = getattr(L, pre + "sample_token")(_ptr(x) if x.size else None, x.size, C.byref(p), seed, C.byref(tok))
+    return rc, (tok.value if rc == 0 else -1)
+
+
+def sample_shortlist(logits: np.ndarray, p: Sampling) -> tuple[int, np.ndarray, int]:
+    """(status, shortlist ids in candidate order, survivors after the nucleus and top-k cuts)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    ids = np.zeros(256, dtype=np.uint32)
+    n, cut = C.c_uint32(0), C.c_uint32(0)
+    rc = lib().orc_sample_shortlist(_ptr(x) if x.size else None, x.size, C.byref(p), _ptr(ids), C.byref(n),
+                                    C.byref(cut))
+    return rc, ids[:n.value].copy(), cut.value
+
+
+def synth_logits(seed: int, vocab: int, scale: float = 4.0, step: float = 0.0) -> np.ndarray:
+    """Deterministic fp32 logits from integer arithmetic only (splitmix64 per index, four 24-bit
+    uniforms summed: roughly normal with std ~`scale`), so a fixture can name them by (seed,
+    vocab, scale, step) instead of storing them. step > 0 rounds to multiples of step, which makes
+    many exact ties."""
+    i = np.arange(vocab, dtype=np.uint64)
+    acc = np.zeros(vocab, dtype=np.float64)
+    with np.errstate(over="ignore"):
+        for j in range(4):
+            z = i * np.uint64(4) + np.uint64(j) + np.uint64(seed) * np.uint64(0x9E3779B97F4A7C15)
+            z = z + np.uint64(0x9E3779B97F4A7C15)
+            z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+            z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+            z = z ^ (z >> np.uint64(31))
+            acc += (z >> np.uint64(40)).astype(np.float64) * 2.0 ** -24 - 0.5
+    v = acc * (scale * 3.0 ** 0.5)   # sum of 4 U(-1/2, 1/2) has variance 1/3
+    if step > 0:
+        v = np.round(v / step) * step
+    return v.astype(np.float32)

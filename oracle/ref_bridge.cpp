@@ -11,6 +11,7 @@
  * LM head, so the block is reassembled from its parts.
  */
 #include GTREF_CPU_REFERENCE_CPP
+#include "gturbo/sampling.hpp"
 
 #include <cstdint>
 #include <cstring>
@@ -156,6 +157,59 @@ __attribute__((visibility("default"))) int gtref_moe_block(const gtref_layer* L,
         if (out->top_w) out->top_w[k] = w[k];
     }
     return 0;
+}
+
+/* ---- token sampling: the reference's src/sampling.cpp, linked into this library ---- */
+
+/* Mirrors orc_sampling in oracle/sampling_oracle.h field for field. */
+struct gtref_sampling {
+    float temperature, top_p;
+    int32_t top_k;
+    float repetition_penalty;
+    int32_t has_seed;
+    uint32_t pad_;
+    uint64_t seed;
+};
+
+static gturbo::SamplingParams params_of(const gtref_sampling* p) {
+    gturbo::SamplingParams q;
+    q.temperature = p->temperature;
+    q.top_p = p->top_p;
+    q.top_k = p->top_k;
+    q.repetition_penalty = p->repetition_penalty;
+    q.has_seed = p->has_seed != 0;
+    q.seed = p->seed;
+    return q;
+}
+
+/* 0 = accepted, 1 = GTurboFormatError. */
+int gtref_validate_sampling(const gtref_sampling* p) {
+    try {
+        gturbo::validate_sampling(params_of(p));
+        return 0;
+    } catch (const gturbo::GTurboFormatError&) {
+        return 1;
+    }
+}
+
+uint64_t gtref_splitmix64(uint64_t x) { return gturbo::splitmix64(x); }
+
+uint64_t gtref_seed_for(const gtref_sampling* p, int position) { return gturbo::seed_for(params_of(p), position); }
+
+void gtref_apply_repetition_penalty(float* logits, uint32_t vocab, const uint32_t* history, size_t n_history,
+                                    float penalty, float softcap) {
+    const std::vector<uint32_t> h(history, history + n_history);
+    gturbo::apply_repetition_penalty(logits, vocab, h, penalty, softcap);
+}
+
+/* 0 = a token in *token, 1 = GTurboFormatError (empty vocabulary, degenerate distribution). */
+int gtref_sample_token(const float* logits, uint32_t vocab, const gtref_sampling* p, uint64_t seed, uint32_t* token) {
+    try {
+        *token = gturbo::sample_token(logits, vocab, params_of(p), seed);
+        return 0;
+    } catch (const gturbo::GTurboFormatError&) {
+        return 1;
+    }
 }
 
 }  // extern "C"
