@@ -4,7 +4,7 @@ Three anchors:
 * tests/golden/sampling.npz -- outputs of the reference's own compiled sampling.cpp
   (tests/golden/make_golden.py), replayed here without the reference tree;
 * the assertions of the reference's tests/test_sampling.cpp, restated: splitmix64 vectors,
-  validation verdicts, greedy ties, truncation order (Top-P over the full distribution, then
+  validation outcomes, greedy ties, truncation order (Top-P over the full distribution, then
   Top-K), determinism, and the repetition-penalty numbers;
 * live comparisons with oracle/_ref/libgtref.so when it is built.
 
