@@ -9,7 +9,8 @@ import pytest
 import gtmoe
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("gtmoe.h", "gtmoe_synth.h", "gtmoe_bundle.h")]
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("gtmoe.h", "gtmoe_synth.h", "gtmoe_bundle.h",
+                                                      "gtmoe_sampling.h")]
 
 
 def declared_symbols():

@@ -93,10 +93,18 @@ class BundleInfo(C.Structure):
                 ("layer_file_bytes", C.c_uint64)]
 
 
+class Sampling(C.Structure):
+    """GtmSampling (include/gtmoe_sampling.h), the reference's SamplingParams
+    (include/gturbo/sampling.hpp:21-30)."""
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int32),
+                ("repetition_penalty", C.c_float), ("has_seed", C.c_int32), ("reserved", C.c_uint32),
+                ("seed", C.c_uint64)]
+
+
 _lib = None
 
-# (name, restype, argtypes) for every entry point in include/gtmoe.h, include/gtmoe_synth.h and
-# include/gtmoe_bundle.h
+# (name, restype, argtypes) for every entry point in include/gtmoe.h, include/gtmoe_synth.h,
+# include/gtmoe_bundle.h and include/gtmoe_sampling.h
 _P, _U32, _U64, _I, _F, _SZ = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_size_t
 SIGNATURES = {
     "gtm_last_error": (C.c_char_p, []),
@@ -159,6 +167,12 @@ SIGNATURES = {
     "gtm_bundle_load_resident": (_I, [_P, _P, _U64]),
     "gtm_bundle_load_experts": (_I, [_P, _U32, _U32, _U32, _P, _U64]),
     "gtm_bundle_layer_desc": (_I, [_P, _U32, _P, _P, C.POINTER(Layer)]),
+    "gtm_sampling_validate": (_I, [C.POINTER(Sampling)]),
+    "gtm_sampling_splitmix64": (_U64, [_U64]),
+    "gtm_sampling_seed_for": (_U64, [C.POINTER(Sampling), _I]),
+    "gtm_sample_workspace_bytes": (_SZ, [_U32]),
+    "gtm_repetition_penalty": (_I, [_P, _U32, _P, _U32, _F, _F, _P, _SZ, _P]),
+    "gtm_sample_token": (_I, [_P, _U32, C.POINTER(Sampling), _U64, _P, _P, _P, _SZ, _P]),
     "gtm_synth_expert_layout": (_I, [_U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_resident_layout": (_I, [_U32, _U32, _U32, C.POINTER(_U64), C.POINTER(_U64)]),
     "gtm_synth_experts": (_I, [_U64, _U32, _U32, _U32, _U32, _U32, _P, _P]),
