@@ -12,10 +12,12 @@
  * ties to the lower id; one xorshift64* uniform per token from a per-position seed.
  * Logits must not contain NaN (the reference's candidate order is undefined there).
  *
- * Device results match the reference bit for bit except where a decision compares two doubles
- * that agree to ~1e-10 relative: the reference sums exp() of the whole vocabulary in order on
- * the host, the device in parallel, and CUDA's double exp() may differ from the C library's in
- * the last bit. The status word reports every decision whose margin lies inside that bound.
+ * The device entries are built to match the reference bit for bit except where a decision
+ * compares two doubles that agree to ~1e-10 relative: the reference sums exp() of the whole
+ * vocabulary in order on the host, the device in parallel, and CUDA's double exp() may differ
+ * from the C library's in the last bit. The status word reports every decision whose margin lies
+ * inside that bound. The device entries have not yet been run on a B200; the host-side rules
+ * (validate, splitmix64, seed_for) are checked against the reference's compiled code.
  */
 #ifndef GTMOE_SAMPLING_H
 #define GTMOE_SAMPLING_H
