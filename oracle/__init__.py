@@ -6,8 +6,9 @@ package; the product path never does.
 Two CPU implementations are exposed:
 
 * ``liboracle.so`` -- the restated MoE block (oracle/moe_oracle.c), which follows the
-  reference's scalar FP32 forward (src/cpu_reference.cpp:422-520) operation by operation, and
-  the restated token sampling (oracle/sampling_oracle.c, src/sampling.cpp:1-171);
+  reference's scalar FP32 forward (src/cpu_reference.cpp:422-520) operation by operation, the
+  restated token sampling (oracle/sampling_oracle.c, src/sampling.cpp:1-171), and the embedding
+  lookup and attention step (oracle/attn_oracle.c, src/cpu_reference.cpp:108-140, 322-417);
 * ``_ref/libgtref.so`` -- the reference's own src/cpu_reference.cpp helpers and src/sampling.cpp
   compiled from its sources (built only where the reference tree is present; it travels as a
   prebuilt .so).
@@ -63,6 +64,19 @@ def sampling_params(temperature=0.0, top_p=1.0, top_k=0, repetition_penalty=1.0,
                     0 if seed is None else seed)
 
 
+class AttnShape(C.Structure):
+    """orc_attn_shape / gtref_attn_shape."""
+    _fields_ = [("hidden", C.c_uint32), ("num_heads", C.c_uint32), ("head_dim", C.c_uint32),
+                ("kv_heads", C.c_uint32), ("rotated_pairs", C.c_uint32), ("theta", C.c_float),
+                ("sliding_window", C.c_int32), ("k_eq_v", C.c_int32), ("eps", C.c_float)]
+
+
+class AttnLayer(C.Structure):
+    """orc_attn_layer / gtref_attn_layer."""
+    _fields_ = [("q", QT), ("k", QT), ("v", QT), ("o", QT), ("input_norm", C.c_void_p), ("q_norm", C.c_void_p),
+                ("k_norm", C.c_void_p)]
+
+
 class BlockOut(C.Structure):
     _fields_ = [("hidden_out", C.c_void_p), ("h1", C.c_void_p), ("h2", C.c_void_p),
                 ("logits", C.c_void_p), ("top_idx", C.c_void_p), ("top_w", C.c_void_p)]
@@ -104,6 +118,15 @@ def lib():
         L.orc_synth_layer_route.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_synth_stack.argtypes = [C.POINTER(C.c_void_p), C.c_uint32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_embed.argtypes = [C.POINTER(QT), C.c_uint32, C.c_void_p]
+        L.orc_rope_neox.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_float, C.c_float]
+        L.orc_qkv_epilogue.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_float, C.c_uint32,
+                                       C.c_float, C.c_float]
+        L.orc_attention_core.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
+                                         C.c_int, C.c_int, C.c_uint32, C.c_void_p]
+        L.orc_attention_step.restype = C.c_int
+        L.orc_attention_step.argtypes = [C.POINTER(AttnShape), C.POINTER(AttnLayer), C.c_int, C.c_void_p,
+                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_validate_sampling.restype = C.c_int
         L.orc_validate_sampling.argtypes = [C.POINTER(Sampling)]
         L.orc_splitmix64.restype = C.c_uint64
@@ -138,6 +161,11 @@ def ref():
         R.gtref_rms_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_void_p]
         R.gtref_matvec.argtypes = [C.POINTER(QT), C.c_void_p, C.c_void_p]
         R.gtref_moe_block.argtypes = [C.POINTER(Layer), C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(BlockOut)]
+        R.gtref_embed.argtypes = [C.POINTER(QT), C.c_uint32, C.c_void_p]
+        R.gtref_rope_neox.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_float, C.c_float]
+        R.gtref_attention_step.restype = C.c_int
+        R.gtref_attention_step.argtypes = [C.POINTER(AttnShape), C.POINTER(AttnLayer), C.c_int, C.c_void_p,
+                                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         R.gtref_validate_sampling.restype = C.c_int
         R.gtref_validate_sampling.argtypes = [C.POINTER(Sampling)]
         R.gtref_splitmix64.restype = C.c_uint64
@@ -328,3 +356,125 @@ def synth_logits(seed: int, vocab: int, scale: float = 4.0, step: float = 0.0) -
     if step > 0:
         v = np.round(v / step) * step
     return v.astype(np.float32)
+
+
+# ---- embedding lookup and attention step (src/cpu_reference.cpp:108-140, 322-417) -------------
+
+SWA_SHAPE = dict(num_heads=16, head_dim=256, kv_heads=8, theta=10000.0, k_eq_v=0)        # sliding-window layers
+FULL_SHAPE = dict(num_heads=16, head_dim=512, kv_heads=2, theta=1000000.0, k_eq_v=1)     # layers 5, 11, 17, 23, 29
+
+
+def attn_shape(full: bool, sliding_window: int = 1024, hidden: int = HIDDEN, **over) -> AttnShape:
+    """The manifest's defaults (include/gturbo/manifest.hpp:22-49): full layers rotate
+    head_dim * 0.25 / 2 pairs and attend to every position; sliding layers rotate all pairs."""
+    d = dict(FULL_SHAPE if full else SWA_SHAPE)
+    d.update(over)
+    pairs = int(d["head_dim"] * 0.25 / 2.0) if full else d["head_dim"] // 2
+    return AttnShape(hidden, d["num_heads"], d["head_dim"], d["kv_heads"], pairs, d["theta"],
+                     0 if full else sliding_window, d["k_eq_v"], EPS)
+
+
+def _synth_u64(seed: int, n: int, stream: int) -> np.ndarray:
+    i = np.arange(n, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = i + np.uint64(seed) * np.uint64(0x9E3779B97F4A7C15) + np.uint64(stream) * np.uint64(0xD1B54A32D192ED03)
+        z = z + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def _bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+
+
+def synth_quant(seed: int, stream: int, rows: int, in_dim: int, scale: float) -> dict:
+    """A deterministic int4 MLX-affine matrix (integer arithmetic only): packed bytes, and bf16
+    scales / biases of about `scale` so a row's outputs stay O(1)."""
+    g = in_dim // 64
+    w = (_synth_u64(seed, rows * in_dim // 2, stream) & np.uint64(0xFF)).astype(np.uint8).reshape(rows, in_dim // 2)
+    r = _synth_u64(seed, 2 * rows * g, stream + 1)
+    u = (r >> np.uint64(40)).astype(np.float64) * 2.0 ** -24
+    s = _bf16_bits((scale * (0.5 + u[:rows * g])).reshape(rows, g))
+    b = _bf16_bits((-7.5 * scale * (0.5 + u[rows * g:])).reshape(rows, g))
+    return {"w": w, "s": s, "b": b, "rows": rows, "in_dim": in_dim}
+
+
+def synth_norm(seed: int, stream: int, n: int) -> np.ndarray:
+    u = (_synth_u64(seed, n, stream) >> np.uint64(40)).astype(np.float64) * 2.0 ** -24
+    return _bf16_bits(0.5 + u)
+
+
+class AttnWeights:
+    """Synthetic weights of one attention layer with the shape `s` (q/k/v/o int4, bf16 norms)."""
+
+    def __init__(self, seed: int, s: AttnShape):
+        D, hd, H, KV = s.hidden, s.head_dim, s.num_heads, s.kv_heads
+        self.shape = s
+        self.q = synth_quant(seed, 10, H * hd, D, 0.02)
+        self.k = synth_quant(seed, 20, KV * hd, D, 0.02)
+        self.v = synth_quant(seed, 30, KV * hd, D, 0.02)
+        self.o = synth_quant(seed, 40, D, H * hd, 0.01)
+        self.input_norm = synth_norm(seed, 50, D)
+        self.q_norm = synth_norm(seed, 60, hd)
+        self.k_norm = synth_norm(seed, 70, hd)
+
+    @staticmethod
+    def _qt(m: dict) -> QT:
+        return QT(_ptr(m["w"]), _ptr(m["s"]), _ptr(m["b"]), m["rows"], m["in_dim"], 4)
+
+    def view(self) -> AttnLayer:
+        return AttnLayer(self._qt(self.q), self._qt(self.k), self._qt(self.v), self._qt(self.o),
+                         _ptr(self.input_norm), _ptr(self.q_norm), _ptr(self.k_norm))
+
+
+def attention_steps(w: AttnWeights, hiddens: np.ndarray, impl: str = "oracle") -> dict:
+    """Runs positions 0..n-1 through one layer (each row of `hiddens` is that position's input);
+    returns the per-position attn outputs and q/k/v vectors, and the final caches."""
+    s = w.shape
+    n = hiddens.shape[0]
+    kn, qn = s.kv_heads * s.head_dim, s.num_heads * s.head_dim
+    kc = np.zeros((n, kn), np.float32)
+    vc = np.zeros((n, kn), np.float32)
+    out = {"attn": np.zeros((n, s.hidden), np.float32), "q": np.zeros((n, qn), np.float32),
+           "k": np.zeros((n, kn), np.float32), "v": np.zeros((n, kn), np.float32)}
+    L, fn = (lib(), "orc_attention_step") if impl == "oracle" else (ref(), "gtref_attention_step")
+    view = w.view()
+    for p in range(n):
+        x = np.ascontiguousarray(hiddens[p], dtype=np.float32)
+        getattr(L, fn)(C.byref(s), C.byref(view), p, _ptr(x), _ptr(kc), _ptr(vc), _ptr(out["attn"][p]),
+                       _ptr(out["q"][p]), _ptr(out["k"][p]), _ptr(out["v"][p]))
+    out["k_cache"], out["v_cache"] = kc, vc
+    return out
+
+
+def embed(m: dict, token: int, impl: str = "oracle") -> np.ndarray:
+    out = np.zeros(m["in_dim"], np.float32)
+    L, fn = (lib(), "orc_embed") if impl == "oracle" else (ref(), "gtref_embed")
+    qt = AttnWeights._qt(m)
+    getattr(L, fn)(C.byref(qt), token, _ptr(out))
+    return out
+
+
+def rope_neox(vec: np.ndarray, head_dim: int, pairs: int, position: float, theta: float, impl: str = "oracle"):
+    out = np.ascontiguousarray(vec, dtype=np.float32).copy()
+    L, fn = (lib(), "orc_rope_neox") if impl == "oracle" else (ref(), "gtref_rope_neox")
+    getattr(L, fn)(_ptr(out), head_dim, pairs, position, theta)
+    return out
+
+
+def qkv_epilogue(vec: np.ndarray, heads: int, head_dim: int, w, eps: float, pairs: int, position: float,
+                 theta: float) -> np.ndarray:
+    out = np.ascontiguousarray(vec, dtype=np.float32).copy()
+    lib().orc_qkv_epilogue(_ptr(out), heads, head_dim, _ptr(w), eps, pairs, position, theta)
+    return out
+
+
+def attention_core(q, k_cache, v_cache, q_heads: int, kv_heads: int, head_dim: int, n_pos: int, first: int,
+                   capacity: int) -> np.ndarray:
+    ctx = np.zeros(q_heads * head_dim, np.float32)
+    q, k_cache, v_cache = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k_cache, v_cache))
+    lib().orc_attention_core(_ptr(q), _ptr(k_cache), _ptr(v_cache), q_heads, kv_heads, head_dim, n_pos, first,
+                             capacity, _ptr(ctx))
+    return ctx

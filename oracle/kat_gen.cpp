@@ -7,18 +7,26 @@
 // Record: u32 name_len, name bytes, u32 dtype (0 f32, 1 u16, 2 u8, 3 u32), u64 count, payload.
 //
 // Cases, in the test's order (the ones not on the MoE path only advance the generator):
-//   GemvInt4 96x2816 (:241-266)       EmbedLookup 64x2816 (:268-292, draws only)
+//   GemvInt4 96x2816 (:241-266)       EmbedLookup 64x2816, row 37 (:268-292)
 //   RMSNormK (:294-336)               GemvInt8 128x2816 (:338-361)
 //   GeGLU n=2112 (:363-387)           Softcap n=4096 (:389-411, draws only)
 //   MulBF16 n=2816 (:413-441)         ScaleAccum 8x2816 (:443-482)
 //   RouterTopK 128, K=8, tie 11/70 (:484-542)
 //   PostAttn D=2816 (:544-601)        LayerTail D=2816 (:603-647)
+//   QKVEpilogue 2x512, 64 pairs (:649-692)
+//   Attention GQA 16/8, window 128, n_pos 300 (:694-741)
+//   LMHeadGreedy 4096x2816 (:743-802, draws only)
+//   Attention across the ring wrap, capacity 128 (:804-858)
+// The attention cases' K/V caches (2.4 MB and 1 MB) are not stored: the record holds the
+// generator state at the start of the case (624 words and the position, the engine's own
+// textual state), from which the inputs are drawn again.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <random>
+#include <sstream>
 #include <string>
 #include <vector>
 
@@ -139,8 +147,22 @@ int main(int argc, char** argv) {
         std::vector<float> x(2816); for (auto& v : x) v = xf(rng);
         m.save("gemv_int4"); put_f("gemv_int4.x", x); put_f("gemv_int4.want", m.expect(x));
     }
-    {   // EmbedLookup: draws only
+    {   // EmbedLookup: row 37 dequantised, times sqrt(2816) as a float
         Quant m; m.draw(64, 2816, 4, rng);
+        const uint32_t token = 37;
+        const float scale = std::sqrt(static_cast<float>(2816));
+        std::vector<float> want(2816);
+        const uint32_t groups = 2816 / kGroup;
+        for (uint32_t g = 0; g < groups; ++g) {
+            const float sc = f_of_bf16(m.scales[size_t(token) * groups + g]);
+            const float b = f_of_bf16(m.biases[size_t(token) * groups + g]);
+            for (uint32_t j = 0; j < kGroup; ++j) {
+                const uint32_t c = g * kGroup + j;
+                want[c] = static_cast<float>(m.q_at(token, c)) * sc + b;
+            }
+        }
+        for (auto& v : want) v *= scale;
+        m.save("embed"); put_u("embed.token", {token}); put_f("embed.want", want);
     }
     {   // RMSNormK, unweighted and weighted
         const uint32_t n = 2816; const float eps = 1e-6f;
@@ -240,6 +262,80 @@ int main(int argc, char** argv) {
         put_h("layertail.w_pf2", wpf2); put_h("layertail.w_pf", wpf); put_f("layertail.scalar", {ls});
         put_f("layertail.want", want);
     }
+    {   // QKVEpilogue: per-head weighted norm, then 64 of 256 pairs rotated at position 7
+        const uint32_t head_dim = 512, heads = 2, rotated = 64, position = 7;
+        const float eps = 1e-6f, theta = 1000000.0f;
+        std::vector<float> vec(heads * head_dim); for (auto& v : vec) v = xf(rng);
+        std::vector<uint16_t> w(head_dim); for (auto& v : w) v = bf16_of_f(0.5f + xf(rng) * 0.2f);
+        std::vector<float> want(vec.size());
+        for (uint32_t h = 0; h < heads; ++h) {
+            const float* src = vec.data() + h * head_dim;
+            float* dst = want.data() + h * head_dim;
+            double a = 0.0;
+            for (uint32_t i = 0; i < head_dim; ++i) a += static_cast<double>(src[i]) * src[i];
+            const float inv = 1.0f / std::sqrt(static_cast<float>(a / head_dim) + eps);
+            for (uint32_t i = 0; i < head_dim; ++i) dst[i] = src[i] * inv * f_of_bf16(w[i]);
+            const uint32_t half = head_dim / 2;
+            for (uint32_t i = 0; i < rotated; ++i) {
+                const float freq = std::pow(theta, -static_cast<float>(2 * i) / static_cast<float>(head_dim));
+                const float ang = static_cast<float>(position) * freq;
+                const float c = std::cos(ang), sn = std::sin(ang);
+                const float x0 = dst[i], x1 = dst[i + half];
+                dst[i] = x0 * c - x1 * sn;
+                dst[i + half] = x0 * sn + x1 * c;
+            }
+        }
+        put_f("qkv.vec", vec); put_h("qkv.w", w); put_f("qkv.want", want);
+        put_u("qkv.shape", {head_dim, heads, rotated, position});
+    }
+    // Attention: q, then the K and V caches, drawn in that order; the want of the test's formula
+    auto attention = [&](const std::string& name, uint32_t n_pos, uint32_t window, uint32_t capacity) {
+        const uint32_t q_heads = 16, kv_heads = 8, head_dim = 256;
+        const uint32_t first = n_pos - window;
+        {
+            std::ostringstream os;
+            os << rng;
+            std::istringstream is(os.str());
+            std::vector<uint32_t> state;
+            unsigned long long w;
+            while (is >> w) state.push_back(static_cast<uint32_t>(w));
+            put_u(name + ".rng_state", state);
+        }
+        std::vector<float> q(q_heads * head_dim);
+        std::vector<float> kc(static_cast<size_t>(capacity) * kv_heads * head_dim), vc(kc.size());
+        for (auto& v : q) v = xf(rng) * 0.1f;
+        for (auto& v : kc) v = xf(rng) * 0.1f;
+        for (auto& v : vc) v = xf(rng);
+        std::vector<float> want(q.size(), 0.0f);
+        const uint32_t gqa = q_heads / kv_heads;
+        for (uint32_t h = 0; h < q_heads; ++h) {
+            const uint32_t kvh = h / gqa;
+            std::vector<float> sc(n_pos, 0.0f);
+            float best = -1e30f;
+            for (uint32_t t = first; t < n_pos; ++t) {
+                const float* kt = kc.data() + ((t % capacity) * size_t(kv_heads) + kvh) * head_dim;
+                float dot = 0.0f;
+                for (uint32_t d = 0; d < head_dim; ++d) dot += q[h * head_dim + d] * kt[d];
+                sc[t] = dot;
+                best = std::max(best, dot);
+            }
+            float sum = 0.0f;
+            for (uint32_t t = first; t < n_pos; ++t) { sc[t] = std::exp(sc[t] - best); sum += sc[t]; }
+            for (uint32_t t = first; t < n_pos; ++t) {
+                const float wt = sc[t] / sum;
+                const float* vt = vc.data() + ((t % capacity) * size_t(kv_heads) + kvh) * head_dim;
+                for (uint32_t d = 0; d < head_dim; ++d) want[h * head_dim + d] += wt * vt[d];
+            }
+        }
+        put_f(name + ".q", q); put_f(name + ".want", want);
+        put_u(name + ".shape", {q_heads, kv_heads, head_dim, n_pos, window, capacity});
+    };
+    attention("attn", 300, 128, 300);   // capacity == n_pos: a linear cache
+    {   // LMHeadGreedy: draws only
+        Quant m; m.draw(4096, 2816, 4, rng);
+        std::vector<float> x(2816); for (auto& v : x) v = xf(rng);
+    }
+    attention("attn_ring", 300, 128, 128);
     std::fclose(g_out);
     return 0;
 }

@@ -159,6 +159,103 @@ __attribute__((visibility("default"))) int gtref_moe_block(const gtref_layer* L,
     return 0;
 }
 
+/* ---- embedding lookup and one attention step, from the reference's own helpers ---- */
+
+/* Mirrors orc_attn_shape / orc_attn_layer in oracle/attn_oracle.h field for field. */
+struct gtref_attn_shape {
+    uint32_t hidden, num_heads, head_dim, kv_heads, rotated_pairs;
+    float theta;
+    int32_t sliding_window, k_eq_v;
+    float eps;
+};
+struct gtref_attn_layer {
+    gtref_qt q, k, v, o;
+    const uint16_t *input_norm, *q_norm, *k_norm;
+};
+
+static QuantTensor qt_of(const gtref_qt& t) { return view(t.data, t.scales, t.biases, t.rows, t.in_dim, t.bits); }
+
+/* cpu_reference.cpp:322-330: dequant_row, then * sqrt(hidden). */
+void gtref_embed(const gtref_qt* embed, uint32_t token, float* out) {
+    const QuantTensor t = qt_of(*embed);
+    gturbo::dequant_row(t, token, out);
+    const float embed_scale = std::sqrt(static_cast<float>(t.in_dim));
+    for (uint32_t i = 0; i < t.in_dim; ++i) out[i] *= embed_scale;
+}
+
+void gtref_rope_neox(float* vec, uint32_t head_dim, uint32_t rotated_pairs, float position, float theta) {
+    gturbo::rope_neox(vec, head_dim, rotated_pairs, position, theta);
+}
+
+/* The attention section of CpuReference::forward (cpu_reference.cpp:345-417) for one layer,
+ * with the layer's KV rows in caller memory instead of LayerKV vectors. */
+int gtref_attention_step(const gtref_attn_shape* s, const gtref_attn_layer* L, int pos, const float* hidden,
+                         float* k_cache, float* v_cache, float* attn_out, float* q_out, float* k_out, float* v_out) {
+    const uint32_t D = s->hidden, head_dim = s->head_dim, q_heads = s->num_heads, kv_heads = s->kv_heads;
+    const float eps = s->eps;
+    std::vector<float> normed(D);
+    gturbo::rms_norm(hidden, L->input_norm, D, eps, normed.data());
+    std::vector<float> q(q_heads * head_dim), k(kv_heads * head_dim), v(kv_heads * head_dim);
+    gturbo::matvec(qt_of(L->q), normed.data(), q.data());
+    gturbo::matvec(qt_of(L->k), normed.data(), k.data());
+    if (s->k_eq_v) {
+        v = k;
+    } else {
+        gturbo::matvec(qt_of(L->v), normed.data(), v.data());
+    }
+    std::vector<float> scratch(head_dim);
+    for (uint32_t h = 0; h < q_heads; ++h) {
+        gturbo::rms_norm(q.data() + h * head_dim, L->q_norm, head_dim, eps, scratch.data());
+        std::copy(scratch.begin(), scratch.end(), q.begin() + h * head_dim);
+        gturbo::rope_neox(q.data() + h * head_dim, head_dim, s->rotated_pairs, static_cast<float>(pos), s->theta);
+    }
+    for (uint32_t h = 0; h < kv_heads; ++h) {
+        gturbo::rms_norm(k.data() + h * head_dim, L->k_norm, head_dim, eps, scratch.data());
+        std::copy(scratch.begin(), scratch.end(), k.begin() + h * head_dim);
+        gturbo::rope_neox(k.data() + h * head_dim, head_dim, s->rotated_pairs, static_cast<float>(pos), s->theta);
+        gturbo::rms_norm(v.data() + h * head_dim, nullptr, head_dim, eps, scratch.data());
+        std::copy(scratch.begin(), scratch.end(), v.begin() + h * head_dim);
+    }
+    const size_t row = static_cast<size_t>(kv_heads) * head_dim;
+    std::copy(k.begin(), k.end(), k_cache + static_cast<size_t>(pos) * row);
+    std::copy(v.begin(), v.end(), v_cache + static_cast<size_t>(pos) * row);
+
+    const uint32_t gqa = q_heads / kv_heads;
+    const int n_pos = pos + 1;
+    const int first = s->sliding_window <= 0 ? 0 : std::max(0, n_pos - s->sliding_window);
+    std::vector<float> ctx(q_heads * head_dim, 0.0f);
+    std::vector<float> scores(static_cast<size_t>(n_pos));
+    for (uint32_t h = 0; h < q_heads; ++h) {
+        const uint32_t kvh = h / gqa;
+        const float* qh = q.data() + h * head_dim;
+        float best = -1e30f;
+        for (int t = first; t < n_pos; ++t) {
+            const float* kt = k_cache + static_cast<size_t>(t) * row + kvh * head_dim;
+            float dot = 0.0f;
+            for (uint32_t d = 0; d < head_dim; ++d) dot += qh[d] * kt[d];
+            scores[static_cast<size_t>(t)] = dot;
+            best = std::max(best, dot);
+        }
+        float sum = 0.0f;
+        for (int t = first; t < n_pos; ++t) {
+            float e = std::exp(scores[static_cast<size_t>(t)] - best);
+            scores[static_cast<size_t>(t)] = e;
+            sum += e;
+        }
+        float* out = ctx.data() + h * head_dim;
+        for (int t = first; t < n_pos; ++t) {
+            const float wgt = scores[static_cast<size_t>(t)] / sum;
+            const float* vt = v_cache + static_cast<size_t>(t) * row + kvh * head_dim;
+            for (uint32_t d = 0; d < head_dim; ++d) out[d] += wgt * vt[d];
+        }
+    }
+    gturbo::matvec(qt_of(L->o), ctx.data(), attn_out);
+    if (q_out) std::copy(q.begin(), q.end(), q_out);
+    if (k_out) std::copy(k.begin(), k.end(), k_out);
+    if (v_out) std::copy(v.begin(), v.end(), v_out);
+    return 0;
+}
+
 /* ---- token sampling: the reference's src/sampling.cpp, linked into this library ---- */
 
 /* Mirrors orc_sampling in oracle/sampling_oracle.h field for field. */
