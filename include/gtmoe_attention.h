@@ -1,0 +1,52 @@
+/*
+ * gtmoe_attention.h -- the decoder remainder around the MoE block for batch-1 decode (C ABI):
+ * embedding lookup, the per-head q/k/v epilogue and attention over the FP32 ring KV cache.
+ *
+ * Replaces, for one token of ForwardRunner::produce_token (src/runner.cpp:487-533), the
+ * EmbedLookup, QKVEpilogue and Attention dispatches (shaders/EmbedLookup.hlsl,
+ * shaders/QKVEpilogue.hlsl, shaders/Attention.hlsl); the q/k/v/o projections stay on
+ * gtm_gemv_q4 (GemvInt4). Arithmetic contract: src/cpu_reference.cpp:108-140, 322-417.
+ * KV rows live where KVCacheManager puts them (src/kv_cache.cpp:36-50): position p of a layer
+ * in row p % capacity, each row kv_heads * head_dim floats.
+ *
+ * These device entries have not yet been run on a B200.
+ */
+#ifndef GTMOE_ATTENTION_H
+#define GTMOE_ATTENTION_H
+
+#include "gtmoe.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* EmbedLookup (cpu_reference.cpp:322-330): out[c] = (q[token][c] * s + b) * scale, int4 MLX
+ * affine rows of in_dim elements (group 64). Bit-identical to the CPU reference with
+ * scale = sqrtf(in_dim). */
+GTM_API int gtm_embed_lookup(uint32_t rows, uint32_t in_dim, const void* w_dev, const uint16_t* s_dev,
+                             const uint16_t* b_dev, uint32_t token, float scale, float* out_dev, void* stream);
+
+/* QKVEpilogue (cpu_reference.cpp:360-376): for each of `heads` vectors of head_dim floats, an
+ * RMS norm with bf16 weight w_dev (NULL = no scale), then NeoX RoPE of the first rotated_pairs
+ * pairs at `position` with base theta (rotated_pairs = 0: no rotation). in_dev and out_dev may
+ * be the same buffer; out_dev may point into a KV cache row. head_dim in {128, 256, 512}. */
+GTM_API int gtm_qkv_epilogue(uint32_t heads, uint32_t head_dim, const float* in_dev, const uint16_t* w_dev, float eps,
+                             uint32_t rotated_pairs, uint32_t position, float theta, float* out_dev, void* stream);
+
+/* Workspace for gtm_attention_decode with at most `max_window` attended positions. */
+GTM_API size_t gtm_attention_workspace_bytes(uint32_t q_heads, uint32_t head_dim, uint32_t max_window);
+
+/* Attention (cpu_reference.cpp:382-414): for each query head h (kv head h / (q_heads /
+ * kv_heads)), scores q.k with scale 1.0 over positions [first, n_pos), softmax, and the
+ * weighted sum of V into ctx_dev [q_heads * head_dim]. Position t is cache row t % capacity.
+ * q_heads a multiple of kv_heads with q_heads / kv_heads <= 8; head_dim in {128, 256, 512};
+ * first < n_pos; n_pos - first <= capacity. */
+GTM_API int gtm_attention_decode(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, uint32_t n_pos,
+                                 uint32_t first, uint32_t capacity, const float* q_dev, const float* k_cache_dev,
+                                 const float* v_cache_dev, float* ctx_dev, void* workspace_dev, size_t workspace_bytes,
+                                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

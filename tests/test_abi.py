@@ -10,7 +10,7 @@ import gtmoe
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADERS = [os.path.join(ROOT, "include", h) for h in ("gtmoe.h", "gtmoe_synth.h", "gtmoe_bundle.h",
-                                                      "gtmoe_sampling.h")]
+                                                      "gtmoe_sampling.h", "gtmoe_attention.h")]
 
 
 def declared_symbols():

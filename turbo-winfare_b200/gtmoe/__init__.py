@@ -104,7 +104,7 @@ class Sampling(C.Structure):
 _lib = None
 
 # (name, restype, argtypes) for every entry point in include/gtmoe.h, include/gtmoe_synth.h,
-# include/gtmoe_bundle.h and include/gtmoe_sampling.h
+# include/gtmoe_bundle.h, include/gtmoe_sampling.h and include/gtmoe_attention.h
 _P, _U32, _U64, _I, _F, _SZ = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_size_t
 SIGNATURES = {
     "gtm_last_error": (C.c_char_p, []),
@@ -167,6 +167,10 @@ SIGNATURES = {
     "gtm_bundle_load_resident": (_I, [_P, _P, _U64]),
     "gtm_bundle_load_experts": (_I, [_P, _U32, _U32, _U32, _P, _U64]),
     "gtm_bundle_layer_desc": (_I, [_P, _U32, _P, _P, C.POINTER(Layer)]),
+    "gtm_embed_lookup": (_I, [_U32, _U32, _P, _P, _P, _U32, _F, _P, _P]),
+    "gtm_qkv_epilogue": (_I, [_U32, _U32, _P, _P, _F, _U32, _U32, _F, _P, _P]),
+    "gtm_attention_workspace_bytes": (_SZ, [_U32, _U32, _U32]),
+    "gtm_attention_decode": (_I, [_U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P, _SZ, _P]),
     "gtm_sampling_validate": (_I, [C.POINTER(Sampling)]),
     "gtm_sampling_splitmix64": (_U64, [_U64]),
     "gtm_sampling_seed_for": (_U64, [C.POINTER(Sampling), _I]),
