@@ -55,6 +55,11 @@ GTM_API uint64_t gtm_sampling_splitmix64(uint64_t x);
 /* seed_for (sampling.cpp:63-72): the generator state for `position`; never 0. Host only. */
 GTM_API uint64_t gtm_sampling_seed_for(const GtmSampling* p, int position);
 
+/* Softcap (shaders/Softcap.hlsl; cpu_reference.cpp:534-538): out = cap * tanh(in / cap) for n
+ * fp32 values, in place when in_dev == out_dev. Device tanhf rounds differently from the C
+ * library's in the last bits. */
+GTM_API int gtm_softcap(uint32_t n, const float* in_dev, float cap, float* out_dev, void* stream);
+
 /* Device workspace for a vocabulary of `vocab` ids (256-byte aligned; no initialisation). */
 GTM_API size_t gtm_sample_workspace_bytes(uint32_t vocab);
 

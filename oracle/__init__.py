@@ -127,6 +127,7 @@ def lib():
         L.orc_attention_step.restype = C.c_int
         L.orc_attention_step.argtypes = [C.POINTER(AttnShape), C.POINTER(AttnLayer), C.c_int, C.c_void_p,
                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_softcap.argtypes = [C.c_void_p, C.c_size_t, C.c_float]
         L.orc_validate_sampling.restype = C.c_int
         L.orc_validate_sampling.argtypes = [C.POINTER(Sampling)]
         L.orc_splitmix64.restype = C.c_uint64
@@ -478,3 +479,9 @@ def attention_core(q, k_cache, v_cache, q_heads: int, kv_heads: int, head_dim: i
     lib().orc_attention_core(_ptr(q), _ptr(k_cache), _ptr(v_cache), q_heads, kv_heads, head_dim, n_pos, first,
                              capacity, _ptr(ctx))
     return ctx
+
+
+def softcap(z: np.ndarray, cap: float) -> np.ndarray:
+    out = np.ascontiguousarray(z, dtype=np.float32).copy()
+    lib().orc_softcap(_ptr(out), out.size, cap)
+    return out

@@ -9,7 +9,7 @@
 // Cases, in the test's order (the ones not on the MoE path only advance the generator):
 //   GemvInt4 96x2816 (:241-266)       EmbedLookup 64x2816, row 37 (:268-292)
 //   RMSNormK (:294-336)               GemvInt8 128x2816 (:338-361)
-//   GeGLU n=2112 (:363-387)           Softcap n=4096 (:389-411, draws only)
+//   GeGLU n=2112 (:363-387)           Softcap n=4096 (:389-411)
 //   MulBF16 n=2816 (:413-441)         ScaleAccum 8x2816 (:443-482)
 //   RouterTopK 128, K=8, tie 11/70 (:484-542)
 //   PostAttn D=2816 (:544-601)        LayerTail D=2816 (:603-647)
@@ -189,9 +189,13 @@ int main(int argc, char** argv) {
         }
         put_f("geglu.g", g); put_f("geglu.u", u); put_f("geglu.want", want);
     }
-    {   // Softcap: draws only
+    {   // Softcap: 30 * tanh(z / 30) in float
+        const float cap = 30.0f;
         std::uniform_real_distribution<float> big(-200.0f, 200.0f);
-        for (int i = 0; i < 4096; ++i) (void)big(rng);
+        std::vector<float> z(4096), want(4096);
+        for (auto& v : z) v = big(rng);
+        for (size_t i = 0; i < z.size(); ++i) want[i] = cap * std::tanh(z[i] / cap);
+        put_f("softcap.z", z); put_f("softcap.want", want);
     }
     {   // MulBF16
         const uint32_t n = 2816; const float scale = 0.0188478f;

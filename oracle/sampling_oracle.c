@@ -20,6 +20,12 @@ int orc_validate_sampling(const orc_sampling* p) {
     return ORC_SAMPLING_OK;
 }
 
+/* cpu_reference.cpp:534-538, in float: z / cap, tanhf, cap * t. */
+void orc_softcap(float* z, size_t n, float cap) {
+    if (!(cap > 0.0f)) return;
+    for (size_t i = 0; i < n; ++i) z[i] = cap * tanhf(z[i] / cap);
+}
+
 /* sampling.cpp:56-61: Vigna's splitmix64 finaliser. */
 uint64_t orc_splitmix64(uint64_t x) {
     uint64_t z = x + kGolden;

@@ -45,6 +45,8 @@ enum { ORC_SAMPLE_OK = 0, ORC_SAMPLE_EMPTY_VOCAB = 1, ORC_SAMPLE_DEGENERATE = 2 
 #define ORC_SAMPLING_MAX_TOP_K 256   /* sampling.cpp:15 */
 
 int orc_validate_sampling(const orc_sampling* p);
+/* Final logit softcapping (cpu_reference.cpp:534-538): z = cap * tanhf(z / cap) when cap > 0. */
+void orc_softcap(float* z, size_t n, float cap);
 uint64_t orc_splitmix64(uint64_t x);
 uint64_t orc_seed_for(const orc_sampling* p, int position);
 void orc_apply_repetition_penalty(float* logits, uint32_t vocab, const uint32_t* history, size_t n_history,

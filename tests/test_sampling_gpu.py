@@ -81,6 +81,20 @@ def test_penalty_matches_reference(g):
         assert np.array_equal(got.view(np.uint32), g[f"penalty{c}.out"].view(np.uint32)), c
 
 
+@pytest.mark.parametrize("in_place", [False, True])
+def test_softcap_known_answer(in_place):
+    """Within the rule the reference holds its own GPU Softcap to (allclose 1e-5 + 1e-4 |want|):
+    device tanhf rounds differently from the C library's."""
+    import torch
+    from gtmoe import sampling
+    k = np.load(os.path.join(ROOT, "tests", "golden", "kat.npz"))
+    z = torch.from_numpy(k["softcap.z"].copy()).cuda()
+    out = z if in_place else torch.empty_like(z)
+    sampling.softcap(z, 30.0, out=out)
+    got, want = out.cpu().numpy(), k["softcap.want"]
+    assert np.all(np.abs(got - want) <= 1e-5 + 1e-4 * np.abs(want))
+
+
 @pytest.mark.parametrize("vocab", [1, 2, 255, 256, 257, 5000, 262144, 1 << 20])
 def test_random_against_oracle(vocab):
     import torch

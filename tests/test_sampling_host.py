@@ -92,6 +92,9 @@ def test_device_entries_reject_bad_arguments_before_the_gpu():
     assert L.gtm_repetition_penalty(fake, 100, None, 3, 1.3, 30.0, fake, 1 << 20, None) == gtmoe.ERR_INVALID
     assert L.gtm_repetition_penalty(fake, 100, fake, 3, 0.0, 30.0, fake, 1 << 20, None) == gtmoe.ERR_INVALID
     assert L.gtm_repetition_penalty(fake, 100, fake, 3, 1.3, 30.0, fake, 16, None) == gtmoe.ERR_WORKSPACE
+    assert L.gtm_softcap(16, fake, 0.0, fake, None) == gtmoe.ERR_INVALID
+    assert L.gtm_softcap(16, None, 30.0, fake, None) == gtmoe.ERR_INVALID
+    assert L.gtm_softcap(0, None, 30.0, None, None) == gtmoe.OK
     # penalty 1 or an empty history is a no-op (sampling.cpp:77): nothing is launched
     assert L.gtm_repetition_penalty(fake, 100, fake, 3, 1.0, 30.0, None, 0, None) == gtmoe.OK
     assert L.gtm_repetition_penalty(fake, 100, None, 0, 2.0, 30.0, None, 0, None) == gtmoe.OK

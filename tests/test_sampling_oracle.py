@@ -170,6 +170,14 @@ def test_shortlist_matches_full_sort():
             assert cut == n
 
 
+def test_softcap_known_answer():
+    # the reference's Softcap case (tests/test_gpu_kernels.cpp:389-411), regenerated into kat.npz
+    k = np.load(os.path.join(ROOT, "tests", "golden", "kat.npz"))
+    got = oracle.softcap(k["softcap.z"], 30.0)
+    assert np.array_equal(got.view(np.uint32), k["softcap.want"].view(np.uint32))
+    assert np.all(np.abs(got) <= 30.0)
+
+
 def test_failures():
     p = params(1.0, 1.0, 0)
     assert oracle.sample_token(np.zeros(0, np.float32), p, 1)[0] == 1            # empty vocabulary

@@ -315,6 +315,12 @@ __global__ void smp_penalty_apply(float* __restrict__ logits, const uint32_t* __
     logits[id] = v;
 }
 
+// in and out may alias: each element is read once, then written by the same thread
+__global__ void smp_softcap(const float* in, uint32_t n, float cap, float* out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __fmul_rn(cap, tanhf(__fdiv_rn(in[i], cap)));
+}
+
 size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 int grid_slices(uint32_t vocab) {
@@ -391,6 +397,22 @@ GTM_API uint64_t gtm_sampling_seed_for(const GtmSampling* p, int position) {
     const uint64_t base = (p && p->has_seed) ? p->seed + pos : (kGolden ^ (pos * 0xD1B54A32D192ED03ULL));
     const uint64_t s = splitmix(base);
     return s != 0 ? s : kGolden;
+}
+
+GTM_API int gtm_softcap(uint32_t n, const float* in, float cap, float* out, void* stream) {
+    const char* fn = "gtm_softcap";
+    if (n == 0) {
+        clear_error();
+        return GTM_OK;
+    }
+    if (!in || !out) return set_error(GTM_ERR_INVALID, "%s: null pointer", fn);
+    if (!(cap > 0.0f) || !std::isfinite(cap)) return set_error(GTM_ERR_INVALID, "%s: cap must be finite and > 0", fn);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    smp_softcap<<<(n + 255) / 256, 256, 0, st>>>(in, n, cap, out);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error(fn, e);
+    clear_error();
+    return GTM_OK;
 }
 
 GTM_API size_t gtm_sample_workspace_bytes(uint32_t vocab) {

@@ -174,6 +174,7 @@ SIGNATURES = {
     "gtm_sampling_validate": (_I, [C.POINTER(Sampling)]),
     "gtm_sampling_splitmix64": (_U64, [_U64]),
     "gtm_sampling_seed_for": (_U64, [C.POINTER(Sampling), _I]),
+    "gtm_softcap": (_I, [_U32, _P, _F, _P, _P]),
     "gtm_sample_workspace_bytes": (_SZ, [_U32]),
     "gtm_repetition_penalty": (_I, [_P, _U32, _P, _U32, _F, _F, _P, _SZ, _P]),
     "gtm_sample_token": (_I, [_P, _U32, C.POINTER(Sampling), _U64, _P, _P, _P, _SZ, _P]),

@@ -48,6 +48,11 @@ def seed_for(p: SamplingParams, position: int) -> int:
     return lib().gtm_sampling_seed_for(C.byref(c), position)
 
 
+def softcap(logits, cap: float, out=None, stream=None) -> None:
+    """cap * tanh(z / cap) on fp32 device logits, in place unless out is given."""
+    check(lib().gtm_softcap(logits.numel(), ptr(logits), cap, ptr(logits if out is None else out), _stream(stream)))
+
+
 class Sampler:
     """Device sampling over a vocabulary of `vocab` ids, with its own workspace."""
 
