@@ -167,6 +167,9 @@ def ref():
         R.gtref_attention_step.restype = C.c_int
         R.gtref_attention_step.argtypes = [C.POINTER(AttnShape), C.POINTER(AttnLayer), C.c_int, C.c_void_p,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        R.gtref_generate.restype = C.c_int
+        R.gtref_generate.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_int, C.c_char_p, C.c_void_p,
+                                     C.POINTER(C.c_uint32), C.c_char_p, C.c_size_t]
         R.gtref_validate_sampling.restype = C.c_int
         R.gtref_validate_sampling.argtypes = [C.POINTER(Sampling)]
         R.gtref_splitmix64.restype = C.c_uint64
@@ -485,3 +488,95 @@ def softcap(z: np.ndarray, cap: float) -> np.ndarray:
     out = np.ascontiguousarray(z, dtype=np.float32).copy()
     lib().orc_softcap(_ptr(out), out.size, cap)
     return out
+
+
+def ref_generate(model_dir: str, prompt, max_tokens: int, dump_dir: str | None = None) -> list[int]:
+    """The reference's CpuReference::generate, greedy, on a bundle directory; with dump_dir, its
+    per-stage tensors of the first prompt token are written there."""
+    p = np.ascontiguousarray(prompt, dtype=np.uint32)
+    out = np.zeros(max_tokens + 1, np.uint32)
+    n = C.c_uint32(0)
+    err = C.create_string_buffer(512)
+    dd = None if dump_dir is None else dump_dir.encode()
+    if ref().gtref_generate(model_dir.encode(), _ptr(p), p.size, max_tokens, dd, _ptr(out), C.byref(n), err,
+                            512) != 0:
+        raise RuntimeError("reference generate failed: " + err.value.decode())
+    return [int(t) for t in out[:n.value]]
+
+
+# ---- the whole decoder: embedding, per layer attention + MoE block, final norm, LM head ------
+
+class SynthDecoder:
+    """A synthetic Gemma-4-shaped decoder on the host, composed from the oracle's pieces in the
+    order of CpuReference::forward (src/cpu_reference.cpp:313-540): embedding x sqrt(D); per
+    layer the attention step, the post-attention norm added to the residual, and the MoE block;
+    then the final norm, the tied LM head and the softcap. Greedy decoding follows
+    CpuReference::generate (:544-595). Layer l is full-attention when full_mask[l] is 1."""
+
+    SOFTCAP = 30.0
+
+    def __init__(self, num_layers: int = 2, vocab: int = 1024, sliding_window: int = 3, seed: int = 0,
+                 full_mask=None, embed_scale: float = 0.002):
+        self.num_layers, self.vocab, self.window, self.seed = num_layers, vocab, sliding_window, seed
+        self.full_mask = list(full_mask) if full_mask is not None else [l % 2 for l in range(num_layers)]
+        self.moe = [SynthLayer(seed, l) for l in range(num_layers)]
+        self.attn = [AttnWeights(1000 + 37 * seed + l, attn_shape(bool(self.full_mask[l]), sliding_window))
+                     for l in range(num_layers)]
+        self.post_attn = [synth_norm(seed, 2000 + l, HIDDEN) for l in range(num_layers)]
+        # small embedding values, so that the layers and not the token's own row decide the argmax
+        self.embed_w = synth_quant(seed, 3000, vocab, HIDDEN, embed_scale)
+        self.final_norm = synth_norm(seed, 3001, HIDDEN)
+        self.used = [set() for _ in range(num_layers)]
+        self.reset(64)
+
+    def reset(self, max_pos: int) -> None:
+        self.caches = []
+        for a in self.attn:
+            kn = a.shape.kv_heads * a.shape.head_dim
+            self.caches.append((np.zeros((max_pos, kn), np.float32), np.zeros((max_pos, kn), np.float32)))
+
+    def forward(self, token: int, pos: int, trace: dict | None = None) -> np.ndarray:
+        """Softcapped logits; `trace` receives the stages the reference dumps (embed,
+        layerN_hidden, final_norm, logits)."""
+        hidden = embed(self.embed_w, token)
+        if trace is not None:
+            trace["embed"] = hidden.copy()
+        for l in range(self.num_layers):
+            a = self.attn[l]
+            kc, vc = self.caches[l]
+            attn = np.zeros(HIDDEN, np.float32)
+            view = a.view()
+            lib().orc_attention_step(C.byref(a.shape), C.byref(view), pos, _ptr(hidden), _ptr(kc), _ptr(vc),
+                                     _ptr(attn), None, None, None)
+            hidden = (hidden + rms_norm(attn, self.post_attn[l])).astype(np.float32)
+            r = self.moe[l].block(hidden)
+            self.used[l].update(int(e) for e in r["idx"])
+            hidden = r["hidden"]
+            if trace is not None:
+                trace[f"layer{l}_hidden"] = hidden.copy()
+        normed = rms_norm(hidden, self.final_norm)
+        e = self.embed_w
+        logits = softcap(matvec(e["w"], e["s"], e["b"], normed, e["rows"], e["in_dim"], 4), self.SOFTCAP)
+        if trace is not None:
+            trace["final_norm"], trace["logits"] = normed, logits
+        return logits
+
+    def greedy(self, prompt, max_tokens: int, stops=(1, 106, 50), trace: dict | None = None) -> list[int]:
+        """Prompt prefilled token by token, then greedy tokens (argmax, ties to the lower id)
+        until max_tokens or a stop id, as CpuReference::generate does; `trace` gets the first
+        prompt token's stages."""
+        self.reset(len(prompt) + max_tokens + 1)
+        logits = None
+        for i, t in enumerate(prompt):
+            logits = self.forward(int(t), i, trace if i == 0 else None)
+        out, pos = [], len(prompt)
+        for step in range(max_tokens):
+            nxt = int(np.argmax(logits))
+            if nxt in stops:
+                break
+            out.append(nxt)
+            if step + 1 >= max_tokens:
+                break
+            logits = self.forward(nxt, pos)
+            pos += 1
+        return out

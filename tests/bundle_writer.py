@@ -179,3 +179,73 @@ def write_bundle(root: str, num_layers: int = 2, seed: int = 0, expert_images=No
     with open(os.path.join(root, "manifest.json"), "w") as f:
         json.dump(manifest, f, indent=2)
     return plan
+
+
+def quant_entry(name: str, m: dict):
+    """An int4 MLX-affine tensor as the converter stores it: u32 words, shape [rows, in_dim / 8]."""
+    return (name, U32, [m["rows"], m["in_dim"] // 8], np.ascontiguousarray(m["w"]).reshape(-1),
+            np.ascontiguousarray(m["s"]).reshape(-1).view(np.uint8),
+            np.ascontiguousarray(m["b"]).reshape(-1).view(np.uint8))
+
+
+def bf16_entry(name: str, v: np.ndarray):
+    return (name, BF16, [v.size], np.ascontiguousarray(v).reshape(-1).view(np.uint8), None, None)
+
+
+def write_model_bundle(root: str, dec) -> None:
+    """Writes the whole synthetic decoder `dec` (oracle.SynthDecoder) as a bundle the reference's
+    CpuReference loads (src/cpu_reference.cpp:167-219): the MoE tensors of write_bundle, the
+    attention tensors (full-attention layers without v_proj), the tied embedding and the final
+    norm in resident.bin; each layer file sparse except for the experts the decoder has routed
+    to (dec.used), which are the only blocks the reference reads when it routes the same way;
+    the manifest's arch; and a minimal tokenizer whose stop pieces lie outside the vocabulary,
+    so generation never stops early."""
+    os.makedirs(os.path.join(root, "packed_experts"), exist_ok=True)
+    os.makedirs(os.path.join(root, "tokenizer"), exist_ok=True)
+    entries = [quant_entry("model.embed_tokens.weight", dec.embed_w), bf16_entry("model.norm.weight", dec.final_norm)]
+    for l in range(dec.num_layers):
+        P = f"model.layers.{l}."
+        entries += layer_entries(l, synth_resident_bytes(dec.seed, l))
+        a = dec.attn[l]
+        entries += [quant_entry(P + "self_attn.q_proj.weight", a.q), quant_entry(P + "self_attn.k_proj.weight", a.k),
+                    quant_entry(P + "self_attn.o_proj.weight", a.o),
+                    bf16_entry(P + "self_attn.q_norm.weight", a.q_norm),
+                    bf16_entry(P + "self_attn.k_norm.weight", a.k_norm),
+                    bf16_entry(P + "input_layernorm.weight", a.input_norm),
+                    bf16_entry(P + "post_attention_layernorm.weight", dec.post_attn[l])]
+        if not dec.full_mask[l]:
+            entries.append(quant_entry(P + "self_attn.v_proj.weight", a.v))
+    write_resident(os.path.join(root, "resident.bin"), entries, extra_names=())
+    block, stride = expert_block()
+    layers = []
+    buf = np.zeros(stride, np.uint8)
+    for l in range(dec.num_layers):
+        fname = f"layer_{l:02d}.bin"
+        with open(os.path.join(root, "packed_experts", fname), "wb") as f:
+            f.truncate(EXPERTS * stride)
+            for e in sorted(dec.used[l]):
+                buf[:] = 0
+                oracle.lib().orc_synth_expert(C.c_uint64(dec.seed), l, e, HIDDEN, MOE_INTER,
+                                              buf.ctypes.data_as(C.c_void_p))
+                f.seek(e * stride)
+                f.write(buf.tobytes())
+        layers.append({"layer": l, "file": fname})
+    layout = {"expertStride": stride, "numLayers": dec.num_layers, "expertsPerLayer": EXPERTS, "expertBlock": block,
+              "layers": layers}
+    arch = {"hiddenSize": HIDDEN, "ffnIntermediate": FFN, "moeIntermediateSize": MOE_INTER, "numHeads": 16,
+            "numKVHeads": 8, "numFullKVHeads": 2, "headDim": 256, "fullHeadDim": 512, "vocabSize": dec.vocab,
+            "slidingWindow": dec.window, "finalLogitSoftcap": dec.SOFTCAP, "ropeTheta": 10000.0,
+            "fullRopeTheta": 1000000.0, "partialRotaryFactor": 0.25, "rmsNormEps": 1e-6,
+            "numLayers": dec.num_layers, "numExperts": EXPERTS, "topKExperts": 8, "tieWordEmbeddings": True,
+            "attentionKEqV": True, "hiddenActivation": "gelu_pytorch_tanh",
+            "fullAttentionLayerMask": list(dec.full_mask)}
+    manifest = {"magic": "GTURBO", "versionMajor": 1, "versionMinor": 0, "flags": {"streamingPresent": True},
+                "modelId": "synthetic-gemma-4-26b-a4b", "numLayers": dec.num_layers, "expertsPerLayer": EXPERTS,
+                "expertStride": stride, "arch": arch, "files": {}}
+    with open(os.path.join(root, "packed_experts", "layout.json"), "w") as f:
+        json.dump(layout, f, indent=2)
+    with open(os.path.join(root, "manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=2)
+    vocab = {"<eos>": dec.vocab + 1, "<turn|>": dec.vocab + 2, "<|tool_response>": dec.vocab + 3, "a": 3}
+    with open(os.path.join(root, "tokenizer", "tokenizer.json"), "w") as f:
+        json.dump({"model": {"type": "BPE", "vocab": vocab, "merges": []}}, f)
