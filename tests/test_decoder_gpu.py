@@ -1,0 +1,61 @@
+"""The whole decoder on the device (gtmoe.decoder.DeviceDecoder: embedding lookup, attention,
+MoE block per layer, final norm, greedy LM head through the C ABI) against the reference's own
+CpuReference::generate tokens on the same synthetic two-layer model (tests/golden/decoder.npz,
+pinned bit-exact to the composed CPU oracle by tests/test_decoder_oracle.py).
+
+Bar: identical greedy tokens (north_star's bar for config 4).
+
+These tests have not run on a B200 yet; they are collected only when GTM_ATTENTION_GPU=1.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROOT, "tests", "golden")]
+
+import oracle  # noqa: E402
+from make_golden import DECODER, DECODER_NEW_TOKENS, DECODER_PROMPTS, DECODER_STOPS  # noqa: E402
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(os.environ.get("GTM_ATTENTION_GPU") != "1",
+                                 reason="device attention not yet run on a B200 (set GTM_ATTENTION_GPU=1)")]
+
+
+def device_decoder():
+    import torch
+    import gtmoe
+    from gtmoe.decoder import AttnLayerWeights, DeviceDecoder
+
+    def quant(m):
+        return {"w": torch.from_numpy(np.ascontiguousarray(m["w"])).cuda(),
+                "s": torch.from_numpy(np.ascontiguousarray(m["s"]).view(np.int16)).cuda(),
+                "b": torch.from_numpy(np.ascontiguousarray(m["b"]).view(np.int16)).cuda(),
+                "rows": m["rows"], "in_dim": m["in_dim"]}
+
+    def bf16(v):
+        return torch.from_numpy(np.ascontiguousarray(v).view(np.int16)).cuda()
+
+    dec = oracle.SynthDecoder(**DECODER)
+    layers = []
+    for l in range(dec.num_layers):
+        a, s = dec.attn[l], dec.attn[l].shape
+        full = bool(dec.full_mask[l])
+        layers.append(AttnLayerWeights(quant(a.q), quant(a.k), None if full else quant(a.v), quant(a.o),
+                                       bf16(a.input_norm), bf16(a.q_norm), bf16(a.k_norm), bf16(dec.post_attn[l]),
+                                       s.num_heads, s.kv_heads, s.head_dim, s.rotated_pairs, s.theta,
+                                       0 if full else s.sliding_window))
+    moe = gtmoe.SynthModel(dec.num_layers, seed=DECODER["seed"])
+    max_pos = max(len(p) for p in DECODER_PROMPTS) + DECODER_NEW_TOKENS + 1
+    return DeviceDecoder(layers, moe.layers, quant(dec.embed_w), bf16(dec.final_norm), max_pos), moe
+
+
+def test_greedy_tokens_match_reference():
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decoder.npz"))
+    dd, _moe = device_decoder()
+    for i, p in enumerate(DECODER_PROMPTS):
+        assert dd.greedy(p, DECODER_NEW_TOKENS, DECODER_STOPS) == g[f"prompt{i}.tokens"].tolist(), i
