@@ -1,6 +1,6 @@
 """The whole decoder on the device (gtmoe.decoder.DeviceDecoder: embedding lookup, attention,
 MoE block per layer, final norm, greedy LM head through the C ABI) against the reference's own
-CpuReference::generate tokens on the same synthetic two-layer model (tests/golden/decoder.npz,
+CpuReference::generate tokens on the same synthetic two- and three-layer models (tests/golden/decoder.npz,
 pinned bit-exact to the composed CPU oracle by tests/test_decoder_oracle.py).
 
 Bar: identical greedy tokens (north_star's bar for config 4).
@@ -19,14 +19,14 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROOT, "tests", "golden")]
 
 import oracle  # noqa: E402
-from make_golden import DECODER, DECODER_NEW_TOKENS, DECODER_PROMPTS, DECODER_STOPS  # noqa: E402
+from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_STOPS  # noqa: E402
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(os.environ.get("GTM_ATTENTION_GPU") != "1",
                                  reason="device attention not yet run on a B200 (set GTM_ATTENTION_GPU=1)")]
 
 
-def device_decoder():
+def device_decoder(args, prompts):
     import torch
     import gtmoe
     from gtmoe.decoder import AttnLayerWeights, DeviceDecoder
@@ -40,7 +40,7 @@ def device_decoder():
     def bf16(v):
         return torch.from_numpy(np.ascontiguousarray(v).view(np.int16)).cuda()
 
-    dec = oracle.SynthDecoder(**DECODER)
+    dec = oracle.SynthDecoder(**args)
     layers = []
     for l in range(dec.num_layers):
         a, s = dec.attn[l], dec.attn[l].shape
@@ -49,13 +49,15 @@ def device_decoder():
                                        bf16(a.input_norm), bf16(a.q_norm), bf16(a.k_norm), bf16(dec.post_attn[l]),
                                        s.num_heads, s.kv_heads, s.head_dim, s.rotated_pairs, s.theta,
                                        0 if full else s.sliding_window))
-    moe = gtmoe.SynthModel(dec.num_layers, seed=DECODER["seed"])
-    max_pos = max(len(p) for p in DECODER_PROMPTS) + DECODER_NEW_TOKENS + 1
+    moe = gtmoe.SynthModel(dec.num_layers, seed=args["seed"])
+    max_pos = max(len(p) for p in prompts) + DECODER_NEW_TOKENS + 1
     return DeviceDecoder(layers, moe.layers, quant(dec.embed_w), bf16(dec.final_norm), max_pos), moe
 
 
-def test_greedy_tokens_match_reference():
+@pytest.mark.parametrize("case", sorted(DECODER_CASES))
+def test_greedy_tokens_match_reference(case):
     g = np.load(os.path.join(ROOT, "tests", "golden", "decoder.npz"))
-    dd, _moe = device_decoder()
-    for i, p in enumerate(DECODER_PROMPTS):
-        assert dd.greedy(p, DECODER_NEW_TOKENS, DECODER_STOPS) == g[f"prompt{i}.tokens"].tolist(), i
+    args, prompts = DECODER_CASES[case]
+    dd, _moe = device_decoder(args, prompts)
+    for i, p in enumerate(prompts):
+        assert dd.greedy(p, DECODER_NEW_TOKENS, DECODER_STOPS) == g[f"{case}.prompt{i}.tokens"].tolist(), (case, i)
