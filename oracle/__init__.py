@@ -168,8 +168,8 @@ def ref():
         R.gtref_attention_step.argtypes = [C.POINTER(AttnShape), C.POINTER(AttnLayer), C.c_int, C.c_void_p,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         R.gtref_generate.restype = C.c_int
-        R.gtref_generate.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_int, C.c_char_p, C.c_void_p,
-                                     C.POINTER(C.c_uint32), C.c_char_p, C.c_size_t]
+        R.gtref_generate.argtypes = [C.c_char_p, C.c_void_p, C.c_uint32, C.c_int, C.c_char_p, C.POINTER(Sampling),
+                                     C.c_void_p, C.POINTER(C.c_uint32), C.c_char_p, C.c_size_t]
         R.gtref_validate_sampling.restype = C.c_int
         R.gtref_validate_sampling.argtypes = [C.POINTER(Sampling)]
         R.gtref_splitmix64.restype = C.c_uint64
@@ -490,15 +490,18 @@ def softcap(z: np.ndarray, cap: float) -> np.ndarray:
     return out
 
 
-def ref_generate(model_dir: str, prompt, max_tokens: int, dump_dir: str | None = None) -> list[int]:
-    """The reference's CpuReference::generate, greedy, on a bundle directory; with dump_dir, its
-    per-stage tensors of the first prompt token are written there."""
+def ref_generate(model_dir: str, prompt, max_tokens: int, dump_dir: str | None = None,
+                 sampling: Sampling | None = None) -> list[int]:
+    """The reference's CpuReference::generate on a bundle directory: greedy, or with `sampling`
+    (a seed of 0 means none there, as CpuGenerationOptions has it); with dump_dir, its per-stage
+    tensors of the first prompt token are written there."""
     p = np.ascontiguousarray(prompt, dtype=np.uint32)
     out = np.zeros(max_tokens + 1, np.uint32)
     n = C.c_uint32(0)
     err = C.create_string_buffer(512)
     dd = None if dump_dir is None else dump_dir.encode()
-    if ref().gtref_generate(model_dir.encode(), _ptr(p), p.size, max_tokens, dd, _ptr(out), C.byref(n), err,
+    sp = None if sampling is None else C.byref(sampling)
+    if ref().gtref_generate(model_dir.encode(), _ptr(p), p.size, max_tokens, dd, sp, _ptr(out), C.byref(n), err,
                             512) != 0:
         raise RuntimeError("reference generate failed: " + err.value.decode())
     return [int(t) for t in out[:n.value]]
@@ -560,6 +563,33 @@ class SynthDecoder:
         if trace is not None:
             trace["final_norm"], trace["logits"] = normed, logits
         return logits
+
+    def sample(self, prompt, max_tokens: int, p: Sampling, stops=(1, 106, 50)) -> list[int]:
+        """CpuReference::generate with sampling (src/cpu_reference.cpp:544-595): the penalty over
+        the prompt and the tokens so far on the softcapped logits, then sample_token with the
+        generator state seed_for(p, position of the next token)."""
+        assert validate_sampling(p) == 0
+        self.reset(len(prompt) + max_tokens + 1)
+        logits = None
+        for i, t in enumerate(prompt):
+            logits = self.forward(int(t), i)
+        history = [int(t) for t in prompt] if p.repetition_penalty != 1.0 else []
+        out, pos = [], len(prompt)
+        for step in range(max_tokens):
+            pen = apply_repetition_penalty(logits, history, p.repetition_penalty, self.SOFTCAP)
+            rc, nxt = sample_token(pen, p, seed_for(p, pos))
+            if rc != 0:
+                raise ValueError(f"sample_token failed ({rc})")
+            if nxt in stops:
+                break
+            out.append(nxt)
+            if p.repetition_penalty != 1.0:
+                history.append(nxt)
+            if step + 1 >= max_tokens:
+                break
+            logits = self.forward(nxt, pos)
+            pos += 1
+        return out
 
     def greedy(self, prompt, max_tokens: int, stops=(1, 106, 50), trace: dict | None = None) -> list[int]:
         """Prompt prefilled token by token, then greedy tokens (argmax, ties to the lower id)

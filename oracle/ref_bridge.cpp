@@ -258,47 +258,6 @@ int gtref_attention_step(const gtref_attn_shape* s, const gtref_attn_layer* L, i
     return 0;
 }
 
-/* ---- the whole model: CpuReference::load + generate on a bundle directory ---- */
-
-static std::string read_all(const std::string& path) {
-    std::ifstream f(path, std::ios::binary);
-    if (!f) throw gturbo::GTurboFormatError("cannot open " + path);
-    std::ostringstream ss;
-    ss << f.rdbuf();
-    return ss.str();
-}
-
-/* The reference's public generation path (cpu_reference.cpp:167-219 load, :544-595 generate)
- * with greedy decoding (temperature 0): the prompt is prefilled token by token, then up to
- * max_tokens tokens are produced, stopping before any stop token. With dump_dir set, the reference
- * also writes the first prompt token's stages there (embed, layerN_hidden, final_norm, logits as
- * raw .f32 files, cpu_reference.cpp:142-150). 0, or 1 with the exception's message in err. */
-int gtref_generate(const char* dir, const uint32_t* prompt, uint32_t n_prompt, int max_tokens, const char* dump_dir,
-                   uint32_t* out, uint32_t* n_out, char* err, size_t err_len) {
-    try {
-        const std::string d(dir);
-        auto manifest = gturbo::GTurboManifestV1::from_json_string(read_all(d + "/manifest.json"));
-        auto layout = gturbo::PackedExpertsLayoutV1::from_json_string(read_all(d + "/packed_experts/layout.json"));
-        gturbo::CpuReference ref(manifest, layout, d);
-        ref.load();
-        gturbo::CpuGenerationOptions opts;
-        opts.max_tokens = max_tokens;
-        opts.temperature = 0.0f;
-        if (dump_dir) opts.dump_dir = dump_dir;   // per-stage tensors of the first prompt token
-        const std::vector<uint32_t> tokens =
-            ref.generate(std::vector<uint32_t>(prompt, prompt + n_prompt), opts);
-        std::copy(tokens.begin(), tokens.end(), out);
-        *n_out = static_cast<uint32_t>(tokens.size());
-        return 0;
-    } catch (const std::exception& e) {
-        if (err && err_len) {
-            std::strncpy(err, e.what(), err_len - 1);
-            err[err_len - 1] = '\0';
-        }
-        return 1;
-    }
-}
-
 /* ---- token sampling: the reference's src/sampling.cpp, linked into this library ---- */
 
 /* Mirrors orc_sampling in oracle/sampling_oracle.h field for field. */
@@ -348,6 +307,56 @@ int gtref_sample_token(const float* logits, uint32_t vocab, const gtref_sampling
         *token = gturbo::sample_token(logits, vocab, params_of(p), seed);
         return 0;
     } catch (const gturbo::GTurboFormatError&) {
+        return 1;
+    }
+}
+
+/* ---- the whole model: CpuReference::load + generate on a bundle directory ---- */
+
+static std::string read_all(const std::string& path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) throw gturbo::GTurboFormatError("cannot open " + path);
+    std::ostringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+/* The reference's public generation path (cpu_reference.cpp:167-219 load, :544-595 generate)
+ * with greedy decoding (temperature 0) or, given `sampling`, the reference's sampling (softcapped
+ * logits, repetition penalty, sample_token with seed_for(position)): the prompt is prefilled
+ * token by token, then up to
+ * max_tokens tokens are produced, stopping before any stop token. With dump_dir set, the reference
+ * also writes the first prompt token's stages there (embed, layerN_hidden, final_norm, logits as
+ * raw .f32 files, cpu_reference.cpp:142-150). 0, or 1 with the exception's message in err. */
+int gtref_generate(const char* dir, const uint32_t* prompt, uint32_t n_prompt, int max_tokens, const char* dump_dir,
+                   const gtref_sampling* sampling, uint32_t* out, uint32_t* n_out, char* err, size_t err_len) {
+    try {
+        const std::string d(dir);
+        auto manifest = gturbo::GTurboManifestV1::from_json_string(read_all(d + "/manifest.json"));
+        auto layout = gturbo::PackedExpertsLayoutV1::from_json_string(read_all(d + "/packed_experts/layout.json"));
+        gturbo::CpuReference ref(manifest, layout, d);
+        ref.load();
+        gturbo::CpuGenerationOptions opts;
+        opts.max_tokens = max_tokens;
+        opts.temperature = 0.0f;
+        if (sampling) {   // CpuGenerationOptions carries the seed as "0 = none"
+            opts.temperature = sampling->temperature;
+            opts.top_p = sampling->top_p;
+            opts.top_k = sampling->top_k;
+            opts.repetition_penalty = sampling->repetition_penalty;
+            opts.seed = sampling->has_seed ? sampling->seed : 0;
+        }
+        if (dump_dir) opts.dump_dir = dump_dir;   // per-stage tensors of the first prompt token
+        const std::vector<uint32_t> tokens =
+            ref.generate(std::vector<uint32_t>(prompt, prompt + n_prompt), opts);
+        std::copy(tokens.begin(), tokens.end(), out);
+        *n_out = static_cast<uint32_t>(tokens.size());
+        return 0;
+    } catch (const std::exception& e) {
+        if (err && err_len) {
+            std::strncpy(err, e.what(), err_len - 1);
+            err[err_len - 1] = '\0';
+        }
         return 1;
     }
 }

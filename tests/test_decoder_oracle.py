@@ -12,7 +12,9 @@ Anchors:
   it, when oracle/_ref is built.
 
 This is the oracle for end-to-end greedy decode (config 4); the stage digests are bit-exact, the
-tokens after the first prompt token are compared as tokens.
+tokens after the first prompt token are compared as tokens. Sampled generation (the reference's
+softcap, repetition penalty, Top-P then Top-K then temperature, per-position seeds) is pinned the
+same way on the three-layer case.
 """
 from __future__ import annotations
 
@@ -26,7 +28,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "tests", "golden")]
 
 import oracle  # noqa: E402
-from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_STOPS, digest  # noqa: E402
+from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_SAMPLING, DECODER_STOPS, digest  # noqa: E402
 
 needs_ref = pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built (reference tree absent)")
 
@@ -77,3 +79,32 @@ def test_live_against_reference_generate(runs, tmp_path):
         for name in stages(dec.num_layers):
             ref = np.fromfile(dd / (name + ".f32"), np.float32)
             assert np.array_equal(ref.view(np.uint32), trace[name].view(np.uint32)), (i, name)
+
+
+@pytest.fixture(scope="module")
+def sampled():
+    args, prompts = DECODER_CASES["d3"]
+    dec = oracle.SynthDecoder(**args)
+    runs = [[dec.sample(p, DECODER_NEW_TOKENS, oracle.sampling_params(t, tp, tk, pen, seed=seed), DECODER_STOPS)
+             for p in prompts] for t, tp, tk, pen, seed in DECODER_SAMPLING]
+    return dec, prompts, runs
+
+
+def test_sampled_matches_reference_golden(sampled):
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decoder.npz"))
+    _, _, runs = sampled
+    for j, per_prompt in enumerate(runs):
+        for i, toks in enumerate(per_prompt):
+            assert toks == g[f"d3.sampled{j}.prompt{i}.tokens"].tolist(), (j, i)
+    assert len({t for per_prompt in runs for toks in per_prompt for t in toks}) > 10   # not a fixed point
+
+
+@needs_ref
+def test_sampled_live_against_reference_generate(sampled, tmp_path):
+    import bundle_writer as bw
+    dec, prompts, runs = sampled
+    bw.write_model_bundle(str(tmp_path), dec)
+    for (t, tp, tk, pen, seed), per_prompt in zip(DECODER_SAMPLING, runs):
+        sp = oracle.sampling_params(t, tp, tk, pen, seed=seed)
+        for p, toks in zip(prompts, per_prompt):
+            assert oracle.ref_generate(str(tmp_path), p, DECODER_NEW_TOKENS, None, sp) == toks
