@@ -3,7 +3,8 @@ MoE block per layer, final norm, greedy LM head through the C ABI) against the r
 CpuReference::generate tokens on the same synthetic two- and three-layer models (tests/golden/decoder.npz,
 pinned bit-exact to the composed CPU oracle by tests/test_decoder_oracle.py).
 
-Bar: identical greedy tokens (north_star's bar for config 4).
+Bar: identical greedy tokens (north_star's bar for config 4); for sampled decoding identical
+tokens with no draw flagged inside the double-exp bound.
 
 These tests have not run on a B200 yet; they are collected only when GTM_ATTENTION_GPU=1.
 """
@@ -19,7 +20,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROOT, "tests", "golden")]
 
 import oracle  # noqa: E402
-from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_STOPS  # noqa: E402
+from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_SAMPLING, DECODER_STOPS  # noqa: E402
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(os.environ.get("GTM_ATTENTION_GPU") != "1",
@@ -61,3 +62,15 @@ def test_greedy_tokens_match_reference(case):
     dd, _moe = device_decoder(args, prompts)
     for i, p in enumerate(prompts):
         assert dd.greedy(p, DECODER_NEW_TOKENS, DECODER_STOPS) == g[f"{case}.prompt{i}.tokens"].tolist(), (case, i)
+
+
+def test_sampled_tokens_match_reference():
+    from gtmoe.sampling import SamplingParams
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decoder.npz"))
+    args, prompts = DECODER_CASES["d3"]
+    dd, _moe = device_decoder(args, prompts)
+    for j, (t, tp, tk, pen, seed) in enumerate(DECODER_SAMPLING):
+        sp = SamplingParams(t, tp, tk, pen, seed is not None, 0 if seed is None else seed)
+        for i, p in enumerate(prompts):
+            assert dd.sample(p, DECODER_NEW_TOKENS, sp, DECODER_STOPS) == g[f"d3.sampled{j}.prompt{i}.tokens"].tolist(), \
+                (j, i)

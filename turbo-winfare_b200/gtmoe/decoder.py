@@ -7,7 +7,10 @@ q, k and v (full-attention layers: V is the raw k_proj output), gtm_qkv_epilogue
 and for K and V straight into their ring-cache rows (position p in row p % capacity),
 gtm_attention_decode, gtm_gemv_q4 for o, gtm_post_attn (the residual), then gtm_moe_decode for
 the layer; finally gtm_rmsnorm (final norm) and gtm_lm_head_greedy. Only the 4-byte token comes
-back to the host.
+back to the host. Sampled decoding (`sample`) instead forms the logits with gtm_gemv_q4 on the
+tied embedding, softcaps them (gtm_softcap), applies the repetition penalty over the device-side
+history and draws with gtm_sample_token, as the sampled branch of produce_token
+(runner.cpp:771-806) and CpuReference::generate (src/cpu_reference.cpp:573-593) do.
 
 The greedy head takes the argmax of the raw logits, as the reference's GPU greedy branch does
 (runner.cpp:720-770); the CPU reference takes it after the softcap, which can only differ when
@@ -48,6 +51,8 @@ class AttnLayerWeights:
 
 
 class DeviceDecoder:
+    SOFTCAP = 30.0   # final_logit_softcap
+
     def __init__(self, attn_layers: list[AttnLayerWeights], moe_layers, embed: dict, final_norm, max_pos: int,
                  eps: float = 1e-6, device: str = "cuda"):
         import torch
@@ -63,6 +68,8 @@ class DeviceDecoder:
         self.attn_out = torch.zeros(HIDDEN, **f32)
         self.views = torch.zeros(3, HIDDEN, **f32)
         self.token = torch.zeros(1, dtype=torch.int32, device=device)
+        self.logits = torch.zeros(embed["rows"], **f32)
+        self.sampler = None
         for a in attn_layers:
             cap = a.window if a.window > 0 else max_pos
             row = a.kv_heads * a.head_dim
@@ -77,8 +84,9 @@ class DeviceDecoder:
     def _gemv(self, m: dict, x, out, st) -> None:
         check(lib().gtm_gemv_q4(m["rows"], m["in_dim"], ptr(m["w"]), ptr(m["s"]), ptr(m["b"]), ptr(x), ptr(out), st))
 
-    def forward(self, token: int, pos: int, stream=None) -> None:
-        """One token through every layer and the greedy head; the token lands in self.token."""
+    def forward(self, token: int, pos: int, stream=None, logits: bool = False) -> None:
+        """One token through every layer, then the greedy head (the token lands in self.token)
+        or, with logits=True, the full softcapped logits in self.logits."""
         if pos >= self.max_pos:
             raise ValueError(f"position {pos} beyond max_pos {self.max_pos}")
         st = _stream(stream)
@@ -112,7 +120,11 @@ class DeviceDecoder:
                                   ptr(self.views[0]), ptr(self.views[1]), ptr(self.views[2]), st))
             self.moe(self.mid, self.hidden, first_layer=l, num_layers=1, norm_between_layers=False, stream=stream)
         check(L.gtm_rmsnorm(HIDDEN, ptr(self.hidden), ptr(self.final_norm), self.eps, ptr(self.normed), st))
-        self.lm(e["w"], e["s"], e["b"], self.normed, self.token, stream=stream)
+        if logits:
+            self._gemv(e, self.normed, self.logits, st)   # tie_word_embeddings
+            check(L.gtm_softcap(e["rows"], ptr(self.logits), self.SOFTCAP, ptr(self.logits), st))
+        else:
+            self.lm(e["w"], e["s"], e["b"], self.normed, self.token, stream=stream)
 
     def greedy(self, prompt, max_tokens: int, stops=(1, 106, 50), stream=None) -> list[int]:
         """CpuReference::generate's loop (src/cpu_reference.cpp:560-593) with greedy tokens."""
@@ -130,6 +142,47 @@ class DeviceDecoder:
             if step + 1 >= max_tokens:
                 break
             self.forward(nxt, pos, stream)
+            pos += 1
+        self.moe.check(stream)
+        return out
+
+    def sample(self, prompt, max_tokens: int, p, stops=(1, 106, 50), stream=None) -> list[int]:
+        """Sampled decoding (gtmoe.sampling.SamplingParams `p`): CpuReference::generate's loop with
+        the penalty, the draw and seed_for(p, position) on the device; one token and its status
+        word come back per step. Raises if a draw is degenerate or compared values inside the
+        double-exp bound (the status word's NEAR bits)."""
+        import torch
+        from .sampling import DEGENERATE, Sampler, seed_for, validate_sampling
+        validate_sampling(p)
+        if self.sampler is None:
+            self.sampler = Sampler(self.embed["rows"])
+        for a in self.attn:
+            for c in a.caches:
+                c.zero_()
+        hist = torch.zeros(len(prompt) + max_tokens, dtype=torch.int32, device=self.hidden.device)
+        n_hist = 0
+        if p.repetition_penalty != 1.0:
+            hist[:len(prompt)] = torch.tensor([int(t) for t in prompt], dtype=torch.int32)
+            n_hist = len(prompt)
+        for i, t in enumerate(prompt):
+            self.forward(int(t), i, stream, logits=True)
+        out, pos = [], len(prompt)
+        for step in range(max_tokens):
+            self.sampler.apply_repetition_penalty(self.logits, hist[:n_hist] if n_hist else None, p.repetition_penalty,
+                                                  self.SOFTCAP, stream=stream)
+            tok, status = (int(v) for v in self.sampler.sample_token(self.logits, p, seed_for(p, pos), stream).tolist())
+            if status:
+                raise RuntimeError(f"sample_token status {status} at position {pos}" +
+                                   (" (degenerate distribution)" if status & DEGENERATE else ""))
+            if tok in stops:
+                break
+            out.append(tok)
+            if p.repetition_penalty != 1.0:
+                hist[n_hist] = tok
+                n_hist += 1
+            if step + 1 >= max_tokens:
+                break
+            self.forward(tok, pos, stream, logits=True)
             pos += 1
         self.moe.check(stream)
         return out
