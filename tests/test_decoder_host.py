@@ -1,0 +1,208 @@
+"""Host orchestration of gtmoe.decoder.DeviceDecoder, checked on the CPU.
+
+DeviceDecoder is host code that sequences C-ABI calls: ring-cache slots, which buffer feeds V on
+a full-attention layer, window starts, the per-layer MoE launch, the device-side penalty history,
+and the order of every argument. Here each gtm_* entry it reaches is replaced by a stand-in
+that does the same arithmetic with the pinned CPU oracle on host memory, and each call's
+argument count is checked against the C ABI's signature table. With those stand-ins the
+decoder's greedy and sampled tokens must equal the reference's own generate tokens
+(tests/golden/decoder.npz): the sequencing is right before the device kernels ever run.
+Nothing here touches a GPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROOT, "tests", "golden")]
+
+import oracle  # noqa: E402
+from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_SAMPLING, DECODER_STOPS  # noqa: E402
+
+
+def addr(p) -> int:
+    if p is None:
+        return 0
+    if isinstance(p, int):
+        return p
+    return C.cast(p, C.c_void_p).value or 0
+
+
+def view(p, n: int, dtype) -> np.ndarray:
+    dt = np.dtype(dtype)
+    return np.frombuffer((C.c_char * (n * dt.itemsize)).from_address(addr(p)), dtype=dt)
+
+
+class OracleLib:
+    """The device entries DeviceDecoder uses, done by the oracle on host memory."""
+
+    def __init__(self, real, moe_layers, synth_layers):
+        self.real, self.moe_base, self.synth = real, C.addressof(moe_layers), synth_layers
+        import gtmoe
+        self.sig = gtmoe.SIGNATURES
+
+    def __getattr__(self, name):
+        fn = getattr(type(self), "_" + name, None)
+        if fn is None:
+            return getattr(self.real, name)   # host-only entries (validate, seed_for, errors)
+
+        def call(*args):
+            assert len(args) == len(self.sig[name][1]), (name, len(args))
+            return fn(self, *args)
+        return call
+
+    # sizes: any non-zero workspace is accepted by the stand-ins
+    def _gtm_moe_decode_workspace_bytes(self, dims):
+        return 256
+
+    def _gtm_lm_head_workspace_bytes(self, rows):
+        return 256
+
+    def _gtm_attention_workspace_bytes(self, q_heads, head_dim, window):
+        return 256
+
+    def _gtm_sample_workspace_bytes(self, vocab):
+        return 256
+
+    def _gtm_moe_decode_check(self, ws, st):
+        return 0
+
+    def _gtm_embed_lookup(self, rows, in_dim, w, s, b, token, scale, out, st):
+        assert token < rows and np.float32(scale) == np.sqrt(np.float32(in_dim))
+        g = in_dim // 64
+        m = {"w": view(w, rows * in_dim // 2, np.uint8), "s": view(s, rows * g, np.uint16),
+             "b": view(b, rows * g, np.uint16), "rows": rows, "in_dim": in_dim}
+        view(out, in_dim, np.float32)[:] = oracle.embed(m, token)
+        return 0
+
+    def _gtm_gemv_q4(self, rows, in_dim, w, s, b, x, out, st):
+        g = in_dim // 64
+        view(out, rows, np.float32)[:] = oracle.matvec(view(w, rows * in_dim // 2, np.uint8),
+                                                      view(s, rows * g, np.uint16), view(b, rows * g, np.uint16),
+                                                      view(x, in_dim, np.float32), rows, in_dim, 4)
+        return 0
+
+    def _gtm_rmsnorm(self, n, x, w, eps, out, st):
+        wa = None if addr(w) == 0 else view(w, n, np.uint16)
+        view(out, n, np.float32)[:] = oracle.rms_norm(view(x, n, np.float32).copy(), wa, eps)
+        return 0
+
+    def _gtm_qkv_epilogue(self, heads, head_dim, inp, w, eps, pairs, position, theta, out, st):
+        wa = None if addr(w) == 0 else view(w, head_dim, np.uint16)
+        vec = view(inp, heads * head_dim, np.float32).copy()
+        view(out, heads * head_dim, np.float32)[:] = oracle.qkv_epilogue(vec, heads, head_dim, wa, eps, pairs,
+                                                                         float(position), theta)
+        return 0
+
+    def _gtm_attention_decode(self, q_heads, kv_heads, head_dim, n_pos, first, capacity, q, kc, vc, ctx, ws, wsb,
+                              st):
+        assert first < n_pos and n_pos - first <= capacity
+        row = kv_heads * head_dim
+        view(ctx, q_heads * head_dim, np.float32)[:] = oracle.attention_core(
+            view(q, q_heads * head_dim, np.float32), view(kc, capacity * row, np.float32),
+            view(vc, capacity * row, np.float32), q_heads, kv_heads, head_dim, n_pos, first, capacity)
+        return 0
+
+    def _gtm_post_attn(self, d, attn, hidden, w_post, w_pre, w_pre2, eps, hidden_out, dense, routed, router, st):
+        h = view(hidden, d, np.float32)
+        view(hidden_out, d, np.float32)[:] = h + oracle.rms_norm(view(attn, d, np.float32).copy(),
+                                                                 view(w_post, d, np.uint16), eps)
+        return 0
+
+    def _gtm_moe_decode(self, dims, layers, n, io, ws, wsb, st):
+        import gtmoe
+        assert n == 1
+        layer = (addr(layers) - self.moe_base) // C.sizeof(gtmoe.Layer)
+        o = io._obj
+        x = view(o.hidden_in_dev, oracle.HIDDEN, np.float32).copy()
+        view(o.hidden_out_dev, oracle.HIDDEN, np.float32)[:] = self.synth[layer].block(x)["hidden"]
+        return 0
+
+    def _gtm_lm_head_greedy(self, rows, in_dim, w, s, b, x, token, logit, ws, wsb, st):
+        g = in_dim // 64
+        lg = oracle.matvec(view(w, rows * in_dim // 2, np.uint8), view(s, rows * g, np.uint16),
+                           view(b, rows * g, np.uint16), view(x, in_dim, np.float32), rows, in_dim, 4)
+        view(token, 1, np.int32)[0] = int(np.argmax(lg))
+        return 0
+
+    def _gtm_softcap(self, n, inp, cap, out, st):
+        view(out, n, np.float32)[:] = oracle.softcap(view(inp, n, np.float32).copy(), cap)
+        return 0
+
+    def _gtm_repetition_penalty(self, logits, vocab, hist, n, penalty, softcap, ws, wsb, st):
+        if penalty == 1.0 or n == 0:
+            return 0
+        lg = view(logits, vocab, np.float32)
+        lg[:] = oracle.apply_repetition_penalty(lg.copy(), view(hist, n, np.uint32).copy(), penalty, softcap)
+        return 0
+
+    def _gtm_sample_token(self, logits, vocab, p, seed, token, status, ws, wsb, st):
+        sp = p._obj
+        op = oracle.Sampling(sp.temperature, sp.top_p, sp.top_k, sp.repetition_penalty, sp.has_seed, 0, sp.seed)
+        rc, tok = oracle.sample_token(view(logits, vocab, np.float32).copy(), op, seed)
+        view(token, 1, np.int32)[0] = tok if rc == 0 else -1
+        view(status, 1, np.int32)[0] = 0 if rc == 0 else 1
+        return 0
+
+
+@pytest.fixture
+def host_decoder(monkeypatch):
+    import torch
+    import gtmoe
+    from gtmoe import attention, decoder, sampling
+    from gtmoe.decoder import AttnLayerWeights, DeviceDecoder
+
+    def make(case):
+        args, prompts = DECODER_CASES[case]
+        dec = oracle.SynthDecoder(**args)
+        moe_layers = (gtmoe.Layer * dec.num_layers)()
+        fake = OracleLib(gtmoe.lib(), moe_layers, dec.moe)
+        for mod in (gtmoe, attention, decoder, sampling):
+            monkeypatch.setattr(mod, "lib", lambda: fake)
+            monkeypatch.setattr(mod, "_stream", lambda stream=None: None)
+
+        def quant(m):
+            return {"w": torch.from_numpy(np.ascontiguousarray(m["w"])),
+                    "s": torch.from_numpy(np.ascontiguousarray(m["s"]).view(np.int16)),
+                    "b": torch.from_numpy(np.ascontiguousarray(m["b"]).view(np.int16)),
+                    "rows": m["rows"], "in_dim": m["in_dim"]}
+
+        def bf16(v):
+            return torch.from_numpy(np.ascontiguousarray(v).view(np.int16))
+
+        layers = []
+        for l in range(dec.num_layers):
+            a, s = dec.attn[l], dec.attn[l].shape
+            full = bool(dec.full_mask[l])
+            layers.append(AttnLayerWeights(quant(a.q), quant(a.k), None if full else quant(a.v), quant(a.o),
+                                           bf16(a.input_norm), bf16(a.q_norm), bf16(a.k_norm),
+                                           bf16(dec.post_attn[l]), s.num_heads, s.kv_heads, s.head_dim,
+                                           s.rotated_pairs, s.theta, 0 if full else s.sliding_window))
+        max_pos = max(len(p) for p in prompts) + DECODER_NEW_TOKENS + 1
+        dd = DeviceDecoder(layers, moe_layers, quant(dec.embed_w), bf16(dec.final_norm), max_pos, device="cpu")
+        return dd, prompts
+    return make
+
+
+@pytest.mark.parametrize("case", sorted(DECODER_CASES))
+def test_greedy_sequencing_reproduces_reference(host_decoder, case):
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decoder.npz"))
+    dd, prompts = host_decoder(case)
+    for i, p in enumerate(prompts):
+        assert dd.greedy(p, DECODER_NEW_TOKENS, DECODER_STOPS) == g[f"{case}.prompt{i}.tokens"].tolist(), (case, i)
+
+
+def test_sampled_sequencing_reproduces_reference(host_decoder):
+    from gtmoe.sampling import SamplingParams
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decoder.npz"))
+    dd, prompts = host_decoder("d3")
+    for j, (t, tp, tk, pen, seed) in enumerate(DECODER_SAMPLING):
+        sp = SamplingParams(t, tp, tk, pen, seed is not None, 0 if seed is None else seed)
+        for i, p in enumerate(prompts):
+            assert dd.sample(p, DECODER_NEW_TOKENS, sp, DECODER_STOPS) == g[f"d3.sampled{j}.prompt{i}.tokens"].tolist(), \
+                (j, i)

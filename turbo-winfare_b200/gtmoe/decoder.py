@@ -155,7 +155,7 @@ class DeviceDecoder:
         from .sampling import DEGENERATE, Sampler, seed_for, validate_sampling
         validate_sampling(p)
         if self.sampler is None:
-            self.sampler = Sampler(self.embed["rows"])
+            self.sampler = Sampler(self.embed["rows"], device=str(self.hidden.device))
         for a in self.attn:
             for c in a.caches:
                 c.zero_()
