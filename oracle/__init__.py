@@ -28,11 +28,22 @@ REF_PATH = os.path.join(HERE, "_ref", "libgtref.so")
 HIDDEN, MOE_INTER, FFN, EXPERTS, TOP_K, EPS = 2816, 704, 2112, 128, 8, 1e-6
 
 
+def reference_dir(ref_dir: str | None = None) -> str | None:
+    """The reference checkout: the argument, else $GTM_REFERENCE_DIR, else a directory named
+    `reference` beside this repository; None when none of them holds src/cpu_reference.cpp."""
+    cands = [ref_dir] if ref_dir else [os.environ.get("GTM_REFERENCE_DIR"),
+                                       os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for c in cands:
+        if c and os.path.isfile(os.path.join(c, "src", "cpu_reference.cpp")):
+            return os.path.abspath(c)
+    return None
+
+
 def build(ref_dir: str | None = None) -> None:
     """Builds liboracle.so, and _ref/libgtref.so when the reference sources are present."""
     subprocess.check_call(["make", "-s", "-C", HERE, "oracle"])
-    ref = ref_dir or "/root/reference"
-    if os.path.isfile(os.path.join(ref, "src", "cpu_reference.cpp")):
+    ref = reference_dir(ref_dir)
+    if ref is not None:
         subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF={ref}"])
 
 

@@ -6,7 +6,6 @@ reference's own GPU kernels are held to (numpy allclose, |got - want| <= 1e-5 + 
 docs/ARCHITECTURE.md), since device powf/sinf/cosf/expf and a parallel softmax round
 differently from the C library and a sequential loop.
 
-These tests have not run on a B200 yet; they are collected only when GTM_ATTENTION_GPU=1.
 """
 from __future__ import annotations
 
@@ -22,9 +21,7 @@ sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROO
 import oracle  # noqa: E402
 from test_attn_oracle import uniform_stream  # noqa: E402
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("GTM_ATTENTION_GPU") != "1",
-                                 reason="device attention not yet run on a B200 (set GTM_ATTENTION_GPU=1)")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(scope="module")

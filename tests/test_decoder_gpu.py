@@ -6,7 +6,6 @@ pinned bit-exact to the composed CPU oracle by tests/test_decoder_oracle.py).
 Bar: identical greedy tokens (north_star's bar for config 4); for sampled decoding identical
 tokens with no draw flagged inside the double-exp bound.
 
-These tests have not run on a B200 yet; they are collected only when GTM_ATTENTION_GPU=1.
 """
 from __future__ import annotations
 
@@ -22,9 +21,7 @@ sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROO
 import oracle  # noqa: E402
 from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_SAMPLING, DECODER_STOPS  # noqa: E402
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("GTM_ATTENTION_GPU") != "1",
-                                 reason="device attention not yet run on a B200 (set GTM_ATTENTION_GPU=1)")]
+pytestmark = pytest.mark.gpu
 
 
 def device_decoder(args, prompts):

@@ -206,3 +206,14 @@ def test_sampled_sequencing_reproduces_reference(host_decoder):
         for i, p in enumerate(prompts):
             assert dd.sample(p, DECODER_NEW_TOKENS, sp, DECODER_STOPS) == g[f"d3.sampled{j}.prompt{i}.tokens"].tolist(), \
                 (j, i)
+
+
+def test_empty_prompt_raises_as_reference(host_decoder):
+    """CpuReference::generate rejects an empty prompt (cpu_reference.cpp:546); so do both loops,
+    before any launch."""
+    from gtmoe.sampling import SamplingParams
+    dd, _ = host_decoder("d2")
+    with pytest.raises(ValueError, match="empty prompt"):
+        dd.greedy([], DECODER_NEW_TOKENS, DECODER_STOPS)
+    with pytest.raises(ValueError, match="empty prompt"):
+        dd.sample([], DECODER_NEW_TOKENS, SamplingParams(1.0, 1.0, 8, 1.0, True, 3), DECODER_STOPS)

@@ -5,7 +5,6 @@ Bar: identical tokens and bit-identical penalised logits; a draw whose status re
 inside the double-exp error bound (NEAR_CUT / NEAR_DRAW) is counted, and none is expected on
 these inputs.
 
-These tests have not run on a B200 yet; they are collected only when GTM_SAMPLING_GPU=1.
 """
 from __future__ import annotations
 
@@ -20,9 +19,7 @@ sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200")]
 
 import oracle  # noqa: E402
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("GTM_SAMPLING_GPU") != "1",
-                                 reason="device sampler not yet run on a B200 (set GTM_SAMPLING_GPU=1)")]
+pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(ROOT, "tests", "golden", "sampling.npz")
 

@@ -16,7 +16,10 @@ The greedy head takes the argmax of the raw logits, as the reference's GPU greed
 (runner.cpp:720-770); the CPU reference takes it after the softcap, which can only differ when
 tanh saturation rounds two logits to the same value.
 
-The attention entries have not yet been run on a B200.
+`greedy` and `sample` queue every launch on the caller's stream (torch's current stream when none
+is given) and make that stream torch's current one for the whole loop, so the host reads of the
+token and the writes into the device-side history are ordered after the kernels that produce and
+consume them. An empty prompt raises, as CpuReference::generate does (cpu_reference.cpp:546).
 """
 from __future__ import annotations
 
@@ -126,8 +129,23 @@ class DeviceDecoder:
         else:
             self.lm(e["w"], e["s"], e["b"], self.normed, self.token, stream=stream)
 
+    def _on_stream(self, stream):
+        """Makes the caller's stream torch's current one (device tensors only)."""
+        import contextlib
+        import torch
+        if self.hidden.device.type != "cuda":
+            return contextlib.nullcontext()
+        return torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream(self.hidden.device))
+
     def greedy(self, prompt, max_tokens: int, stops=(1, 106, 50), stream=None) -> list[int]:
         """CpuReference::generate's loop (src/cpu_reference.cpp:560-593) with greedy tokens."""
+        if len(prompt) == 0:
+            raise ValueError("empty prompt")   # cpu_reference.cpp:546
+        with self._on_stream(stream):
+            return self._greedy(prompt, max_tokens, stops)
+
+    def _greedy(self, prompt, max_tokens: int, stops) -> list[int]:
+        stream = None   # the caller's stream is torch's current one here
         for a in self.attn:
             for c in a.caches:
                 c.zero_()
@@ -151,8 +169,15 @@ class DeviceDecoder:
         the penalty, the draw and seed_for(p, position) on the device; one token and its status
         word come back per step. Raises if a draw is degenerate or compared values inside the
         double-exp bound (the status word's NEAR bits)."""
+        if len(prompt) == 0:
+            raise ValueError("empty prompt")   # cpu_reference.cpp:546
+        with self._on_stream(stream):
+            return self._sample(prompt, max_tokens, p, stops)
+
+    def _sample(self, prompt, max_tokens: int, p, stops) -> list[int]:
         import torch
         from .sampling import DEGENERATE, Sampler, seed_for, validate_sampling
+        stream = None   # the caller's stream is torch's current one here
         validate_sampling(p)
         if self.sampler is None:
             self.sampler = Sampler(self.embed["rows"], device=str(self.hidden.device))
