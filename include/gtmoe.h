@@ -249,6 +249,16 @@ GTM_API int gtm_moe_tokens(const GtmDims* dims, const GtmLayer* layer, const Gtm
 /* Reads back and clears the device-side error flag (synchronises `stream`). */
 GTM_API int gtm_moe_tokens_check(void* workspace_dev, void* stream);
 
+/* Stage timing of gtm_moe_tokens with device events, replacing the reference's wall-clock
+ * PerformanceMetrics timers around its fences (include/gturbo/runner.hpp:87-106,
+ * src/runner.cpp:396-421). `events` are n caller-owned cudaEvent_t handles (created, timing
+ * enabled); the calling thread's next gtm_moe_tokens calls record events[i] on their stream at
+ * stage boundary i (for i < n): 0 before the views and router, 1 before the routing tables,
+ * 2 before the grouped gate/up GEMM, 3 before the grouped down GEMM, 4 before the combine,
+ * 5 after it. The handles are kept (not owned) until the next call; n = 0 turns it off. */
+enum { GTM_PHASE_EVENTS = 6 };
+GTM_API int gtm_set_phase_events(void* const* events, int n);
+
 /* ---------------------------------------------------------------------------------------
  * Tied LM head with greedy argmax: LMHeadGreedy + ArgmaxReduce (shaders/LMHeadGreedy.hlsl:1-73,
  * shaders/ArgmaxReduce.hlsl:1-62; runner.cpp:720-770). token = argmax_r logits[r], ties to the

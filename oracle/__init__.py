@@ -266,6 +266,15 @@ class SynthLayer:
         e = np.ascontiguousarray(np.asarray(experts, dtype=np.uint32))
         lib().orc_synth_layer_ensure(self.h, _ptr(e), e.size)
 
+    def route(self, hidden_in, logit_bias=None, route_logits=None) -> np.ndarray:
+        """Views, router and top-k only (the selected experts are generated): the top-k ids."""
+        x = np.ascontiguousarray(hidden_in, dtype=np.float32)
+        lb = None if logit_bias is None else np.ascontiguousarray(logit_bias, dtype=np.float32)
+        rl = None if route_logits is None else np.ascontiguousarray(route_logits, dtype=np.float32)
+        idx = np.zeros(self.top_k, np.uint32)
+        lib().orc_synth_layer_route(self.h, _ptr(x), _ptr(lb), _ptr(rl), _ptr(idx))
+        return idx
+
     def block(self, hidden_in, logit_bias=None, route_logits=None, impl: str = "oracle"):
         """Runs the MoE block for one token. impl='ref' runs the reference's compiled helpers."""
         D, K = self.hidden, self.top_k

@@ -126,3 +126,13 @@ def test_ipc_argument_checks():
     assert L.gtm_ipc_close(None) == gtmoe.ERR_INVALID
     assert L.gtm_ipc_free(None) == gtmoe.ERR_INVALID
     assert C.sizeof(gtmoe.EpPeers) == 8 * gtmoe.EP_PEER_MAX_WORLD
+
+
+def test_phase_events_argument_checks():
+    L = gtmoe.lib()
+    assert L.gtm_set_phase_events(None, 0) == gtmoe.OK   # off
+    assert L.gtm_set_phase_events(None, 3) == gtmoe.ERR_INVALID
+    arr = (C.c_void_p * 7)()
+    assert L.gtm_set_phase_events(arr, 7) == gtmoe.ERR_INVALID and "0..6" in gtmoe.last_error()
+    assert L.gtm_set_phase_events(arr, 2) == gtmoe.ERR_INVALID and "NULL" in gtmoe.last_error()
+    assert L.gtm_set_phase_events(None, 0) == gtmoe.OK

@@ -8,15 +8,20 @@ to the last bit) and against the CPU oracle on sampled tokens (top-8 bit-exact, 
 2e-3 x RMS). Configurations: BASELINE config 3 shape (bf16 tokens, uniform routing logits) at
 P = 2, 4, 8, and config 2 (router GEMV, Zipf logit bias) at P = 2.
 """
+import os
+import sys
+
 import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 import gtmoe  # noqa: E402
 from gtmoe import ep, workloads  # noqa: E402
 import oracle  # noqa: E402
+from block_f64 import block_f64, rel_err_per_token  # noqa: E402
 
 D, E, K = gtmoe.HIDDEN, gtmoe.EXPERTS, gtmoe.TOP_K
 TOL = 2e-3
@@ -124,16 +129,21 @@ def make_peer_ops(P, max_tokens):
     return shards, ops
 
 
-def run_peer(ops, xs, route_logits=None, logit_bias=None, h2=None):
-    """h2: list that receives the routed sums (combine input) of all ranks' tokens."""
+def run_peer(ops, xs, route_logits=None, logit_bias=None, h2=None, extra=None):
+    """h2: list that receives the routed sums (combine input) of all ranks' tokens; extra: dict
+    that receives h1, h2 and the routing weights of all ranks' tokens."""
     P = len(ops)
     outs = [torch.empty(x.shape[0], D, device="cuda") for x in xs]
     idx = [torch.empty(x.shape[0], K, dtype=torch.int32, device="cuda") for x in xs]
     h2s = [torch.empty(x.shape[0], D, device="cuda") for x in xs]
+    h1s = [torch.empty(x.shape[0], D, device="cuda") for x in xs]
+    ws = [torch.empty(x.shape[0], K, device="cuda") for x in xs]
     kw, off = [], 0
     for r in range(P):
         n = xs[r].shape[0]
-        d = {"topk_idx": idx[r], "h2": h2s[r] if h2 is not None else None}
+        d = {"topk_idx": idx[r], "h2": h2s[r] if (h2 is not None or extra is not None) else None}
+        if extra is not None:
+            d["h1"], d["topk_w"] = h1s[r], ws[r]
         if route_logits is not None:
             d["route_logits"] = route_logits[off:off + n]
         if logit_bias is not None:
@@ -146,6 +156,8 @@ def run_peer(ops, xs, route_logits=None, logit_bias=None, h2=None):
     torch.cuda.synchronize()
     if h2 is not None:
         h2.append(torch.cat(h2s).cpu().numpy())
+    if extra is not None:
+        extra.update(h1=torch.cat(h1s), h2=torch.cat(h2s), w=torch.cat(ws))
     return torch.cat(outs).cpu().numpy(), torch.cat(idx).cpu().numpy().view(np.uint32)
 
 
@@ -210,3 +222,34 @@ def test_ep_peer_ragged_ranks_and_stale_entries(full_model, ref_layer):
         ref = ref_layer.block(xs[t], logit_bias=b)
         assert np.array_equal(gidx[t], ref["idx"])
         assert rel_max(got[t], ref["hidden"]) <= TOL
+
+
+def test_ep_peer_eight_ranks_every_token_config3(full_model):
+    """BASELINE config 3 at emulated P = 8 (4096 bf16 tokens, 512 per rank, 16 experts per rank):
+    every token's top-8 against the oracle's selection, and h1, h2 and the new residual of every
+    token against the float64 whole-batch restatement (tests/block_f64.py) fed the device's
+    routing."""
+    P, T = 8, 4096
+    x32 = torch.empty(T * D, device="cuda")
+    gtmoe.synth_x(0, 0, T, x32)
+    x = x32.view(T, D).to(torch.bfloat16)
+    rl_np = workloads.uniform_route_logits(T)
+    rl = torch.from_numpy(rl_np).cuda()
+    _, ops = make_peer_ops(P, T // P)
+    ex = {}
+    try:
+        got, gidx = run_peer(ops, list(x.split(T // P)), route_logits=rl, extra=ex)
+    finally:
+        for o in ops:
+            o.close()
+    res = full_model.resident[0].cpu().numpy()
+    o = full_model.layers[0].per_expert_scale
+    pes = res[o:o + 2 * E].view(np.uint16)
+    for t in range(T):
+        idx, _ = oracle.topk(rl_np[t], K, pes)
+        assert np.array_equal(gidx[t], idx), f"token {t}"
+    ref = block_f64(full_model.layers[0], full_model.resident[0], full_model.experts[0], x.float(),
+                    torch.from_numpy(gidx.astype(np.int64)), ex["w"])
+    for k, v in (("h1", ex["h1"]), ("h2", ex["h2"]), ("hidden", torch.from_numpy(got))):
+        e = rel_err_per_token(v, ref[k])
+        assert float(e.max()) <= TOL, f"{k}: token {int(e.argmax())} at {float(e.max()):.3e}"

@@ -5,18 +5,24 @@ logits bit-identical when the router GEMV runs), routing weights within 1e-5 rel
 h2 and the new residual within max|y - ref| <= 2e-3 * RMS(ref) per token.
 
 Configurations: BASELINE config 2 (64 tokens, Zipf(1.1) logit bias), config 3 (4096 bf16 tokens,
-uniform-random routing logits; indices checked on every token, the full block on a sample), and
-ragged token counts around the 128-row tile edges.
+uniform-random routing logits; indices checked on every token against the oracle, h1, h2 and the
+new residual of every token against the float64 whole-batch restatement tests/block_f64.py, and
+the exact oracle on a sample), and ragged token counts around the 128-row tile edges.
 """
+import os
+import sys
+
 import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 import gtmoe  # noqa: E402
 from gtmoe import workloads  # noqa: E402
 import oracle  # noqa: E402
+from block_f64 import block_f64, rel_err_per_token  # noqa: E402
 
 D, E, K = gtmoe.HIDDEN, gtmoe.EXPERTS, gtmoe.TOP_K
 TOL = 2e-3
@@ -110,10 +116,18 @@ def test_config3_prefill_4096_bf16(model, ref_layer, block):
     sample = sorted(set(rng.choice(T, 12, replace=False).tolist()) | {0, T - 1})
     for t in sample:
         check_token(ref_layer, got, t, xs[t], route_logits=rl[t], exact_logits=False)
-    # full-size property: the routed sum h2 equals sum_k w_k * out_k, so its RMS norm over all
-    # tokens is finite and every token has distinct experts
     assert np.isfinite(got["hidden"]).all()
     assert all(len(set(got["idx"][t].tolist())) == K for t in range(T))
+    # every token: h1, h2 and the residual against the float64 restatement fed the device's routing
+    ref = block_f64(model.layers[0], model.resident[0], model.experts[0], x.float(),
+                    torch.from_numpy(got["idx"].astype(np.int64)), torch.from_numpy(got["w"]))
+    worst = {}
+    for k in ("h1", "h2", "hidden"):
+        e = rel_err_per_token(torch.from_numpy(got[k]), ref[k])
+        worst[k] = (float(e.max()), int(e.argmax()))
+        assert worst[k][0] <= TOL, f"{k}: token {worst[k][1]} at {worst[k][0]:.3e}"
+    print(f"\nconfig 3, all {T} tokens, max err / RMS vs float64: " +
+          ", ".join(f"{k} {v[0]:.2e} (token {v[1]})" for k, v in worst.items()))
 
 
 def test_config3_topk_all_tokens_match_oracle(model, block):

@@ -327,6 +327,12 @@ GTM_API int gtm_moe_tokens_check(void* ws, void* stream) {
     return rc;
 }
 
+GTM_API int gtm_set_phase_events(void* const* events, int n) {
+    const int rc = set_phase_events(events, n);
+    if (rc == GTM_OK) clear_error();
+    return rc;
+}
+
 // ---- tied LM head, greedy --------------------------------------------------------------------------
 static int sm_count(const char* fn, int* sms);
 

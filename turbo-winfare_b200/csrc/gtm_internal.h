@@ -27,6 +27,7 @@ size_t tokens_workspace_bytes(uint32_t max_tokens);
 int launch_tokens(const GtmDims& dims, const GtmLayer& layer, const GtmTokensIO& io, void* ws, size_t ws_bytes,
                   cudaStream_t stream, int num_sms);
 int tokens_check(void* ws, cudaStream_t stream);
+int set_phase_events(void* const* events, int n);
 size_t ep_workspace_bytes(uint32_t max_tokens, uint32_t max_recv);
 int launch_ep_dispatch(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io, const GtmEpConfig& ep,
                        float* send_rows, GtmEpMeta* send_meta, int32_t* send_counts, void* ws, cudaStream_t st);

@@ -1329,6 +1329,13 @@ struct Plan {
     int* nrows;                   // rows routed to this rank (written by the routing scan)
 };
 
+// Stage events of gtm_set_phase_events (thread-local: each host thread times its own calls).
+thread_local cudaEvent_t t_phase_ev[GTM_PHASE_EVENTS];
+thread_local int t_phase_n = 0;
+inline void mark_phase(int i, cudaStream_t st) {
+    if (i < t_phase_n) cudaEventRecord(t_phase_ev[i], st);
+}
+
 int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaStream_t st) {
     const WsLayout& W = w.W;
     const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
@@ -1365,6 +1372,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     ra.nsrc = pl.nsrc; ra.per_src = pl.per_src;
     for (int s = 0; s < pl.nsrc; ++s) { ra.src_idx[s] = pl.src_idx[s]; ra.src_ntok[s] = pl.src_ntok[s]; }
     ra.nrows = pl.nrows;
+    mark_phase(1, st);
     if (ra.nchunks > 0) tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
     tok_route_scan<<<1, 1024, 0, st>>>(ra);
     if (ra.nchunks > 0) tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
@@ -1391,6 +1399,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     g0.act_s_hi = w.p<__half>(W.act_s_hi); g0.act_s_lo = w.p<__half>(W.act_s_lo);
     g0.act_src = pl.act_src; g0.act_row = ra.perm_src; g0.act_div = pl.act_div > 0 ? pl.act_div : 1;
     g0.err = w.p<int>(0);
+    mark_phase(2, st);
     grouped_gemm<0><<<num_sms, THREADS, SMEM_BYTES, st>>>(g0);
 
     g1.tiles = ra.tiles1; g1.n_tiles = ra.n_tiles + 1;
@@ -1403,6 +1412,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     g1.per_src = pl.nsrc > 0 ? pl.per_src : 0;
     for (int s = 0; s < pl.nsrc; ++s) g1.out_peer[s] = pl.src_ret[s];
     g1.err = w.p<int>(0);
+    mark_phase(3, st);
     grouped_gemm<1><<<num_sms, THREADS, SMEM_BYTES, st>>>(g1);
     return GTM_OK;
 }
@@ -1434,6 +1444,7 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     const uint32_t T = io.num_tokens;
     const Ws w{ws_layout(T, T * TOPK, WS_SINGLE), static_cast<uint8_t*>(ws)};
     if (ws_bytes < w.W.total) return set_error(GTM_ERR_WORKSPACE, "gtm_moe_tokens: workspace needs %zu bytes", w.W.total);
+    mark_phase(0, st);
     launch_views(dims, L, io, w, st);
     Plan pl;
     memset(&pl, 0, sizeof(pl));
@@ -1442,7 +1453,9 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     pl.out_r = w.p<float>(w.W.out_r);
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
+    mark_phase(4, st);
     launch_combine(dims, L, io, w, w.p<int>(w.W.pos), pl.out_r, st);
+    mark_phase(5, st);
     return finish("gtm_moe_tokens", &io, &w, st);
 }
 
@@ -1553,6 +1566,17 @@ int launch_ep_peer_combine(const GtmDims& dims, const GtmLayer& L, const GtmToke
     const Ws w = peer_ws(ep, ws);
     launch_combine(dims, L, io, w, nullptr, w.p<float>(w.W.ret), st);
     return finish("gtm_moe_ep_peer_combine", nullptr, nullptr, st);
+}
+
+int set_phase_events(void* const* events, int n) {
+    if (n < 0 || n > GTM_PHASE_EVENTS || (n > 0 && !events))
+        return set_error(GTM_ERR_INVALID, "gtm_set_phase_events: n=%d (0..%d) and events needed", n, GTM_PHASE_EVENTS);
+    for (int i = 0; i < n; ++i) {
+        if (!events[i]) return set_error(GTM_ERR_INVALID, "gtm_set_phase_events: event %d is NULL", i);
+        t_phase_ev[i] = static_cast<cudaEvent_t>(events[i]);
+    }
+    t_phase_n = n;
+    return GTM_OK;
 }
 
 int tokens_check(void* ws, cudaStream_t st) {

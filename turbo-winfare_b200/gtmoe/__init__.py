@@ -135,6 +135,7 @@ SIGNATURES = {
     "gtm_moe_tokens_workspace_bytes": (_SZ, [C.POINTER(Dims), _U32]),
     "gtm_moe_tokens": (_I, [C.POINTER(Dims), C.POINTER(Layer), C.POINTER(TokensIO), _P, _SZ, _P]),
     "gtm_moe_tokens_check": (_I, [_P, _P]),
+    "gtm_set_phase_events": (_I, [C.POINTER(_P), _I]),
     "gtm_lm_head_workspace_bytes": (_SZ, [_U32]),
     "gtm_lm_head_greedy": (_I, [_U32, _U32, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "gtm_lm_head_candidates": (_I, [_P, _P, C.POINTER(C.c_int32)]),
@@ -405,6 +406,18 @@ class TokenBlock:
     def check(self, stream=None):
         check(lib().gtm_moe_tokens_check(self.ws_ptr, _stream(stream)))
 
+
+
+PHASE_EVENTS = 6
+PHASE_NAMES = ("views_router", "routing", "gemm_gate_up", "gemm_down", "combine")
+
+
+def set_phase_events(events) -> None:
+    """Stage timing of this thread's next gtm_moe_tokens calls (gtm_set_phase_events): `events`
+    are up to PHASE_EVENTS torch.cuda.Event(enable_timing=True) objects, recorded once on the
+    current stream first so their handles exist; an empty list turns it off."""
+    arr = (C.c_void_p * max(1, len(events)))(*[e.cuda_event for e in events])
+    check(lib().gtm_set_phase_events(arr, len(events)))
 
 
 def decode_noalloc(layers, hidden_in, hidden_out, *, num_layers: int | None = None, first_layer: int = 0,
