@@ -9,7 +9,9 @@
  * KV rows live where KVCacheManager puts them (src/kv_cache.cpp:36-50): position p of a layer
  * in row p % capacity, each row kv_heads * head_dim floats.
  *
- * These device entries have not yet been run on a B200.
+ * Checked on a B200 against the reference's kernel-test known answers (EmbedLookup bit-identical,
+ * QKVEpilogue and Attention with window and ring wrap within its allclose rule) and, chained with
+ * the MoE block and the greedy LM head, against the reference's own generate tokens.
  */
 #ifndef GTMOE_ATTENTION_H
 #define GTMOE_ATTENTION_H

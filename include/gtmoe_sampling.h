@@ -16,8 +16,9 @@
  * compares two doubles that agree to ~1e-10 relative: the reference sums exp() of the whole
  * vocabulary in order on the host, the device in parallel, and CUDA's double exp() may differ
  * from the C library's in the last bit. The status word reports every decision whose margin lies
- * inside that bound. The device entries have not yet been run on a B200; the host-side rules
- * (validate, splitmix64, seed_for) are checked against the reference's compiled code.
+ * inside that bound. The device entries are checked on a B200 against the reference's compiled
+ * sampling.cpp outputs (tokens and penalised logits bit-identical, no draw flagged); the
+ * host-side rules (validate, splitmix64, seed_for) against the same code on the CPU.
  */
 #ifndef GTMOE_SAMPLING_H
 #define GTMOE_SAMPLING_H

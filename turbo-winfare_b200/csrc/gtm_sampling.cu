@@ -308,6 +308,13 @@ __global__ void smp_penalty_apply(float* __restrict__ logits, const uint32_t* __
     const uint32_t c = atomicExch(cnt + id, 0u);
     if (c == 0) return;
     float v = logits[id];
+    if (v != v) {
+        // NaN: the reference's `v * penalty` on the host returns the NaN operand quieted (x86 SSE
+        // propagates its payload) and its clamp keeps it; the device multiply would return the
+        // canonical NaN instead
+        logits[id] = __uint_as_float(__float_as_uint(v) | 0x00400000u);
+        return;
+    }
     for (uint32_t j = 0; j < c; ++j) {
         v = v > 0.0f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty);
         if (limit > 0.0f) v = v < -limit ? -limit : (limit < v ? limit : v);

@@ -1,7 +1,6 @@
 """Batch-1 decode around the MoE block through libgtmoe (include/gtmoe_attention.h): the
 reference's EmbedLookup, QKVEpilogue and Attention steps on device tensors, with the KV cache in
 the reference's ring layout (position p in row p % capacity, kv_heads * head_dim floats a row).
-The device entries have not yet been run on a B200.
 """
 from __future__ import annotations
 
