@@ -167,7 +167,12 @@ typedef struct GtmDims {
 } GtmDims;
 
 enum {
-    GTM_DECODE_NORM_BETWEEN_LAYERS = 1   /* weightless RMSNorm on the residual after every layer but the last */
+    GTM_DECODE_NORM_BETWEEN_LAYERS = 1,  /* weightless RMSNorm on the residual after every layer but the last */
+    /* Test hook for the bounded device-side waits: the launch's first grid-barrier wait waits for
+     * an epoch no CTA arrives with, under a 2 ms limit instead of 2 s, so every CTA gives up,
+     * records GTM_ERR_TIMEOUT (read by gtm_moe_decode_check) and returns; outputs are not
+     * written. The workspace stays usable for the next launch. */
+    GTM_DECODE_TEST_WAIT_RUNS_OUT = 0x100
 };
 
 typedef struct GtmDecodeIO {

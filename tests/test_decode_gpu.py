@@ -130,3 +130,26 @@ def test_config1_thirty_layer_stack():
     free = oracle.synth_stack(layers, x0)
     assert rel_max(g["hidden"], free["hidden"]) <= TOL
     assert np.array_equal(g["idx"], free["idx"])
+
+
+def test_bounded_wait_runs_out_then_workspace_recovers(model1):
+    """A grid-barrier wait that can never be satisfied (GTM_DECODE_TEST_WAIT_RUNS_OUT: the first
+    wait's epoch is one no CTA arrives with, under a 2 ms limit) ends in GTM_ERR_TIMEOUT read back
+    by gtm_moe_decode_check, with the context usable; the next launch on the same workspace is
+    exact again."""
+    import time
+    dec = gtmoe.Decoder(model1.layers, 1)
+    x = torch.from_numpy(oracle.synth_x(0, 3)).cuda()
+    out = torch.empty(D, device="cuda")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    dec(x, out, num_layers=1, norm_between_layers=False, extra_flags=gtmoe.DECODE_TEST_WAIT_RUNS_OUT)
+    with pytest.raises(gtmoe.GtmError) as e:
+        dec.check()
+    assert e.value.status == gtmoe.ERR_TIMEOUT and "timed out" in str(e.value)
+    assert time.perf_counter() - t0 < 1.0
+    dec.check()   # the sticky word was cleared by the failing check
+    g = run(dec, x, 1, norm_between_layers=False)
+    want = oracle.SynthLayer(0, 0).block(oracle.synth_x(0, 3))
+    assert np.array_equal(g["idx"][0], want["idx"])
+    assert rel_max(g["hidden"], want["hidden"]) <= TOL

@@ -273,3 +273,56 @@ def test_ep_peer_protocol_two_gloo_ranks(tmp_path):
         assert p.exitcode == 0
     for r in range(world):
         assert max(out[r]) < 1e-5, out[r]
+
+
+def leave_worker(rank, world, port, q):
+    """Both ranks run one layer; then rank 1 leaves (the process ends without a word to the group)
+    and rank 0 starts the next layer, whose first exchange must fail within the group's timeout."""
+    import time
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+        xch = ep.NcclExchange()
+        x = np.random.default_rng(300 + rank).standard_normal((4, D)).astype(np.float32)
+        ops = StandInOps(rank, world, np.zeros(E, np.float32))
+        out = torch.zeros(4, D)
+        ep.ep_layer(ops, xch, torch.from_numpy(x), out)
+        err = float(np.abs(out.numpy() - expected(x, np.zeros(E, np.float32))).max())
+        if rank == 1:
+            q.put((rank, err, None, 0.0))
+            q.close()
+            q.join_thread()   # the message is sent before the process ends abruptly
+            os._exit(0)
+        time.sleep(0.5)   # the peer is gone before the next step starts
+        t0 = time.perf_counter()
+        try:
+            ep.ep_layer(ops, xch, torch.from_numpy(x), out)
+            q.put((rank, err, "second layer completed without its peer", time.perf_counter() - t0))
+        except Exception as e:   # the expected outcome
+            q.put((rank, err, "raised: " + type(e).__name__, time.perf_counter() - t0))
+    except Exception as e:
+        q.put((rank, None, "setup: " + repr(e), 0.0))
+
+
+def test_ep_rank_leaving_between_steps_is_reported():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=leave_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        rank, err, msg, dt = q.get(timeout=120)
+        got[rank] = (err, msg, dt)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert got[1][0] is not None and got[1][0] < 1e-5          # the first layer was right on both
+    assert got[0][0] is not None and got[0][0] < 1e-5
+    assert got[0][1].startswith("raised"), got[0]              # the survivor learned of it ...
+    assert got[0][2] < 30.0, got[0]                            # ... within a bounded time

@@ -26,6 +26,7 @@ LIB_PATH = os.path.join(PKG, "libgtmoe.so")
 HIDDEN, MOE_INTER, FFN, EXPERTS, TOP_K, EPS = 2816, 704, 2112, 128, 8, 1e-6
 MAX_LAYERS = 64
 NORM_BETWEEN_LAYERS = 1
+DECODE_TEST_WAIT_RUNS_OUT = 0x100   # GTM_DECODE_TEST_WAIT_RUNS_OUT (include/gtmoe.h)
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE, ERR_MISALIGNED = 0, -1, -2, -3, -4, -5, -6
 
@@ -362,11 +363,12 @@ class Decoder:
 
     def __call__(self, hidden_in, hidden_out, *, topk_idx=None, topk_w=None, logits=None, h1=None, h2=None,
                  hidden_layers=None, logit_bias=None, norm_between_layers=True, stream=None, first_layer: int = 0,
-                 num_layers: int | None = None):
+                 num_layers: int | None = None, extra_flags: int = 0):
         n = num_layers if num_layers is not None else self.num_layers
         layer_arr = C.cast(C.addressof(self.layers) + first_layer * C.sizeof(Layer), C.POINTER(Layer))
         io = DecodeIO(hidden_in.data_ptr(), hidden_out.data_ptr(), ptr(topk_idx), ptr(topk_w), ptr(logits), ptr(h1),
-                      ptr(h2), ptr(hidden_layers), ptr(logit_bias), NORM_BETWEEN_LAYERS if norm_between_layers else 0)
+                      ptr(h2), ptr(hidden_layers), ptr(logit_bias),
+                      (NORM_BETWEEN_LAYERS if norm_between_layers else 0) | extra_flags)
         check(lib().gtm_moe_decode(C.byref(self.dims), layer_arr, n, C.byref(io), self.ws_ptr, self.ws_bytes,
                                    _stream(stream)))
 
