@@ -37,6 +37,14 @@ GTM_API int gtm_synth_resident(uint64_t seed, uint32_t layer, uint32_t hidden, u
                                void* dst_dev, void* stream);
 /* Block inputs x ~ N(0,1) for tokens [token0, token0 + count): fp32 [count][hidden]. */
 GTM_API int gtm_synth_x(uint64_t seed, uint32_t token0, uint32_t count, uint32_t hidden, float* dst_dev, void* stream);
+/* A synthetic int4 matrix outside the MoE block (attention projections, tied embedding of the
+ * decoder benchmark): packed words [rows][in_dim/8], bf16 scales and biases [rows][in_dim/64]
+ * drawn like the expert matrices (q ~ U{0..15}, scale |N(0, 0.02)|, bias -8 scale) from the
+ * streams (seed, layer, kind_w) and (seed, layer, kind_s); callers use kinds >= 32. */
+GTM_API int gtm_synth_quant(uint64_t seed, uint32_t layer, uint32_t kind_w, uint32_t kind_s, uint32_t rows,
+                            uint32_t in_dim, void* w_dev, uint16_t* s_dev, uint16_t* b_dev, void* stream);
+/* A synthetic bf16 norm vector of n elements (1 + N(0, 0.1), like the MoE norm weights). */
+GTM_API int gtm_synth_norm(uint64_t seed, uint32_t layer, uint32_t kind, uint32_t n, uint16_t* dst_dev, void* stream);
 /* Fills a GtmLayer for a synthetic layer whose resident image and expert image live at the
  * given device addresses. */
 GTM_API int gtm_synth_layer_desc(uint32_t hidden, uint32_t moe_inter, uint32_t ffn, uint32_t experts,

@@ -19,12 +19,13 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROOT, "tests", "golden")]
 
 import oracle  # noqa: E402
-from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_SAMPLING, DECODER_STOPS  # noqa: E402
+from make_golden import (BATCH_CASE, BATCH_NEW_TOKENS, DECODER_CASES, DECODER_NEW_TOKENS,  # noqa: E402
+                         DECODER_SAMPLING, DECODER_STOPS)
 
 pytestmark = pytest.mark.gpu
 
 
-def device_decoder(args, prompts):
+def device_decoder(args, prompts, batch: bool = False, new_tokens: int = DECODER_NEW_TOKENS):
     import torch
     import gtmoe
     from gtmoe.decoder import AttnLayerWeights, DeviceDecoder
@@ -48,7 +49,11 @@ def device_decoder(args, prompts):
                                        s.num_heads, s.kv_heads, s.head_dim, s.rotated_pairs, s.theta,
                                        0 if full else s.sliding_window))
     moe = gtmoe.SynthModel(dec.num_layers, seed=args["seed"])
-    max_pos = max(len(p) for p in prompts) + DECODER_NEW_TOKENS + 1
+    max_pos = max(len(p) for p in prompts) + new_tokens + 1
+    if batch:
+        from gtmoe.batch import BatchDecoder, LocalMoe
+        return BatchDecoder(layers, LocalMoe(moe.layers, len(prompts)), quant(dec.embed_w), bf16(dec.final_norm),
+                            max_pos, len(prompts)), moe
     return DeviceDecoder(layers, moe.layers, quant(dec.embed_w), bf16(dec.final_norm), max_pos), moe
 
 
@@ -71,3 +76,25 @@ def test_sampled_tokens_match_reference():
         for i, p in enumerate(prompts):
             assert dd.sample(p, DECODER_NEW_TOKENS, sp, DECODER_STOPS) == g[f"d3.sampled{j}.prompt{i}.tokens"].tolist(), \
                 (j, i)
+
+
+def test_batched_greedy_64_tokens_match_reference():
+    """BASELINE config 4's bar in miniature: four sequences of different prompt lengths decoded
+    together (gtmoe.batch.BatchDecoder: attention per sequence, one gtm_moe_tokens call per layer
+    for all the step's tokens, the greedy LM head per sequence); every sequence's 64 greedy ids
+    equal the reference's own CpuReference::generate ids (tests/golden/batch_decode.npz)."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "batch_decode.npz"))
+    args, prompts = BATCH_CASE
+    bd, _moe = device_decoder(args, prompts, batch=True, new_tokens=BATCH_NEW_TOKENS)
+    got = bd.greedy(prompts, BATCH_NEW_TOKENS, DECODER_STOPS)
+    for i in range(len(prompts)):
+        assert got[i] == g[f"b4.prompt{i}.tokens"].tolist(), i
+
+
+def test_single_sequence_64_tokens_match_reference():
+    """The same bar through the single-sequence DeviceDecoder (the fused batch-1 decode per layer):
+    sequence 0 of the batch case, 64 greedy ids."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "batch_decode.npz"))
+    args, prompts = BATCH_CASE
+    dd, _moe = device_decoder(args, prompts, new_tokens=BATCH_NEW_TOKENS)
+    assert dd.greedy(prompts[0], BATCH_NEW_TOKENS, DECODER_STOPS) == g["b4.prompt0.tokens"].tolist()

@@ -22,7 +22,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [ROOT, os.path.join(ROOT, "turbo-winfare_b200"), os.path.join(ROOT, "tests", "golden")]
 
 import oracle  # noqa: E402
-from make_golden import DECODER_CASES, DECODER_NEW_TOKENS, DECODER_SAMPLING, DECODER_STOPS  # noqa: E402
+from make_golden import (BATCH_CASE, BATCH_NEW_TOKENS, DECODER_CASES, DECODER_NEW_TOKENS,  # noqa: E402
+                         DECODER_SAMPLING, DECODER_STOPS)
 
 
 def addr(p) -> int:
@@ -123,6 +124,24 @@ class OracleLib:
         view(o.hidden_out_dev, oracle.HIDDEN, np.float32)[:] = self.synth[layer].block(x)["hidden"]
         return 0
 
+    def _gtm_moe_tokens_workspace_bytes(self, dims, n):
+        return 256
+
+    def _gtm_moe_tokens_check(self, ws, st):
+        return 0
+
+    def _gtm_moe_tokens(self, dims, layer, io, ws, wsb, st):
+        import gtmoe
+        layer = (addr(layer) - self.moe_base) // C.sizeof(gtmoe.Layer)
+        o = io._obj
+        assert o.x_dev and not o.x_bf16_dev
+        D = oracle.HIDDEN
+        xs = view(o.x_dev, o.num_tokens * D, np.float32).copy().reshape(o.num_tokens, D)
+        out = view(o.hidden_out_dev, o.num_tokens * D, np.float32).reshape(o.num_tokens, D)
+        for t in range(o.num_tokens):
+            out[t] = self.synth[layer].block(xs[t])["hidden"]
+        return 0
+
     def _gtm_lm_head_greedy(self, rows, in_dim, w, s, b, x, token, logit, ws, wsb, st):
         g = in_dim // 64
         lg = oracle.matvec(view(w, rows * in_dim // 2, np.uint8), view(s, rows * g, np.uint16),
@@ -157,8 +176,8 @@ def host_decoder(monkeypatch):
     from gtmoe import attention, decoder, sampling
     from gtmoe.decoder import AttnLayerWeights, DeviceDecoder
 
-    def make(case):
-        args, prompts = DECODER_CASES[case]
+    def make(case, batch=False):
+        args, prompts = BATCH_CASE if case == "b4" else DECODER_CASES[case]
         dec = oracle.SynthDecoder(**args)
         moe_layers = (gtmoe.Layer * dec.num_layers)()
         fake = OracleLib(gtmoe.lib(), moe_layers, dec.moe)
@@ -184,6 +203,14 @@ def host_decoder(monkeypatch):
                                            bf16(dec.post_attn[l]), s.num_heads, s.kv_heads, s.head_dim,
                                            s.rotated_pairs, s.theta, 0 if full else s.sliding_window))
         max_pos = max(len(p) for p in prompts) + DECODER_NEW_TOKENS + 1
+        if batch:
+            from gtmoe import batch as gbatch
+            monkeypatch.setattr(gbatch, "lib", lambda: fake)
+            monkeypatch.setattr(gbatch, "_stream", lambda stream=None: None)
+            max_pos = max(len(p) for p in prompts) + BATCH_NEW_TOKENS + 1
+            moe = gbatch.LocalMoe(moe_layers, len(prompts), device="cpu")
+            return gbatch.BatchDecoder(layers, moe, quant(dec.embed_w), bf16(dec.final_norm), max_pos, len(prompts),
+                                       device="cpu"), prompts
         dd = DeviceDecoder(layers, moe_layers, quant(dec.embed_w), bf16(dec.final_norm), max_pos, device="cpu")
         return dd, prompts
     return make
@@ -217,3 +244,15 @@ def test_empty_prompt_raises_as_reference(host_decoder):
         dd.greedy([], DECODER_NEW_TOKENS, DECODER_STOPS)
     with pytest.raises(ValueError, match="empty prompt"):
         dd.sample([], DECODER_NEW_TOKENS, SamplingParams(1.0, 1.0, 8, 1.0, True, 3), DECODER_STOPS)
+
+
+def test_batch_sequencing_reproduces_reference(host_decoder):
+    """gtmoe.batch.BatchDecoder's lockstep over sequences of different prompt lengths (prefill
+    token by token, the first greedy token after the last prompt token, 64 tokens each) with the
+    oracle behind every entry: each sequence's tokens equal the reference's own generate tokens
+    (tests/golden/batch_decode.npz)."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "batch_decode.npz"))
+    bd, prompts = host_decoder("b4", batch=True)
+    got = bd.greedy(prompts, BATCH_NEW_TOKENS, DECODER_STOPS)
+    for i in range(len(prompts)):
+        assert got[i] == g[f"b4.prompt{i}.tokens"].tolist(), i

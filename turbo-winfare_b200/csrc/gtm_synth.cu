@@ -30,6 +30,20 @@ __global__ void synth_quant_kernel(uint64_t seed, uint32_t layer, uint32_t kind_
     }
 }
 
+// A standalone int4 matrix (zero point 8) into three separate arrays.
+__global__ void synth_matrix_kernel(uint64_t seed, uint32_t layer, uint32_t kind_w, uint32_t kind_s, uint32_t* w,
+                                    uint16_t* s, uint16_t* b, uint64_t words, uint64_t nscale) {
+    const uint64_t sw = gtm_stream(seed, layer, kind_w, 0);
+    const uint64_t ss = gtm_stream(seed, layer, kind_s, 0);
+    const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += step) w[i] = gtm_qword(sw, i);
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nscale; i += step) {
+        const uint16_t sc = gtm_scale_bits(ss, i);
+        s[i] = sc;
+        b[i] = gtm_bias_bits(sc, 8.0f);
+    }
+}
+
 __global__ void synth_zero_kernel(uint8_t* base, uint64_t stride, uint64_t from, uint64_t to) {
     uint8_t* blk = base + (uint64_t)blockIdx.y * stride;
     for (uint64_t i = from + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < to; i += (uint64_t)gridDim.x * blockDim.x)
@@ -142,6 +156,29 @@ GTM_API int gtm_synth_x(uint64_t seed, uint32_t token0, uint32_t count, uint32_t
     synth_x_kernel<<<dim3((hidden + 255) / 256, count), 256, 0, (cudaStream_t)stream>>>(seed, token0, hidden, dst);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("gtm_synth_x", e);
+    clear_error();
+    return GTM_OK;
+}
+
+GTM_API int gtm_synth_quant(uint64_t seed, uint32_t layer, uint32_t kind_w, uint32_t kind_s, uint32_t rows,
+                            uint32_t in_dim, void* w_dev, uint16_t* s_dev, uint16_t* b_dev, void* stream) {
+    if (!w_dev || !s_dev || !b_dev || rows == 0 || in_dim == 0 || in_dim % 64 != 0)
+        return set_error(GTM_ERR_INVALID, "gtm_synth_quant: null pointer or in_dim %u not a multiple of 64", in_dim);
+    synth_matrix_kernel<<<512, 256, 0, (cudaStream_t)stream>>>(seed, layer, kind_w, kind_s, static_cast<uint32_t*>(w_dev),
+                                                               s_dev, b_dev, (uint64_t)rows * in_dim / 8,
+                                                               (uint64_t)rows * (in_dim / 64));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("gtm_synth_quant", e);
+    clear_error();
+    return GTM_OK;
+}
+
+GTM_API int gtm_synth_norm(uint64_t seed, uint32_t layer, uint32_t kind, uint32_t n, uint16_t* dst_dev, void* stream) {
+    if (!dst_dev || n == 0) return set_error(GTM_ERR_INVALID, "gtm_synth_norm: null pointer or n = 0");
+    synth_vec_kernel<<<(n + 255) / 256 < 64 ? (n + 255) / 256 : 64, 256, 0, (cudaStream_t)stream>>>(seed, layer, kind, n,
+                                                                                                   0, dst_dev);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("gtm_synth_norm", e);
     clear_error();
     return GTM_OK;
 }

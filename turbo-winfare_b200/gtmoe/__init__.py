@@ -186,6 +186,8 @@ SIGNATURES = {
     "gtm_synth_resident": (_I, [_U64, _U32, _U32, _U32, _U32, _P, _P]),
     "gtm_synth_x": (_I, [_U64, _U32, _U32, _U32, _P, _P]),
     "gtm_synth_layer_desc": (_I, [_U32, _U32, _U32, _U32, _P, _P, C.POINTER(Layer)]),
+    "gtm_synth_quant": (_I, [_U64, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P]),
+    "gtm_synth_norm": (_I, [_U64, _U32, _U32, _U32, _P, _P]),
 }
 
 
