@@ -112,6 +112,21 @@ GTM_API int gtm_layer_tail(uint32_t d, const float* h2_dev, const float* h1_dev,
                            const uint16_t* w_pf2_dev, const uint16_t* w_pf_dev, float eps, float layer_scalar,
                            float* hidden_out_dev, void* stream);
 
+/* The same kernels over n vectors at once (a batched decode step; the reference dispatches one
+ * vector per call). Row i of each [n][...] array is vector i; every row's result is
+ * bit-identical to the single-vector entry on it. n <= 512. */
+/* GemvInt4 of x_dev row i ([n][in_dim]) into out_dev row i ([n][rows]). */
+GTM_API int gtm_gemv_q4_rows(uint32_t rows, uint32_t in_dim, uint32_t n, const void* w_dev, const uint16_t* s_dev,
+                             const uint16_t* b_dev, const float* x_dev, float* out_dev, void* stream);
+/* RMSNormK of each of `rows` vectors of n elements ([rows][n]). */
+GTM_API int gtm_rmsnorm_rows(uint32_t rows, uint32_t n, const float* x_dev, const uint16_t* w_dev, float eps,
+                             float* out_dev, void* stream);
+/* PostAttn of each of `rows` vectors of d elements; the three views may be NULL (not written). */
+GTM_API int gtm_post_attn_rows(uint32_t rows, uint32_t d, const float* attn_dev, const float* hidden_dev,
+                               const uint16_t* w_post_dev, const uint16_t* w_pre_dev, const uint16_t* w_pre2_dev,
+                               float eps, float* hidden_out_dev, float* dense_x_dev, float* routed_x_dev,
+                               float* router_x_dev, void* stream);
+
 /* Kernel ids for gtm_dispatch, in the order of gturbo::KernelType (include/gturbo/pipeline.hpp:17-33). */
 typedef enum gtm_kernel {
     GTM_KERNEL_RMSNORMK = 1, GTM_KERNEL_GEMV_INT4 = 2, GTM_KERNEL_GEMV_INT8 = 3,

@@ -48,6 +48,37 @@ GTM_API int gtm_attention_decode(uint32_t q_heads, uint32_t kv_heads, uint32_t h
                                  const float* v_cache_dev, float* ctx_dev, void* workspace_dev, size_t workspace_bytes,
                                  void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * The same steps for n sequences at once (a batched decode step; the reference decodes one
+ * sequence per produce_token call, runner.cpp:487-533). Row i of every [n][...] array belongs to
+ * the i-th sequence of the step; per-row token ids, positions and sequence indices are HOST
+ * arrays of n values (n <= 512), checked on the host and passed to the kernels by value. Every
+ * row's result is bit-identical to the single-sequence entry on that row.
+ * ------------------------------------------------------------------------------------- */
+/* EmbedLookup of tokens[i] into out_dev row i ([n][in_dim]). */
+GTM_API int gtm_embed_lookup_rows(uint32_t rows, uint32_t in_dim, const void* w_dev, const uint16_t* s_dev,
+                                  const uint16_t* b_dev, const uint32_t* tokens, uint32_t n, float scale, float* out_dev,
+                                  void* stream);
+/* QKVEpilogue of in_dev row i ([n][heads * head_dim]) at positions[i]. capacity = 0: into out_dev
+ * row i (out may be in). capacity > 0: into ring row positions[i] % capacity of the cache of
+ * sequence seqs[i] < num_seqs, the caches laid out [num_seqs][capacity][heads * head_dim]. */
+GTM_API int gtm_qkv_epilogue_rows(uint32_t heads, uint32_t head_dim, uint32_t n, const float* in_dev,
+                                  const uint16_t* w_dev, float eps, uint32_t rotated_pairs, const uint32_t* positions,
+                                  float theta, float* out_dev, const uint32_t* seqs, uint32_t num_seqs,
+                                  uint32_t capacity, void* stream);
+/* Workspace of gtm_attention_decode_rows for n rows attending at most max_window positions. */
+GTM_API size_t gtm_attention_rows_workspace_bytes(uint32_t q_heads, uint32_t head_dim, uint32_t max_window,
+                                                  uint32_t n);
+/* Attention of q_dev row i ([n][q_heads * head_dim]) over the caches of sequence seqs[i]
+ * ([num_seqs][capacity][kv_heads * head_dim]) at position positions[i]: positions
+ * [first, positions[i]] with first = max(0, positions[i] + 1 - window) (window 0 = all), into
+ * ctx_dev row i. The attended span must fit the ring (<= capacity). */
+GTM_API int gtm_attention_decode_rows(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, uint32_t n,
+                                      uint32_t window, uint32_t capacity, const float* q_dev, const float* k_cache_dev,
+                                      const float* v_cache_dev, const uint32_t* seqs, uint32_t num_seqs,
+                                      const uint32_t* positions, float* ctx_dev, void* workspace_dev,
+                                      size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -115,3 +115,107 @@ def test_timing_sliding_window_layer():
     us = e0.elapsed_time(e1) * 10
     nbytes = 2 * window * kv_heads * hd * 4
     print(f"\nattention window {window}: {us:.1f} us per call, {nbytes / us / 1e3:.0f} GB/s of K/V")
+
+
+def test_rows_entries_bit_identical_to_single_rows():
+    """The batched-decode entries (gtm_*_rows) on 5 rows with ragged positions, ring wrap, a full
+    layer and windows whose chunk counts are not monotonic (37 and 38 positions at 8 kv heads):
+    every row equals the single-sequence entry on it, bit for bit."""
+    import ctypes as C
+    import torch
+    import gtmoe
+    from gtmoe import attention
+    L = gtmoe.lib()
+    g = torch.Generator(device="cpu").manual_seed(11)
+    D = gtmoe.HIDDEN
+
+    def u32(v):
+        return (C.c_uint32 * len(v))(*v)
+
+    def bits(t):
+        return t.cpu().numpy().view(np.uint32)
+
+    n = 5
+    # embedding rows
+    vocab = 300
+    w = torch.randint(0, 256, (vocab, D // 2), dtype=torch.uint8, generator=g).cuda()
+    s = (torch.rand(vocab, D // 64, generator=g) * 0.02).to(torch.bfloat16).view(torch.int16).cuda()
+    b = (-torch.rand(vocab, D // 64, generator=g) * 0.1).to(torch.bfloat16).view(torch.int16).cuda()
+    toks = [3, 299, 0, 150, 3]
+    out = torch.empty(n, D, device="cuda")
+    gtmoe.check(L.gtm_embed_lookup_rows(vocab, D, gtmoe.ptr(w), gtmoe.ptr(s), gtmoe.ptr(b), u32(toks), n, 53.0,
+                                        gtmoe.ptr(out), None))
+    for i, t in enumerate(toks):
+        one = torch.empty(D, device="cuda")
+        attention.embed_lookup(w, s, b, t, one, scale=53.0)
+        assert np.array_equal(bits(out[i]), bits(one)), i
+    assert L.gtm_embed_lookup_rows(vocab, D, gtmoe.ptr(w), gtmoe.ptr(s), gtmoe.ptr(b), u32([1, vocab]), 2, 1.0,
+                                   gtmoe.ptr(out), None) == gtmoe.ERR_INVALID
+
+    # rmsnorm, gemv, post_attn rows
+    x = torch.randn(n, D, generator=g).cuda()
+    nw = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16).view(torch.int16).cuda()
+    rn = torch.empty(n, D, device="cuda")
+    gtmoe.check(L.gtm_rmsnorm_rows(n, D, gtmoe.ptr(x), gtmoe.ptr(nw), 1e-6, gtmoe.ptr(rn), None))
+    rows_w = 512
+    wq = torch.randint(0, 256, (rows_w, D // 2), dtype=torch.uint8, generator=g).cuda()
+    gv = torch.empty(n, rows_w, device="cuda")
+    gtmoe.check(L.gtm_gemv_q4_rows(rows_w, D, n, gtmoe.ptr(wq), gtmoe.ptr(s), gtmoe.ptr(b), gtmoe.ptr(x), gtmoe.ptr(gv),
+                                   None))
+    att = torch.randn(n, D, generator=g).cuda()
+    hout = torch.empty(n, D, device="cuda")
+    gtmoe.check(L.gtm_post_attn_rows(n, D, gtmoe.ptr(att), gtmoe.ptr(x), gtmoe.ptr(nw), None, None, 1e-6,
+                                     gtmoe.ptr(hout), None, None, None, None))
+    for i in range(n):
+        one = torch.empty(D, device="cuda")
+        gtmoe.rmsnorm(x[i], nw, 1e-6, one)
+        assert np.array_equal(bits(rn[i]), bits(one)), i
+        og = torch.empty(rows_w, device="cuda")
+        gtmoe.gemv_q4(wq, s, b, x[i], og, rows_w, D)
+        assert np.array_equal(bits(gv[i]), bits(og)), i
+        views = [torch.empty(D, device="cuda") for _ in range(4)]
+        gtmoe.post_attn(att[i], x[i], nw, nw, nw, 1e-6, *views)
+        assert np.array_equal(bits(hout[i]), bits(views[0])), i
+
+    # epilogue and attention rows over per-sequence ring caches
+    for H, KV, hd, window, cap, pos in ((16, 8, 256, 64, 64, [0, 37, 36, 200, 63]),
+                                        (16, 2, 512, 0, 300, [0, 5, 299, 150, 37])):
+        S = 4
+        seqs = [2, 0, 3, 1, 2] if window else [0, 1, 2, 3, 3]
+        kw, qw = KV * hd, H * hd
+        kc = torch.randn(S, cap, kw, generator=g).cuda()
+        vc = torch.randn(S, cap, kw, generator=g).cuda()
+        q = torch.randn(n, qw, generator=g).cuda()
+        kin = torch.randn(n, kw, generator=g).cuda()
+        qn = (1 + 0.1 * torch.randn(hd, generator=g)).to(torch.bfloat16).view(torch.int16).cuda()
+        kc_single = kc.clone()
+        q_single = q.clone()
+        ws_n = L.gtm_attention_rows_workspace_bytes(H, hd, cap, n)
+        ws = torch.empty(ws_n // 4 + 64, device="cuda")
+        ctx = torch.empty(n, qw, device="cuda")
+        # q in place; K into the caches, one row per distinct (sequence, slot), as a decode step has
+        gtmoe.check(L.gtm_qkv_epilogue_rows(H, hd, n, gtmoe.ptr(q), gtmoe.ptr(qn), 1e-6, hd // 4, u32(pos), 1e4,
+                                            gtmoe.ptr(q), None, 0, 0, None))
+        uniq = [i for i in range(n) if (seqs[i], pos[i] % cap) not in
+                {(seqs[j], pos[j] % cap) for j in range(i)}]
+        m = len(uniq)
+        gtmoe.check(L.gtm_qkv_epilogue_rows(KV, hd, m, gtmoe.ptr(kin), gtmoe.ptr(qn), 1e-6, hd // 4,
+                                            u32([pos[i] for i in uniq]), 1e4, gtmoe.ptr(kc),
+                                            u32([seqs[i] for i in uniq]), S, cap, None))
+        gtmoe.check(L.gtm_attention_decode_rows(H, KV, hd, n, window, cap, gtmoe.ptr(q), gtmoe.ptr(kc), gtmoe.ptr(vc),
+                                                u32(seqs), S, u32(pos), gtmoe.ptr(ctx), C.c_void_p(ws.data_ptr()),
+                                                ws_n, None))
+        for i in range(n):
+            attention.qkv_epilogue(q_single[i], H, hd, qn, 1e-6, hd // 4, pos[i], 1e4)
+            assert np.array_equal(bits(q[i]), bits(q_single[i])), ("q", i)
+        for j, i in enumerate(uniq):
+            slot = kc_single[seqs[i], pos[i] % cap]
+            attention.qkv_epilogue(kin[j], KV, hd, qn, 1e-6, hd // 4, pos[i], 1e4, out=slot)
+        assert np.array_equal(bits(kc), bits(kc_single))
+        for i in range(n):
+            n_pos = pos[i] + 1
+            first = n_pos - window if window and n_pos > window else 0
+            op = attention.Attention(H, KV, hd, cap)
+            one = torch.empty(qw, device="cuda")
+            op(q[i], kc[seqs[i]], vc[seqs[i]], one, n_pos, first, cap)
+            assert np.array_equal(bits(ctx[i]), bits(one)), ("attention", H, KV, hd, i)

@@ -124,6 +124,53 @@ class OracleLib:
         view(o.hidden_out_dev, oracle.HIDDEN, np.float32)[:] = self.synth[layer].block(x)["hidden"]
         return 0
 
+    # the *_rows entries: row i at the stated offsets, each row through the single stand-in
+    def _gtm_attention_rows_workspace_bytes(self, q_heads, head_dim, window, n):
+        return 256
+
+    def _gtm_embed_lookup_rows(self, rows, in_dim, w, s, b, tokens, n, scale, out, st):
+        for i in range(n):
+            self._gtm_embed_lookup(rows, in_dim, w, s, b, tokens[i], scale, addr(out) + 4 * i * in_dim, st)
+        return 0
+
+    def _gtm_rmsnorm_rows(self, rows, n, x, w, eps, out, st):
+        for i in range(rows):
+            self._gtm_rmsnorm(n, addr(x) + 4 * i * n, w, eps, addr(out) + 4 * i * n, st)
+        return 0
+
+    def _gtm_gemv_q4_rows(self, rows, in_dim, n, w, s, b, x, out, st):
+        for i in range(n):
+            self._gtm_gemv_q4(rows, in_dim, w, s, b, addr(x) + 4 * i * in_dim, addr(out) + 4 * i * rows, st)
+        return 0
+
+    def _gtm_qkv_epilogue_rows(self, heads, head_dim, n, inp, w, eps, pairs, positions, theta, out, seqs, num_seqs,
+                               capacity, st):
+        width = heads * head_dim
+        for i in range(n):
+            row = i if capacity == 0 else seqs[i] * capacity + positions[i] % capacity
+            assert capacity == 0 or seqs[i] < num_seqs
+            self._gtm_qkv_epilogue(heads, head_dim, addr(inp) + 4 * i * width, w, eps, pairs, positions[i], theta,
+                                   addr(out) + 4 * row * width, st)
+        return 0
+
+    def _gtm_attention_decode_rows(self, q_heads, kv_heads, head_dim, n, window, capacity, q, kc, vc, seqs, num_seqs,
+                                   positions, ctx, ws, wsb, st):
+        qw, kw = q_heads * head_dim, kv_heads * head_dim
+        for i in range(n):
+            n_pos = positions[i] + 1
+            first = n_pos - window if window and n_pos > window else 0
+            cache = 4 * seqs[i] * capacity * kw
+            self._gtm_attention_decode(q_heads, kv_heads, head_dim, n_pos, first, capacity, addr(q) + 4 * i * qw,
+                                       addr(kc) + cache, addr(vc) + cache, addr(ctx) + 4 * i * qw, ws, wsb, st)
+        return 0
+
+    def _gtm_post_attn_rows(self, rows, d, attn, hidden, w_post, w_pre, w_pre2, eps, hout, dense, routed, router, st):
+        for i in range(rows):
+            o = 4 * i * d
+            self._gtm_post_attn(d, addr(attn) + o, addr(hidden) + o, w_post, w_pre, w_pre2, eps, addr(hout) + o, None,
+                                None, None, st)
+        return 0
+
     def _gtm_moe_tokens_workspace_bytes(self, dims, n):
         return 256
 

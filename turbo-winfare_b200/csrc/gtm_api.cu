@@ -69,6 +69,21 @@ GTM_API int gtm_gemv_q8(uint32_t rows, uint32_t in_dim, const void* w, const uin
     return gemv_common(8, rows, in_dim, w, s, b, x, out, 0, rows, stream, "gtm_gemv_q8");
 }
 
+GTM_API int gtm_gemv_q4_rows(uint32_t rows, uint32_t in_dim, uint32_t n, const void* w, const uint16_t* s,
+                             const uint16_t* b, const float* x, float* out, void* stream) {
+    if (n == 0) { clear_error(); return GTM_OK; }
+    if (n > kMaxBatchRows)
+        return set_error(GTM_ERR_INVALID, "gtm_gemv_q4_rows: n=%u vectors (1..%u)", n, kMaxBatchRows);
+    if (!w || !s || !b || !x || !out) return set_error(GTM_ERR_INVALID, "gtm_gemv_q4_rows: null pointer");
+    if (rows == 0 || in_dim == 0 || in_dim % kGroup != 0 || in_dim / kGroup > 1024)
+        return set_error(GTM_ERR_INVALID, "gtm_gemv_q4_rows: rows=%u in_dim=%u (a multiple of 64, at most 65536)", rows,
+                         in_dim);
+    if (!aligned(w, 16) || !aligned(s, 2) || !aligned(b, 2) || !aligned(x, 4) || !aligned(out, 4))
+        return set_error(GTM_ERR_MISALIGNED, "gtm_gemv_q4_rows: weights need 16-byte alignment");
+    k_gemv_exact(4, rows, in_dim, w, s, b, x, out, 0, rows, (cudaStream_t)stream, n);
+    return check_launch("gtm_gemv_q4_rows");
+}
+
 GTM_API int gtm_router_topk(uint32_t n, uint32_t k, const float* logits, const uint16_t* pes, uint32_t* idx,
                             float* w, void* stream) {
     if (!logits || !pes || !idx || !w) return set_error(GTM_ERR_INVALID, "gtm_router_topk: null pointer");
@@ -106,6 +121,30 @@ GTM_API int gtm_rmsnorm(uint32_t n, const float* x, const uint16_t* w, float eps
     if (n == 0 || n > kMaxNormDim) return set_error(GTM_ERR_INVALID, "gtm_rmsnorm: n=%u (1..%u)", n, kMaxNormDim);
     k_rmsnorm(n, x, w, eps, out, (cudaStream_t)stream);
     return check_launch("gtm_rmsnorm");
+}
+
+GTM_API int gtm_rmsnorm_rows(uint32_t rows, uint32_t n, const float* x, const uint16_t* w, float eps, float* out,
+                             void* stream) {
+    if (rows == 0) { clear_error(); return GTM_OK; }
+    if (!x || !out) return set_error(GTM_ERR_INVALID, "gtm_rmsnorm_rows: null pointer");
+    if (n == 0 || n > kMaxNormDim || rows > kMaxBatchRows)
+        return set_error(GTM_ERR_INVALID, "gtm_rmsnorm_rows: n=%u (1..%u), rows=%u (at most %u)", n, kMaxNormDim, rows,
+                         kMaxBatchRows);
+    k_rmsnorm(n, x, w, eps, out, (cudaStream_t)stream, rows);
+    return check_launch("gtm_rmsnorm_rows");
+}
+
+GTM_API int gtm_post_attn_rows(uint32_t rows, uint32_t d, const float* attn, const float* hidden,
+                               const uint16_t* wpost, const uint16_t* wpre, const uint16_t* wpre2, float eps,
+                               float* hout, float* dense, float* routed, float* router, void* stream) {
+    if (rows == 0) { clear_error(); return GTM_OK; }
+    if (!attn || !hidden || !wpost || !hout || (dense && !wpre) || (routed && !wpre2))
+        return set_error(GTM_ERR_INVALID, "gtm_post_attn_rows: null pointer");
+    if (d == 0 || d > kMaxNormDim / 2 || rows > kMaxBatchRows)
+        return set_error(GTM_ERR_INVALID, "gtm_post_attn_rows: d=%u (1..%u), rows=%u (at most %u)", d, kMaxNormDim / 2,
+                         rows, kMaxBatchRows);
+    k_post_attn(d, attn, hidden, wpost, wpre, wpre2, eps, hout, dense, routed, router, (cudaStream_t)stream, rows);
+    return check_launch("gtm_post_attn_rows");
 }
 
 GTM_API int gtm_post_attn(uint32_t d, const float* attn, const float* hidden, const uint16_t* wpost,

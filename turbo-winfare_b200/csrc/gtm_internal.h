@@ -47,19 +47,22 @@ int launch_ep_peer_combine(const GtmDims& dims, const GtmLayer& L, const GtmToke
 
 // generic kernels (gtm_kernels.cu); arguments already validated
 void k_gemv_exact(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
-                  const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st);
+                  const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st,
+                  uint32_t nvec = 1);
 void k_router_topk(uint32_t n, uint32_t k, const float* logits, const uint16_t* pes, uint32_t* idx, float* w,
                    cudaStream_t st);
 void k_geglu(uint32_t n, const float* g, const float* u, float* out, cudaStream_t st);
 void k_scale_accum(uint32_t n, const float* in, const float* w, uint32_t wi, int acc, float* out, cudaStream_t st);
 void k_mul_bf16(uint32_t n, const float* in, const uint16_t* w, float scale, float* out, cudaStream_t st);
-void k_rmsnorm(uint32_t n, const float* x, const uint16_t* w, float eps, float* out, cudaStream_t st);
+void k_rmsnorm(uint32_t n, const float* x, const uint16_t* w, float eps, float* out, cudaStream_t st,
+               uint32_t rows = 1);
 void k_post_attn(uint32_t d, const float* attn, const float* hidden, const uint16_t* wpost, const uint16_t* wpre,
                  const uint16_t* wpre2, float eps, float* hout, float* dense, float* routed, float* router,
-                 cudaStream_t st);
+                 cudaStream_t st, uint32_t rows = 1);
 void k_layer_tail(uint32_t d, const float* h2, const float* h1, const float* hidden, const uint16_t* wpf2,
                   const uint16_t* wpf, float eps, float ls, float* hout, cudaStream_t st);
 
 constexpr uint32_t kMaxNormDim = 16384;   // vectors normalised in one CTA's shared memory
+constexpr uint32_t kMaxBatchRows = 512;    // vectors of one *_rows call (per-row arguments travel by value)
 
 }  // namespace gtm

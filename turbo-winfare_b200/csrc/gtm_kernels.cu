@@ -17,8 +17,11 @@ namespace gtm {
 template <int BITS>
 __global__ void gemv_exact_kernel(uint32_t in_dim, const uint8_t* __restrict__ w, const uint16_t* __restrict__ s,
                                   const uint16_t* __restrict__ b, const float* __restrict__ x, float* __restrict__ out,
-                                  uint32_t row_begin, uint32_t row_end) {
+                                  uint32_t row_begin, uint32_t row_end, uint32_t out_rows) {
     extern __shared__ float terms[];          // [rows_per_block][groups]
+    // vector blockIdx.y: x row y of in_dim floats, out row y of out_rows floats
+    x += (size_t)blockIdx.y * in_dim;
+    out += (size_t)blockIdx.y * out_rows;
     const uint32_t groups = in_dim / kGroup;
     const uint32_t rpb = blockDim.x / groups;  // rows per block (>= 1)
     const uint32_t t = threadIdx.x;
@@ -68,18 +71,19 @@ __global__ void gemv_exact_kernel(uint32_t in_dim, const uint8_t* __restrict__ w
 }
 
 void k_gemv_exact(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
-                  const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st) {
-    (void)rows;
+                  const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st, uint32_t nvec) {
     const uint32_t groups = in_dim / kGroup;
     const uint32_t threads = groups >= 256 ? groups : (256 / groups) * groups;
     const uint32_t rpb = threads / groups;
     const uint32_t n = row_end - row_begin;
-    const uint32_t grid = (n + rpb - 1) / rpb;
+    const dim3 grid((n + rpb - 1) / rpb, nvec);
     const size_t smem = sizeof(float) * threads;
     if (bits == 4)
-        gemv_exact_kernel<4><<<grid, threads, smem, st>>>(in_dim, (const uint8_t*)w, s, b, x, out, row_begin, row_end);
+        gemv_exact_kernel<4><<<grid, threads, smem, st>>>(in_dim, (const uint8_t*)w, s, b, x, out, row_begin, row_end,
+                                                          rows);
     else
-        gemv_exact_kernel<8><<<grid, threads, smem, st>>>(in_dim, (const uint8_t*)w, s, b, x, out, row_begin, row_end);
+        gemv_exact_kernel<8><<<grid, threads, smem, st>>>(in_dim, (const uint8_t*)w, s, b, x, out, row_begin, row_end,
+                                                          rows);
 }
 
 // ---- RouterTopK -------------------------------------------------------------------------------
@@ -173,6 +177,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(uint32_t n, const
                                                                float* out) {
     extern __shared__ float sx[];
     __shared__ double red[40];
+    x += (size_t)blockIdx.x * n;     // row blockIdx.x
+    out += (size_t)blockIdx.x * n;
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) sx[i] = x[i];
     __syncthreads();
     const float inv = exact_rms_inv(sx, (int)n, eps, red);
@@ -181,8 +187,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(uint32_t n, const
         out[i] = w ? __fmul_rn(v, bf16f(w[i])) : v;
     }
 }
-void k_rmsnorm(uint32_t n, const float* x, const uint16_t* w, float eps, float* out, cudaStream_t st) {
-    rmsnorm_kernel<<<1, kNormThreads, sizeof(float) * n, st>>>(n, x, w, eps, out);
+void k_rmsnorm(uint32_t n, const float* x, const uint16_t* w, float eps, float* out, cudaStream_t st, uint32_t rows) {
+    rmsnorm_kernel<<<rows, kNormThreads, sizeof(float) * n, st>>>(n, x, w, eps, out);
 }
 
 // src/cpu_reference.cpp:423-434 (the reference's PostAttn shader fuses the same steps).
@@ -194,6 +200,13 @@ __global__ void __launch_bounds__(kNormThreads) post_attn_kernel(uint32_t d, con
     float* sa = sm;
     float* sh = sm + d;
     __shared__ double red[40];
+    const size_t r = (size_t)blockIdx.x * d;   // row blockIdx.x of every vector
+    attn += r;
+    hidden += r;
+    hout += r;
+    if (dense) dense += r;
+    if (routed) routed += r;
+    if (router) router += r;
     for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) { sa[i] = attn[i]; sh[i] = hidden[i]; }
     __syncthreads();
     const float ainv = exact_rms_inv(sa, (int)d, eps, red);
@@ -204,16 +217,16 @@ __global__ void __launch_bounds__(kNormThreads) post_attn_kernel(uint32_t d, con
     for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) {
         const float h = __fmul_rn(sh[i], hinv);
         hout[i] = sh[i];
-        dense[i] = __fmul_rn(h, bf16f(wpre[i]));
-        routed[i] = __fmul_rn(h, bf16f(wpre2[i]));
-        router[i] = h;
+        if (dense) dense[i] = __fmul_rn(h, bf16f(wpre[i]));
+        if (routed) routed[i] = __fmul_rn(h, bf16f(wpre2[i]));
+        if (router) router[i] = h;
     }
 }
 void k_post_attn(uint32_t d, const float* attn, const float* hidden, const uint16_t* wpost, const uint16_t* wpre,
                  const uint16_t* wpre2, float eps, float* hout, float* dense, float* routed, float* router,
-                 cudaStream_t st) {
-    post_attn_kernel<<<1, kNormThreads, 2 * sizeof(float) * d, st>>>(d, attn, hidden, wpost, wpre, wpre2, eps, hout,
-                                                                     dense, routed, router);
+                 cudaStream_t st, uint32_t rows) {
+    post_attn_kernel<<<rows, kNormThreads, 2 * sizeof(float) * d, st>>>(d, attn, hidden, wpost, wpre, wpre2, eps, hout,
+                                                                        dense, routed, router);
 }
 
 // src/cpu_reference.cpp:512-520.

@@ -173,6 +173,15 @@ SIGNATURES = {
     "gtm_qkv_epilogue": (_I, [_U32, _U32, _P, _P, _F, _U32, _U32, _F, _P, _P]),
     "gtm_attention_workspace_bytes": (_SZ, [_U32, _U32, _U32]),
     "gtm_attention_decode": (_I, [_U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P, _SZ, _P]),
+    "gtm_gemv_q4_rows": (_I, [_U32, _U32, _U32, _P, _P, _P, _P, _P, _P]),
+    "gtm_rmsnorm_rows": (_I, [_U32, _U32, _P, _P, _F, _P, _P]),
+    "gtm_post_attn_rows": (_I, [_U32, _U32, _P, _P, _P, _P, _P, _F, _P, _P, _P, _P, _P]),
+    "gtm_embed_lookup_rows": (_I, [_U32, _U32, _P, _P, _P, C.POINTER(_U32), _U32, _F, _P, _P]),
+    "gtm_qkv_epilogue_rows": (_I, [_U32, _U32, _U32, _P, _P, _F, _U32, C.POINTER(_U32), _F, _P, C.POINTER(_U32), _U32,
+                                   _U32, _P]),
+    "gtm_attention_rows_workspace_bytes": (_SZ, [_U32, _U32, _U32, _U32]),
+    "gtm_attention_decode_rows": (_I, [_U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, C.POINTER(_U32), _U32,
+                                       C.POINTER(_U32), _P, _P, _SZ, _P]),
     "gtm_sampling_validate": (_I, [C.POINTER(Sampling)]),
     "gtm_sampling_splitmix64": (_U64, [_U64]),
     "gtm_sampling_seed_for": (_U64, [C.POINTER(Sampling), _I]),
