@@ -25,6 +25,11 @@ tokens:
             Zipf(1.1) routing, HBM roofline)
 
 --workload decode30|batch64 makes config 1 or config 2 the main line (N > 1: replicas).
+--workload decode_batch32 is BASELINE config 4: greedy decode of 32 sequences (1024-token
+random-id prompts, 64 generated tokens) through a 30-layer Gemma-4-26B-A4B-shaped random-init
+model (vocab 262144, sliding/full attention, MoE as config 0) with gtmoe.batch.BatchDecoder; at
+N > 1 the sequences split over the ranks and the experts are sharded (expert parallel over peer
+memory). Metric: generated tokens/s of the whole job; prefill tokens/s beside it.
 
 --impl reference runs the reference's own CPU arithmetic (src/cpu_reference.cpp compiled from
 its sources into oracle/_ref/libgtref.so, single-threaded as shipped, one token at a time as its
@@ -56,22 +61,28 @@ NORM_BYTES = 6 * 2816 * 2 + 128 * 2 + 2                           # norm weights
 LAYER_FLOPS = 2 * (8 * 3 * 704 * 2816 + 3 * 2112 * 2816 + 128 * 2816)  # 131,563,520
 EXPERT_SHARED_FLOPS = LAYER_FLOPS - 2 * 128 * 2816                # routing logits given (config 3)
 
-WORKLOADS = ("prefill4096", "batch64", "decode30")
+WORKLOADS = ("prefill4096", "batch64", "decode30", "decode_batch32")
 METRIC = {"prefill4096": "MoE-layer tokens/s (prefill 4096 bf16 tokens)",
           "batch64": "MoE-layer tokens/s (batch 64 decode, Zipf routing)",
-          "decode30": "MoE-layer tokens/s (batch-1 decode, 30-layer stack)"}
-UNIT = {"prefill4096": "tokens/s", "batch64": "tokens/s", "decode30": "layer-tokens/s"}
+          "decode30": "MoE-layer tokens/s (batch-1 decode, 30-layer stack)",
+          "decode_batch32": "generated tokens/s (greedy decode, 32 sequences, 30-layer model)"}
+UNIT = {"prefill4096": "tokens/s", "batch64": "tokens/s", "decode30": "layer-tokens/s", "decode_batch32": "tokens/s"}
 WORKLOAD_TEXT = {
     "prefill4096": "config3: 4096 bf16 tokens through one MoE layer (hidden 2816, 128 experts top-8, int4 experts "
                    "704, shared 2112), uniform routing logits",
     "batch64": "config2: 64 tokens through one MoE layer, Zipf(1.1) router bias",
     "decode30": "config1: batch-1 decode, 30-layer MoE stack (hidden 2816, 128 experts top-8, int4 experts 704, "
-                "shared 2112, int8 router), weights HBM-resident"}
+                "shared 2112, int8 router), weights HBM-resident",
+    "decode_batch32": "config4: 30-layer Gemma-4-26B-A4B-shaped model (vocab 262144, hidden 2816, MoE as config 0), "
+                      "32 sequences, 1024-token random-id prompts, 64 greedy tokens"}
 TOKENS_PER_STEP = {"prefill4096": 4096, "batch64": 64}
 
 
 def bench_config(workload: str, world: int, ep_mode: str) -> dict:
     """The line's `config`: static descriptors only, so the reference arm prints the same one."""
+    if workload == "decode_batch32":
+        return {"workload": WORKLOAD_TEXT[workload], "sequences": 32, "prompt_tokens": 1024, "new_tokens": 64,
+                "layers": LAYERS_DEFAULT, "parallelism": f"ep{world}" if world > 1 else "single"}
     if workload == "decode30":
         return {"workload": WORKLOAD_TEXT[workload], "layers": LAYERS_DEFAULT,
                 "l2": "inputs larger than L2: 1.1 GB of distinct weights touched per step, new token per step",
@@ -282,6 +293,12 @@ def run_reference_arm(args):
     cores = len(os.sched_getaffinity(0))
     per_step = max(2.0, 20.0 / max(1, args.steps + args.warmup))
     cfg = args.workload
+    if cfg == "decode_batch32":
+        print(json.dumps({"impl": "reference", "metric": METRIC[cfg], "unit": UNIT[cfg], "config": bench_config(cfg, world, args.ep),
+                          "unavailable": "the reference decodes on its CPU at about 14 s per token of this model; "
+                                         "35,000 tokens of config 4 do not fit a bounded run (its per-layer cost is "
+                                         "the decode30 arm)"}), flush=True)
+        return 0
     if cfg == "decode30":
         cb = decode_cpu_baseline(per_step * args.steps, cores)
         ms = 1000.0 * LAYERS_DEFAULT / cb["value"]
@@ -688,6 +705,68 @@ def measure_tokens(cfg: str, steps: int, warmup: int, rank: int, world: int, loc
     return r
 
 
+def measure_batch_decode(rank: int, world: int, local: int, dist, seqs: int = 32, prompt_len: int = 1024,
+                         new_tokens: int = 64, layers: int = LAYERS_DEFAULT):
+    """Config 4: greedy decode of `seqs` sequences through the whole synthetic model; wall clock
+    around the run (every generation step reads its tokens back, so the host waits on the device
+    each step), split at the step that ends the prefill."""
+    import numpy as np
+    import torch
+    import gtmoe
+    from gtmoe import batch, ep
+    S = seqs // world
+    attn, embed, final = batch.synth_decoder(layers)
+    if world == 1:
+        model = gtmoe.SynthModel(layers, seed=0)
+        moe = batch.LocalMoe(model.layers, S)
+        ops = None
+    else:
+        shards = [ep.EpShardModel(l, rank, world) for l in range(layers)]
+        ops = ep.PeerEpOps(shards[0].layer, rank, world, max_tokens=S)
+        ops.connect()
+        moe = batch.PeerEpMoe(ops, ep.NcclBarrier(), [sh.layer for sh in shards])
+    bd = batch.BatchDecoder(attn, moe, embed, final, prompt_len + new_tokens + 1, S, dist=dist)
+    prompts = np.random.default_rng(7).integers(0, embed["rows"], size=(seqs, prompt_len))
+    mine = prompts[rank * S:(rank + 1) * S].tolist()
+    stops = (1, 106, 50)
+    bd.greedy([p[:3] for p in mine], 2, stops)   # warm-up
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    marks = {}
+
+    def on_step(step):
+        if step == prompt_len - 1:
+            marks["prefill"] = time.perf_counter()
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        out = bd.greedy(mine, new_tokens, stops, on_step=on_step)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        clk.sample()
+    gen = sum(len(o) for o in out)
+    vals = torch.tensor([t1 - t0, marks["prefill"] - t0, float(gen)], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        mx = vals[:2].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        g = vals[2:].clone()
+        dist.all_reduce(g)
+        vals = torch.cat([mx, g])
+    total_s, prefill_s, gen = float(vals[0]), float(vals[1]), int(vals[2])
+    gen_s = total_s - prefill_s
+    r = {"value": gen / gen_s, "ms_per_step": 1000.0 * gen_s / max(1, new_tokens - 1),
+         "prefill_tokens_per_s": seqs * prompt_len / prefill_s, "prefill_s": prefill_s, "generate_s": gen_s,
+         "generated_tokens": gen, "seq0_first_tokens": out[0][:8] if rank == 0 else None,
+         "clocks": clk.summary(), "gpu_launches": None,
+         "roofline": None}
+    if ops is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        ops.close()
+        dist.barrier()
+    return r
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -715,7 +794,7 @@ def main():
 
     # CPU baseline first: worker processes are spawned before this process touches the GPU
     cb = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg != "decode_batch32":
         cb = decode_cpu_baseline(args.cpu_seconds, 1) if cfg == "decode30" else token_cpu_baseline(args.cpu_seconds,
                                                                                                    cfg)
     import torch
@@ -726,6 +805,22 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
 
+    if cfg == "decode_batch32":
+        m = measure_batch_decode(rank, world, local, dist)
+        if rank == 0:
+            line = {"metric": METRIC[cfg], "value": m["value"], "unit": UNIT[cfg], "n_gpus": world, "steps": 64,
+                    "warmup": 1, "ms_per_step": m["ms_per_step"], "higher_is_better": True,
+                    "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+                    "dtype": "f32 (fp16 hi/lo tensor-core operands in the MoE block)",
+                    "data": "synthetic (random-init weights, random-id prompts)",
+                    "config": bench_config(cfg, world, args.ep),
+                    **{k: m[k] for k in ("prefill_tokens_per_s", "prefill_s", "generate_s", "generated_tokens",
+                                         "seq0_first_tokens", "clocks")}}
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     if cfg == "decode30":
         m = measure_decode(args.steps, args.warmup, args.layers, rank, local, dist)
     else:

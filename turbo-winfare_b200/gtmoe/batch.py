@@ -167,10 +167,10 @@ class BatchDecoder:
         self.dist.all_reduce(flag)
         return int(flag.item()) == 0
 
-    def greedy(self, prompts, max_tokens: int, stops=(1, 106, 50)) -> list[list[int]]:
+    def greedy(self, prompts, max_tokens: int, stops=(1, 106, 50), on_step=None) -> list[list[int]]:
         """CpuReference::generate's greedy loop for every prompt, advanced together: sequence i
         prefills prompts[i] at positions 0.., then feeds back its argmax token until it has
-        max_tokens tokens or meets a stop id."""
+        max_tokens tokens or meets a stop id. on_step(step) is called after every step."""
         if len(prompts) > self.max_seqs:
             raise ValueError(f"{len(prompts)} prompts > max_seqs {self.max_seqs}")
         if any(len(p) == 0 for p in prompts):
@@ -209,6 +209,8 @@ class BatchDecoder:
                     out[i].append(nxt)
                     if len(out[i]) >= max_tokens:
                         live[i] = False
+            if on_step is not None:
+                on_step(step)
             step += 1
         self.moe.check()
         return out
