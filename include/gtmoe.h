@@ -226,7 +226,9 @@ GTM_API int gtm_moe_decode_check(void* workspace_dev, void* stream);
  * cannot allocate device memory (a bare C/FFI host with no device allocator, or a process that
  * reserves all device memory at start-up and forbids later allocation): the scratch is a
  * statically sized array of the library, 256 KB per device, so the call allocates nothing. The
- * first call on each device looks that array up and should come before any stream capture.
+ * first call on each device looks that array up and should come before any stream capture; the
+ * address it keeps is the primary context's, so call from the primary context and do not reset
+ * the device after the first call.
  * Every call on a device shares the one array: calls that overlap on the GPU race. layers ==
  * NULL with num_layers == 0 reads and clears the array's device-side error word instead
  * (synchronises `stream`; returns GTM_OK or GTM_ERR_TIMEOUT). */

@@ -47,14 +47,12 @@ constexpr int TILES_R = TOPK * FE / 8;    // 704 routed gate/up tiles (8 row pai
 constexpr int TILES_S = FS / 8;           // 264 shared gate/up tiles
 constexpr int OT = D / 16;                // 176 output row tiles of the down projection
 constexpr int NSEG = 3 + TOPK;            // down partials: 3 shared thirds + 8 routed experts
-constexpr int ITEMS_SD = OT * 3;          // 528 shared-down items (3 thirds of K x 176 row tiles)
-constexpr int ITEMS_DN = OT * NSEG;       // 1936 down items: segment s = item / OT, shared thirds first
+constexpr int ITEMS_DN = OT * NSEG;       // 1936 down items: row tile item / NSEG, segment item % NSEG
 constexpr int MAX_ITEMS = 17;             // per CTA and phase (down items over >= 118 CTAs)
 constexpr int ROW_GU = D / 2;             // 1408 bytes per gate/up row
 constexpr int RIN_PITCH = 65;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr int ACT_R = TOPK * FE;          // 5632 routed activations, after the 2112 shared ones
-constexpr int SEGK = FE;                  // 704 activations per down segment (a shared third or a slot)
 
 enum { BAR_A1 = 0, BAR_B = 2, BAR_C = 3 };
 
@@ -71,7 +69,7 @@ struct Params {
     int* sticky;
     float* logits;     // [NE]
     float* act;        // [FS + ACT_R]: shared activations, then the 8 routed slots (segment s at s * 704)
-    float* part;       // [NSEG][D]
+    float* part;       // [2 contributors][2: shared, routed][D] down sums (the rest of NSEG x D unused)
 };
 
 // B-operand fragment tables: per 64-element group, 8 slots (4 thread columns x hi/lo) of 8
@@ -178,7 +176,7 @@ __device__ __forceinline__ uint32_t cvt2(float lo_half, float hi_half) {   // (l
 // nv (1 or 2) tables in one pass: items [0, 4 groups) build table 0, [4 groups, 8 groups) table 1
 // (4 groups is a multiple of 4, so no 4-lane shuffle group straddles the two)
 __device__ void build_tables(int nv, int groups, const float* v0, uint32_t* tbl0, float* xs0, float* cs0,
-                             const float* v1, uint32_t* tbl1, float* xs1, float* cs1) {
+                             const float* v1, uint32_t* tbl1, float* xs1, float* cs1, bool from_global = false) {
     // one thread per (group j, thread column t): both parts of its 16 elements, then the group's
     // sums over the 4 columns (adjacent lanes). Items past the last table read row 0 of table 0.
     for (int i2 = threadIdx.x; i2 < ((nv * groups * 4 + 31) & ~31); i2 += blockDim.x) {
@@ -194,7 +192,8 @@ __device__ void build_tables(int nv, int groups, const float* v0, uint32_t* tbl0
         float x[16], hi[16], lo[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const float4 f = src[q];
+            // global sources were written by other CTAs in this launch: read them from L2
+            const float4 f = from_global ? __ldcg(src + q) : src[q];
             x[4 * q] = f.x; x[4 * q + 1] = f.y; x[4 * q + 2] = f.z; x[4 * q + 3] = f.w;
         }
 #pragma unroll
@@ -232,14 +231,6 @@ __device__ void build_tables(int nv, int groups, const float* v0, uint32_t* tbl0
 
 __device__ void build_table(const float* v, int groups, uint32_t* tbl, float* xs, float* cs) {
     build_tables(1, groups, v, tbl, xs, cs, v, tbl, xs, cs);
-}
-
-// Copies n floats (n % 4 == 0) written by other CTAs in this launch into shared memory.
-__device__ __forceinline__ void stage_from_global(float* dst, const float* src, int n) {
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    float4* d4 = reinterpret_cast<float4*>(dst);
-    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
-    __syncthreads();
 }
 
 // One warp: groups [j0, j1) of a 16-row tile. Rows g (pointer set a) and g + 8 (set b); lane
@@ -352,6 +343,38 @@ __device__ __forceinline__ void warp_items(Smem& s, int slot_base, int n_items, 
         if (t == 0) {
             s.slot[slot_base + item][warp][g] = ya;
             s.slot[slot_base + item][warp][8 + g] = yb;
+        }
+        p += j1 - j0;
+    }
+}
+
+// As warp_items, with each item's own table and K-group base (the down phase mixes segments).
+struct ItemSrc {
+    TileRows R;
+    const uint32_t* tbl;
+    const float* xs;
+    const float* cs;
+    int jbase;
+};
+template <class SrcFn>
+__device__ __forceinline__ void warp_items_src(Smem& s, int n_items, int L, SrcFn src_of) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int total = n_items * L;
+    int p = warp * total / NW;
+    const int p1 = (warp + 1) * total / NW;
+    while (p < p1) {
+        const int item = p / L, j0 = p - item * L;
+        const int j1 = min(L, j0 + (p1 - p));
+        const ItemSrc S = src_of(item);
+        float ya = 0.0f, yb = 0.0f;
+        gemv_groups(S.R, S.jbase + j0, S.jbase + j1, S.tbl, S.xs, S.cs, ya, yb);
+        ya += __shfl_xor_sync(0xffffffffu, ya, 1);
+        ya += __shfl_xor_sync(0xffffffffu, ya, 2);
+        yb += __shfl_xor_sync(0xffffffffu, yb, 1);
+        yb += __shfl_xor_sync(0xffffffffu, yb, 2);
+        if (t == 0) {
+            s.slot[item][warp][g] = ya;
+            s.slot[item][warp][8 + g] = yb;
         }
         p += j1 - j0;
     }
@@ -499,16 +522,12 @@ __device__ void tail_and_views(Smem& s, const Params& P, const GtmLayer* Lp, boo
         const float ls = bf16f(*rp16(Lp->resident_dev, Lp->layer_scalar));
         double b = 0.0;
         for (int i = tid; i < D / 4; i += NT) {
+            // part [contributor][shared, routed][D]: shared = p00 + p10, routed h2 = p01 + p11
             const float4* pp = reinterpret_cast<const float4*>(P.part) + i;
-            float4 vs = __ldcg(pp), vh = __ldcg(pp + 3 * (D / 4));
-            const float4 s1 = __ldcg(pp + (D / 4)), s2 = __ldcg(pp + 2 * (D / 4));
+            float4 vs = __ldcg(pp), vh = __ldcg(pp + (D / 4));
+            const float4 s1 = __ldcg(pp + 2 * (D / 4)), r1 = __ldcg(pp + 3 * (D / 4));
             vs.x += s1.x; vs.y += s1.y; vs.z += s1.z; vs.w += s1.w;
-            vs.x += s2.x; vs.y += s2.y; vs.z += s2.z; vs.w += s2.w;
-#pragma unroll
-            for (int k = 1; k < TOPK; ++k) {
-                const float4 r = __ldcg(pp + (3 + k) * (D / 4));
-                vh.x += r.x; vh.y += r.y; vh.z += r.z; vh.w += r.w;
-            }
+            vh.x += r1.x; vh.y += r1.y; vh.z += r1.z; vh.w += r1.w;
             reinterpret_cast<float4*>(sh)[i] = vs;
             reinterpret_cast<float4*>(h2)[i] = vh;
             a += (double)vs.x * vs.x + (double)vs.y * vs.y + (double)vs.z * vs.z + (double)vs.w * vs.w;
@@ -721,10 +740,13 @@ __device__ void routed_gate_up(Smem& s, const Params& P, const GtmLayer& L, int 
     }
 }
 
-// Down items [i0, i1) of the shared expert and the 8 routed experts, one pass: item i ->
-// segment q = i / OT, row tile ot = i % OT. Segments 0..2: K groups [11q, 11q + 11) of the shared
-// down rows (33 groups) -> part[q][16*ot + r]; segments 3..10: expert slot k = q - 3, all 11 groups
-// of its down rows -> part[q][16*ot + r] = w_k * row. The table of segment q is tbl_dn + 11 q.
+// Down items [i0, i1) of the shared expert and the 8 routed experts, one pass, in row-tile-major
+// order: item i -> row tile ot = i / NSEG, segment q = i % NSEG. Segments 0..2: K groups
+// [11q, 11q + 11) of the shared down rows (33 groups); segments 3..10: expert slot k = q - 3, all 11
+// groups of its down rows, times w_k. The table of segment q is tbl_dn + 11 q. The CTA sums its
+// segments of each row tile in segment order, shared and routed apart, into contributor slot 0
+// (the CTA holding segment 0 of the tile) or 1: a CTA holds >= 13 consecutive items, so a tile of
+// 11 has at most two contributors, and the tail reads part[0] + part[1] (4 vectors, not 11).
 __device__ void down_items(Smem& s, const Params& P, const GtmLayer& L, int i0, int i1) {
     const int n = i1 - i0;
     if (n <= 0) return;
@@ -732,33 +754,45 @@ __device__ void down_items(Smem& s, const Params& P, const GtmLayer& L, int i0, 
     __syncthreads();
     const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
     const int lane_g = (threadIdx.x & 31) >> 2;
-    // items of different segments use different rows and tables: walk segment by segment
-    int a = i0;
-    while (a < i1) {
-        const int q = a / OT;
-        const int b = min(i1, (q + 1) * OT);
-        const int off = a - i0, nn = b - a;
+    warp_items_src(s, n, GFE, [&](int item) {
+        const int it = i0 + item, ot = it / NSEG, q = it - ot * NSEG;
+        ItemSrc S;
         if (q < 3) {
-            warp_items(s, off, nn, GFE, q * GFE, s.tbl_dn, s.xs_dn, s.cs_dn, [&](int item) {
-                const int ot = (a + item) - q * OT;
-                return down_rows(res, L.shared_down, ot * 16 + lane_g, FS / 2, GFS);
-            });
+            S.R = down_rows(res, L.shared_down, ot * 16 + lane_g, FS / 2, GFS);
+            S.tbl = s.tbl_dn;
+            S.xs = s.xs_dn;
+            S.cs = s.cs_dn;
+            S.jbase = q * GFE;
         } else {
             const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[q - 3] * L.expert_stride);
-            warp_items(s, off, nn, GFE, 0, s.tbl_dn + q * GFE * TBL_WORDS, s.xs_dn + q * GFE, s.cs_dn + q * GFE,
-                       [&](int item) {
-                           const int ot = (a + item) - q * OT;
-                           return down_rows(blk, L.expert_down, ot * 16 + lane_g, FE / 2, GFE);
-                       });
+            S.R = down_rows(blk, L.expert_down, ot * 16 + lane_g, FE / 2, GFE);
+            S.tbl = s.tbl_dn + q * GFE * TBL_WORDS;
+            S.xs = s.xs_dn + q * GFE;
+            S.cs = s.cs_dn + q * GFE;
+            S.jbase = 0;
         }
-        a = b;
-    }
+        return S;
+    });
     __syncthreads();
-    for (int i = threadIdx.x; i < n * 16; i += NT) {
-        const int item = i >> 4, r = i & 15;
-        const int it = i0 + item, q = it / OT, ot = it - q * OT;
-        const float v = slot_sum(s, item, r);
-        P.part[(size_t)q * D + ot * 16 + r] = q < 3 ? v : s.topw[q - 3] * v;
+    const int ot0 = i0 / NSEG, ot1 = (i1 - 1) / NSEG;
+    for (int i = threadIdx.x; i < (ot1 - ot0 + 1) * 16; i += NT) {
+        const int ot = ot0 + (i >> 4), r = i & 15;
+        const int a = max(i0, ot * NSEG), b = min(i1, ot * NSEG + NSEG);
+        float sh = 0.0f, h2 = 0.0f;
+        for (int it = a; it < b; ++it) {
+            const int q = it - ot * NSEG;
+            const float v = slot_sum(s, it - i0, r);
+            if (q < 3) sh = __fadd_rn(sh, v);
+            else h2 = __fadd_rn(h2, __fmul_rn(s.topw[q - 3], v));   // the product rounded, as the combine had it
+        }
+        const int c = a == ot * NSEG ? 0 : 1;
+        float* pc = P.part + (size_t)c * 2 * D + ot * 16 + r;
+        pc[0] = sh;
+        pc[D] = h2;
+        if (c == 0 && b == ot * NSEG + NSEG) {   // the whole tile here: no second contributor
+            pc[2 * D] = 0.0f;
+            pc[3 * D] = 0.0f;
+        }
     }
 }
 
@@ -770,7 +804,7 @@ __device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
     const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
     const int nrow = cta < NE ? (NE - 1 - cta) / G + 1 : 0;          // router rows of this CTA
     const int t0 = share(TILES_S, cta, G), t1 = share(TILES_S, cta + 1, G);
-    const int i0 = min(share(ITEMS_DN, cta, G), ITEMS_SD), i1 = min(share(ITEMS_DN, cta + 1, G), ITEMS_SD);
+    const int i0 = share(ITEMS_DN, cta, G), i1 = share(ITEMS_DN, cta + 1, G);   // this CTA's down items
     const int n_router = 3 * nrow, n_sgu = t1 > t0 ? 6 : 0, n_sd = 18 * (i1 - i0), n_vec = 6;
     const int total = n_router + n_sgu + n_sd + n_vec;
     for (int i = warp; i < total; i += NW) {
@@ -787,8 +821,10 @@ __device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
             if (part == 0) { p = base + q.weight + (uint64_t)t0 * 8 * ROW_GU; n = (t1 - t0) * 8 * ROW_GU; }
             else { p = base + (part == 1 ? q.scales : q.biases) + (uint64_t)t0 * 8 * GD * 2; n = (t1 - t0) * 8 * GD * 2; }
         } else if (i < n_router + n_sgu + n_sd) {
+            // the shared-down items among them (segments 0..2); routed ones prefetch after the top-8
             const int k = i - n_router - n_sgu, it = i0 + k / 18, part = k % 18;
-            const int q = it / OT, ot = it - q * OT;
+            const int ot = it / NSEG, q = it - ot * NSEG;
+            if (q >= 3) continue;
             if (part < 16) {
                 p = base + L.shared_down.weight + ((uint64_t)ot * 16 + part) * (FS / 2) + q * GFE * 32;
                 n = GFE * 32;
@@ -825,10 +861,11 @@ __device__ void prefetch_routed_gate_up(const Smem& s, const GtmLayer& L, int ct
 // L2 prefetch of this CTA's routed-down rows (known once the top-8 is).
 __device__ void prefetch_routed_down(const Smem& s, const GtmLayer& L, int cta, int G) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i0 = max(share(ITEMS_DN, cta, G), ITEMS_SD) - ITEMS_SD, i1 = max(share(ITEMS_DN, cta + 1, G), ITEMS_SD) - ITEMS_SD;
+    const int i0 = share(ITEMS_DN, cta, G), i1 = share(ITEMS_DN, cta + 1, G);
     for (int i = warp; i < 3 * (i1 - i0); i += NW) {
-        const int it = i0 + i / 3, part = i % 3, k = it / OT, ot = it - k * OT;
-        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
+        const int it = i0 + i / 3, part = i % 3, ot = it / NSEG, q = it - ot * NSEG;
+        if (q < 3) continue;   // shared-down items were prefetched with the layer's static weights
+        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[q - 3] * L.expert_stride);
         if (part == 0) prefetch_lines(blk + L.expert_down.weight + (uint64_t)ot * 16 * (FE / 2), 16 * (FE / 2), lane);
         else prefetch_lines(blk + (part == 1 ? L.expert_down.scales : L.expert_down.biases) + (uint64_t)ot * 16 * GFE * 2,
                             16 * GFE * 2, lane);
@@ -889,11 +926,9 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
         if (!wait_all(P, s, BAR_B, ep)) return;
         const int d0 = share(ITEMS_DN, cta, G), d1 = share(ITEMS_DN, cta + 1, G);
         if (d1 > d0) {
-            // the segments this CTA's items read (at most 2 for >= 118 CTAs), staged from 0
-            const int qmin = d0 / OT, qmax = (d1 - 1) / OT;
-            stage_from_global(s.ab, P.act + qmin * SEGK, (qmax - qmin + 1) * SEGK);
-            build_table(s.ab, (qmax - qmin + 1) * GFE, s.tbl_dn + qmin * GFE * TBL_WORDS, s.xs_dn + qmin * GFE,
-                        s.cs_dn + qmin * GFE);
+            // a CTA's >= 11 consecutive row-tile-major items read every segment: the tables of all
+            // 11 (the shared activations, then the 8 routed slots), built straight from L2
+            build_tables(1, NSEG * GFE, P.act, s.tbl_dn, s.xs_dn, s.cs_dn, P.act, s.tbl_dn, s.xs_dn, s.cs_dn, true);
         }
         __syncthreads();
         if (l + 1 < P.num_layers) prefetch_layer_static(P.layers[l + 1], cta, G);

@@ -15,7 +15,11 @@
 //   * one scratch per device, shared by every call: calls that overlap on one device (two
 //     streams, or two host threads) race on it and must be serialised by the caller;
 //   * the first call on each device looks the array's device address up (cudaGetSymbolAddress,
-//     with that device current) and keeps it; make that first call before any stream capture;
+//     with that device current) and keeps it; make that first call before any stream capture.
+//     The kept address belongs to the device's primary context as it was then: use the entry from
+//     the primary context (the runtime's default), and do not reset the device
+//     (cudaDeviceReset) after the first call, which unloads the module and leaves the kept
+//     address pointing at nothing;
 //   * what must start at zero: the barrier flags and the per-launch error word are cleared by
 //     every call before its launch; the sticky error word starts at zero (static device storage
 //     is zero-initialised at module load) and is cleared whenever it is read back;
