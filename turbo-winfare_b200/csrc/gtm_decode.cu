@@ -5,27 +5,43 @@
 // MulBF16 -> GemvInt8 -> RouterTopK -> CPU read-back -> shared expert (GemvInt4 x3, GeGLU,
 // RMSNormK) -> per expert GemvInt4 gate/up, GeGLU, GemvInt4 down, ScaleAccum -> LayerTail.
 //
-// Int4 products (gemv_groups): weights are dequantised to fp16 in registers (exact integers
-// 0..15, two LOP3 masks per nibble pair) and fed as the A operand of mma.sync.m16n8k16; the
-// activation goes in as B split into an fp16 high part (column 0) and low part (column 1), so
-// sum_k q_k * x_k comes out in fp32 to ~2^-22 of x. The group's bf16 scale and bias are applied
-// in fp32 after each 64-element group: y += s * (d_hi + d_lo) + b * sum(x). A 16-row tile is
-// either 8 gate rows on top of the same 8 up rows (so GeGLU happens in registers) or 16 rows of a
-// down projection. tcgen05 would need the dequantised tile staged through shared memory for a
-// one-column product; mma.sync consumes the register fragments the dequant produces directly.
+// Weight streaming. Each CTA (one per SM) has a fixed list of weight "chunks" per layer: its
+// router row, its shared gate/up tiles, its routed gate/up tiles (the expert ids come from the
+// layer's top-8) and its down rows. A producer warp copies them with cp.async.bulk (the TMA's
+// global -> shared bulk copy, one instruction per contiguous range) into a 144 KB shared-memory
+// ring, in the order the compute warps use them, as far ahead as the ring has room. So the static
+// weights of the next phase or layer stream in while the CTA waits at a grid barrier or works
+// through the layer tail, and the routed weights are all requested the moment the top-8 is known.
+// The 22 compute warps wait on each chunk's mbarrier and hand it back to the producer with an
+// arrival on the chunk's "empty" mbarrier.
 //
-// Per layer (one token), with split arrive/wait grid barriers (bounded waits):
-//   P1  every CTA: layer tail of the previous layer from the down partials, optional
-//       between-layer RMSNorm, views (dense_x, routed_x, router input); CTAs 0..127: one router
-//       logit each in the reference's exact order (bit-identical logits)      -> arrive A1
-//       every CTA: its share of the 264 shared gate/up tiles (+GeGLU)
-//   P2  wait A1; top-8 (each CTA); L2-prefetch its routed down rows; its share of the 704 routed
-//       gate/up tiles (+GeGLU)                                                -> arrive B
-//   P3  wait B (every CTA's shared and routed activations); its share of the 1936 down items,
-//       the shared down (3 thirds of K x 176 row tiles) and the routed down (8 experts x 176 row
-//       tiles, partials x w_k) in one pass; L2-prefetch the next layer's router row, shared
-//       gate/up and down                                                      -> arrive C
-// The down partials [3 shared + 8 routed][2816] are summed in fixed order by the next tail.
+// Int4 products. A 16-row tile is processed one "quad" of 4 quantisation groups (128 bytes of a
+// row) at a time. Lane (g, t) of a warp loads 16 bytes of row g and 16 of row g + 8 per double
+// group h (bytes 64 h + 16 t of the quad): rows of 1408 bytes start on the same bank, so gate/up
+// tiles put 4 gate rows and 4 up rows in each half of the tile, and the up rows sit 64 bytes off
+// the gate rows in shared memory; down rows (352 and 1056 bytes) land on four bank offsets by
+// themselves. Every 16-byte load of a warp is then conflict-free. The products are integer
+// tensor-core MMAs (mma.sync.m16n8k32, u8 x s8 -> s32): a word of 8 nibbles becomes two registers
+// of four u8 (w & 0x0F0F0F0F and (w >> 4) & 0x0F0F0F0F), the A operand of rows g and g + 8. The
+// activation enters as the B operand: each group of 64 is written as x = 2^(E-6) (L0 + L1 / 2^7
+// + L2 / 2^14) with a power-of-two group scale (|x| < 2^E) and three signed limbs of at most 64
+// in magnitude, so each x is carried to 2^-21 of the group's largest; the limbs of the two groups
+// of a double group sit in B columns 0-2 and 4-6. Integer accumulation is exact, so D holds per
+// row and group the three limb sums of sum_k q_k x_k exactly. After a double group the lane pair
+// holding a group combines them in fp32 and applies the group's bf16 scale and bias:
+// y += s * 2^(E-6) * (D0 + D1 2^-7 + D2 2^-14) + b * sum(x).
+//
+// Per layer (one token), with bounded grid-wide waits:
+//   tail    every CTA: layer tail of the previous layer from the down partials, optional
+//           between-layer RMSNorm, views (dense_x, routed_x, router input), fragment tables
+//   router  CTAs 0..127: their router logit in the reference's exact order (bit-identical), published
+//           with the layer number in one 64-bit word; the words double as barrier A
+//   shared  each CTA's share of the 264 shared gate/up tiles (+GeGLU)
+//   top-8   wait for all 128 logit words; top-8 on every CTA; the producer starts the routed copies
+//   routed  each CTA's share of the 704 routed gate/up tiles (+GeGLU)            -> barrier B
+//   down    fragment tables of the 7744 activations; each CTA's share of the 1936 down items
+//           (row tile x segment: 3 thirds of the shared down, 8 routed experts) -> barrier C
+// The down partials [2 contributors][shared, routed][2816] are summed in fixed order by the tail.
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
@@ -33,28 +49,42 @@
 #include <cuda_runtime.h>
 
 #include "gtm_common.cuh"
+#include "gtm_frag.cuh"
 #include "gtm_internal.h"
+#include "gtm_tcgen05.cuh"
 
 namespace gtm {
 namespace dec {
 
 constexpr int D = 2816, FE = 704, FS = 2112, NE = 128, TOPK = 8;
-constexpr int NT = 512, NW = NT / 32;
+constexpr int NWC = 22;                   // compute warps
+constexpr int NTC = NWC * 32;             // 704 compute threads: one float4 of a hidden vector each
+constexpr int NT = NTC + 32;              // + the producer warp
 constexpr int GD = D / kGroup;            // 44 groups in a hidden-sized input
 constexpr int GFE = FE / kGroup;          // 11
 constexpr int GFS = FS / kGroup;          // 33
-constexpr int TILES_R = TOPK * FE / 8;    // 704 routed gate/up tiles (8 row pairs each)
+constexpr int QD = GD / 4;                // 11 quads of a hidden-sized input
+constexpr int QS = 3;                     // quads of an 11-group down segment (the last holds 3 groups)
+constexpr int TILES_R = TOPK * FE / 8;    // 704 routed gate/up tiles (8 features each)
 constexpr int TILES_S = FS / 8;           // 264 shared gate/up tiles
+constexpr int TPE = FE / 8;               // 88 tiles per routed expert
 constexpr int OT = D / 16;                // 176 output row tiles of the down projection
-constexpr int NSEG = 3 + TOPK;            // down partials: 3 shared thirds + 8 routed experts
+constexpr int NSEG = 3 + TOPK;            // down segments: 3 shared thirds + 8 routed experts
 constexpr int ITEMS_DN = OT * NSEG;       // 1936 down items: row tile item / NSEG, segment item % NSEG
-constexpr int MAX_ITEMS = 17;             // per CTA and phase (down items over >= 118 CTAs)
 constexpr int ROW_GU = D / 2;             // 1408 bytes per gate/up row
+constexpr int SROW_GU = GD * 2;           // 88 bytes of bf16 scales per gate/up row
+constexpr int DROW_R = FE / 2, SROW_R = GFE * 2;   // routed down: 352 bytes per row, 22 of scales
+constexpr int DROW_S = FS / 2, SROW_S = GFS * 2;   // shared down: 1056, 66
 constexpr int RIN_PITCH = 65;
-constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr int QW = 192;                   // fragment-table words per quad: 2 double groups x 12 lane entries x 8
+constexpr uint32_t RING = 144 * 1024;     // chunk ring
+constexpr int NB = 32;                    // chunk mbarrier slots (> the chunks of any one phase)
+constexpr int GU_TILES = 2;               // tiles per gate/up chunk
+constexpr int MAX_DN = 24;                // down items per CTA (>= 1936 / 88)
+constexpr int MAX_OTS = 4;                // down row tiles per CTA
 constexpr int ACT_R = TOPK * FE;          // 5632 routed activations, after the 2112 shared ones
-
-enum { BAR_A1 = 0, BAR_B = 2, BAR_C = 3 };
+constexpr int SLOTS = 1024;               // partial-sum floats: items x max contributors x 16 rows
+constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 struct Params {
     GtmLayer layers[GTM_MAX_LAYERS];
@@ -62,47 +92,64 @@ struct Params {
     int num_layers;
     float eps;
     float inv_sqrt_d;
-    unsigned* flags;   // [4][256]
-    uint64_t wait_limit_ns;      // bound of every grid-barrier wait
-    unsigned first_wait_extra;   // added to the first wait's epoch (test hook: 1 = never reached)
+    unsigned long long* logit_words;   // [NE]: (layer + 1) << 32 | logit bits
+    unsigned* flags_b;                 // [256] barrier B, one word per CTA
+    unsigned* flags_c;                 // [256] barrier C
+    uint64_t wait_limit_ns;            // bound of every wait
+    unsigned first_wait_extra;         // added to the first wait's epoch (test hook: 1 = never reached)
     int* err;
     int* sticky;
-    float* logits;     // [NE]
-    float* act;        // [FS + ACT_R]: shared activations, then the 8 routed slots (segment s at s * 704)
-    float* part;       // [2 contributors][2: shared, routed][D] down sums (the rest of NSEG x D unused)
+    float* act;        // [FS + ACT_R]: shared activations, then the 8 routed slots (segment q at q * 704)
+    float* part;       // [2 contributors][2: shared, routed][D] down sums
 };
 
-// B-operand fragment tables: per 64-element group, 8 slots (4 thread columns x hi/lo) of 8
-// packed fp16 pairs, stored half-major so the 8 reading lanes hit consecutive 16-byte chunks.
-constexpr int TBL_WORDS = 64;   // 32-bit words per group (256 bytes)
+// Per-CTA work lists (identical on every thread; derived from the CTA index and grid size).
+struct Plan {
+    int nr;              // router rows: cta, cta + G, ...
+    int st0, st1;        // shared gate/up tiles
+    int rt0, rt1;        // routed gate/up tiles
+    int d0, d1;          // down items (row-tile-major)
+    int n_sgu, n_rgu;    // gate/up chunks
+    int ot0;             // first down row tile of the CTA
+    int sh_a, sh_b;      // shared-down row tiles [sh_a, sh_b] of the shared-down chunk
+    int c_sgu, c_rgu, c_dn, cpl;   // first chunk of each phase within a layer, chunks per layer
+};
 
-// Arrays read or written with 16-byte vector accesses or cp.async carry alignas(16).
 struct Smem {
+    alignas(128) uint8_t ring[RING + 128];   // chunks (+ slack read by a down row's partial last quad)
     alignas(16) float hid[D];
-    alignas(16) float ab[2 * D];   // scratch: [0, D) and [D, 2D), or one 2D-float vector
-    alignas(16) float rin[GD * RIN_PITCH];
-    alignas(16) uint32_t tbl_r[GD * TBL_WORDS];        // routed_x
-    alignas(16) uint32_t tbl_d[GD * TBL_WORDS];        // dense_x
-    alignas(16) uint32_t tbl_dn[NSEG * GFE * TBL_WORDS];  // down inputs: shared act, then routed slots
-    float xs_r[GD], xs_d[GD], xs_dn[NSEG * GFE];
-    float cs_r[GD], cs_d[GD], cs_dn[NSEG * GFE];
-    // bf16 norm vectors, copied ahead of use: this layer's pre_ffn_norm, pre_ffn_norm_2,
-    // router.scale and the previous layer's post_ffn_norm_1, post_ffn_norm_2, post_ffn_norm
-    alignas(16) uint16_t nw[6][D];
-    alignas(16) uint16_t pes[NE];   // per_expert_scale of the layer (copied with the pre-FFN norms)
-    float slot[MAX_ITEMS][NW][16];
+    union {
+        struct {
+            alignas(16) float ab[2 * D];     // routed_x [0, D), dense_x [D, 2D)
+            alignas(16) float rin[GD * RIN_PITCH];
+        } t;
+        alignas(16) uint32_t tbl_dn[NSEG * QS * QW];   // down inputs: segment q at q * 576 words
+    } u;
+    alignas(16) uint32_t tbl_r[QD * QW];     // routed_x
+    alignas(16) uint32_t tbl_d[QD * QW];     // dense_x
+    float2 gs_r[GD], gs_d[GD];               // per group of the views: (sum of x, 2^(E-6))
+    float2 gs_dn[NSEG * 4 * QS];             // and of the down inputs
+    float slot[SLOTS];                       // partial sums: [item][contributing warp k][16 rows]
+    double red[2][NWC][2];
+    float redf[2][NWC][2];
+    double seq_sum;                          // certified RMS fallback
     float terms[GD];
-    double red[40];
-    double red2[2][NW][2];   // two-value block reductions, double-buffered
     float topw[TOPK];
     int topi[TOPK];
+    int dn_ot[MAX_DN], dn_q[MAX_DN];         // down items in processing (chunk) order
+    int dn_pos[MAX_OTS][NSEG];               // processing index of (row tile ot0 + i, segment q)
+    uint64_t full[NB];                       // chunk landed (producer arrive + bytes)
+    uint64_t empty[NB];                      // chunk released (one arrival per compute warp)
+    uint32_t meta[NB];                       // ring offset of a chunk in flight
+    uint32_t meta_end[NB];                   // ring position after it (producer only)
+    volatile int topk_ready;                 // layer + 1 whose top-8 is in topi
+    volatile int abort;                      // a wait gave up: every role unwinds
     int flag;
 };
-
-static_assert(offsetof(Smem, nw) % 16 == 0 && offsetof(Smem, ab) % 16 == 0 && offsetof(Smem, tbl_r) % 16 == 0 &&
-                  offsetof(Smem, tbl_d) % 16 == 0 && offsetof(Smem, tbl_dn) % 16 == 0 &&
-                  offsetof(Smem, hid) % 16 == 0,
-              "vector-accessed shared arrays must be 16-byte aligned");
+static_assert(sizeof(Smem) + 128 <= 232448, "decode shared memory");
+static_assert(offsetof(Smem, hid) % 16 == 0 && offsetof(Smem, u) % 16 == 0 && offsetof(Smem, tbl_r) % 16 == 0 &&
+                  offsetof(Smem, tbl_d) % 16 == 0 && offsetof(Smem, ring) % 128 == 0,
+              "vector-accessed shared arrays must be aligned");
 
 __device__ __forceinline__ const uint8_t* rp(const void* base, uint64_t off) {
     return static_cast<const uint8_t*>(base) + off;
@@ -110,305 +157,492 @@ __device__ __forceinline__ const uint8_t* rp(const void* base, uint64_t off) {
 __device__ __forceinline__ const uint16_t* rp16(const void* base, uint64_t off) {
     return reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(base) + off);
 }
+__device__ __forceinline__ int share(int n, int c, int G) { return (int)((long long)c * n / G); }
 
-__device__ __forceinline__ uint2 ldg_nc_u2(const void* p) {
-    uint2 v;
-    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint16_t ldg_nc_u16(const void* p) {
-    uint16_t v;
-    asm("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
-    return v;
-}
-// L2 prefetch hint for [p, p + bytes): one prefetch.global.L2 per 128-byte line, the warp's lanes
-// striding over the lines. Per-thread hints cost the issuing warp next to nothing, whereas a bulk
-// prefetch is a TMA operation (~64 cycles each, measured) and a warp issuing dozens of small ones
-// blocked for microseconds while the other warps waited for it at the phase's first barrier.
-__device__ __forceinline__ void prefetch_lines(const void* p, uint32_t bytes, int lane) {
-    const uint8_t* b = static_cast<const uint8_t*>(p);
-    for (uint32_t o = (uint32_t)lane * 128u; o < bytes; o += 32u * 128u)
-        asm volatile("prefetch.global.L2 [%0];" :: "l"(b + o));
-}
+__device__ __forceinline__ void csync() { tc::named_bar_sync(1, NTC); }   // the compute warps only
 
-// ---- fp16 fragments ------------------------------------------------------------------------
-// Dequantise one 32-bit word (8 int4, low nibble first) into four fp16x2 registers with one LOP3
-// each: (1024+n0, 1024+n4), (1024+16n1, 1024+16n5), (1024+n2, 1024+n6), (1024+16n3, 1024+16n7),
-// all exact in fp16. The activation table carries x for the even elements and x/16 for the odd
-// ones, so each product is 1024*x + n*x or 64*x + n*x; the per-group constant
-// C = 1024 * sum(x_even) + 64 * sum(x_odd) is subtracted once per group in fp32.
-__device__ __forceinline__ void dq_word(uint32_t w, uint32_t (&r)[4]) {
-    const uint32_t m = 0x64006400u;                         // fp16 1024.0 in both halves
-    const uint32_t w8 = w >> 8;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[0]) : "r"(w), "r"(0x000F000Fu), "r"(m));
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[1]) : "r"(w), "r"(0x00F000F0u), "r"(m));
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[2]) : "r"(w8), "r"(0x000F000Fu), "r"(m));
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r[3]) : "r"(w8), "r"(0x00F000F0u), "r"(m));
-}
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%0,%1,%2,%3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// ---- plan ------------------------------------------------------------------------------------------
+// Routed gate/up chunks: the CTA's tiles [rt0, rt1) cut at expert boundaries (every 88 tiles) and
+// into pieces of at most GU_TILES.
+__device__ __forceinline__ int rgu_next(const Plan& p, int s) {
+    return min(min(p.rt1, (s / TPE + 1) * TPE), s + GU_TILES);
+}
+__device__ void rgu_chunk(const Plan& p, int k, int& t0, int& n) {
+    int s = p.rt0;
+    for (; k > 0; --k) s = rgu_next(p, s);
+    t0 = s;
+    n = rgu_next(p, s) - s;
+}
+__device__ void rgu_locate(const Plan& p, int T, int& k, int& t0) {
+    int s = p.rt0;
+    k = 0;
+    for (;;) {
+        const int e = rgu_next(p, s);
+        if (T < e) { t0 = s; return; }
+        s = e;
+        ++k;
+    }
+}
+// First / last down item of segment q in [d0, d1) (the range holds >= 11 items, so every segment).
+__device__ __forceinline__ int seg_first(const Plan& p, int q) { return p.d0 + (q - p.d0 % NSEG + NSEG) % NSEG; }
+__device__ __forceinline__ int seg_last(const Plan& p, int q) {
+    return (p.d1 - 1) - ((p.d1 - 1) % NSEG - q + NSEG) % NSEG;
 }
 
-
-// Builds the fragment table of `groups` 64-element groups of the fp32 vector v (in shared
-// memory): for thread column t and part hl (0 = fp16 high part, 1 = low part) the 16 elements
-// 16t..16t+15 as (x0,x4)(x1,x5)(x2,x6)(x3,x7)(x8,x12)(x9,x13)(x10,x14)(x11,x15), odd elements
-// divided by 16 (exact). Also per-group sums xs (for the bias) and the offset constants cs.
-// hi + lo = b with hi = b rounded to 11 significant bits (Veltkamp split, exact in fp32) and lo =
-// b - hi; converted in pairs with one packed instruction each. hi is exact in fp16 for
-// |b| >= 2^-14; below that the fp16 conversion rounds it again (an absolute error under 2^-25).
-__device__ __forceinline__ void split11(float b, float& hi, float& lo) {
-    const float c = __fmul_rn(b, 8193.0f);
-    hi = __fsub_rn(c, __fsub_rn(c, b));
-    lo = __fsub_rn(b, hi);
+__device__ Plan make_plan(int cta, int G) {
+    Plan p;
+    p.nr = cta < NE ? (NE - 1 - cta) / G + 1 : 0;
+    p.st0 = share(TILES_S, cta, G); p.st1 = share(TILES_S, cta + 1, G);
+    p.rt0 = share(TILES_R, cta, G); p.rt1 = share(TILES_R, cta + 1, G);
+    p.d0 = share(ITEMS_DN, cta, G); p.d1 = share(ITEMS_DN, cta + 1, G);
+    p.n_sgu = (p.st1 - p.st0 + GU_TILES - 1) / GU_TILES;
+    p.n_rgu = 0;
+    for (int s = p.rt0; s < p.rt1; s = rgu_next(p, s)) ++p.n_rgu;
+    p.ot0 = p.d0 / NSEG;
+    p.sh_a = OT; p.sh_b = -1;
+    for (int q = 0; q < 3; ++q) {
+        p.sh_a = min(p.sh_a, seg_first(p, q) / NSEG);
+        p.sh_b = max(p.sh_b, seg_last(p, q) / NSEG);
+    }
+    p.c_sgu = p.nr;
+    p.c_rgu = p.c_sgu + p.n_sgu;
+    p.c_dn = p.c_rgu + p.n_rgu;
+    p.cpl = p.c_dn + 1 + TOPK;
+    return p;
 }
-__device__ __forceinline__ uint32_t cvt2(float lo_half, float hi_half) {   // (low 16 bits, high 16 bits)
-    uint32_t r;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi_half), "f"(lo_half));
-    return r;
+
+// Chunk i of a layer: ring bytes (copied; the allocation adds the 64-byte gate/up offset and rounds
+// to 128) and whether it needs the layer's top-8.
+__device__ uint32_t chunk_bytes(const Plan& p, int i) {
+    if (i < p.c_sgu) return D;
+    if (i < p.c_dn) {
+        int nt;
+        if (i < p.c_rgu) nt = min(GU_TILES, p.st1 - p.st0 - (i - p.c_sgu) * GU_TILES);
+        else { int t0; rgu_chunk(p, i - p.c_rgu, t0, nt); }
+        return (uint32_t)(8 * nt) * (2 * ROW_GU + 4 * SROW_GU);
+    }
+    if (i == p.c_dn) return (uint32_t)(16 * (p.sh_b - p.sh_a + 1)) * (DROW_S + 2 * SROW_S);
+    const int q = 3 + (i - p.c_dn - 1);
+    return (uint32_t)(16 * (seg_last(p, q) / NSEG - seg_first(p, q) / NSEG + 1)) * (DROW_R + 2 * SROW_R);
 }
 
-// nv (1 or 2) tables in one pass: items [0, 4 groups) build table 0, [4 groups, 8 groups) table 1
-// (4 groups is a multiple of 4, so no 4-lane shuffle group straddles the two)
-__device__ void build_tables(int nv, int groups, const float* v0, uint32_t* tbl0, float* xs0, float* cs0,
-                             const float* v1, uint32_t* tbl1, float* xs1, float* cs1, bool from_global = false) {
-    // one thread per (group j, thread column t): both parts of its 16 elements, then the group's
-    // sums over the 4 columns (adjacent lanes). Items past the last table read row 0 of table 0.
-    for (int i2 = threadIdx.x; i2 < ((nv * groups * 4 + 31) & ~31); i2 += blockDim.x) {
-        const bool on = i2 < nv * groups * 4;
-        const bool second = on && i2 >= groups * 4;
-        const int i = second ? i2 - groups * 4 : i2;
-        const float* v = second ? v1 : v0;
-        uint32_t* tbl = second ? tbl1 : tbl0;
-        float* xs = second ? xs1 : xs0;
-        float* cs = second ? cs1 : cs0;
-        const int j = on ? i >> 2 : 0, t = i & 3;
-        const float4* src = reinterpret_cast<const float4*>(v + j * 64 + t * 16);
-        float x[16], hi[16], lo[16];
+// ---- mbarrier waits --------------------------------------------------------------------------------
+// Bounded wait on a chunk barrier (every lane of the calling warp); false on timeout or abort.
+__device__ bool wait_bar(Smem& s, const Params& P, uint64_t* bar, uint32_t parity) {
+    if (tc::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (tc::mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (s.abort) return false;
+        if (globaltimer_ns() - t0 > P.wait_limit_ns) {
+            s.abort = 1;
+            atomicExch(P.err, 1);
+            atomicExch(P.sticky, 1);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ bool wait_full(Smem& s, const Params& P, int c) {
+    return wait_bar(s, P, &s.full[c % NB], (uint32_t)(c / NB) & 1u);
+}
+// This warp is done with chunks [cur, c): each is waited for (a warp that never read it still
+// waits, so a released chunk has always landed) and released; then chunk c is waited for.
+__device__ bool advance_to(Smem& s, const Params& P, int& cur, int c) {
+    const int lane = threadIdx.x & 31;
+    for (; cur < c; ++cur) {
+        if (!wait_full(s, P, cur)) return false;
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&s.empty[cur % NB]);
+    }
+    return wait_full(s, P, c);
+}
+__device__ __forceinline__ bool release_to(Smem& s, const Params& P, int& cur, int c_end) {
+    const int lane = threadIdx.x & 31;
+    for (; cur < c_end; ++cur) {
+        if (!wait_full(s, P, cur)) return false;
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&s.empty[cur % NB]);
+    }
+    return true;
+}
+
+// ---- producer warp ---------------------------------------------------------------------------------
+__device__ void producer(Smem& s, const Params& P, const Plan& p) {
+    if ((threadIdx.x & 31) != 0) return;
+    uint32_t head = 0, tail = 0;
+    int issued = 0, released = 0;
+    int tk[TOPK] = {0, 0, 0, 0, 0, 0, 0, 0};
+    bool ok = true;
+    const int cta = blockIdx.x, G = gridDim.x;
+    for (int l = 0; l < P.num_layers && ok; ++l) {
+        const GtmLayer& L = P.layers[l];
+        const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
+        for (int i = 0; i < p.cpl && ok; ++i) {
+            if (i == p.c_rgu) {   // the routed chunks follow: wait for this layer's top-8
+                const uint64_t t0 = globaltimer_ns();
+                while (s.topk_ready < l + 1) {
+                    if (s.abort) { ok = false; break; }
+                    if (globaltimer_ns() - t0 > P.wait_limit_ns) {
+                        s.abort = 1; atomicExch(P.err, 1); atomicExch(P.sticky, 1);
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+                if (!ok) break;
+                __threadfence_block();
+#pragma unroll
+                for (int k = 0; k < TOPK; ++k) tk[k] = s.topi[k];
+            }
+            const uint32_t bytes = chunk_bytes(p, i);
+            const uint32_t alloc = (bytes + 64 + 127) & ~127u;
+            uint32_t pos = head % RING;
+            if (pos + alloc > RING) { head += RING - pos; pos = 0; }
+            while (head + alloc - tail > RING || issued - released >= NB) {
+                if (!wait_bar(s, P, &s.empty[released % NB], (uint32_t)(released / NB) & 1u)) { ok = false; break; }
+                tail = s.meta_end[released % NB];
+                ++released;
+            }
+            if (!ok) break;
+            const int slot = issued % NB;
+            s.meta[slot] = pos;
+            s.meta_end[slot] = head + alloc;
+            head += alloc;
+            uint64_t* bar = &s.full[slot];
+            uint8_t* dst = s.ring + pos;
+            tc::mbar_arrive_expect_tx(bar, bytes);
+            if (i < p.c_sgu) {
+                const int row = cta + i * G;
+                tc::bulk_load(dst, res + L.router.weight + (uint64_t)row * D, D, bar);
+            } else if (i < p.c_dn) {
+                const bool routed = i >= p.c_rgu;
+                int t0, nt;
+                if (!routed) { t0 = p.st0 + (i - p.c_sgu) * GU_TILES; nt = min(GU_TILES, p.st1 - t0); }
+                else rgu_chunk(p, i - p.c_rgu, t0, nt);
+                const uint8_t* base = res;
+                const GtmQuant *qg = &L.shared_gate, *qu = &L.shared_up;
+                int f0 = 8 * t0;
+                if (routed) {
+                    base = rp(L.experts_dev, (uint64_t)tk[t0 / TPE] * L.expert_stride);
+                    qg = &L.expert_gate;
+                    qu = &L.expert_up;
+                    f0 = 8 * (t0 % TPE);
+                }
+                const uint32_t F = 8 * nt, wb = F * ROW_GU, sb = F * SROW_GU;
+                tc::bulk_load(dst, base + qg->weight + (uint64_t)f0 * ROW_GU, wb, bar);
+                tc::bulk_load(dst + wb + 64, base + qu->weight + (uint64_t)f0 * ROW_GU, wb, bar);
+                uint8_t* sd = dst + 2 * wb + 64;
+                tc::bulk_load(sd, base + qg->scales + (uint64_t)f0 * SROW_GU, sb, bar);
+                tc::bulk_load(sd + sb, base + qg->biases + (uint64_t)f0 * SROW_GU, sb, bar);
+                tc::bulk_load(sd + 2 * sb, base + qu->scales + (uint64_t)f0 * SROW_GU, sb, bar);
+                tc::bulk_load(sd + 3 * sb, base + qu->biases + (uint64_t)f0 * SROW_GU, sb, bar);
+            } else if (i == p.c_dn) {
+                const uint32_t R = 16 * (p.sh_b - p.sh_a + 1), r0 = 16 * p.sh_a;
+                tc::bulk_load(dst, res + L.shared_down.weight + (uint64_t)r0 * DROW_S, R * DROW_S, bar);
+                tc::bulk_load(dst + R * DROW_S, res + L.shared_down.scales + (uint64_t)r0 * SROW_S, R * SROW_S, bar);
+                tc::bulk_load(dst + R * (DROW_S + SROW_S), res + L.shared_down.biases + (uint64_t)r0 * SROW_S,
+                              R * SROW_S, bar);
+            } else {
+                const int q = 3 + (i - p.c_dn - 1);
+                const int a = seg_first(p, q) / NSEG, b = seg_last(p, q) / NSEG;
+                const uint32_t R = 16 * (b - a + 1), r0 = 16 * a;
+                const uint8_t* blk = rp(L.experts_dev, (uint64_t)tk[q - 3] * L.expert_stride);
+                tc::bulk_load(dst, blk + L.expert_down.weight + (uint64_t)r0 * DROW_R, R * DROW_R, bar);
+                tc::bulk_load(dst + R * DROW_R, blk + L.expert_down.scales + (uint64_t)r0 * SROW_R, R * SROW_R, bar);
+                tc::bulk_load(dst + R * (DROW_R + SROW_R), blk + L.expert_down.biases + (uint64_t)r0 * SROW_R,
+                              R * SROW_R, bar);
+            }
+            ++issued;
+        }
+    }
+    // no exit while bulk copies into this CTA's shared memory are in flight: the chunks not yet
+    // released may still be landing (released ones have been waited for by every compute warp)
+    const uint64_t t0 = globaltimer_ns();
+    for (int j = released; j < issued; ++j)
+        while (!tc::mbar_try_wait_sleep(&s.full[j % NB], (uint32_t)(j / NB) & 1u, 20000u))
+            if (globaltimer_ns() - t0 > P.wait_limit_ns) return;
+}
+
+// ---- fragment tables -----------------------------------------------------------------------------
+// Table of a vector, per quad Q and double group h: 12 lane entries of 8 words at (2 Q + h) * 96
+// + e * 8, one per lane (g, t) that holds nonzero B values: g = 4 a + limb (limb < 3) with a = t >> 1
+// (the lane pair of group 2 h + a), e = 6 a + 2 limb + (t & 1). Words 2 w, 2 w + 1 of the entry are
+// the lane's b0, b1 for the MMA of word w: limb `limb` of the elements 128 h + 32 t + 8 w + {0, 2,
+// 4, 6} and {1, 3, 5, 7} of the quad, one signed byte each (K slot 4 t + i and 4 t + 16 + i hold
+// nibbles 2 i and 2 i + 1 of the lane's word w). The 12 reading lanes of a double group take 384
+// consecutive bytes.
+// One builder thread per (group j, sub): the 16 elements 16 sub + (0..15) of the group, i.e. words
+// 2 (sub & 1) and 2 (sub & 1) + 1 of lane t = 2 (j & 1) + (sub >> 1) of the group's double group;
+// the four builder lanes of a group (adjacent) share its largest magnitude and its sum.
+// The low bytes of four words, a in the lowest.
+__device__ __forceinline__ uint32_t pack_s8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+__device__ __forceinline__ void table_item(const float (&x)[16], bool on, uint32_t* tbl_q, int gq, int sub,
+                                           float2* gs, int j) {
+    float mx = 0.0f, sx = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) { mx = fmaxf(mx, fabsf(x[e])); sx += x[e]; }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+    sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+    // |x| < 2^E for the group (exponent field of the largest magnitude, minus 126), kept >= -120
+    const int E = max((int)((__float_as_uint(mx) >> 23) & 0xFFu) - 126, -120);
+    const float up = __int_as_float((127 + 6 - E) << 23);     // 2^(6-E): |x up| < 64
+    // round to nearest even by adding 1.5 * 2^23 (|v| <= 64): the sum's low mantissa bits are the
+    // integer, whose low byte is the limb in two's complement; all steps are exact
+    constexpr float kMagic = 12582912.0f;
+    uint32_t L[3][16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        const float v = x[e] * up;                            // exact (power of two)
+        const float f0 = v + kMagic;
+        const float v1 = (v - (f0 - kMagic)) * 128.0f;        // exact; |v1| <= 64
+        const float f1 = v1 + kMagic;
+        const float f2 = (v1 - (f1 - kMagic)) * 128.0f + kMagic;
+        L[0][e] = __float_as_uint(f0);
+        L[1][e] = __float_as_uint(f1);
+        L[2][e] = __float_as_uint(f2);
+    }
+    const int h = gq >> 1, a = gq & 1, tl = sub >> 1, wp = sub & 1;
+    uint32_t* base = tbl_q + h * 96;
+    if (on) {
+#pragma unroll
+        for (int limb = 0; limb < 3; ++limb) {
+            uint32_t* ent = base + (6 * a + 2 * limb + tl) * 8;
+#pragma unroll
+            for (int ww = 0; ww < 2; ++ww) {
+                const int b = 8 * ww;
+                ent[2 * (2 * wp + ww)] = pack_s8(L[limb][b], L[limb][b + 2], L[limb][b + 4], L[limb][b + 6]);
+                ent[2 * (2 * wp + ww) + 1] = pack_s8(L[limb][b + 1], L[limb][b + 3], L[limb][b + 5], L[limb][b + 7]);
+            }
+        }
+        if (sub == 0) gs[j] = make_float2(sx, __int_as_float((127 + E - 6) << 23));
+    }
+}
+
+// Tables of routed_x (ab[0, D)) and dense_x (ab[D, 2D)): 2 x 176 items (whole warps take part in
+// the builder's shuffles; threads past the items compute item 0 and store nothing).
+__device__ void build_views_tables(Smem& s) {
+    constexpr int N = 2 * 4 * GD;
+    const int i0 = threadIdx.x;
+    if (i0 < ((N + 31) & ~31)) {
+        const bool on = i0 < N;
+        const int i = on ? i0 : (i0 & 3);
+        const int v = i / (4 * GD), k = i - v * 4 * GD, j = k >> 2, sub = k & 3;
+        const float* src = s.u.t.ab + v * D + j * kGroup + 16 * sub;
+        float x[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            // global sources were written by other CTAs in this launch: read them from L2
-            const float4 f = from_global ? __ldcg(src + q) : src[q];
+            const float4 f = reinterpret_cast<const float4*>(src)[q];
             x[4 * q] = f.x; x[4 * q + 1] = f.y; x[4 * q + 2] = f.z; x[4 * q + 3] = f.w;
         }
+        uint32_t* tbl = v ? s.tbl_d : s.tbl_r;
+        table_item(x, on, tbl + (j >> 2) * QW, j & 3, sub, v ? s.gs_d : s.gs_r, j);
+    }
+}
+
+// Tables of the 11 down segments (act[704 q, 704 q + 704), written by every CTA before barrier B,
+// read from L2): 11 x 12 groups x 4 items; group 11 of a segment (past its 704 inputs) is zero.
+__device__ void build_down_tables(Smem& s, const Params& P) {
+    constexpr int N = NSEG * 12 * 4;
+    const int i0 = threadIdx.x;
+    if (i0 < ((N + 31) & ~31)) {
+        const bool on = i0 < N;
+        const int i = on ? i0 : (i0 & 3);
+        const int q = i / 48, k = i - q * 48, j = k >> 2, sub = k & 3;
+        float x[16];
+        if (j < GFE) {
+            const float4* src = reinterpret_cast<const float4*>(P.act + q * FE + j * kGroup + 16 * sub);
 #pragma unroll
-        for (int q = 0; q < 16; ++q) split11((q & 1) ? x[q] * 0.0625f : x[q], hi[q], lo[q]);
-        // pairs (x0,x4)(x1,x5)(x2,x6)(x3,x7) | (x8,x12)(x9,x13)(x10,x14)(x11,x15)
-        const uint4 h0 = make_uint4(cvt2(hi[0], hi[4]), cvt2(hi[1], hi[5]), cvt2(hi[2], hi[6]), cvt2(hi[3], hi[7]));
-        const uint4 h1 = make_uint4(cvt2(hi[8], hi[12]), cvt2(hi[9], hi[13]), cvt2(hi[10], hi[14]), cvt2(hi[11], hi[15]));
-        const uint4 l0 = make_uint4(cvt2(lo[0], lo[4]), cvt2(lo[1], lo[5]), cvt2(lo[2], lo[6]), cvt2(lo[3], lo[7]));
-        const uint4 l1 = make_uint4(cvt2(lo[8], lo[12]), cvt2(lo[9], lo[13]), cvt2(lo[10], lo[14]), cvt2(lo[11], lo[15]));
-        float sx = 0.0f, c = 0.0f;
-        if (on) {
-            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 0) * 8 + t * 2 + 0) * 4) = h0;
-            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 1) * 8 + t * 2 + 0) * 4) = h1;
-            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 0) * 8 + t * 2 + 1) * 4) = l0;
-            *reinterpret_cast<uint4*>(tbl + ((j * 2 + 1) * 8 + t * 2 + 1) * 4) = l1;
-            // what the MMA adds besides n*x: 1024 * (hi + lo) as the fp16 operands hold them
-            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-            const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float2 fh = __half22float2(*reinterpret_cast<const __half2*>(&hw[q]));
-                const float2 fl = __half22float2(*reinterpret_cast<const __half2*>(&lw[q]));
-                c += 1024.0f * ((fh.x + fl.x) + (fh.y + fl.y));
+            for (int c = 0; c < 4; ++c) {
+                const float4 f = __ldcg(src + c);
+                x[4 * c] = f.x; x[4 * c + 1] = f.y; x[4 * c + 2] = f.z; x[4 * c + 3] = f.w;
             }
+        } else {
 #pragma unroll
-            for (int q = 0; q < 16; ++q) sx += x[q];
+            for (int e = 0; e < 16; ++e) x[e] = 0.0f;
         }
-        sx += __shfl_xor_sync(0xffffffffu, sx, 1);
-        sx += __shfl_xor_sync(0xffffffffu, sx, 2);
-        c += __shfl_xor_sync(0xffffffffu, c, 1);
-        c += __shfl_xor_sync(0xffffffffu, c, 2);
-        if (on && t == 0) { xs[j] = sx; cs[j] = c; }
+        table_item(x, on, s.u.tbl_dn + q * QS * QW + (j >> 2) * QW, j & 3, sub, s.gs_dn + q * 12, j);
     }
 }
 
-__device__ void build_table(const float* v, int groups, uint32_t* tbl, float* xs, float* cs) {
-    build_tables(1, groups, v, tbl, xs, cs, v, tbl, xs, cs);
-}
-
-// One warp: groups [j0, j1) of a 16-row tile. Rows g (pointer set a) and g + 8 (set b); lane
-// (g, t = 0) accumulates y_a (row g) and y_b (row g + 8).
-struct TileRows {
-    const uint8_t* wa;     // row g, byte 0 of group 0
-    const uint8_t* wb;     // row g + 8
-    const uint16_t* sa;    // scales of row g
-    const uint16_t* ba;
-    const uint16_t* sb;
-    const uint16_t* bb;
-};
-
-// Groups are taken four at a time: group q0 + m puts its activation in B columns 2m (fp16 high
-// part) and 2m + 1 (low part), so after the quad lane (g, t) holds group q0 + t's products for
-// rows g and g + 8 and applies that group's scale, bias and offset constant. The per-lane sums
-// cover the groups congruent to t mod 4; the caller adds the four lanes of a row.
-// Global loads of one quad: the 4 groups' weight words for rows g and g + 8 (always from a valid
-// group of the run) and this lane's group's scales and biases.
-struct QuadLoads {
-    uint2 wa[4], wb[4];
-    uint16_t sa, ba, sb, bb;
-};
-
-__device__ __forceinline__ QuadLoads load_quad(const TileRows& R, int q0, int j0, int j1, int t) {
-    QuadLoads Q;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const int j = q0 + m;
-        const int jc = (j >= j0 && j < j1) ? j : j0;
-        Q.wa[m] = ldg_nc_u2(R.wa + 32 * jc + 8 * t);
-        Q.wb[m] = ldg_nc_u2(R.wb + 32 * jc + 8 * t);
-    }
-    const int j = q0 + t;
-    const int jc = (j >= j0 && j < j1) ? j : j0;
-    Q.sa = ldg_nc_u16(R.sa + jc);
-    Q.ba = ldg_nc_u16(R.ba + jc);
-    Q.sb = ldg_nc_u16(R.sb + jc);
-    Q.bb = ldg_nc_u16(R.bb + jc);
-    return Q;
-}
-
-__device__ __forceinline__ void compute_quad(const QuadLoads& Q, int q0, int j0, int j1, const uint32_t* tbl,
-                                             const float* xs, const float* cs, float& ya, float& yb) {
+// ---- int4 tile products --------------------------------------------------------------------------
+// One warp: groups [j0, j1) of a 16-row tile. ra / rb: row g / g + 8 of lane (g, t), at group 0 of
+// the K range; sa, ba, sb, bb: their bf16 scales and biases at group 0; gs: per group (sum of x,
+// 2^(E-6)). Lanes t = 0 and 2 accumulate groups 4Q + {0, 2} and 4Q + {1, 3} of each quad into ya
+// (row g) and yb (row g + 8); the caller adds the 4 lanes of a row.
+__device__ __forceinline__ void tile_groups(const uint8_t* ra, const uint8_t* rb, const uint16_t* sa, const uint16_t* ba,
+                                            const uint16_t* sb, const uint16_t* bb, int j0, int j1,
+                                            const uint32_t* tbl, const float2* gs, float& ya, float& yb) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int slotn = t * 2 + (g & 1);
-    float dE[4] = {0.0f, 0.0f, 0.0f, 0.0f}, dO[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const bool entry = (g & 3) < 3 && (g >> 2) == (t >> 1);
+    const int e = 6 * (t >> 1) + 2 * (g & 3) + (t & 1);
+    for (int Q = j0 >> 2; Q * 4 < j1; ++Q) {
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const int j = q0 + m;
-        const bool on = j >= j0 && j < j1;           // warp-uniform
-        uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = make_uint4(0u, 0u, 0u, 0u);
-        if (on && (g >> 1) == m) {
-            b0 = *reinterpret_cast<const uint4*>(tbl + ((j * 2 + 0) * 8 + slotn) * 4);
-            b1 = *reinterpret_cast<const uint4*>(tbl + ((j * 2 + 1) * 8 + slotn) * 4);
+        for (int h = 0; h < 2; ++h) {
+            const int j = 4 * Q + 2 * h + (t >> 1);   // the group of this lane's K slots and B entry
+            if (4 * Q + 2 * h + 1 < j0 || 4 * Q + 2 * h >= j1) continue;   // warp-uniform
+            const uint4 wa = lds128(ra + 128 * Q + 64 * h + 16 * t);
+            const uint4 wb = lds128(rb + 128 * Q + 64 * h + 16 * t);
+            uint4 b01 = make_uint4(0u, 0u, 0u, 0u), b23 = b01;
+            if (entry && j >= j0 && j < j1) {
+                const uint32_t* ep = tbl + (2 * Q + h) * 96 + e * 8;
+                b01 = lds128(ep);
+                b23 = lds128(ep + 4);
+            }
+            const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w}, wB[4] = {wb.x, wb.y, wb.z, wb.w};
+            const uint32_t bw[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
+            int d[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+                mma_u8s8(d, wA[w] & 0x0F0F0F0Fu, wB[w] & 0x0F0F0F0Fu, (wA[w] >> 4) & 0x0F0F0F0Fu, (wB[w] >> 4) & 0x0F0F0F0Fu,
+                         bw[2 * w], bw[2 * w + 1]);
+            // columns 2t, 2t + 1: lane t even holds limbs 0, 1 of its group, t odd limb 2 (and a zero column)
+            float pa = (t & 1) ? (float)d[0] * 6.103515625e-05f : fmaf((float)d[1], 0.0078125f, (float)d[0]);
+            float pb = (t & 1) ? (float)d[2] * 6.103515625e-05f : fmaf((float)d[3], 0.0078125f, (float)d[2]);
+            pa += __shfl_xor_sync(0xffffffffu, pa, 1);
+            pb += __shfl_xor_sync(0xffffffffu, pb, 1);
+            if (!(t & 1) && j >= j0 && j < j1) {
+                const float2 gj = gs[j];
+                ya = fmaf(bf16f(ba[j]), gj.x, fmaf(bf16f(sa[j]) * gj.y, pa, ya));
+                yb = fmaf(bf16f(bb[j]), gj.x, fmaf(bf16f(sb[j]) * gj.y, pb, yb));
+            }
         }
-        uint32_t qa0[4], qa1[4], qb0[4], qb1[4];
-        dq_word(Q.wa[m].x, qa0);
-        dq_word(Q.wa[m].y, qa1);
-        dq_word(Q.wb[m].x, qb0);
-        dq_word(Q.wb[m].y, qb1);
-        float (&d)[4] = (m & 1) ? dO : dE;
-        mma16816(d, qa0[0], qb0[0], qa0[1], qb0[1], b0.x, b0.y);
-        mma16816(d, qa0[2], qb0[2], qa0[3], qb0[3], b0.z, b0.w);
-        mma16816(d, qa1[0], qb1[0], qa1[1], qb1[1], b1.x, b1.y);
-        mma16816(d, qa1[2], qb1[2], qa1[3], qb1[3], b1.z, b1.w);
-    }
-    const int j = q0 + t;
-    if (j >= j0 && j < j1) {
-        const float x = xs[j], c = cs[j];
-        ya = fmaf(bf16f(Q.ba), x, fmaf(bf16f(Q.sa), ((dE[0] + dO[0]) + (dE[1] + dO[1])) - c, ya));
-        yb = fmaf(bf16f(Q.bb), x, fmaf(bf16f(Q.sb), ((dE[2] + dO[2]) + (dE[3] + dO[3])) - c, yb));
     }
 }
 
-// Loads of the next quad are issued before the current one is computed, so each warp keeps two
-// quads (4 KB of weights) in flight.
-__device__ __forceinline__ void gemv_groups(const TileRows& R, int j0, int j1, const uint32_t* tbl, const float* xs,
-                                            const float* cs, float& ya, float& yb) {
-    const int t = threadIdx.x & 3;
-    int q0 = j0 & ~3;
-    QuadLoads cur = load_quad(R, q0, j0, j1, t);
-    for (; q0 < j1; q0 += 4) {
-        QuadLoads nxt = cur;
-        if (q0 + 4 < j1) nxt = load_quad(R, q0 + 4, j0, j1, t);
-        compute_quad(cur, q0, j0, j1, tbl, xs, cs, ya, yb);
-        cur = nxt;
-    }
-}
+// The warps' split of n_items x L (item, group) pairs: warp w takes pairs [pw0(w), pw0(w + 1)).
+__device__ __forceinline__ int pw0(int w, int total) { return w * total / NWC; }   // total <= 1024
 
-// Splits n_items x L groups evenly over the CTA's warps; each warp walks its contiguous run of
-// (item, group) pairs and leaves one partial per item it touched in s.slot[item][warp].
-template <class RowsFn>
-__device__ __forceinline__ void warp_items(Smem& s, int slot_base, int n_items, int L, int jbase, const uint32_t* tbl,
-                                           const float* xs, const float* cs, RowsFn rows_of) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int total = n_items * L;
-    int p = warp * total / NW;
-    const int p1 = (warp + 1) * total / NW;
-    while (p < p1) {
-        const int item = p / L, j0 = p - item * L;
-        const int j1 = min(L, j0 + (p1 - p));
-        const TileRows R = rows_of(item);
-        float ya = 0.0f, yb = 0.0f;
-        gemv_groups(R, jbase + j0, jbase + j1, tbl, xs, cs, ya, yb);
-        ya += __shfl_xor_sync(0xffffffffu, ya, 1);
-        ya += __shfl_xor_sync(0xffffffffu, ya, 2);
-        yb += __shfl_xor_sync(0xffffffffu, yb, 1);
-        yb += __shfl_xor_sync(0xffffffffu, yb, 2);
-        if (t == 0) {
-            s.slot[slot_base + item][warp][g] = ya;
-            s.slot[slot_base + item][warp][8 + g] = yb;
-        }
-        p += j1 - j0;
-    }
-}
-
-// As warp_items, with each item's own table and K-group base (the down phase mixes segments).
-struct ItemSrc {
-    TileRows R;
-    const uint32_t* tbl;
-    const float* xs;
-    const float* cs;
-    int jbase;
+// Warps that work on item i: from the last warp whose range starts at or before pair i L, i.e.
+// ceil((i L + 1) NWC / total) - 1, to the one holding pair (i + 1) L - 1. A warp's range holds at
+// least floor(total / NWC) pairs, so at most max_k = ceil((L - 1) / floor(total / NWC)) + 1 warps
+// share an item; warp w keeps its partial of item i in slot [(i max_k + w - first(i)) 16 + row].
+struct Split {
+    int total, max_k;
 };
-template <class SrcFn>
-__device__ __forceinline__ void warp_items_src(Smem& s, int n_items, int L, SrcFn src_of) {
+__device__ __forceinline__ Split make_split(int n, int L) {
+    Split sp;
+    sp.total = n * L;
+    const int ppw = sp.total / NWC;
+    sp.max_k = ppw > 0 ? (L - 1 + ppw - 1) / ppw + 1 : NWC;
+    return sp;
+}
+__device__ __forceinline__ int first_warp(const Split& sp, int i, int L) {
+    return ((i * L + 1) * NWC + sp.total - 1) / sp.total - 1;
+}
+// Sum of item i's partials for tile row r, in warp order.
+__device__ __forceinline__ float item_sum(const Smem& s, const Split& sp, int i, int L, int r) {
+    const int last = min(NWC - 1, ((i + 1) * L * NWC + sp.total - 1) / sp.total - 1);   // holds pair (i + 1) L - 1
+    const int k_end = last - first_warp(sp, i, L) + 1;
+    const float* p = s.slot + (i * sp.max_k) * 16 + r;
+    float v = 0.0f;
+    for (int k = 0; k < k_end; ++k) v += p[16 * k];
+    return v;
+}
+__device__ __forceinline__ float* slot_of(Smem& s, const Split& sp, int i, int L, int warp) {
+    return s.slot + (i * sp.max_k + warp - first_warp(sp, i, L)) * 16;
+}
+
+// Source rows of one 16-row tile for tile_groups.
+struct TileSrc {
+    const uint8_t* ra; const uint8_t* rb;
+    const uint16_t* sa; const uint16_t* ba; const uint16_t* sb; const uint16_t* bb;
+    const uint32_t* tbl; const float2* gs;
+};
+
+// Gate/up tile lt of a chunk of F features per matrix at `base`: rows 0-3 gate f0..3, 4-7 up f0..3,
+// 8-11 gate f0+4..7, 12-15 up f0+4..7 (f0 = 8 lt within the chunk).
+__device__ __forceinline__ TileSrc gu_src(const uint8_t* base, int F, int lt, const uint32_t* tbl, const float2* gs) {
+    const int g = (threadIdx.x & 31) >> 2;
+    const bool up = g >= 4;
+    const int r = 8 * lt + (g & 3);
+    const uint32_t wb = (uint32_t)F * ROW_GU, sbytes = (uint32_t)F * SROW_GU;
+    const uint8_t* w = base + (up ? wb + 64 : 0);
+    const uint8_t* sc = base + 2 * wb + 64 + (up ? 2 * sbytes : 0);
+    TileSrc S;
+    S.ra = w + (uint32_t)r * ROW_GU;
+    S.rb = S.ra + 4 * ROW_GU;
+    S.sa = reinterpret_cast<const uint16_t*>(sc) + r * GD;
+    S.ba = reinterpret_cast<const uint16_t*>(sc + sbytes) + r * GD;
+    S.sb = S.sa + 4 * GD;
+    S.bb = S.ba + 4 * GD;
+    S.tbl = tbl; S.gs = gs;
+    return S;
+}
+
+// One phase of gate/up tiles [t_first, t_first + n): locate(tile) gives (chunk index c, first tile of
+// the chunk, tiles in the chunk). Every warp works its pairs, then releases the phase's chunks
+// [c_begin, c_end). Returns false when a wait gave up.
+template <class Locate>
+__device__ bool gu_phase(Smem& s, const Params& P, int n, int c_begin, int c_end, const uint32_t* tbl, const float2* gs,
+                         Locate locate) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int total = n_items * L;
-    int p = warp * total / NW;
-    const int p1 = (warp + 1) * total / NW;
+    const Split sp = make_split(n, GD);
+    int p = pw0(warp, sp.total);
+    const int p1 = pw0(warp + 1, sp.total);
+    int cur = c_begin;
+    bool ok = true;
     while (p < p1) {
-        const int item = p / L, j0 = p - item * L;
-        const int j1 = min(L, j0 + (p1 - p));
-        const ItemSrc S = src_of(item);
+        const int item = p / GD, j0 = p - item * GD, j1 = min(GD, j0 + (p1 - p));
+        int c, lt, F;
+        locate(item, c, lt, F);
+        if (!advance_to(s, P, cur, c)) { ok = false; break; }
+        const TileSrc S = gu_src(s.ring + s.meta[c % NB], F, lt, tbl, gs);
         float ya = 0.0f, yb = 0.0f;
-        gemv_groups(S.R, S.jbase + j0, S.jbase + j1, S.tbl, S.xs, S.cs, ya, yb);
+        tile_groups(S.ra, S.rb, S.sa, S.ba, S.sb, S.bb, j0, j1, S.tbl, S.gs, ya, yb);
         ya += __shfl_xor_sync(0xffffffffu, ya, 1);
         ya += __shfl_xor_sync(0xffffffffu, ya, 2);
         yb += __shfl_xor_sync(0xffffffffu, yb, 1);
         yb += __shfl_xor_sync(0xffffffffu, yb, 2);
         if (t == 0) {
-            s.slot[item][warp][g] = ya;
-            s.slot[item][warp][8 + g] = yb;
+            float* sl = slot_of(s, sp, item, GD, warp);
+            sl[g] = ya;
+            sl[8 + g] = yb;
         }
         p += j1 - j0;
     }
-}
-
-__device__ __forceinline__ void zero_slots(Smem& s, int n_items) {
-    float* f = &s.slot[0][0][0];
-    for (int i = threadIdx.x; i < n_items * NW * 16; i += blockDim.x) f[i] = 0.0f;
-}
-
-__device__ __forceinline__ float slot_sum(const Smem& s, int item, int r) {
-    float v = 0.0f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) v += s.slot[item][w][r];
-    return v;
+    if (ok) ok = release_to(s, P, cur, c_end);
+    return ok;
 }
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
     return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
 }
 
-// ---- barriers ------------------------------------------------------------------------------
-__device__ __forceinline__ void arrive(const Params& P, int kind, unsigned value) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        st_release(P.flags + kind * 256 + blockIdx.x, value);
+// GeGLU of the phase's n tiles -> act[off + 8 * (first + item) + f].
+__device__ void gu_epilogue(const Smem& s, float* act, int n) {
+    const Split sp = make_split(n, GD);
+    for (int i = threadIdx.x; i < n * 8; i += NTC) {
+        const int item = i >> 3, f = i & 7;
+        const int rg = (f & 3) + 8 * (f >> 2);
+        const float gt = item_sum(s, sp, item, GD, rg), up = item_sum(s, sp, item, GD, rg + 4);
+        act[8 * item + f] = gelu_tanh_f(gt) * up;
     }
 }
 
-__device__ bool wait_all(const Params& P, Smem& s, int kind, unsigned value) {
+// ---- barriers ----------------------------------------------------------------------------------
+// The CTA's writes before the barrier are ordered before the flag by the release store (its fence
+// is cumulative over the writes the barrier made visible to thread 0).
+__device__ __forceinline__ void arrive(const Params& P, unsigned* flags, unsigned value) {
+    csync();
+    if (threadIdx.x == 0) st_release(flags + blockIdx.x, value);
+}
+
+// Warp 0 polls every CTA's flag; the other compute warps wait at the named barrier.
+__device__ bool wait_all(Smem& s, const Params& P, const unsigned* f, unsigned value) {
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        const unsigned* f = P.flags + kind * 256;
         const uint64_t t0 = globaltimer_ns();
         bool ok = true;
         for (;;) {
@@ -424,39 +658,58 @@ __device__ bool wait_all(const Params& P, Smem& s, int kind, unsigned value) {
             }
         }
         __threadfence();
-        if (lane == 0) s.flag = ok ? 0 : 1;
+        if (lane == 0) { s.flag = ok ? 0 : 1; if (!ok) s.abort = 1; }
     }
-    __syncthreads();
+    csync();
     return s.flag == 0;
 }
 
-// ---- P1 pieces ----------------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(sa), "l"(gmem) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// A logit word carries its own payload (layer number and value in one 64-bit store), so it needs
+// no release ordering.
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
 }
 
-// Starts copying norm vectors into s.nw: the pre-FFN set (pre_ffn_norm, pre_ffn_norm_2,
-// router.scale) of layer Lpre into slots 0..2 and the post-FFN set (post_ffn_norm_1, _2, and
-// post_ffn_norm) of layer Lpost into slots 3..5; either may be null. Completed by
-// tail_and_views.
-__device__ void load_norms_async(Smem& s, const GtmLayer* Lpre, const GtmLayer* Lpost) {
-    constexpr int per = D * 2 / 16;   // 16-byte chunks per vector
-    for (int i = threadIdx.x; i < 6 * per; i += NT) {
-        const int v = i / per, c = i - v * per;
-        const GtmLayer* L = v < 3 ? Lpre : Lpost;
-        if (!L) continue;
-        const uint64_t off = v == 0 ? L->pre_ffn_norm : v == 1 ? L->pre_ffn_norm_2 : v == 2 ? L->router_scale
-                           : v == 3 ? L->post_ffn_norm_1 : v == 4 ? L->post_ffn_norm_2 : L->post_ffn_norm;
-        cp_async16(&s.nw[v][c * 8], rp(L->resident_dev, off) + c * 16);
+// ---- layer tail and views --------------------------------------------------------------------------
+// Norm vectors of one compute thread's four elements (4 bf16 each), loaded before the tail's wait.
+struct Norms {
+    uint2 w1, w2, w3;       // post_ffn_norm_1, post_ffn_norm_2, post_ffn_norm of the previous layer
+    uint2 pre, pre2, rsc;   // pre_ffn_norm, pre_ffn_norm_2, router.scale of this layer
+    float ls;               // layer_scalar of the previous layer
+};
+__device__ __forceinline__ uint2 ldg_u2(const void* base, uint64_t off, int i) {
+    return __ldg(reinterpret_cast<const uint2*>(rp(base, off)) + i);
+}
+__device__ Norms load_norms(const GtmLayer* Lp, const GtmLayer* L) {
+    Norms n;
+    const int i = threadIdx.x;
+    n.w1 = n.w2 = n.w3 = n.pre = n.pre2 = n.rsc = make_uint2(0u, 0u);
+    n.ls = 0.0f;
+    if (Lp) {
+        n.w1 = ldg_u2(Lp->resident_dev, Lp->post_ffn_norm_1, i);
+        n.w2 = ldg_u2(Lp->resident_dev, Lp->post_ffn_norm_2, i);
+        n.w3 = ldg_u2(Lp->resident_dev, Lp->post_ffn_norm, i);
+        n.ls = bf16f(__ldg(rp16(Lp->resident_dev, Lp->layer_scalar)));
     }
-    if (Lpre && threadIdx.x < NE * 2 / 16)
-        cp_async16(&s.pes[threadIdx.x * 8], rp(Lpre->resident_dev, Lpre->per_expert_scale) + threadIdx.x * 16);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (L) {
+        n.pre = ldg_u2(L->resident_dev, L->pre_ffn_norm, i);
+        n.pre2 = ldg_u2(L->resident_dev, L->pre_ffn_norm_2, i);
+        n.rsc = ldg_u2(L->resident_dev, L->router_scale, i);
+    }
+    return n;
+}
+__device__ __forceinline__ float bfw(const uint2& v, int k) {   // element k (0..3) of 4 packed bf16
+    const uint32_t w = k < 2 ? v.x : v.y;
+    return bf16f((uint16_t)((k & 1) ? (w >> 16) : (w & 0xFFFFu)));
 }
 
-// Sums a and b over the block with one barrier: each thread adds the warp partials itself in
-// warp order, so every thread (and every CTA, given the same data) gets the same bits.
+// Sums a and b over the compute threads with one barrier: every thread adds the warp partials itself
+// in warp order, so every thread (and every CTA, given the same data) gets the same bits.
 // Consecutive calls must alternate `buf`.
 __device__ __forceinline__ double2 block_sum2(Smem& s, double a, double b, int buf) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -465,19 +718,38 @@ __device__ __forceinline__ double2 block_sum2(Smem& s, double a, double b, int b
         a += __shfl_xor_sync(0xffffffffu, a, o);
         b += __shfl_xor_sync(0xffffffffu, b, o);
     }
-    if (lane == 0) { s.red2[buf][warp][0] = a; s.red2[buf][warp][1] = b; }
-    __syncthreads();
-    double ra = 0.0, rb = 0.0;
+    if (lane == 0) { s.red[buf][warp][0] = a; s.red[buf][warp][1] = b; }
+    csync();
+    double ra[4] = {0.0, 0.0, 0.0, 0.0}, rb[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-    for (int w = 0; w < NW; ++w) { ra += s.red2[buf][w][0]; rb += s.red2[buf][w][1]; }
-    return make_double2(ra, rb);
+    for (int w = 0; w < NWC; ++w) { ra[w & 3] += s.red[buf][w][0]; rb[w & 3] += s.red[buf][w][1]; }
+    return make_double2((ra[0] + ra[1]) + (ra[2] + ra[3]), (rb[0] + rb[1]) + (rb[2] + rb[3]));
 }
 
-// 1 / sqrt(float(sum / D) + eps), the reference's formula (src/cpu_reference.cpp:46); the mean
-// is formed with a multiply by 1/D (one extra rounding, far below the float conversion).
+// The same in float, for the tail's norms (not the exact one of the views): about 1e-7 relative.
+__device__ __forceinline__ float2 block_sum2f(Smem& s, float a, float b, int buf) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (lane == 0) { s.redf[buf][warp][0] = a; s.redf[buf][warp][1] = b; }
+    csync();
+    float ra[4] = {0.0f, 0.0f, 0.0f, 0.0f}, rb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int w = 0; w < NWC; ++w) { ra[w & 3] += s.redf[buf][w][0]; rb[w & 3] += s.redf[buf][w][1]; }
+    return make_float2((ra[0] + ra[1]) + (ra[2] + ra[3]), (rb[0] + rb[1]) + (rb[2] + rb[3]));
+}
+
+// 1 / sqrt(float(sum / D) + eps), the reference's formula (src/cpu_reference.cpp:46), from a float
+// sum of squares; the mean is formed with a multiply by 1/D.
 constexpr double kInvD = 1.0 / (double)D;
-__device__ __forceinline__ float rms_inv_from_sum(double sum, float eps) {
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(__dmul_rn(sum, kInvD)), eps)));
+__device__ __forceinline__ float rms_inv_from_sumf(float sum, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sum * (1.0f / (float)D), eps)));
+}
+__device__ __forceinline__ float sq4f(const float (&v)[4]) {
+    return fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], v[3] * v[3])));
 }
 
 // The same with the reference's exact bits when `sum` is a parallel double sum of x*x: see
@@ -495,108 +767,101 @@ __device__ float certified_rms_inv(Smem& s, const float* x, double sum, float ep
         if (threadIdx.x == 0) {
             double seq = 0.0;
             for (int i = 0; i < D; ++i) seq = __dadd_rn(seq, __dmul_rn((double)x[i], (double)x[i]));
-            s.red[32] = seq;
+            s.seq_sum = seq;
         }
-        __syncthreads();
-        f = __double2float_rn(__ddiv_rn(s.red[32], (double)D));
+        csync();
+        f = __double2float_rn(__ddiv_rn(s.seq_sum, (double)D));
     }
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, eps)));
 }
 
-// Layer tail of the previous layer Lp (src/cpu_reference.cpp:512-520), when there is one, from
-// the down partials (shared output = the 3 shared thirds, h2 = the 8 routed experts in router
-// order), the optional weightless RMSNorm between layers, then the views of layer L
-// (src/cpu_reference.cpp:425-443): dense_x = h*w_pre, routed_x = h*w_pre2 and
-// router_in = h*bf16(router.scale)*(1/sqrt(D)) with h = rmsnorm_no_scale(hidden), exactly as the
-// reference rounds them; finally the fragment tables of dense_x and routed_x.
-__device__ void tail_and_views(Smem& s, const Params& P, const GtmLayer* Lp, bool norm_between, bool do_views,
-                               float* h1_out, float* h2_out, float* hid_out) {
-    const int tid = threadIdx.x;
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();
-    float* h2 = s.ab;
-    float* sh = s.ab + D;
-    double a = 0.0;
-    int buf = 0;
-    if (Lp) {
-        const float ls = bf16f(*rp16(Lp->resident_dev, Lp->layer_scalar));
-        double b = 0.0;
-        for (int i = tid; i < D / 4; i += NT) {
-            // part [contributor][shared, routed][D]: shared = p00 + p10, routed h2 = p01 + p11
-            const float4* pp = reinterpret_cast<const float4*>(P.part) + i;
-            float4 vs = __ldcg(pp), vh = __ldcg(pp + (D / 4));
-            const float4 s1 = __ldcg(pp + 2 * (D / 4)), r1 = __ldcg(pp + 3 * (D / 4));
-            vs.x += s1.x; vs.y += s1.y; vs.z += s1.z; vs.w += s1.w;
-            vh.x += r1.x; vh.y += r1.y; vh.z += r1.z; vh.w += r1.w;
-            reinterpret_cast<float4*>(sh)[i] = vs;
-            reinterpret_cast<float4*>(h2)[i] = vh;
-            a += (double)vs.x * vs.x + (double)vs.y * vs.y + (double)vs.z * vs.z + (double)vs.w * vs.w;
-            b += (double)vh.x * vh.x + (double)vh.y * vh.y + (double)vh.z * vh.z + (double)vh.w * vh.w;
-        }
-        double2 r = block_sum2(s, a, b, buf); buf ^= 1;
-        const float inv1 = rms_inv_from_sum(r.x, P.eps), inv2 = rms_inv_from_sum(r.y, P.eps);
-        a = 0.0;
-        for (int i = tid; i < D; i += NT) {
-            const float h1 = __fmul_rn(__fmul_rn(sh[i], inv1), bf16f(s.nw[3][i]));
-            if (h1_out) h1_out[i] = h1;
-            if (h2_out) h2_out[i] = h2[i];
-            const float t = __fadd_rn(__fmul_rn(__fmul_rn(h2[i], inv2), bf16f(s.nw[4][i])), h1);
-            h2[i] = t;
-            a += (double)t * t;
-        }
-        r = block_sum2(s, a, 0.0, buf); buf ^= 1;
-        const float inv3 = rms_inv_from_sum(r.x, P.eps);
-        a = 0.0;
-        for (int i = tid; i < D; i += NT) {
-            const float hv = __fmul_rn(__fadd_rn(s.hid[i], __fmul_rn(__fmul_rn(h2[i], inv3), bf16f(s.nw[5][i]))), ls);
-            s.hid[i] = hv;
-            a += (double)hv * hv;
-        }
-        if (norm_between) {
-            r = block_sum2(s, a, 0.0, buf); buf ^= 1;
-            const float inv4 = rms_inv_from_sum(r.x, P.eps);
-            a = 0.0;
-            for (int i = tid; i < D; i += NT) {
-                const float hv = __fmul_rn(s.hid[i], inv4);
-                s.hid[i] = hv;
-                a += (double)hv * hv;
-            }
-        }
-        if (hid_out)
-            for (int i = tid; i < D; i += NT) hid_out[i] = s.hid[i];
-    } else {
-        for (int i = tid; i < D; i += NT) a += (double)s.hid[i] * s.hid[i];
-    }
-    if (!do_views) {
-        __syncthreads();
-        return;
-    }
-    const double2 r = block_sum2(s, a, 0.0, buf);
-    const float inv = certified_rms_inv(s, s.hid, r.x, P.eps);
-    for (int i = tid; i < D; i += NT) {
-        const float h = __fmul_rn(s.hid[i], inv);
-        sh[i] = __fmul_rn(h, bf16f(s.nw[0][i]));    // dense_x
-        h2[i] = __fmul_rn(h, bf16f(s.nw[1][i]));    // routed_x
-        s.rin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(h, bf16f(s.nw[2][i])), P.inv_sqrt_d);
-    }
-    __syncthreads();
-    build_tables(2, GD, h2, s.tbl_r, s.xs_r, s.cs_r, sh, s.tbl_d, s.xs_d, s.cs_d);
-    __syncthreads();
+__device__ __forceinline__ double sq4(const float (&v)[4]) {
+    return (double)v[0] * v[0] + (double)v[1] * v[1] + (double)v[2] * v[2] + (double)v[3] * v[3];
 }
 
-// One router logit in src/cpu_reference.cpp:86-106's order (bit-identical).
-__device__ float router_row(Smem& s, const GtmLayer& L, int row) {
+// Layer tail of the previous layer (src/cpu_reference.cpp:512-520), when there is one, from the down
+// partials (shared output = the 3 shared thirds, h2 = the 8 routed experts in router order), the
+// optional weightless RMSNorm between layers, then the views of this layer
+// (src/cpu_reference.cpp:425-443): dense_x = h*w_pre, routed_x = h*w_pre2 and
+// router_in = h*bf16(router.scale)*(1/sqrt(D)) with h = rmsnorm_no_scale(hidden), exactly as the
+// reference rounds them; finally the fragment tables of dense_x and routed_x. Compute thread i owns
+// elements 4i..4i+3.
+__device__ void tail_and_views(Smem& s, const Params& P, const Norms& nv, bool has_prev, bool norm_between,
+                               bool do_views, float* h1_out, float* h2_out, float* hid_out) {
+    const int i = threadIdx.x;
+    float hv[4];
+    {
+        const float4 v = reinterpret_cast<const float4*>(s.hid)[i];
+        hv[0] = v.x; hv[1] = v.y; hv[2] = v.z; hv[3] = v.w;
+    }
+    int buf = 0;
+    if (has_prev) {
+        // part [contributor][shared, routed][D]: shared = p00 + p10, routed h2 = p01 + p11
+        const float4* pp = reinterpret_cast<const float4*>(P.part);
+        const float4 p00 = __ldcg(pp + i), p01 = __ldcg(pp + D / 4 + i);
+        const float4 p10 = __ldcg(pp + 2 * (D / 4) + i), p11 = __ldcg(pp + 3 * (D / 4) + i);
+        float sh[4] = {p00.x + p10.x, p00.y + p10.y, p00.z + p10.z, p00.w + p10.w};
+        float h2[4] = {p01.x + p11.x, p01.y + p11.y, p01.z + p11.z, p01.w + p11.w};
+        float2 r = block_sum2f(s, sq4f(sh), sq4f(h2), buf); buf ^= 1;
+        const float inv1 = rms_inv_from_sumf(r.x, P.eps), inv2 = rms_inv_from_sumf(r.y, P.eps);
+        float tt[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float h1 = __fmul_rn(__fmul_rn(sh[k], inv1), bfw(nv.w1, k));
+            tt[k] = __fadd_rn(__fmul_rn(__fmul_rn(h2[k], inv2), bfw(nv.w2, k)), h1);
+            sh[k] = h1;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {   // caller buffers: scalar stores (4-byte alignment is all they promise)
+            if (h1_out) h1_out[4 * i + k] = sh[k];
+            if (h2_out) h2_out[4 * i + k] = h2[k];
+        }
+        r = block_sum2f(s, sq4f(tt), 0.0f, buf); buf ^= 1;
+        const float inv3 = rms_inv_from_sumf(r.x, P.eps);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            hv[k] = __fmul_rn(__fadd_rn(hv[k], __fmul_rn(__fmul_rn(tt[k], inv3), bfw(nv.w3, k))), nv.ls);
+        if (norm_between) {
+            r = block_sum2f(s, sq4f(hv), 0.0f, buf); buf ^= 1;
+            const float inv4 = rms_inv_from_sumf(r.x, P.eps);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) hv[k] = __fmul_rn(hv[k], inv4);
+        }
+        reinterpret_cast<float4*>(s.hid)[i] = make_float4(hv[0], hv[1], hv[2], hv[3]);
+        if (hid_out)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) hid_out[4 * i + k] = hv[k];
+    }
+    if (!do_views) {
+        csync();
+        return;
+    }
+    const double2 r = block_sum2(s, sq4(hv), 0.0, buf);   // its barrier also publishes s.hid
+    const float inv = certified_rms_inv(s, s.hid, r.x, P.eps);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = 4 * i + k;
+        const float h = __fmul_rn(hv[k], inv);
+        s.u.t.ab[D + e] = __fmul_rn(h, bfw(nv.pre, k));    // dense_x
+        s.u.t.ab[e] = __fmul_rn(h, bfw(nv.pre2, k));       // routed_x
+        s.u.t.rin[(e >> 6) * RIN_PITCH + (e & 63)] = __fmul_rn(__fmul_rn(h, bfw(nv.rsc, k)), P.inv_sqrt_d);
+    }
+    csync();
+    build_views_tables(s);
+    csync();
+}
+
+// One router logit in src/cpu_reference.cpp:86-106's order (bit-identical), row weights in `W`
+// (shared memory); threads 0..43 take a group each (their scale and bias already loaded), thread 0
+// adds the 44 terms in order. Called by the first two compute warps.
+__device__ float router_row(Smem& s, const uint8_t* W, float sc, float bi) {
     const int tid = threadIdx.x;
-    const uint8_t* W = rp(L.resident_dev, L.router.weight) + (size_t)row * D;
-    const uint16_t* S = rp16(L.resident_dev, L.router.scales) + row * GD;
-    const uint16_t* B = rp16(L.resident_dev, L.router.biases) + row * GD;
     if (tid < GD) {
         const uint4* wg = reinterpret_cast<const uint4*>(W + tid * kGroup);
         uint4 q[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = ldg_stream_u4(wg + i);
-        const float sc = bf16f(ldg_u16(S + tid)), bi = bf16f(ldg_u16(B + tid));
-        const float* x = s.rin + tid * RIN_PITCH;
+        for (int i = 0; i < 4; ++i) q[i] = wg[i];
+        const float* x = s.u.t.rin + tid * RIN_PITCH;
         float dot = 0.0f, sum = 0.0f;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -613,37 +878,33 @@ __device__ float router_row(Smem& s, const GtmLayer& L, int row) {
         }
         s.terms[tid] = __fadd_rn(__fmul_rn(sc, dot), __fmul_rn(bi, sum));
     }
-    __syncthreads();
+    tc::named_bar_sync(2, 64);
     float acc = 0.0f;
     if (tid == 0)
         for (int g = 0; g < GD; ++g) acc = __fadd_rn(acc, s.terms[g]);
     return acc;
 }
 
-// Top-8 of the 128 logits by (value desc, index asc), softmax over the 8, times
-// per_expert_scale (src/cpu_reference.cpp:447-480). Warp 0; results in s.topi / s.topw.
-__device__ void select_topk(Smem& s, const GtmLayer& L, const float* logits, bool writer, uint32_t* idx_out,
+// Top-8 of the 128 logits (lane j of warp 0 holds rows j + 32 k) by (value desc, index asc),
+// softmax over the 8, times per_expert_scale (src/cpu_reference.cpp:447-480); pes_w holds the
+// per-expert scales of the same rows. Results in s.topi / s.topw.
+__device__ void select_topk(Smem& s, const float (&v)[4], const uint16_t (&pes_w)[4], bool writer, uint32_t* idx_out,
                             float* w_out, float* logits_out) {
-    if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
-    float v[4];
     bool taken[4] = {false, false, false, false};
+    if (writer && logits_out)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        v[j] = __ldcg(logits + lane + 32 * j);
-        if (writer && logits_out) logits_out[lane + 32 * j] = v[j];
-    }
-    // Order-preserving unsigned keys (-0 folded onto +0, which compare equal as floats); each
-    // round takes the largest key, then the lowest index holding it: (value desc, index asc).
+        for (int j = 0; j < 4; ++j) logits_out[lane + 32 * j] = v[j];
+    // order-preserving unsigned keys (-0 folded onto +0, which compare equal as floats); each
+    // round takes the largest key, then the lowest index holding it: (value desc, index asc)
     uint32_t key[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t u = __float_as_uint(v[j] == 0.0f ? 0.0f : v[j]);
         key[j] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     }
-    float my_sel = 0.0f;
+    float my_sel = 0.0f, top0 = 0.0f;
     int my_idx = 0;
-    float top0 = 0.0f;
 #pragma unroll
     for (int k = 0; k < TOPK; ++k) {
         uint32_t ck = 0u, ci = 0xFFFFFFFFu;          // this lane's best untaken (key desc, index asc)
@@ -658,9 +919,15 @@ __device__ void select_topk(Smem& s, const GtmLayer& L, const float* logits, boo
 #pragma unroll
         for (int j = 0; j < 4; ++j) if ((uint32_t)(lane + 32 * j) == bi) taken[j] = true;
     }
-    // lanes 0..7: exp and per-expert scale in parallel, the sum in order on every lane
+    // the selected rows' per-expert scales from the lanes holding them
+    uint16_t pes_bits = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint16_t pv = (uint16_t)__shfl_sync(0xffffffffu, (int)pes_w[j], my_idx & 31);
+        if ((my_idx >> 5) == j) pes_bits = pv;
+    }
+    // lanes 0..7: exp in parallel, the sum in order on every lane
     const float e = lane < TOPK ? expf(__fsub_rn(my_sel, top0)) : 0.0f;
-    const uint16_t pes_bits = lane < TOPK ? s.pes[my_idx] : 0;
     float sum = 0.0f;
 #pragma unroll
     for (int k = 0; k < TOPK; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, k));
@@ -673,115 +940,75 @@ __device__ void select_topk(Smem& s, const GtmLayer& L, const float* logits, boo
     }
 }
 
-// ---- work lists ----------------------------------------------------------------------------------
-__device__ __forceinline__ int share(int n, int c, int G) { return (int)((long long)c * n / G); }
-
-// gate/up tile rows: row g = gate row r0 + g, row g + 8 = up row r0 + g (same x)
-__device__ __forceinline__ TileRows gu_rows(const uint8_t* base_g, const uint8_t* base_u, const GtmQuant& qg,
-                                            const GtmQuant& qu, int r) {
-    TileRows R;
-    R.wa = base_g + qg.weight + (uint64_t)r * ROW_GU;
-    R.wb = base_u + qu.weight + (uint64_t)r * ROW_GU;
-    R.sa = reinterpret_cast<const uint16_t*>(base_g + qg.scales) + (uint64_t)r * GD;
-    R.ba = reinterpret_cast<const uint16_t*>(base_g + qg.biases) + (uint64_t)r * GD;
-    R.sb = reinterpret_cast<const uint16_t*>(base_u + qu.scales) + (uint64_t)r * GD;
-    R.bb = reinterpret_cast<const uint16_t*>(base_u + qu.biases) + (uint64_t)r * GD;
-    return R;
+// ---- down phase ------------------------------------------------------------------------------------
+// Down items [d0, d1) in chunk order: the shared thirds (row tiles sh_a..sh_b, row-tile-major), then
+// the 8 routed segments, each over its row tiles. dn_pos maps (row tile, segment) to that order.
+__device__ void plan_down(Smem& s, const Plan& p) {
+    if (threadIdx.x != 0) return;
+    int k = 0;
+    for (int it = p.d0; it < p.d1; ++it)
+        if (it % NSEG < 3) { s.dn_ot[k] = it / NSEG; s.dn_q[k] = it % NSEG; ++k; }
+    for (int q = 3; q < NSEG; ++q)
+        for (int it = seg_first(p, q); it <= seg_last(p, q); it += NSEG) { s.dn_ot[k] = it / NSEG; s.dn_q[k] = q; ++k; }
+    for (int a = 0; a < MAX_OTS; ++a)
+        for (int q = 0; q < NSEG; ++q) s.dn_pos[a][q] = -1;
+    for (int j = 0; j < k; ++j) s.dn_pos[s.dn_ot[j] - p.ot0][s.dn_q[j]] = j;
 }
 
-__device__ __forceinline__ TileRows down_rows(const uint8_t* base, const GtmQuant& q, int row, uint32_t row_bytes,
-                                              uint32_t groups) {
-    TileRows R;
-    R.wa = base + q.weight + (uint64_t)row * row_bytes;
-    R.wb = base + q.weight + (uint64_t)(row + 8) * row_bytes;
-    R.sa = reinterpret_cast<const uint16_t*>(base + q.scales) + (uint64_t)row * groups;
-    R.ba = reinterpret_cast<const uint16_t*>(base + q.biases) + (uint64_t)row * groups;
-    R.sb = reinterpret_cast<const uint16_t*>(base + q.scales) + (uint64_t)(row + 8) * groups;
-    R.bb = reinterpret_cast<const uint16_t*>(base + q.biases) + (uint64_t)(row + 8) * groups;
-    return R;
-}
-
-// Shared gate/up tiles [t0, t1) -> act[8*T + r]
-__device__ void shared_gate_up(Smem& s, const Params& P, const GtmLayer& L, int t0, int t1) {
-    const int n = t1 - t0;
-    if (n <= 0) return;
-    zero_slots(s, n);
-    __syncthreads();
-    const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
-    const int lane_g = (threadIdx.x & 31) >> 2;
-    warp_items(s, 0, n, GD, 0, s.tbl_d, s.xs_d, s.cs_d, [&](int item) {
-        return gu_rows(base, base, L.shared_gate, L.shared_up, (t0 + item) * 8 + lane_g);
-    });
-    __syncthreads();
-    for (int i = threadIdx.x; i < n * 8; i += NT) {
-        const int item = i >> 3, r = i & 7;
-        const float gt = slot_sum(s, item, r), up = slot_sum(s, item, 8 + r);
-        P.act[(t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
-    }
-}
-
-// Routed gate/up tiles [t0, t1) (tile T: expert slot T / 88, rows 8 * (T % 88) ..) -> act[FS + 8*T + r]
-__device__ void routed_gate_up(Smem& s, const Params& P, const GtmLayer& L, int t0, int t1) {
-    const int n = t1 - t0;
-    if (n <= 0) return;
-    zero_slots(s, n);
-    __syncthreads();
-    const int lane_g = (threadIdx.x & 31) >> 2;
-    warp_items(s, 0, n, GD, 0, s.tbl_r, s.xs_r, s.cs_r, [&](int item) {
-        const int T = t0 + item, k = T / (FE / 8), r = (T - k * (FE / 8)) * 8 + lane_g;
-        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
-        return gu_rows(blk, blk, L.expert_gate, L.expert_up, r);
-    });
-    __syncthreads();
-    for (int i = threadIdx.x; i < n * 8; i += NT) {
-        const int item = i >> 3, r = i & 7;
-        const float gt = slot_sum(s, item, r), up = slot_sum(s, item, 8 + r);
-        P.act[FS + (t0 + item) * 8 + r] = gelu_tanh_f(gt) * up;
-    }
-}
-
-// Down items [i0, i1) of the shared expert and the 8 routed experts, one pass, in row-tile-major
-// order: item i -> row tile ot = i / NSEG, segment q = i % NSEG. Segments 0..2: K groups
-// [11q, 11q + 11) of the shared down rows (33 groups); segments 3..10: expert slot k = q - 3, all 11
-// groups of its down rows, times w_k. The table of segment q is tbl_dn + 11 q. The CTA sums its
-// segments of each row tile in segment order, shared and routed apart, into contributor slot 0
-// (the CTA holding segment 0 of the tile) or 1: a CTA holds >= 13 consecutive items, so a tile of
-// 11 has at most two contributors, and the tail reads part[0] + part[1] (4 vectors, not 11).
-__device__ void down_items(Smem& s, const Params& P, const GtmLayer& L, int i0, int i1) {
-    const int n = i1 - i0;
-    if (n <= 0) return;
-    zero_slots(s, n);
-    __syncthreads();
-    const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
-    const int lane_g = (threadIdx.x & 31) >> 2;
-    warp_items_src(s, n, GFE, [&](int item) {
-        const int it = i0 + item, ot = it / NSEG, q = it - ot * NSEG;
-        ItemSrc S;
-        if (q < 3) {
-            S.R = down_rows(res, L.shared_down, ot * 16 + lane_g, FS / 2, GFS);
-            S.tbl = s.tbl_dn;
-            S.xs = s.xs_dn;
-            S.cs = s.cs_dn;
-            S.jbase = q * GFE;
-        } else {
-            const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[q - 3] * L.expert_stride);
-            S.R = down_rows(blk, L.expert_down, ot * 16 + lane_g, FE / 2, GFE);
-            S.tbl = s.tbl_dn + q * GFE * TBL_WORDS;
-            S.xs = s.xs_dn + q * GFE;
-            S.cs = s.cs_dn + q * GFE;
-            S.jbase = 0;
+__device__ bool down_phase(Smem& s, const Params& P, const Plan& p, int c_first) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const Split sp = make_split(p.d1 - p.d0, GFE);
+    int pp = pw0(warp, sp.total);
+    const int p1 = pw0(warp + 1, sp.total);
+    int cur = c_first;
+    bool ok = true;
+    while (pp < p1) {
+        const int k = pp / GFE, j0 = pp - k * GFE, j1 = min(GFE, j0 + (p1 - pp));
+        const int ot = s.dn_ot[k], q = s.dn_q[k];
+        const bool shared = q < 3;
+        const int c = shared ? c_first : c_first + 1 + (q - 3);
+        if (!advance_to(s, P, cur, c)) { ok = false; break; }
+        const uint8_t* base = s.ring + s.meta[c % NB];
+        const int first = shared ? p.sh_a : seg_first(p, q) / NSEG;
+        const int last = shared ? p.sh_b : seg_last(p, q) / NSEG;
+        const int R = 16 * (last - first + 1), row = 16 * (ot - first) + g;
+        const int rowb = shared ? DROW_S : DROW_R, srow = shared ? GFS : GFE;   // bytes, scales per row
+        const int kofs = shared ? q * GFE : 0;                                  // first group of the segment
+        const uint8_t* w = base + (uint32_t)row * rowb + kofs * 32;
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(base + (uint32_t)R * rowb) + row * srow + kofs;
+        const uint16_t* bi = sc + R * srow;
+        float ya = 0.0f, yb = 0.0f;
+        tile_groups(w, w + 8 * rowb, sc, bi, sc + 8 * srow, bi + 8 * srow, j0, j1, s.u.tbl_dn + q * QS * QW,
+                    s.gs_dn + q * 12, ya, yb);
+        ya += __shfl_xor_sync(0xffffffffu, ya, 1);
+        ya += __shfl_xor_sync(0xffffffffu, ya, 2);
+        yb += __shfl_xor_sync(0xffffffffu, yb, 1);
+        yb += __shfl_xor_sync(0xffffffffu, yb, 2);
+        if (t == 0) {
+            float* sl = slot_of(s, sp, k, GFE, warp);
+            sl[g] = ya;
+            sl[8 + g] = yb;
         }
-        return S;
-    });
-    __syncthreads();
-    const int ot0 = i0 / NSEG, ot1 = (i1 - 1) / NSEG;
-    for (int i = threadIdx.x; i < (ot1 - ot0 + 1) * 16; i += NT) {
-        const int ot = ot0 + (i >> 4), r = i & 15;
-        const int a = max(i0, ot * NSEG), b = min(i1, ot * NSEG + NSEG);
+        pp += j1 - j0;
+    }
+    if (ok) ok = release_to(s, P, cur, c_first + 1 + TOPK);
+    return ok;
+}
+
+// The CTA sums its segments of each row tile in segment order, shared and routed apart, into
+// contributor slot 0 (the CTA holding segment 0 of the tile) or 1: a CTA holds >= 11 consecutive
+// row-tile-major items, so a tile of 11 has at most two contributors, and the tail reads
+// part[0] + part[1].
+__device__ void down_epilogue(Smem& s, const Params& P, const Plan& p) {
+    const Split sp = make_split(p.d1 - p.d0, GFE);
+    const int ot1 = (p.d1 - 1) / NSEG;
+    for (int i = threadIdx.x; i < (ot1 - p.ot0 + 1) * 16; i += NTC) {
+        const int ot = p.ot0 + (i >> 4), r = i & 15;
+        const int a = max(p.d0, ot * NSEG), b = min(p.d1, ot * NSEG + NSEG);
         float sh = 0.0f, h2 = 0.0f;
         for (int it = a; it < b; ++it) {
             const int q = it - ot * NSEG;
-            const float v = slot_sum(s, it - i0, r);
+            const float v = item_sum(s, sp, s.dn_pos[ot - p.ot0][q], GFE, r);
             if (q < 3) sh = __fadd_rn(sh, v);
             else h2 = __fadd_rn(h2, __fmul_rn(s.topw[q - 3], v));   // the product rounded, as the combine had it
         }
@@ -796,358 +1023,186 @@ __device__ void down_items(Smem& s, const Params& P, const GtmLayer& L, int i0, 
     }
 }
 
-// L2 prefetch of the weights this CTA reads in the next layer's P1 (router row, shared gate/up
-// tiles, norm vectors) and of its shared-down rows.
-// Every range below lies inside one tensor; the CTA's warps take the ranges round-robin.
-__device__ void prefetch_layer_static(const GtmLayer& L, int cta, int G) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint8_t* base = static_cast<const uint8_t*>(L.resident_dev);
-    const int nrow = cta < NE ? (NE - 1 - cta) / G + 1 : 0;          // router rows of this CTA
-    const int t0 = share(TILES_S, cta, G), t1 = share(TILES_S, cta + 1, G);
-    const int i0 = share(ITEMS_DN, cta, G), i1 = share(ITEMS_DN, cta + 1, G);   // this CTA's down items
-    const int n_router = 3 * nrow, n_sgu = t1 > t0 ? 6 : 0, n_sd = 18 * (i1 - i0), n_vec = 6;
-    const int total = n_router + n_sgu + n_sd + n_vec;
-    for (int i = warp; i < total; i += NW) {
-        const uint8_t* p;
-        uint32_t n;
-        if (i < n_router) {
-            const uint64_t row = (uint64_t)(cta + (i / 3) * G);
-            const int part = i % 3;
-            if (part == 0) { p = base + L.router.weight + row * D; n = D; }
-            else { p = base + (part == 1 ? L.router.scales : L.router.biases) + row * GD * 2; n = GD * 2; }
-        } else if (i < n_router + n_sgu) {
-            const int k = i - n_router, m = k / 3, part = k % 3;
-            const GtmQuant& q = m ? L.shared_up : L.shared_gate;
-            if (part == 0) { p = base + q.weight + (uint64_t)t0 * 8 * ROW_GU; n = (t1 - t0) * 8 * ROW_GU; }
-            else { p = base + (part == 1 ? q.scales : q.biases) + (uint64_t)t0 * 8 * GD * 2; n = (t1 - t0) * 8 * GD * 2; }
-        } else if (i < n_router + n_sgu + n_sd) {
-            // the shared-down items among them (segments 0..2); routed ones prefetch after the top-8
-            const int k = i - n_router - n_sgu, it = i0 + k / 18, part = k % 18;
-            const int ot = it / NSEG, q = it - ot * NSEG;
-            if (q >= 3) continue;
-            if (part < 16) {
-                p = base + L.shared_down.weight + ((uint64_t)ot * 16 + part) * (FS / 2) + q * GFE * 32;
-                n = GFE * 32;
-            } else {
-                p = base + (part == 16 ? L.shared_down.scales : L.shared_down.biases) + (uint64_t)ot * 16 * GFS * 2;
-                n = 16 * GFS * 2;
-            }
-        } else {
-            const int v = i - n_router - n_sgu - n_sd;
-            const uint64_t off = v == 0 ? L.pre_ffn_norm : v == 1 ? L.pre_ffn_norm_2 : v == 2 ? L.router_scale
-                               : v == 3 ? L.post_ffn_norm_1 : v == 4 ? L.post_ffn_norm_2 : L.post_ffn_norm;
-            p = base + off;
-            n = D * 2;
-        }
-        prefetch_lines(p, n, lane);
-    }
-}
-
-// L2 prefetch of this CTA's routed gate/up rows (known once the top-8 is): per tile 8 gate rows,
-// 8 up rows and their scales and biases, each a contiguous range.
-__device__ void prefetch_routed_gate_up(const Smem& s, const GtmLayer& L, int cta, int G) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t0 = share(TILES_R, cta, G), t1 = share(TILES_R, cta + 1, G);
-    for (int i = warp; i < 6 * (t1 - t0); i += NW) {
-        const int T = t0 + i / 6, part = i % 6, k = T / (FE / 8), r8 = T - k * (FE / 8);
-        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[k] * L.expert_stride);
-        const GtmQuant& q = part < 3 ? L.expert_gate : L.expert_up;
-        const int pp = part % 3;
-        if (pp == 0) prefetch_lines(blk + q.weight + (uint64_t)r8 * 8 * ROW_GU, 8 * ROW_GU, lane);
-        else prefetch_lines(blk + (pp == 1 ? q.scales : q.biases) + (uint64_t)r8 * 8 * GD * 2, 8 * GD * 2, lane);
-    }
-}
-
-// L2 prefetch of this CTA's routed-down rows (known once the top-8 is).
-__device__ void prefetch_routed_down(const Smem& s, const GtmLayer& L, int cta, int G) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i0 = share(ITEMS_DN, cta, G), i1 = share(ITEMS_DN, cta + 1, G);
-    for (int i = warp; i < 3 * (i1 - i0); i += NW) {
-        const int it = i0 + i / 3, part = i % 3, ot = it / NSEG, q = it - ot * NSEG;
-        if (q < 3) continue;   // shared-down items were prefetched with the layer's static weights
-        const uint8_t* blk = rp(L.experts_dev, (uint64_t)s.topi[q - 3] * L.expert_stride);
-        if (part == 0) prefetch_lines(blk + L.expert_down.weight + (uint64_t)ot * 16 * (FE / 2), 16 * (FE / 2), lane);
-        else prefetch_lines(blk + (part == 1 ? L.expert_down.scales : L.expert_down.biases) + (uint64_t)ot * 16 * GFE * 2,
-                            16 * GFE * 2, lane);
-    }
-}
-
+// ---- the kernel --------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant__ Params P) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    Smem& s = *reinterpret_cast<Smem*>(smem_raw);
-    const int tid = threadIdx.x;
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const GtmDecodeIO& io = P.io;
     const bool writer = cta == 0;
+    const Plan p = make_plan(cta, G);
 
-    prefetch_layer_static(P.layers[0], cta, G);
-    load_norms_async(s, &P.layers[0], nullptr);
-    for (int i = tid; i < D; i += NT) s.hid[i] = io.hidden_in_dev[i];
-    __syncthreads();
-
-    for (int l = 0; l < P.num_layers; ++l) {
-        const GtmLayer& L = P.layers[l];
-        const unsigned ep = (unsigned)(l + 1);
-        // ---- P1 ----
-        if (l > 0) {
-            if (!wait_all(P, s, BAR_C, ep - 1)) return;
-            tail_and_views(s, P, &P.layers[l - 1], (io.flags & GTM_DECODE_NORM_BETWEEN_LAYERS) != 0, true,
-                           writer && io.h1_dev ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
-                           writer && io.h2_dev ? io.h2_dev + (size_t)(l - 1) * D : nullptr,
-                           writer && io.hidden_layers_dev ? io.hidden_layers_dev + (size_t)(l - 1) * D : nullptr);
-        } else {
-            tail_and_views(s, P, nullptr, false, true, nullptr, nullptr, nullptr);
-        }
-        for (int row = cta; row < NE; row += G) {
-            float lg = router_row(s, L, row);
-            if (tid == 0) {
-                if (io.logit_bias_dev) lg = __fadd_rn(lg, io.logit_bias_dev[(size_t)l * NE + row]);
-                P.logits[row] = lg;
-            }
-            __syncthreads();
-        }
-        arrive(P, BAR_A1, ep);
-        // (its shared activations are published by the B arrival below, which follows in order)
-        shared_gate_up(s, P, L, share(TILES_S, cta, G), share(TILES_S, cta + 1, G));
-
-        // ---- P2 ----
-        if (!wait_all(P, s, BAR_A1, ep + (l == 0 ? P.first_wait_extra : 0u))) return;
-        select_topk(s, L, P.logits, writer, io.topk_idx_dev ? io.topk_idx_dev + (size_t)l * TOPK : nullptr,
-                    io.topk_w_dev ? io.topk_w_dev + (size_t)l * TOPK : nullptr,
-                    io.logits_dev ? io.logits_dev + (size_t)l * NE : nullptr);
-        __syncthreads();
-        prefetch_routed_gate_up(s, L, cta, G);
-        prefetch_routed_down(s, L, cta, G);
-        routed_gate_up(s, P, L, share(TILES_R, cta, G), share(TILES_R, cta + 1, G));
-        arrive(P, BAR_B, ep);
-
-        // ---- P3: shared and routed down in one pass (every CTA's B arrival follows its shared
-        //      gate/up, so B covers both activation sets) ----
-        if (!wait_all(P, s, BAR_B, ep)) return;
-        const int d0 = share(ITEMS_DN, cta, G), d1 = share(ITEMS_DN, cta + 1, G);
-        if (d1 > d0) {
-            // a CTA's >= 11 consecutive row-tile-major items read every segment: the tables of all
-            // 11 (the shared activations, then the 8 routed slots), built straight from L2
-            build_tables(1, NSEG * GFE, P.act, s.tbl_dn, s.xs_dn, s.cs_dn, P.act, s.tbl_dn, s.xs_dn, s.cs_dn, true);
-        }
-        __syncthreads();
-        if (l + 1 < P.num_layers) prefetch_layer_static(P.layers[l + 1], cta, G);
-        load_norms_async(s, l + 1 < P.num_layers ? &P.layers[l + 1] : nullptr, &L);
-        down_items(s, P, L, d0, d1);
-        arrive(P, BAR_C, ep);
+    if (tid == 0) {
+        for (int b = 0; b < NB; ++b) { tc::mbar_init(&s.full[b], 1); tc::mbar_init(&s.empty[b], NWC); }
+        s.topk_ready = 0;
+        s.abort = 0;
+        tc::mbar_fence_init();
     }
+    plan_down(s, p);
+    __syncthreads();
+    if (warp == NWC) {
+        producer(s, P, p);
+        return;
+    }
+
+    for (int i = tid; i < D; i += NTC) s.hid[i] = io.hidden_in_dev[i];
+    csync();
+    const bool norm_between = (io.flags & GTM_DECODE_NORM_BETWEEN_LAYERS) != 0;
+    int cbase = 0;   // chunk sequence number of the layer's first chunk
+    for (int l = 0; l < P.num_layers; ++l, cbase += p.cpl) {
+        const GtmLayer& L = P.layers[l];
+        const GtmLayer* Lp = l > 0 ? &P.layers[l - 1] : nullptr;
+        const unsigned ep = (unsigned)(l + 1);
+        // loads that need no barrier: the norm vectors of the tail and views, this CTA's router
+        // scale and bias (first row), the per-expert scales for the top-8
+        const Norms nv = load_norms(Lp, &L);
+        float rsc = 0.0f, rbi = 0.0f;
+        if (tid < GD && p.nr > 0) {
+            rsc = bf16f(__ldg(rp16(L.resident_dev, L.router.scales) + cta * GD + tid));
+            rbi = bf16f(__ldg(rp16(L.resident_dev, L.router.biases) + cta * GD + tid));
+        }
+        uint16_t pes_w[4] = {0, 0, 0, 0};
+        if (warp == 0)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) pes_w[j] = __ldg(rp16(L.resident_dev, L.per_expert_scale) + lane + 32 * j);
+
+        // ---- tail + views ----
+        if (l > 0 && !wait_all(s, P, P.flags_c, ep - 1)) break;
+        tail_and_views(s, P, nv, l > 0, norm_between, true,
+                       writer && io.h1_dev && l > 0 ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
+                       writer && io.h2_dev && l > 0 ? io.h2_dev + (size_t)(l - 1) * D : nullptr,
+                       writer && io.hidden_layers_dev && l > 0 ? io.hidden_layers_dev + (size_t)(l - 1) * D : nullptr);
+
+        // ---- router rows (the logit words double as barrier A) ----
+        int cur = cbase;
+        bool ok = true;
+        for (int k = 0; k < p.nr; ++k) {
+            if (warp < 2) {
+                const int row = cta + k * G;
+                if (!advance_to(s, P, cur, cbase + k)) ok = false;
+                if (k > 0 && tid < GD) {
+                    rsc = bf16f(__ldg(rp16(L.resident_dev, L.router.scales) + row * GD + tid));
+                    rbi = bf16f(__ldg(rp16(L.resident_dev, L.router.biases) + row * GD + tid));
+                }
+                float lg = router_row(s, s.ring + s.meta[(cbase + k) % NB], rsc, rbi);
+                if (tid == 0 && ok) {
+                    if (io.logit_bias_dev) lg = __fadd_rn(lg, io.logit_bias_dev[(size_t)l * NE + row]);
+                    st_relaxed_u64(P.logit_words + row, ((unsigned long long)ep << 32) | __float_as_uint(lg));
+                }
+                tc::named_bar_sync(2, 64);   // the row's words are read before the chunk is released
+            }
+        }
+        if (ok) ok = release_to(s, P, cur, cbase + p.nr);
+        if (!ok) s.abort = 1;
+
+        // ---- shared gate/up ----
+        if (ok && p.st1 > p.st0) {
+            ok = gu_phase(s, P, p.st1 - p.st0, cbase + p.c_sgu, cbase + p.c_rgu, s.tbl_d, s.gs_d,
+                          [&](int item, int& c, int& lt, int& F) {
+                              const int k = item / GU_TILES;
+                              c = cbase + p.c_sgu + k;
+                              lt = item - k * GU_TILES;
+                              F = 8 * min(GU_TILES, p.st1 - p.st0 - k * GU_TILES);
+                          });
+            if (!ok) s.abort = 1;
+            csync();
+            if (!s.abort) gu_epilogue(s, P.act + 8 * p.st0, p.st1 - p.st0);
+        }
+        csync();
+        if (s.abort) break;
+
+        // ---- wait for every router logit; top-8 ----
+        if (warp == 0) {
+            const unsigned want = ep + (l == 0 ? P.first_wait_extra : 0u);
+            float v[4];
+            const uint64_t t0 = globaltimer_ns();
+            bool wok = true;
+            for (;;) {
+                bool mine = true;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const unsigned long long w = ld_relaxed_u64(P.logit_words + lane + 32 * j);
+                    mine &= (unsigned)(w >> 32) >= want;
+                    v[j] = __uint_as_float((uint32_t)w);
+                }
+                const int e = lane == 0 ? ld_volatile_int(P.err) : 0;
+                if (__all_sync(0xffffffffu, mine)) break;
+                if (__shfl_sync(0xffffffffu, e, 0) != 0) { wok = false; break; }
+                if (globaltimer_ns() - t0 > P.wait_limit_ns) {
+                    if (lane == 0) { atomicExch(P.err, 1); atomicExch(P.sticky, 1); }
+                    wok = false;
+                    break;
+                }
+            }
+            __threadfence();
+            if (wok) {
+                select_topk(s, v, pes_w, writer, io.topk_idx_dev ? io.topk_idx_dev + (size_t)l * TOPK : nullptr,
+                            io.topk_w_dev ? io.topk_w_dev + (size_t)l * TOPK : nullptr,
+                            io.logits_dev ? io.logits_dev + (size_t)l * NE : nullptr);
+                __syncwarp();
+                __threadfence_block();
+                if (lane == 0) s.topk_ready = l + 1;
+            } else if (lane == 0) {
+                s.abort = 1;
+            }
+        }
+        csync();
+        if (s.abort) break;
+
+        // ---- routed gate/up ----
+        ok = gu_phase(s, P, p.rt1 - p.rt0, cbase + p.c_rgu, cbase + p.c_dn, s.tbl_r, s.gs_r,
+                      [&](int item, int& c, int& lt, int& F) {
+                          int k, t0;
+                          rgu_locate(p, p.rt0 + item, k, t0);
+                          int tt, nt;
+                          rgu_chunk(p, k, tt, nt);
+                          c = cbase + p.c_rgu + k;
+                          lt = p.rt0 + item - t0;
+                          F = 8 * nt;
+                      });
+        if (!ok) s.abort = 1;
+        csync();
+        if (s.abort) break;
+        gu_epilogue(s, P.act + FS + 8 * p.rt0, p.rt1 - p.rt0);
+        arrive(P, P.flags_b, ep);
+
+        // ---- down: the shared and routed activations of every CTA ----
+        if (!wait_all(s, P, P.flags_b, ep)) break;
+        build_down_tables(s, P);
+        csync();
+        ok = down_phase(s, P, p, cbase + p.c_dn);
+        if (!ok) s.abort = 1;
+        csync();
+        if (s.abort) break;
+        down_epilogue(s, P, p);
+        arrive(P, P.flags_c, ep);
+    }
+    csync();
+    if (s.abort) return;
 
     // final tail by CTA 0
     if (!writer) return;
     const int l = P.num_layers;
-    if (!wait_all(P, s, BAR_C, (unsigned)l)) return;
-    tail_and_views(s, P, &P.layers[l - 1], false, false, io.h1_dev ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
+    const Norms nv = load_norms(&P.layers[l - 1], nullptr);
+    if (!wait_all(s, P, P.flags_c, (unsigned)l)) return;
+    tail_and_views(s, P, nv, true, false, false, io.h1_dev ? io.h1_dev + (size_t)(l - 1) * D : nullptr,
                    io.h2_dev ? io.h2_dev + (size_t)(l - 1) * D : nullptr,
                    io.hidden_layers_dev ? io.hidden_layers_dev + (size_t)(l - 1) * D : nullptr);
-    for (int i = tid; i < D; i += NT) io.hidden_out_dev[i] = s.hid[i];
-}
-
-// ================================================================================================
-// Tied LM head + greedy argmax (LMHeadGreedy.hlsl:1-73 + ArgmaxReduce.hlsl:1-62, runner.cpp:720-770)
-//
-// token = argmax_r logits[r], ties to the lower row, where logits = the int4 matvec of the normed
-// hidden state in the CPU reference's exact operation order (cpu_reference.cpp:55-83; softcap is
-// monotonic and skipped, as in the reference's greedy path). Computing every row in that order
-// is issue-bound, so:
-//   1. lm_approx: every row by the decode's mma.sync tiles (fp16 integer weights, fp16 high/low
-//      activations, fp32 accumulation), HBM-bound, together with a rigorous bound E_r on the
-//      distance between that value and the exact CPU-order value:
-//        E_r = 2^-14 * sum_g (1100 |s_g| + 2 |b_g|) * sum_{k in g} |x_k|
-//      (the MMA path's fp32 accumulation around its 1024 offset errs by < 64 * 2^-23 * 1039 |s| A_g
-//      per group, the CPU order's own roundings by < (64 * 15 + 44 * 16) * 2^-24 (|s| + |b|) A_g,
-//      and the x-sum orders differ by < 64 * 2^-24 A_g: E_r is 8x or more above each);
-//   2. lm_exact: L = max_r (approx_r - E_r); only rows with approx_r + E_r >= L can hold the
-//      maximum. Each of them is recomputed in the exact CPU order (one warp per row, a lane per
-//      group, the groups summed in order by one lane) and folded into a 64-bit key (orderable
-//      value, then the complement of the row) by atomicMax, which keeps (value desc, row asc)
-//      independently of the order the rows arrive in;
-//   3. lm_finish: the key -> token id and exact logit.
-// Degenerate inputs (x = 0: every row ties) only make step 2 longer: every candidate is exact.
-// ================================================================================================
-constexpr int LM_THREADS = 256;   // 75 registers: three CTAs (24 warps) per SM
-
-struct LmArgs {
-    const uint8_t* w;        // [rows][D/2] packed int4, low nibble first
-    const uint16_t* s;       // [rows][GD] bf16 scales
-    const uint16_t* b;       // [rows][GD] bf16 biases
-    const float* x;          // [D] normed hidden state
-    int rows;
-    float2* ae;              // [rows] (approximate logit, bound)
-    float* cta_lb;           // [gridDim of lm_approx] max of approx - bound per CTA
-    int n_lb;
-    unsigned long long* key; // best (value, row)
-    int* n_cand;             // rows recomputed exactly
-    uint32_t* token;
-    float* logit;            // exact logit of the token (nullable)
-};
-
-__device__ __forceinline__ uint32_t orderable(float v) {
-    const uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float from_orderable(uint32_t k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
-}
-
-__global__ void __launch_bounds__(LM_THREADS) lm_approx(const __grid_constant__ LmArgs A) {
-    __shared__ __align__(16) float sx[D];
-    __shared__ __align__(16) uint32_t tbl[GD * TBL_WORDS];
-    __shared__ float xs[GD], cs[GD], xa[GD];
-    __shared__ float wlb[LM_THREADS / 32];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-    if (blockIdx.x == 0 && tid == 0) { *A.key = 0ull; *A.n_cand = 0; }
-    for (int i = tid; i < D; i += blockDim.x) sx[i] = A.x[i];
-    __syncthreads();
-    build_table(sx, GD, tbl, xs, cs);
-    for (int j = tid; j < GD; j += blockDim.x) {
-        float a = 0.0f;
-        for (int k = 0; k < kGroup; ++k) a += fabsf(sx[j * kGroup + k]);
-        xa[j] = a;
-    }
-    __syncthreads();
-    float lb = -INFINITY;
-    const int ntiles = (A.rows + 15) / 16;
-    for (int tile = blockIdx.x * (LM_THREADS / 32) + warp; tile < ntiles; tile += gridDim.x * (LM_THREADS / 32)) {
-        const int ra = min(tile * 16 + g, A.rows - 1), rb = min(tile * 16 + 8 + g, A.rows - 1);
-        TileRows R;
-        R.wa = A.w + (size_t)ra * (D / 2);
-        R.wb = A.w + (size_t)rb * (D / 2);
-        R.sa = A.s + (size_t)ra * GD;
-        R.ba = A.b + (size_t)ra * GD;
-        R.sb = A.s + (size_t)rb * GD;
-        R.bb = A.b + (size_t)rb * GD;
-        float ya = 0.0f, yb = 0.0f, ea = 0.0f, eb = 0.0f;
-        QuadLoads cur = load_quad(R, 0, 0, GD, t);
-        for (int q0 = 0; q0 < GD; q0 += 4) {
-            QuadLoads nxt = cur;
-            if (q0 + 4 < GD) nxt = load_quad(R, q0 + 4, 0, GD, t);
-            compute_quad(cur, q0, 0, GD, tbl, xs, cs, ya, yb);
-            const int j = q0 + t;
-            if (j < GD) {
-                ea = fmaf(fmaf(1100.0f, fabsf(bf16f(cur.sa)), 2.0f * fabsf(bf16f(cur.ba))), xa[j], ea);
-                eb = fmaf(fmaf(1100.0f, fabsf(bf16f(cur.sb)), 2.0f * fabsf(bf16f(cur.bb))), xa[j], eb);
-            }
-            cur = nxt;
-        }
-#pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) {
-            ya += __shfl_xor_sync(0xffffffffu, ya, o);
-            yb += __shfl_xor_sync(0xffffffffu, yb, o);
-            ea += __shfl_xor_sync(0xffffffffu, ea, o);
-            eb += __shfl_xor_sync(0xffffffffu, eb, o);
-        }
-        // the bound's own fp32 sums are below 2^-20 of it: round it up by 2^-10
-        ea *= 6.103515625e-05f * 1.0009765625f;
-        eb *= 6.103515625e-05f * 1.0009765625f;
-        if (t == 0) {
-            const int r0 = tile * 16 + g, r1 = r0 + 8;
-            if (r0 < A.rows) { A.ae[r0] = make_float2(ya, ea); lb = fmaxf(lb, ya - ea); }
-            if (r1 < A.rows) { A.ae[r1] = make_float2(yb, eb); lb = fmaxf(lb, yb - eb); }
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lb = fmaxf(lb, __shfl_xor_sync(0xffffffffu, lb, o));
-    if (lane == 0) wlb[warp] = lb;
-    __syncthreads();
-    if (tid == 0) {
-        float m = wlb[0];
-        for (int w = 1; w < LM_THREADS / 32; ++w) m = fmaxf(m, wlb[w]);
-        A.cta_lb[blockIdx.x] = m;
-    }
-}
-
-// Exact CPU-order logit of one row (cpu_reference.cpp:55-83): lane l takes groups l and l + 32;
-// per group dot += q_lo * x0, dot += q_hi * x1, sum += x0 + x1 element pair by pair, then
-// term = s * dot + b * sum; lane 0 adds the 44 terms in group order.
-__device__ float exact_row(const LmArgs& A, const float* sx, float* terms, int row) {
-    const int lane = threadIdx.x & 31;
-    const uint8_t* wr = A.w + (size_t)row * (D / 2);
-    for (int gi = lane; gi < GD; gi += 32) {
-        const float s = bf16f(A.s[(size_t)row * GD + gi]), b = bf16f(A.b[(size_t)row * GD + gi]);
-        const uint4* wq = reinterpret_cast<const uint4*>(wr + gi * (kGroup / 2));
-        const uint4 q0 = wq[0], q1 = wq[1];
-        const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const float* xg = sx + gi * kGroup;
-        float dot = 0.0f, sum = 0.0f;
-#pragma unroll
-        for (int wi = 0; wi < 8; ++wi) {
-#pragma unroll
-            for (int by = 0; by < 4; ++by) {
-                const uint32_t byte = (words[wi] >> (8 * by)) & 0xFFu;
-                const int e = wi * 8 + by * 2;
-                const float x0 = xg[e], x1 = xg[e + 1];
-                dot = __fadd_rn(dot, __fmul_rn((float)(byte & 0x0Fu), x0));
-                dot = __fadd_rn(dot, __fmul_rn((float)(byte >> 4), x1));
-                sum = __fadd_rn(sum, __fadd_rn(x0, x1));
-            }
-        }
-        terms[gi] = __fadd_rn(__fmul_rn(s, dot), __fmul_rn(b, sum));
-    }
-    __syncwarp();
-    float acc = 0.0f;
-    if (lane == 0)
-        for (int gi = 0; gi < GD; ++gi) acc = __fadd_rn(acc, terms[gi]);
-    __syncwarp();
-    return acc;
-}
-
-__global__ void __launch_bounds__(256) lm_exact(const __grid_constant__ LmArgs A) {
-    __shared__ __align__(16) float sx[D];
-    __shared__ float terms[256 / 32][GD];
-    __shared__ float s_l;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < D; i += blockDim.x) sx[i] = A.x[i];
-    if (tid < 32) {
-        float m = -INFINITY;
-        for (int i = tid; i < A.n_lb; i += 32) m = fmaxf(m, A.cta_lb[i]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (tid == 0) s_l = m;
-    }
-    __syncthreads();
-    const float L = s_l;
-    const int nw = gridDim.x * (blockDim.x >> 5);
-    for (int base = (blockIdx.x * (blockDim.x >> 5) + warp) * 32; base < A.rows; base += nw * 32) {
-        const int r = base + lane;
-        bool cand = false;
-        if (r < A.rows) {
-            const float2 v = A.ae[r];
-            cand = v.x + v.y >= L;
-        }
-        unsigned m = __ballot_sync(0xffffffffu, cand);
-        while (m) {
-            const int k = __ffs(m) - 1;
-            m &= m - 1;
-            const int row = base + k;
-            const float v = exact_row(A, sx, terms[warp], row);
-            if (lane == 0) {
-                atomicMax(A.key, ((unsigned long long)orderable(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row));
-                atomicAdd(A.n_cand, 1);
-            }
-        }
-    }
-}
-
-__global__ void lm_finish(const __grid_constant__ LmArgs A) {
-    const unsigned long long k = *A.key;
-    *A.token = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
-    if (A.logit) *A.logit = from_orderable((uint32_t)(k >> 32));
+    csync();
+    for (int i = tid; i < D; i += NTC) io.hidden_out_dev[i] = s.hid[i];
 }
 
 }  // namespace dec
 
-// Workspace: [0, 4096) barrier flags (4 kinds x 256 CTAs) and [4096] this launch's error word,
-// both cleared before every launch; [4100] the sticky error word (zero-initialised once by the
-// workspace's owner, read and cleared by gtm_moe_decode_check); from 4352: logits, act, partials.
+// Workspace: [0, 1024) the 128 router logit words, [2048, 3072) barrier-B flags, [3072, 4096)
+// barrier-C flags and [4096] this launch's error word, all cleared before every launch; [4100] the
+// sticky error word (zero-initialised once by the workspace's owner, read and cleared by
+// gtm_moe_decode_check); from 4352: activations and down partials.
 constexpr size_t kErrOffset = 4096, kStickyOffset = 4100, kDataOffset = 4352;
 
 size_t decode_workspace_bytes() {
-    return kDataOffset + sizeof(float) * (dec::NE + dec::ACT_R + dec::FS + (size_t)dec::NSEG * dec::D) + 256;
+    return kDataOffset + sizeof(float) * (dec::ACT_R + dec::FS + (size_t)4 * dec::D) + 256;
 }
 size_t decode_sticky_offset() { return kStickyOffset; }
 
@@ -1155,6 +1210,8 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
                   void* ws, size_t ws_bytes, cudaStream_t stream, int num_ctas) {
     using namespace dec;
     (void)ws_bytes;
+    if (num_ctas > OT || num_ctas * MAX_DN < ITEMS_DN)
+        return set_error(GTM_ERR_UNSUPPORTED, "gtm_moe_decode: %d CTAs outside the decode's work split", num_ctas);
     Params P;
     memset(&P, 0, sizeof(P));
     for (int l = 0; l < num_layers; ++l) P.layers[l] = layers[l];
@@ -1166,16 +1223,17 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
     P.wait_limit_ns = test_wait ? 2000000ull : kTimeoutNs;
     P.first_wait_extra = test_wait ? 1u : 0u;
     unsigned char* w = static_cast<unsigned char*>(ws);
-    P.flags = reinterpret_cast<unsigned*>(w);
+    P.logit_words = reinterpret_cast<unsigned long long*>(w);
+    P.flags_b = reinterpret_cast<unsigned*>(w + 2048);
+    P.flags_c = reinterpret_cast<unsigned*>(w + 3072);
     P.err = reinterpret_cast<int*>(w + kErrOffset);
     P.sticky = reinterpret_cast<int*>(w + kStickyOffset);
     float* f = reinterpret_cast<float*>(w + kDataOffset);
-    P.logits = f;
-    P.act = f + NE;
+    P.act = f;
     P.part = P.act + FS + ACT_R;
     cudaError_t e = cudaMemsetAsync(w, 0, kErrOffset + sizeof(int), stream);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: memset", e);
-    const size_t smem = sizeof(Smem);
+    const size_t smem = sizeof(Smem) + 128;
     static bool attr_done = false;
     if (!attr_done) {
         e = cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1185,43 +1243,6 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
     void* args[] = {(void*)&P};
     e = cudaLaunchCooperativeKernel((const void*)moe_decode_kernel, dim3(num_ctas), dim3(NT), args, smem, stream);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: cooperative launch", e);
-    return GTM_OK;
-}
-
-}  // namespace gtm
-
-namespace gtm {
-
-size_t lm_head_workspace_bytes(uint32_t rows) {
-    return 256 + (size_t)rows * 8 + 4096 * 4;
-}
-
-int launch_lm_head(uint32_t rows, const void* w, const uint16_t* s, const uint16_t* b, const float* x, uint32_t* token,
-                   float* logit, void* ws, cudaStream_t st, int num_sms) {
-    using namespace dec;
-    uint8_t* p = static_cast<uint8_t*>(ws);
-    LmArgs A;
-    memset(&A, 0, sizeof(A));
-    A.w = static_cast<const uint8_t*>(w); A.s = s; A.b = b; A.x = x; A.rows = (int)rows;
-    A.key = reinterpret_cast<unsigned long long*>(p);
-    A.n_cand = reinterpret_cast<int*>(p + 8);
-    A.ae = reinterpret_cast<float2*>(p + 256);
-    A.cta_lb = reinterpret_cast<float*>(p + 256 + (size_t)rows * 8);
-    A.token = token; A.logit = logit;
-    const int g1 = std::min(num_sms * 3, 4096);   // persistent: three CTAs per SM
-    A.n_lb = g1;
-    lm_approx<<<g1, LM_THREADS, 0, st>>>(A);
-    lm_exact<<<num_sms * 4, 256, 0, st>>>(A);
-    lm_finish<<<1, 1, 0, st>>>(A);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return set_cuda_error("gtm_lm_head_greedy", e);
-    return GTM_OK;
-}
-
-int lm_head_candidates(void* ws, cudaStream_t st, int* n) {
-    const cudaError_t e = cudaMemcpyAsync(n, static_cast<uint8_t*>(ws) + 8, sizeof(int), cudaMemcpyDeviceToHost, st);
-    const cudaError_t e2 = e == cudaSuccess ? cudaStreamSynchronize(st) : e;
-    if (e2 != cudaSuccess) return set_cuda_error("gtm_lm_head_candidates", e2);
     return GTM_OK;
 }
 
