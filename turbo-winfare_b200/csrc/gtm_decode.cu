@@ -137,6 +137,8 @@ struct Smem {
     float topw[TOPK];
     int topi[TOPK];
     int dn_ot[MAX_DN], dn_q[MAX_DN];         // down items in processing (chunk) order
+    uint8_t it_first[3][MAX_DN], it_kend[3][MAX_DN];   // per phase (shared, routed, down) and item:
+                                                       // first contributing warp, contributors
     int dn_pos[MAX_OTS][NSEG];               // processing index of (row tile ot0 + i, segment q)
     uint64_t full[NB];                       // chunk landed (producer arrive + bytes)
     uint64_t empty[NB];                      // chunk released (one arrival per compute warp)
@@ -275,6 +277,31 @@ __device__ __forceinline__ bool release_to(Smem& s, const Params& P, int& cur, i
 }
 
 // ---- producer warp ---------------------------------------------------------------------------------
+// L2 prefetches (one bulk prefetch per contiguous range) of static weights whose shared-memory
+// copies are issued later, so those copies read L2 instead of HBM: while the producer waits for a
+// layer's top-8 it prefetches the layer's shared-down rows and the next layer's router and shared
+// gate/up rows (HBM is otherwise idle until the top-8). Bulk prefetches queue in the same TMA unit
+// as the copies, so none is issued after the top-8: there they delayed the routed copies.
+__device__ void l2_static(const Plan& p, const GtmLayer& L, const GtmLayer* Ln, int cta, int G) {
+    const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
+    const uint32_t R = 16 * (p.sh_b - p.sh_a + 1), r0 = 16 * p.sh_a;
+    tc::prefetch_l2_bulk(res + L.shared_down.weight + (uint64_t)r0 * DROW_S, R * DROW_S);
+    tc::prefetch_l2_bulk(res + L.shared_down.scales + (uint64_t)r0 * SROW_S, R * SROW_S);
+    tc::prefetch_l2_bulk(res + L.shared_down.biases + (uint64_t)r0 * SROW_S, R * SROW_S);
+    if (!Ln) return;
+    const uint8_t* rn = static_cast<const uint8_t*>(Ln->resident_dev);
+    for (int k = 0; k < p.nr; ++k) tc::prefetch_l2_bulk(rn + Ln->router.weight + (uint64_t)(cta + k * G) * D, D);
+    if (p.st1 > p.st0) {
+        const uint64_t f0 = 8 * (uint64_t)p.st0, F = 8 * (uint64_t)(p.st1 - p.st0);
+        tc::prefetch_l2_bulk(rn + Ln->shared_gate.weight + f0 * ROW_GU, F * ROW_GU);
+        tc::prefetch_l2_bulk(rn + Ln->shared_up.weight + f0 * ROW_GU, F * ROW_GU);
+        tc::prefetch_l2_bulk(rn + Ln->shared_gate.scales + f0 * SROW_GU, F * SROW_GU);
+        tc::prefetch_l2_bulk(rn + Ln->shared_gate.biases + f0 * SROW_GU, F * SROW_GU);
+        tc::prefetch_l2_bulk(rn + Ln->shared_up.scales + f0 * SROW_GU, F * SROW_GU);
+        tc::prefetch_l2_bulk(rn + Ln->shared_up.biases + f0 * SROW_GU, F * SROW_GU);
+    }
+}
+
 __device__ void producer(Smem& s, const Params& P, const Plan& p) {
     if ((threadIdx.x & 31) != 0) return;
     uint32_t head = 0, tail = 0;
@@ -287,6 +314,7 @@ __device__ void producer(Smem& s, const Params& P, const Plan& p) {
         const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
         for (int i = 0; i < p.cpl && ok; ++i) {
             if (i == p.c_rgu) {   // the routed chunks follow: wait for this layer's top-8
+                l2_static(p, L, l + 1 < P.num_layers ? &P.layers[l + 1] : nullptr, cta, G);
                 const uint64_t t0 = globaltimer_ns();
                 while (s.topk_ready < l + 1) {
                     if (s.abort) { ok = false; break; }
@@ -430,11 +458,14 @@ __device__ __forceinline__ void table_item(const float (&x)[16], bool on, uint32
     }
 }
 
-// Tables of routed_x (ab[0, D)) and dense_x (ab[D, 2D)): 2 x 176 items (whole warps take part in
-// the builder's shuffles; threads past the items compute item 0 and store nothing).
-__device__ void build_views_tables(Smem& s) {
-    constexpr int N = 2 * 4 * GD;
-    const int i0 = threadIdx.x;
+// Tables of routed_x (ab[0, D)) and dense_x (ab[D, 2D)): 2 x 176 items, built by the compute
+// threads from `first` on (whole warps: they take part in the builder's shuffles).
+constexpr int VIEW_ITEMS = 2 * 4 * GD;
+static_assert(VIEW_ITEMS % 32 == 0, "view-table items fill whole warps");
+__device__ void build_views_tables(Smem& s, int first) {
+    constexpr int N = VIEW_ITEMS;
+    const int i0 = threadIdx.x - first;
+    if (i0 < 0) return;
     if (i0 < ((N + 31) & ~31)) {
         const bool on = i0 < N;
         const int i = on ? i0 : (i0 & 3);
@@ -541,17 +572,28 @@ __device__ __forceinline__ Split make_split(int n, int L) {
 __device__ __forceinline__ int first_warp(const Split& sp, int i, int L) {
     return ((i * L + 1) * NWC + sp.total - 1) / sp.total - 1;
 }
+// The contributor table of one phase (ph: 0 shared gate/up, 1 routed gate/up, 2 down), once per
+// launch by one thread.
+__device__ void fill_items(Smem& s, int ph, int n, int L) {
+    if (n <= 0) return;
+    const Split sp = make_split(n, L);
+    for (int i = 0; i < n; ++i) {
+        const int f = first_warp(sp, i, L);
+        const int last = min(NWC - 1, ((i + 1) * L * NWC + sp.total - 1) / sp.total - 1);   // holds pair (i + 1) L - 1
+        s.it_first[ph][i] = (uint8_t)f;
+        s.it_kend[ph][i] = (uint8_t)(last - f + 1);
+    }
+}
 // Sum of item i's partials for tile row r, in warp order.
-__device__ __forceinline__ float item_sum(const Smem& s, const Split& sp, int i, int L, int r) {
-    const int last = min(NWC - 1, ((i + 1) * L * NWC + sp.total - 1) / sp.total - 1);   // holds pair (i + 1) L - 1
-    const int k_end = last - first_warp(sp, i, L) + 1;
+__device__ __forceinline__ float item_sum(const Smem& s, const Split& sp, int ph, int i, int r) {
     const float* p = s.slot + (i * sp.max_k) * 16 + r;
+    const int k_end = s.it_kend[ph][i];
     float v = 0.0f;
     for (int k = 0; k < k_end; ++k) v += p[16 * k];
     return v;
 }
-__device__ __forceinline__ float* slot_of(Smem& s, const Split& sp, int i, int L, int warp) {
-    return s.slot + (i * sp.max_k + warp - first_warp(sp, i, L)) * 16;
+__device__ __forceinline__ float* slot_of(Smem& s, const Split& sp, int ph, int i, int warp) {
+    return s.slot + (i * sp.max_k + warp - s.it_first[ph][i]) * 16;
 }
 
 // Source rows of one 16-row tile for tile_groups.
@@ -585,8 +627,8 @@ __device__ __forceinline__ TileSrc gu_src(const uint8_t* base, int F, int lt, co
 // the chunk, tiles in the chunk). Every warp works its pairs, then releases the phase's chunks
 // [c_begin, c_end). Returns false when a wait gave up.
 template <class Locate>
-__device__ bool gu_phase(Smem& s, const Params& P, int n, int c_begin, int c_end, const uint32_t* tbl, const float2* gs,
-                         Locate locate) {
+__device__ bool gu_phase(Smem& s, const Params& P, int ph, int n, int c_begin, int c_end, const uint32_t* tbl,
+                         const float2* gs, Locate locate) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const Split sp = make_split(n, GD);
     int p = pw0(warp, sp.total);
@@ -606,7 +648,7 @@ __device__ bool gu_phase(Smem& s, const Params& P, int n, int c_begin, int c_end
         yb += __shfl_xor_sync(0xffffffffu, yb, 1);
         yb += __shfl_xor_sync(0xffffffffu, yb, 2);
         if (t == 0) {
-            float* sl = slot_of(s, sp, item, GD, warp);
+            float* sl = slot_of(s, sp, ph, item, warp);
             sl[g] = ya;
             sl[8 + g] = yb;
         }
@@ -621,12 +663,12 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 }
 
 // GeGLU of the phase's n tiles -> act[off + 8 * (first + item) + f].
-__device__ void gu_epilogue(const Smem& s, float* act, int n) {
+__device__ void gu_epilogue(const Smem& s, int ph, float* act, int n) {
     const Split sp = make_split(n, GD);
     for (int i = threadIdx.x; i < n * 8; i += NTC) {
         const int item = i >> 3, f = i & 7;
         const int rg = (f & 3) + 8 * (f >> 2);
-        const float gt = item_sum(s, sp, item, GD, rg), up = item_sum(s, sp, item, GD, rg + 4);
+        const float gt = item_sum(s, sp, ph, item, rg), up = item_sum(s, sp, ph, item, rg + 4);
         act[8 * item + f] = gelu_tanh_f(gt) * up;
     }
 }
@@ -784,8 +826,8 @@ __device__ __forceinline__ double sq4(const float (&v)[4]) {
 // optional weightless RMSNorm between layers, then the views of this layer
 // (src/cpu_reference.cpp:425-443): dense_x = h*w_pre, routed_x = h*w_pre2 and
 // router_in = h*bf16(router.scale)*(1/sqrt(D)) with h = rmsnorm_no_scale(hidden), exactly as the
-// reference rounds them; finally the fragment tables of dense_x and routed_x. Compute thread i owns
-// elements 4i..4i+3.
+// reference rounds them (their fragment tables are built next to the router rows). Compute thread
+// i owns elements 4i..4i+3.
 __device__ void tail_and_views(Smem& s, const Params& P, const Norms& nv, bool has_prev, bool norm_between,
                                bool do_views, float* h1_out, float* h2_out, float* hid_out) {
     const int i = threadIdx.x;
@@ -846,8 +888,6 @@ __device__ void tail_and_views(Smem& s, const Params& P, const Norms& nv, bool h
         s.u.t.ab[e] = __fmul_rn(h, bfw(nv.pre2, k));       // routed_x
         s.u.t.rin[(e >> 6) * RIN_PITCH + (e & 63)] = __fmul_rn(__fmul_rn(h, bfw(nv.rsc, k)), P.inv_sqrt_d);
     }
-    csync();
-    build_views_tables(s);
     csync();
 }
 
@@ -953,6 +993,9 @@ __device__ void plan_down(Smem& s, const Plan& p) {
     for (int a = 0; a < MAX_OTS; ++a)
         for (int q = 0; q < NSEG; ++q) s.dn_pos[a][q] = -1;
     for (int j = 0; j < k; ++j) s.dn_pos[s.dn_ot[j] - p.ot0][s.dn_q[j]] = j;
+    fill_items(s, 0, p.st1 - p.st0, GD);
+    fill_items(s, 1, p.rt1 - p.rt0, GD);
+    fill_items(s, 2, p.d1 - p.d0, GFE);
 }
 
 __device__ bool down_phase(Smem& s, const Params& P, const Plan& p, int c_first) {
@@ -985,7 +1028,7 @@ __device__ bool down_phase(Smem& s, const Params& P, const Plan& p, int c_first)
         yb += __shfl_xor_sync(0xffffffffu, yb, 1);
         yb += __shfl_xor_sync(0xffffffffu, yb, 2);
         if (t == 0) {
-            float* sl = slot_of(s, sp, k, GFE, warp);
+            float* sl = slot_of(s, sp, 2, k, warp);
             sl[g] = ya;
             sl[8 + g] = yb;
         }
@@ -1008,7 +1051,7 @@ __device__ void down_epilogue(Smem& s, const Params& P, const Plan& p) {
         float sh = 0.0f, h2 = 0.0f;
         for (int it = a; it < b; ++it) {
             const int q = it - ot * NSEG;
-            const float v = item_sum(s, sp, s.dn_pos[ot - p.ot0][q], GFE, r);
+            const float v = item_sum(s, sp, 2, s.dn_pos[ot - p.ot0][q], r);
             if (q < 3) sh = __fadd_rn(sh, v);
             else h2 = __fadd_rn(h2, __fmul_rn(s.topw[q - 3], v));   // the product rounded, as the combine had it
         }
@@ -1074,9 +1117,11 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
                        writer && io.h2_dev && l > 0 ? io.h2_dev + (size_t)(l - 1) * D : nullptr,
                        writer && io.hidden_layers_dev && l > 0 ? io.hidden_layers_dev + (size_t)(l - 1) * D : nullptr);
 
-        // ---- router rows (the logit words double as barrier A) ----
+        // ---- router rows (the logit words double as barrier A) on warps 0-1, while warps 2-12
+        //      build the fragment tables of the views ----
         int cur = cbase;
         bool ok = true;
+        if (warp >= 2) build_views_tables(s, 64);
         for (int k = 0; k < p.nr; ++k) {
             if (warp < 2) {
                 const int row = cta + k * G;
@@ -1095,10 +1140,11 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
         }
         if (ok) ok = release_to(s, P, cur, cbase + p.nr);
         if (!ok) s.abort = 1;
+        csync();   // the view tables are complete
 
         // ---- shared gate/up ----
         if (ok && p.st1 > p.st0) {
-            ok = gu_phase(s, P, p.st1 - p.st0, cbase + p.c_sgu, cbase + p.c_rgu, s.tbl_d, s.gs_d,
+            ok = gu_phase(s, P, 0, p.st1 - p.st0, cbase + p.c_sgu, cbase + p.c_rgu, s.tbl_d, s.gs_d,
                           [&](int item, int& c, int& lt, int& F) {
                               const int k = item / GU_TILES;
                               c = cbase + p.c_sgu + k;
@@ -1107,7 +1153,7 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
                           });
             if (!ok) s.abort = 1;
             csync();
-            if (!s.abort) gu_epilogue(s, P.act + 8 * p.st0, p.st1 - p.st0);
+            if (!s.abort) gu_epilogue(s, 0, P.act + 8 * p.st0, p.st1 - p.st0);
         }
         csync();
         if (s.abort) break;
@@ -1151,7 +1197,7 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
         if (s.abort) break;
 
         // ---- routed gate/up ----
-        ok = gu_phase(s, P, p.rt1 - p.rt0, cbase + p.c_rgu, cbase + p.c_dn, s.tbl_r, s.gs_r,
+        ok = gu_phase(s, P, 1, p.rt1 - p.rt0, cbase + p.c_rgu, cbase + p.c_dn, s.tbl_r, s.gs_r,
                       [&](int item, int& c, int& lt, int& F) {
                           int k, t0;
                           rgu_locate(p, p.rt0 + item, k, t0);
@@ -1164,7 +1210,7 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
         if (!ok) s.abort = 1;
         csync();
         if (s.abort) break;
-        gu_epilogue(s, P.act + FS + 8 * p.rt0, p.rt1 - p.rt0);
+        gu_epilogue(s, 1, P.act + FS + 8 * p.rt0, p.rt1 - p.rt0);
         arrive(P, P.flags_b, ep);
 
         // ---- down: the shared and routed activations of every CTA ----
