@@ -153,3 +153,28 @@ def test_bounded_wait_runs_out_then_workspace_recovers(model1):
     want = oracle.SynthLayer(0, 0).block(oracle.synth_x(0, 3))
     assert np.array_equal(g["idx"][0], want["idx"])
     assert rel_max(g["hidden"], want["hidden"]) <= TOL
+
+
+@pytest.mark.parametrize("case", ["zero_group", "outlier", "tiny", "mixed_scale"])
+def test_config0_activation_ranges(model1, case):
+    """The decode carries each 64-element group of an activation as three 7-bit limbs under a
+    power-of-two group scale: a group of zeros, one element 1e4 times its neighbours, values near
+    the float minimum and groups of very different magnitude keep exact routing and the 2e-3 gate."""
+    x = oracle.synth_x(0, 11).copy()
+    if case == "zero_group":
+        x[64:128] = 0.0
+        x[1000:1064] = 0.0
+    elif case == "outlier":
+        x[70] = 1.0e4
+        x[2000] = -3.0e3
+    elif case == "tiny":
+        x[:704] *= 1.0e-30
+    else:
+        x *= np.repeat(np.float32(10.0) ** np.arange(-3, 3, 6 / 44, dtype=np.float32)[:44], 64)
+    dec = gtmoe.Decoder(model1.layers, 1)
+    g = run(dec, torch.from_numpy(x).cuda(), 1, norm_between_layers=False)
+    want = oracle.SynthLayer(0, 0).block(x)
+    assert np.array_equal(g["logits"][0], want["logits"]), "router logits not bit-identical"
+    assert np.array_equal(g["idx"][0], want["idx"])
+    for key, gv in (("h1", g["h1"][0]), ("h2", g["h2"][0]), ("hidden", g["hidden"])):
+        assert rel_max(gv, want[key]) <= TOL, (key, rel_max(gv, want[key]))

@@ -165,12 +165,6 @@ __device__ __forceinline__ void csync() { tc::named_bar_sync(1, NTC); }   // the
 
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
-__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 // ---- plan ------------------------------------------------------------------------------------------
 // Routed gate/up chunks: the CTA's tiles [rt0, rt1) cut at expert boundaries (every 88 tiles) and
 // into pieces of at most GU_TILES.
@@ -400,64 +394,6 @@ __device__ void producer(Smem& s, const Params& P, const Plan& p) {
 }
 
 // ---- fragment tables -----------------------------------------------------------------------------
-// Table of a vector, per quad Q and double group h: 12 lane entries of 8 words at (2 Q + h) * 96
-// + e * 8, one per lane (g, t) that holds nonzero B values: g = 4 a + limb (limb < 3) with a = t >> 1
-// (the lane pair of group 2 h + a), e = 6 a + 2 limb + (t & 1). Words 2 w, 2 w + 1 of the entry are
-// the lane's b0, b1 for the MMA of word w: limb `limb` of the elements 128 h + 32 t + 8 w + {0, 2,
-// 4, 6} and {1, 3, 5, 7} of the quad, one signed byte each (K slot 4 t + i and 4 t + 16 + i hold
-// nibbles 2 i and 2 i + 1 of the lane's word w). The 12 reading lanes of a double group take 384
-// consecutive bytes.
-// One builder thread per (group j, sub): the 16 elements 16 sub + (0..15) of the group, i.e. words
-// 2 (sub & 1) and 2 (sub & 1) + 1 of lane t = 2 (j & 1) + (sub >> 1) of the group's double group;
-// the four builder lanes of a group (adjacent) share its largest magnitude and its sum.
-// The low bytes of four words, a in the lowest.
-__device__ __forceinline__ uint32_t pack_s8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
-}
-__device__ __forceinline__ void table_item(const float (&x)[16], bool on, uint32_t* tbl_q, int gq, int sub,
-                                           float2* gs, int j) {
-    float mx = 0.0f, sx = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) { mx = fmaxf(mx, fabsf(x[e])); sx += x[e]; }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    sx += __shfl_xor_sync(0xffffffffu, sx, 1);
-    sx += __shfl_xor_sync(0xffffffffu, sx, 2);
-    // |x| < 2^E for the group (exponent field of the largest magnitude, minus 126), kept >= -120
-    const int E = max((int)((__float_as_uint(mx) >> 23) & 0xFFu) - 126, -120);
-    const float up = __int_as_float((127 + 6 - E) << 23);     // 2^(6-E): |x up| < 64
-    // round to nearest even by adding 1.5 * 2^23 (|v| <= 64): the sum's low mantissa bits are the
-    // integer, whose low byte is the limb in two's complement; all steps are exact
-    constexpr float kMagic = 12582912.0f;
-    uint32_t L[3][16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-        const float v = x[e] * up;                            // exact (power of two)
-        const float f0 = v + kMagic;
-        const float v1 = (v - (f0 - kMagic)) * 128.0f;        // exact; |v1| <= 64
-        const float f1 = v1 + kMagic;
-        const float f2 = (v1 - (f1 - kMagic)) * 128.0f + kMagic;
-        L[0][e] = __float_as_uint(f0);
-        L[1][e] = __float_as_uint(f1);
-        L[2][e] = __float_as_uint(f2);
-    }
-    const int h = gq >> 1, a = gq & 1, tl = sub >> 1, wp = sub & 1;
-    uint32_t* base = tbl_q + h * 96;
-    if (on) {
-#pragma unroll
-        for (int limb = 0; limb < 3; ++limb) {
-            uint32_t* ent = base + (6 * a + 2 * limb + tl) * 8;
-#pragma unroll
-            for (int ww = 0; ww < 2; ++ww) {
-                const int b = 8 * ww;
-                ent[2 * (2 * wp + ww)] = pack_s8(L[limb][b], L[limb][b + 2], L[limb][b + 4], L[limb][b + 6]);
-                ent[2 * (2 * wp + ww) + 1] = pack_s8(L[limb][b + 1], L[limb][b + 3], L[limb][b + 5], L[limb][b + 7]);
-            }
-        }
-        if (sub == 0) gs[j] = make_float2(sx, __int_as_float((127 + E - 6) << 23));
-    }
-}
-
 // Tables of routed_x (ab[0, D)) and dense_x (ab[D, 2D)): 2 x 176 items, built by the compute
 // threads from `first` on (whole warps: they take part in the builder's shuffles).
 constexpr int VIEW_ITEMS = 2 * 4 * GD;
@@ -478,7 +414,7 @@ __device__ void build_views_tables(Smem& s, int first) {
             x[4 * q] = f.x; x[4 * q + 1] = f.y; x[4 * q + 2] = f.z; x[4 * q + 3] = f.w;
         }
         uint32_t* tbl = v ? s.tbl_d : s.tbl_r;
-        table_item(x, on, tbl + (j >> 2) * QW, j & 3, sub, v ? s.gs_d : s.gs_r, j);
+        limb_item(x, on, tbl + (j >> 2) * QW, j & 3, sub, v ? s.gs_d : s.gs_r, j);
     }
 }
 
@@ -503,7 +439,7 @@ __device__ void build_down_tables(Smem& s, const Params& P) {
 #pragma unroll
             for (int e = 0; e < 16; ++e) x[e] = 0.0f;
         }
-        table_item(x, on, s.u.tbl_dn + q * QS * QW + (j >> 2) * QW, j & 3, sub, s.gs_dn + q * 12, j);
+        limb_item(x, on, s.u.tbl_dn + q * QS * QW + (j >> 2) * QW, j & 3, sub, s.gs_dn + q * 12, j);
     }
 }
 
