@@ -257,7 +257,17 @@ typedef struct GtmTokensIO {
     const float* logit_bias_dev;     /* [experts] added to every token's logits (NULL = none) */
     const float* route_logits_dev;   /* [T][experts] routing logits given by the caller; the
                                         router GEMV is skipped (NULL = compute them)        */
+    uint32_t flags;                  /* 0, or GTM_TOKENS_TEST_WAIT_RUNS_OUT (gtm_moe_tokens) */
 } GtmTokensIO;
+
+enum {
+    /* Test hook for the grouped GEMM's bounded pipeline waits (gtm_moe_tokens only): in the
+     * gate/up GEMM the MMA warp of every CTA first waits on a barrier nothing arrives at, under a
+     * 2 ms limit instead of 1 s, gives up and raises the CTA's abort flag, so every role leaves
+     * its loop, the CTA frees its tensor memory and GTM_ERR_TIMEOUT is recorded (read by
+     * gtm_moe_tokens_check); outputs are not written. The workspace stays usable. */
+    GTM_TOKENS_TEST_WAIT_RUNS_OUT = 0x100
+};
 
 /* Workspace for gtm_moe_tokens with up to `max_tokens` tokens (0 for unsupported dims).
  * Zero it once before its first use; a workspace serves one stream at a time. */

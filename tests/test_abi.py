@@ -87,7 +87,8 @@ def test_resident_layout_is_16k_aligned():
     assert all(o % 16384 == 0 for o in off) and total % 16384 == 0
 
 
-@pytest.mark.parametrize("field,size", [("Layer", 8 + 24 + 16 + 72 + 48 + 8 + 8 + 72), ("DecodeIO", 9 * 8 + 8)])
+@pytest.mark.parametrize("field,size", [("Layer", 8 + 24 + 16 + 72 + 48 + 8 + 8 + 72), ("DecodeIO", 9 * 8 + 8),
+                                        ("TokensIO", 8 + 10 * 8 + 8)])
 def test_struct_sizes(field, size):
     assert C.sizeof(getattr(gtmoe, field)) == size
 

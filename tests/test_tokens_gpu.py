@@ -166,3 +166,28 @@ def test_forced_routing_tile_edges(model, ref_layer, block, T):
     xs = x.cpu().numpy()
     for t in sorted({0, 31 % T, 32 % T, 63 % T, 64 % T, T // 2, T - 1}):
         check_token(ref_layer, got, t, xs[t], route_logits=rl[t], exact_logits=False)
+
+
+def test_grouped_gemm_wait_runs_out_then_workspace_recovers(model, ref_layer, block):
+    """GTM_TOKENS_TEST_WAIT_RUNS_OUT: in the gate/up GEMM the MMA warp of every CTA first waits on
+    a barrier nothing arrives at, under a 2 ms limit. It gives up and raises the CTA's abort flag;
+    the producers, the dequant and the epilogue leave their bounded waits through that flag, the
+    CTA frees its tensor memory, and gtm_moe_tokens_check reports GTM_ERR_TIMEOUT with the context
+    usable. The next call on the same workspace matches the oracle (routed tiles gathered by
+    cp.async and shared-expert tiles loaded by TMA are both in flight when the wait runs out)."""
+    import time
+    T = 200
+    x = synth_tokens(T, token0=900)
+    out = torch.empty(T, D, device="cuda")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    block(model.layers[0], x, out, extra_flags=gtmoe.TOKENS_TEST_WAIT_RUNS_OUT)
+    with pytest.raises(gtmoe.GtmError) as e:
+        block.check()
+    assert e.value.status == gtmoe.ERR_TIMEOUT and "timed out" in str(e.value)
+    assert time.perf_counter() - t0 < 10.0
+    block.check()   # the failing check cleared the error word
+    got = run(block, model, x)
+    xs = x.cpu().numpy()
+    for t in (0, T // 2, T - 1):
+        check_token(ref_layer, got, t, xs[t])

@@ -559,6 +559,7 @@ struct GemmArgs {
     const int* act_row;
     int act_div;
     int* err;
+    int test_wait;                        // GTM_TOKENS_TEST_WAIT_RUNS_OUT: the MMA warp's first wait never ends
 };
 
 __device__ __forceinline__ float* remap_row(const GemmArgs& A, int orow) {
@@ -665,8 +666,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NSLOT);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+    __shared__ uint64_t never_bar;               // test hook: a barrier nothing arrives at
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
+        tc::mbar_init(&never_bar, 1);
         for (int s = 0; s < SX; ++s) { tc::mbar_init(&act_full[s], 2); tc::mbar_init(&act_empty[s], 1); }
         for (int s = 0; s < RS; ++s) { tc::mbar_init(&raw_full[s], 1); tc::mbar_init(&raw_empty[s], DQ_THREADS); }
         for (int s = 0; s < SW; ++s) { tc::mbar_init(&w_full[s], DQ_THREADS); tc::mbar_init(&w_empty[s], 1); }
@@ -807,6 +810,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm(const __grid_constant
         //      block 1 of the last gate/up tile lies past the matrix: skipped. ----
         uint32_t it = 0, acc_it = 0;
         bool ok = true;
+        if (A.test_wait && !__all_sync(0xffffffffu, tc::mbar_wait(&never_bar, 0, abort_flag, 2000000ull))) ok = false;
         for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x, ++acc_it) {
             const TileInfo ti = tile_info(A, i);
             const int kout = ti.routed ? A.rows_r : A.rows_s;
@@ -1319,6 +1323,7 @@ struct Plan {
     const int* out_index;         // mode 1 output row of each expert-ordered row (null: same)
     float* out_r;                 // mode 1 routed output rows
     bool own_tiles;               // shared-expert-only plan: tile lists in the stiles* regions
+    bool test_wait;               // GTM_TOKENS_TEST_WAIT_RUNS_OUT (gate/up GEMM)
     // peer-memory expert parallelism (nsrc > 0): entry i is entry i % per_src of rank i / per_src,
     // read from that rank's workspace; its result goes to that rank's return region
     int nsrc, per_src;
@@ -1390,7 +1395,7 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     g1.w_rb = g1.w_ra;
     g1.w_sb = g1.w_sa;
 
-    g0.tiles = ra.tiles0; g0.n_tiles = ra.n_tiles;
+    g0.tiles = ra.tiles0; g0.n_tiles = ra.n_tiles; g0.test_wait = pl.test_wait ? 1 : 0;
     g0.experts = exb; g0.expert_stride = L.expert_stride; g0.resident = res;
     g0.r_sa = L.expert_gate.scales; g0.r_ba = L.expert_gate.biases; g0.r_sb = L.expert_up.scales; g0.r_bb = L.expert_up.biases;
     g0.s_sa = L.shared_gate.scales; g0.s_ba = L.shared_gate.biases; g0.s_sb = L.shared_up.scales; g0.s_bb = L.shared_up.biases;
@@ -1451,6 +1456,7 @@ int launch_tokens(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
     pl.n = (int)(T * TOPK); pl.src_div = TOPK; pl.idx = w.p<uint32_t>(w.W.idx); pl.stride = 1;
     pl.e0 = 0; pl.ne = NE; pl.t_shared = (int)T; pl.act_src = w.p<__half>(w.W.routed); pl.out_index = nullptr;
     pl.out_r = w.p<float>(w.W.out_r);
+    pl.test_wait = (io.flags & GTM_TOKENS_TEST_WAIT_RUNS_OUT) != 0;
     const int rc = run_gemms(L, w, pl, num_sms, st);
     if (rc) return rc;
     mark_phase(4, st);

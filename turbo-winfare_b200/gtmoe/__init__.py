@@ -27,6 +27,7 @@ HIDDEN, MOE_INTER, FFN, EXPERTS, TOP_K, EPS = 2816, 704, 2112, 128, 8, 1e-6
 MAX_LAYERS = 64
 NORM_BETWEEN_LAYERS = 1
 DECODE_TEST_WAIT_RUNS_OUT = 0x100   # GTM_DECODE_TEST_WAIT_RUNS_OUT (include/gtmoe.h)
+TOKENS_TEST_WAIT_RUNS_OUT = 0x100   # GTM_TOKENS_TEST_WAIT_RUNS_OUT (include/gtmoe.h)
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE, ERR_MISALIGNED = 0, -1, -2, -3, -4, -5, -6
 
@@ -70,7 +71,7 @@ class TokensIO(C.Structure):
     _fields_ = [("num_tokens", C.c_uint32), ("x_dev", C.c_void_p), ("x_bf16_dev", C.c_void_p),
                 ("hidden_out_dev", C.c_void_p), ("topk_idx_dev", C.c_void_p), ("topk_w_dev", C.c_void_p),
                 ("logits_dev", C.c_void_p), ("h1_dev", C.c_void_p), ("h2_dev", C.c_void_p),
-                ("logit_bias_dev", C.c_void_p), ("route_logits_dev", C.c_void_p)]
+                ("logit_bias_dev", C.c_void_p), ("route_logits_dev", C.c_void_p), ("flags", C.c_uint32)]
 
 
 class EpConfig(C.Structure):
@@ -403,7 +404,7 @@ class TokenBlock:
         self.ws_bytes = n
 
     def __call__(self, layer: Layer, x, hidden_out, *, topk_idx=None, topk_w=None, logits=None, h1=None, h2=None,
-                 logit_bias=None, route_logits=None, stream=None):
+                 logit_bias=None, route_logits=None, stream=None, extra_flags=0):
         """x: [T, hidden] float32 or bfloat16 on the device; hidden_out: [T, hidden] float32."""
         import torch
         T = x.shape[0]
@@ -412,7 +413,7 @@ class TokenBlock:
         if xf is None and xb is None:
             raise TypeError("x must be float32 or bfloat16")
         io = TokensIO(T, ptr(xf), ptr(xb), hidden_out.data_ptr(), ptr(topk_idx), ptr(topk_w), ptr(logits), ptr(h1),
-                      ptr(h2), ptr(logit_bias), ptr(route_logits))
+                      ptr(h2), ptr(logit_bias), ptr(route_logits), extra_flags)
         check(lib().gtm_moe_tokens(C.byref(self.dims), C.byref(layer), C.byref(io), self.ws_ptr, self.ws_bytes,
                                    _stream(stream)))
 
