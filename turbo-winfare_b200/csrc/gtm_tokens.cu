@@ -134,6 +134,148 @@ struct ViewsArgs {
     int npeers, epr;
 };
 
+// Top-8 of one token's 128 logits by (value desc, index asc), softmax over the 8 times the
+// per-expert scale (src/cpu_reference.cpp:447-480). One warp; lane holds experts lane + 32 j
+// (`raw`: before the logit bias). Writes the token's ids and weights (and its biased logits when
+// asked); lane k < 8 returns the k-th id.
+__device__ __forceinline__ int route_top8(const ViewsArgs& A, int t, const float (&raw)[4]) {
+    const GtmLayer& L = A.L;
+    const int lane = threadIdx.x & 31;
+    uint32_t key[4];
+    bool taken[4] = {false, false, false, false};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int e = lane + 32 * j;
+        const float v = A.logit_bias ? __fadd_rn(raw[j], A.logit_bias[e]) : raw[j];
+        if (A.logits_out) A.logits_out[(size_t)t * NE + e] = v;
+        const uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
+        key[j] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    }
+    float my_sel = 0.0f, top0 = 0.0f;
+    int my_idx = 0;
+#pragma unroll
+    for (int k = 0; k < TOPK; ++k) {
+        uint32_t ck = 0u, ci = 0xFFFFFFFFu;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (!taken[j] && (ci == 0xFFFFFFFFu || key[j] > ck)) { ck = key[j]; ci = (uint32_t)(lane + 32 * j); }
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, ck);
+        const uint32_t bi = __reduce_min_sync(0xffffffffu, ck == mk ? ci : 0xFFFFFFFFu);
+        const float bv = __uint_as_float((mk & 0x80000000u) ? (mk & 0x7FFFFFFFu) : ~mk);
+        if (k == 0) top0 = bv;
+        if (lane == k) { my_sel = bv; my_idx = (int)bi; }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) if ((uint32_t)(lane + 32 * j) == bi) taken[j] = true;
+    }
+    const float e = lane < TOPK ? expf(__fsub_rn(my_sel, top0)) : 0.0f;
+    const uint16_t pes = lane < TOPK ? *rp16(L.resident_dev, L.per_expert_scale + 2ull * (uint32_t)my_idx) : 0;
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < TOPK; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, k));
+    if (lane < TOPK) {
+        A.idx[(size_t)t * TOPK + lane] = (uint32_t)my_idx;
+        A.w[(size_t)t * TOPK + lane] = __fmul_rn(__fdiv_rn(e, sum), bf16f(pes));
+    }
+    return my_idx;
+}
+
+// Views of one token when the caller gives the routing logits, no peer takes the rows (no
+// router GEMV, no staging for pushes) and x is 16-byte aligned: 128 threads, each holding three 8-element chunks of x in
+// registers; the RMS is the same certified double sum as exact_rms_inv (bit-identical result in
+// any summation order, sequential recomputation when too close to a rounding midpoint); the four
+// fp16 views of a chunk go out as one 16-byte store each (kperm permutes inside 8 elements). Same
+// arithmetic, element for element, as tok_views_router.
+constexpr int VG_THREADS = 128, VG_CH = (D / 8 + VG_THREADS - 1) / VG_THREADS;
+__global__ void __launch_bounds__(VG_THREADS) tok_views_given(const __grid_constant__ ViewsArgs A) {
+    __shared__ double red[VG_THREADS / 32 + 1];
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const GtmLayer& L = A.L;
+    float x[VG_CH][8];
+    double acc = 0.0;
+#pragma unroll
+    for (int c = 0; c < VG_CH; ++c) {
+        const int ch = tid + c * VG_THREADS;
+        if (ch < D / 8) {
+            if (A.x_f32) {
+                const float4* p4 = reinterpret_cast<const float4*>(A.x_f32 + (size_t)t * D + 8 * ch);
+                const float4 a = p4[0], b = p4[1];
+                x[c][0] = a.x; x[c][1] = a.y; x[c][2] = a.z; x[c][3] = a.w;
+                x[c][4] = b.x; x[c][5] = b.y; x[c][6] = b.z; x[c][7] = b.w;
+            } else {
+                const uint4 q = *reinterpret_cast<const uint4*>(A.x_bf16 + (size_t)t * D + 8 * ch);
+                const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    x[c][2 * k] = __uint_as_float(wv[k] << 16);
+                    x[c][2 * k + 1] = __uint_as_float(wv[k] & 0xFFFF0000u);
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc = __dadd_rn(acc, __dmul_rn((double)x[c][e], (double)x[c][e]));
+        }
+    }
+    acc = warp_sum_d(acc);
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    if (tid == 0) {
+        double sm = 0.0;
+        for (int w = 0; w < VG_THREADS / 32; ++w) sm = __dadd_rn(sm, red[w]);
+        const double q = __ddiv_rn(sm, (double)D);
+        float f = __double2float_rn(q);
+        const double fd = (double)f;
+        const double lo = (fd + (double)nextafterf(f, -INFINITY)) * 0.5;
+        const double hi = (fd + (double)nextafterf(f, INFINITY)) * 0.5;
+        const double bound = q * ((double)D + 48.0) * 1.1102230246251565e-16;   // (n + 48) 2^-53
+        if (!(q - lo > bound && hi - q > bound)) {   // too close to call: the sequential sum
+            double seq = 0.0;
+            for (int i = 0; i < D; ++i) {
+                const double v = A.x_f32 ? (double)A.x_f32[(size_t)t * D + i] : (double)bf16f(A.x_bf16[(size_t)t * D + i]);
+                seq = __dadd_rn(seq, __dmul_rn(v, v));
+            }
+            f = __double2float_rn(__ddiv_rn(seq, (double)D));
+        }
+        red[VG_THREADS / 32] = (double)__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, A.eps)));
+    }
+    __syncthreads();
+    const float inv = (float)red[VG_THREADS / 32];
+    const uint16_t* w_pre = rp16(L.resident_dev, L.pre_ffn_norm);
+    const uint16_t* w_pre2 = rp16(L.resident_dev, L.pre_ffn_norm_2);
+#pragma unroll
+    for (int c = 0; c < VG_CH; ++c) {
+        const int ch = tid + c * VG_THREADS;
+        if (ch >= D / 8) continue;
+        const int i0 = 8 * ch;
+        uint16_t dh[8], dl[8], rh[8], rl[8];   // at positions kperm(i) - i0
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int pe = kperm(e);
+            const float h = __fmul_rn(x[c][e], inv);
+            const float dx = __fmul_rn(h, bf16f(w_pre[i0 + e]));
+            const __half hi = __float2half_rn(dx);
+            dh[pe] = __half_as_ushort(hi);
+            dl[pe] = __half_as_ushort(__float2half_rn(dx - __half2float(hi)));
+            const float rx = __fmul_rn(h, bf16f(w_pre2[i0 + e]));
+            const __half r = __float2half_rn(rx);
+            rh[pe] = __half_as_ushort(r);
+            rl[pe] = __half_as_ushort(__float2half_rn(rx - __half2float(r)));
+        }
+        auto pack = [](const uint16_t (&v)[8]) {
+            return make_uint4(v[0] | ((uint32_t)v[1] << 16), v[2] | ((uint32_t)v[3] << 16), v[4] | ((uint32_t)v[5] << 16),
+                              v[6] | ((uint32_t)v[7] << 16));
+        };
+        *reinterpret_cast<uint4*>(A.dense_hi + (size_t)t * D + i0) = pack(dh);
+        *reinterpret_cast<uint4*>(A.dense_lo + (size_t)t * D + i0) = pack(dl);
+        *reinterpret_cast<uint4*>(A.routed_hl + (size_t)t * 2 * D + i0) = pack(rh);
+        *reinterpret_cast<uint4*>(A.routed_hl + (size_t)t * 2 * D + D + i0) = pack(rl);
+    }
+    if (warp == 0) {
+        float raw[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) raw[j] = A.route_logits[(size_t)t * NE + lane + 32 * j];
+        route_top8(A, t, raw);
+    }
+}
+
 // 512 threads a token when the routing logits are given; 1024 when the router GEMV runs, so that
 // one round covers 23 router rows (44 threads a row) instead of 11.
 constexpr int VIEWS_RR_MAX = 1024 / GD;
@@ -223,48 +365,15 @@ __global__ void __launch_bounds__(1024) tok_views_router(const __grid_constant__
     }
     __syncthreads();
     if (tid < 32) {
-        // top-8 by (value desc, index asc), src/cpu_reference.cpp:447-480
-        const int lane = tid;
-        uint32_t key[4];
-        bool taken[4] = {false, false, false, false};
+        float raw[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int e = lane + 32 * j;
-            const float v = A.logit_bias ? __fadd_rn(slog[e], A.logit_bias[e]) : slog[e];
-            if (A.logits_out) A.logits_out[(size_t)t * NE + e] = v;
-            const uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
-            key[j] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-        }
-        float my_sel = 0.0f, top0 = 0.0f;
-        int my_idx = 0;
-#pragma unroll
-        for (int k = 0; k < TOPK; ++k) {
-            uint32_t ck = 0u, ci = 0xFFFFFFFFu;
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (!taken[j] && (ci == 0xFFFFFFFFu || key[j] > ck)) { ck = key[j]; ci = (uint32_t)(lane + 32 * j); }
-            const uint32_t mk = __reduce_max_sync(0xffffffffu, ck);
-            const uint32_t bi = __reduce_min_sync(0xffffffffu, ck == mk ? ci : 0xFFFFFFFFu);
-            const float bv = __uint_as_float((mk & 0x80000000u) ? (mk & 0x7FFFFFFFu) : ~mk);
-            if (k == 0) top0 = bv;
-            if (lane == k) { my_sel = bv; my_idx = (int)bi; }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) if ((uint32_t)(lane + 32 * j) == bi) taken[j] = true;
-        }
-        const float e = lane < TOPK ? expf(__fsub_rn(my_sel, top0)) : 0.0f;
-        const uint16_t pes = lane < TOPK ? *rp16(L.resident_dev, L.per_expert_scale + 2ull * (uint32_t)my_idx) : 0;
-        float sum = 0.0f;
-#pragma unroll
-        for (int k = 0; k < TOPK; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, k));
-        if (lane < TOPK) {
-            A.idx[(size_t)t * TOPK + lane] = (uint32_t)my_idx;
-            A.w[(size_t)t * TOPK + lane] = __fmul_rn(__fdiv_rn(e, sum), bf16f(pes));
-        }
+        for (int j = 0; j < 4; ++j) raw[j] = slog[tid + 32 * j];
+        const int my_idx = route_top8(A, t, raw);
         if (A.npeers > 0) {
-            const uint32_t dest = __reduce_or_sync(0xffffffffu, lane < TOPK ? 1u << (my_idx / A.epr) : 0u);
-            if (lane == 0) sdest = dest;
+            const uint32_t dest = __reduce_or_sync(0xffffffffu, tid < TOPK ? 1u << (my_idx / A.epr) : 0u);
+            if (tid == 0) sdest = dest;
             for (int s = 0; s < A.npeers; ++s)
-                if (A.push_idx[s] && lane < TOPK) A.push_idx[s][(size_t)t * TOPK + lane] = (uint32_t)my_idx;
+                if (A.push_idx[s] && tid < TOPK) A.push_idx[s][(size_t)t * TOPK + tid] = (uint32_t)my_idx;
         }
     }
     if (A.npeers > 0) {
@@ -1308,7 +1417,9 @@ void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
             va.push_views[s] = ps.p<__half>(w.W.routed);
         }
     }
-    tok_views_router<<<io.num_tokens, io.route_logits_dev ? 512 : 1024, 0, st>>>(va);
+    const uintptr_t xa = reinterpret_cast<uintptr_t>(io.x_dev ? static_cast<const void*>(io.x_dev) : io.x_bf16_dev);
+    if (io.route_logits_dev && !peer_ws && (xa & 15) == 0) tok_views_given<<<io.num_tokens, VG_THREADS, 0, st>>>(va);
+    else tok_views_router<<<io.num_tokens, io.route_logits_dev ? 512 : 1024, 0, st>>>(va);
 }
 
 // What one pass of the two grouped GEMMs runs over.
