@@ -481,9 +481,10 @@ def measure_tokens(cfg: str, steps: int, warmup: int, rank: int, world: int, loc
     idx_hist = torch.empty(n_sets, T, K, dtype=torch.int32, device="cuda")
 
     # kernels of ours per step (NCCL collectives not counted): views 1, routing 3 (count, scan,
-    # scatter), grouped GEMMs 2, combine 1; peer expert parallelism adds the token-count word and the
-    # shared-expert pass (scan + 2 GEMMs); the NCCL variant the dispatch pair
-    launches = 7
+    # scatter; one fused kernel when the entries fit one 1024-entry chunk), grouped GEMMs 2,
+    # combine 1; peer expert parallelism adds the token-count word and the shared-expert pass
+    # (scan + 2 GEMMs); the NCCL variant the dispatch pair
+    launches = 7 if T * K > 1024 else 5
     phase_names = None
     if expert_parallel:
         shard = ep.EpShardModel(0, rank, world)

@@ -179,8 +179,8 @@ __device__ __forceinline__ int route_top8(const ViewsArgs& A, int t, const float
     return my_idx;
 }
 
-// Views of one token when the caller gives the routing logits, no peer takes the rows (no
-// router GEMV, no staging for pushes) and x is 16-byte aligned: 128 threads, each holding three 8-element chunks of x in
+// Views of one token when the routing logits are given (by the caller, or by tok_router_rows), no
+// peer takes the rows (no staging for pushes) and x is 16-byte aligned: 128 threads, each holding three 8-element chunks of x in
 // registers; the RMS is the same certified double sum as exact_rms_inv (bit-identical result in
 // any summation order, sequential recomputation when too close to a rounding midpoint); the four
 // fp16 views of a chunk go out as one 16-byte store each (kperm permutes inside 8 elements). Same
@@ -273,6 +273,66 @@ __global__ void __launch_bounds__(VG_THREADS) tok_views_given(const __grid_const
 #pragma unroll
         for (int j = 0; j < 4; ++j) raw[j] = A.route_logits[(size_t)t * NE + lane + 32 * j];
         route_top8(A, t, raw);
+    }
+}
+
+// Router logits of token blockIdx.x, rows 16 blockIdx.y .. + 15, in src/cpu_reference.cpp:86-106's
+// order (per row and group the 64 products summed in element order, the group's scale times that
+// plus its bias times the group's input sum, the 44 group terms summed in group order): the same
+// arithmetic as the router rows of tok_views_router, one round of 16 rows x 44 groups. Every CTA of
+// a token recomputes the token's exact RMS and router input (2816 elements, far less than its
+// 45 KB of router rows). The logits go to `rlog` (before the logit bias) for tok_views_given.
+constexpr int RR_ROWS = 16, RR_THREADS = RR_ROWS * GD;   // 704
+__global__ void __launch_bounds__(RR_THREADS) tok_router_rows(const __grid_constant__ ViewsArgs A, float* rlog) {
+    __shared__ __align__(16) float sx[D];
+    __shared__ __align__(16) float srin[GD * RIN_PITCH];
+    __shared__ float xsum[GD];
+    __shared__ float terms[RR_ROWS][GD];
+    __shared__ double red[40];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const GtmLayer& L = A.L;
+    for (int i = tid; i < D; i += RR_THREADS)
+        sx[i] = A.x_f32 ? A.x_f32[(size_t)t * D + i] : bf16f(A.x_bf16[(size_t)t * D + i]);
+    __syncthreads();
+    const float inv = exact_rms_inv(sx, D, A.eps, red);
+    const uint16_t* rs = rp16(L.resident_dev, L.router_scale);
+    for (int i = tid; i < D; i += RR_THREADS)
+        srin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(__fmul_rn(sx[i], inv), bf16f(rs[i])), A.inv_sqrt_d);
+    __syncthreads();
+    if (tid < GD) {
+        float sm = 0.0f;
+        for (int k = 0; k < kGroup; ++k) sm = __fadd_rn(sm, srin[tid * RIN_PITCH + k]);
+        xsum[tid] = sm;
+    }
+    __syncthreads();
+    const int rr = tid / GD, g = tid - rr * GD, row = blockIdx.y * RR_ROWS + rr;
+    const uint8_t* W = static_cast<const uint8_t*>(L.resident_dev) + L.router.weight;
+    const uint4* wg = reinterpret_cast<const uint4*>(W + (size_t)row * D + g * kGroup);
+    const float4* x4 = reinterpret_cast<const float4*>(srin + g * RIN_PITCH);
+    float dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 q = ldg_stream_u4(wg + i);
+        const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float4 xv = x4[i * 4 + c];
+            const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const float wf = __uint_as_float(__byte_perm(wv[c], 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388608.0f;
+                dot = __fadd_rn(dot, __fmul_rn(wf, xs[b]));
+            }
+        }
+    }
+    const uint16_t* Sc = rp16(L.resident_dev, L.router.scales);
+    const uint16_t* Bi = rp16(L.resident_dev, L.router.biases);
+    terms[rr][g] = __fadd_rn(__fmul_rn(bf16f(Sc[row * GD + g]), dot), __fmul_rn(bf16f(Bi[row * GD + g]), xsum[g]));
+    __syncthreads();
+    if (tid < RR_ROWS) {
+        float acc = 0.0f;
+        for (int g2 = 0; g2 < GD; ++g2) acc = __fadd_rn(acc, terms[tid][g2]);
+        rlog[(size_t)t * NE + blockIdx.y * RR_ROWS + tid] = acc;
     }
 }
 
@@ -437,12 +497,12 @@ __device__ __forceinline__ int route_expert(const RouteArgs& A, int i) {
 constexpr int RC = 1024;   // entries per counting CTA
 
 // 2a. per-chunk counts and in-chunk ranks (warp match_any, then a prefix over the warps)
-__global__ void __launch_bounds__(RC) tok_route_count(const __grid_constant__ RouteArgs A) {
+__device__ __forceinline__ void route_count(const RouteArgs& A, int chunk) {
     __shared__ int wc[RC / 32][NE];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int j = tid; j < (RC / 32) * NE; j += RC) (&wc[0][0])[j] = 0;
     __syncthreads();
-    const int i = blockIdx.x * RC + tid;
+    const int i = chunk * RC + tid;
     const int e = route_expert(A, i);   // -1: another rank's expert (or no entry)
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_w = __popc(peers & ((1u << lane) - 1u));
@@ -451,14 +511,15 @@ __global__ void __launch_bounds__(RC) tok_route_count(const __grid_constant__ Ro
     for (int ex = tid; ex < A.ne; ex += RC) {
         int run = 0;
         for (int w = 0; w < RC / 32; ++w) { const int c = wc[w][ex]; wc[w][ex] = run; run += c; }
-        A.chunk[(size_t)blockIdx.x * NE + ex] = run;
+        A.chunk[(size_t)chunk * NE + ex] = run;
     }
     __syncthreads();
     if (i < A.n) A.pos[i] = e >= 0 ? wc[warp][e] + rank_w : -1;
 }
+__global__ void __launch_bounds__(RC) tok_route_count(const __grid_constant__ RouteArgs A) { route_count(A, blockIdx.x); }
 
 // 2b. expert offsets, each chunk's first row per expert, and the tile lists (one CTA)
-__global__ void __launch_bounds__(1024) tok_route_scan(const __grid_constant__ RouteArgs A) {
+__device__ __forceinline__ void route_scan(const RouteArgs& A) {
     constexpr int SP = 8;   // threads per expert in the chunk scan (1024 / NE)
     __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
     __shared__ int wsum[NE / 32][3];
@@ -551,17 +612,29 @@ __global__ void __launch_bounds__(1024) tok_route_scan(const __grid_constant__ R
         A.n_tiles[1] = b1 + nts * FB1;
     }
 }
+__global__ void __launch_bounds__(1024) tok_route_scan(const __grid_constant__ RouteArgs A) { route_scan(A); }
 
 // 2c. final rows: pos = expert-ordered row of each entry, perm_src = its source row
-__global__ void __launch_bounds__(RC) tok_route_scatter(const __grid_constant__ RouteArgs A) {
-    const int i = blockIdx.x * RC + threadIdx.x;
+__device__ __forceinline__ void route_scatter(const RouteArgs& A, int chunk) {
+    const int i = chunk * RC + threadIdx.x;
     if (i >= A.n) return;
     const int r = A.pos[i];
     if (r < 0) return;
     const int e = route_expert(A, i);
-    const int row = A.chunk[(size_t)blockIdx.x * NE + e] + r;
+    const int row = A.chunk[(size_t)chunk * NE + e] + r;
     A.pos[i] = row;
     A.perm_src[row] = i / A.src_div;
+}
+__global__ void __launch_bounds__(RC) tok_route_scatter(const __grid_constant__ RouteArgs A) { route_scatter(A, blockIdx.x); }
+
+// At most one chunk (up to RC entries: up to 128 tokens on one GPU): the three steps in one CTA.
+// A thread's global writes are visible to the CTA's other threads after __syncthreads.
+__global__ void __launch_bounds__(RC) tok_route_one(const __grid_constant__ RouteArgs A) {
+    if (A.nchunks > 0) route_count(A, 0);
+    __syncthreads();
+    route_scan(A);
+    __syncthreads();
+    if (A.nchunks > 0) route_scatter(A, 0);
 }
 
 // ================================================================================================
@@ -1264,7 +1337,7 @@ __global__ void __launch_bounds__(CT, 2) tok_combine(const __grid_constant__ Com
 // ================================================================================================
 struct WsLayout {
     size_t dense_hi, dense_lo, routed, idx, w, perm_src, pos, chunk, tiles0, tiles1, n_tiles, stiles0, stiles1, sn_tiles, act_r_hi,
-        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, views_all, idx_all, hdr, ret, total;
+        act_r_lo, act_s_hi, act_s_lo, out_r, out_s, send_pos, send_src, views_all, idx_all, hdr, ret, rlog, total;
 };
 
 // single GPU; expert parallelism with the caller's all-to-all; expert parallelism over peer memory
@@ -1320,6 +1393,7 @@ static WsLayout ws_layout(uint32_t T, uint32_t Rrows, WsMode mode, uint32_t P = 
     // ret: [T * top_k][D] expert outputs of the own entries, stored by the experts' owners
     W.hdr = mode == WS_PEER ? take((P + 1) * 4) : 0;
     W.ret = mode == WS_PEER ? take(E8 * D * 4) : 0;
+    W.rlog = take((size_t)T * NE * 4);
     W.total = o;
     return W;
 }
@@ -1418,8 +1492,15 @@ void launch_views(const GtmDims& dims, const GtmLayer& L, const GtmTokensIO& io,
         }
     }
     const uintptr_t xa = reinterpret_cast<uintptr_t>(io.x_dev ? static_cast<const void*>(io.x_dev) : io.x_bf16_dev);
-    if (io.route_logits_dev && !peer_ws && (xa & 15) == 0) tok_views_given<<<io.num_tokens, VG_THREADS, 0, st>>>(va);
-    else tok_views_router<<<io.num_tokens, io.route_logits_dev ? 512 : 1024, 0, st>>>(va);
+    if (!peer_ws && (xa & 15) == 0) {
+        if (!io.route_logits_dev) {   // the router rows first, 16 rows per CTA
+            tok_router_rows<<<dim3(io.num_tokens, NE / RR_ROWS), RR_THREADS, 0, st>>>(va, w.p<float>(w.W.rlog));
+            va.route_logits = w.p<float>(w.W.rlog);
+        }
+        tok_views_given<<<io.num_tokens, VG_THREADS, 0, st>>>(va);
+    } else {
+        tok_views_router<<<io.num_tokens, io.route_logits_dev ? 512 : 1024, 0, st>>>(va);
+    }
 }
 
 // What one pass of the two grouped GEMMs runs over.
@@ -1489,9 +1570,13 @@ int run_gemms(const GtmLayer& L, const Ws& w, const Plan& pl, int num_sms, cudaS
     for (int s = 0; s < pl.nsrc; ++s) { ra.src_idx[s] = pl.src_idx[s]; ra.src_ntok[s] = pl.src_ntok[s]; }
     ra.nrows = pl.nrows;
     mark_phase(1, st);
-    if (ra.nchunks > 0) tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
-    tok_route_scan<<<1, 1024, 0, st>>>(ra);
-    if (ra.nchunks > 0) tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
+    if (ra.nchunks <= 1) {
+        tok_route_one<<<1, RC, 0, st>>>(ra);
+    } else {
+        tok_route_count<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
+        tok_route_scan<<<1, 1024, 0, st>>>(ra);
+        tok_route_scatter<<<(unsigned)ra.nchunks, RC, 0, st>>>(ra);
+    }
     cudaFuncSetAttribute(grouped_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     cudaFuncSetAttribute(grouped_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
 
