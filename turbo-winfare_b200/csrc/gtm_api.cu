@@ -271,8 +271,7 @@ GTM_API int gtm_moe_decode(const GtmDims* dims, const GtmLayer* layers, int num_
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return set_cuda_error("gtm_moe_decode: device query", e);
-    // at most 176 CTAs (= the 176 down row tiles): every CTA then holds >= 11 consecutive down items,
-    // so each row tile's down sum has at most two contributors
+    // at most 176 CTAs: the per-CTA down chunks are sized for 120..176 CTAs
     const int ctas = sms < 176 ? sms : 176;
     if (ctas < kDecodeMinCtas)
         return set_error(GTM_ERR_UNSUPPORTED, "gtm_moe_decode: needs >= %d SMs (device has %d)", kDecodeMinCtas, sms);

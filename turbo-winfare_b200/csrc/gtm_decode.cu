@@ -31,17 +31,21 @@
 // holding a group combines them in fp32 and applies the group's bf16 scale and bias:
 // y += s * 2^(E-6) * (D0 + D1 2^-7 + D2 2^-14) + b * sum(x).
 //
-// Per layer (one token), with bounded grid-wide waits:
-//   tail    every CTA: layer tail of the previous layer from the down partials, optional
-//           between-layer RMSNorm, views (dense_x, routed_x, router input), fragment tables
+// The grid splits into the shared-expert group (40 of 148 CTAs) and eight slot groups (13-14 CTAs
+// each, one per top-8 slot). Per layer (one token), with bounded waits:
+//   tail    every CTA: layer tail of the previous layer from the down rows, optional
+//           between-layer RMSNorm, views (dense_x, routed_x, router input), the group's view table
 //   router  CTAs 0..127: their router logit in the reference's exact order (bit-identical), published
 //           with the layer number in one 64-bit word; the words double as barrier A
-//   shared  each CTA's share of the 264 shared gate/up tiles (+GeGLU)
-//   top-8   wait for all 128 logit words; top-8 on every CTA; the producer starts the routed copies
-//   routed  each CTA's share of the 704 routed gate/up tiles (+GeGLU)            -> barrier B
-//   down    fragment tables of the 7744 activations; each CTA's share of the 1936 down items
-//           (row tile x segment: 3 thirds of the shared down, 8 routed experts) -> barrier C
-// The down partials [2 contributors][shared, routed][2816] are summed in fixed order by the tail.
+//   slots   wait for all 128 logit words, top-8; the producer starts the slot expert's copies;
+//           the group's share of the expert's 88 gate/up tiles (+GeGLU) -> the group's barrier;
+//           fragment tables of the expert's 704 activations; the group's share of its 176 down
+//           row tiles, each over the whole K                                  -> barrier C
+//   shared  the group's share of the 264 shared gate/up tiles (+GeGLU) -> the group's barrier;
+//           tables of the 2112 activations; its share of the 176 down row tiles (K 2112); then the
+//           top-8 (the tail's weights)                                        -> barrier C
+// Every down row comes from one CTA: part [shared, slot 0..7][2816]; the tail weights and sums the
+// slots in router order.
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
@@ -65,12 +69,9 @@ constexpr int GFE = FE / kGroup;          // 11
 constexpr int GFS = FS / kGroup;          // 33
 constexpr int QD = GD / 4;                // 11 quads of a hidden-sized input
 constexpr int QS = 3;                     // quads of an 11-group down segment (the last holds 3 groups)
-constexpr int TILES_R = TOPK * FE / 8;    // 704 routed gate/up tiles (8 features each)
 constexpr int TILES_S = FS / 8;           // 264 shared gate/up tiles
 constexpr int TPE = FE / 8;               // 88 tiles per routed expert
 constexpr int OT = D / 16;                // 176 output row tiles of the down projection
-constexpr int NSEG = 3 + TOPK;            // down segments: 3 shared thirds + 8 routed experts
-constexpr int ITEMS_DN = OT * NSEG;       // 1936 down items: row tile item / NSEG, segment item % NSEG
 constexpr int ROW_GU = D / 2;             // 1408 bytes per gate/up row
 constexpr int SROW_GU = GD * 2;           // 88 bytes of bf16 scales per gate/up row
 constexpr int DROW_R = FE / 2, SROW_R = GFE * 2;   // routed down: 352 bytes per row, 22 of scales
@@ -80,8 +81,10 @@ constexpr int QW = 192;                   // fragment-table words per quad: 2 do
 constexpr uint32_t RING = 144 * 1024;     // chunk ring
 constexpr int NB = 32;                    // chunk mbarrier slots (> the chunks of any one phase)
 constexpr int GU_TILES = 2;               // tiles per gate/up chunk
-constexpr int MAX_DN = 24;                // down items per CTA (>= 1936 / 88)
-constexpr int MAX_OTS = 4;                // down row tiles per CTA
+constexpr int DN_TILES_R = 6, DN_TILES_S = 3;   // down row tiles per chunk (38 KB routed, 57 KB shared)
+constexpr int MAX_DN = 24;                // items of one phase per CTA (tiles or down row tiles)
+constexpr int QSS = 9;                    // quads of the shared down's 33 groups (the last holds 1)
+constexpr int MIN_CTAS = 120, MAX_CTAS = 176;   // grid sizes whose per-CTA chunks fit the ring
 constexpr int ACT_R = TOPK * FE;          // 5632 routed activations, after the 2112 shared ones
 constexpr int SLOTS = 1024;               // partial-sum floats: items x max contributors x 16 rows
 constexpr uint64_t kTimeoutNs = 2000000000ull;
@@ -100,20 +103,26 @@ struct Params {
     int* err;
     int* sticky;
     float* act;        // [FS + ACT_R]: shared activations, then the 8 routed slots (segment q at q * 704)
-    float* part;       // [2 contributors][2: shared, routed][D] down sums
+    float* part;       // [1 + TOPK][D]: the shared down, then the routed down of slot k (unweighted)
 };
 
-// Per-CTA work lists (identical on every thread; derived from the CTA index and grid size).
+// Per-CTA work lists (identical on every thread; derived from the CTA index and grid size). The
+// grid splits into the shared-expert group (CTAs [0, S)) and one group per top-8 slot (the rest,
+// in eight near-equal ranges): a group computes its expert's gate/up tiles, waits for its own
+// members only, then the expert's down rows over the whole K, so every down output row comes from
+// one CTA.
 struct Plan {
     int nr;              // router rows: cta, cta + G, ...
-    int st0, st1;        // shared gate/up tiles
-    int rt0, rt1;        // routed gate/up tiles
-    int d0, d1;          // down items (row-tile-major)
-    int n_sgu, n_rgu;    // gate/up chunks
-    int ot0;             // first down row tile of the CTA
-    int sh_a, sh_b;      // shared-down row tiles [sh_a, sh_b] of the shared-down chunk
-    int c_sgu, c_rgu, c_dn, cpl;   // first chunk of each phase within a layer, chunks per layer
+    bool sh;             // shared-expert group (else the group of top-8 slot `slot`)
+    int slot;
+    int g0, g1;          // the group's CTAs (its barrier)
+    int t0, t1;          // gate/up tiles: of the shared expert's 264, or of the slot expert's 88
+    int ot0, ot1;        // down row tiles, each over the expert's whole K (33 or 11 groups)
+    int n_gu, n_dn;      // gate/up chunks, down chunks
+    int dt;              // down row tiles per down chunk
+    int c_gu, c_dn, cpl; // first gate/up chunk, first down chunk, chunks per layer
 };
+__host__ __device__ constexpr int shared_ctas(int G) { return G * 40 / 148; }
 
 struct Smem {
     alignas(128) uint8_t ring[RING + 128];   // chunks (+ slack read by a down row's partial last quad)
@@ -123,12 +132,12 @@ struct Smem {
             alignas(16) float ab[2 * D];     // routed_x [0, D), dense_x [D, 2D)
             alignas(16) float rin[GD * RIN_PITCH];
         } t;
-        alignas(16) uint32_t tbl_dn[NSEG * QS * QW];   // down inputs: segment q at q * 576 words
+        alignas(16) uint32_t tbl_dn[QSS * QW];         // down inputs: 33 (shared) or 11 (routed) groups
     } u;
     alignas(16) uint32_t tbl_r[QD * QW];     // routed_x
     alignas(16) uint32_t tbl_d[QD * QW];     // dense_x
     float2 gs_r[GD], gs_d[GD];               // per group of the views: (sum of x, 2^(E-6))
-    float2 gs_dn[NSEG * 4 * QS];             // and of the down inputs
+    float2 gs_dn[4 * QSS];                   // and of the down inputs
     float slot[SLOTS];                       // partial sums: [item][contributing warp k][16 rows]
     double red[2][NWC][2];
     float redf[2][NWC][2];
@@ -136,10 +145,8 @@ struct Smem {
     float terms[GD];
     float topw[TOPK];
     int topi[TOPK];
-    int dn_ot[MAX_DN], dn_q[MAX_DN];         // down items in processing (chunk) order
     uint8_t it_first[3][MAX_DN], it_kend[3][MAX_DN];   // per phase (shared, routed, down) and item:
                                                        // first contributing warp, contributors
-    int dn_pos[MAX_OTS][NSEG];               // processing index of (row tile ot0 + i, segment q)
     uint64_t full[NB];                       // chunk landed (producer arrive + bytes)
     uint64_t empty[NB];                      // chunk released (one arrival per compute warp)
     uint32_t meta[NB];                       // ring offset of a chunk in flight
@@ -166,69 +173,54 @@ __device__ __forceinline__ void csync() { tc::named_bar_sync(1, NTC); }   // the
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 // ---- plan ------------------------------------------------------------------------------------------
-// Routed gate/up chunks: the CTA's tiles [rt0, rt1) cut at expert boundaries (every 88 tiles) and
-// into pieces of at most GU_TILES.
-__device__ __forceinline__ int rgu_next(const Plan& p, int s) {
-    return min(min(p.rt1, (s / TPE + 1) * TPE), s + GU_TILES);
-}
-__device__ void rgu_chunk(const Plan& p, int k, int& t0, int& n) {
-    int s = p.rt0;
-    for (; k > 0; --k) s = rgu_next(p, s);
-    t0 = s;
-    n = rgu_next(p, s) - s;
-}
-__device__ void rgu_locate(const Plan& p, int T, int& k, int& t0) {
-    int s = p.rt0;
-    k = 0;
-    for (;;) {
-        const int e = rgu_next(p, s);
-        if (T < e) { t0 = s; return; }
-        s = e;
-        ++k;
-    }
-}
-// First / last down item of segment q in [d0, d1) (the range holds >= 11 items, so every segment).
-__device__ __forceinline__ int seg_first(const Plan& p, int q) { return p.d0 + (q - p.d0 % NSEG + NSEG) % NSEG; }
-__device__ __forceinline__ int seg_last(const Plan& p, int q) {
-    return (p.d1 - 1) - ((p.d1 - 1) % NSEG - q + NSEG) % NSEG;
-}
-
 __device__ Plan make_plan(int cta, int G) {
     Plan p;
     p.nr = cta < NE ? (NE - 1 - cta) / G + 1 : 0;
-    p.st0 = share(TILES_S, cta, G); p.st1 = share(TILES_S, cta + 1, G);
-    p.rt0 = share(TILES_R, cta, G); p.rt1 = share(TILES_R, cta + 1, G);
-    p.d0 = share(ITEMS_DN, cta, G); p.d1 = share(ITEMS_DN, cta + 1, G);
-    p.n_sgu = (p.st1 - p.st0 + GU_TILES - 1) / GU_TILES;
-    p.n_rgu = 0;
-    for (int s = p.rt0; s < p.rt1; s = rgu_next(p, s)) ++p.n_rgu;
-    p.ot0 = p.d0 / NSEG;
-    p.sh_a = OT; p.sh_b = -1;
-    for (int q = 0; q < 3; ++q) {
-        p.sh_a = min(p.sh_a, seg_first(p, q) / NSEG);
-        p.sh_b = max(p.sh_b, seg_last(p, q) / NSEG);
+    const int S = shared_ctas(G), R = G - S;
+    p.sh = cta < S;
+    int n, i;
+    if (p.sh) {
+        p.slot = 0; p.g0 = 0; p.g1 = S;
+        n = S; i = cta;
+        p.t0 = share(TILES_S, i, n); p.t1 = share(TILES_S, i + 1, n);
+    } else {
+        int k = 0;
+        while (k + 1 < TOPK && S + share(R, k + 1, TOPK) <= cta) ++k;
+        p.slot = k;
+        p.g0 = S + share(R, k, TOPK); p.g1 = S + share(R, k + 1, TOPK);
+        n = p.g1 - p.g0; i = cta - p.g0;
+        p.t0 = share(TPE, i, n); p.t1 = share(TPE, i + 1, n);
     }
-    p.c_sgu = p.nr;
-    p.c_rgu = p.c_sgu + p.n_sgu;
-    p.c_dn = p.c_rgu + p.n_rgu;
-    p.cpl = p.c_dn + 1 + TOPK;
+    p.ot0 = share(OT, i, n); p.ot1 = share(OT, i + 1, n);
+    p.n_gu = (p.t1 - p.t0 + GU_TILES - 1) / GU_TILES;
+    p.dt = p.sh ? DN_TILES_S : DN_TILES_R;
+    p.n_dn = (p.ot1 - p.ot0 + p.dt - 1) / p.dt;
+    p.c_gu = p.nr;
+    p.c_dn = p.c_gu + p.n_gu;
+    p.cpl = p.c_dn + p.n_dn;
     return p;
 }
+__device__ __forceinline__ int dn_groups(const Plan& p) { return p.sh ? GFS : GFE; }
 
 // Chunk i of a layer: ring bytes (copied; the allocation adds the 64-byte gate/up offset and rounds
-// to 128) and whether it needs the layer's top-8.
+// to 128).
 __device__ uint32_t chunk_bytes(const Plan& p, int i) {
-    if (i < p.c_sgu) return D;
+    if (i < p.c_gu) return D;
     if (i < p.c_dn) {
-        int nt;
-        if (i < p.c_rgu) nt = min(GU_TILES, p.st1 - p.st0 - (i - p.c_sgu) * GU_TILES);
-        else { int t0; rgu_chunk(p, i - p.c_rgu, t0, nt); }
+        const int nt = min(GU_TILES, p.t1 - p.t0 - (i - p.c_gu) * GU_TILES);
         return (uint32_t)(8 * nt) * (2 * ROW_GU + 4 * SROW_GU);
     }
-    if (i == p.c_dn) return (uint32_t)(16 * (p.sh_b - p.sh_a + 1)) * (DROW_S + 2 * SROW_S);
-    const int q = 3 + (i - p.c_dn - 1);
-    return (uint32_t)(16 * (seg_last(p, q) / NSEG - seg_first(p, q) / NSEG + 1)) * (DROW_R + 2 * SROW_R);
+    const int nt = min(p.dt, p.ot1 - p.ot0 - (i - p.c_dn) * p.dt);
+    return (uint32_t)(16 * nt) * (p.sh ? DROW_S + 2 * SROW_S : DROW_R + 2 * SROW_R);
 }
+// Chunks stay under half the ring, so two are in flight at any ring position.
+static_assert(16 * GU_TILES * 8 / 16 * (2 * ROW_GU + 4 * SROW_GU) + 192 <= RING / 2 &&
+                  16 * DN_TILES_S * (DROW_S + 2 * SROW_S) + 192 <= RING / 2 &&
+                  16 * DN_TILES_R * (DROW_R + 2 * SROW_R) + 192 <= RING / 2,
+              "chunks fit half the ring");
+static_assert((TILES_S + shared_ctas(MIN_CTAS) - 1) / shared_ctas(MIN_CTAS) <= MAX_DN &&
+                  (OT + (MIN_CTAS - shared_ctas(MIN_CTAS)) / TOPK - 1) / ((MIN_CTAS - shared_ctas(MIN_CTAS)) / TOPK) <= MAX_DN,
+              "per-CTA items fit the contributor tables");
 
 // ---- mbarrier waits --------------------------------------------------------------------------------
 // Bounded wait on a chunk barrier (every lane of the calling warp); false on timeout or abort.
@@ -276,39 +268,26 @@ __device__ __forceinline__ bool release_to(Smem& s, const Params& P, int& cur, i
 // layer's top-8 it prefetches the layer's shared-down rows and the next layer's router and shared
 // gate/up rows (HBM is otherwise idle until the top-8). Bulk prefetches queue in the same TMA unit
 // as the copies, so none is issued after the top-8: there they delayed the routed copies.
-__device__ void l2_static(const Plan& p, const GtmLayer& L, const GtmLayer* Ln, int cta, int G) {
-    const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
-    const uint32_t R = 16 * (p.sh_b - p.sh_a + 1), r0 = 16 * p.sh_a;
-    tc::prefetch_l2_bulk(res + L.shared_down.weight + (uint64_t)r0 * DROW_S, R * DROW_S);
-    tc::prefetch_l2_bulk(res + L.shared_down.scales + (uint64_t)r0 * SROW_S, R * SROW_S);
-    tc::prefetch_l2_bulk(res + L.shared_down.biases + (uint64_t)r0 * SROW_S, R * SROW_S);
+// While a slot group's producer waits for the top-8: the next layer's router rows into L2.
+__device__ void l2_static(const Plan& p, const GtmLayer* Ln, int cta, int G) {
     if (!Ln) return;
     const uint8_t* rn = static_cast<const uint8_t*>(Ln->resident_dev);
     for (int k = 0; k < p.nr; ++k) tc::prefetch_l2_bulk(rn + Ln->router.weight + (uint64_t)(cta + k * G) * D, D);
-    if (p.st1 > p.st0) {
-        const uint64_t f0 = 8 * (uint64_t)p.st0, F = 8 * (uint64_t)(p.st1 - p.st0);
-        tc::prefetch_l2_bulk(rn + Ln->shared_gate.weight + f0 * ROW_GU, F * ROW_GU);
-        tc::prefetch_l2_bulk(rn + Ln->shared_up.weight + f0 * ROW_GU, F * ROW_GU);
-        tc::prefetch_l2_bulk(rn + Ln->shared_gate.scales + f0 * SROW_GU, F * SROW_GU);
-        tc::prefetch_l2_bulk(rn + Ln->shared_gate.biases + f0 * SROW_GU, F * SROW_GU);
-        tc::prefetch_l2_bulk(rn + Ln->shared_up.scales + f0 * SROW_GU, F * SROW_GU);
-        tc::prefetch_l2_bulk(rn + Ln->shared_up.biases + f0 * SROW_GU, F * SROW_GU);
-    }
 }
 
 __device__ void producer(Smem& s, const Params& P, const Plan& p) {
     if ((threadIdx.x & 31) != 0) return;
     uint32_t head = 0, tail = 0;
     int issued = 0, released = 0;
-    int tk[TOPK] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int expert = 0;   // the slot group's expert of the current layer
     bool ok = true;
     const int cta = blockIdx.x, G = gridDim.x;
     for (int l = 0; l < P.num_layers && ok; ++l) {
         const GtmLayer& L = P.layers[l];
         const uint8_t* res = static_cast<const uint8_t*>(L.resident_dev);
         for (int i = 0; i < p.cpl && ok; ++i) {
-            if (i == p.c_rgu) {   // the routed chunks follow: wait for this layer's top-8
-                l2_static(p, L, l + 1 < P.num_layers ? &P.layers[l + 1] : nullptr, cta, G);
+            if (!p.sh && i == p.c_gu) {   // the slot expert's chunks follow: wait for this layer's top-8
+                l2_static(p, l + 1 < P.num_layers ? &P.layers[l + 1] : nullptr, cta, G);
                 const uint64_t t0 = globaltimer_ns();
                 while (s.topk_ready < l + 1) {
                     if (s.abort) { ok = false; break; }
@@ -321,14 +300,16 @@ __device__ void producer(Smem& s, const Params& P, const Plan& p) {
                 }
                 if (!ok) break;
                 __threadfence_block();
-#pragma unroll
-                for (int k = 0; k < TOPK; ++k) tk[k] = s.topi[k];
+                expert = s.topi[p.slot];
             }
             const uint32_t bytes = chunk_bytes(p, i);
             const uint32_t alloc = (bytes + 64 + 127) & ~127u;
             uint32_t pos = head % RING;
             if (pos + alloc > RING) { head += RING - pos; pos = 0; }
             while (head + alloc - tail > RING || issued - released >= NB) {
+                // nothing in flight: the ring is empty (a skipped end of the ring counts as used
+                // only while chunks issued before the skip are held)
+                if (released == issued) { tail = head; break; }
                 if (!wait_bar(s, P, &s.empty[released % NB], (uint32_t)(released / NB) & 1u)) { ok = false; break; }
                 tail = s.meta_end[released % NB];
                 ++released;
@@ -341,23 +322,15 @@ __device__ void producer(Smem& s, const Params& P, const Plan& p) {
             uint64_t* bar = &s.full[slot];
             uint8_t* dst = s.ring + pos;
             tc::mbar_arrive_expect_tx(bar, bytes);
-            if (i < p.c_sgu) {
+            if (i < p.c_gu) {
                 const int row = cta + i * G;
                 tc::bulk_load(dst, res + L.router.weight + (uint64_t)row * D, D, bar);
             } else if (i < p.c_dn) {
-                const bool routed = i >= p.c_rgu;
-                int t0, nt;
-                if (!routed) { t0 = p.st0 + (i - p.c_sgu) * GU_TILES; nt = min(GU_TILES, p.st1 - t0); }
-                else rgu_chunk(p, i - p.c_rgu, t0, nt);
-                const uint8_t* base = res;
-                const GtmQuant *qg = &L.shared_gate, *qu = &L.shared_up;
-                int f0 = 8 * t0;
-                if (routed) {
-                    base = rp(L.experts_dev, (uint64_t)tk[t0 / TPE] * L.expert_stride);
-                    qg = &L.expert_gate;
-                    qu = &L.expert_up;
-                    f0 = 8 * (t0 % TPE);
-                }
+                const int t0 = p.t0 + (i - p.c_gu) * GU_TILES, nt = min(GU_TILES, p.t1 - t0);
+                const uint8_t* base = p.sh ? res : rp(L.experts_dev, (uint64_t)expert * L.expert_stride);
+                const GtmQuant* qg = p.sh ? &L.shared_gate : &L.expert_gate;
+                const GtmQuant* qu = p.sh ? &L.shared_up : &L.expert_up;
+                const int f0 = 8 * t0;
                 const uint32_t F = 8 * nt, wb = F * ROW_GU, sb = F * SROW_GU;
                 tc::bulk_load(dst, base + qg->weight + (uint64_t)f0 * ROW_GU, wb, bar);
                 tc::bulk_load(dst + wb + 64, base + qu->weight + (uint64_t)f0 * ROW_GU, wb, bar);
@@ -366,21 +339,15 @@ __device__ void producer(Smem& s, const Params& P, const Plan& p) {
                 tc::bulk_load(sd + sb, base + qg->biases + (uint64_t)f0 * SROW_GU, sb, bar);
                 tc::bulk_load(sd + 2 * sb, base + qu->scales + (uint64_t)f0 * SROW_GU, sb, bar);
                 tc::bulk_load(sd + 3 * sb, base + qu->biases + (uint64_t)f0 * SROW_GU, sb, bar);
-            } else if (i == p.c_dn) {
-                const uint32_t R = 16 * (p.sh_b - p.sh_a + 1), r0 = 16 * p.sh_a;
-                tc::bulk_load(dst, res + L.shared_down.weight + (uint64_t)r0 * DROW_S, R * DROW_S, bar);
-                tc::bulk_load(dst + R * DROW_S, res + L.shared_down.scales + (uint64_t)r0 * SROW_S, R * SROW_S, bar);
-                tc::bulk_load(dst + R * (DROW_S + SROW_S), res + L.shared_down.biases + (uint64_t)r0 * SROW_S,
-                              R * SROW_S, bar);
-            } else {
-                const int q = 3 + (i - p.c_dn - 1);
-                const int a = seg_first(p, q) / NSEG, b = seg_last(p, q) / NSEG;
-                const uint32_t R = 16 * (b - a + 1), r0 = 16 * a;
-                const uint8_t* blk = rp(L.experts_dev, (uint64_t)tk[q - 3] * L.expert_stride);
-                tc::bulk_load(dst, blk + L.expert_down.weight + (uint64_t)r0 * DROW_R, R * DROW_R, bar);
-                tc::bulk_load(dst + R * DROW_R, blk + L.expert_down.scales + (uint64_t)r0 * SROW_R, R * SROW_R, bar);
-                tc::bulk_load(dst + R * (DROW_R + SROW_R), blk + L.expert_down.biases + (uint64_t)r0 * SROW_R,
-                              R * SROW_R, bar);
+            } else {   // down chunk j: rows of row tiles [ot0 + j dt, ...) over the whole K
+                const int j = i - p.c_dn, a = p.ot0 + j * p.dt;
+                const uint32_t R = 16 * min(p.dt, p.ot1 - a), r0 = 16 * a;
+                const uint8_t* base = p.sh ? res : rp(L.experts_dev, (uint64_t)expert * L.expert_stride);
+                const GtmQuant& q = p.sh ? L.shared_down : L.expert_down;
+                const uint32_t rowb = p.sh ? DROW_S : DROW_R, srow = p.sh ? SROW_S : SROW_R;
+                tc::bulk_load(dst, base + q.weight + (uint64_t)r0 * rowb, R * rowb, bar);
+                tc::bulk_load(dst + R * rowb, base + q.scales + (uint64_t)r0 * srow, R * srow, bar);
+                tc::bulk_load(dst + R * (rowb + srow), base + q.biases + (uint64_t)r0 * srow, R * srow, bar);
             }
             ++issued;
         }
@@ -394,18 +361,16 @@ __device__ void producer(Smem& s, const Params& P, const Plan& p) {
 }
 
 // ---- fragment tables -----------------------------------------------------------------------------
-// Tables of routed_x (ab[0, D)) and dense_x (ab[D, 2D)): 2 x 176 items, built by the compute
-// threads from `first` on (whole warps: they take part in the builder's shuffles).
-constexpr int VIEW_ITEMS = 2 * 4 * GD;
-static_assert(VIEW_ITEMS % 32 == 0, "view-table items fill whole warps");
-__device__ void build_views_tables(Smem& s, int first) {
+// Table of one view (v = 0: routed_x, ab[0, D); v = 1: dense_x, ab[D, 2D)): 176 items, built by the
+// compute threads from `first` on (whole warps: they take part in the builder's shuffles).
+constexpr int VIEW_ITEMS = 4 * GD;
+__device__ void build_views_tables(Smem& s, int first, int v) {
     constexpr int N = VIEW_ITEMS;
     const int i0 = threadIdx.x - first;
     if (i0 < 0) return;
     if (i0 < ((N + 31) & ~31)) {
         const bool on = i0 < N;
-        const int i = on ? i0 : (i0 & 3);
-        const int v = i / (4 * GD), k = i - v * 4 * GD, j = k >> 2, sub = k & 3;
+        const int k = on ? i0 : (i0 & 3), j = k >> 2, sub = k & 3;
         const float* src = s.u.t.ab + v * D + j * kGroup + 16 * sub;
         float x[16];
 #pragma unroll
@@ -418,18 +383,19 @@ __device__ void build_views_tables(Smem& s, int first) {
     }
 }
 
-// Tables of the 11 down segments (act[704 q, 704 q + 704), written by every CTA before barrier B,
-// read from L2): 11 x 12 groups x 4 items; group 11 of a segment (past its 704 inputs) is zero.
-__device__ void build_down_tables(Smem& s, const Params& P) {
-    constexpr int N = NSEG * 12 * 4;
+// Table of the group's down inputs (written by the group's CTAs before the group barrier, read
+// from L2): the shared expert's 2112 activations (33 groups, padded to 36 with zero groups) or
+// the slot expert's 704 (11 groups, padded to 12).
+__device__ void build_down_tables(Smem& s, const Params& P, const Plan& p) {
+    const int ng = p.sh ? 4 * QSS : 4 * QS, nv = dn_groups(p), N = 4 * ng;
+    const float* act = P.act + (p.sh ? 0 : FS + FE * p.slot);
     const int i0 = threadIdx.x;
     if (i0 < ((N + 31) & ~31)) {
         const bool on = i0 < N;
-        const int i = on ? i0 : (i0 & 3);
-        const int q = i / 48, k = i - q * 48, j = k >> 2, sub = k & 3;
+        const int i = on ? i0 : (i0 & 3), j = i >> 2, sub = i & 3;
         float x[16];
-        if (j < GFE) {
-            const float4* src = reinterpret_cast<const float4*>(P.act + q * FE + j * kGroup + 16 * sub);
+        if (j < nv) {
+            const float4* src = reinterpret_cast<const float4*>(act + j * kGroup + 16 * sub);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const float4 f = __ldcg(src + c);
@@ -439,7 +405,7 @@ __device__ void build_down_tables(Smem& s, const Params& P) {
 #pragma unroll
             for (int e = 0; e < 16; ++e) x[e] = 0.0f;
         }
-        limb_item(x, on, s.u.tbl_dn + q * QS * QW + (j >> 2) * QW, j & 3, sub, s.gs_dn + q * 12, j);
+        limb_item(x, on, s.u.tbl_dn + (j >> 2) * QW, j & 3, sub, s.gs_dn, j);
     }
 }
 
@@ -617,15 +583,15 @@ __device__ __forceinline__ void arrive(const Params& P, unsigned* flags, unsigne
     if (threadIdx.x == 0) st_release(flags + blockIdx.x, value);
 }
 
-// Warp 0 polls every CTA's flag; the other compute warps wait at the named barrier.
-__device__ bool wait_all(Smem& s, const Params& P, const unsigned* f, unsigned value) {
+// Warp 0 polls the flags of CTAs [lo, hi); the other compute warps wait at the named barrier.
+__device__ bool wait_range(Smem& s, const Params& P, const unsigned* f, int lo, int hi, unsigned value) {
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         const uint64_t t0 = globaltimer_ns();
         bool ok = true;
         for (;;) {
             bool mine = true;
-            for (unsigned b = lane; b < gridDim.x; b += 32) mine &= (ld_relaxed(f + b) >= value);
+            for (int b = lo + lane; b < hi; b += 32) mine &= (ld_relaxed(f + b) >= value);
             const int e = lane == 0 ? ld_volatile_int(P.err) : 0;
             if (__all_sync(0xffffffffu, mine)) break;
             if (__shfl_sync(0xffffffffu, e, 0) != 0) { ok = false; break; }
@@ -640,6 +606,9 @@ __device__ bool wait_all(Smem& s, const Params& P, const unsigned* f, unsigned v
     }
     csync();
     return s.flag == 0;
+}
+__device__ __forceinline__ bool wait_all(Smem& s, const Params& P, const unsigned* f, unsigned value) {
+    return wait_range(s, P, f, 0, (int)gridDim.x, value);
 }
 
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
@@ -774,12 +743,23 @@ __device__ void tail_and_views(Smem& s, const Params& P, const Norms& nv, bool h
     }
     int buf = 0;
     if (has_prev) {
-        // part [contributor][shared, routed][D]: shared = p00 + p10, routed h2 = p01 + p11
+        // part [1 + TOPK][D]: the shared down row, then the slots' rows; h2 = sum_k w_k out_k in
+        // router order (src/cpu_reference.cpp:508-509), each product rounded
         const float4* pp = reinterpret_cast<const float4*>(P.part);
-        const float4 p00 = __ldcg(pp + i), p01 = __ldcg(pp + D / 4 + i);
-        const float4 p10 = __ldcg(pp + 2 * (D / 4) + i), p11 = __ldcg(pp + 3 * (D / 4) + i);
-        float sh[4] = {p00.x + p10.x, p00.y + p10.y, p00.z + p10.z, p00.w + p10.w};
-        float h2[4] = {p01.x + p11.x, p01.y + p11.y, p01.z + p11.z, p01.w + p11.w};
+        float4 pr[TOPK];
+        const float4 ps = __ldcg(pp + i);
+#pragma unroll
+        for (int k = 0; k < TOPK; ++k) pr[k] = __ldcg(pp + (1 + k) * (D / 4) + i);
+        float sh[4] = {ps.x, ps.y, ps.z, ps.w};
+        float h2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int k = 0; k < TOPK; ++k) {
+            const float w = s.topw[k];
+            h2[0] = __fadd_rn(h2[0], __fmul_rn(w, pr[k].x));
+            h2[1] = __fadd_rn(h2[1], __fmul_rn(w, pr[k].y));
+            h2[2] = __fadd_rn(h2[2], __fmul_rn(w, pr[k].z));
+            h2[3] = __fadd_rn(h2[3], __fmul_rn(w, pr[k].w));
+        }
         float2 r = block_sum2f(s, sq4f(sh), sq4f(h2), buf); buf ^= 1;
         const float inv1 = rms_inv_from_sumf(r.x, P.eps), inv2 = rms_inv_from_sumf(r.y, P.eps);
         float tt[4];
@@ -917,48 +897,35 @@ __device__ void select_topk(Smem& s, const float (&v)[4], const uint16_t (&pes_w
 }
 
 // ---- down phase ------------------------------------------------------------------------------------
-// Down items [d0, d1) in chunk order: the shared thirds (row tiles sh_a..sh_b, row-tile-major), then
-// the 8 routed segments, each over its row tiles. dn_pos maps (row tile, segment) to that order.
-__device__ void plan_down(Smem& s, const Plan& p) {
+// Contributor tables of the CTA's gate/up tiles and down row tiles, once per launch.
+__device__ void plan_items(Smem& s, const Plan& p) {
     if (threadIdx.x != 0) return;
-    int k = 0;
-    for (int it = p.d0; it < p.d1; ++it)
-        if (it % NSEG < 3) { s.dn_ot[k] = it / NSEG; s.dn_q[k] = it % NSEG; ++k; }
-    for (int q = 3; q < NSEG; ++q)
-        for (int it = seg_first(p, q); it <= seg_last(p, q); it += NSEG) { s.dn_ot[k] = it / NSEG; s.dn_q[k] = q; ++k; }
-    for (int a = 0; a < MAX_OTS; ++a)
-        for (int q = 0; q < NSEG; ++q) s.dn_pos[a][q] = -1;
-    for (int j = 0; j < k; ++j) s.dn_pos[s.dn_ot[j] - p.ot0][s.dn_q[j]] = j;
-    fill_items(s, 0, p.st1 - p.st0, GD);
-    fill_items(s, 1, p.rt1 - p.rt0, GD);
-    fill_items(s, 2, p.d1 - p.d0, GFE);
+    fill_items(s, p.sh ? 0 : 1, p.t1 - p.t0, GD);
+    fill_items(s, 2, p.ot1 - p.ot0, dn_groups(p));
 }
 
-__device__ bool down_phase(Smem& s, const Params& P, const Plan& p, int c_first) {
+// The CTA's down row tiles [ot0, ot1) over the whole K of its expert (33 or 11 groups) from the
+// down chunks c, c + 1, ... (dt row tiles each): n row tiles x groups pairs split over the warps.
+__device__ bool down_phase(Smem& s, const Params& P, const Plan& p, int c) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const Split sp = make_split(p.d1 - p.d0, GFE);
+    const int Lg = dn_groups(p), n = p.ot1 - p.ot0;
+    const Split sp = make_split(n, Lg);
     int pp = pw0(warp, sp.total);
     const int p1 = pw0(warp + 1, sp.total);
-    int cur = c_first;
+    int cur = c;
     bool ok = true;
+    const int rowb = p.sh ? DROW_S : DROW_R;
     while (pp < p1) {
-        const int k = pp / GFE, j0 = pp - k * GFE, j1 = min(GFE, j0 + (p1 - pp));
-        const int ot = s.dn_ot[k], q = s.dn_q[k];
-        const bool shared = q < 3;
-        const int c = shared ? c_first : c_first + 1 + (q - 3);
-        if (!advance_to(s, P, cur, c)) { ok = false; break; }
-        const uint8_t* base = s.ring + s.meta[c % NB];
-        const int first = shared ? p.sh_a : seg_first(p, q) / NSEG;
-        const int last = shared ? p.sh_b : seg_last(p, q) / NSEG;
-        const int R = 16 * (last - first + 1), row = 16 * (ot - first) + g;
-        const int rowb = shared ? DROW_S : DROW_R, srow = shared ? GFS : GFE;   // bytes, scales per row
-        const int kofs = shared ? q * GFE : 0;                                  // first group of the segment
-        const uint8_t* w = base + (uint32_t)row * rowb + kofs * 32;
-        const uint16_t* sc = reinterpret_cast<const uint16_t*>(base + (uint32_t)R * rowb) + row * srow + kofs;
-        const uint16_t* bi = sc + R * srow;
+        const int k = pp / Lg, j0 = pp - k * Lg, j1 = min(Lg, j0 + (p1 - pp));
+        const int ck = k / p.dt, R = 16 * min(p.dt, n - ck * p.dt);   // its chunk, rows in the chunk
+        if (!advance_to(s, P, cur, c + ck)) { ok = false; break; }
+        const uint8_t* base = s.ring + s.meta[(c + ck) % NB];
+        const int row = 16 * (k - ck * p.dt) + g;
+        const uint8_t* w = base + (uint32_t)row * rowb;
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(base + (uint32_t)R * rowb) + row * Lg;
+        const uint16_t* bi = sc + R * Lg;
         float ya = 0.0f, yb = 0.0f;
-        tile_groups(w, w + 8 * rowb, sc, bi, sc + 8 * srow, bi + 8 * srow, j0, j1, s.u.tbl_dn + q * QS * QW,
-                    s.gs_dn + q * 12, ya, yb);
+        tile_groups(w, w + 8 * rowb, sc, bi, sc + 8 * Lg, bi + 8 * Lg, j0, j1, s.u.tbl_dn, s.gs_dn, ya, yb);
         ya += __shfl_xor_sync(0xffffffffu, ya, 1);
         ya += __shfl_xor_sync(0xffffffffu, ya, 2);
         yb += __shfl_xor_sync(0xffffffffu, yb, 1);
@@ -970,36 +937,59 @@ __device__ bool down_phase(Smem& s, const Params& P, const Plan& p, int c_first)
         }
         pp += j1 - j0;
     }
-    if (ok) ok = release_to(s, P, cur, c_first + 1 + TOPK);
+    if (ok) ok = release_to(s, P, cur, c + p.n_dn);
     return ok;
 }
 
-// The CTA sums its segments of each row tile in segment order, shared and routed apart, into
-// contributor slot 0 (the CTA holding segment 0 of the tile) or 1: a CTA holds >= 11 consecutive
-// row-tile-major items, so a tile of 11 has at most two contributors, and the tail reads
-// part[0] + part[1].
+// The CTA's down rows (each row whole: its warps' partials summed in warp order) into the shared
+// row of part, or the slot's (the tail weights and sums the slots in router order).
 __device__ void down_epilogue(Smem& s, const Params& P, const Plan& p) {
-    const Split sp = make_split(p.d1 - p.d0, GFE);
-    const int ot1 = (p.d1 - 1) / NSEG;
-    for (int i = threadIdx.x; i < (ot1 - p.ot0 + 1) * 16; i += NTC) {
-        const int ot = p.ot0 + (i >> 4), r = i & 15;
-        const int a = max(p.d0, ot * NSEG), b = min(p.d1, ot * NSEG + NSEG);
-        float sh = 0.0f, h2 = 0.0f;
-        for (int it = a; it < b; ++it) {
-            const int q = it - ot * NSEG;
-            const float v = item_sum(s, sp, 2, s.dn_pos[ot - p.ot0][q], r);
-            if (q < 3) sh = __fadd_rn(sh, v);
-            else h2 = __fadd_rn(h2, __fmul_rn(s.topw[q - 3], v));   // the product rounded, as the combine had it
+    const int n = p.ot1 - p.ot0;
+    const Split sp = make_split(n, dn_groups(p));
+    float* dst = P.part + (p.sh ? 0 : (size_t)(1 + p.slot) * D) + 16 * p.ot0;
+    for (int i = threadIdx.x; i < n * 16; i += NTC) dst[i] = item_sum(s, sp, 2, i >> 4, i & 15);
+}
+
+// Wait for all 128 logit words of layer l (warp 0), then the top-8 (topi, topw; the writer's outputs).
+__device__ bool topk_step(Smem& s, const Params& P, int l, unsigned ep, const uint16_t (&pes_w)[4], bool writer) {
+    const GtmDecodeIO& io = P.io;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const unsigned want = ep + (l == 0 ? P.first_wait_extra : 0u);
+        float v[4];
+        const uint64_t t0 = globaltimer_ns();
+        bool wok = true;
+        for (;;) {
+            bool mine = true;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const unsigned long long w = ld_relaxed_u64(P.logit_words + lane + 32 * j);
+                mine &= (unsigned)(w >> 32) >= want;
+                v[j] = __uint_as_float((uint32_t)w);
+            }
+            const int e = lane == 0 ? ld_volatile_int(P.err) : 0;
+            if (__all_sync(0xffffffffu, mine)) break;
+            if (__shfl_sync(0xffffffffu, e, 0) != 0) { wok = false; break; }
+            if (globaltimer_ns() - t0 > P.wait_limit_ns) {
+                if (lane == 0) { atomicExch(P.err, 1); atomicExch(P.sticky, 1); }
+                wok = false;
+                break;
+            }
         }
-        const int c = a == ot * NSEG ? 0 : 1;
-        float* pc = P.part + (size_t)c * 2 * D + ot * 16 + r;
-        pc[0] = sh;
-        pc[D] = h2;
-        if (c == 0 && b == ot * NSEG + NSEG) {   // the whole tile here: no second contributor
-            pc[2 * D] = 0.0f;
-            pc[3 * D] = 0.0f;
+        __threadfence();
+        if (wok) {
+            select_topk(s, v, pes_w, writer, io.topk_idx_dev ? io.topk_idx_dev + (size_t)l * TOPK : nullptr,
+                        io.topk_w_dev ? io.topk_w_dev + (size_t)l * TOPK : nullptr,
+                        io.logits_dev ? io.logits_dev + (size_t)l * NE : nullptr);
+            __syncwarp();
+            __threadfence_block();
+            if (lane == 0) s.topk_ready = l + 1;
+        } else if (lane == 0) {
+            s.abort = 1;
         }
     }
+    csync();
+    return !s.abort;
 }
 
 // ---- the kernel --------------------------------------------------------------------------------------
@@ -1018,7 +1008,7 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
         s.abort = 0;
         tc::mbar_fence_init();
     }
-    plan_down(s, p);
+    plan_items(s, p);
     __syncthreads();
     if (warp == NWC) {
         producer(s, P, p);
@@ -1053,11 +1043,11 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
                        writer && io.h2_dev && l > 0 ? io.h2_dev + (size_t)(l - 1) * D : nullptr,
                        writer && io.hidden_layers_dev && l > 0 ? io.hidden_layers_dev + (size_t)(l - 1) * D : nullptr);
 
-        // ---- router rows (the logit words double as barrier A) on warps 0-1, while warps 2-12
-        //      build the fragment tables of the views ----
+        // ---- router rows (the logit words double as barrier A) on warps 0-1, while warps 2-7
+        //      build the fragment table of the group's view ----
         int cur = cbase;
         bool ok = true;
-        if (warp >= 2) build_views_tables(s, 64);
+        if (warp >= 2) build_views_tables(s, 64, p.sh ? 1 : 0);
         for (int k = 0; k < p.nr; ++k) {
             if (warp < 2) {
                 const int row = cta + k * G;
@@ -1076,88 +1066,40 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
         }
         if (ok) ok = release_to(s, P, cur, cbase + p.nr);
         if (!ok) s.abort = 1;
-        csync();   // the view tables are complete
-
-        // ---- shared gate/up ----
-        if (ok && p.st1 > p.st0) {
-            ok = gu_phase(s, P, 0, p.st1 - p.st0, cbase + p.c_sgu, cbase + p.c_rgu, s.tbl_d, s.gs_d,
-                          [&](int item, int& c, int& lt, int& F) {
-                              const int k = item / GU_TILES;
-                              c = cbase + p.c_sgu + k;
-                              lt = item - k * GU_TILES;
-                              F = 8 * min(GU_TILES, p.st1 - p.st0 - k * GU_TILES);
-                          });
-            if (!ok) s.abort = 1;
-            csync();
-            if (!s.abort) gu_epilogue(s, 0, P.act + 8 * p.st0, p.st1 - p.st0);
-        }
-        csync();
+        csync();   // the view table is complete
         if (s.abort) break;
 
-        // ---- wait for every router logit; top-8 ----
-        if (warp == 0) {
-            const unsigned want = ep + (l == 0 ? P.first_wait_extra : 0u);
-            float v[4];
-            const uint64_t t0 = globaltimer_ns();
-            bool wok = true;
-            for (;;) {
-                bool mine = true;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const unsigned long long w = ld_relaxed_u64(P.logit_words + lane + 32 * j);
-                    mine &= (unsigned)(w >> 32) >= want;
-                    v[j] = __uint_as_float((uint32_t)w);
-                }
-                const int e = lane == 0 ? ld_volatile_int(P.err) : 0;
-                if (__all_sync(0xffffffffu, mine)) break;
-                if (__shfl_sync(0xffffffffu, e, 0) != 0) { wok = false; break; }
-                if (globaltimer_ns() - t0 > P.wait_limit_ns) {
-                    if (lane == 0) { atomicExch(P.err, 1); atomicExch(P.sticky, 1); }
-                    wok = false;
-                    break;
-                }
-            }
-            __threadfence();
-            if (wok) {
-                select_topk(s, v, pes_w, writer, io.topk_idx_dev ? io.topk_idx_dev + (size_t)l * TOPK : nullptr,
-                            io.topk_w_dev ? io.topk_w_dev + (size_t)l * TOPK : nullptr,
-                            io.logits_dev ? io.logits_dev + (size_t)l * NE : nullptr);
-                __syncwarp();
-                __threadfence_block();
-                if (lane == 0) s.topk_ready = l + 1;
-            } else if (lane == 0) {
-                s.abort = 1;
-            }
-        }
-        csync();
-        if (s.abort) break;
+        // the slot groups need the top-8 first; the shared group takes it after its down rows
+        // (every logit word of the layer is out by then, and none is overwritten before barrier C)
+        if (!p.sh && !topk_step(s, P, l, ep, pes_w, writer)) break;
 
-        // ---- routed gate/up ----
-        ok = gu_phase(s, P, 1, p.rt1 - p.rt0, cbase + p.c_rgu, cbase + p.c_dn, s.tbl_r, s.gs_r,
-                      [&](int item, int& c, int& lt, int& F) {
-                          int k, t0;
-                          rgu_locate(p, p.rt0 + item, k, t0);
-                          int tt, nt;
-                          rgu_chunk(p, k, tt, nt);
-                          c = cbase + p.c_rgu + k;
-                          lt = p.rt0 + item - t0;
-                          F = 8 * nt;
+        // ---- the group expert's gate/up tiles ----
+        const int ph = p.sh ? 0 : 1;
+        ok = gu_phase(s, P, ph, p.t1 - p.t0, cbase + p.c_gu, cbase + p.c_dn, p.sh ? s.tbl_d : s.tbl_r,
+                      p.sh ? s.gs_d : s.gs_r, [&](int item, int& c, int& lt, int& F) {
+                          const int k = item / GU_TILES;
+                          c = cbase + p.c_gu + k;
+                          lt = item - k * GU_TILES;
+                          F = 8 * min(GU_TILES, p.t1 - p.t0 - k * GU_TILES);
                       });
         if (!ok) s.abort = 1;
         csync();
         if (s.abort) break;
-        gu_epilogue(s, 1, P.act + FS + 8 * p.rt0, p.rt1 - p.rt0);
-        arrive(P, P.flags_b, ep);
+        gu_epilogue(s, ph, P.act + (p.sh ? 0 : FS + FE * p.slot) + 8 * p.t0, p.t1 - p.t0);
 
-        // ---- down: the shared and routed activations of every CTA ----
-        if (!wait_all(s, P, P.flags_b, ep)) break;
-        build_down_tables(s, P);
+        // ---- the group barrier: every activation of the group's expert ----
+        arrive(P, P.flags_b, ep);
+        if (!wait_range(s, P, P.flags_b, p.g0, p.g1, ep)) break;
+
+        // ---- the expert's down rows [16 ot0, 16 ot1) ----
+        build_down_tables(s, P, p);
         csync();
         ok = down_phase(s, P, p, cbase + p.c_dn);
         if (!ok) s.abort = 1;
         csync();
         if (s.abort) break;
         down_epilogue(s, P, p);
+        if (p.sh && !topk_step(s, P, l, ep, pes_w, writer)) break;
         arrive(P, P.flags_c, ep);
     }
     csync();
@@ -1184,7 +1126,7 @@ __global__ void __launch_bounds__(NT, 1) moe_decode_kernel(const __grid_constant
 constexpr size_t kErrOffset = 4096, kStickyOffset = 4100, kDataOffset = 4352;
 
 size_t decode_workspace_bytes() {
-    return kDataOffset + sizeof(float) * (dec::ACT_R + dec::FS + (size_t)4 * dec::D) + 256;
+    return kDataOffset + sizeof(float) * (dec::ACT_R + dec::FS + (size_t)(1 + dec::TOPK) * dec::D) + 256;
 }
 size_t decode_sticky_offset() { return kStickyOffset; }
 
@@ -1192,7 +1134,7 @@ int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, c
                   void* ws, size_t ws_bytes, cudaStream_t stream, int num_ctas) {
     using namespace dec;
     (void)ws_bytes;
-    if (num_ctas > OT || num_ctas * MAX_DN < ITEMS_DN)
+    if (num_ctas < MIN_CTAS || num_ctas > MAX_CTAS)
         return set_error(GTM_ERR_UNSUPPORTED, "gtm_moe_decode: %d CTAs outside the decode's work split", num_ctas);
     Params P;
     memset(&P, 0, sizeof(P));

@@ -14,7 +14,7 @@ void clear_error();
 
 size_t decode_workspace_bytes();
 size_t decode_sticky_offset();
-constexpr int kDecodeMinCtas = 118;   // per-CTA work lists of the fused decode fit its slot arrays
+constexpr int kDecodeMinCtas = 120;   // per-CTA work lists of the fused decode fit its slot arrays
 int launch_decode(const GtmDims& dims, const GtmLayer* layers, int num_layers, const GtmDecodeIO& io,
                   void* ws, size_t ws_bytes, cudaStream_t stream, int num_ctas);
 

@@ -279,15 +279,16 @@ __global__ void __launch_bounds__(VG_THREADS) tok_views_given(const __grid_const
 // Router logits of token blockIdx.x, rows 16 blockIdx.y .. + 15, in src/cpu_reference.cpp:86-106's
 // order (per row and group the 64 products summed in element order, the group's scale times that
 // plus its bias times the group's input sum, the 44 group terms summed in group order): the same
-// arithmetic as the router rows of tok_views_router, one round of 16 rows x 44 groups. Every CTA of
-// a token recomputes the token's exact RMS and router input (2816 elements, far less than its
-// 45 KB of router rows). The logits go to `rlog` (before the logit bias) for tok_views_given.
+// arithmetic as the router rows of tok_views_router, one round of 16 rows x 44 groups; the serial
+// sums read their operands four at a time. Every CTA of a token recomputes the token's exact RMS
+// and router input (2816 elements, against its 45 KB of router rows; measured, 8-row CTAs were
+// slower). The logits go to `rlog` (before the logit bias) for tok_views_given.
 constexpr int RR_ROWS = 16, RR_THREADS = RR_ROWS * GD;   // 704
 __global__ void __launch_bounds__(RR_THREADS) tok_router_rows(const __grid_constant__ ViewsArgs A, float* rlog) {
     __shared__ __align__(16) float sx[D];
     __shared__ __align__(16) float srin[GD * RIN_PITCH];
     __shared__ float xsum[GD];
-    __shared__ float terms[RR_ROWS][GD];
+    __shared__ __align__(16) float terms[RR_ROWS][GD];
     __shared__ double red[40];
     const int t = blockIdx.x, tid = threadIdx.x;
     const GtmLayer& L = A.L;
@@ -300,8 +301,13 @@ __global__ void __launch_bounds__(RR_THREADS) tok_router_rows(const __grid_const
         srin[(i >> 6) * RIN_PITCH + (i & 63)] = __fmul_rn(__fmul_rn(__fmul_rn(sx[i], inv), bf16f(rs[i])), A.inv_sqrt_d);
     __syncthreads();
     if (tid < GD) {
+        const float4* s4 = reinterpret_cast<const float4*>(srin + tid * RIN_PITCH);
         float sm = 0.0f;
-        for (int k = 0; k < kGroup; ++k) sm = __fadd_rn(sm, srin[tid * RIN_PITCH + k]);
+#pragma unroll
+        for (int k = 0; k < kGroup / 4; ++k) {
+            const float4 v = s4[k];
+            sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v.x), v.y), v.z), v.w);
+        }
         xsum[tid] = sm;
     }
     __syncthreads();
@@ -330,8 +336,13 @@ __global__ void __launch_bounds__(RR_THREADS) tok_router_rows(const __grid_const
     terms[rr][g] = __fadd_rn(__fmul_rn(bf16f(Sc[row * GD + g]), dot), __fmul_rn(bf16f(Bi[row * GD + g]), xsum[g]));
     __syncthreads();
     if (tid < RR_ROWS) {
+        const float4* t4 = reinterpret_cast<const float4*>(&terms[tid][0]);
         float acc = 0.0f;
-        for (int g2 = 0; g2 < GD; ++g2) acc = __fadd_rn(acc, terms[tid][g2]);
+#pragma unroll
+        for (int k = 0; k < GD / 4; ++k) {
+            const float4 v = t4[k];
+            acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+        }
         rlog[(size_t)t * NE + blockIdx.y * RR_ROWS + tid] = acc;
     }
 }
