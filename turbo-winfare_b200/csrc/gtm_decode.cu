@@ -80,7 +80,7 @@ constexpr int RIN_PITCH = 65;
 constexpr int QW = 192;                   // fragment-table words per quad: 2 double groups x 12 lane entries x 8
 constexpr uint32_t RING = 144 * 1024;     // chunk ring
 constexpr int NB = 32;                    // chunk mbarrier slots (> the chunks of any one phase)
-constexpr int GU_TILES = 2;               // tiles per gate/up chunk
+constexpr int GU_TILES = 1;               // tiles per gate/up chunk
 constexpr int DN_TILES_R = 6, DN_TILES_S = 3;   // down row tiles per chunk (38 KB routed, 57 KB shared)
 constexpr int MAX_DN = 24;                // items of one phase per CTA (tiles or down row tiles)
 constexpr int QSS = 9;                    // quads of the shared down's 33 groups (the last holds 1)
