@@ -80,7 +80,8 @@ GTM_API int gtm_gemv_q4_rows(uint32_t rows, uint32_t in_dim, uint32_t n, const v
                          in_dim);
     if (!aligned(w, 16) || !aligned(s, 2) || !aligned(b, 2) || !aligned(x, 4) || !aligned(out, 4))
         return set_error(GTM_ERR_MISALIGNED, "gtm_gemv_q4_rows: weights need 16-byte alignment");
-    k_gemv_exact(4, rows, in_dim, w, s, b, x, out, 0, rows, (cudaStream_t)stream, n);
+    if (n == 1 || !aligned(x, 16) || !k_gemv_exact_rows4(rows, in_dim, n, w, s, b, x, out, (cudaStream_t)stream))
+        k_gemv_exact(4, rows, in_dim, w, s, b, x, out, 0, rows, (cudaStream_t)stream, n);
     return check_launch("gtm_gemv_q4_rows");
 }
 

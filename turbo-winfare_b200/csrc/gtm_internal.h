@@ -49,6 +49,10 @@ int launch_ep_peer_combine(const GtmDims& dims, const GtmLayer& L, const GtmToke
 void k_gemv_exact(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
                   const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st,
                   uint32_t nvec = 1);
+// int4 rows of n >= 2 vectors (x 16-byte aligned), the same results as k_gemv_exact per vector;
+// false (nothing launched) when in_dim is outside its shapes
+bool k_gemv_exact_rows4(uint32_t rows, uint32_t in_dim, uint32_t n, const void* w, const uint16_t* s, const uint16_t* b,
+                        const float* x, float* out, cudaStream_t st);
 void k_router_topk(uint32_t n, uint32_t k, const float* logits, const uint16_t* pes, uint32_t* idx, float* w,
                    cudaStream_t st);
 void k_geglu(uint32_t n, const float* g, const float* u, float* out, cudaStream_t st);

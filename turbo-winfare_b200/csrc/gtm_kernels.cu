@@ -70,6 +70,75 @@ __global__ void gemv_exact_kernel(uint32_t in_dim, const uint8_t* __restrict__ w
     }
 }
 
+// int4 rows of n vectors (gtm_gemv_q4_rows): the same arithmetic, in the same order, as
+// gemv_exact_kernel<4> for each vector, mapped for the load path. A thread owns (group g, vector
+// v): the group's 64 inputs of its vector in registers and their sum taken once in the reference's
+// order (x0 + x1 per byte, then accumulated); it then walks GR rows, loading only their 32 bytes
+// of packed weights (shared through L1 by the block's GV vector threads) and running the group's
+// products in element order. The (row, vector) sums over the groups, in group order, follow.
+constexpr int GV = 4, GR = 16;
+__global__ void gemv_exact_rows4_kernel(uint32_t in_dim, uint32_t n, const uint8_t* __restrict__ w,
+                                        const uint16_t* __restrict__ s, const uint16_t* __restrict__ b,
+                                        const float* __restrict__ x, float* __restrict__ out, uint32_t rows) {
+    extern __shared__ float terms[];   // [GR][GV][groups]
+    const uint32_t groups = in_dim / kGroup;
+    const uint32_t t = threadIdx.x, v = t / groups, g = t - v * groups;
+    const uint32_t row0 = blockIdx.x * GR, vv = blockIdx.y * GV + v;
+    const uint32_t nr = min((uint32_t)GR, rows - row0);
+    const bool live = vv < n;
+    float xr[kGroup];
+    float gsum = 0.0f;
+    if (live) {
+        const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)vv * in_dim + (size_t)g * kGroup);
+#pragma unroll
+        for (int c = 0; c < kGroup / 4; ++c) {
+            const float4 q = __ldg(x4 + c);
+            xr[4 * c] = q.x; xr[4 * c + 1] = q.y; xr[4 * c + 2] = q.z; xr[4 * c + 3] = q.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) gsum = __fadd_rn(gsum, __fadd_rn(xr[2 * j], xr[2 * j + 1]));
+        for (uint32_t r = 0; r < nr; ++r) {
+            const uint32_t row = row0 + r;
+            const uint4* wq = reinterpret_cast<const uint4*>(w + (size_t)row * (in_dim / 2) + (size_t)g * 32);
+            const uint4 q0 = __ldg(wq), q1 = __ldg(wq + 1);
+            const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            float dot = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {   // byte j holds elements 2j (low) and 2j + 1 (high)
+                const uint32_t byte = (words[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                dot = __fadd_rn(dot, __fmul_rn((float)(byte & 0x0Fu), xr[2 * j]));
+                dot = __fadd_rn(dot, __fmul_rn((float)(byte >> 4), xr[2 * j + 1]));
+            }
+            const size_t si = (size_t)row * groups + g;
+            terms[((size_t)r * GV + v) * groups + g] =
+                __fadd_rn(__fmul_rn(bf16f(__ldg(s + si)), dot), __fmul_rn(bf16f(__ldg(b + si)), gsum));
+        }
+    }
+    __syncthreads();
+    if (t < GR * GV) {   // (row, vector): the group terms in group order
+        const uint32_t r = t / GV, v2 = t - r * GV, vo = blockIdx.y * GV + v2;
+        if (r < nr && vo < n) {
+            const float* tp = terms + ((size_t)r * GV + v2) * groups;
+            float acc = 0.0f;
+#pragma unroll 4
+            for (uint32_t gg = 0; gg < groups; ++gg) acc = __fadd_rn(acc, tp[gg]);
+            out[(size_t)vo * rows + row0 + r] = acc;
+        }
+    }
+}
+
+// Grids for in_dim / 64 groups with GV x groups <= 1024 threads and GR x GV x groups floats of
+// shared memory <= 48 KB (in_dim <= 12288); the caller takes gemv_exact_kernel otherwise.
+bool k_gemv_exact_rows4(uint32_t rows, uint32_t in_dim, uint32_t n, const void* w, const uint16_t* s, const uint16_t* b,
+                        const float* x, float* out, cudaStream_t st) {
+    const uint32_t groups = in_dim / kGroup;
+    const size_t smem = sizeof(float) * (size_t)GR * GV * groups;
+    if (GV * groups > 1024 || smem > 48 * 1024) return false;
+    const dim3 grid((rows + GR - 1) / GR, (n + GV - 1) / GV);
+    gemv_exact_rows4_kernel<<<grid, GV * groups, smem, st>>>(in_dim, n, (const uint8_t*)w, s, b, x, out, rows);
+    return true;
+}
+
 void k_gemv_exact(int bits, uint32_t rows, uint32_t in_dim, const void* w, const uint16_t* s, const uint16_t* b,
                   const float* x, float* out, uint32_t row_begin, uint32_t row_end, cudaStream_t st, uint32_t nvec) {
     const uint32_t groups = in_dim / kGroup;
