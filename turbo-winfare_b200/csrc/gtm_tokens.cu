@@ -63,8 +63,11 @@ constexpr int D = 2816, FE = 704, FS = 2112, NE = 128, TOPK = 8, GD = D / kGroup
 constexpr int BK = 64;                  // K block = one quantisation group
 constexpr int MW = 256;                 // weight rows per tile: two M=128 row blocks
 constexpr int NT = 128;                 // tokens per tile (MMA N, at most)
-constexpr int SX = 6;                   // activation stages (shared memory, high + low part each)
-constexpr int RS = 4;                   // packed-weight stages (shared memory)
+constexpr int SX = 4;                   // activation stages (shared memory, high + low part each)
+// Packed-weight stages (shared memory). A TMA weight load takes ~4,800 cycles from issue to the
+// dequant warps under load (clock stamps at 64 and 4096 tokens), so the weight ring is the deeper
+// one; activations are ready ~8,000 cycles before the MMA with 6 stages, so 4 suffice (3 starve it).
+constexpr int RS = 12;
 constexpr int SW = 2;                   // dequantised-weight stages (tensor memory, 2 x 32 columns each)
 constexpr int NSLOT = 3;                // accumulator slots of NT columns; row blocks rotate through them
 constexpr uint32_t A_COL0 = NSLOT * NT; // first tensor-memory column of the weight stages
