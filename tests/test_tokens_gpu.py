@@ -152,6 +152,24 @@ def test_repeat_is_deterministic(model, block):
         assert np.array_equal(a[k], b[k]), k
 
 
+def test_io_rows_aligned_to_4_bytes_only(model, block):
+    """The C ABI asks only element alignment of the io pointers. With the block input and every
+    output one float past a 16-byte boundary (the combine's scalar path), the results are
+    bit-identical to the 16-byte-aligned call."""
+    T = 70
+    x = synth_tokens(T, token0=321)
+    a = run(block, model, x)
+    xo = torch.empty(T * D + 1, device="cuda")[1:].view(T, D)
+    xo.copy_(x)
+    o = {k: torch.empty(T * D + 1, device="cuda")[1:].view(T, D) for k in ("hidden", "h1", "h2")}
+    assert all(t.data_ptr() % 16 == 4 for t in (xo, *o.values()))
+    block(model.layers[0], xo, o["hidden"], h1=o["h1"], h2=o["h2"])
+    block.check()
+    torch.cuda.synchronize()
+    for k, t in o.items():
+        assert np.array_equal(t.cpu().numpy(), a[k]), k
+
+
 @pytest.mark.parametrize("T", [1, 31, 32, 33, 63, 64, 65, 127, 128, 129, 200])
 def test_forced_routing_tile_edges(model, ref_layer, block, T):
     """Every token routed to the same 8 experts, so each expert's token count is T: covers the

@@ -1244,6 +1244,38 @@ struct CombineArgs {
     float* h2_out;            // [T][D] or null
 };
 
+// Four bf16 (elements 4c .. 4c+3) as floats: one 8-byte load when p is 8-byte aligned.
+__device__ __forceinline__ void ld4_bf16(const uint16_t* p, int c, float (&w)[4]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 7) == 0) {
+        const uint2 g = reinterpret_cast<const uint2*>(p)[c];
+        w[0] = __uint_as_float(g.x << 16); w[1] = __uint_as_float(g.x & 0xFFFF0000u);
+        w[2] = __uint_as_float(g.y << 16); w[3] = __uint_as_float(g.y & 0xFFFF0000u);
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = bf16f(p[4 * c + e]);
+    }
+}
+
+// Elements 4c .. 4c+3 of a float row: one 16-byte access when the row is 16-byte aligned (the
+// io pointers of gtm_moe_tokens need only 4-byte alignment).
+__device__ __forceinline__ void ld4_f32(const float* p, int c, float (&v)[4]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        const float4 f = reinterpret_cast<const float4*>(p)[c];
+        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = p[4 * c + e];
+    }
+}
+__device__ __forceinline__ void st4_f32(float* p, int c, const float (&v)[4]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        reinterpret_cast<float4*>(p)[c] = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p[4 * c + e] = v[e];
+    }
+}
+
 constexpr int CT = D / 4;                     // combine: threads per token, one float4 of each row
 constexpr int CV = (D / 4 + CT - 1) / CT;     // float4 chunks of a row per thread
 
@@ -1297,11 +1329,11 @@ __global__ void __launch_bounds__(CT, 2) tok_combine(const __grid_constant__ Com
                 acc[3] = __fadd_rn(acc[3], __fmul_rn(wk[k], r.w));
             }
             sv[v][0] = so.x; sv[v][1] = so.y; sv[v][2] = so.z; sv[v][3] = so.w;
+            if (A.x_f32) ld4_f32(A.x_f32 + (size_t)t * D, c, xv[v]);
+            else ld4_bf16(A.x_bf16 + (size_t)t * D, c, xv[v]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 hv[v][e] = acc[e];
-                const size_t xi = (size_t)t * D + 4 * c + e;
-                xv[v][e] = A.x_f32 ? A.x_f32[xi] : bf16f(A.x_bf16[xi]);
                 a += (double)sv[v][e] * sv[v][e];
                 b += (double)acc[e] * acc[e];
             }
@@ -1319,16 +1351,19 @@ __global__ void __launch_bounds__(CT, 2) tok_combine(const __grid_constant__ Com
     for (int v = 0; v < CV; ++v) {
         const int c = tid + v * CT;
         if (c < D / 4) {
+            float w1[4], w2[4], h1[4];
+            ld4_bf16(w_pf1, c, w1);
+            ld4_bf16(w_pf2, c, w2);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int i = 4 * c + e;
-                const float h1 = (sv[v][e] * inv1) * bf16f(w_pf1[i]);
-                if (A.h1_out) A.h1_out[(size_t)t * D + i] = h1;
-                if (A.h2_out) A.h2_out[(size_t)t * D + i] = hv[v][e];
-                const float tv = (hv[v][e] * inv2) * bf16f(w_pf2[i]) + h1;
+                h1[e] = (sv[v][e] * inv1) * w1[e];
+                const float tv = (hv[v][e] * inv2) * w2[e] + h1[e];
+                sv[v][e] = hv[v][e];   // h2, kept for its store
                 hv[v][e] = tv;
                 a += (double)tv * tv;
             }
+            if (A.h1_out) st4_f32(A.h1_out + (size_t)t * D, c, h1);
+            if (A.h2_out) st4_f32(A.h2_out + (size_t)t * D, c, sv[v]);
         }
     }
     r = combine_sum2(a, 0.0, red, 1);
@@ -1337,11 +1372,11 @@ __global__ void __launch_bounds__(CT, 2) tok_combine(const __grid_constant__ Com
     for (int v = 0; v < CV; ++v) {
         const int c = tid + v * CT;
         if (c < D / 4) {
+            float w[4], o[4];
+            ld4_bf16(w_pf, c, w);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int i = 4 * c + e;
-                A.hidden_out[(size_t)t * D + i] = (xv[v][e] + (hv[v][e] * inv3) * bf16f(w_pf[i])) * ls;
-            }
+            for (int e = 0; e < 4; ++e) o[e] = (xv[v][e] + (hv[v][e] * inv3) * w[e]) * ls;
+            st4_f32(A.hidden_out + (size_t)t * D, c, o);
         }
     }
 }
