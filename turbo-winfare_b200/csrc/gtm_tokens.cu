@@ -189,6 +189,21 @@ __device__ __forceinline__ int route_top8(const ViewsArgs& A, int t, const float
 // fp16 views of a chunk go out as one 16-byte store each (kperm permutes inside 8 elements). Same
 // arithmetic, element for element, as tok_views_router.
 constexpr int VG_THREADS = 128, VG_CH = (D / 8 + VG_THREADS - 1) / VG_THREADS;
+// Elements 8c .. 8c+7 of a bf16 vector as floats: one 16-byte load when p is 16-byte aligned.
+__device__ __forceinline__ void ld8_bf16(const uint16_t* p, int c, float (&w)[8]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        const uint4 g = __ldg(reinterpret_cast<const uint4*>(p) + c);
+        const uint32_t v[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            w[2 * k] = __uint_as_float(v[k] << 16);
+            w[2 * k + 1] = __uint_as_float(v[k] & 0xFFFF0000u);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[e] = bf16f(p[8 * c + e]);
+    }
+}
 __global__ void __launch_bounds__(VG_THREADS) tok_views_given(const __grid_constant__ ViewsArgs A) {
     __shared__ double red[VG_THREADS / 32 + 1];
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -248,16 +263,19 @@ __global__ void __launch_bounds__(VG_THREADS) tok_views_given(const __grid_const
         const int ch = tid + c * VG_THREADS;
         if (ch >= D / 8) continue;
         const int i0 = 8 * ch;
+        float wp[8], wp2[8];
+        ld8_bf16(w_pre, ch, wp);
+        ld8_bf16(w_pre2, ch, wp2);
         uint16_t dh[8], dl[8], rh[8], rl[8];   // at positions kperm(i) - i0
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const int pe = kperm(e);
             const float h = __fmul_rn(x[c][e], inv);
-            const float dx = __fmul_rn(h, bf16f(w_pre[i0 + e]));
+            const float dx = __fmul_rn(h, wp[e]);
             const __half hi = __float2half_rn(dx);
             dh[pe] = __half_as_ushort(hi);
             dl[pe] = __half_as_ushort(__float2half_rn(dx - __half2float(hi)));
-            const float rx = __fmul_rn(h, bf16f(w_pre2[i0 + e]));
+            const float rx = __fmul_rn(h, wp2[e]);
             const __half r = __float2half_rn(rx);
             rh[pe] = __half_as_ushort(r);
             rl[pe] = __half_as_ushort(__float2half_rn(rx - __half2float(r)));
@@ -538,30 +556,24 @@ __device__ __forceinline__ void route_scan(const RouteArgs& A) {
     __shared__ int cnt[NE], off[NE + 1], t0[NE + 1], t1[NE + 1];
     __shared__ int wsum[NE / 32][3];
     const int tid = threadIdx.x, lane = tid & 31;
-    // (1) per expert, exclusive prefix of its per-chunk counts: SP adjacent lanes per expert, each a
-    //     contiguous run of chunks, combined by shuffles inside the warp
+    // (1) per expert, the total and each of the SP threads' exclusive prefix of its per-chunk counts:
+    //     SP adjacent lanes per expert, each a contiguous run of chunks, combined by shuffles
+    const int se = tid / SP, sp = tid % SP;
+    const int per = (A.nchunks + SP - 1) / SP, sc0 = sp * per, sc1 = min(A.nchunks, sc0 + per);
+    int srun;
     {
-        const int e = tid / SP, p = tid % SP;
-        const int per = (A.nchunks + SP - 1) / SP, c0 = p * per, c1 = min(A.nchunks, c0 + per);
         int local = 0;
-        if (e < A.ne)
-            for (int c = c0; c < c1; ++c) local += A.chunk[(size_t)c * NE + e];
+        if (se < A.ne)
+            for (int c = sc0; c < sc1; ++c) local += A.chunk[(size_t)c * NE + se];
         int incl = local;
 #pragma unroll
         for (int o = 1; o < SP; o <<= 1) {
             const int v = __shfl_up_sync(0xffffffffu, incl, o, SP);
-            if (p >= o) incl += v;
+            if (sp >= o) incl += v;
         }
-        int run = incl - local;
+        srun = incl - local;
         const int total = __shfl_sync(0xffffffffu, incl, SP - 1, SP);
-        if (e < A.ne) {
-            for (int c = c0; c < c1; ++c) {
-                const int v = A.chunk[(size_t)c * NE + e];
-                A.chunk[(size_t)c * NE + e] = run;
-                run += v;
-            }
-            if (p == 0) cnt[e] = total;
-        }
+        if (se < A.ne && sp == 0) cnt[se] = total;
     }
     __syncthreads();
     // (2) expert offsets and tile-list bases: a block scan over the experts
@@ -587,30 +599,29 @@ __device__ __forceinline__ void route_scan(const RouteArgs& A) {
     if (tid == 0) { off[0] = 0; t0[0] = 0; t1[0] = 0; }
     __syncthreads();
     if (tid == 0 && A.nrows) *A.nrows = off[A.ne];
-    for (int j = tid; j < A.nchunks * A.ne; j += blockDim.x) {
-        const int c = j / A.ne, ex = j - c * A.ne;
-        A.chunk[(size_t)c * NE + ex] += off[ex];
-    }
-    // (3) routed tiles, one thread per entry: entry t0[e] + f * nt + m of expert e covers token range
-    //     m of nt and row block f, so the tiles of one (expert, row block) stay adjacent over the token
-    //     ranges (L2 reuse of the weights); the expert of an entry is found by binary search
-    auto expert_of = [&](const int* base, int i) {
-        int lo = 0, hi = A.ne - 1;   // largest e with base[e] <= i
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (base[mid] <= i) lo = mid; else hi = mid - 1;
+    // each chunk's first row per expert: the expert's offset plus the chunks before it (the same
+    // threads as in (1), which read these counts)
+    if (se < A.ne) {
+        int run = off[se] + srun;
+        for (int c = sc0; c < sc1; ++c) {
+            const int v = A.chunk[(size_t)c * NE + se];
+            A.chunk[(size_t)c * NE + se] = run;
+            run += v;
         }
-        return lo;
-    };
-    for (int i = tid; i < t0[A.ne]; i += blockDim.x) {
-        const int e = expert_of(t0, i), c = cnt[e], nt = ntok_tiles(c), k = i - t0[e], f = k / nt, m = k - f * nt;
-        const int r0 = c * m / nt, r1 = c * (m + 1) / nt;
-        A.tiles0[i] = Tile{e, off[e] + r0, r1 - r0, f};
     }
-    for (int i = tid; i < t1[A.ne]; i += blockDim.x) {
-        const int e = expert_of(t1, i), c = cnt[e], nt = ntok_tiles(c), k = i - t1[e], f = k / nt, m = k - f * nt;
-        const int r0 = c * m / nt, r1 = c * (m + 1) / nt;
-        A.tiles1[i] = Tile{e, off[e] + r0, r1 - r0, f};
+    // (3) routed tiles, a warp per expert: entry t0[e] + f * nt + m of expert e covers token range
+    //     m of nt and row block f, so the tiles of one (expert, row block) stay adjacent over the token
+    //     ranges (L2 reuse of the weights)
+    for (int e = tid >> 5; e < A.ne; e += blockDim.x >> 5) {
+        const int c = cnt[e], nt = ntok_tiles(c);
+        for (int k = lane; k < nt * FB0_R; k += 32) {
+            const int f = k / nt, m = k - f * nt, r0 = c * m / nt, r1 = c * (m + 1) / nt;
+            A.tiles0[t0[e] + k] = Tile{e, off[e] + r0, r1 - r0, f};
+        }
+        for (int k = lane; k < nt * FB1; k += 32) {
+            const int f = k / nt, m = k - f * nt, r0 = c * m / nt, r1 = c * (m + 1) / nt;
+            A.tiles1[t1[e] + k] = Tile{e, off[e] + r0, r1 - r0, f};
+        }
     }
     const int T = A.t_shared, nts = ntok_tiles(T), b0 = t0[A.ne], b1 = t1[A.ne];
     for (int i = tid; i < nts * FB0_S; i += blockDim.x) {
